@@ -1,0 +1,111 @@
+// Python bindings of the native library: tensor checks + launches on the current torch stream.
+// Kernels are declared in the csrc headers and take raw pointers; this is the only file that includes torch.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <vector>
+
+#include "binding_utils.h"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace {
+// One 16-word status buffer per device: bounded waits and bounds checks OR their error codes into word 0.
+std::mutex g_status_mu;
+std::vector<at::Tensor> g_status;
+}  // namespace
+
+namespace afb_bind {
+uint32_t* status_ptr(int dev) {
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if ((int)g_status.size() <= dev) g_status.resize(dev + 1);
+  if (!g_status[dev].defined())
+    g_status[dev] = torch::zeros({16}, torch::dtype(torch::kInt32).device(torch::kCUDA, dev));
+  return reinterpret_cast<uint32_t*>(g_status[dev].data_ptr<int32_t>());
+}
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+}  // namespace afb_bind
+
+namespace {
+using namespace afb_bind;
+
+at::Tensor status_tensor(int64_t dev) {
+  status_ptr((int)dev);
+  return g_status[dev];
+}
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_DT(x, dt) TORCH_CHECK((x).scalar_type() == (dt), #x " has dtype ", (x).scalar_type(), ", expected ", dt)
+#define CHECK_ROWMAJOR(x) TORCH_CHECK((x).dim() == 2 && (x).stride(1) == 1, #x " must be 2-D with unit inner stride")
+
+// ------------------------------------------------------------------------------------------ GEMM
+at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tensor> out,
+                c10::optional<at::Tensor> residual, double alpha, bool out_fp32, int64_t bn, int64_t splits) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  CHECK_DT(a, at::kBFloat16);
+  CHECK_DT(b, at::kBFloat16);
+  CHECK_ROWMAJOR(a);
+  CHECK_ROWMAJOR(b);
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(b.size(1) == K, "gemm: K mismatch");
+  c10::cuda::CUDAGuard g(a.device());
+  at::Tensor o = out.has_value() ? *out
+                                 : torch::empty({M, N}, a.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  CHECK_ROWMAJOR(o);
+  TORCH_CHECK(o.size(0) == M && o.size(1) == N, "gemm: out shape");
+  TORCH_CHECK(o.scalar_type() == (out_fp32 ? at::kFloat : at::kBFloat16), "gemm: out dtype");
+  afb::GemmEpilogue epi;
+  epi.out = o.data_ptr();
+  epi.ldo = o.stride(0);
+  epi.out_fp32 = out_fp32;
+  epi.alpha = (float)alpha;
+  if (residual.has_value()) {
+    CHECK_DT((*residual), at::kBFloat16);
+    CHECK_ROWMAJOR((*residual));
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N, "gemm: residual shape");
+    epi.residual = residual->data_ptr();
+    epi.ldr = residual->stride(0);
+  }
+  afb::GemmPlan p = afb::plan_gemm(M, N, K, num_sms());
+  if (bn > 0) p.bn = (int)bn;
+  if (splits > 0) p.splits = (int)splits;
+  at::Tensor part;
+  if (p.splits > 1) {
+    part = torch::empty({p.splits, M, N}, a.options().dtype(at::kFloat));
+    epi.partial = part.data_ptr();
+  }
+  check_rc(afb::gemm_bf16_tn(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), M, N, K, epi, p.bn, p.splits,
+                             status_ptr(a.get_device()), stream()),
+           "gemm_bf16_tn");
+  return o;
+}
+
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
+  afb::GemmPlan p = afb::plan_gemm(M, N, K, num_sms());
+  return {p.bn, p.splits};
+}
+
+}  // namespace
+
+void register_kernel_ops(pybind11::module& m);  // defined in ops_bindings.cpp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "arc_forge_2026_b200 native kernels (sm_100a)";
+  m.def("status_tensor", &status_tensor, "per-device kernel status words (int32[16])");
+  m.def("gemm", &gemm, "bf16 tcgen05 GEMM: out = alpha * a @ b.T (+ residual)", py::arg("a"), py::arg("b"),
+        py::arg("out") = py::none(), py::arg("residual") = py::none(), py::arg("alpha") = 1.0,
+        py::arg("out_fp32") = false, py::arg("bn") = 0, py::arg("splits") = 0);
+  m.def("gemm_plan", &gemm_plan);
+  register_kernel_ops(m);
+}

@@ -1,0 +1,446 @@
+// Memory-bound fused kernels of the decode/verify step: RMSNorm (+residual), per-head q/k norm + partial
+// RoPE + paged KV store, router softmax/top-k, deterministic expert sort, fp8 group quantisation for the
+// expert GEMMs, SwiGLU, the top-k combine with the shared expert, and the embedding gather.
+// Each is one pass over HBM with vectorised 16-byte accesses; reductions are per warp in a fixed order,
+// so results are bitwise reproducible run to run.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace afb {
+
+// ------------------------------------------------------------------------------------------ RMSNorm
+// y = x/rms(x) * (1 + w) (zero-centred) or * w; with `residual`: h = x + residual, residual <- h (bf16),
+// y = norm(h). One warp per row; pass 2 re-reads the row (L1/L2 hit) instead of holding it in registers.
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
+                               const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int rows, int H,
+                               float eps, int zero_centered) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + (size_t)row * H;
+  __nv_bfloat16* rr = residual ? residual + (size_t)row * H : nullptr;
+  float ss = 0.f;
+  for (int c = lane * 8; c < H; c += 256) {
+    uint4 q = *reinterpret_cast<const uint4*>(xr + c);
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&q);
+    float f[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) f[t] = __bfloat162float(h[t]);
+    if (rr) {
+      uint4 r = *reinterpret_cast<const uint4*>(rr + c);
+      const __nv_bfloat16* hr = reinterpret_cast<const __nv_bfloat16*>(&r);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) f[t] += __bfloat162float(hr[t]);
+      uint4 o = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                           pack_bf16x2(f[6], f[7]));
+      *reinterpret_cast<uint4*>(rr + c) = o;
+      const __nv_bfloat16* ho = reinterpret_cast<const __nv_bfloat16*>(&o);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) f[t] = __bfloat162float(ho[t]);  // normalise the stored bf16 stream
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) ss += f[t] * f[t];
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / H + eps);
+  const __nv_bfloat16* src = rr ? rr : xr;
+  for (int c = lane * 8; c < H; c += 256) {
+    uint4 q = *reinterpret_cast<const uint4*>(src + c);
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&q);
+    uint4 wq = *reinterpret_cast<const uint4*>(w + c);
+    const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wq);
+    float o[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float ww = __bfloat162float(wh[t]);
+      o[t] = __bfloat162float(h[t]) * inv * (zero_centered ? 1.f + ww : ww);
+    }
+    *reinterpret_cast<uint4*>(y + (size_t)row * H + c) =
+        make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  }
+}
+
+int rmsnorm(const void* x, void* residual, const void* w, void* y, int rows, int H, float eps, int zero_centered,
+            cudaStream_t st) {
+  if (H % 8) return 3;
+  if (!rows) return 0;
+  const int warps = 4;
+  rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, st>>>(
+      (const __nv_bfloat16*)x, (__nv_bfloat16*)residual, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, rows, H, eps,
+      zero_centered);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------ q/k norm + RoPE + KV store
+// qkv: [T, Hq*2D + 2*Hkv*D] bf16 GEMM output, per token [q_h | gate_h] x Hq, then k x Hkv, v x Hkv.
+// Writes q_out [T, Hq, D] (RMS-normed with (1+w), NeoX RoPE on the first `rot` channels) and k (same) / v into
+// the paged cache at slots[t] (page = slot / page_size): cache layout [num_pages, Hkv, page_size, D].
+// cos/sin come from a table [max_pos, rot/2] built in fp64 on the host. One warp per (token, head);
+// the head vector is staged in shared memory so each lane can read its rotation partner.
+__global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, int T, int Hq, int Hkv, int D,
+                                          int rot, const __nv_bfloat16* __restrict__ qw,
+                                          const __nv_bfloat16* __restrict__ kw, const int* __restrict__ positions,
+                                          const int* __restrict__ slots, const float* __restrict__ cos_t,
+                                          const float* __restrict__ sin_t, float eps, __nv_bfloat16* __restrict__ q_out,
+                                          __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache,
+                                          int page_size) {
+  __shared__ float buf[8][256];
+  const int wi = threadIdx.x >> 5;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + wi;
+  const int lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  if (gw >= T * heads) return;
+  const int t = gw / heads, h = gw % heads;
+  const int row_len = Hq * 2 * D + 2 * Hkv * D;
+  const __nv_bfloat16* src;
+  int kind;  // 0 q, 1 k, 2 v
+  if (h < Hq) {
+    src = qkv + (size_t)t * row_len + h * 2 * D;
+    kind = 0;
+  } else if (h < Hq + Hkv) {
+    src = qkv + (size_t)t * row_len + Hq * 2 * D + (h - Hq) * D;
+    kind = 1;
+  } else {
+    src = qkv + (size_t)t * row_len + Hq * 2 * D + Hkv * D + (h - Hq - Hkv) * D;
+    kind = 2;
+  }
+  const int slot = slots[t];
+  const int page = slot / page_size, tok = slot % page_size;
+  if (kind == 2) {
+    __nv_bfloat16* dst = vcache + (((size_t)page * Hkv + (h - Hq - Hkv)) * page_size + tok) * D;
+    for (int j = lane; j < D; j += 32) dst[j] = src[j];
+    return;
+  }
+  float* b = buf[wi];
+  float ss = 0.f;
+  for (int j = lane; j < D; j += 32) {
+    const float f = __bfloat162float(src[j]);
+    b[j] = f;
+    ss += f * f;
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / D + eps);
+  const __nv_bfloat16* nw = kind == 0 ? qw : kw;
+  for (int j = lane; j < D; j += 32) b[j] = b[j] * inv * (1.f + __bfloat162float(nw[j]));
+  __syncwarp();
+  const int half = rot / 2;
+  const int p = positions[t];
+  __nv_bfloat16* dst = kind == 0 ? q_out + ((size_t)t * Hq + h) * D
+                                 : kcache + (((size_t)page * Hkv + (h - Hq)) * page_size + tok) * D;
+  for (int j = lane; j < D; j += 32) {
+    float o = b[j];
+    if (j < rot) {
+      const int fi = j < half ? j : j - half;
+      const float cs = cos_t[(size_t)p * half + fi], sn = sin_t[(size_t)p * half + fi];
+      o = j < half ? b[j] * cs - b[j + half] * sn : b[j] * cs + b[j - half] * sn;
+    }
+    dst[j] = __float2bfloat16(o);
+  }
+}
+
+int qk_norm_rope_store(const void* qkv, int T, int Hq, int Hkv, int D, int rot, const void* qw, const void* kw,
+                       const int* positions, const int* slots, const float* cos_t, const float* sin_t, float eps,
+                       void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st) {
+  if (D > 256 || rot > D || rot % 2) return 3;
+  if (!T) return 0;
+  const int warps = 8;
+  const int total = T * (Hq + 2 * Hkv);
+  qk_norm_rope_store_kernel<<<(total + warps - 1) / warps, warps * 32, 0, st>>>(
+      (const __nv_bfloat16*)qkv, T, Hq, Hkv, D, rot, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, positions,
+      slots, cos_t, sin_t, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)kcache, (__nv_bfloat16*)vcache, page_size);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------ router
+// logits [T, ld] fp32 (first E columns are experts). softmax -> top-k (ties: lower id) -> renorm.
+// One warp per token; lane i owns experts i, i+32, ... (E <= 1024).
+__global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int k, int renorm,
+                                   int* __restrict__ ids, float* __restrict__ weights) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* l = logits + (size_t)t * ld;
+  float v[32];
+  const int per = (E + 31) / 32;
+  float mx = -INFINITY;
+  for (int i = 0; i < per; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < E ? l[e] : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+  for (int i = 0; i < per; ++i) {
+    v[i] = (i * 32 + lane) < E ? __expf(v[i] - mx) : 0.f;
+    sum += v[i];
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.f / sum;
+  float picked_sum = 0.f;
+  float wsel = 0.f;
+  int isel = 0;
+  for (int j = 0; j < k; ++j) {
+    // local best (value desc, id asc)
+    float bv = -1.f;
+    int be = 0x7fffffff;
+    for (int i = 0; i < per; ++i) {
+      const int e = i * 32 + lane;
+      if (e < E && (v[i] > bv || (v[i] == bv && e < be))) {
+        bv = v[i];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    if ((be & 31) == lane) v[be >> 5] = -2.f;  // remove
+    const float p = bv * inv;
+    picked_sum += p;
+    if (lane == j) {
+      wsel = p;
+      isel = be;
+    }
+  }
+  if (lane < k) {
+    ids[(size_t)t * k + lane] = isel;
+    weights[(size_t)t * k + lane] = renorm ? wsel / picked_sum : wsel;
+  }
+}
+
+int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, int* ids, float* weights,
+                cudaStream_t st) {
+  if (E > 1024 || k > 32) return 3;
+  const int warps = 4;
+  router_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(logits, ld, T, E, k, renorm, ids, weights);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------ expert sort
+// Stable counting sort of the T*k (token, slot) entries by expert, in one CTA of 1024 threads:
+// entry i -> position offsets[e] + (# entries i' < i with the same expert). Outputs:
+//   offsets [E+1] (exclusive scan of counts), row_token [T*k] (token of each sorted row),
+//   row_entry [T*k] (entry index t*k+j of each sorted row), entry_row [T*k] (inverse).
+// `expert_map` (optional) maps global expert ids to local ones (-1 = not on this rank) for EP.
+__global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict__ ids, int n, int E,
+                                                           const int* __restrict__ expert_map, int* __restrict__ offsets,
+                                                           int* __restrict__ row_token, int* __restrict__ row_entry,
+                                                           int* __restrict__ entry_row, int k) {
+  extern __shared__ int sm[];
+  int* cnt = sm;             // [E] running base per expert
+  int* hist = sm + E;        // [32 warps][E] per-warp counts of the current chunk
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  // pass 1: counts
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int e = ids[i];
+    if (expert_map) e = expert_map[e];
+    if (e >= 0) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      offsets[e] = acc;
+      acc += cnt[e];
+      cnt[e] = offsets[e];
+    }
+    offsets[E] = acc;
+  }
+  __syncthreads();
+  // pass 2: stable positions, chunk of 1024 entries at a time
+  for (int base = 0; base < n; base += blockDim.x) {
+    for (int x = threadIdx.x; x < 32 * E; x += blockDim.x) hist[x] = 0;
+    __syncthreads();
+    const int i = base + threadIdx.x;
+    int e = -1;
+    if (i < n) {
+      e = ids[i];
+      if (expert_map) e = expert_map[e];
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_in_warp = __popc(peers & ((1u << lane) - 1));
+    if (e >= 0 && rank_in_warp == 0) hist[warp * E + e] = __popc(peers);
+    __syncthreads();
+    // exclusive prefix over warps per expert (in place), then add the running base
+    for (int x = threadIdx.x; x < E; x += blockDim.x) {
+      int acc = cnt[x];
+      for (int w = 0; w < 32; ++w) {
+        const int c = hist[w * E + x];
+        hist[w * E + x] = acc;
+        acc += c;
+      }
+      cnt[x] = acc;
+    }
+    __syncthreads();
+    if (e >= 0) {
+      const int pos = hist[warp * E + e] + rank_in_warp;
+      row_token[pos] = i / k;
+      row_entry[pos] = i;
+      entry_row[i] = pos;
+    } else if (i < n) {
+      entry_row[i] = -1;
+    }
+    __syncthreads();
+  }
+}
+
+int expert_sort(const int* ids, int n, int E, const int* expert_map, int* offsets, int* row_token, int* row_entry,
+                int* entry_row, int k, cudaStream_t st) {
+  const size_t smem = (size_t)(E + 32 * E) * sizeof(int);
+  if (smem > 200 * 1024) return 3;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(expert_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  expert_sort_kernel<<<1, 1024, smem, st>>>(ids, n, E, expert_map, offsets, row_token, row_entry, entry_row, k);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------ fp8 group quant + gather
+// out_q[r, :] = e4m3(x[src(r), :] / s), s = amax/448 per 128-column group (1 if the group is all zero);
+// src(r) = row_token[r] when given, else r. One warp per (row, group): lane owns 4 consecutive values.
+__global__ void quant_rows_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const int* __restrict__ row_token,
+                                       const int* __restrict__ nrows_dev, int nrows, int K,
+                                       __nv_fp8_e4m3* __restrict__ q, float* __restrict__ scales) {
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int groups = K / 128;
+  const int n = nrows_dev ? *nrows_dev : nrows;
+  const int r = gw / groups, g = gw % groups;
+  if (r >= n) return;
+  const int src = row_token ? row_token[r] : r;
+  const __nv_bfloat16* p = x + (size_t)src * ldx + g * 128 + lane * 4;
+  uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+  float f[4];
+  float a = 0.f;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    f[t] = __bfloat162float(h[t]);
+    a = fmaxf(a, fabsf(f[t]));
+  }
+  a = warp_max(a);
+  const float s = a > 0.f ? a / 448.f : 1.f;
+  const float inv = 1.f / s;
+  __nv_fp8x4_e4m3 o(make_float4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv));
+  *reinterpret_cast<__nv_fp8x4_e4m3*>(q + (size_t)r * K + g * 128 + lane * 4) = o;
+  if (lane == 0) scales[(size_t)r * groups + g] = s;
+}
+
+int quant_rows_e4m3(const void* x, int ldx, const int* row_token, const int* nrows_dev, int nrows, int K, void* q,
+                    float* scales, cudaStream_t st) {
+  if (K % 128) return 3;
+  const int warps = 8;
+  const long total = (long)nrows * (K / 128);
+  if (total == 0) return 0;
+  quant_rows_e4m3_kernel<<<(unsigned)((total + warps - 1) / warps), warps * 32, 0, st>>>(
+      (const __nv_bfloat16*)x, ldx, row_token, nrows_dev, nrows, K, (__nv_fp8_e4m3*)q, scales);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------ MoE combine
+// out[t] = x_res[t] + sigmoid(sg[t]) * shared[t] + sum_j y[entry_row[t*k+j]]   (y already carries the route weight)
+// sg is read from column `sg_col` of the router logits (the shared-expert gate rides along the router GEMM).
+// One warp per token, 8 bf16 per lane per step; rows of y absent on this rank (entry_row < 0) are skipped.
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ entry_row, int k,
+                                   const __nv_bfloat16* __restrict__ shared, const float* __restrict__ router_logits,
+                                   int ld_logits, int sg_col, const __nv_bfloat16* __restrict__ resid,
+                                   __nv_bfloat16* __restrict__ out, int T, int H) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  float sg = 1.f;
+  if (router_logits) sg = 1.f / (1.f + __expf(-router_logits[(size_t)t * ld_logits + sg_col]));
+  int rows[32];
+  for (int j = 0; j < k; ++j) rows[j] = entry_row[t * k + j];
+  for (int c = lane * 8; c < H; c += 256) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < k; ++j) {
+      if (rows[j] < 0) continue;
+      uint4 q = *reinterpret_cast<const uint4*>(y + (size_t)rows[j] * H + c);
+      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
+    }
+    if (shared) {
+      uint4 q = *reinterpret_cast<const uint4*>(shared + (size_t)t * H + c);
+      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += sg * __bfloat162float(hq[i]);
+    }
+    if (resid) {
+      uint4 q = *reinterpret_cast<const uint4*>(resid + (size_t)t * H + c);
+      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = make_uint4(
+        pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+  }
+}
+
+int moe_combine(const void* y, const int* entry_row, int k, const void* shared, const float* router_logits,
+                int ld_logits, int sg_col, const void* resid, void* out, int T, int H, cudaStream_t st) {
+  if (H % 8 || k > 32) return 3;
+  const int warps = 4;
+  moe_combine_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(
+      (const __nv_bfloat16*)y, entry_row, k, (const __nv_bfloat16*)shared, router_logits, ld_logits, sg_col,
+      (const __nv_bfloat16*)resid, (__nv_bfloat16*)out, T, H);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------ SwiGLU (dense)
+// x [T, 2I] = [gate | up] -> y [T, I] = silu(gate) * up
+__global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int T, int I) {
+  const size_t i8 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i8 >= (size_t)T * I) return;
+  const size_t t = i8 / I, c = i8 % I;
+  uint4 g = *reinterpret_cast<const uint4*>(x + t * 2 * I + c);
+  uint4 u = *reinterpret_cast<const uint4*>(x + t * 2 * I + I + c);
+  const __nv_bfloat16* gh = reinterpret_cast<const __nv_bfloat16*>(&g);
+  const __nv_bfloat16* uh = reinterpret_cast<const __nv_bfloat16*>(&u);
+  float o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = silu(__bfloat162float(gh[j])) * __bfloat162float(uh[j]);
+  *reinterpret_cast<uint4*>(y + t * I + c) =
+      make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+}
+
+int swiglu(const void* x, void* y, int T, int I, cudaStream_t st) {
+  if (I % 8) return 3;
+  const size_t n = (size_t)T * I / 8;
+  if (!n) return 0;
+  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)y, T, I);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------ embedding
+__global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                                 __nv_bfloat16* __restrict__ out, int T, int H, int V, uint32_t* status) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  if (id < 0 || id >= V) {
+    flag_error(status, AFB_ERR_BOUNDS);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+int embedding(const int* ids, const void* table, void* out, int T, int H, int V, uint32_t* status, cudaStream_t st) {
+  if (H % 8) return 3;
+  if (!T) return 0;
+  embedding_kernel<<<T, 128, 0, st>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, H, V, status);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace afb

@@ -1,0 +1,273 @@
+// Dense bf16 GEMM on the 5th-gen tensor cores: C[M,N] = alpha * A[M,K] * B[N,K]^T (+ residual).
+//
+// Both operands are K-major (nn.Linear layout). One CTA computes a 128 x BN tile:
+//   warp 0      one elected thread issues TMA loads (128-byte swizzle) into a STAGES-deep ring
+//   warp 1      allocates TMEM and one elected thread issues tcgen05.mma (M=128, N=BN, K=16 per op)
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, convert, optional residual add, store
+// Split-K (gridDim.z > 1) writes fp32 partials that a reduce kernel sums in a fixed order.
+// Used for every dense projection of the serving and training paths (QKV/in_proj, o_proj/out_proj,
+// shared expert, router, LM head) in place of the reference's cuBLAS/CUTLASS dense GEMMs.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm.h"
+
+namespace afb {
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t BAR_OFF = STAGES * (A_BYTES + B_BYTES);
+  static constexpr uint32_t TOTAL = BAR_OFF + (2 * STAGES + 1) * 8 + 16 + 1024;  // +1024 for manual alignment
+  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                        int K, GemmEpilogue epi, uint32_t* status) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_n = blockIdx.x, tile_m = blockIdx.y;
+  // split-K range of this CTA
+  const int num_kb_total = (K + S::BK - 1) / S::BK;
+  const int splits = gridDim.z;
+  const int kb_per = (num_kb_total + splits - 1) / splits;
+  const int kb0 = blockIdx.z * kb_per;
+  const int kb1 = min(num_kb_total, kb0 + kb_per);
+  const int num_kb = max(0, kb1 - kb0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int issued = 0;
+      for (int i = 0; i < num_kb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (i >= STAGES && !mbar_wait(&empty[s], ph ^ 1, status)) break;
+        mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
+        tma_load_2d(sA + s * S::A_BYTES, &tmA, &full[s], (kb0 + i) * S::BK, tile_m * S::BM);
+        tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], (kb0 + i) * S::BK, tile_n * BN);
+        ++issued;
+      }
+      // drain: every issued copy has landed before the CTA may exit (bounded)
+      for (int i = max(0, issued - STAGES); i < issued; ++i) mbar_wait(&full[i % STAGES], (i / STAGES) & 1, status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(128, BN, 1);
+      for (int i = 0; i < num_kb; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&full[s], (i / STAGES) & 1, status)) break;
+        tc_fence_after();
+        const uint64_t da = sw128_desc(smem_u32(sA + s * S::A_BYTES));
+        const uint64_t db = sw128_desc(smem_u32(sB + s * S::B_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < S::BK / 16; ++kk) {
+          // +32 bytes along K per MMA: the descriptor's start address is in 16-byte units
+          umma_f16(tmem, da + 2 * kk, db + 2 * kk, idesc, (i | kk) != 0);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(done);  // also covers the error path: the epilogue waits for every issued MMA
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    const int quad = warp & 3;
+    const bool ok = mbar_wait(done, 0, status);
+    tc_fence_after();
+    const int row = tile_m * S::BM + quad * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(taddr + c, v);
+      tmem_ld_wait();
+      const int col0 = tile_n * BN + c;
+      if (!ok || row >= M || col0 >= N) continue;
+      if (num_kb == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;  // an empty split-K slice contributes zeros
+      }
+      if (splits > 1) {
+        float* out = reinterpret_cast<float*>(epi.partial) + ((size_t)blockIdx.z * M + row) * N + col0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          if (col0 + j < N) *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        continue;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= epi.alpha;
+      if (epi.residual) {
+        const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(epi.residual) + (size_t)row * epi.ldr + col0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          if (col0 + j >= N) break;
+          uint4 q = *reinterpret_cast<const uint4*>(r + j);
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) v[j + t] += __bfloat162float(h[t]);
+        }
+      }
+      if (epi.out_fp32) {
+        float* out = reinterpret_cast<float*>(epi.out) + (size_t)row * epi.ldo + col0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          if (col0 + j < N) *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      } else {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(epi.out) + (size_t)row * epi.ldo + col0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          if (col0 + j >= N) break;
+          uint4 q = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                               pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+          *reinterpret_cast<uint4*>(out + j) = q;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+// Fixed-order sum of split-K partials [splits, M, N] fp32 -> out (+ residual), alpha applied.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, GemmEpilogue epi) {
+  const size_t idx = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const size_t total = (size_t)M * N;
+  if (idx >= total) return;
+  const int row = idx / N, col = idx % N;
+  float4 acc = *reinterpret_cast<const float4*>(part + idx);
+  for (int s = 1; s < splits; ++s) {
+    float4 p = *reinterpret_cast<const float4*>(part + (size_t)s * total + idx);
+    acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+  }
+  float v[4] = {acc.x * epi.alpha, acc.y * epi.alpha, acc.z * epi.alpha, acc.w * epi.alpha};
+  if (epi.residual) {
+    const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(epi.residual) + (size_t)row * epi.ldr + col;
+    for (int t = 0; t < 4; ++t) v[t] += __bfloat162float(r[t]);
+  }
+  if (epi.out_fp32) {
+    float* o = reinterpret_cast<float*>(epi.out) + (size_t)row * epi.ldo + col;
+    *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(epi.out) + (size_t)row * epi.ldo + col;
+    *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  }
+}
+
+// ------------------------------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, int dtype_bytes, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle128) {
+  auto encode = get_encode();
+  if (!encode) return -1;
+  CUtensorMapDataType dt = dtype_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                           : dtype_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                              : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+template <int BN, int STAGES>
+static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int splits,
+                       const GemmEpilogue& epi, uint32_t* status, cudaStream_t stream) {
+  using S = GemmSmem<BN, STAGES>;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, 2, K, M, (uint64_t)lda * 2, S::BK, S::BM, 1);
+  if (rc) return 1000 + rc;
+  rc = make_tmap_2d(&tb, B, 2, K, N, (uint64_t)ldb * 2, S::BK, BN, 1);
+  if (rc) return 2000 + rc;
+  auto kern = gemm_bf16_tn_kernel<BN, STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+    attr = true;
+  }
+  dim3 grid((N + BN - 1) / BN, (M + S::BM - 1) / S::BM, splits);
+  kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, M, N, K, epi, status);
+  return (int)cudaGetLastError();
+}
+
+// Tile/split choice: fill 148 SMs (two CTAs fit per SM at BN<=128 with 3-4 stages).
+GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
+  GemmPlan p;
+  const int mt = (M + 127) / 128;
+  const int t128 = mt * ((N + 127) / 128);
+  p.bn = (t128 >= num_sms) ? 128 : 64;
+  const int tiles = mt * ((N + p.bn - 1) / p.bn);
+  const int kb = (K + 63) / 64;
+  p.splits = 1;
+  while (tiles * p.splits * 2 <= 2 * num_sms && kb / (p.splits * 2) >= 4 && p.splits < 8) p.splits *= 2;
+  return p;
+}
+
+int gemm_bf16_tn(const void* A, int lda, const void* B, int ldb, int M, int N, int K, const GemmEpilogue& epi,
+                 int bn, int splits, uint32_t* status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((K % 8) || (N % 8) || (lda % 8) || (ldb % 8)) return 3;
+  if (splits > 1 && !epi.partial) return 4;
+  int rc;
+  if (bn == 128)
+    rc = launch_gemm<128, 3>(A, lda, B, ldb, M, N, K, splits, epi, status, stream);
+  else if (bn == 256)
+    rc = launch_gemm<256, 4>(A, lda, B, ldb, M, N, K, splits, epi, status, stream);
+  else
+    rc = launch_gemm<64, 4>(A, lda, B, ldb, M, N, K, splits, epi, status, stream);
+  if (rc || splits <= 1) return rc;
+  const size_t total = (size_t)M * N;
+  const int threads = 256;
+  const int blocks = (int)((total / 4 + threads - 1) / threads);
+  splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(reinterpret_cast<const float*>(epi.partial), splits, M, N, epi);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace afb
