@@ -20,8 +20,8 @@
 #define AFB_ERR_BOUNDS 0x4u
 #define AFB_ERR_TMEM 0x8u
 
-#ifndef AFB_SPIN_LIMIT
-#define AFB_SPIN_LIMIT (1u << 26)  // ~1-2 s of polling with backoff
+#ifndef AFB_WAIT_NS
+#define AFB_WAIT_NS 2000000000ull  // bounded waits give up after 2 s (globaltimer)
 #endif
 
 namespace afb {
@@ -56,11 +56,23 @@ AFB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on a phase parity. Returns false (and flags the status word) on timeout.
+AFB_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait on a phase parity: spins (try_wait suspends in hardware between polls), checks the clock every
+// 1024 polls and gives up after AFB_WAIT_NS. Returns false (and flags the status word) on timeout.
 AFB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
-  for (uint32_t i = 0; i < AFB_SPIN_LIMIT; ++i) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(i > 4096 ? 256 : 32);
+    if ((i & 1023u) == 1023u) {
+      const uint64_t now = globaltimer_ns();
+      if (!t0) t0 = now;
+      else if (now - t0 > AFB_WAIT_NS) break;
+      if (i > (1u << 16)) __nanosleep(64);
+    }
   }
   flag_error(status, AFB_ERR_MBAR_TIMEOUT);
   return false;

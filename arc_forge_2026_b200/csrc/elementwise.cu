@@ -223,38 +223,48 @@ int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, in
 
 // ------------------------------------------------------------------------------------------ expert sort
 // Stable counting sort of the T*k (token, slot) entries by expert, in one CTA of 1024 threads:
-// entry i -> position offsets[e] + (# entries i' < i with the same expert). Outputs:
-//   offsets [E+1] (exclusive scan of counts), row_token [T*k] (token of each sorted row),
-//   row_entry [T*k] (entry index t*k+j of each sorted row), entry_row [T*k] (inverse).
+// entry i -> position offsets[e] + (# entries i' < i with the same expert). Each expert's segment starts on a
+// multiple of `pad` rows (the expert GEMM moves per-segment scale vectors with 16-byte bulk copies); pad rows
+// get row_token 0 and row_entry -1. Outputs:
+//   offsets [E+1] (segment starts; offsets[E] = rows used), row_token [rows] (token of each sorted row),
+//   row_entry [rows] (entry index t*k+j), entry_row [T*k] (inverse; -1 if the expert is not local).
 // `expert_map` (optional) maps global expert ids to local ones (-1 = not on this rank) for EP.
 __global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict__ ids, int n, int E,
                                                            const int* __restrict__ expert_map, int* __restrict__ offsets,
                                                            int* __restrict__ row_token, int* __restrict__ row_entry,
-                                                           int* __restrict__ entry_row, int k) {
+                                                           int* __restrict__ entry_row, int k, int pad) {
   extern __shared__ int sm[];
   int* cnt = sm;             // [E] running base per expert
   int* hist = sm + E;        // [32 warps][E] per-warp counts of the current chunk
+  int* ccount = sm + 33 * E; // [E] counts
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) ccount[e] = 0;
   __syncthreads();
-  // pass 1: counts
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     int e = ids[i];
     if (expert_map) e = expert_map[e];
-    if (e >= 0) atomicAdd(&cnt[e], 1);
+    if (e >= 0) atomicAdd(&ccount[e], 1);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     int acc = 0;
     for (int e = 0; e < E; ++e) {
       offsets[e] = acc;
-      acc += cnt[e];
-      cnt[e] = offsets[e];
+      cnt[e] = acc;
+      acc += (ccount[e] + pad - 1) / pad * pad;
     }
     offsets[E] = acc;
   }
   __syncthreads();
-  // pass 2: stable positions, chunk of 1024 entries at a time
+  // pad rows
+  for (int e = warp; e < E; e += 32) {
+    const int start = offsets[e] + ccount[e], end = offsets[e + 1];
+    for (int r = start + lane; r < end; r += 32) {
+      row_token[r] = 0;
+      row_entry[r] = -1;
+    }
+  }
+  // stable positions, chunk of 1024 entries at a time
   for (int base = 0; base < n; base += blockDim.x) {
     for (int x = threadIdx.x; x < 32 * E; x += blockDim.x) hist[x] = 0;
     __syncthreads();
@@ -268,7 +278,6 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict
     const int rank_in_warp = __popc(peers & ((1u << lane) - 1));
     if (e >= 0 && rank_in_warp == 0) hist[warp * E + e] = __popc(peers);
     __syncthreads();
-    // exclusive prefix over warps per expert (in place), then add the running base
     for (int x = threadIdx.x; x < E; x += blockDim.x) {
       int acc = cnt[x];
       for (int w = 0; w < 32; ++w) {
@@ -292,24 +301,26 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict
 }
 
 int expert_sort(const int* ids, int n, int E, const int* expert_map, int* offsets, int* row_token, int* row_entry,
-                int* entry_row, int k, cudaStream_t st) {
-  const size_t smem = (size_t)(E + 32 * E) * sizeof(int);
+                int* entry_row, int k, int pad, cudaStream_t st) {
+  const size_t smem = (size_t)(34 * E) * sizeof(int);
   if (smem > 200 * 1024) return 3;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(expert_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
-  expert_sort_kernel<<<1, 1024, smem, st>>>(ids, n, E, expert_map, offsets, row_token, row_entry, entry_row, k);
+  expert_sort_kernel<<<1, 1024, smem, st>>>(ids, n, E, expert_map, offsets, row_token, row_entry, entry_row, k,
+                                              pad < 1 ? 1 : pad);
   return (int)cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------------ fp8 group quant + gather
 // out_q[r, :] = e4m3(x[src(r), :] / s), s = amax/448 per 128-column group (1 if the group is all zero);
-// src(r) = row_token[r] when given, else r. One warp per (row, group): lane owns 4 consecutive values.
+// src(r) = row_token[r] when given, else r. Scales are row-major [rows, K/128], or group-major
+// [K/128, ld_s] when ld_s > 0 (the layout the expert GEMM reads). One warp per (row, group): lane owns 4 consecutive values.
 __global__ void quant_rows_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const int* __restrict__ row_token,
                                        const int* __restrict__ nrows_dev, int nrows, int K,
-                                       __nv_fp8_e4m3* __restrict__ q, float* __restrict__ scales) {
+                                       __nv_fp8_e4m3* __restrict__ q, float* __restrict__ scales, int ld_s) {
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int groups = K / 128;
@@ -332,17 +343,17 @@ __global__ void quant_rows_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int 
   const float inv = 1.f / s;
   __nv_fp8x4_e4m3 o(make_float4(f[0] * inv, f[1] * inv, f[2] * inv, f[3] * inv));
   *reinterpret_cast<__nv_fp8x4_e4m3*>(q + (size_t)r * K + g * 128 + lane * 4) = o;
-  if (lane == 0) scales[(size_t)r * groups + g] = s;
+  if (lane == 0) scales[ld_s > 0 ? (size_t)g * ld_s + r : (size_t)r * groups + g] = s;
 }
 
 int quant_rows_e4m3(const void* x, int ldx, const int* row_token, const int* nrows_dev, int nrows, int K, void* q,
-                    float* scales, cudaStream_t st) {
+                    float* scales, int ld_s, cudaStream_t st) {
   if (K % 128) return 3;
   const int warps = 8;
   const long total = (long)nrows * (K / 128);
   if (total == 0) return 0;
   quant_rows_e4m3_kernel<<<(unsigned)((total + warps - 1) / warps), warps * 32, 0, st>>>(
-      (const __nv_bfloat16*)x, ldx, row_token, nrows_dev, nrows, K, (__nv_fp8_e4m3*)q, scales);
+      (const __nv_bfloat16*)x, ldx, row_token, nrows_dev, nrows, K, (__nv_fp8_e4m3*)q, scales, ld_s);
   return (int)cudaGetLastError();
 }
 

@@ -2,6 +2,7 @@
 // Every launcher returns 0 on success, 3 for an unsupported shape, or a cudaError_t code.
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stdint.h>
 
 namespace afb {
@@ -15,12 +16,57 @@ int qk_norm_rope_store(const void* qkv, int T, int Hq, int Hkv, int D, int rot, 
 int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, int* ids, float* weights,
                 cudaStream_t st);
 int expert_sort(const int* ids, int n, int E, const int* expert_map, int* offsets, int* row_token, int* row_entry,
-                int* entry_row, int k, cudaStream_t st);
+                int* entry_row, int k, int pad, cudaStream_t st);
 int quant_rows_e4m3(const void* x, int ldx, const int* row_token, const int* nrows_dev, int nrows, int K, void* q,
-                    float* scales, cudaStream_t st);
+                    float* scales, int ld_s, cudaStream_t st);
 int moe_combine(const void* y, const int* entry_row, int k, const void* shared, const float* router_logits,
                 int ld_logits, int sg_col, const void* resid, void* out, int T, int H, cudaStream_t st);
 int swiglu(const void* x, void* y, int T, int I, cudaStream_t st);
 int embedding(const int* ids, const void* table, void* out, int T, int H, int V, uint32_t* status, cudaStream_t st);
+
+// attention.cu
+struct AttnArgs {
+  const __nv_bfloat16* q = nullptr;  // [num_tokens, Hq, D], num_tokens = num_seqs * q_per_seq
+  const void* kcache = nullptr;      // [num_pages, Hkv, 64, D] bf16
+  const void* vcache = nullptr;
+  int num_pages = 0;
+  const int* block_table = nullptr;  // [num_seqs, max_pages]
+  int max_pages = 0;
+  const int* seq_lens = nullptr;     // [num_seqs], including the q_per_seq new tokens
+  int num_seqs = 0, q_per_seq = 1, num_tokens = 0;
+  int Hq = 0, Hkv = 0, D = 0;
+  float scale_log2 = 0.f;            // softmax scale * log2(e)
+  int pages_per_split = 1 << 30;
+  const __nv_bfloat16* gate = nullptr;  // optional output gate: out *= sigmoid(gate[tok*gate_ld + head*stride + d])
+  int gate_ld = 0, gate_head_stride = 0;
+  __nv_bfloat16* out = nullptr;         // [num_tokens, Hq, D]
+  float* part_o = nullptr;              // [splits, num_tokens, Hq, D]
+  float* part_lse = nullptr;            // [splits, num_tokens, Hq]
+};
+int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st);
+
+// gdn.cu
+struct GdnArgs {
+  const __nv_bfloat16* mixed = nullptr;  // in_proj output [tokens, mixed_ld]: [q|k|v] conv channels, z, b, a
+  int mixed_ld = 0, z_off = 0, ba_off = 0;
+  const float* conv_w = nullptr;         // [C, 4]
+  __nv_bfloat16* conv_state = nullptr;   // [slots, 3, C]
+  float* ssm_state = nullptr;            // [slots, Hv, Dk, Dv]
+  __nv_bfloat16* pend_in = nullptr;      // [2, pend_slots, max_q, C]
+  __nv_bfloat16* pend_qk = nullptr;      // [2, pend_slots, max_q, 2*Hk*Dk]
+  __nv_bfloat16* pend_v = nullptr;       // [2, pend_slots, max_q, Hv*Dv]
+  float* pend_gb = nullptr;              // [2, pend_slots, max_q, 2*Hv] (g, beta)
+  const int* n_commit = nullptr;         // [slots] accepted tokens of the previous cycle
+  const int* seq_slot = nullptr;         // [num_seqs]
+  const float* A_log = nullptr;
+  const float* dt_bias = nullptr;
+  const __nv_bfloat16* norm_w = nullptr; // [Dv]
+  __nv_bfloat16* out = nullptr;          // [tokens, Hv*Dv]
+  int num_seqs = 0, q_per_seq = 1, max_q = 1, num_slots = 0, pend_slots = 0;
+  int conv_dim = 0, Hk = 0, Hv = 0, Dk = 0, Dv = 0;
+  int commit_current = 0;
+  float eps = 1e-6f;
+};
+int gdn_decode(const GdnArgs& a, int parity, cudaStream_t st);
 
 }  // namespace afb

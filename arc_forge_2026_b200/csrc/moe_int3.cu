@@ -159,24 +159,22 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           uint8_t* st = smem + s * L::STAGE;
-          // activation scales of this group for the chunk's tokens (group-major layout)
-          float sx = 0.f;
-          if (lane < cn) sx = args.x_scales[(size_t)g * args.ld_xs + crow + lane];
-          reinterpret_cast<float*>(st + L::SX_OFF)[lane] = sx;
-          __syncwarp();
           if (lane == 0) {
-            const uint32_t bytes = L::T * (moe::CODE_TILE + 256) + moe::X_TILE;
+            // activation scales of this group for the chunk's 32 rows (group-major, segment starts are 8-aligned)
+            const uint32_t bytes = L::T * (moe::CODE_TILE + 256) + moe::X_TILE + moe::NTOK * 4;
             mbar_arrive_expect_tx(&full[s], bytes);
+            bulk_g2s(st + L::SX_OFF, args.x_scales + (size_t)g * args.ld_xs + crow, moe::NTOK * 4, &full[s]);
 #pragma unroll
             for (int t = 0; t < L::T; ++t) {
               const int rb = PAIR ? (t == 0 ? j : NB + j) : j;  // gate block j, up block NB + j
               const size_t tile = ((size_t)e * (args.rows / 128) + rb) * KG + g;
               bulk_g2s(st + L::C_OFF + t * moe::CODE_TILE, args.codes + tile * (moe::CODE_TILE / 4), moe::CODE_TILE,
                        &full[s]);
-              bulk_g2s(st + L::SW_OFF + t * 256, args.scales + tile * 128, 256, &full[s]);
+              bulk_g2s(st + L::SW_OFF + t * 256, reinterpret_cast<const uint16_t*>(args.scales) + tile * 128, 256, &full[s]);
             }
             tma_load_2d(st + L::X_OFF, &tmX, &full[s], g * 128, crow);
           }
+          __syncwarp();
         }
       } else if (warp >= 1 && warp <= 4) {
         // ---------------------------------------------------------------- dequant
@@ -298,7 +296,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int i = 0; i < moe::NTOK; ++i) {
             if (i >= cn) break;
             const float w = args.route_w ? args.route_w[args.row_entry[crow + i]] : 1.f;
-            args.out_bf16[(size_t)(crow + i) * args.out_ld + col] = __float2bfloat16(acc0[i] * w);
+            reinterpret_cast<__nv_bfloat16*>(args.out_bf16)[(size_t)(crow + i) * args.out_ld + col] = __float2bfloat16(acc0[i] * w);
           }
         }
       }

@@ -1,6 +1,7 @@
 // Bindings of the elementwise / routing / attention / GDN / sampling kernels.
 #include "binding_utils.h"
 #include "kernels.h"
+#include "moe.h"
 
 using namespace afb_bind;
 
@@ -47,22 +48,72 @@ void router_topk_op(const at::Tensor& logits, int64_t E, int64_t k, bool renorm,
 }
 
 void expert_sort_op(const at::Tensor& ids, int64_t E, c10::optional<at::Tensor> expert_map, at::Tensor& offsets,
-                    at::Tensor& row_token, at::Tensor& row_entry, at::Tensor& entry_row) {
+                    at::Tensor& row_token, at::Tensor& row_entry, at::Tensor& entry_row, int64_t pad) {
   AFB_CHECK_DT(ids, at::kInt);
   AFB_CHECK_CONTIG(ids);
   const int k = ids.size(-1);
+  TORCH_CHECK(row_token.numel() >= ids.numel() + (pad - 1) * E, "row_token capacity must cover the padding");
   check_rc(afb::expert_sort(ptr<int>(ids), ids.numel(), E, optr<int>(expert_map), ptr<int>(offsets),
-                            ptr<int>(row_token), ptr<int>(row_entry), ptr<int>(entry_row), k, stream()),
+                            ptr<int>(row_token), ptr<int>(row_entry), ptr<int>(entry_row), k, (int)pad, stream()),
            "expert_sort");
 }
 
 void quant_rows_e4m3_op(const at::Tensor& x, c10::optional<at::Tensor> row_token, c10::optional<at::Tensor> nrows_dev,
-                        int64_t nrows, at::Tensor& q, at::Tensor& scales) {
+                        int64_t nrows, at::Tensor& q, at::Tensor& scales, bool group_major) {
   AFB_CHECK_DT(x, at::kBFloat16);
   TORCH_CHECK(x.stride(-1) == 1, "x inner stride");
-  check_rc(afb::quant_rows_e4m3(x.data_ptr(), x.stride(0), optr<int>(row_token), optr<int>(nrows_dev), nrows,
-                                x.size(1), q.data_ptr(), ptr<float>(scales), stream()),
+  const int K = x.size(1);
+  if (group_major) TORCH_CHECK(scales.size(0) == K / 128 && scales.size(1) >= nrows, "group-major scales shape");
+  check_rc(afb::quant_rows_e4m3(x.data_ptr(), x.stride(0), optr<int>(row_token), optr<int>(nrows_dev), nrows, K,
+                                q.data_ptr(), ptr<float>(scales), group_major ? (int)scales.stride(0) : 0, stream()),
            "quant_rows_e4m3");
+}
+
+// INT3 grouped expert GEMM. pair=True: w13 with SwiGLU + e4m3 requant (out_q, out_scales group-major);
+// pair=False: w2 with the routing weight (out_bf16).
+void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& offsets,
+                      const at::Tensor& x_q, const at::Tensor& x_scales, bool pair, c10::optional<at::Tensor> out_q,
+                      c10::optional<at::Tensor> out_scales, c10::optional<at::Tensor> out_bf16,
+                      c10::optional<at::Tensor> route_w, c10::optional<at::Tensor> row_entry) {
+  AFB_CHECK_DT(codes, at::kInt);
+  AFB_CHECK_DT(scales, at::kBFloat16);
+  AFB_CHECK_DT(offsets, at::kInt);
+  AFB_CHECK_CONTIG(codes);
+  AFB_CHECK_CONTIG(scales);
+  AFB_CHECK_CONTIG(x_q);
+  TORCH_CHECK(codes.dim() == 5 && codes.size(3) == 128 && codes.size(4) == 12, "codes must be tile layout");
+  afb::MoeGemmArgs a;
+  a.codes = ptr<int32_t>(codes);
+  a.scales = scales.data_ptr();
+  a.num_experts = codes.size(0);
+  a.rows = codes.size(1) * 128;
+  a.K = codes.size(2) * 128;
+  TORCH_CHECK(offsets.numel() == a.num_experts + 1, "offsets must have E+1 entries");
+  TORCH_CHECK(x_q.size(1) == a.K, "x_q width");
+  a.expert_offsets = ptr<int>(offsets);
+  a.x_q = x_q.data_ptr();
+  a.x_scales = ptr<float>(x_scales);
+  a.ld_xs = x_scales.stride(0);
+  a.num_rows_total = x_q.size(0);
+  TORCH_CHECK(a.ld_xs % 4 == 0 && x_scales.size(1) >= a.num_rows_total + 32,
+              "x_scales must be group-major [K/128, >= rows + 32] with a row stride divisible by 4");
+  if (pair) {
+    TORCH_CHECK(out_q.has_value() && out_scales.has_value(), "pair needs out_q and out_scales");
+    a.out_q = optr<uint8_t>(out_q);
+    a.out_scales = optr<float>(out_scales);
+    a.ld_os = out_scales->stride(0);
+    TORCH_CHECK(out_scales->size(1) >= a.num_rows_total, "out_scales capacity");
+    a.out_ld = out_q->stride(0);
+    TORCH_CHECK(out_q->size(1) == a.rows / 2, "out_q width must be I");
+  } else {
+    TORCH_CHECK(out_bf16.has_value(), "w2 needs out_bf16");
+    a.out_bf16 = out_bf16->data_ptr();
+    a.out_ld = out_bf16->stride(0);
+    a.route_w = optr<float>(route_w);
+    a.row_entry = optr<int>(row_entry);
+    TORCH_CHECK(!a.route_w || a.row_entry, "route_w needs row_entry");
+  }
+  check_rc(afb::moe_int3_gemm(a, pair, num_sms(), status_ptr(codes.get_device()), stream()), "moe_int3_gemm");
 }
 
 void moe_combine_op(const at::Tensor& y, const at::Tensor& entry_row, int64_t k, c10::optional<at::Tensor> shared,
@@ -73,6 +124,102 @@ void moe_combine_op(const at::Tensor& y, const at::Tensor& entry_row, int64_t k,
   check_rc(afb::moe_combine(y.data_ptr(), ptr<int>(entry_row), k, optr<void>(shared), optr<float>(router_logits), ld,
                             sg_col, optr<void>(resid), out.data_ptr(), T, H, stream()),
            "moe_combine");
+}
+
+// Paged decode/verify attention. gate (optional): a strided view whose element (tok, head, d) sits at
+// gate.data_ptr() + tok * gate_ld + head * gate_head_stride + d.
+void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
+                        const at::Tensor& block_table, const at::Tensor& seq_lens, int64_t q_per_seq, double scale,
+                        at::Tensor& out, c10::optional<at::Tensor> gate, int64_t gate_ld, int64_t gate_head_stride,
+                        int64_t splits, int64_t pages_per_split) {
+  AFB_CHECK_DT(q, at::kBFloat16);
+  AFB_CHECK_CONTIG(q);
+  AFB_CHECK_CONTIG(kcache);
+  AFB_CHECK_CONTIG(out);
+  AFB_CHECK_DT(block_table, at::kInt);
+  AFB_CHECK_DT(seq_lens, at::kInt);
+  TORCH_CHECK(kcache.dim() == 4 && kcache.size(2) == 64, "kv cache must be [pages, Hkv, 64, D]");
+  afb::AttnArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.kcache = kcache.data_ptr();
+  a.vcache = vcache.data_ptr();
+  a.num_pages = kcache.size(0);
+  a.Hkv = kcache.size(1);
+  a.D = kcache.size(3);
+  a.Hq = q.size(1);
+  a.block_table = ptr<int>(block_table);
+  a.max_pages = block_table.size(1);
+  a.seq_lens = ptr<int>(seq_lens);
+  a.num_seqs = seq_lens.size(0);
+  a.q_per_seq = q_per_seq;
+  a.num_tokens = q.size(0);
+  TORCH_CHECK(a.num_tokens == a.num_seqs * q_per_seq, "q rows must be num_seqs * q_per_seq");
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.pages_per_split = (int)pages_per_split;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (gate.has_value()) {
+    a.gate = reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr());
+    a.gate_ld = gate_ld;
+    a.gate_head_stride = gate_head_stride;
+  }
+  at::Tensor po, pl;
+  if (splits > 1) {
+    po = torch::empty({splits, a.num_tokens, a.Hq, a.D}, q.options().dtype(at::kFloat));
+    pl = torch::empty({splits, a.num_tokens, a.Hq}, q.options().dtype(at::kFloat));
+    a.part_o = ptr<float>(po);
+    a.part_lse = ptr<float>(pl);
+  }
+  check_rc(afb::paged_attention(a, (int)splits, status_ptr(q.get_device()), stream()), "paged_attention");
+}
+
+// GDN decode/verify (see gdn.cu). pend: (pend_in, pend_qk, pend_v, pend_gb) with a leading parity dim of 2.
+void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const at::Tensor& conv_w,
+                   at::Tensor& conv_state, at::Tensor& ssm_state, at::Tensor& pend_in, at::Tensor& pend_qk,
+                   at::Tensor& pend_v, at::Tensor& pend_gb, const at::Tensor& n_commit, const at::Tensor& seq_slot,
+                   const at::Tensor& A_log, const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor& out,
+                   int64_t q_per_seq, int64_t Hk, int64_t Dk, int64_t Hv, int64_t Dv, bool commit_current,
+                   int64_t parity, double eps) {
+  AFB_CHECK_DT(mixed, at::kBFloat16);
+  AFB_CHECK_DT(ssm_state, at::kFloat);
+  AFB_CHECK_DT(conv_w, at::kFloat);
+  AFB_CHECK_DT(seq_slot, at::kInt);
+  AFB_CHECK_DT(n_commit, at::kInt);
+  TORCH_CHECK(mixed.stride(1) == 1, "mixed inner stride");
+  afb::GdnArgs a;
+  a.mixed = reinterpret_cast<const __nv_bfloat16*>(mixed.data_ptr());
+  a.mixed_ld = mixed.stride(0);
+  a.z_off = z_off;
+  a.ba_off = ba_off;
+  a.conv_w = ptr<float>(conv_w);
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.ssm_state = ptr<float>(ssm_state);
+  a.pend_in = reinterpret_cast<__nv_bfloat16*>(pend_in.data_ptr());
+  a.pend_qk = reinterpret_cast<__nv_bfloat16*>(pend_qk.data_ptr());
+  a.pend_v = reinterpret_cast<__nv_bfloat16*>(pend_v.data_ptr());
+  a.pend_gb = ptr<float>(pend_gb);
+  a.n_commit = ptr<int>(n_commit);
+  a.seq_slot = ptr<int>(seq_slot);
+  a.A_log = ptr<float>(A_log);
+  a.dt_bias = ptr<float>(dt_bias);
+  a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.num_seqs = seq_slot.size(0);
+  a.q_per_seq = q_per_seq;
+  a.pend_slots = pend_in.size(1);
+  a.max_q = pend_in.size(2);
+  a.num_slots = ssm_state.size(0);
+  a.conv_dim = conv_w.size(0);
+  a.Hk = Hk;
+  a.Hv = Hv;
+  a.Dk = Dk;
+  a.Dv = Dv;
+  a.commit_current = commit_current;
+  a.eps = (float)eps;
+  TORCH_CHECK(mixed.size(0) == a.num_seqs * q_per_seq, "mixed rows must be num_seqs * q_per_seq");
+  TORCH_CHECK(a.conv_dim == 2 * Hk * Dk + Hv * Dv, "conv_dim");
+  TORCH_CHECK(pend_in.size(0) == 2 && pend_in.size(3) == a.conv_dim, "pend_in shape");
+  TORCH_CHECK(!commit_current || a.pend_slots >= a.num_seqs, "prefill scratch needs one pending slot per sequence");
+  check_rc(afb::gdn_decode(a, (int)parity, stream()), "gdn_decode");
 }
 
 void swiglu_op(const at::Tensor& x, at::Tensor& y) {
@@ -96,6 +243,9 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("expert_sort", &expert_sort_op);
   m.def("quant_rows_e4m3", &quant_rows_e4m3_op);
   m.def("moe_combine", &moe_combine_op);
+  m.def("moe_int3_gemm", &moe_int3_gemm_op);
   m.def("swiglu", &swiglu_op);
+  m.def("gdn_decode", &gdn_decode_op);
+  m.def("paged_attention", &paged_attention_op);
   m.def("embedding", &embedding_op);
 }

@@ -1,0 +1,59 @@
+"""Paged decode / verify attention on the native kernel, its split heuristic, and the fp32 oracle."""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._ext import C
+
+PAGE = 64
+
+
+def plan_splits(num_seqs: int, Hkv: int, max_pages: int, num_sms: int = 148) -> tuple[int, int]:
+    """Split KV so that the grid covers ~2 waves of SMs with >= 8 pages per split."""
+    ctas = max(1, num_seqs * Hkv)
+    splits = 1
+    while ctas * splits < 2 * num_sms and math.ceil(max_pages / (splits * 2)) >= 8:
+        splits *= 2
+    pps = math.ceil(max(1, max_pages) / splits)
+    return math.ceil(max(1, max_pages) / pps), pps
+
+
+def paged_attention(q, kcache, vcache, block_table, seq_lens, q_per_seq, out, gate=None, gate_ld=0,
+                    gate_head_stride=0, splits=None, max_pages=None):
+    D = q.shape[-1]
+    if splits is None:
+        mp = max_pages if max_pages is not None else block_table.shape[1]
+        splits, pps = plan_splits(seq_lens.shape[0], kcache.shape[1], mp)
+    else:
+        pps = math.ceil(block_table.shape[1] / splits)
+    C().paged_attention(q, kcache, vcache, block_table, seq_lens, q_per_seq, 1.0 / math.sqrt(D), out, gate,
+                        gate_ld, gate_head_stride, splits, pps)
+    return out
+
+
+def paged_attention_reference(q, kcache, vcache, block_table, seq_lens, q_per_seq, gate=None):
+    """fp32 oracle. q [S*qp, Hq, D]; gate [S*qp, Hq, D] or None."""
+    S = seq_lens.shape[0]
+    Hq, D = q.shape[1], q.shape[2]
+    Hkv = kcache.shape[1]
+    rep = Hq // Hkv
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    for s in range(S):
+        L = int(seq_lens[s])
+        pages = block_table[s, : (L + PAGE - 1) // PAGE].long()
+        k = kcache[pages].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :L].float()
+        v = vcache[pages].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :L].float()
+        qq = q[s * q_per_seq:(s + 1) * q_per_seq].float()  # [qp, Hq, D]
+        kk = k.repeat_interleave(rep, 0)
+        vv = v.repeat_interleave(rep, 0)
+        sc = torch.einsum("thd,hld->htl", qq, kk) / math.sqrt(D)
+        pos = torch.arange(L - q_per_seq, L, device=q.device)
+        mask = torch.arange(L, device=q.device)[None, :] > pos[:, None]
+        sc = sc.masked_fill(mask[None], float("-inf"))
+        o = torch.einsum("htl,hld->thd", torch.softmax(sc, -1), vv)
+        out[s * q_per_seq:(s + 1) * q_per_seq] = o
+    if gate is not None:
+        out = out * torch.sigmoid(gate.float())
+    return out

@@ -1,0 +1,116 @@
+"""Kernel micro-benchmarks (CUDA events, warm-up, L2 flushed between timed launches).
+
+    python -m arc_forge_2026_b200.utils.kbench moe      # INT3 w13/w2 expert GEMMs at the verify-step shape
+    python -m arc_forge_2026_b200.utils.kbench gemm     # dense bf16 GEMMs of the decode step
+
+Prints one JSON line per kernel: time, bytes, FLOPs and the fraction of MEASURED_PEAKS.json.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+PEAKS = {"hbm_gbs": 6554.9, "bf16_tflops": 1668.7}
+
+
+def load_peaks(path: str | None = None):
+    path = path or os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"]}
+    except (OSError, KeyError, ValueError):
+        return dict(PEAKS)
+
+
+def time_cuda(fn, iters: int = 20, warmup: int = 3, flush_bytes: int = 256 << 20) -> float:
+    """Median milliseconds of ``fn`` with an L2 flush (write of ``flush_bytes``) before every timed launch."""
+    flush = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def bench_moe(T=640, E=320, H=2048, I=512, k=10):
+    from ..ops import C
+    from ..ops.moe import Int3ExpertBank, MoEWorkspace
+    peaks = load_peaks()
+    dev = "cuda"
+    bank = Int3ExpertBank.random(E, H, I, dev)
+    ws = MoEWorkspace(T, E, k, H, I, I, dev)
+    x = torch.randn(T, H, device=dev).bfloat16()
+    logits = torch.randn(T, E + 8, device=dev)
+    c = C()
+    c.router_topk(logits, E, k, True, ws.ids[:T], ws.weights[:T])
+    n = T * k
+    R = ws.rows
+    c.expert_sort(ws.ids[:T], E, None, ws.offsets, ws.row_token, ws.row_entry, ws.entry_row[:n], 8)
+    c.quant_rows_e4m3(x, ws.row_token, ws.offsets[E:], R, ws.xq, ws.xs, True)
+    w13 = lambda: c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.offsets, ws.xq, ws.xs, True,  # noqa
+                                  ws.hq, ws.hs, None, None, None)
+    w2 = lambda: c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.offsets, ws.hq, ws.hs, False, None,  # noqa
+                                 None, ws.y, ws.weights[:T].view(-1), ws.row_entry)
+    out = []
+    for name, fn, wbytes, rows, kdim, ncols in (
+            ("moe_w13_int3", w13, bank.w13_codes.nbytes + bank.w13_scales.nbytes, n, H, 2 * I),
+            ("moe_w2_int3", w2, bank.w2_codes.nbytes + bank.w2_scales.nbytes, n, I, H)):
+        ms = time_cuda(fn)
+        act = rows * kdim + rows * ncols * (1 if name.endswith("w13_int3") else 2) // (2 if "w13" in name else 1)
+        byts = wbytes + act
+        out.append({"kernel": name, "T": T, "E": E, "ms": round(ms, 4), "bytes": byts,
+                    "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
+                    "tflops": round(2 * rows * kdim * ncols / ms / 1e9, 1)})
+    return out
+
+
+def bench_gemm(M=640):
+    from ..ops import C
+    peaks = load_peaks()
+    out = []
+    for name, N, K in (("in_proj_gdn", 12352, 2048), ("qkv_attn", 9216, 2048), ("out_proj_gdn", 2048, 4096),
+                       ("o_proj_attn", 2048, 4096), ("lm_head", 151936, 2048), ("router+shared", 1352, 2048)):
+        a = torch.randn(M, K, device="cuda").bfloat16()
+        b = torch.randn(N, K, device="cuda").bfloat16()
+        o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ms = time_cuda(lambda: C().gemm(a, b, out=o))
+        byts = (M * K + N * K + M * N) * 2
+        fl = 2 * M * N * K
+        ms_ref = time_cuda(lambda: torch.matmul(a, b.t(), out=o))
+        out.append({"kernel": "gemm_bf16_tn", "shape": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                    "tflops": round(fl / ms / 1e9, 1), "gbs": round(byts / ms / 1e6, 1),
+                    "frac_bf16_of_measured": round(fl / ms / 1e9 / peaks["bf16_tflops"], 3),
+                    "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
+                    "cublas_ms": round(ms_ref, 4)})
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["moe", "gemm", "all"])
+    ap.add_argument("--T", type=int, default=640)
+    a = ap.parse_args()
+    res = []
+    if a.what in ("moe", "all"):
+        res += bench_moe(T=a.T)
+    if a.what in ("gemm", "all"):
+        res += bench_gemm(M=a.T)
+    for r in res:
+        print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

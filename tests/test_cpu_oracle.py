@@ -161,3 +161,37 @@ def test_config1_pipeline_prune_quantize_decode():
     assert toks_p.shape == (1, 64)
     torch.testing.assert_close(logits_p, logits_t, rtol=1e-4, atol=1e-5)
     assert torch.equal(toks_p, toks_t)
+
+
+def _emulate_kernel_decode(tiles):
+    """Bit-exact emulation of the kernel's byte-permute decode: tile words -> e4m3 bytes of (code - 4)."""
+    table = [0xC8, 0xC4, 0xC0, 0xB8, 0x00, 0x38, 0x40, 0x44]
+    w = tiles.reshape(-1, 3).to(torch.int64) & 0xFFFFFFFF
+    out = []
+    for L0, L1, H in w.tolist():
+        m3, m4 = 0x33333333, 0x44444444
+        sels = [(L0 & m3) | (H & m4), ((L0 >> 2) & m3) | ((H >> 1) & m4),
+                (L1 & m3) | ((H << 2) & m4 & 0xFFFFFFFF), ((L1 >> 2) & m3) | ((H << 1) & m4 & 0xFFFFFFFF)]
+        for s in sels:
+            for nib in range(8):
+                out.append(table[(s >> (4 * nib)) & 7])
+    return torch.tensor(out, dtype=torch.uint8)
+
+
+def test_int3_tile_layout_roundtrip_and_kernel_decode():
+    from arc_forge_2026_b200.quant import int3_tiles
+    g = torch.Generator().manual_seed(9)
+    codes = torch.randint(0, 8, (2, 256, 384), generator=g, dtype=torch.uint8)
+    tiles = int3_tiles.codes_to_tiles(codes)
+    assert tiles.shape == (2, 2, 3, 128, 12)
+    assert torch.equal(int3_tiles.tiles_to_codes(tiles), codes)
+    # Humming pack -> tiles path
+    packed = uint3.pack_uint3(codes)
+    scales = torch.randn(2, 256, 3, generator=g).to(torch.bfloat16)
+    t2, s2 = int3_tiles.pack_to_tiles(packed, scales, 384)
+    assert torch.equal(t2, tiles) and torch.equal(int3_tiles.tiles_to_scales(s2), scales)
+    # the kernel decode of one tile row equals e4m3(code - 4) in code order
+    row = tiles[0, 1, 2, 5]  # expert 0, row block 1, group 2, row 5
+    dec = _emulate_kernel_decode(row)
+    ref = (codes[0, 128 + 5, 256:384].to(torch.float32) - 4).to(torch.float8_e4m3fn).view(torch.uint8)
+    assert torch.equal(dec, ref)

@@ -106,17 +106,31 @@ def test_router_sort_quant_combine():
     row_token = torch.empty(T * k, device=dev, dtype=torch.int32)
     row_entry = torch.empty_like(row_token)
     entry_row = torch.empty_like(row_token)
-    C().expert_sort(ids, E, None, off, row_token, row_entry, entry_row)
+    C().expert_sort(ids, E, None, off, row_token, row_entry, entry_row, 1)
     flat = ids.flatten().long()
     order = torch.sort(flat, stable=True).indices
     assert torch.equal(row_entry.long(), order)
     assert torch.equal(entry_row.long()[order], torch.arange(T * k, device=dev))
     counts = torch.bincount(flat, minlength=E)
     assert torch.equal(off[1:].long(), counts.cumsum(0))
+    # padded segments: starts are multiples of 8, rows keep the stable order inside each segment
+    rows = T * k + 7 * E
+    off8 = torch.empty(E + 1, device=dev, dtype=torch.int32)
+    rt8, re8 = torch.empty(rows, device=dev, dtype=torch.int32), torch.empty(rows, device=dev, dtype=torch.int32)
+    er8 = torch.empty(T * k, device=dev, dtype=torch.int32)
+    C().expert_sort(ids, E, None, off8, rt8, re8, er8, 8)
+    assert torch.all(off8 % 8 == 0)
+    for e in (0, 5, E - 1):
+        a, c_ = int(off8[e]), int(counts[e])
+        assert torch.equal(re8[a:a + c_].long(), order[int(off[e]):int(off[e]) + c_])
+        assert torch.all(re8[a + c_:int(off8[e + 1])] == -1)
     x = torch.randn(T, H, device=dev, generator=g).bfloat16()
     q = torch.empty(T * k, H, device=dev, dtype=torch.float8_e4m3fn)
     sc = torch.empty(T * k, H // 128, device=dev)
-    C().quant_rows_e4m3(x, row_token, None, T * k, q, sc)
+    C().quant_rows_e4m3(x, row_token, None, T * k, q, sc, False)
+    sc_gm = torch.empty(H // 128, T * k + 32, device=dev)
+    C().quant_rows_e4m3(x, row_token, None, T * k, q, sc_gm, True)
+    assert torch.equal(sc_gm[:, :T * k].t(), sc)
     rq, rs = fp8.quantize_act_groups(x[row_token.long()].float())
     torch.testing.assert_close(sc, rs, rtol=1e-6, atol=0)
     assert _rel(q.float(), rq.float()) < 1e-2
