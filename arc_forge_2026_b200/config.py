@@ -173,6 +173,8 @@ class QADConfig:
 
 PRESETS: dict[str, dict[str, Any]] = {
     "tiny_cpu": dict(name="tiny_cpu"),
+    # the tiny shape with the head size the GPU attention kernels take (128)
+    "tiny_gpu": dict(name="tiny_gpu", head_dim=128, expert_format="int3"),
     "qwen3next_80b": dict(
         name="qwen3next_80b", vocab_size=151936, hidden_size=2048, num_layers=48, full_attention_interval=4,
         num_attention_heads=16, num_kv_heads=2, head_dim=256, partial_rotary_factor=0.25, rope_theta=1.0e7,
@@ -191,6 +193,19 @@ PRESETS: dict[str, dict[str, Any]] = {
         moe_intermediate_size=640, shared_expert_intermediate_size=640, hc_count=4, qsa_block=4, qsa_topk=512,
         expert_format="int3"),
 }
+
+
+DRAFTER_PRESETS: dict[str, dict[str, Any]] = {
+    "dflash_8l": dict(),
+    "tiny": dict(num_layers=2, hidden_size=256, num_attention_heads=4, num_kv_heads=2, head_dim=128,
+                 intermediate_size=512),
+}
+
+
+def drafter_preset(name: str, **overrides) -> DrafterConfig:
+    kw = dict(DRAFTER_PRESETS[name])
+    kw.update(overrides)
+    return DrafterConfig(**kw)
 
 
 def preset(name: str, **overrides) -> ModelConfig:
@@ -249,5 +264,6 @@ def apply_env_overrides(cfg, section: str, environ: dict[str, str] | None = None
     return dataclasses.replace(cfg, **updates) if updates else cfg
 
 
-__all__ = ["ModelConfig", "DrafterConfig", "ServeConfig", "QADConfig", "PRESETS", "preset", "to_json", "from_json",
+__all__ = ["ModelConfig", "DrafterConfig", "ServeConfig", "QADConfig", "PRESETS", "preset", "drafter_preset",
+           "to_json", "from_json",
            "apply_env_overrides", "LINEAR", "FULL", "field"]

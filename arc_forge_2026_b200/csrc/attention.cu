@@ -76,10 +76,13 @@ __global__ void __launch_bounds__(256, 1)
   const int seq_len = a.seq_lens[seq];
   const int past = seq_len - a.q_per_seq;
   const int npages = (seq_len + attn::PAGE - 1) / attn::PAGE;
-  const int p0 = split * a.pages_per_split;
+  // sliding window: query t sees keys [past + t + 1 - window, past + t]
+  const int kv_lo = a.window > 0 ? max(0, past + 1 - a.window) : 0;
+  const int pbeg = kv_lo / attn::PAGE;
+  const int p0 = pbeg + split * a.pages_per_split;
   const int p1 = min(npages, p0 + a.pages_per_split);
   const int n = max(0, p1 - p0);
-  const int* bt = a.block_table + (size_t)seq * a.max_pages;
+  const int* bt = a.block_table + (size_t)(a.bt_row ? a.bt_row[seq] : seq) * a.max_pages;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -173,8 +176,8 @@ __global__ void __launch_bounds__(256, 1)
         for (int e = 0; e < 2; ++e) {
           const int key = kbase + j * 8 + (lane & 3) * 2 + e;
           float v0 = sc[j][e] * a.scale_log2, v1 = sc[j][2 + e] * a.scale_log2;
-          if (key >= past + t0 + 1 || r0 >= QR) v0 = -INFINITY;
-          if (key >= past + t1 + 1 || r1 >= QR) v1 = -INFINITY;
+          if (key >= past + t0 + 1 || r0 >= QR || (a.window > 0 && key < past + t0 + 1 - a.window)) v0 = -INFINITY;
+          if (key >= past + t1 + 1 || r1 >= QR || (a.window > 0 && key < past + t1 + 1 - a.window)) v1 = -INFINITY;
           sc[j][e] = v0;
           sc[j][2 + e] = v1;
           mx0 = fmaxf(mx0, v0);

@@ -99,6 +99,7 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
 }  // namespace
 
 void register_kernel_ops(pybind11::module& m);  // defined in ops_bindings.cpp
+void register_runtime(pybind11::module& m);     // defined in runtime.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "arc_forge_2026_b200 native kernels (sm_100a)";
@@ -108,4 +109,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_fp32") = false, py::arg("bn") = 0, py::arg("splits") = 0);
   m.def("gemm_plan", &gemm_plan);
   register_kernel_ops(m);
+  register_runtime(m);
 }

@@ -37,6 +37,8 @@ struct AttnArgs {
   int Hq = 0, Hkv = 0, D = 0;
   float scale_log2 = 0.f;            // softmax scale * log2(e)
   int pages_per_split = 1 << 30;
+  int window = 0;                    // > 0: sliding-window attention over the last `window` keys per query
+  const int* bt_row = nullptr;       // optional [num_seqs]: block-table row of each (virtual) sequence
   const __nv_bfloat16* gate = nullptr;  // optional output gate: out *= sigmoid(gate[tok*gate_ld + head*stride + d])
   int gate_ld = 0, gate_head_stride = 0;
   __nv_bfloat16* out = nullptr;         // [num_tokens, Hq, D]
@@ -68,5 +70,43 @@ struct GdnArgs {
   float eps = 1e-6f;
 };
 int gdn_decode(const GdnArgs& a, int parity, cudaStream_t st);
+
+// sampling.cu
+int select_tokens(const void* logits, int ld, int rows, int V, int* out, float temperature, uint64_t seed,
+                  const int* step, cudaStream_t st);
+struct SpecArgs {
+  const int* window = nullptr;   // [S, K+1] verify window tokens (anchor, drafts)
+  const int* target = nullptr;   // [S, K+1] target choice after each window row
+  const int* seq_slot = nullptr; // [S]
+  const int* active = nullptr;   // [S] or null
+  int* ctx_len = nullptr;        // [S] committed tokens (in/out)
+  int* n_commit = nullptr;       // [slots] out
+  int* out_tokens = nullptr;     // [S, K+1] emitted tokens (-1 padded)
+  int* out_count = nullptr;      // [S]
+  int* anchor = nullptr;         // [S] next window's first token
+  int* last_row = nullptr;       // [S] row index (into the window rows) of the last committed token
+  const int* step = nullptr;     // device step counter (bernoulli draws)
+  unsigned long long* total_emitted = nullptr;
+  int num_seqs = 0, k = 4, mode = 0;
+  float accept_prob = 0.7f;
+  uint64_t seed = 0;
+};
+int spec_accept(const SpecArgs& a, cudaStream_t st);
+struct WindowArgs {
+  const int* anchor = nullptr;      // [S]
+  const int* drafts = nullptr;      // [S, drafts_ld] or null (rows after the anchor get fill_token)
+  int drafts_ld = 0, fill_token = 0;
+  const int* ctx_len = nullptr;     // [S]
+  const int* block_table = nullptr; // [S, max_pages]
+  int max_pages = 0;
+  int* ids = nullptr;               // [S*W]
+  int* positions = nullptr;         // [S*W]
+  int* slots = nullptr;             // [S*W]
+  int* attn_len = nullptr;          // [S]
+  int* step = nullptr;              // optional counter bumped once per call
+  int num_seqs = 0, width = 5, pos_offset = 0;
+};
+int build_window(const WindowArgs& a, cudaStream_t st);
+int gather_rows(const void* src, const int* idx, void* out, int rows, int H, cudaStream_t st);
 
 }  // namespace afb

@@ -26,6 +26,7 @@ struct MoeGemmArgs {
   int out_ld = 0;
   const float* route_w = nullptr;  // !PAIR: routing weight per (token, slot) entry, or null
   const int* row_entry = nullptr;  // !PAIR: sorted row -> entry index
+  long long* dbg = nullptr;        // optional profiling counters [grid, 4 roles, 3]: wait cycles, total, k-steps
 };
 
 int moe_int3_gemm(const MoeGemmArgs& a, int pair, int num_sms, uint32_t* status, cudaStream_t st);

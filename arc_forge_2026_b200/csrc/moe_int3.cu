@@ -15,9 +15,10 @@
 // so each 8-code selector word is one AND/OR of a plane and a shifted H, and one byte-permute maps 4 selectors
 // to 4 e4m3 bytes through an 8-entry table held in two registers.
 //
-// One persistent CTA per SM, warp-specialised:
-//   warp 0      loader: bulk copies of the code/scale tiles, TMA of the activation rows (no multicast),
-//               activation scales by the 32 lanes
+// One persistent CTA per SM, warp-specialised: a ring of raw stages feeds a ring of dequantised tiles (4 deep for
+// w13, 6 for w2) and the MMA runs up to 8 (w13) / 16 (w2) groups ahead of the epilogue in TMEM:
+//   warp 0      loader: bulk copies of the code/scale tiles and of the activation scales, TMA of the activation
+//               rows (no multicast)
 //   warps 1-4   dequant: codes -> e4m3 (c-4) into the 128-byte-swizzled A tile, then arrive
 //   warp 5      MMA: M=128 (weight rows) x N=32 (tokens) x K=32 per op, one 128-K group per accumulator buffer
 //   warps 6-9   epilogue: per group D * s_w * s_x into registers; at the end of a chunk:
@@ -39,23 +40,32 @@ constexpr uint32_t A_TILE = 128 * 128;    // e4m3 128x128
 constexpr uint32_t X_TILE = NTOK * 128;   // e4m3 32x128
 constexpr uint32_t E4M3_LO = 0xB8C0C4C8u; // table bytes 0..3: e4m3(-4), e4m3(-3), e4m3(-2), e4m3(-1)
 constexpr uint32_t E4M3_HI = 0x44403800u; // table bytes 4..7: e4m3(0), e4m3(1), e4m3(2), e4m3(3)
+constexpr int MAX_E = 1024;               // experts whose segment offsets are staged in shared memory
 
+// Two rings: a deep one of raw stages (codes, weight scales, activation tile and scales, all moved by
+// bulk/TMA copies) and a 2-deep one of dequantised e4m3 A tiles (dequant -> MMA).
 template <bool PAIR>
 struct Layout {
   static constexpr int T = PAIR ? 2 : 1;  // weight tiles per k-step
-  static constexpr uint32_t A_OFF = 0;
-  static constexpr uint32_t X_OFF = A_OFF + T * A_TILE;
+  static constexpr uint32_t X_OFF = 0;    // 1024-aligned (TMA 128-byte swizzle)
   static constexpr uint32_t C_OFF = X_OFF + X_TILE;
   static constexpr uint32_t SW_OFF = C_OFF + T * CODE_TILE;
   static constexpr uint32_t SX_OFF = SW_OFF + T * 128 * 2;
-  static constexpr uint32_t STAGE_RAW = SX_OFF + NTOK * 4;
-  static constexpr uint32_t STAGE = (STAGE_RAW + 1023) & ~1023u;
-  static constexpr int STAGES = PAIR ? 4 : 6;
-  static constexpr uint32_t BAR_OFF = STAGES * STAGE;
-  // full[S], aready[S], empty[S], dfull[2], dempty[2]
-  static constexpr uint32_t TOTAL = BAR_OFF + (3 * STAGES + 4) * 8 + 16 + 4 * 32 * 4 + 1024;
-  static constexpr uint32_t RED_OFF = BAR_OFF + (3 * STAGES + 4) * 8 + 16;
-  static constexpr uint32_t TMEM_COLS = 128;
+  static constexpr uint32_t RAW_BYTES = SX_OFF + NTOK * 4;
+  static constexpr uint32_t RAW = (RAW_BYTES + 1023) & ~1023u;
+  // w13 (PAIR): one CTA per SM; w2: two CTAs per SM (half the shared memory and TMEM each)
+  static constexpr int CTAS_PER_SM = PAIR ? 1 : 2;
+  static constexpr int RS = PAIR ? 4 : 4;     // raw stages
+  static constexpr int AS = PAIR ? 4 : 3;     // dequantised stages
+  static constexpr int NBUF = PAIR ? 8 : 8;   // TMEM accumulator buffers (T * 32 columns each)
+  static constexpr uint32_t A_STAGE = T * A_TILE;
+  static constexpr uint32_t A_OFF = RS * RAW;
+  static constexpr uint32_t OFFS_OFF = A_OFF + AS * A_STAGE;        // int offsets[MAX_E + 1]
+  static constexpr uint32_t RED_OFF = OFFS_OFF + (MAX_E + 1) * 4;   // float [4][32]
+  static constexpr uint32_t BAR_OFF = (RED_OFF + 4 * 32 * 4 + 7) & ~7u;
+  // full[RS], empty[RS], afull[AS], aempty[AS], dfull[NBUF], dempty[NBUF], tmem slot
+  static constexpr uint32_t TOTAL = BAR_OFF + (2 * RS + 2 * AS + 2 * NBUF) * 8 + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512 / CTAS_PER_SM;
 };
 }  // namespace moe
 
@@ -100,18 +110,20 @@ AFB_DEV void dequant_row(const uint32_t* src, uint8_t* tile, int r) {
 }
 
 template <bool PAIR>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(320, PAIR ? 1 : 2)
     moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmX, MoeGemmArgs args, uint32_t* status) {
   using L = moe::Layout<PAIR>;
-  constexpr int S = L::STAGES;
+  constexpr int RS = L::RS, AS = L::AS, NBUF = L::NBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* aready = full + S;
-  uint64_t* empty = aready + S;
-  uint64_t* dfull = empty + S;
-  uint64_t* dempty = dfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 2);
+  uint64_t* empty = full + RS;
+  uint64_t* afull = empty + RS;
+  uint64_t* aempty = afull + AS;
+  uint64_t* dfull = aempty + AS;
+  uint64_t* dempty = dfull + NBUF;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + NBUF);
+  int* off = reinterpret_cast<int*>(smem + L::OFFS_OFF);
   float* red = reinterpret_cast<float*>(smem + L::RED_OFF);  // [4 warps][32 tokens] amax exchange
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -120,13 +132,17 @@ __global__ void __launch_bounds__(320, 1)
   const int KG = args.K / 128;                       // k-steps (groups) per chunk
   const int units = E * NB;
 
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) off[e] = args.expert_offsets[e];
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
+    for (int s = 0; s < RS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&aready[s], 128);
-      mbar_init(&empty[s], 1 + 4);
+      mbar_init(&empty[s], 4 + 1 + 4);  // dequant warps + MMA commit + epilogue warps
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(&afull[s], 4);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(&dfull[b], 1);
       mbar_init(&dempty[b], 4);
     }
@@ -137,11 +153,13 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int* off = args.expert_offsets;
 
   // every role walks the same (unit, chunk, group) sequence
   uint32_t kstep = 0;
   bool bail = false;
+  long long t_wait = 0;  // profiling counters (args.dbg): cycles spent in waits by this role
+  const long long t_start = clock64();
+#define AFB_TIMED_WAIT(expr) ([&]() { const long long _t = clock64(); const bool _r = (expr); t_wait += clock64() - _t; return _r; }())
   for (int u = blockIdx.x; u < units && !bail; u += gridDim.x) {
     const int e = u % E, j = u / E;  // neighbouring CTAs take different experts
     const int row0 = off[e], n = off[e + 1] - row0;
@@ -151,18 +169,17 @@ __global__ void __launch_bounds__(320, 1)
       const int cn = min(moe::NTOK, n - ch * moe::NTOK);
       if (warp == 0) {
         // ---------------------------------------------------------------- loader
-        for (int g = 0; g < KG; ++g, ++kstep) {
-          const int s = kstep % S;
-          const uint32_t ph = (kstep / S) & 1;
-          if (kstep >= (uint32_t)S && !mbar_wait(&empty[s], ph ^ 1, status)) {
-            bail = true;
-            break;
-          }
-          uint8_t* st = smem + s * L::STAGE;
-          if (lane == 0) {
-            // activation scales of this group for the chunk's 32 rows (group-major, segment starts are 8-aligned)
-            const uint32_t bytes = L::T * (moe::CODE_TILE + 256) + moe::X_TILE + moe::NTOK * 4;
-            mbar_arrive_expect_tx(&full[s], bytes);
+        if (lane == 0) {
+          for (int g = 0; g < KG; ++g, ++kstep) {
+            const int s = kstep % RS;
+            const uint32_t ph = (kstep / RS) & 1;
+            if (kstep >= (uint32_t)RS && !AFB_TIMED_WAIT(mbar_wait(&empty[s], ph ^ 1, status))) {
+              bail = true;
+              break;
+            }
+            uint8_t* st = smem + s * L::RAW;
+            mbar_arrive_expect_tx(&full[s], L::T * (moe::CODE_TILE + 256) + moe::X_TILE + moe::NTOK * 4);
+            // activation scales of this group for the chunk's 32 rows (group-major, segment starts 8-aligned)
             bulk_g2s(st + L::SX_OFF, args.x_scales + (size_t)g * args.ld_xs + crow, moe::NTOK * 4, &full[s]);
 #pragma unroll
             for (int t = 0; t < L::T; ++t) {
@@ -170,56 +187,66 @@ __global__ void __launch_bounds__(320, 1)
               const size_t tile = ((size_t)e * (args.rows / 128) + rb) * KG + g;
               bulk_g2s(st + L::C_OFF + t * moe::CODE_TILE, args.codes + tile * (moe::CODE_TILE / 4), moe::CODE_TILE,
                        &full[s]);
-              bulk_g2s(st + L::SW_OFF + t * 256, reinterpret_cast<const uint16_t*>(args.scales) + tile * 128, 256, &full[s]);
+              bulk_g2s(st + L::SW_OFF + t * 256, reinterpret_cast<const uint16_t*>(args.scales) + tile * 128, 256,
+                       &full[s]);
             }
             tma_load_2d(st + L::X_OFF, &tmX, &full[s], g * 128, crow);
           }
-          __syncwarp();
         }
+        __syncwarp();
+        bail = __shfl_sync(0xffffffffu, bail, 0);
       } else if (warp >= 1 && warp <= 4) {
         // ---------------------------------------------------------------- dequant
         const int r = threadIdx.x - 32;  // 0..127: row of the weight tile
         for (int g = 0; g < KG; ++g, ++kstep) {
-          const int s = kstep % S;
-          const uint32_t ph = (kstep / S) & 1;
-          if (!mbar_wait(&full[s], ph, status)) {
+          const int s = kstep % RS;
+          const int as = kstep % AS;
+          bool ok = AFB_TIMED_WAIT(mbar_wait(&full[s], (kstep / RS) & 1, status));
+          if (ok && kstep >= (uint32_t)AS) ok = AFB_TIMED_WAIT(mbar_wait(&aempty[as], ((kstep / AS) & 1) ^ 1, status));
+          if (!ok) {
             bail = true;
             break;
           }
-          uint8_t* st = smem + s * L::STAGE;
+          const uint8_t* st = smem + s * L::RAW;
+          uint8_t* at = smem + L::A_OFF + as * L::A_STAGE;
 #pragma unroll
           for (int t = 0; t < L::T; ++t)
             dequant_row(reinterpret_cast<const uint32_t*>(st + L::C_OFF + t * moe::CODE_TILE) + r * 12,
-                        st + L::A_OFF + t * moe::A_TILE, r);
+                        at + t * moe::A_TILE, r);
           fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the tensor core
-          mbar_arrive(&aready[s]);
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&afull[as]);
+            mbar_arrive(&empty[s]);
+          }
         }
       } else if (warp == 5) {
         // ---------------------------------------------------------------- MMA
         constexpr uint32_t idesc = idesc_e4m3(128, moe::NTOK);
         for (int g = 0; g < KG; ++g, ++kstep) {
-          const int s = kstep % S;
-          const uint32_t ph = (kstep / S) & 1;
-          const int b = kstep & 1;
-          const uint32_t bph = (kstep >> 1) & 1;
-          bool ok = mbar_wait(&aready[s], ph, status);
-          if (ok && kstep >= 2) ok = mbar_wait(&dempty[b], bph ^ 1, status);
+          const int s = kstep % RS;
+          const int as = kstep % AS;
+          const int b = kstep % NBUF;
+          bool ok = AFB_TIMED_WAIT(mbar_wait(&afull[as], (kstep / AS) & 1, status));
+          if (ok && kstep >= (uint32_t)NBUF) ok = AFB_TIMED_WAIT(mbar_wait(&dempty[b], ((kstep / NBUF) & 1) ^ 1, status));
           if (!ok) {
             bail = true;
             break;
           }
           tc_fence_after();
           if (lane == 0) {
-            uint8_t* st = smem + s * L::STAGE;
+            const uint8_t* st = smem + s * L::RAW;
+            const uint8_t* at = smem + L::A_OFF + as * L::A_STAGE;
             const uint64_t dx = sw128_desc(smem_u32(st + L::X_OFF));
 #pragma unroll
             for (int t = 0; t < L::T; ++t) {
-              const uint64_t da = sw128_desc(smem_u32(st + L::A_OFF + t * moe::A_TILE));
-              const uint32_t d = tmem + (uint32_t)((b * 2 + t) * moe::NTOK);
+              const uint64_t da = sw128_desc(smem_u32(at + t * moe::A_TILE));
+              const uint32_t d = tmem + (uint32_t)((b * L::T + t) * moe::NTOK);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) umma_f8(d, da + 2 * kk, dx + 2 * kk, idesc, kk != 0);
             }
             umma_commit(&dfull[b]);
+            umma_commit(&aempty[as]);
             umma_commit(&empty[s]);
           }
           __syncwarp();
@@ -234,73 +261,78 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int i = 0; i < (PAIR ? moe::NTOK : 1); ++i) acc1[i] = 0.f;
         for (int g = 0; g < KG; ++g, ++kstep) {
-          const int s = kstep % S;
-          const int b = kstep & 1;
-          const uint32_t bph = (kstep >> 1) & 1;
-          if (!mbar_wait(&dfull[b], bph, status)) {
+          const int s = kstep % RS;
+          const int b = kstep % NBUF;
+          if (!AFB_TIMED_WAIT(mbar_wait(&dfull[b], (kstep / NBUF) & 1, status))) {
             bail = true;
             break;
           }
           tc_fence_after();
-          float d0[moe::NTOK], d1[moe::NTOK];
-          const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * 2 * moe::NTOK);
-          tmem_ld32(ta, d0);
-          if (PAIR) tmem_ld32(ta + moe::NTOK, d1);
-          tmem_ld_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&dempty[b]);
-          const uint8_t* st = smem + s * L::STAGE;
+          const uint8_t* st = smem + s * L::RAW;
           const float* sx = reinterpret_cast<const float*>(st + L::SX_OFF);
           const float sw0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L::SW_OFF)[r]);
           const float sw1 = PAIR ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L::SW_OFF + 256)[r]) : 0.f;
+          const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * L::T * moe::NTOK);
 #pragma unroll
-          for (int i = 0; i < moe::NTOK; ++i) {
-            const float x = sx[i];
-            acc0[i] = fmaf(sw0 * x, d0[i], acc0[i]);
-            if (PAIR) acc1[i] = fmaf(sw1 * x, d1[i], acc1[i]);
+          for (int hf = 0; hf < 2; ++hf) {
+            float d0[16], d1[16];
+            tmem_ld16(ta + hf * 16, d0);
+            if (PAIR) tmem_ld16(ta + moe::NTOK + hf * 16, d1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float x = sx[hf * 16 + i];
+              acc0[hf * 16 + i] = fmaf(sw0 * x, d0[i], acc0[hf * 16 + i]);
+              if (PAIR) acc1[hf * 16 + i] = fmaf(sw1 * x, d1[i], acc1[hf * 16 + i]);
+            }
           }
+          tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
+          if (lane == 0) {
+            mbar_arrive(&dempty[b]);
+            mbar_arrive(&empty[s]);
+          }
         }
         if (bail) break;
         if (PAIR) {
           // h = silu(gate) * up -> e4m3 with a scale per (token, this 128-column group)
           const int col = j * 128 + r;  // intermediate column
-          float amax[moe::NTOK];
 #pragma unroll
           for (int i = 0; i < moe::NTOK; ++i) {
             acc0[i] = silu(acc0[i]) * acc1[i];
-            amax[i] = warp_max(fabsf(acc0[i]));
-          }
-          if (lane == 0) {
-#pragma unroll
-            for (int i = 0; i < moe::NTOK; ++i) red[quad * 32 + i] = amax[i];
+            const float m = warp_max(fabsf(acc0[i]));
+            if (lane == 0) red[quad * 32 + i] = m;
           }
           named_bar(1, 128);
 #pragma unroll
-          for (int i = 0; i < moe::NTOK; ++i)
-            amax[i] = fmaxf(fmaxf(red[i], red[32 + i]), fmaxf(red[64 + i], red[96 + i]));
-          named_bar(1, 128);  // red is reused by the next chunk
-#pragma unroll
           for (int i = 0; i < moe::NTOK; ++i) {
             if (i >= cn) break;
-            const float sc = amax[i] > 0.f ? amax[i] / 448.f : 1.f;
+            const float amax = fmaxf(fmaxf(red[i], red[32 + i]), fmaxf(red[64 + i], red[96 + i]));
+            const float sc = amax > 0.f ? amax / 448.f : 1.f;
             const __nv_fp8_e4m3 q(acc0[i] / sc);
             args.out_q[(size_t)(crow + i) * args.out_ld + col] = *reinterpret_cast<const uint8_t*>(&q);
             if (r == 0) args.out_scales[(size_t)j * args.ld_os + crow + i] = sc;
           }
+          named_bar(1, 128);  // red is reused by the next chunk
         } else {
           const int col = j * 128 + r;  // hidden column
 #pragma unroll
           for (int i = 0; i < moe::NTOK; ++i) {
             if (i >= cn) break;
             const float w = args.route_w ? args.route_w[args.row_entry[crow + i]] : 1.f;
-            reinterpret_cast<__nv_bfloat16*>(args.out_bf16)[(size_t)(crow + i) * args.out_ld + col] = __float2bfloat16(acc0[i] * w);
+            reinterpret_cast<__nv_bfloat16*>(args.out_bf16)[(size_t)(crow + i) * args.out_ld + col] =
+                __float2bfloat16(acc0[i] * w);
           }
         }
       }
     }
+  }
+#undef AFB_TIMED_WAIT
+  if (args.dbg && lane == 0 && (warp == 0 || warp == 1 || warp == 5 || warp == 6)) {
+    const int role = warp == 0 ? 0 : warp == 1 ? 1 : warp == 5 ? 2 : 3;
+    args.dbg[(blockIdx.x * 4 + role) * 3 + 0] = t_wait;
+    args.dbg[(blockIdx.x * 4 + role) * 3 + 1] = clock64() - t_start;
+    args.dbg[(blockIdx.x * 4 + role) * 3 + 2] = kstep;
   }
   tc_fence_before();
   __syncthreads();
@@ -312,13 +344,14 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 int moe_int3_gemm(const MoeGemmArgs& a, int pair, int num_sms, uint32_t* status, cudaStream_t st) {
-  if (a.K % 128 || a.rows % (pair ? 256 : 128)) return 3;
+  if (a.K % 128 || a.rows % (pair ? 256 : 128) || a.num_experts > moe::MAX_E) return 3;
   if (a.num_rows_total <= 0) return 0;
   CUtensorMap tx;
   int rc = make_tmap_2d(&tx, a.x_q, 1, a.K, a.num_rows_total, (uint64_t)a.K, 128, moe::NTOK, 1);
   if (rc) return 1000 + rc;
   const int units = a.num_experts * (a.rows / 128 / (pair ? 2 : 1));
-  const int grid = units < num_sms ? units : num_sms;
+  const int slots = num_sms * (pair ? moe::Layout<true>::CTAS_PER_SM : moe::Layout<false>::CTAS_PER_SM);
+  const int grid = units < slots ? units : slots;
   if (pair) {
     using L = moe::Layout<true>;
     static bool attr = false;

@@ -74,7 +74,8 @@ void quant_rows_e4m3_op(const at::Tensor& x, c10::optional<at::Tensor> row_token
 void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& offsets,
                       const at::Tensor& x_q, const at::Tensor& x_scales, bool pair, c10::optional<at::Tensor> out_q,
                       c10::optional<at::Tensor> out_scales, c10::optional<at::Tensor> out_bf16,
-                      c10::optional<at::Tensor> route_w, c10::optional<at::Tensor> row_entry) {
+                      c10::optional<at::Tensor> route_w, c10::optional<at::Tensor> row_entry,
+                      c10::optional<at::Tensor> dbg) {
   AFB_CHECK_DT(codes, at::kInt);
   AFB_CHECK_DT(scales, at::kBFloat16);
   AFB_CHECK_DT(offsets, at::kInt);
@@ -113,6 +114,7 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
     a.row_entry = optr<int>(row_entry);
     TORCH_CHECK(!a.route_w || a.row_entry, "route_w needs row_entry");
   }
+  a.dbg = optr<long long>(dbg);
   check_rc(afb::moe_int3_gemm(a, pair, num_sms(), status_ptr(codes.get_device()), stream()), "moe_int3_gemm");
 }
 
@@ -131,7 +133,7 @@ void moe_combine_op(const at::Tensor& y, const at::Tensor& entry_row, int64_t k,
 void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
                         const at::Tensor& block_table, const at::Tensor& seq_lens, int64_t q_per_seq, double scale,
                         at::Tensor& out, c10::optional<at::Tensor> gate, int64_t gate_ld, int64_t gate_head_stride,
-                        int64_t splits, int64_t pages_per_split) {
+                        int64_t splits, int64_t pages_per_split, int64_t window, c10::optional<at::Tensor> bt_row) {
   AFB_CHECK_DT(q, at::kBFloat16);
   AFB_CHECK_CONTIG(q);
   AFB_CHECK_CONTIG(kcache);
@@ -156,6 +158,8 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
   TORCH_CHECK(a.num_tokens == a.num_seqs * q_per_seq, "q rows must be num_seqs * q_per_seq");
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.pages_per_split = (int)pages_per_split;
+  a.window = (int)window;
+  a.bt_row = optr<int>(bt_row);
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   if (gate.has_value()) {
     a.gate = reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr());
@@ -222,6 +226,69 @@ void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const
   check_rc(afb::gdn_decode(a, (int)parity, stream()), "gdn_decode");
 }
 
+void select_tokens_op(const at::Tensor& logits, int64_t V, at::Tensor& out, double temperature, int64_t seed,
+                      c10::optional<at::Tensor> step) {
+  AFB_CHECK_DT(logits, at::kBFloat16);
+  AFB_CHECK_DT(out, at::kInt);
+  TORCH_CHECK(logits.stride(1) == 1, "logits inner stride");
+  check_rc(afb::select_tokens(logits.data_ptr(), logits.stride(0), logits.size(0), V, ptr<int>(out),
+                              (float)temperature, (uint64_t)seed, optr<int>(step), stream()),
+           "select_tokens");
+}
+
+void spec_accept_op(const at::Tensor& window, const at::Tensor& target, const at::Tensor& seq_slot,
+                    c10::optional<at::Tensor> active, at::Tensor& ctx_len, at::Tensor& n_commit, at::Tensor& out_tokens,
+                    at::Tensor& out_count, at::Tensor& anchor, at::Tensor& last_row, const at::Tensor& step,
+                    c10::optional<at::Tensor> total_emitted, int64_t mode, double accept_prob, int64_t seed) {
+  afb::SpecArgs a;
+  a.window = ptr<int>(window);
+  a.target = ptr<int>(target);
+  a.seq_slot = ptr<int>(seq_slot);
+  a.active = optr<int>(active);
+  a.ctx_len = ptr<int>(ctx_len);
+  a.n_commit = ptr<int>(n_commit);
+  a.out_tokens = ptr<int>(out_tokens);
+  a.out_count = ptr<int>(out_count);
+  a.anchor = ptr<int>(anchor);
+  a.last_row = ptr<int>(last_row);
+  a.step = ptr<int>(step);
+  a.total_emitted = optr<unsigned long long>(total_emitted);
+  a.num_seqs = ctx_len.size(0);
+  a.k = window.size(1) - 1;
+  a.mode = mode;
+  a.accept_prob = (float)accept_prob;
+  a.seed = (uint64_t)seed;
+  check_rc(afb::spec_accept(a, stream()), "spec_accept");
+}
+
+void build_window_op(const at::Tensor& anchor, c10::optional<at::Tensor> drafts, int64_t fill_token,
+                     const at::Tensor& ctx_len, const at::Tensor& block_table, at::Tensor& ids, at::Tensor& positions,
+                     at::Tensor& slots, at::Tensor& attn_len, c10::optional<at::Tensor> step, int64_t width,
+                     int64_t pos_offset) {
+  afb::WindowArgs a;
+  a.anchor = ptr<int>(anchor);
+  a.drafts = optr<int>(drafts);
+  a.drafts_ld = drafts.has_value() ? drafts->stride(0) : 0;
+  a.fill_token = fill_token;
+  a.ctx_len = ptr<int>(ctx_len);
+  a.block_table = ptr<int>(block_table);
+  a.max_pages = block_table.size(1);
+  a.ids = ptr<int>(ids);
+  a.positions = ptr<int>(positions);
+  a.slots = ptr<int>(slots);
+  a.attn_len = ptr<int>(attn_len);
+  a.step = optr<int>(step);
+  a.num_seqs = ctx_len.size(0);
+  a.width = width;
+  a.pos_offset = pos_offset;
+  check_rc(afb::build_window(a, stream()), "build_window");
+}
+
+void gather_rows_op(const at::Tensor& src, const at::Tensor& idx, at::Tensor& out) {
+  check_rc(afb::gather_rows(src.data_ptr(), ptr<int>(idx), out.data_ptr(), idx.numel(), src.size(1), stream()),
+           "gather_rows");
+}
+
 void swiglu_op(const at::Tensor& x, at::Tensor& y) {
   const int T = x.size(0), I = x.size(1) / 2;
   check_rc(afb::swiglu(x.data_ptr(), y.data_ptr(), T, I, stream()), "swiglu");
@@ -243,8 +310,14 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("expert_sort", &expert_sort_op);
   m.def("quant_rows_e4m3", &quant_rows_e4m3_op);
   m.def("moe_combine", &moe_combine_op);
-  m.def("moe_int3_gemm", &moe_int3_gemm_op);
+  m.def("moe_int3_gemm", &moe_int3_gemm_op, py::arg("codes"), py::arg("scales"), py::arg("offsets"), py::arg("x_q"),
+        py::arg("x_scales"), py::arg("pair"), py::arg("out_q"), py::arg("out_scales"), py::arg("out_bf16"),
+        py::arg("route_w"), py::arg("row_entry"), py::arg("dbg") = py::none());
   m.def("swiglu", &swiglu_op);
+  m.def("select_tokens", &select_tokens_op);
+  m.def("spec_accept", &spec_accept_op);
+  m.def("build_window", &build_window_op);
+  m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
   m.def("paged_attention", &paged_attention_op);
   m.def("embedding", &embedding_op);

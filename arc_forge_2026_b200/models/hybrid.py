@@ -1,0 +1,278 @@
+"""The hybrid MoE on the native kernels: decode / speculative verify / prefill forward passes.
+
+Weights live in the layouts the kernels want:
+
+* GDN layers: one fused in-projection ``[q|k|v|z|b|a]`` (``in_proj_qkvz`` and ``in_proj_ba`` stacked), conv
+  weight fp32 ``[C, 4]``, ``A_log``/``dt_bias`` fp32, output norm weight, ``out_proj``.
+* Attention layers: one fused ``[q+gate | k | v]`` projection (``q_proj`` rows keep the per-head
+  ``[q_h | gate_h]`` interleave), q/k norm weights, ``o_proj``.
+* MoE: router rows + the shared-expert gate row (``router_ext``), routed experts as an INT3 tile bank, the shared
+  expert as ``[gate; up]`` and ``down``.
+
+The residual stream is bf16 and is updated in place by the GEMM epilogues (``out = acc + residual``) and the MoE
+combine. A step over N tokens launches, per layer, 6-9 kernels; the whole decode step is CUDA-graph capturable
+(all shapes fixed by the batch layout, all indices on the device).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..config import FULL, ModelConfig
+from ..ops import C
+from ..ops.attention import PAGE, paged_attention
+from ..ops.gdn import GdnScratch, GdnShape, GdnState, gdn_decode
+from ..ops.moe import Int3ExpertBank, MoEWorkspace, moe_forward, router_weight_with_shared_gate
+from .reference import HybridMoE, rope_cos_sin
+
+
+@dataclass
+class LayerWeights:
+    kind: str
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    # attention
+    w_qkv: torch.Tensor | None = None
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
+    w_o: torch.Tensor | None = None
+    # GDN
+    w_in: torch.Tensor | None = None
+    conv_w: torch.Tensor | None = None
+    A_log: torch.Tensor | None = None
+    dt_bias: torch.Tensor | None = None
+    g_norm: torch.Tensor | None = None
+    w_out: torch.Tensor | None = None
+    # MoE
+    router_ext: torch.Tensor | None = None
+    bank: Int3ExpertBank | None = None
+    shared_w13: torch.Tensor | None = None
+    shared_w2: torch.Tensor | None = None
+
+
+@dataclass
+class StepBatch:
+    """Device-side description of one forward over ``num_seqs * q_per_seq`` tokens (uniform rows per sequence)."""
+    ids: torch.Tensor          # [N] int32
+    positions: torch.Tensor    # [N] int32
+    slots: torch.Tensor        # [N] int32 KV slot (page * 64 + offset)
+    block_table: torch.Tensor  # [S, max_pages] int32
+    seq_lens: torch.Tensor     # [S] int32: tokens in the KV cache including this step's rows
+    seq_slot: torch.Tensor     # [S] int32 GDN state slot
+    n_commit: torch.Tensor     # [slots] int32 accepted rows of the previous cycle
+    q_per_seq: int
+    parity: int = 0
+    commit_current: bool = False
+    max_pages: int | None = None  # bound on pages per sequence (split plan)
+    attn_bt_row: torch.Tensor | None = None    # prefill: virtual rows -> block-table row
+    attn_seq_lens: torch.Tensor | None = None  # prefill: per-virtual-row lengths
+    attn_q_per_seq: int | None = None
+
+    @property
+    def num_tokens(self) -> int:
+        return self.ids.shape[0]
+
+
+class HybridModel:
+    def __init__(self, cfg: ModelConfig, layers: list[LayerWeights], embed, final_norm, lm_head, device):
+        self.cfg = cfg
+        self.layers = layers
+        self.embed = embed
+        self.final_norm = final_norm
+        self.lm_head = lm_head
+        self.device = torch.device(device)
+        c = cfg
+        self.gdn_shape = GdnShape(c.linear_num_key_heads, c.linear_key_head_dim, c.linear_num_value_heads,
+                                  c.linear_value_head_dim)
+        cos, sin = rope_cos_sin(torch.arange(1 << 17, device=self.device), c.rotary_dim, c.rope_theta)
+        self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def random(cls, cfg: ModelConfig, device, seed: int = 0, std: float | None = None):
+        """Random-init weights of ``cfg`` generated directly on the device (INT3 experts as random codes)."""
+        std = cfg.init_std if std is None else std
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev).manual_seed(seed)
+
+        def randn(*shape):
+            return (torch.randn(*shape, generator=gen, device=dev) * std).to(torch.bfloat16)
+
+        H = cfg.hidden_size
+        gs = GdnShape(cfg.linear_num_key_heads, cfg.linear_key_head_dim, cfg.linear_num_value_heads,
+                      cfg.linear_value_head_dim)
+        layers = []
+        for kind in cfg.layer_types:
+            lw = LayerWeights(kind, torch.zeros(H, dtype=torch.bfloat16, device=dev),
+                              torch.zeros(H, dtype=torch.bfloat16, device=dev))
+            if kind == FULL:
+                D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_kv_heads
+                lw.w_qkv = randn(Hq * 2 * D + 2 * Hkv * D, H)
+                lw.q_norm = torch.zeros(D, dtype=torch.bfloat16, device=dev)
+                lw.k_norm = torch.zeros(D, dtype=torch.bfloat16, device=dev)
+                lw.w_o = randn(H, Hq * D)
+            else:
+                lw.w_in = randn(gs.mixed_dim, H)
+                lw.conv_w = (torch.randn(gs.conv_dim, 4, generator=gen, device=dev) * 0.3).float()
+                lw.A_log = torch.log(torch.empty(gs.Hv, device=dev).uniform_(1, 16, generator=gen))
+                dt = torch.exp(torch.empty(gs.Hv, device=dev).uniform_(math.log(1e-3), math.log(1e-1),
+                                                                        generator=gen))
+                lw.dt_bias = dt + torch.log(-torch.expm1(-dt))
+                lw.g_norm = torch.ones(gs.Dv, dtype=torch.bfloat16, device=dev)
+                lw.w_out = randn(H, gs.Hv * gs.Dv)
+            E, I, Is = cfg.num_experts, cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
+            lw.router_ext = router_weight_with_shared_gate(randn(E, H), randn(1, H))
+            lw.bank = Int3ExpertBank(
+                torch.randint(-2**31, 2**31 - 1, (E, 2 * I // 128, H // 128, 128, 12), dtype=torch.int32,
+                              device=dev, generator=gen),
+                (torch.randn(E, 2 * I // 128, H // 128, 128, generator=gen, device=dev) * std / 2.3).to(
+                    torch.bfloat16),
+                torch.randint(-2**31, 2**31 - 1, (E, H // 128, I // 128, 128, 12), dtype=torch.int32, device=dev,
+                              generator=gen),
+                (torch.randn(E, H // 128, I // 128, 128, generator=gen, device=dev) * std / 2.3).to(
+                    torch.bfloat16))
+            lw.shared_w13 = randn(2 * Is, H)
+            lw.shared_w2 = randn(H, Is)
+            layers.append(lw)
+        embed = randn(cfg.vocab_size, H)
+        return cls(cfg, layers, embed, torch.zeros(H, dtype=torch.bfloat16, device=dev),
+                   randn(cfg.vocab_size, H), dev)
+
+    @classmethod
+    def from_reference(cls, ref: HybridMoE, device, codes_scales: list | None = None):
+        """Convert the oracle model. ``codes_scales``: per layer (w13_codes, w13_scales, w2_codes, w2_scales) of
+        INT3-quantised experts; without it the experts are RTN-quantised here."""
+        from ..quant.gptq import rtn_quantize
+        cfg = ref.cfg
+        dev = torch.device(device)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        layers = []
+        for i, L in enumerate(ref.layers):
+            lw = LayerWeights(L.kind, L.input_layernorm.weight.detach().to(**bf),
+                              L.post_attention_layernorm.weight.detach().to(**bf))
+            m = L.mixer
+            if L.kind == FULL:
+                lw.w_qkv = torch.cat([m.q_proj.weight, m.k_proj.weight, m.v_proj.weight]).detach().to(**bf)
+                lw.q_norm = m.q_norm.weight.detach().to(**bf)
+                lw.k_norm = m.k_norm.weight.detach().to(**bf)
+                lw.w_o = m.o_proj.weight.detach().to(**bf).contiguous()
+            else:
+                lw.w_in = torch.cat([m.in_proj_qkvz.weight, m.in_proj_ba.weight]).detach().to(**bf)
+                lw.conv_w = m.conv1d.detach().float().to(dev).contiguous()
+                lw.A_log = m.A_log.detach().float().to(dev)
+                lw.dt_bias = m.dt_bias.detach().float().to(dev)
+                lw.g_norm = m.norm.detach().to(**bf)
+                lw.w_out = m.out_proj.weight.detach().to(**bf).contiguous()
+            moe = L.mlp
+            lw.router_ext = router_weight_with_shared_gate(moe.gate.weight.detach().to(**bf),
+                                                           moe.shared_expert_gate.weight.detach().to(**bf))
+            if codes_scales is not None:
+                c13, s13, c2, s2 = codes_scales[i]
+            else:
+                c13, s13 = rtn_quantize(moe.w13.detach().float())
+                c2, s2 = rtn_quantize(moe.w2.detach().float())
+            lw.bank = Int3ExpertBank.from_codes(c13, s13.to(torch.bfloat16), c2, s2.to(torch.bfloat16), dev)
+            lw.shared_w13 = torch.cat([moe.shared_gate_proj.weight, moe.shared_up_proj.weight]).detach().to(**bf)
+            lw.shared_w2 = moe.shared_down_proj.weight.detach().to(**bf).contiguous()
+            layers.append(lw)
+        return cls(cfg, layers, ref.embed_tokens.weight.detach().to(**bf), ref.norm.weight.detach().to(**bf),
+                   ref.lm_head.weight.detach().to(**bf), dev)
+
+    def nbytes(self) -> int:
+        tot = self.embed.nbytes + self.lm_head.nbytes
+        for lw in self.layers:
+            for v in lw.__dict__.values():
+                if isinstance(v, torch.Tensor):
+                    tot += v.nbytes
+                elif isinstance(v, Int3ExpertBank):
+                    tot += v.nbytes()
+        return tot
+
+    # ------------------------------------------------------------------ caches
+    def new_kv_cache(self, num_pages: int):
+        c = self.cfg
+        shape = (num_pages, c.num_kv_heads, PAGE, c.head_dim)
+        return [(torch.zeros(shape, dtype=torch.bfloat16, device=self.device),
+                 torch.zeros(shape, dtype=torch.bfloat16, device=self.device)) for _ in range(c.num_attention_layers)]
+
+    def new_gdn_states(self, slots: int, max_q: int):
+        return [GdnState(self.gdn_shape, slots, max_q, self.device) for _ in range(self.cfg.num_gdn_layers)]
+
+    def new_workspace(self, max_tokens: int):
+        return Workspace(self, max_tokens)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, b: StepBatch, kv, gdn, ws: "Workspace", gdn_scratch: GdnScratch | None = None):
+        """Runs the stack over b.ids; returns the final-normed hidden rows [N, H] (a view into the workspace)."""
+        c, cC = self.cfg, C()
+        N, H = b.num_tokens, c.hidden_size
+        h = ws.h[:N]
+        cC.embedding(b.ids, self.embed, h)
+        y = ws.y[:N]
+        ai = gi = 0
+        D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_kv_heads
+        for lw in self.layers:
+            cC.rmsnorm(h, None, lw.in_norm, y, c.rms_norm_eps, True)
+            if lw.kind == FULL:
+                qkv = ws.qkv[:N]
+                cC.gemm(y, lw.w_qkv, out=qkv)
+                kc, vc = kv[ai]
+                q = ws.q[:N]
+                cC.qk_norm_rope_store(qkv, Hq, Hkv, D, c.rotary_dim, lw.q_norm, lw.k_norm, b.positions, b.slots,
+                                      self.rope_cos, self.rope_sin, c.rms_norm_eps, q, kc, vc)
+                attn = ws.attn[:N]
+                row_len = qkv.shape[1]
+                gate = qkv[:, D:]
+                if b.attn_bt_row is not None:
+                    # prefill: virtual rows of attn_q_per_seq queries; rows past N are padding (scratch)
+                    qp = b.attn_q_per_seq
+                    nv = b.attn_bt_row.shape[0]
+                    paged_attention(ws.q[: nv * qp].view(-1, Hq, D), kc, vc, b.block_table, b.attn_seq_lens, qp,
+                                    ws.attn[: nv * qp].view(-1, Hq, D), gate=ws.qkv[: nv * qp, D:], gate_ld=row_len,
+                                    gate_head_stride=2 * D, max_pages=b.max_pages, bt_row=b.attn_bt_row)
+                else:
+                    paged_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, b.q_per_seq,
+                                    attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
+                                    max_pages=b.max_pages)
+                cC.gemm(attn, lw.w_o, out=h, residual=h)
+                ai += 1
+            else:
+                mixed = ws.mixed[:N]
+                cC.gemm(y, lw.w_in, out=mixed)
+                o = ws.gdn_out[:N]
+                gdn_decode(mixed, self.gdn_shape, gdn[gi], lw.conv_w, lw.A_log, lw.dt_bias, lw.g_norm, b.n_commit,
+                           b.seq_slot, o, b.q_per_seq, b.parity, b.commit_current, gdn_scratch, c.rms_norm_eps)
+                cC.gemm(o, lw.w_out, out=h, residual=h)
+                gi += 1
+            cC.rmsnorm(h, None, lw.post_norm, y, c.rms_norm_eps, True)
+            moe_forward(y, h, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, c.num_experts_per_tok, ws.moe,
+                        out=h, renorm=c.norm_topk_prob)
+        cC.rmsnorm(h, None, self.final_norm, y, c.rms_norm_eps, True)
+        return y
+
+    def logits(self, hidden: torch.Tensor, out: torch.Tensor | None = None, fp32: bool = False):
+        return C().gemm(hidden, self.lm_head, out=out, out_fp32=fp32)
+
+
+class Workspace:
+    """All per-step activations for up to ``max_tokens`` rows (fixed addresses: CUDA-graph safe)."""
+
+    def __init__(self, model: HybridModel, max_tokens: int):
+        c = model.cfg
+        dev = model.device
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        H = c.hidden_size
+        self.max_tokens = max_tokens
+        self.h = torch.empty(max_tokens, H, **bf)
+        self.y = torch.empty(max_tokens, H, **bf)
+        D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_kv_heads
+        self.qkv = torch.empty(max_tokens + 8, Hq * 2 * D + 2 * Hkv * D, **bf)
+        self.q = torch.empty(max_tokens + 8, Hq * D, **bf)
+        self.attn = torch.empty(max_tokens + 8, Hq * D, **bf)
+        gs = model.gdn_shape
+        self.mixed = torch.empty(max_tokens, gs.mixed_dim, **bf)
+        self.gdn_out = torch.empty(max_tokens, gs.Hv * gs.Dv, **bf)
+        self.moe = MoEWorkspace(max_tokens, c.num_experts, c.num_experts_per_tok, H, c.moe_intermediate_size,
+                                c.shared_expert_intermediate_size, dev)

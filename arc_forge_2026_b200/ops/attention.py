@@ -21,19 +21,24 @@ def plan_splits(num_seqs: int, Hkv: int, max_pages: int, num_sms: int = 148) -> 
 
 
 def paged_attention(q, kcache, vcache, block_table, seq_lens, q_per_seq, out, gate=None, gate_ld=0,
-                    gate_head_stride=0, splits=None, max_pages=None):
+                    gate_head_stride=0, splits=None, max_pages=None, window=0, bt_row=None):
+    """``max_pages`` bounds the pages any sequence spans (it sizes the split plan; defaults to the table width).
+    ``window`` > 0 restricts each query to its last ``window`` keys. ``bt_row`` maps (virtual) sequences to
+    block-table rows (prefill chunks of 8 queries share their sequence's row)."""
     D = q.shape[-1]
+    mp = max_pages if max_pages is not None else block_table.shape[1]
+    if window > 0:
+        mp = min(mp, window // PAGE + 2)
     if splits is None:
-        mp = max_pages if max_pages is not None else block_table.shape[1]
         splits, pps = plan_splits(seq_lens.shape[0], kcache.shape[1], mp)
     else:
-        pps = math.ceil(block_table.shape[1] / splits)
+        pps = math.ceil(mp / splits)
     C().paged_attention(q, kcache, vcache, block_table, seq_lens, q_per_seq, 1.0 / math.sqrt(D), out, gate,
-                        gate_ld, gate_head_stride, splits, pps)
+                        gate_ld, gate_head_stride, splits, pps, window, bt_row)
     return out
 
 
-def paged_attention_reference(q, kcache, vcache, block_table, seq_lens, q_per_seq, gate=None):
+def paged_attention_reference(q, kcache, vcache, block_table, seq_lens, q_per_seq, gate=None, window=0):
     """fp32 oracle. q [S*qp, Hq, D]; gate [S*qp, Hq, D] or None."""
     S = seq_lens.shape[0]
     Hq, D = q.shape[1], q.shape[2]
@@ -50,7 +55,10 @@ def paged_attention_reference(q, kcache, vcache, block_table, seq_lens, q_per_se
         vv = v.repeat_interleave(rep, 0)
         sc = torch.einsum("thd,hld->htl", qq, kk) / math.sqrt(D)
         pos = torch.arange(L - q_per_seq, L, device=q.device)
-        mask = torch.arange(L, device=q.device)[None, :] > pos[:, None]
+        keys = torch.arange(L, device=q.device)[None, :]
+        mask = keys > pos[:, None]
+        if window > 0:
+            mask = mask | (keys <= pos[:, None] - window)
         sc = sc.masked_fill(mask[None], float("-inf"))
         o = torch.einsum("htl,hld->thd", torch.softmax(sc, -1), vv)
         out[s * q_per_seq:(s + 1) * q_per_seq] = o

@@ -1,0 +1,264 @@
+"""Speculative serving engine on one GPU (the EP variant in ``parallel/ep_engine.py`` reuses it per rank).
+
+One decode cycle for all resident sessions (fixed shapes, no host inputs, CUDA-graph replayable):
+
+1. ``build_window``: verify rows [anchor, d1..dK] at positions ctx..ctx+K, KV slots from the page table;
+2. target forward over S*(K+1) rows (GDN layers commit the previous cycle's accepted prefix on the fly);
+3. LM head + token selection (argmax or Gumbel-max sampling);
+4. ``spec_accept``: accepted prefix (greedy match, or seeded Bernoulli(p) for benchmarks), emitted tokens,
+   ctx += m+1, next anchor;
+5. drafter: inject the window rows' context K/V, then propose the next K drafts from a block
+   [anchor, mask x K-1] conditioned on the target hidden state of the last committed row.
+
+The cycle alternates the GDN pending-buffer parity, so two graphs are captured and replayed in turn. The host
+reads back only the emitted tokens of each cycle (pinned, asynchronous) and keeps page allocation one cycle ahead.
+Prefill runs the target over the prompt in chunks (attention as virtual rows of 8 queries sharing the page-table
+row; GDN in commit-all mode) and injects the prompt tail into the drafter cache.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from ..config import ServeConfig
+from ..models.drafter import Drafter
+from ..models.hybrid import HybridModel, StepBatch
+from ..ops import C
+from ..ops.attention import PAGE
+from ..ops.gdn import GdnScratch
+
+PREFILL_CHUNK = 2048
+
+
+@dataclass
+class Session:
+    sid: int
+    row: int
+    prompt: list[int]
+    max_new_tokens: int
+    generated: list[int] = field(default_factory=list)
+    done: bool = False
+
+
+class SpecEngine:
+    def __init__(self, model: HybridModel, drafter: Drafter | None, scfg: ServeConfig, max_sessions: int,
+                 max_context: int, num_pages: int | None = None):
+        self.model, self.drafter, self.scfg = model, drafter, scfg
+        dev = model.device
+        self.device = dev
+        S = self.S = max_sessions
+        K = self.K = scfg.spec_k if drafter is not None else 0
+        W = self.W = K + 1
+        self.max_context = max_context
+        self.maxp = math.ceil((max_context + 2 * W + 8) / PAGE)
+        num_pages = (num_pages or S * self.maxp) + 1
+        # the last page is a scratch sink: rows without a session point at it, so their (ignored) window
+        # writes never land in another session's pages
+        self.scratch_page = num_pages - 1
+        self.alloc = C().PageAllocator(num_pages - 1, PAGE)
+        self.kv = model.new_kv_cache(num_pages)
+        self.gdn = model.new_gdn_states(S, W)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.block_table = torch.full((S, self.maxp), self.scratch_page, **i32)
+        self.bt_host = torch.full((S, self.maxp), self.scratch_page, dtype=torch.int32).pin_memory()
+        self.ctx_len = torch.zeros(S, **i32)
+        self.anchor = torch.zeros(S, **i32)
+        self.drafts = torch.zeros(S, max(K, 1), **i32)
+        self.win_ids = torch.zeros(S * W, **i32)
+        self.win_pos = torch.zeros(S * W, **i32)
+        self.win_slots = torch.zeros(S * W, **i32)
+        self.attn_len = torch.zeros(S, **i32)
+        self.seq_slot = torch.arange(S, **i32)
+        self.n_commit = torch.zeros(S, **i32)
+        self.tgt_tok = torch.zeros(S * W, **i32)
+        self.out_tokens = torch.zeros(S, W, **i32)
+        self.out_count = torch.zeros(S, **i32)
+        self.last_row = torch.zeros(S, **i32)
+        self.step = torch.zeros(1, **i32)
+        self.total = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.active = torch.zeros(S, **i32)
+        self.ws = model.new_workspace(max(S * W, PREFILL_CHUNK))
+        self.logits = torch.empty(max(S * W, 8), model.cfg.vocab_size, dtype=torch.bfloat16, device=dev)
+        self.parity = 0
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.sessions: dict[int, Session] = {}
+        self.free_rows = list(range(S))
+        self.out_host = torch.zeros(S, W, dtype=torch.int32).pin_memory()
+        self.cnt_host = torch.zeros(S, dtype=torch.int32).pin_memory()
+        if drafter is not None:
+            dc = drafter.cfg
+            self.ring = dc.window // PAGE + 3
+            dpages = S * self.ring
+            self.dkv = drafter.new_kv_cache(dpages)
+            p = torch.arange(self.maxp, device=dev)
+            self.d_block_table = (torch.arange(S, device=dev)[:, None] * self.ring + p[None, :] % self.ring).int()
+            self.dws = drafter.new_workspace(max(S * W, PREFILL_CHUNK))
+            self.d_ids = torch.zeros(S * K, **i32)
+            self.d_pos = torch.zeros(S * K, **i32)
+            self.d_slots = torch.zeros(S * K, **i32)
+            self.d_attn_len = torch.zeros(S, **i32)
+            self.win_dslots = torch.zeros(S * W, **i32)
+            self.scratch_ids = torch.zeros(S * W, **i32)
+            self.scratch_pos = torch.zeros(S * W, **i32)
+            self.scratch_len = torch.zeros(S, **i32)
+            self.cond = torch.empty(S, model.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+        self.mode = {"greedy": 0, "rejection": 0, "bernoulli": 1}[scfg.accept_mode]
+        self.gdn_scratch = GdnScratch(model.gdn_shape, 1, PREFILL_CHUNK, dev)
+
+    # ------------------------------------------------------------------ one cycle (device only)
+    def _cycle(self, parity: int):
+        cC, m = C(), self.model
+        S, K, W = self.S, self.K, self.W
+        cC.build_window(self.anchor, self.drafts if K else None, 0, self.ctx_len, self.block_table, self.win_ids,
+                        self.win_pos, self.win_slots, self.attn_len, self.step, W, 0)
+        b = StepBatch(self.win_ids, self.win_pos, self.win_slots, self.block_table, self.attn_len, self.seq_slot,
+                      self.n_commit, W, parity, max_pages=self.maxp)
+        hidden = m.forward(b, self.kv, self.gdn, self.ws)
+        logits = self.logits[: S * W]
+        m.logits(hidden, out=logits)
+        cC.select_tokens(logits, m.cfg.vocab_size, self.tgt_tok, float(self.scfg.temperature), self.scfg.seed,
+                         self.step)
+        if self.drafter is not None:  # drafter slots of the window positions (before ctx advances)
+            cC.build_window(self.anchor, self.drafts, 0, self.ctx_len, self.d_block_table, self.scratch_ids,
+                            self.scratch_pos, self.win_dslots, self.scratch_len, None, W, 0)
+        cC.spec_accept(self.win_ids.view(S, W), self.tgt_tok.view(S, W), self.seq_slot, self.active, self.ctx_len,
+                       self.n_commit, self.out_tokens, self.out_count, self.anchor, self.last_row, self.step,
+                       self.total, self.mode, float(self.scfg.accept_prob), self.scfg.seed)
+        if self.drafter is not None:
+            d = self.drafter
+            d.inject(self.win_ids, hidden, self.win_pos, self.win_dslots, self.dkv, self.dws)
+            cC.build_window(self.anchor, None, d.mask_id, self.ctx_len, self.d_block_table, self.d_ids, self.d_pos,
+                            self.d_slots, self.d_attn_len, None, K, 0)
+            cC.gather_rows(hidden, self.last_row, self.cond)
+            d.propose(self.d_ids, self.cond, self.d_pos, self.d_slots, self.d_block_table, self.d_attn_len,
+                      self.dkv, self.dws, self.drafts, S, max_pages=self.maxp)
+
+    def capture(self):
+        """Capture one graph per GDN parity (warm-up runs first so every lazy allocation happens outside)."""
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            for p in (0, 1):
+                self._cycle(p)
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        for p in (0, 1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._cycle(p)
+            self.graphs[p] = g
+        torch.cuda.synchronize()
+
+    def run_cycle(self):
+        if self.graphs:
+            self.graphs[self.parity].replay()
+        else:
+            self._cycle(self.parity)
+        self.parity ^= 1
+
+    # ------------------------------------------------------------------ host side
+    def _sync_pages(self, rows=None):
+        """Refresh the page-table rows of live sessions (host, native allocator) and upload the table."""
+        rows = set(range(self.S) if rows is None else rows)
+        for s in self.sessions.values():
+            if s.row in rows:
+                self.alloc.fill_row(s.sid, self.bt_host, s.row)
+                n = len(self.alloc.pages(s.sid))
+                self.bt_host[s.row, n:] = self.scratch_page
+        self.block_table.copy_(self.bt_host, non_blocking=True)
+
+    def add_session(self, sid: int, prompt: list[int], max_new_tokens: int):
+        if not self.free_rows:
+            raise RuntimeError("no free session slot")
+        if len(prompt) + max_new_tokens + 2 * self.W > self.max_context:
+            raise ValueError("prompt + max_new_tokens exceed max_context")
+        row = self.free_rows.pop(0)
+        sess = Session(sid, row, list(prompt), max_new_tokens)
+        self.sessions[sid] = sess
+        self.alloc.ensure(sid, len(prompt) + 2 * self.W + 8)
+        self._sync_pages([row])
+        self._prefill(sess)
+        return sess
+
+    @torch.no_grad()
+    def _prefill(self, sess: Session):
+        cC, m = C(), self.model
+        dev = self.device
+        L = len(sess.prompt)
+        ids_all = torch.tensor(sess.prompt, dtype=torch.int32, device=dev)
+        pages = torch.tensor(self.alloc.pages(sess.sid), dtype=torch.int64, device=dev)
+        slot_row = torch.tensor([sess.row], dtype=torch.int32, device=dev)
+        for st in self.gdn:  # fresh recurrent state for this row
+            st.conv[sess.row].zero_()
+            st.ssm[sess.row].zero_()
+        hidden_last = None
+        for c0 in range(0, L, PREFILL_CHUNK):
+            T = min(PREFILL_CHUNK, L - c0)
+            pos = torch.arange(c0, c0 + T, device=dev, dtype=torch.int32)
+            slots = (pages[pos.long() // PAGE] * PAGE + (pos.long() % PAGE)).int()
+            nv = (T + 7) // 8
+            vlen = torch.clamp(torch.arange(1, nv + 1, device=dev, dtype=torch.int32) * 8 + c0, max=c0 + nv * 8)
+            b = StepBatch(ids_all[c0:c0 + T].contiguous(), pos, slots, self.block_table, None, slot_row,
+                          self.n_commit, T, 0, commit_current=True, max_pages=self.maxp,
+                          attn_bt_row=torch.full((nv,), sess.row, dtype=torch.int32, device=dev),
+                          attn_seq_lens=vlen, attn_q_per_seq=8)
+            hidden = m.forward(b, self.kv, self.gdn, self.ws, self.gdn_scratch)
+            if self.drafter is not None:
+                keep = max(0, T - (self.drafter.cfg.window + 64))
+                dslots = (self.d_block_table[sess.row, (pos.long() // PAGE)] * PAGE + pos.long() % PAGE).int()
+                self.drafter.inject(ids_all[c0 + keep:c0 + T].contiguous(), hidden[keep:T], pos[keep:].contiguous(),
+                                    dslots[keep:].contiguous(), self.dkv, self.dws)
+            hidden_last = hidden[T - 1:T]
+        logits = self.logits[:1]
+        m.logits(hidden_last, out=logits)
+        tok = torch.empty(1, dtype=torch.int32, device=dev)
+        cC.select_tokens(logits, m.cfg.vocab_size, tok, 0.0, 0, None)
+        r = sess.row
+        self.ctx_len[r] = L
+        self.anchor[r] = tok[0]
+        self.n_commit[r] = 0
+        self.active[r] = 1
+        if self.drafter is not None:  # first drafts: propose from the prefill's last hidden state
+            self.drafts[r].fill_(0)
+        sess.generated.append(int(tok.item()))
+
+    def release(self, sid: int):
+        sess = self.sessions.pop(sid)
+        self.active[sess.row] = 0
+        self.alloc.release(sid)
+        self.bt_host[sess.row] = self.scratch_page
+        self.free_rows.append(sess.row)
+
+    def step(self) -> dict[int, list[int]]:
+        """One cycle for every session + host bookkeeping; returns the tokens emitted per session."""
+        for s in self.sessions.values():  # pages for this cycle's window (at most W new tokens)
+            self.alloc.ensure(s.sid, len(s.prompt) + len(s.generated) + 2 * self.W + 8)
+        self._sync_pages()
+        self.run_cycle()
+        self.out_host.copy_(self.out_tokens, non_blocking=True)
+        self.cnt_host.copy_(self.out_count, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        emitted = {}
+        for s in list(self.sessions.values()):
+            n = int(self.cnt_host[s.row])
+            toks = self.out_host[s.row, :n].tolist()
+            room = s.max_new_tokens - len(s.generated)
+            toks = toks[:room]
+            s.generated.extend(toks)
+            emitted[s.sid] = toks
+            if len(s.generated) >= s.max_new_tokens:
+                s.done = True
+                self.active[s.row] = 0
+        return emitted
+
+    def generate(self, prompts: list[list[int]], max_new_tokens: int) -> list[list[int]]:
+        for i, p in enumerate(prompts):
+            self.add_session(i, p, max_new_tokens)
+        while any(not s.done for s in self.sessions.values()):
+            self.step()
+        outs = [self.sessions[i].generated[:max_new_tokens] for i in range(len(prompts))]
+        for i in range(len(prompts)):
+            self.release(i)
+        return outs

@@ -64,7 +64,14 @@ def bench_moe(T=640, E=320, H=2048, I=512, k=10):
                                   ws.hq, ws.hs, None, None, None)
     w2 = lambda: c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.offsets, ws.hq, ws.hs, False, None,  # noqa
                                  None, ws.y, ws.weights[:T].view(-1), ws.row_entry)
-    out = []
+    dbg = torch.zeros(148 * 4 * 3, dtype=torch.int64, device=dev)
+    c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.offsets, ws.xq, ws.xs, True, ws.hq, ws.hs, None, None, None,
+                    dbg)
+    torch.cuda.synchronize()
+    d = dbg.view(148, 4, 3).float()
+    prof = {"kernel": "moe_w13_int3_roles", "wait_frac": [round(float(x), 3) for x in (d[:, :, 0] / d[:, :, 1]).mean(0)],
+            "cycles_per_kstep": round(float((d[:, 0, 1] / d[:, 0, 2].clamp_min(1)).mean()), 1)}
+    out = [prof]
     for name, fn, wbytes, rows, kdim, ncols in (
             ("moe_w13_int3", w13, bank.w13_codes.nbytes + bank.w13_scales.nbytes, n, H, 2 * I),
             ("moe_w2_int3", w2, bank.w2_codes.nbytes + bank.w2_scales.nbytes, n, I, H)):

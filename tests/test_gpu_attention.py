@@ -38,3 +38,26 @@ def test_paged_attention(D, Hq, Hkv, qp, lens, splits):
     check_status()
     ref = paged_attention_reference(q, kc, vc, perm, seq_lens, qp, gate=gate_view)
     assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("window", [64, 1024])
+def test_paged_attention_window_and_virtual_rows(window):
+    """Sliding window (drafter) and prefill-style virtual sequences sharing one block-table row."""
+    g = torch.Generator(device="cpu").manual_seed(window)
+    D, Hq, Hkv, qp = 128, 16, 2, 4
+    L = 3000
+    maxp = (L + 63) // 64
+    kc = torch.randn(maxp + 2, Hkv, 64, D, generator=g).bfloat16().to(dev)
+    vc = torch.randn(maxp + 2, Hkv, 64, D, generator=g).bfloat16().to(dev)
+    bt = torch.randperm(maxp + 2, generator=g)[:maxp].view(1, maxp).int().to(dev)
+    # three virtual sequences = query chunks ending at 1000, 2000, 3000 of the same sequence
+    ends = [1000, 2000, 3000]
+    seq_lens = torch.tensor(ends, dtype=torch.int32, device=dev)
+    bt_row = torch.zeros(3, dtype=torch.int32, device=dev)
+    q = torch.randn(3 * qp, Hq, D, generator=g).bfloat16().to(dev)
+    out = torch.empty_like(q)
+    paged_attention(q, kc, vc, bt, seq_lens, qp, out, window=window, bt_row=bt_row, max_pages=maxp)
+    torch.cuda.synchronize()
+    check_status()
+    ref = paged_attention_reference(q, kc, vc, bt.expand(3, maxp), seq_lens, qp, window=window)
+    assert _rel(out, ref) < 1e-2
