@@ -77,7 +77,7 @@ int rmsnorm(const void* x, void* residual, const void* w, void* y, int rows, int
 // the paged cache at slots[t] (page = slot / page_size): cache layout [num_pages, Hkv, page_size, D].
 // cos/sin come from a table [max_pos, rot/2] built in fp64 on the host. One warp per (token, head);
 // the head vector is staged in shared memory so each lane can read its rotation partner.
-__global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, int T, int Hq, int Hkv, int D,
+__global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, int ld, int T, int Hq, int Hkv, int D,
                                           int rot, const __nv_bfloat16* __restrict__ qw,
                                           const __nv_bfloat16* __restrict__ kw, const int* __restrict__ positions,
                                           const int* __restrict__ slots, const float* __restrict__ cos_t,
@@ -91,7 +91,7 @@ __global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv,
   const int heads = Hq + 2 * Hkv;
   if (gw >= T * heads) return;
   const int t = gw / heads, h = gw % heads;
-  const int row_len = Hq * 2 * D + 2 * Hkv * D;
+  const int row_len = ld;  // row stride of the projection output (>= Hq*2D + 2*Hkv*D)
   const __nv_bfloat16* src;
   int kind;  // 0 q, 1 k, 2 v
   if (h < Hq) {
@@ -138,7 +138,7 @@ __global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv,
   }
 }
 
-int qk_norm_rope_store(const void* qkv, int T, int Hq, int Hkv, int D, int rot, const void* qw, const void* kw,
+int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, int rot, const void* qw, const void* kw,
                        const int* positions, const int* slots, const float* cos_t, const float* sin_t, float eps,
                        void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st) {
   if (D > 256 || rot > D || rot % 2) return 3;
@@ -146,7 +146,7 @@ int qk_norm_rope_store(const void* qkv, int T, int Hq, int Hkv, int D, int rot, 
   const int warps = 8;
   const int total = T * (Hq + 2 * Hkv);
   qk_norm_rope_store_kernel<<<(total + warps - 1) / warps, warps * 32, 0, st>>>(
-      (const __nv_bfloat16*)qkv, T, Hq, Hkv, D, rot, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, positions,
+      (const __nv_bfloat16*)qkv, ld, T, Hq, Hkv, D, rot, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, positions,
       slots, cos_t, sin_t, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)kcache, (__nv_bfloat16*)vcache, page_size);
   return (int)cudaGetLastError();
 }

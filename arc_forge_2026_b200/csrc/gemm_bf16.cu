@@ -39,7 +39,9 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_n = blockIdx.x, tile_m = blockIdx.y;
+  // M tiles vary fastest: the CTAs that share a weight (B) tile run together, so B streams from HBM once while
+  // the (small) activation tiles stay in L2
+  const int tile_m = blockIdx.x, tile_n = blockIdx.y;
   // split-K range of this CTA
   const int num_kb_total = (K + S::BK - 1) / S::BK;
   const int splits = gridDim.z;
@@ -232,7 +234,7 @@ static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, in
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
     attr = true;
   }
-  dim3 grid((N + BN - 1) / BN, (M + S::BM - 1) / S::BM, splits);
+  dim3 grid((M + S::BM - 1) / S::BM, (N + BN - 1) / BN, splits);
   kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, M, N, K, epi, status);
   return (int)cudaGetLastError();
 }

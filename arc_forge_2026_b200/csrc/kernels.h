@@ -10,7 +10,7 @@ namespace afb {
 // elementwise.cu
 int rmsnorm(const void* x, void* residual, const void* w, void* y, int rows, int H, float eps, int zero_centered,
             cudaStream_t st);
-int qk_norm_rope_store(const void* qkv, int T, int Hq, int Hkv, int D, int rot, const void* qw, const void* kw,
+int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, int rot, const void* qw, const void* kw,
                        const int* positions, const int* slots, const float* cos_t, const float* sin_t, float eps,
                        void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st);
 int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, int* ids, float* weights,
@@ -73,7 +73,7 @@ int gdn_decode(const GdnArgs& a, int parity, cudaStream_t st);
 
 // sampling.cu
 int select_tokens(const void* logits, int ld, int rows, int V, int* out, float temperature, uint64_t seed,
-                  const int* step, cudaStream_t st);
+                  const int* step, uint32_t* status, cudaStream_t st);
 struct SpecArgs {
   const int* window = nullptr;   // [S, K+1] verify window tokens (anchor, drafts)
   const int* target = nullptr;   // [S, K+1] target choice after each window row
@@ -108,5 +108,14 @@ struct WindowArgs {
 };
 int build_window(const WindowArgs& a, cudaStream_t st);
 int gather_rows(const void* src, const int* idx, void* out, int rows, int H, cudaStream_t st);
+
+// train_kernels.cu
+int int3_dequant(const void* codes, const float* scales, int E, int R, int K, void* out, cudaStream_t st);
+int int3_scale_grad(const void* codes, const void* dW, int E, int R, int K, float* dS, cudaStream_t st);
+int fp8_block_fakequant(const float* w, int N, int K, void* out, float* scale_inv, cudaStream_t st);
+int topk_tail_kl(const float* z, int ldz, int rows, int V, const long long* ids, int k, const float* t_lp,
+                 const float* t_tail, int reverse, float grad_scale, float* loss, void* dz, int ldd, cudaStream_t st);
+int adamw(float* p, const float* g, void* m, void* v, void* w, size_t n, float lr, float b1, float b2, float eps,
+          float wd, int step, cudaStream_t st);
 
 }  // namespace afb

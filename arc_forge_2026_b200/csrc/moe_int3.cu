@@ -15,13 +15,16 @@
 // so each 8-code selector word is one AND/OR of a plane and a shifted H, and one byte-permute maps 4 selectors
 // to 4 e4m3 bytes through an 8-entry table held in two registers.
 //
-// One persistent CTA per SM, warp-specialised: a ring of raw stages feeds a ring of dequantised tiles (4 deep for
-// w13, 6 for w2) and the MMA runs up to 8 (w13) / 16 (w2) groups ahead of the epilogue in TMEM:
+// One persistent CTA per SM, warp-specialised; the dequant and epilogue roles are latency-bound chains, so each has
+// 8 warps. A ring of raw stages feeds a ring of dequantised tiles and the MMA runs up to 8 (w13) / 16 (w2) groups
+// ahead of the epilogue in TMEM:
 //   warp 0      loader: bulk copies of the code/scale tiles and of the activation scales, TMA of the activation
 //               rows (no multicast)
-//   warps 1-4   dequant: codes -> e4m3 (c-4) into the 128-byte-swizzled A tile, then arrive
-//   warp 5      MMA: M=128 (weight rows) x N=32 (tokens) x K=32 per op, one 128-K group per accumulator buffer
-//   warps 6-9   epilogue: per group D * s_w * s_x into registers; at the end of a chunk:
+//   warps 1-8   dequant: codes -> e4m3 (c-4) into the 128-byte-swizzled A tile (one row per thread for w13,
+//               half a row for w2), then arrive
+//   warp 9      MMA: M=128 (weight rows) x N=32 (tokens) x K=32 per op, one 128-K group per accumulator buffer
+//   warps 10-17 epilogue (two per TMEM lane quadrant, 16 token columns each): per group D * s_w * s_x into
+//               registers; at the end of a chunk:
 //               PAIR (w13): h = silu(gate) * up, quantised to e4m3 per (token, 128-column group) for w2
 //               !PAIR (w2): y = acc * route_weight, bf16
 // A work unit is (expert, 128 output rows [+ the matching 128 up rows when PAIR]) x chunks of 32 tokens.
@@ -54,15 +57,15 @@ struct Layout {
   static constexpr uint32_t RAW_BYTES = SX_OFF + NTOK * 4;
   static constexpr uint32_t RAW = (RAW_BYTES + 1023) & ~1023u;
   // w13 (PAIR): one CTA per SM; w2: two CTAs per SM (half the shared memory and TMEM each)
-  static constexpr int CTAS_PER_SM = PAIR ? 1 : 2;
-  static constexpr int RS = PAIR ? 4 : 4;     // raw stages
-  static constexpr int AS = PAIR ? 4 : 3;     // dequantised stages
-  static constexpr int NBUF = PAIR ? 8 : 8;   // TMEM accumulator buffers (T * 32 columns each)
+  static constexpr int CTAS_PER_SM = 1;
+  static constexpr int RS = PAIR ? 4 : 6;     // raw stages
+  static constexpr int AS = PAIR ? 4 : 6;     // dequantised stages
+  static constexpr int NBUF = PAIR ? 8 : 16;  // TMEM accumulator buffers (T * 32 columns each)
   static constexpr uint32_t A_STAGE = T * A_TILE;
   static constexpr uint32_t A_OFF = RS * RAW;
   static constexpr uint32_t OFFS_OFF = A_OFF + AS * A_STAGE;        // int offsets[MAX_E + 1]
-  static constexpr uint32_t RED_OFF = OFFS_OFF + (MAX_E + 1) * 4;   // float [4][32]
-  static constexpr uint32_t BAR_OFF = (RED_OFF + 4 * 32 * 4 + 7) & ~7u;
+  static constexpr uint32_t RED_OFF = OFFS_OFF + (MAX_E + 1) * 4;   // float [2 halves][4 quads][16]
+  static constexpr uint32_t BAR_OFF = (RED_OFF + 2 * 4 * 16 * 4 + 7) & ~7u;
   // full[RS], empty[RS], afull[AS], aempty[AS], dfull[NBUF], dempty[NBUF], tmem slot
   static constexpr uint32_t TOTAL = BAR_OFF + (2 * RS + 2 * AS + 2 * NBUF) * 8 + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512 / CTAS_PER_SM;
@@ -109,8 +112,28 @@ AFB_DEV void dequant_row(const uint32_t* src, uint8_t* tile, int r) {
   }
 }
 
+// dequantise half a row (codes 64*hf .. 64*hf+63)
+AFB_DEV void dequant_half_row(const uint32_t* src, uint8_t* tile, int r, int hf) {
+  const uint2* p = reinterpret_cast<const uint2*>(src + 6 * hf);  // words 6hf .. 6hf+5 (8-byte aligned)
+  const uint2 a = p[0], b = p[1], c = p[2];
+  const uint32_t w[6] = {a.x, a.y, b.x, b.y, c.x, c.y};
+#pragma unroll
+  for (int qq = 0; qq < 2; ++qq) {
+    const int q = hf * 2 + qq;
+    uint32_t o[8];
+    decode32(w[3 * qq], w[3 * qq + 1], w[3 * qq + 2], o);
+    *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// warp roles (18 warps): 0 loader, 1-8 dequant, 9 MMA (+TMEM alloc), 10-17 epilogue
+namespace moe {
+constexpr int W_DQ0 = 1, N_DQ = 8, W_MMA = 9, W_EP0 = 10, N_EP = 8, THREADS = 18 * 32;
+}
+
 template <bool PAIR>
-__global__ void __launch_bounds__(320, PAIR ? 1 : 2)
+__global__ void __maxnreg__(112)
     moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmX, MoeGemmArgs args, uint32_t* status) {
   using L = moe::Layout<PAIR>;
   constexpr int RS = L::RS, AS = L::AS, NBUF = L::NBUF;
@@ -124,7 +147,7 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
   uint64_t* dempty = dfull + NBUF;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + NBUF);
   int* off = reinterpret_cast<int*>(smem + L::OFFS_OFF);
-  float* red = reinterpret_cast<float*>(smem + L::RED_OFF);  // [4 warps][32 tokens] amax exchange
+  float* red = reinterpret_cast<float*>(smem + L::RED_OFF);  // [2 halves][4 quads][16 tokens] amax exchange
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = args.num_experts;
@@ -136,19 +159,19 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
   if (threadIdx.x == 0) {
     for (int s = 0; s < RS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4 + 1 + 4);  // dequant warps + MMA commit + epilogue warps
+      mbar_init(&empty[s], moe::N_DQ + 1 + moe::N_EP);  // dequant warps + MMA commit + epilogue warps
     }
     for (int s = 0; s < AS; ++s) {
-      mbar_init(&afull[s], 4);
+      mbar_init(&afull[s], moe::N_DQ);
       mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&dfull[b], 1);
-      mbar_init(&dempty[b], 4);
+      mbar_init(&dempty[b], moe::N_EP);
     }
     fence_mbar_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  if (warp == moe::W_MMA) tmem_alloc(tmem_slot, L::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -195,9 +218,11 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
         }
         __syncwarp();
         bail = __shfl_sync(0xffffffffu, bail, 0);
-      } else if (warp >= 1 && warp <= 4) {
-        // ---------------------------------------------------------------- dequant
-        const int r = threadIdx.x - 32;  // 0..127: row of the weight tile
+      } else if (warp >= moe::W_DQ0 && warp < moe::W_DQ0 + moe::N_DQ) {
+        // ---------------------------------------------------------------- dequant: 256 threads
+        const int q = threadIdx.x - 32 * moe::W_DQ0;  // 0..255
+        const int r = q & 127;                         // row of the weight tile
+        const int part = q >> 7;                       // PAIR: tile 0/1; otherwise half of the row
         for (int g = 0; g < KG; ++g, ++kstep) {
           const int s = kstep % RS;
           const int as = kstep % AS;
@@ -209,10 +234,11 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
           }
           const uint8_t* st = smem + s * L::RAW;
           uint8_t* at = smem + L::A_OFF + as * L::A_STAGE;
-#pragma unroll
-          for (int t = 0; t < L::T; ++t)
-            dequant_row(reinterpret_cast<const uint32_t*>(st + L::C_OFF + t * moe::CODE_TILE) + r * 12,
-                        at + t * moe::A_TILE, r);
+          if (PAIR)
+            dequant_row(reinterpret_cast<const uint32_t*>(st + L::C_OFF + part * moe::CODE_TILE) + r * 12,
+                        at + part * moe::A_TILE, r);
+          else
+            dequant_half_row(reinterpret_cast<const uint32_t*>(st + L::C_OFF) + r * 12, at, r, part);
           fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the tensor core
           __syncwarp();
           if (lane == 0) {
@@ -220,7 +246,7 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
             mbar_arrive(&empty[s]);
           }
         }
-      } else if (warp == 5) {
+      } else if (warp == moe::W_MMA) {
         // ---------------------------------------------------------------- MMA
         constexpr uint32_t idesc = idesc_e4m3(128, moe::NTOK);
         for (int g = 0; g < KG; ++g, ++kstep) {
@@ -252,14 +278,17 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
           __syncwarp();
         }
       } else {
-        // ---------------------------------------------------------------- epilogue (warps 6..9)
+        // ---------------------------------------------------------------- epilogue (warps 10..17)
+        // each TMEM lane quadrant is read by two warps: half 0 takes token columns 0..15, half 1 columns 16..31
         const int quad = warp & 3;
+        const int half = (warp - moe::W_EP0) >> 2;
         const int r = quad * 32 + lane;  // TMEM lane = row of the weight tile
-        float acc0[moe::NTOK], acc1[PAIR ? moe::NTOK : 1];
+        constexpr int NH = moe::NTOK / 2;
+        float acc0[NH], acc1[PAIR ? NH : 1];
 #pragma unroll
-        for (int i = 0; i < moe::NTOK; ++i) acc0[i] = 0.f;
+        for (int i = 0; i < NH; ++i) acc0[i] = 0.f;
 #pragma unroll
-        for (int i = 0; i < (PAIR ? moe::NTOK : 1); ++i) acc1[i] = 0.f;
+        for (int i = 0; i < (PAIR ? NH : 1); ++i) acc1[i] = 0.f;
         for (int g = 0; g < KG; ++g, ++kstep) {
           const int s = kstep % RS;
           const int b = kstep % NBUF;
@@ -269,58 +298,56 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
           }
           tc_fence_after();
           const uint8_t* st = smem + s * L::RAW;
-          const float* sx = reinterpret_cast<const float*>(st + L::SX_OFF);
+          const float* sx = reinterpret_cast<const float*>(st + L::SX_OFF) + half * NH;
           const float sw0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L::SW_OFF)[r]);
           const float sw1 = PAIR ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L::SW_OFF + 256)[r]) : 0.f;
-          const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * L::T * moe::NTOK);
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            float d0[16], d1[16];
-            tmem_ld16(ta + hf * 16, d0);
-            if (PAIR) tmem_ld16(ta + moe::NTOK + hf * 16, d1);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float x = sx[hf * 16 + i];
-              acc0[hf * 16 + i] = fmaf(sw0 * x, d0[i], acc0[hf * 16 + i]);
-              if (PAIR) acc1[hf * 16 + i] = fmaf(sw1 * x, d1[i], acc1[hf * 16 + i]);
-            }
-          }
+          const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * L::T * moe::NTOK + half * NH);
+          float d0[NH], d1[PAIR ? NH : 1];
+          tmem_ld16(ta, d0);
+          if (PAIR) tmem_ld16(ta + moe::NTOK, d1);
+          tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&dempty[b]);
-            mbar_arrive(&empty[s]);
+          if (lane == 0) mbar_arrive(&dempty[b]);
+#pragma unroll
+          for (int i = 0; i < NH; ++i) {
+            const float x = sx[i];
+            acc0[i] = fmaf(sw0 * x, d0[i], acc0[i]);
+            if (PAIR) acc1[i] = fmaf(sw1 * x, d1[i], acc1[i]);
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
         }
         if (bail) break;
+        const int t0 = half * NH;  // first token column of this warp
         if (PAIR) {
           // h = silu(gate) * up -> e4m3 with a scale per (token, this 128-column group)
           const int col = j * 128 + r;  // intermediate column
+          float* rd = red + half * 4 * NH;
 #pragma unroll
-          for (int i = 0; i < moe::NTOK; ++i) {
+          for (int i = 0; i < NH; ++i) {
             acc0[i] = silu(acc0[i]) * acc1[i];
             const float m = warp_max(fabsf(acc0[i]));
-            if (lane == 0) red[quad * 32 + i] = m;
+            if (lane == 0) rd[quad * NH + i] = m;
           }
-          named_bar(1, 128);
+          named_bar(1 + half, 128);
 #pragma unroll
-          for (int i = 0; i < moe::NTOK; ++i) {
-            if (i >= cn) break;
-            const float amax = fmaxf(fmaxf(red[i], red[32 + i]), fmaxf(red[64 + i], red[96 + i]));
+          for (int i = 0; i < NH; ++i) {
+            if (t0 + i >= cn) break;
+            const float amax = fmaxf(fmaxf(rd[i], rd[NH + i]), fmaxf(rd[2 * NH + i], rd[3 * NH + i]));
             const float sc = amax > 0.f ? amax / 448.f : 1.f;
             const __nv_fp8_e4m3 q(acc0[i] / sc);
-            args.out_q[(size_t)(crow + i) * args.out_ld + col] = *reinterpret_cast<const uint8_t*>(&q);
-            if (r == 0) args.out_scales[(size_t)j * args.ld_os + crow + i] = sc;
+            args.out_q[(size_t)(crow + t0 + i) * args.out_ld + col] = *reinterpret_cast<const uint8_t*>(&q);
+            if (r == 0) args.out_scales[(size_t)j * args.ld_os + crow + t0 + i] = sc;
           }
-          named_bar(1, 128);  // red is reused by the next chunk
+          named_bar(1 + half, 128);  // rd is reused by the next chunk
         } else {
           const int col = j * 128 + r;  // hidden column
 #pragma unroll
-          for (int i = 0; i < moe::NTOK; ++i) {
-            if (i >= cn) break;
-            const float w = args.route_w ? args.route_w[args.row_entry[crow + i]] : 1.f;
-            reinterpret_cast<__nv_bfloat16*>(args.out_bf16)[(size_t)(crow + i) * args.out_ld + col] =
+          for (int i = 0; i < NH; ++i) {
+            if (t0 + i >= cn) break;
+            const float w = args.route_w ? args.route_w[args.row_entry[crow + t0 + i]] : 1.f;
+            reinterpret_cast<__nv_bfloat16*>(args.out_bf16)[(size_t)(crow + t0 + i) * args.out_ld + col] =
                 __float2bfloat16(acc0[i] * w);
           }
         }
@@ -328,15 +355,15 @@ __global__ void __launch_bounds__(320, PAIR ? 1 : 2)
     }
   }
 #undef AFB_TIMED_WAIT
-  if (args.dbg && lane == 0 && (warp == 0 || warp == 1 || warp == 5 || warp == 6)) {
-    const int role = warp == 0 ? 0 : warp == 1 ? 1 : warp == 5 ? 2 : 3;
+  if (args.dbg && lane == 0 && (warp == 0 || warp == moe::W_DQ0 || warp == moe::W_MMA || warp == moe::W_EP0)) {
+    const int role = warp == 0 ? 0 : warp == moe::W_DQ0 ? 1 : warp == moe::W_MMA ? 2 : 3;
     args.dbg[(blockIdx.x * 4 + role) * 3 + 0] = t_wait;
     args.dbg[(blockIdx.x * 4 + role) * 3 + 1] = clock64() - t_start;
     args.dbg[(blockIdx.x * 4 + role) * 3 + 2] = kstep;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == moe::W_MMA) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, L::TMEM_COLS);
@@ -359,7 +386,7 @@ int moe_int3_gemm(const MoeGemmArgs& a, int pair, int num_sms, uint32_t* status,
       cudaFuncSetAttribute(moe_int3_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
       attr = true;
     }
-    moe_int3_gemm_kernel<true><<<grid, 320, L::TOTAL, st>>>(tx, a, status);
+    moe_int3_gemm_kernel<true><<<grid, moe::THREADS, L::TOTAL, st>>>(tx, a, status);
   } else {
     using L = moe::Layout<false>;
     static bool attr = false;
@@ -367,7 +394,7 @@ int moe_int3_gemm(const MoeGemmArgs& a, int pair, int num_sms, uint32_t* status,
       cudaFuncSetAttribute(moe_int3_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
       attr = true;
     }
-    moe_int3_gemm_kernel<false><<<grid, 320, L::TOTAL, st>>>(tx, a, status);
+    moe_int3_gemm_kernel<false><<<grid, moe::THREADS, L::TOTAL, st>>>(tx, a, status);
   }
   return (int)cudaGetLastError();
 }

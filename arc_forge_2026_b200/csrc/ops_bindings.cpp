@@ -28,8 +28,9 @@ void qk_norm_rope_store_op(const at::Tensor& qkv, int64_t Hq, int64_t Hkv, int64
   AFB_CHECK_DT(cos_t, at::kFloat);
   const int T = qkv.size(0);
   TORCH_CHECK(qkv.size(1) == Hq * 2 * D + 2 * Hkv * D, "qkv width");
+  TORCH_CHECK(qkv.stride(1) == 1, "qkv inner stride");
   const int page_size = kcache.size(2);
-  check_rc(afb::qk_norm_rope_store(qkv.data_ptr(), T, Hq, Hkv, D, rot, qw.data_ptr(), kw.data_ptr(),
+  check_rc(afb::qk_norm_rope_store(qkv.data_ptr(), qkv.stride(0), T, Hq, Hkv, D, rot, qw.data_ptr(), kw.data_ptr(),
                                    ptr<int>(positions), ptr<int>(slots), ptr<float>(cos_t), ptr<float>(sin_t),
                                    (float)eps, q_out.data_ptr(), kcache.data_ptr(), vcache.data_ptr(), page_size,
                                    stream()),
@@ -232,7 +233,8 @@ void select_tokens_op(const at::Tensor& logits, int64_t V, at::Tensor& out, doub
   AFB_CHECK_DT(out, at::kInt);
   TORCH_CHECK(logits.stride(1) == 1, "logits inner stride");
   check_rc(afb::select_tokens(logits.data_ptr(), logits.stride(0), logits.size(0), V, ptr<int>(out),
-                              (float)temperature, (uint64_t)seed, optr<int>(step), stream()),
+                              (float)temperature, (uint64_t)seed, optr<int>(step), status_ptr(logits.get_device()),
+                              stream()),
            "select_tokens");
 }
 
@@ -289,6 +291,52 @@ void gather_rows_op(const at::Tensor& src, const at::Tensor& idx, at::Tensor& ou
            "gather_rows");
 }
 
+// ---- training kernels
+void int3_dequant_op(const at::Tensor& codes, const at::Tensor& scales, at::Tensor& out) {
+  AFB_CHECK_DT(scales, at::kFloat);
+  AFB_CHECK_CONTIG(codes);
+  AFB_CHECK_CONTIG(scales);
+  const int E = codes.size(0), R = codes.size(1) * 128, K = codes.size(2) * 128;
+  TORCH_CHECK(out.numel() == (int64_t)E * R * K && out.is_contiguous(), "int3_dequant: out must be [E, R, K]");
+  check_rc(afb::int3_dequant(codes.data_ptr(), ptr<float>(scales), E, R, K, out.data_ptr(), stream()), "int3_dequant");
+}
+
+void int3_scale_grad_op(const at::Tensor& codes, const at::Tensor& dW, at::Tensor& dS) {
+  AFB_CHECK_DT(dW, at::kBFloat16);
+  AFB_CHECK_CONTIG(dW);
+  const int E = codes.size(0), R = codes.size(1) * 128, K = codes.size(2) * 128;
+  check_rc(afb::int3_scale_grad(codes.data_ptr(), dW.data_ptr(), E, R, K, ptr<float>(dS), stream()), "int3_scale_grad");
+}
+
+void fp8_block_fakequant_op(const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> scale_inv) {
+  AFB_CHECK_DT(w, at::kFloat);
+  AFB_CHECK_CONTIG(w);
+  check_rc(afb::fp8_block_fakequant(ptr<float>(w), w.size(0), w.size(1), out.data_ptr(), optr<float>(scale_inv),
+                                    stream()),
+           "fp8_block_fakequant");
+}
+
+void topk_tail_kl_op(const at::Tensor& z, const at::Tensor& ids, const at::Tensor& t_lp, const at::Tensor& t_tail,
+                     bool reverse, double grad_scale, at::Tensor& loss, at::Tensor& dz) {
+  AFB_CHECK_DT(z, at::kFloat);
+  AFB_CHECK_DT(ids, at::kLong);
+  AFB_CHECK_DT(dz, at::kBFloat16);
+  check_rc(afb::topk_tail_kl(ptr<float>(z), z.stride(0), z.size(0), z.size(1), ptr<long long>(ids), ids.size(1),
+                             ptr<float>(t_lp), ptr<float>(t_tail), reverse, (float)grad_scale, ptr<float>(loss),
+                             dz.data_ptr(), dz.stride(0), stream()),
+           "topk_tail_kl");
+}
+
+void adamw_op(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, c10::optional<at::Tensor> w, double lr,
+              double b1, double b2, double eps, double wd, int64_t step) {
+  AFB_CHECK_DT(p, at::kFloat);
+  AFB_CHECK_DT(g, at::kFloat);
+  AFB_CHECK_DT(m, at::kBFloat16);
+  check_rc(afb::adamw(ptr<float>(p), ptr<float>(g), m.data_ptr(), v.data_ptr(), optr<void>(w), p.numel(), (float)lr,
+                      (float)b1, (float)b2, (float)eps, (float)wd, (int)step, stream()),
+           "adamw");
+}
+
 void swiglu_op(const at::Tensor& x, at::Tensor& y) {
   const int T = x.size(0), I = x.size(1) / 2;
   check_rc(afb::swiglu(x.data_ptr(), y.data_ptr(), T, I, stream()), "swiglu");
@@ -314,6 +362,11 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("x_scales"), py::arg("pair"), py::arg("out_q"), py::arg("out_scales"), py::arg("out_bf16"),
         py::arg("route_w"), py::arg("row_entry"), py::arg("dbg") = py::none());
   m.def("swiglu", &swiglu_op);
+  m.def("int3_dequant", &int3_dequant_op);
+  m.def("int3_scale_grad", &int3_scale_grad_op);
+  m.def("fp8_block_fakequant", &fp8_block_fakequant_op);
+  m.def("topk_tail_kl", &topk_tail_kl_op);
+  m.def("adamw", &adamw_op);
   m.def("select_tokens", &select_tokens_op);
   m.def("spec_accept", &spec_accept_op);
   m.def("build_window", &build_window_op);

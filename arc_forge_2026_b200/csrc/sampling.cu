@@ -32,7 +32,7 @@ AFB_DEV float uniform01(uint64_t seed, uint64_t a, uint64_t b, uint64_t c) {
 // one CTA per row; 8 bf16 per thread per step; ties -> lower index
 __global__ void __launch_bounds__(256) select_tokens_kernel(const __nv_bfloat16* __restrict__ logits, int ld, int V,
                                                             int* __restrict__ out, float inv_temp, uint64_t seed,
-                                                            const int* __restrict__ step) {
+                                                            const int* __restrict__ step, uint32_t* status) {
   const int row = blockIdx.x;
   const __nv_bfloat16* z = logits + (size_t)row * ld;
   const uint64_t st = step ? (uint64_t)*step : 0;
@@ -84,16 +84,20 @@ __global__ void __launch_bounds__(256) select_tokens_kernel(const __nv_bfloat16*
         best = sv[w];
         bi = si[w];
       }
+    if (bi >= V) {  // every logit NaN: report it and hand out a valid id
+      flag_error(status, AFB_ERR_BOUNDS);
+      bi = 0;
+    }
     out[row] = bi;
   }
 }
 
 int select_tokens(const void* logits, int ld, int rows, int V, int* out, float temperature, uint64_t seed,
-                  const int* step, cudaStream_t st) {
+                  const int* step, uint32_t* status, cudaStream_t st) {
   if (!rows) return 0;
   if (ld % 8) return 3;
   select_tokens_kernel<<<rows, 256, 0, st>>>((const __nv_bfloat16*)logits, ld, V, out,
-                                             temperature > 0.f ? 1.f / temperature : 0.f, seed, step);
+                                             temperature > 0.f ? 1.f / temperature : 0.f, seed, step, status);
   return (int)cudaGetLastError();
 }
 

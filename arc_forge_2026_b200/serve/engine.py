@@ -76,7 +76,7 @@ class SpecEngine:
         self.out_tokens = torch.zeros(S, W, **i32)
         self.out_count = torch.zeros(S, **i32)
         self.last_row = torch.zeros(S, **i32)
-        self.step = torch.zeros(1, **i32)
+        self.step_ctr = torch.zeros(1, **i32)
         self.total = torch.zeros(1, dtype=torch.int64, device=dev)
         self.active = torch.zeros(S, **i32)
         self.ws = model.new_workspace(max(S * W, PREFILL_CHUNK))
@@ -112,19 +112,19 @@ class SpecEngine:
         cC, m = C(), self.model
         S, K, W = self.S, self.K, self.W
         cC.build_window(self.anchor, self.drafts if K else None, 0, self.ctx_len, self.block_table, self.win_ids,
-                        self.win_pos, self.win_slots, self.attn_len, self.step, W, 0)
+                        self.win_pos, self.win_slots, self.attn_len, self.step_ctr, W, 0)
         b = StepBatch(self.win_ids, self.win_pos, self.win_slots, self.block_table, self.attn_len, self.seq_slot,
                       self.n_commit, W, parity, max_pages=self.maxp)
         hidden = m.forward(b, self.kv, self.gdn, self.ws)
         logits = self.logits[: S * W]
         m.logits(hidden, out=logits)
         cC.select_tokens(logits, m.cfg.vocab_size, self.tgt_tok, float(self.scfg.temperature), self.scfg.seed,
-                         self.step)
+                         self.step_ctr)
         if self.drafter is not None:  # drafter slots of the window positions (before ctx advances)
             cC.build_window(self.anchor, self.drafts, 0, self.ctx_len, self.d_block_table, self.scratch_ids,
                             self.scratch_pos, self.win_dslots, self.scratch_len, None, W, 0)
         cC.spec_accept(self.win_ids.view(S, W), self.tgt_tok.view(S, W), self.seq_slot, self.active, self.ctx_len,
-                       self.n_commit, self.out_tokens, self.out_count, self.anchor, self.last_row, self.step,
+                       self.n_commit, self.out_tokens, self.out_count, self.anchor, self.last_row, self.step_ctr,
                        self.total, self.mode, float(self.scfg.accept_prob), self.scfg.seed)
         if self.drafter is not None:
             d = self.drafter
