@@ -101,14 +101,15 @@ __global__ void __launch_bounds__(DK) gdn_conv_prep_kernel(GdnArgs a, int parity
   }
 }
 
-// Two threads per value column (adjacent lanes), each holding half of the DK state rows in registers;
-// dot products over DK are reduced with one shuffle.
-template <int DK, int DV>
-__global__ void __launch_bounds__(2 * DV) gdn_recurrent_kernel(GdnArgs a, int parity) {
-  constexpr int HK = DK / 2;
+// QT threads per value column (adjacent lanes), each holding DK/QT state rows in registers; dot products over DK
+// are reduced with log2(QT) shuffles. QT=4 (512 threads) doubles the warps per SM over one thread pair per column,
+// so the strided state loads of some warps overlap the recurrence of others.
+template <int DK, int DV, int QT>
+__global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, int parity) {
+  constexpr int HK = DK / QT;
   const int seq = blockIdx.x, h = blockIdx.y;
   const int slot = a.seq_slot[seq];
-  const int v = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int v = threadIdx.x / QT, part = threadIdx.x % QT;
   const int T = a.q_per_seq;
   const int kh = h / (a.Hv / a.Hk);
   const int nq = a.Hk * DK;
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(2 * DV) gdn_recurrent_kernel(GdnArgs a, int pa
   __shared__ float red[32];
 
   float S[HK];
-  float* sp = a.ssm_state + (((size_t)slot * a.Hv + h) * DK + half * HK) * DV + v;
+  float* sp = a.ssm_state + (((size_t)slot * a.Hv + h) * DK + part * HK) * DV + v;
 #pragma unroll
   for (int k = 0; k < HK; ++k) S[k] = sp[(size_t)k * DV];
 
@@ -133,18 +134,23 @@ __global__ void __launch_bounds__(2 * DV) gdn_recurrent_kernel(GdnArgs a, int pa
     __syncthreads();
     return base;
   };
+  auto reduce = [&](float x) {
+#pragma unroll
+    for (int o = 1; o < QT; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+  };
   auto update = [&](size_t base) {
     const float* gb = a.pend_gb + base * (2 * a.Hv);
     const float decay = __expf(gb[h]), beta = gb[a.Hv + h];
     const float vv = __bfloat162float(a.pend_v[base * (a.Hv * DV) + h * DV + v]);
-    const float* kk = kq[0] + half * HK;
+    const float* kk = kq[0] + part * HK;
     float mem = 0.f;
 #pragma unroll
     for (int k = 0; k < HK; ++k) {
       S[k] *= decay;
       mem = fmaf(kk[k], S[k], mem);
     }
-    mem += __shfl_xor_sync(0xffffffffu, mem, 1);
+    mem = reduce(mem);
     const float delta = beta * (vv - mem);
 #pragma unroll
     for (int k = 0; k < HK; ++k) S[k] = fmaf(kk[k], delta, S[k]);
@@ -158,18 +164,18 @@ __global__ void __launch_bounds__(2 * DV) gdn_recurrent_kernel(GdnArgs a, int pa
   }
   for (int t = 0; t < T; ++t) {
     update(load_kq(cur, t));
-    const float* qq = kq[1] + half * HK;
+    const float* qq = kq[1] + part * HK;
     float o = 0.f;
 #pragma unroll
     for (int k = 0; k < HK; ++k) o = fmaf(qq[k], S[k], o);
-    o += __shfl_xor_sync(0xffffffffu, o, 1);
+    o = reduce(o);
     // gated RMSNorm over the DV outputs of this head (each column counted once)
-    const float ss = warp_sum(half ? 0.f : o * o);
+    const float ss = warp_sum(part ? 0.f : o * o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     float tot = 0.f;
-    for (int w = 0; w < (2 * DV) / 32; ++w) tot += red[w];
-    if (!half) {
+    for (int w = 0; w < (QT * DV) / 32; ++w) tot += red[w];
+    if (!part) {
       const size_t tok = (size_t)seq * T + t;
       const float z = __bfloat162float(a.mixed[tok * a.mixed_ld + a.z_off + h * DV + v]);
       const float y = o * rsqrtf(tot / DV + a.eps) * __bfloat162float(a.norm_w[v]) * silu(z);
@@ -189,11 +195,11 @@ int gdn_decode(const GdnArgs& a, int parity, cudaStream_t st) {
   if (a.Dk == 128 && a.Dv == 128) {
     if (C % 128) return 3;
     gdn_conv_prep_kernel<128><<<dim3(a.num_seqs, C / 128), 128, 0, st>>>(a, parity);
-    gdn_recurrent_kernel<128, 128><<<dim3(a.num_seqs, a.Hv), 256, 0, st>>>(a, parity);
+    gdn_recurrent_kernel<128, 128, 4><<<dim3(a.num_seqs, a.Hv), 512, 0, st>>>(a, parity);
   } else if (a.Dk == 64 && a.Dv == 64) {
     if (C % 64) return 3;
     gdn_conv_prep_kernel<64><<<dim3(a.num_seqs, C / 64), 64, 0, st>>>(a, parity);
-    gdn_recurrent_kernel<64, 64><<<dim3(a.num_seqs, a.Hv), 128, 0, st>>>(a, parity);
+    gdn_recurrent_kernel<64, 64, 2><<<dim3(a.num_seqs, a.Hv), 128, 0, st>>>(a, parity);
   } else {
     return 3;
   }

@@ -133,7 +133,7 @@ constexpr int W_DQ0 = 1, N_DQ = 8, W_MMA = 9, W_EP0 = 10, N_EP = 8, THREADS = 18
 }
 
 template <bool PAIR>
-__global__ void __maxnreg__(112)
+__global__ void __maxnreg__(104)
     moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmX, MoeGemmArgs args, uint32_t* status) {
   using L = moe::Layout<PAIR>;
   constexpr int RS = L::RS, AS = L::AS, NBUF = L::NBUF;

@@ -11,10 +11,11 @@ PAGE = 64
 
 
 def plan_splits(num_seqs: int, Hkv: int, max_pages: int, num_sms: int = 148) -> tuple[int, int]:
-    """Split KV so that the grid covers ~2 waves of SMs with >= 8 pages per split."""
+    """Split KV so that the grid covers ~6 waves of SMs (short tail when context lengths differ) while each split
+    keeps >= 12 pages to amortise its prologue."""
     ctas = max(1, num_seqs * Hkv)
     splits = 1
-    while ctas * splits < 2 * num_sms and math.ceil(max_pages / (splits * 2)) >= 8:
+    while ctas * splits < 6 * num_sms and math.ceil(max_pages / (splits * 2)) >= 12:
         splits *= 2
     pps = math.ceil(max(1, max_pages) / splits)
     return math.ceil(max(1, max_pages) / pps), pps

@@ -1,0 +1,261 @@
+"""Trainable QAD student: the hybrid MoE with INT3 experts (frozen codes, trainable fp32 group scales), block-FP8 QAT
+dense projections, an fp32 router, bf16 shared experts, and frozen norms / embeddings / LM head.
+
+Trainable parameter groups (names of the reference's QAD v2, ``training/work/qwen38fn_qad/train_qad.py:100-126``):
+``scale`` (expert w13/w2 scales), ``router``, ``shared`` (shared expert + its gate), ``dense_fp8`` (GDN
+in_proj_qkvz / out_proj, attention q/k/v), ``dense_bf16`` (GDN in_proj_ba, attention o_proj). Every trainable
+tensor is an fp32 master; the forward computes in bf16 (FP8 QAT weights round-trip through e4m3 128x128 blocks).
+
+Layers are activation-checkpointed (one layer's inputs kept, the rest recomputed in backward) so a 16k-token
+sequence fits with the dequantised expert banks of only one layer alive at a time.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+from torch.utils.checkpoint import checkpoint
+
+from ..config import FULL, ModelConfig
+from ..models import reference as R
+from ..quant.int3_tiles import codes_to_tiles
+from .fakequant import fp8_weight, int3_weight
+from .gdn_chunk import chunk_gated_delta_rule
+
+GROUPS = ("scale", "router", "shared", "dense_fp8", "dense_bf16")
+
+
+def _master(t: torch.Tensor) -> nn.Parameter:
+    return nn.Parameter(t.detach().float().clone())
+
+
+def grouped_linear(x: torch.Tensor, w: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
+    """x [R, K] rows sorted by expert, w [E, N, K], counts [E] -> [R, N]."""
+    if x.is_cuda and hasattr(torch, "_grouped_mm"):
+        offs = counts.cumsum(0).to(torch.int32)
+        return torch._grouped_mm(x, w.transpose(-2, -1), offs=offs)
+    outs, o = [], 0
+    for e, c in enumerate(counts.tolist()):
+        if c:
+            outs.append(x[o:o + c] @ w[e].t())
+        o += c
+    return torch.cat(outs) if outs else x.new_zeros(0, w.shape[1])
+
+
+class StudentMoE(nn.Module):
+    def __init__(self, cfg: ModelConfig, router, w13_codes, w13_scales, w2_codes, w2_scales, shared_gate, shared_up,
+                 shared_down, shared_expert_gate):
+        super().__init__()
+        self.cfg = cfg
+        self.router = _master(router)
+        self.register_buffer("w13_codes", w13_codes, persistent=True)
+        self.register_buffer("w2_codes", w2_codes, persistent=True)
+        self.w13_scales = _master(w13_scales)
+        self.w2_scales = _master(w2_scales)
+        self.shared_w13 = _master(torch.cat([shared_gate, shared_up]))
+        self.shared_down = _master(shared_down)
+        self.shared_expert_gate = _master(shared_expert_gate)
+
+    def forward(self, x):
+        c = self.cfg
+        T, H = x.shape
+        logits = x.float() @ self.router.t()
+        w, ids = R.route(logits, c.num_experts_per_tok, c.norm_topk_prob)
+        flat = ids.flatten()
+        order = torch.argsort(flat, stable=True)
+        counts = torch.bincount(flat, minlength=c.num_experts)
+        tok = order // c.num_experts_per_tok
+        xs = x[tok]
+        W13 = int3_weight(self.w13_scales, self.w13_codes).to(x.dtype)
+        h = grouped_linear(xs, W13, counts)
+        I = c.moe_intermediate_size
+        h = F.silu(h[:, :I].float()).to(x.dtype) * h[:, I:]
+        W2 = int3_weight(self.w2_scales, self.w2_codes).to(x.dtype)
+        y = grouped_linear(h, W2, counts)
+        y = y * w.flatten()[order][:, None].to(y.dtype)
+        out = torch.zeros_like(x).index_add(0, tok, y)
+        gu = x @ self.shared_w13.to(x.dtype).t()
+        Is = c.shared_expert_intermediate_size
+        sh = (F.silu(gu[:, :Is].float()).to(x.dtype) * gu[:, Is:]) @ self.shared_down.to(x.dtype).t()
+        sg = torch.sigmoid(x.float() @ self.shared_expert_gate.t()).to(x.dtype)
+        return out + sg * sh
+
+
+def layer_tensors_from_reference(L: R.DecoderLayer, codes_scales) -> dict:
+    m, moe = L.mixer, L.mlp
+    t = dict(in_norm=L.input_layernorm.weight, post_norm=L.post_attention_layernorm.weight)
+    if L.kind == FULL:
+        t.update(q_proj=m.q_proj.weight, k_proj=m.k_proj.weight, v_proj=m.v_proj.weight, o_proj=m.o_proj.weight,
+                 q_norm=m.q_norm.weight, k_norm=m.k_norm.weight)
+    else:
+        t.update(in_proj_qkvz=m.in_proj_qkvz.weight, in_proj_ba=m.in_proj_ba.weight, out_proj=m.out_proj.weight,
+                 conv1d=m.conv1d, A_log=m.A_log, dt_bias=m.dt_bias, g_norm=m.norm)
+    c13, s13, c2, s2 = codes_scales
+    t.update(router=moe.gate.weight, w13_codes=codes_to_tiles(c13), w13_scales=s13, w2_codes=codes_to_tiles(c2),
+             w2_scales=s2, shared_gate=moe.shared_gate_proj.weight, shared_up=moe.shared_up_proj.weight,
+             shared_down=moe.shared_down_proj.weight, shared_expert_gate=moe.shared_expert_gate.weight)
+    return {k: v.detach() for k, v in t.items()}
+
+
+def random_layer_tensors(cfg: ModelConfig, kind: str, device, gen: torch.Generator) -> dict:
+    """Random weights of one layer made on the device (INT3 codes as random tile words: every bit pattern is valid)."""
+    std = cfg.init_std
+    H = cfg.hidden_size
+
+    def rn(*shape, s=std):
+        return torch.randn(*shape, generator=gen, device=device) * s
+    t = dict(in_norm=torch.zeros(H, device=device), post_norm=torch.zeros(H, device=device))
+    if kind == FULL:
+        D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_kv_heads
+        t.update(q_proj=rn(Hq * 2 * D, H), k_proj=rn(Hkv * D, H), v_proj=rn(Hkv * D, H), o_proj=rn(H, Hq * D),
+                 q_norm=torch.zeros(D, device=device), k_norm=torch.zeros(D, device=device))
+    else:
+        Hv, Dv = cfg.linear_num_value_heads, cfg.linear_value_head_dim
+        dt = torch.exp(torch.empty(Hv, device=device).uniform_(math.log(1e-3), math.log(1e-1), generator=gen))
+        t.update(in_proj_qkvz=rn(cfg.gdn_qkvz_dim, H), in_proj_ba=rn(2 * Hv, H), out_proj=rn(H, Hv * Dv),
+                 conv1d=rn(cfg.gdn_conv_dim, cfg.linear_conv_kernel, s=0.3),
+                 A_log=torch.log(torch.empty(Hv, device=device).uniform_(1, 16, generator=gen)),
+                 dt_bias=dt + torch.log(-torch.expm1(-dt)), g_norm=torch.ones(Dv, device=device))
+    E, I, Is = cfg.num_experts, cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
+    t.update(router=rn(E, H),
+             w13_codes=torch.randint(-2**31, 2**31 - 1, (E, 2 * I // 128, H // 128, 128, 12), dtype=torch.int32,
+                                     device=device, generator=gen),
+             w13_scales=rn(E, 2 * I, H // 128, s=std / 2.3),
+             w2_codes=torch.randint(-2**31, 2**31 - 1, (E, H // 128, I // 128, 128, 12), dtype=torch.int32,
+                                    device=device, generator=gen),
+             w2_scales=rn(E, H, I // 128, s=std / 2.3),
+             shared_gate=rn(Is, H), shared_up=rn(Is, H), shared_down=rn(H, Is), shared_expert_gate=rn(1, H))
+    return t
+
+
+class StudentLayer(nn.Module):
+    def __init__(self, cfg: ModelConfig, kind: str, t: dict):
+        super().__init__()
+        self.cfg, self.kind = cfg, kind
+
+        def buf(name):
+            self.register_buffer(name, t[name].float().clone())
+        buf("in_norm")
+        buf("post_norm")
+        if kind == FULL:
+            for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                setattr(self, n, _master(t[n]))
+            buf("q_norm")
+            buf("k_norm")
+        else:
+            for n in ("in_proj_qkvz", "in_proj_ba", "out_proj"):
+                setattr(self, n, _master(t[n]))
+            for n in ("conv1d", "A_log", "dt_bias", "g_norm"):
+                buf(n)
+        self.moe = StudentMoE(cfg, t["router"], t["w13_codes"], t["w13_scales"], t["w2_codes"], t["w2_scales"],
+                              t["shared_gate"], t["shared_up"], t["shared_down"], t["shared_expert_gate"])
+
+    def groups(self):
+        g = {k: [] for k in GROUPS}
+        g["scale"] += [self.moe.w13_scales, self.moe.w2_scales]
+        g["router"].append(self.moe.router)
+        g["shared"] += [self.moe.shared_w13, self.moe.shared_down, self.moe.shared_expert_gate]
+        if self.kind == FULL:
+            g["dense_fp8"] += [self.q_proj, self.k_proj, self.v_proj]
+            g["dense_bf16"].append(self.o_proj)
+        else:
+            g["dense_fp8"] += [self.in_proj_qkvz, self.out_proj]
+            g["dense_bf16"].append(self.in_proj_ba)
+        return g
+
+    def _attn(self, x, B, T):
+        c = self.cfg
+        D = c.head_dim
+        qg = F.linear(x, fp8_weight(self.q_proj).to(x.dtype)).view(B, T, c.num_attention_heads, 2 * D)
+        q, gate = qg[..., :D], qg[..., D:].reshape(B, T, -1)
+        k = F.linear(x, fp8_weight(self.k_proj).to(x.dtype)).view(B, T, c.num_kv_heads, D)
+        v = F.linear(x, fp8_weight(self.v_proj).to(x.dtype)).view(B, T, c.num_kv_heads, D)
+        q, k = R.rms_norm(q, self.q_norm, c.rms_norm_eps), R.rms_norm(k, self.k_norm, c.rms_norm_eps)
+        cos, sin = R.rope_cos_sin(torch.arange(T, device=x.device), c.rotary_dim, c.rope_theta)
+        q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
+                                           enable_gqa=True).transpose(1, 2).reshape(B, T, -1)
+        o = o * torch.sigmoid(gate.float()).to(o.dtype)
+        return F.linear(o, self.o_proj.to(o.dtype))
+
+    def _gdn(self, x, B, T):
+        c = self.cfg
+        qkvz = F.linear(x, fp8_weight(self.in_proj_qkvz).to(x.dtype))
+        ba = F.linear(x, self.in_proj_ba.to(x.dtype))
+        mixed, z = qkvz[..., : c.gdn_conv_dim], qkvz[..., c.gdn_conv_dim:]
+        b, a = ba[..., : c.linear_num_value_heads], ba[..., c.linear_num_value_heads:]
+        mixed, _ = R.causal_conv1d(mixed, self.conv1d)
+        nk = c.linear_num_key_heads * c.linear_key_head_dim
+        q = mixed[..., :nk].reshape(B, T, c.linear_num_key_heads, -1)
+        k = mixed[..., nk:2 * nk].reshape(B, T, c.linear_num_key_heads, -1)
+        v = mixed[..., 2 * nk:].reshape(B, T, c.linear_num_value_heads, -1)
+        rep = c.linear_num_value_heads // c.linear_num_key_heads
+        q = (R.l2norm(q) * c.linear_key_head_dim ** -0.5).repeat_interleave(rep, 2)
+        k = R.l2norm(k).repeat_interleave(rep, 2)
+        g, beta = R.gdn_gates(b, a, self.A_log, self.dt_bias)
+        o, _ = chunk_gated_delta_rule(q, k, v, g, beta)
+        o = R.gated_rms_norm(o.to(x.dtype), z.reshape(B, T, c.linear_num_value_heads, -1), self.g_norm, c.rms_norm_eps)
+        return F.linear(o.reshape(B, T, -1), fp8_weight(self.out_proj).to(o.dtype))
+
+    def forward(self, x):
+        c = self.cfg
+        B, T, H = x.shape
+        y = R.rms_norm(x, self.in_norm, c.rms_norm_eps)
+        x = x + (self._attn(y, B, T) if self.kind == FULL else self._gdn(y, B, T))
+        y = R.rms_norm(x, self.post_norm, c.rms_norm_eps)
+        return x + self.moe(y.reshape(B * T, H)).reshape(B, T, H)
+
+
+class QADStudent(nn.Module):
+    def __init__(self, cfg: ModelConfig, ref: R.HybridMoE, codes_scales, compute_dtype=torch.bfloat16,
+                 checkpoint_layers: bool = True):
+        super().__init__()
+        self.cfg = cfg
+        self.dtype = compute_dtype
+        self.ckpt = checkpoint_layers
+        self.register_buffer("embed", ref.embed_tokens.weight.detach().to(compute_dtype).clone())
+        self.register_buffer("final_norm", ref.norm.weight.detach().float().clone())
+        self.register_buffer("lm_head", ref.lm_head.weight.detach().to(compute_dtype).clone())
+        self.layers = nn.ModuleList([StudentLayer(cfg, L.kind, layer_tensors_from_reference(L, codes_scales[i]))
+                                     for i, L in enumerate(ref.layers)])
+        self._lm_head_t = None
+
+    @property
+    def lm_head_t(self):
+        if self._lm_head_t is None or self._lm_head_t.device != self.lm_head.device:
+            self._lm_head_t = self.lm_head.t().contiguous()
+        return self._lm_head_t
+
+    def param_groups(self):
+        g = {k: [] for k in GROUPS}
+        for L in self.layers:
+            for k, v in L.groups().items():
+                g[k] += v
+        return g
+
+    def hidden(self, ids):
+        x = F.embedding(ids, self.embed)
+        for L in self.layers:
+            if self.ckpt and torch.is_grad_enabled():
+                x = checkpoint(L, x, use_reentrant=False)
+            else:
+                x = L(x)
+        return R.rms_norm(x, self.final_norm, self.cfg.rms_norm_eps)
+
+
+def random_student(cfg: ModelConfig, device, seed: int = 0, checkpoint_layers=True) -> "QADStudent":
+    """Student of ``cfg`` with random weights made directly on ``device`` (synthetic benchmarking)."""
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    st = QADStudent.__new__(QADStudent)
+    nn.Module.__init__(st)
+    st.cfg, st.dtype, st.ckpt, st._lm_head_t = cfg, torch.bfloat16, checkpoint_layers, None
+    H, V = cfg.hidden_size, cfg.vocab_size
+    st.register_buffer("embed", (torch.randn(V, H, generator=gen, device=dev) * cfg.init_std).to(torch.bfloat16))
+    st.register_buffer("final_norm", torch.zeros(H, device=dev))
+    st.register_buffer("lm_head", (torch.randn(V, H, generator=gen, device=dev) * cfg.init_std).to(torch.bfloat16))
+    st.layers = nn.ModuleList([StudentLayer(cfg, kind, random_layer_tensors(cfg, kind, dev, gen))
+                               for kind in cfg.layer_types])
+    return st

@@ -105,9 +105,61 @@ def bench_gemm(M=640):
     return out
 
 
+def bench_gdn(S=128, T=5):
+    from ..ops.gdn import GdnShape, GdnState, gdn_decode
+    peaks = load_peaks()
+    dev = "cuda"
+    sh = GdnShape(16, 128, 32, 128)
+    st = GdnState(sh, S, T, dev)
+    st.ssm.normal_(0, 0.02)
+    mixed = torch.randn(S * T, sh.mixed_dim, device=dev).bfloat16()
+    conv_w = torch.randn(sh.conv_dim, 4, device=dev) * 0.3
+    A_log = torch.zeros(sh.Hv, device=dev)
+    dt = torch.zeros(sh.Hv, device=dev)
+    nw = torch.ones(sh.Dv, device=dev).bfloat16()
+    n_commit = torch.full((S,), 3, dtype=torch.int32, device=dev)
+    slots = torch.arange(S, dtype=torch.int32, device=dev)
+    out = torch.empty(S * T, sh.Hv * sh.Dv, device=dev).bfloat16()
+    par = [0]
+
+    def fn():
+        gdn_decode(mixed, sh, st, conv_w, A_log, dt, nw, n_commit, slots, out, T, par[0] & 1)
+        par[0] += 1
+    ms = time_cuda(fn)
+    byts = 2 * st.ssm.nbytes + mixed.nbytes + out.nbytes
+    return [{"kernel": "gdn_decode(conv_prep+recurrent)", "S": S, "T": T, "ms": round(ms, 4), "bytes": byts,
+             "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)}]
+
+
+def bench_attn(S=128, T=5, seed=0):
+    from ..ops.attention import paged_attention
+    peaks = load_peaks()
+    dev = "cuda"
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(4096, 24577, (S,), generator=g) + T
+    pages = (lens + 63) // 64
+    P = int(pages.sum())
+    maxp = int(pages.max())
+    kc = torch.randn(P, 2, 64, 256, device=dev).bfloat16()
+    vc = torch.randn(P, 2, 64, 256, device=dev).bfloat16()
+    bt = torch.zeros(S, maxp, dtype=torch.int32)
+    o = 0
+    for i in range(S):
+        bt[i, : int(pages[i])] = torch.arange(o, o + int(pages[i]))
+        o += int(pages[i])
+    bt = bt.to(dev)
+    seq_lens = lens.int().to(dev)
+    q = torch.randn(S * T, 16, 256, device=dev).bfloat16()
+    out = torch.empty_like(q)
+    ms = time_cuda(lambda: paged_attention(q, kc, vc, bt, seq_lens, T, out, max_pages=maxp), flush_bytes=1 << 20)
+    byts = int(lens.sum()) * 2 * 2 * 256 * 2
+    return [{"kernel": "paged_attn_verify", "S": S, "T": T, "ms": round(ms, 4), "kv_bytes": byts,
+             "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)}]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "all"])
     ap.add_argument("--T", type=int, default=640)
     a = ap.parse_args()
     res = []
@@ -115,6 +167,10 @@ def main():
         res += bench_moe(T=a.T)
     if a.what in ("gemm", "all"):
         res += bench_gemm(M=a.T)
+    if a.what in ("gdn", "all"):
+        res += bench_gdn()
+    if a.what in ("attn", "all"):
+        res += bench_attn()
     for r in res:
         print(json.dumps(r))
 
