@@ -36,11 +36,11 @@ def test_student_forward_close_to_reference_and_trains():
     rel = ((h.float() - h_ref.float()).norm() / h_ref.float().norm()).item()
     assert rel < 0.2, rel
     # distillation against the reference teacher's top-8 targets decreases the loss
-    with torch.no_grad():
-        zt = ref(ids).reshape(-1, cfg.vocab_size)
+    with torch.no_grad():  # a sharper teacher than the student, so there is something to learn
+        zt = 3.0 * ref(ids).reshape(-1, cfg.vocab_size)
     t_ids, t_lp, t_tail = teacher_topk(zt, 8)
     groups = st.param_groups()
-    opt = AdamWBF16([{"params": groups[k], "lr": 3e-3} for k in groups])
+    opt = AdamWBF16([{"params": groups[k], "lr": 1e-4} for k in groups])
     losses = []
     for _ in range(6):
         opt.zero_grad()
@@ -50,5 +50,5 @@ def test_student_forward_close_to_reference_and_trains():
         assert st.layers[0].moe.w13_scales.grad is not None
         assert st.layers[3].q_proj.grad is not None
         opt.step()
-        losses.append(float(loss))
+        losses.append(float(loss.detach()))
     assert losses[-1] < losses[0]
