@@ -15,15 +15,15 @@
 // so each 8-code selector word is one AND/OR of a plane and a shifted H, and one byte-permute maps 4 selectors
 // to 4 e4m3 bytes through an 8-entry table held in two registers.
 //
-// One persistent CTA per SM, warp-specialised; the dequant and epilogue roles are latency-bound chains, so each has
-// 8 warps. A ring of raw stages feeds a ring of dequantised tiles and the MMA runs up to 8 (w13) / 16 (w2) groups
-// ahead of the epilogue in TMEM:
+// One persistent CTA per SM, warp-specialised; the dequant and epilogue roles are latency-bound chains, so they get
+// 6 and 8 warps. A ring of raw stages feeds a ring of dequantised tiles and the MMA runs up to 8 (w13) / 16 (w2)
+// groups ahead of the epilogue in TMEM:
 //   warp 0      loader: bulk copies of the code/scale tiles and of the activation scales, TMA of the activation
 //               rows (no multicast)
-//   warps 1-8   dequant: codes -> e4m3 (c-4) into the 128-byte-swizzled A tile (one row per thread for w13,
-//               half a row for w2), then arrive
-//   warp 9      MMA: M=128 (weight rows) x N=32 (tokens) x K=32 per op, one 128-K group per accumulator buffer
-//   warps 10-17 epilogue (two per TMEM lane quadrant, 16 token columns each): per group D * s_w * s_x into
+//   warps 1-6   dequant: codes -> e4m3 (c-4) into the 128-byte-swizzled A tile, in tasks of 32 codes spread
+//               evenly over the 192 threads, then arrive
+//   warp 7      MMA: M=128 (weight rows) x N=32 (tokens) x K=32 per op, one 128-K group per accumulator buffer
+//   warps 8-15  epilogue (two per TMEM lane quadrant, 16 token columns each): per group D * s_w * s_x into
 //               registers; at the end of a chunk:
 //               PAIR (w13): h = silu(gate) * up, quantised to e4m3 per (token, 128-column group) for w2
 //               !PAIR (w2): y = acc * route_weight, bf16
@@ -97,43 +97,23 @@ AFB_DEV void decode32(uint32_t L0, uint32_t L1, uint32_t H, uint32_t* o) {
   o[7] = __byte_perm(moe::E4M3_LO, moe::E4M3_HI, s3 >> 16);
 }
 
-// dequantise one 128-code row (12 words at `src`) into row `r` of a 128x128 e4m3 SW128 tile
-AFB_DEV void dequant_row(const uint32_t* src, uint8_t* tile, int r) {
-  const uint4 a = reinterpret_cast<const uint4*>(src)[0];
-  const uint4 b = reinterpret_cast<const uint4*>(src)[1];
-  const uint4 c = reinterpret_cast<const uint4*>(src)[2];
-  const uint32_t w[12] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t o[8];
-    decode32(w[3 * q], w[3 * q + 1], w[3 * q + 2], o);
-    *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-  }
-}
-
-// dequantise half a row (codes 64*hf .. 64*hf+63)
-AFB_DEV void dequant_half_row(const uint32_t* src, uint8_t* tile, int r, int hf) {
-  const uint2* p = reinterpret_cast<const uint2*>(src + 6 * hf);  // words 6hf .. 6hf+5 (8-byte aligned)
-  const uint2 a = p[0], b = p[1], c = p[2];
-  const uint32_t w[6] = {a.x, a.y, b.x, b.y, c.x, c.y};
-#pragma unroll
-  for (int qq = 0; qq < 2; ++qq) {
-    const int q = hf * 2 + qq;
-    uint32_t o[8];
-    decode32(w[3 * qq], w[3 * qq + 1], w[3 * qq + 2], o);
-    *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-  }
-}
-
-// warp roles (18 warps): 0 loader, 1-8 dequant, 9 MMA (+TMEM alloc), 10-17 epilogue
+// warp roles (16 warps = 4 per SM sub-partition, so 128 registers per thread fit; with 18 warps some
+// sub-partitions hold 5 and the per-thread budget drops below 100): 0 loader, 1-6 dequant, 7 MMA (+TMEM alloc),
+// 8-15 epilogue
 namespace moe {
-constexpr int W_DQ0 = 1, N_DQ = 8, W_MMA = 9, W_EP0 = 10, N_EP = 8, THREADS = 18 * 32;
+constexpr int W_DQ0 = 1, N_DQ = 6, W_MMA = 7, W_EP0 = 8, N_EP = 8, THREADS = 16 * 32;
+}
+
+// one dequant task = 32 codes (3 words at word offset 3*q of the row) -> 32 e4m3 bytes (2 swizzled chunks)
+AFB_DEV void dequant_task(const uint32_t* row_words, uint8_t* tile, int r, int q) {
+  uint32_t o[8];
+  decode32(row_words[3 * q], row_words[3 * q + 1], row_words[3 * q + 2], o);
+  *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q)) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 template <bool PAIR>
-__global__ void __maxnreg__(104)
+__global__ void __launch_bounds__(moe::THREADS, 1)
     moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmX, MoeGemmArgs args, uint32_t* status) {
   using L = moe::Layout<PAIR>;
   constexpr int RS = L::RS, AS = L::AS, NBUF = L::NBUF;
@@ -219,10 +199,10 @@ __global__ void __maxnreg__(104)
         __syncwarp();
         bail = __shfl_sync(0xffffffffu, bail, 0);
       } else if (warp >= moe::W_DQ0 && warp < moe::W_DQ0 + moe::N_DQ) {
-        // ---------------------------------------------------------------- dequant: 256 threads
-        const int q = threadIdx.x - 32 * moe::W_DQ0;  // 0..255
-        const int r = q & 127;                         // row of the weight tile
-        const int part = q >> 7;                       // PAIR: tile 0/1; otherwise half of the row
+        // ---------------------------------------------------------------- dequant: 192 threads, 32-code tasks
+        const int dq = threadIdx.x - 32 * moe::W_DQ0;  // 0..191
+        constexpr int NT = moe::N_DQ * 32;
+        constexpr int TASKS = L::T * 128 * 4;         // (tile, row, 32-code sub-group)
         for (int g = 0; g < KG; ++g, ++kstep) {
           const int s = kstep % RS;
           const int as = kstep % AS;
@@ -234,11 +214,12 @@ __global__ void __maxnreg__(104)
           }
           const uint8_t* st = smem + s * L::RAW;
           uint8_t* at = smem + L::A_OFF + as * L::A_STAGE;
-          if (PAIR)
-            dequant_row(reinterpret_cast<const uint32_t*>(st + L::C_OFF + part * moe::CODE_TILE) + r * 12,
-                        at + part * moe::A_TILE, r);
-          else
-            dequant_half_row(reinterpret_cast<const uint32_t*>(st + L::C_OFF) + r * 12, at, r, part);
+#pragma unroll 2
+          for (int task = dq; task < TASKS; task += NT) {
+            const int t = task >> 9, r = (task >> 2) & 127, sq = task & 3;
+            dequant_task(reinterpret_cast<const uint32_t*>(st + L::C_OFF + t * moe::CODE_TILE) + r * 12,
+                         at + t * moe::A_TILE, r, sq);
+          }
           fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the tensor core
           __syncwarp();
           if (lane == 0) {

@@ -1,0 +1,222 @@
+"""Quantisation-aware distillation (QAD) of the INT3 student against teacher top-k targets.
+
+Modes (the reference's ``training/work/qwen38fn_qad/train_qad.py:1-21``):
+
+* ``teacher`` -- run the teacher over the data and write ``qad-topk-v1`` targets (top-k ids, log-probs, tail) for
+  every supervised position;
+* ``train``   -- student forward (INT3 scale STE, FP8 QAT, fp32 router), fused LM-head + top-k tail KL (forward or
+  reverse), backward with per-layer recompute, global-norm clipping, bf16-state AdamW with one learning rate per
+  parameter group, and the scale invariants (a zero scale stays zero; no scale changes sign);
+* ``score``   -- the loss of the current student without updates.
+
+Distributed: one process per GPU (torchrun). Every rank trains on its own sequences; the trainable masters live in
+a ZeRO-style sharded optimizer (``parallel/shard_optim.py``): gradients are reduce-scattered, each rank updates its
+shard, masters are all-gathered. Checkpoints hold the trainable masters and optimizer state per rank plus a
+``trainer.json`` with the step and the plan hash; resume refuses a different plan. ``--export`` writes the trained
+tensors as a ``gean320-qad-v2-delta``.
+
+    python -m arc_forge_2026_b200.train.qad --mode train --preset qwen3next_80b --synthetic --steps 10
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+from ..config import QADConfig, preset
+from ..formats.topk_targets import TopKReader, TopKWriter, synthetic_targets
+from ..parallel.shard_optim import ShardedAdamW
+from .kl import teacher_topk
+from .losses import fused_topk_tail_kl
+from .optim import AdamWBF16, clip_grad_norm_
+from .student import QADStudent, random_student
+
+
+def lr_for(group: str, qc: QADConfig) -> float:
+    return {"scale": qc.lr_scale, "router": qc.lr_router}.get(group, qc.lr_dense)
+
+
+def build_optimizer(student: QADStudent, qc: QADConfig, sharded: bool = False, group=None):
+    groups = student.param_groups()
+    spec = [{"params": groups[g], "lr": lr_for(g, qc), "name": g} for g in groups if groups[g]]
+    if sharded:
+        return ShardedAdamW(spec, betas=qc.betas, weight_decay=qc.weight_decay, group=group)
+    return AdamWBF16(spec, betas=qc.betas, weight_decay=qc.weight_decay)
+
+
+def _scales(student: QADStudent):
+    return [p for L in student.layers for p in (L.moe.w13_scales, L.moe.w2_scales)]
+
+
+@torch.no_grad()
+def enforce_scale_invariants(student: QADStudent, signs: list[torch.Tensor] | None):
+    """Zero scales stay zero and no scale crosses zero (a group's sign belongs to its INT3 codes)."""
+    if signs is None:
+        return [torch.sign(p).to(torch.int8) for p in _scales(student)]
+    for p, s in zip(_scales(student), signs):
+        sf = s.float()
+        p.copy_(torch.where(sf == 0, torch.zeros_like(p), torch.where(torch.sign(p) != sf, sf * 1e-12, p)))
+    return signs
+
+
+def mask_zero_scale_grads(student: QADStudent, signs):
+    for p, s in zip(_scales(student), signs):
+        if p.grad is not None:
+            p.grad.masked_fill_(s == 0, 0.0)
+
+
+def train_step(student: QADStudent, opt, ids: torch.Tensor, targets: dict, qc: QADConfig, signs):
+    """One optimizer step over ``ids`` [B, T] (every position supervised). Returns (mean loss, grad norm)."""
+    sharded = isinstance(opt, ShardedAdamW)
+    opt.zero_grad(set_to_none=not sharded)
+    n = ids.numel()
+    h = student.hidden(ids).reshape(n, -1)
+    loss = fused_topk_tail_kl(h, student.lm_head, student.lm_head_t, targets["ids"], targets["lp"], targets["tail"],
+                              qc.direction) / n
+    loss.backward()
+    mask_zero_scale_grads(student, signs)
+    if sharded:
+        norm = opt.step(qc.grad_clip)
+    else:
+        norm = clip_grad_norm_([p for g in opt.param_groups for p in g["params"]], qc.grad_clip)
+        opt.step()
+    enforce_scale_invariants(student, signs)
+    return float(loss.detach()), norm
+
+
+def plan_hash(args) -> str:
+    keys = ("preset", "seq_len", "batch", "steps", "topk", "direction", "seed", "layers")
+    return hashlib.sha256(json.dumps({k: getattr(args, k) for k in keys}, sort_keys=True).encode()).hexdigest()[:16]
+
+
+def save_checkpoint(path: Path, student: QADStudent, opt, step: int, phash: str, rank: int):
+    path = Path(path)
+    path.mkdir(parents=True, exist_ok=True)
+    trainable = {n: p.detach() for n, p in student.named_parameters()}
+    torch.save({"params": trainable, "opt": opt.state_dict()}, path / f"rank{rank:03d}.pt.tmp")
+    os.replace(path / f"rank{rank:03d}.pt.tmp", path / f"rank{rank:03d}.pt")
+    if rank == 0:
+        (path / "trainer.json.tmp").write_text(json.dumps({"step": step, "plan": phash}) + "\n")
+        os.replace(path / "trainer.json.tmp", path / "trainer.json")
+
+
+def load_checkpoint(path: Path, student: QADStudent, opt, phash: str, rank: int) -> int:
+    meta = json.loads((Path(path) / "trainer.json").read_text())
+    if meta["plan"] != phash:
+        raise RuntimeError(f"checkpoint plan {meta['plan']} != this run's plan {phash}: refusing to resume")
+    st = torch.load(Path(path) / f"rank{rank:03d}.pt", map_location="cpu", weights_only=False)
+    with torch.no_grad():
+        for n, p in student.named_parameters():
+            p.copy_(st["params"][n])
+    opt.load_state_dict(st["opt"])
+    return int(meta["step"])
+
+
+def export(student: QADStudent, out: Path, meta: dict):
+    from ..formats.qad_delta import delta_tensors, export_delta
+    named = dict(student.named_parameters())
+    fp8 = {n for n in named if n.rsplit(".", 1)[-1] in ("q_proj", "k_proj", "v_proj", "in_proj_qkvz", "out_proj")}
+    scales = {n: n.replace("moe.w13_scales", "mlp.experts.w13_scales").replace("moe.w2_scales", "mlp.experts.w2_scales")
+              for n in named if n.endswith("_scales")}
+    return export_delta(delta_tensors(named, fp8, scales), out, meta)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", choices=["train", "teacher", "score"], default="train")
+    ap.add_argument("--preset", default="qwen3next_80b")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (0 = preset)")
+    ap.add_argument("--seq-len", dest="seq_len", type=int, default=16384)
+    ap.add_argument("--batch", type=int, default=1, help="sequences per rank per step")
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--topk", type=int, default=64)
+    ap.add_argument("--direction", default="reverse", choices=["forward", "reverse"])
+    ap.add_argument("--synthetic", action="store_true", help="random tokens and random valid teacher targets")
+    ap.add_argument("--targets", type=Path, help="qad-topk-v1 root (train/score)")
+    ap.add_argument("--out", type=Path, help="teacher: targets root; train: checkpoint directory")
+    ap.add_argument("--resume", action="store_true")
+    ap.add_argument("--export", type=Path)
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args(argv)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    if dev.type == "cuda":
+        torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl" if dev.type == "cuda" else "gloo", timeout=datetime.timedelta(seconds=600))
+    kw = {"num_layers": args.layers} if args.layers else {}
+    cfg = preset(args.preset, **kw)
+    qc = QADConfig(seq_len=args.seq_len, topk=args.topk, direction=args.direction)
+    student = random_student(cfg, dev, seed=args.seed)
+    gen = torch.Generator().manual_seed(args.seed * 7919 + rank)
+
+    def batch(step):
+        ids = torch.randint(0, cfg.vocab_size, (args.batch, args.seq_len), generator=gen).to(dev)
+        n = ids.numel()
+        if args.synthetic or args.targets is None:
+            t = synthetic_targets(n, args.topk, cfg.vocab_size, gen, dev)
+        else:
+            r = TopKReader(args.targets, "train")
+            start = ((step * world + rank) * n) % max(1, r.rows - n)
+            t = r.rows_slice(start, start + n, dev)
+        return ids, t
+
+    if args.mode == "teacher":
+        if args.out is None:
+            raise SystemExit("--out is required in teacher mode")
+        w = TopKWriter(args.out, "train", args.topk)
+        with torch.no_grad():
+            for step in range(args.steps):
+                ids, _ = batch(step)
+                h = student.hidden(ids).reshape(ids.numel(), -1)
+                z = (h @ student.lm_head.t()).float()
+                t_ids, t_lp, t_tail = teacher_topk(z, args.topk)
+                w.append(t_ids, t_lp, t_tail, ids.reshape(-1))
+        w.close({"source": "trainer-prefill", "teacher": args.preset})
+        return
+
+    opt = build_optimizer(student, qc, sharded=True, group=dist.group.WORLD if world > 1 else None)
+    signs = enforce_scale_invariants(student, None)
+    phash = plan_hash(args)
+    start = 0
+    if args.resume and args.out and (args.out / "trainer.json").exists():
+        start = load_checkpoint(args.out, student, opt, phash, rank)
+    for step in range(start, args.steps):
+        ids, t = batch(step)
+        t0 = time.perf_counter()
+        if args.mode == "score":
+            with torch.no_grad():
+                h = student.hidden(ids).reshape(ids.numel(), -1)
+                loss = float(fused_topk_tail_kl(h, student.lm_head, student.lm_head_t, t["ids"], t["lp"], t["tail"],
+                                                qc.direction) / ids.numel())
+            norm = 0.0
+        else:
+            loss, norm = train_step(student, opt, ids, t, qc, signs)
+        if dev.type == "cuda":
+            torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        if rank == 0:
+            print(json.dumps({"step": step, "loss": round(loss, 6), "grad_norm": round(norm, 4),
+                              "tok_s": round(ids.numel() * world / dt, 1),
+                              "peak_gib": round(torch.cuda.max_memory_allocated() / 2**30, 2)
+                              if dev.type == "cuda" else None}), flush=True)
+        if args.out and args.mode == "train":
+            save_checkpoint(args.out, student, opt, step + 1, phash, rank)
+    if args.export and rank == 0:
+        export(student, args.export, {"preset": args.preset, "plan": phash})
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

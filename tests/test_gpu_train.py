@@ -1,0 +1,97 @@
+"""GPU numerics of the QAD training kernels against their fp32 PyTorch oracles, and a tiny GPU training run."""
+import pytest
+import torch
+
+from arc_forge_2026_b200.ops import C, check_status
+from arc_forge_2026_b200.quant import fp8 as fp8q
+from arc_forge_2026_b200.quant.int3_tiles import codes_to_tiles
+from arc_forge_2026_b200.train.fakequant import FP8BlockSTE, Int3ScaleSTE
+from arc_forge_2026_b200.train.kl import teacher_topk, topk_tail_kl
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+def test_int3_dequant_and_scale_grad():
+    g = torch.Generator().manual_seed(0)
+    codes = torch.randint(0, 8, (3, 256, 384), generator=g, dtype=torch.uint8)
+    tiles = codes_to_tiles(codes)
+    scales = torch.randn(3, 256, 3, generator=g) * 0.01
+    w_cpu = Int3ScaleSTE.apply(scales, tiles)
+    w_gpu = Int3ScaleSTE.apply(scales.to(dev), tiles.to(dev))
+    assert torch.equal(w_gpu.cpu(), w_cpu)
+    dW = torch.randn(3, 256, 384, generator=g).bfloat16()
+    s_cpu = scales.clone().requires_grad_(True)
+    Int3ScaleSTE.apply(s_cpu, tiles).backward(dW)
+    s_gpu = scales.to(dev).requires_grad_(True)
+    Int3ScaleSTE.apply(s_gpu, tiles.to(dev)).backward(dW.to(dev))
+    torch.testing.assert_close(s_gpu.grad.cpu(), s_cpu.grad, rtol=1e-5, atol=1e-4)
+
+
+def test_fp8_block_fakequant():
+    g = torch.Generator().manual_seed(1)
+    w = torch.randn(300, 520, generator=g) * 0.05
+    ref = FP8BlockSTE.apply(w)
+    got = FP8BlockSTE.apply(w.to(dev)).cpu()
+    assert _rel(got, ref) < 2e-3  # the two sides may round a handful of values at ties differently
+    _, s = fp8q.quantize_weight_block(w.bfloat16().float())
+    sinv = torch.empty(3, 5, device=dev)
+    out = torch.empty(300, 520, dtype=torch.bfloat16, device=dev)
+    C().fp8_block_fakequant(w.to(dev), out, sinv)
+    torch.testing.assert_close(sinv.cpu(), s, rtol=1e-6, atol=0)
+
+
+@pytest.mark.parametrize("reverse", [False, True])
+def test_topk_tail_kl_kernel(reverse):
+    g = torch.Generator().manual_seed(2)
+    N, V, k = 37, 5000, 64
+    zt = torch.randn(N, V, generator=g) * 2
+    ids, lp, tail = teacher_topk(zt, k)
+    zs = torch.randn(N, V, generator=g) * 2
+    loss_ref, dz_ref = topk_tail_kl(zs, ids, lp, tail, "reverse" if reverse else "forward")
+    loss = torch.empty(N, device=dev)
+    dz = torch.empty(N, V, dtype=torch.bfloat16, device=dev)
+    C().topk_tail_kl(zs.to(dev), ids.to(dev), lp.to(dev), tail.to(dev), reverse, 1.0, loss, dz)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(loss.cpu(), loss_ref, rtol=2e-3, atol=1e-4)
+    assert _rel(dz.cpu(), dz_ref) < 1e-2
+
+
+def test_adamw_kernel():
+    g = torch.Generator().manual_seed(3)
+    p = torch.randn(10000, generator=g)
+    grad = torch.randn(10000, generator=g)
+    m = torch.zeros(10000, dtype=torch.bfloat16)
+    v = torch.zeros(10000, dtype=torch.bfloat16)
+    pg, mg, vg = p.to(dev), m.to(dev), v.to(dev)
+    for step in (1, 2, 3):
+        C().adamw(pg, grad.to(dev), mg, vg, None, 1e-3, 0.9, 0.95, 1e-8, 0.01, step)
+        mm = 0.9 * m.float() + 0.1 * grad
+        vv = 0.95 * v.float() + 0.05 * grad * grad
+        m.copy_(mm)
+        v.copy_(vv)
+        p -= 1e-3 * (0.01 * p + (mm / (1 - 0.9**step)) / ((vv / (1 - 0.95**step)).sqrt() + 1e-8))
+    torch.testing.assert_close(pg.cpu(), p, rtol=1e-4, atol=1e-5)
+
+
+def test_tiny_qad_training_on_gpu():
+    from arc_forge_2026_b200.config import QADConfig, preset
+    from arc_forge_2026_b200.formats.topk_targets import synthetic_targets
+    from arc_forge_2026_b200.train.qad import build_optimizer, enforce_scale_invariants, train_step
+    from arc_forge_2026_b200.train.student import random_student
+    cfg = preset("tiny_gpu")
+    st = random_student(cfg, dev, seed=0)
+    qc = QADConfig(seq_len=256, topk=16, direction="reverse", lr_scale=1e-3, lr_router=1e-3, lr_dense=1e-3)
+    opt = build_optimizer(st, qc, sharded=True)
+    signs = enforce_scale_invariants(st, None)
+    gen = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (2, 256), generator=gen).to(dev)
+    t = synthetic_targets(ids.numel(), 16, cfg.vocab_size, gen, dev)
+    losses = [train_step(st, opt, ids, t, qc, signs)[0] for _ in range(5)]
+    torch.cuda.synchronize()
+    check_status()
+    assert losses[-1] < losses[0], losses
