@@ -93,9 +93,9 @@ __global__ void __launch_bounds__(DK) gdn_conv_prep_kernel(GdnArgs a, int parity
         const float b = __bfloat162float(row[h]);
         const float av = __bfloat162float(row[a.Hv + h]) + dt;
         const float sp = av > 20.f ? av : log1pf(__expf(av));
-        float* gb = a.pend_gb + (((size_t)cur * a.pend_slots + ps) * a.max_q + t) * (2 * a.Hv);
-        gb[h] = A * sp;                          // g (log decay)
-        gb[a.Hv + h] = 1.f / (1.f + __expf(-b));  // beta
+        float* gb = a.pend_gb + ((((size_t)cur * a.pend_slots + ps) * a.Hv + h) * a.max_q + t) * 2;
+        gb[0] = A * sp;                       // g (log decay)
+        gb[1] = 1.f / (1.f + __expf(-b));     // beta
       }
     }
   }
@@ -140,8 +140,9 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
     return x;
   };
   auto update = [&](size_t base) {
-    const float* gb = a.pend_gb + base * (2 * a.Hv);
-    const float decay = __expf(gb[h]), beta = gb[a.Hv + h];
+    const size_t pslot = base / a.max_q, tt = base % a.max_q;  // base = (par * pend_slots + ps) * max_q + t
+    const float* gb = a.pend_gb + ((pslot * a.Hv + h) * a.max_q + tt) * 2;
+    const float decay = __expf(gb[0]), beta = gb[1];
     const float vv = __bfloat162float(a.pend_v[base * (a.Hv * DV) + h * DV + v]);
     const float* kk = kq[0] + part * HK;
     float mem = 0.f;
@@ -188,13 +189,170 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
   }
 }
 
-int gdn_decode(const GdnArgs& a, int parity, cudaStream_t st) {
+// ------------------------------------------------------------------------------------------ persistent verify path
+// One CTA (512 threads, 4 per value column) per SM loops over (sequence, value head) items. While it runs the
+// recurrence of item i from registers, bulk copies (no multicast) stage item i+1 into the other half of a shared
+// memory double buffer: its 64 KB committed state, the k (and q) rows of the previous cycle's and this cycle's
+// tokens, their v rows, gates and the z rows of the output gate. So the token steps never wait on global memory,
+// and the state loads of the next item overlap the math of the current one.
+namespace gdnp {
+constexpr int DK = 128, DV = 128, QT = 4, HK = DK / QT, THREADS = QT * DV, MAXT = 8, MAXS = 1024;
+struct Smem {
+  float state[2][DK * DV];
+  __nv_bfloat16 kq[2][2 * MAXT][2][DK];  // token slots 0..7: previous cycle (k only), 8..15: this cycle (k, q)
+  __nv_bfloat16 v[2][2 * MAXT][DV];
+  __nv_bfloat16 z[2][MAXT][DV];
+  float gb[2][2][2 * MAXT];              // [buf][previous / this cycle][token * 2 + (g, beta)]
+  float red[THREADS / 32];
+  int slot[MAXS], ncommit[MAXS];
+  uint64_t full[2];
+};
+}  // namespace gdnp
+
+AFB_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel(GdnArgs a, int parity,
+                                                                                  uint32_t* status) {
+  using namespace gdnp;
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int tid = threadIdx.x, v = tid / QT, part = tid % QT;
+  const int T = a.q_per_seq;
+  const int nq = a.Hk * DK;
+  const int cur = parity, prev = parity ^ 1;
+  const int items = a.num_seqs * a.Hv;
+  for (int i = tid; i < a.num_seqs; i += THREADS) {
+    const int sl = a.seq_slot[i];
+    sm.slot[i] = sl;
+    sm.ncommit[i] = a.n_commit[sl];
+  }
+  if (tid == 0) {
+    mbar_init(&sm.full[0], 1);
+    mbar_init(&sm.full[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int item, int b) {  // thread 0 only
+    const int seq = item / a.Hv, h = item % a.Hv;
+    const int slot = sm.slot[seq], np = sm.ncommit[seq];
+    const int kh = h / (a.Hv / a.Hk);
+    const uint32_t bytes = DK * DV * 4 + np * (DK + DV) * 2 + T * (2 * DK + 2 * DV) * 2 + 2 * a.max_q * 8;
+    mbar_arrive_expect_tx(&sm.full[b], bytes);
+    bulk_copy(sm.state[b], a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV, DK * DV * 4, &sm.full[b]);
+    for (int t = 0; t < np; ++t) {
+      const size_t base = ((size_t)prev * a.pend_slots + slot) * a.max_q + t;
+      bulk_copy(sm.kq[b][t][0], a.pend_qk + base * (2 * nq) + nq + kh * DK, DK * 2, &sm.full[b]);
+      bulk_copy(sm.v[b][t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
+    }
+    for (int t = 0; t < T; ++t) {
+      const size_t base = ((size_t)cur * a.pend_slots + slot) * a.max_q + t;
+      bulk_copy(sm.kq[b][MAXT + t][0], a.pend_qk + base * (2 * nq) + nq + kh * DK, DK * 2, &sm.full[b]);
+      bulk_copy(sm.kq[b][MAXT + t][1], a.pend_qk + base * (2 * nq) + kh * DK, DK * 2, &sm.full[b]);
+      bulk_copy(sm.v[b][MAXT + t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
+      bulk_copy(sm.z[b][t], a.mixed + ((size_t)seq * T + t) * a.mixed_ld + a.z_off + h * DV, DV * 2, &sm.full[b]);
+    }
+    bulk_copy(sm.gb[b][0], a.pend_gb + (((size_t)prev * a.pend_slots + slot) * a.Hv + h) * a.max_q * 2,
+              a.max_q * 8, &sm.full[b]);
+    bulk_copy(sm.gb[b][1], a.pend_gb + (((size_t)cur * a.pend_slots + slot) * a.Hv + h) * a.max_q * 2,
+              a.max_q * 8, &sm.full[b]);
+  };
+
+  int issued = 0, done = 0;
+  if (tid == 0 && blockIdx.x < items) {
+    issue(blockIdx.x, 0);
+    issued = 1;
+  }
+  bool ok = true;
+  int i = 0;
+  for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++i) {
+    const int b = i & 1;
+    const int next = item + gridDim.x;
+    if (tid == 0 && next < items) {
+      issue(next, b ^ 1);
+      ++issued;
+    }
+    if (!mbar_wait(&sm.full[b], (i >> 1) & 1, status)) {
+      ok = false;
+      break;
+    }
+    ++done;
+    const int seq = item / a.Hv, h = item % a.Hv;
+    const int slot = sm.slot[seq], np = sm.ncommit[seq];
+    float S[HK];
+#pragma unroll
+    for (int k = 0; k < HK; ++k) S[k] = sm.state[b][(part * HK + k) * DV + v];
+    auto step = [&](int ts, float decay, float beta) {
+      const __nv_bfloat16* kk = sm.kq[b][ts][0] + part * HK;
+      const float vv = __bfloat162float(sm.v[b][ts][v]);
+      float mem = 0.f;
+#pragma unroll
+      for (int k = 0; k < HK; ++k) {
+        S[k] *= decay;
+        mem = fmaf(__bfloat162float(kk[k]), S[k], mem);
+      }
+#pragma unroll
+      for (int o = 1; o < QT; o <<= 1) mem += __shfl_xor_sync(0xffffffffu, mem, o);
+      const float delta = beta * (vv - mem);
+#pragma unroll
+      for (int k = 0; k < HK; ++k) S[k] = fmaf(__bfloat162float(kk[k]), delta, S[k]);
+    };
+    for (int t = 0; t < np; ++t) step(t, __expf(sm.gb[b][0][2 * t]), sm.gb[b][0][2 * t + 1]);
+    float* sp = a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV + (size_t)(part * HK) * DV + v;
+#pragma unroll
+    for (int k = 0; k < HK; ++k) sp[(size_t)k * DV] = S[k];  // the committed state
+    for (int t = 0; t < T; ++t) {
+      step(MAXT + t, __expf(sm.gb[b][1][2 * t]), sm.gb[b][1][2 * t + 1]);
+      const __nv_bfloat16* qq = sm.kq[b][MAXT + t][1] + part * HK;
+      float o = 0.f;
+#pragma unroll
+      for (int k = 0; k < HK; ++k) o = fmaf(__bfloat162float(qq[k]), S[k], o);
+#pragma unroll
+      for (int x = 1; x < QT; x <<= 1) o += __shfl_xor_sync(0xffffffffu, o, x);
+      const float ssq = warp_sum(part ? 0.f : o * o);
+      if ((tid & 31) == 0) sm.red[tid >> 5] = ssq;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < THREADS / 32; ++w) tot += sm.red[w];
+      if (!part) {
+        const size_t tok = (size_t)seq * T + t;
+        const float z = __bfloat162float(sm.z[b][t][v]);
+        const float y = o * rsqrtf(tot / DV + a.eps) * __bfloat162float(a.norm_w[v]) * silu(z);
+        a.out[tok * (a.Hv * DV) + h * DV + v] = __float2bfloat16(y);
+      }
+      __syncthreads();  // red is rewritten by the next token
+    }
+    __syncthreads();  // buffer b is refilled two items later
+  }
+  // drain copies still in flight (only after a failed wait), bounded
+  if (tid == 0)
+    for (int j = done; j < issued; ++j) mbar_wait(&sm.full[j & 1], (j >> 1) & 1, status);
+}
+
+int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cudaStream_t st) {
   if (a.num_seqs == 0) return 0;
   if (a.q_per_seq > a.max_q) return 3;
   const int C = a.conv_dim;
   if (a.Dk == 128 && a.Dv == 128) {
     if (C % 128) return 3;
     gdn_conv_prep_kernel<128><<<dim3(a.num_seqs, C / 128), 128, 0, st>>>(a, parity);
+    if (!a.commit_current && a.max_q <= gdnp::MAXT && a.max_q % 2 == 0 && a.num_seqs <= gdnp::MAXS && num_sms > 0) {
+      const size_t smem = sizeof(gdnp::Smem) + 128;
+      static bool attr = false;
+      if (!attr) {
+        cudaFuncSetAttribute(gdn_verify_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+      }
+      const int items = a.num_seqs * a.Hv;
+      gdn_verify_persistent_kernel<<<items < num_sms ? items : num_sms, gdnp::THREADS, smem, st>>>(a, parity, status);
+      return (int)cudaGetLastError();
+    }
     gdn_recurrent_kernel<128, 128, 4><<<dim3(a.num_seqs, a.Hv), 512, 0, st>>>(a, parity);
   } else if (a.Dk == 64 && a.Dv == 64) {
     if (C % 64) return 3;

@@ -57,7 +57,7 @@ struct GdnArgs {
   __nv_bfloat16* pend_in = nullptr;      // [2, pend_slots, max_q, C]
   __nv_bfloat16* pend_qk = nullptr;      // [2, pend_slots, max_q, 2*Hk*Dk]
   __nv_bfloat16* pend_v = nullptr;       // [2, pend_slots, max_q, Hv*Dv]
-  float* pend_gb = nullptr;              // [2, pend_slots, max_q, 2*Hv] (g, beta)
+  float* pend_gb = nullptr;              // [2, pend_slots, Hv, max_q, 2] (g, beta), head-major
   const int* n_commit = nullptr;         // [slots] accepted tokens of the previous cycle
   const int* seq_slot = nullptr;         // [num_seqs]
   const float* A_log = nullptr;
@@ -69,7 +69,7 @@ struct GdnArgs {
   int commit_current = 0;
   float eps = 1e-6f;
 };
-int gdn_decode(const GdnArgs& a, int parity, cudaStream_t st);
+int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cudaStream_t st);
 
 // sampling.cu
 int select_tokens(const void* logits, int ld, int rows, int V, int* out, float temperature, uint64_t seed,

@@ -17,7 +17,8 @@
 //
 // One persistent CTA per SM, warp-specialised; the dequant and epilogue roles are latency-bound chains, so they get
 // 6 and 8 warps. A ring of raw stages feeds a ring of dequantised tiles and the MMA runs up to 8 (w13) / 16 (w2)
-// groups ahead of the epilogue in TMEM:
+// groups ahead of the epilogue in TMEM. The dequant warps also copy each group's scales into a per-accumulator-buffer
+// slot, so a raw stage is released once dequant and MMA are done with it and never waits on the epilogue:
 //   warp 0      loader: bulk copies of the code/scale tiles and of the activation scales, TMA of the activation
 //               rows (no multicast)
 //   warps 1-6   dequant: codes -> e4m3 (c-4) into the 128-byte-swizzled A tile, in tasks of 32 codes spread
@@ -45,8 +46,8 @@ constexpr uint32_t E4M3_LO = 0xB8C0C4C8u; // table bytes 0..3: e4m3(-4), e4m3(-3
 constexpr uint32_t E4M3_HI = 0x44403800u; // table bytes 4..7: e4m3(0), e4m3(1), e4m3(2), e4m3(3)
 constexpr int MAX_E = 1024;               // experts whose segment offsets are staged in shared memory
 
-// Two rings: a deep one of raw stages (codes, weight scales, activation tile and scales, all moved by
-// bulk/TMA copies) and a 2-deep one of dequantised e4m3 A tiles (dequant -> MMA).
+// Rings: raw stages (codes, weight scales, activation tile and scales, all moved by bulk/TMA copies), dequantised
+// e4m3 A tiles (dequant -> MMA), and per TMEM accumulator buffer a copy of the group's scales (dequant -> epilogue).
 template <bool PAIR>
 struct Layout {
   static constexpr int T = PAIR ? 2 : 1;  // weight tiles per k-step
@@ -58,16 +59,18 @@ struct Layout {
   static constexpr uint32_t RAW = (RAW_BYTES + 1023) & ~1023u;
   // w13 (PAIR): one CTA per SM; w2: two CTAs per SM (half the shared memory and TMEM each)
   static constexpr int CTAS_PER_SM = 1;
-  static constexpr int RS = PAIR ? 4 : 6;     // raw stages
-  static constexpr int AS = PAIR ? 4 : 6;     // dequantised stages
+  static constexpr int RS = PAIR ? 6 : 8;     // raw stages
+  static constexpr int AS = PAIR ? 3 : 4;     // dequantised stages
   static constexpr int NBUF = PAIR ? 8 : 16;  // TMEM accumulator buffers (T * 32 columns each)
+  static constexpr uint32_t ESC = 640;        // per-buffer copy of the group's scales: T*128 bf16 s_w + 32 fp32 s_x
   static constexpr uint32_t A_STAGE = T * A_TILE;
   static constexpr uint32_t A_OFF = RS * RAW;
-  static constexpr uint32_t OFFS_OFF = A_OFF + AS * A_STAGE;        // int offsets[MAX_E + 1]
+  static constexpr uint32_t ESC_OFF = A_OFF + AS * A_STAGE;         // scale ring [NBUF][ESC]
+  static constexpr uint32_t OFFS_OFF = ESC_OFF + NBUF * ESC;         // int offsets[MAX_E + 1]
   static constexpr uint32_t RED_OFF = OFFS_OFF + (MAX_E + 1) * 4;   // float [2 halves][4 quads][16]
   static constexpr uint32_t BAR_OFF = (RED_OFF + 2 * 4 * 16 * 4 + 7) & ~7u;
-  // full[RS], empty[RS], afull[AS], aempty[AS], dfull[NBUF], dempty[NBUF], tmem slot
-  static constexpr uint32_t TOTAL = BAR_OFF + (2 * RS + 2 * AS + 2 * NBUF) * 8 + 16 + 1024;
+  // full[RS], empty[RS], afull[AS], aempty[AS], dfull[NBUF], dempty[NBUF], sready[NBUF], tmem slot
+  static constexpr uint32_t TOTAL = BAR_OFF + (2 * RS + 2 * AS + 3 * NBUF) * 8 + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512 / CTAS_PER_SM;
 };
 }  // namespace moe
@@ -125,7 +128,8 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
   uint64_t* aempty = afull + AS;
   uint64_t* dfull = aempty + AS;
   uint64_t* dempty = dfull + NBUF;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + NBUF);
+  uint64_t* sready = dempty + NBUF;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sready + NBUF);
   int* off = reinterpret_cast<int*>(smem + L::OFFS_OFF);
   float* red = reinterpret_cast<float*>(smem + L::RED_OFF);  // [2 halves][4 quads][16 tokens] amax exchange
 
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < RS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], moe::N_DQ + 1 + moe::N_EP);  // dequant warps + MMA commit + epilogue warps
+      mbar_init(&empty[s], moe::N_DQ + 1);  // dequant warps (codes and scales read) + MMA commit (X read)
     }
     for (int s = 0; s < AS; ++s) {
       mbar_init(&afull[s], moe::N_DQ);
@@ -148,6 +152,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&dfull[b], 1);
       mbar_init(&dempty[b], moe::N_EP);
+      mbar_init(&sready[b], moe::N_DQ);
     }
     fence_mbar_init();
   }
@@ -206,14 +211,24 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
         for (int g = 0; g < KG; ++g, ++kstep) {
           const int s = kstep % RS;
           const int as = kstep % AS;
+          const int b = kstep % NBUF;
           bool ok = AFB_TIMED_WAIT(mbar_wait(&full[s], (kstep / RS) & 1, status));
           if (ok && kstep >= (uint32_t)AS) ok = AFB_TIMED_WAIT(mbar_wait(&aempty[as], ((kstep / AS) & 1) ^ 1, status));
+          if (ok && kstep >= (uint32_t)NBUF)
+            ok = AFB_TIMED_WAIT(mbar_wait(&dempty[b], ((kstep / NBUF) & 1) ^ 1, status));
           if (!ok) {
             bail = true;
             break;
           }
           const uint8_t* st = smem + s * L::RAW;
           uint8_t* at = smem + L::A_OFF + as * L::A_STAGE;
+          {  // the group's scales move to the epilogue's ring slot b, so the raw stage can be refilled early
+            constexpr int SW_WORDS = L::T * 64, WORDS = SW_WORDS + moe::NTOK;
+            uint32_t* dst = reinterpret_cast<uint32_t*>(smem + L::ESC_OFF + b * L::ESC);
+            if (dq < WORDS)
+              dst[dq] = dq < SW_WORDS ? reinterpret_cast<const uint32_t*>(st + L::SW_OFF)[dq]
+                                      : reinterpret_cast<const uint32_t*>(st + L::SX_OFF)[dq - SW_WORDS];
+          }
 #pragma unroll 2
           for (int task = dq; task < TASKS; task += NT) {
             const int t = task >> 9, r = (task >> 2) & 127, sq = task & 3;
@@ -224,6 +239,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           __syncwarp();
           if (lane == 0) {
             mbar_arrive(&afull[as]);
+            mbar_arrive(&sready[b]);
             mbar_arrive(&empty[s]);
           }
         }
@@ -259,7 +275,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           __syncwarp();
         }
       } else {
-        // ---------------------------------------------------------------- epilogue (warps 10..17)
+        // ---------------------------------------------------------------- epilogue (warps 8..15)
         // each TMEM lane quadrant is read by two warps: half 0 takes token columns 0..15, half 1 columns 16..31
         const int quad = warp & 3;
         const int half = (warp - moe::W_EP0) >> 2;
@@ -271,33 +287,32 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
 #pragma unroll
         for (int i = 0; i < (PAIR ? NH : 1); ++i) acc1[i] = 0.f;
         for (int g = 0; g < KG; ++g, ++kstep) {
-          const int s = kstep % RS;
           const int b = kstep % NBUF;
-          if (!AFB_TIMED_WAIT(mbar_wait(&dfull[b], (kstep / NBUF) & 1, status))) {
+          const uint32_t ph = (kstep / NBUF) & 1;
+          if (!AFB_TIMED_WAIT(mbar_wait(&dfull[b], ph, status) && mbar_wait(&sready[b], ph, status))) {
             bail = true;
             break;
           }
           tc_fence_after();
-          const uint8_t* st = smem + s * L::RAW;
-          const float* sx = reinterpret_cast<const float*>(st + L::SX_OFF) + half * NH;
-          const float sw0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L::SW_OFF)[r]);
-          const float sw1 = PAIR ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L::SW_OFF + 256)[r]) : 0.f;
+          const uint8_t* esc = smem + L::ESC_OFF + b * L::ESC;  // [T][128] bf16 s_w, then [32] fp32 s_x
+          const float* sx = reinterpret_cast<const float*>(esc + L::T * 256) + half * NH;
+          const float sw0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(esc)[r]);
+          const float sw1 = PAIR ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(esc + 256)[r]) : 0.f;
           const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * L::T * moe::NTOK + half * NH);
-          float d0[NH], d1[PAIR ? NH : 1];
-          tmem_ld16(ta, d0);
-          if (PAIR) tmem_ld16(ta + moe::NTOK, d1);
+          float d[NH];  // one 16-column load at a time keeps the role inside 128 registers
+          tmem_ld16(ta, d);
           tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < NH; ++i) acc0[i] = fmaf(sw0 * sx[i], d[i], acc0[i]);
+          if (PAIR) {
+            tmem_ld16(ta + moe::NTOK, d);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < NH; ++i) acc1[i] = fmaf(sw1 * sx[i], d[i], acc1[i]);
+          }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&dempty[b]);
-#pragma unroll
-          for (int i = 0; i < NH; ++i) {
-            const float x = sx[i];
-            acc0[i] = fmaf(sw0 * x, d0[i], acc0[i]);
-            if (PAIR) acc1[i] = fmaf(sw1 * x, d1[i], acc1[i]);
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
+          if (lane == 0) mbar_arrive(&dempty[b]);  // TMEM buffer b and scale slot b are free again
         }
         if (bail) break;
         const int t0 = half * NH;  // first token column of this warp

@@ -224,7 +224,7 @@ void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const
   TORCH_CHECK(a.conv_dim == 2 * Hk * Dk + Hv * Dv, "conv_dim");
   TORCH_CHECK(pend_in.size(0) == 2 && pend_in.size(3) == a.conv_dim, "pend_in shape");
   TORCH_CHECK(!commit_current || a.pend_slots >= a.num_seqs, "prefill scratch needs one pending slot per sequence");
-  check_rc(afb::gdn_decode(a, (int)parity, stream()), "gdn_decode");
+  check_rc(afb::gdn_decode(a, (int)parity, num_sms(), status_ptr(mixed.get_device()), stream()), "gdn_decode");
 }
 
 void select_tokens_op(const at::Tensor& logits, int64_t V, at::Tensor& out, double temperature, int64_t seed,

@@ -45,13 +45,14 @@ class GdnState:
     def __init__(self, shape: GdnShape, slots: int, max_q: int, device, state_dtype=torch.float32):
         s = shape
         dev = torch.device(device)
+        max_q += max_q % 2  # even: each head's (g, beta) block is then 16-byte aligned for bulk copies
         self.shape = s
         self.conv = torch.zeros(slots, 3, s.conv_dim, dtype=torch.bfloat16, device=dev)
         self.ssm = torch.zeros(slots, s.Hv, s.Dk, s.Dv, dtype=state_dtype, device=dev)
         self.pend_in = torch.zeros(2, slots, max_q, s.conv_dim, dtype=torch.bfloat16, device=dev)
         self.pend_qk = torch.zeros(2, slots, max_q, 2 * s.Hk * s.Dk, dtype=torch.bfloat16, device=dev)
         self.pend_v = torch.zeros(2, slots, max_q, s.Hv * s.Dv, dtype=torch.bfloat16, device=dev)
-        self.pend_gb = torch.zeros(2, slots, max_q, 2 * s.Hv, dtype=torch.float32, device=dev)
+        self.pend_gb = torch.zeros(2, slots, s.Hv, max_q, 2, dtype=torch.float32, device=dev)
 
     def nbytes(self):
         return sum(t.numel() * t.element_size() for t in (self.conv, self.ssm, self.pend_in, self.pend_qk,
@@ -67,7 +68,7 @@ class GdnScratch:
         self.pend_in = torch.empty(2, seqs, max_q, s.conv_dim, dtype=torch.bfloat16, device=device)
         self.pend_qk = torch.empty(2, seqs, max_q, 2 * s.Hk * s.Dk, dtype=torch.bfloat16, device=device)
         self.pend_v = torch.empty(2, seqs, max_q, s.Hv * s.Dv, dtype=torch.bfloat16, device=device)
-        self.pend_gb = torch.empty(2, seqs, max_q, 2 * s.Hv, dtype=torch.float32, device=device)
+        self.pend_gb = torch.empty(2, seqs, s.Hv, max_q, 2, dtype=torch.float32, device=device)
 
 
 def gdn_decode(mixed, shape: GdnShape, state: GdnState, conv_w, A_log, dt_bias, norm_w, n_commit, seq_slot, out,
