@@ -71,22 +71,37 @@ def mask_zero_scale_grads(student: QADStudent, signs):
             p.grad.masked_fill_(s == 0, 0.0)
 
 
-def train_step(student: QADStudent, opt, ids: torch.Tensor, targets: dict, qc: QADConfig, signs):
-    """One optimizer step over ``ids`` [B, T] (every position supervised). Returns (mean loss, grad norm)."""
+def train_step(student: QADStudent, opt, ids: torch.Tensor, targets: dict, qc: QADConfig, signs,
+               accumulate: bool = False, sync: bool = True, micro_batches: int = 1, first: bool | None = None):
+    """One micro-batch over ``ids`` [B, T] (every position supervised) and, unless ``accumulate``, the optimizer step.
+
+    Gradient accumulation: call with ``accumulate=True`` for all but the last of ``micro_batches`` micro-batches
+    (gradients are zeroed at the first one, ``first`` defaults to "the optimizer has no pending gradients"); the
+    loss is divided by ``micro_batches`` so the step sees the mean over the whole global batch.
+    Returns (mean loss, grad norm) as floats when ``sync``, else the loss as a device tensor (no host sync)."""
     sharded = isinstance(opt, ShardedAdamW)
-    opt.zero_grad(set_to_none=not sharded)
+    if first is None:
+        first = not getattr(opt, "_afb_pending", False)
+    if first:
+        opt.zero_grad(set_to_none=not sharded)
+    opt._afb_pending = True
     n = ids.numel()
     h = student.hidden(ids).reshape(n, -1)
     loss = fused_topk_tail_kl(h, student.lm_head, student.lm_head_t, targets["ids"], targets["lp"], targets["tail"],
                               qc.direction) / n
-    loss.backward()
-    mask_zero_scale_grads(student, signs)
-    if sharded:
-        norm = opt.step(qc.grad_clip)
-    else:
-        norm = clip_grad_norm_([p for g in opt.param_groups for p in g["params"]], qc.grad_clip)
-        opt.step()
-    enforce_scale_invariants(student, signs)
+    (loss / micro_batches).backward()
+    norm = None
+    if not accumulate:
+        mask_zero_scale_grads(student, signs)
+        if sharded:
+            norm = opt.step(qc.grad_clip)
+        else:
+            norm = clip_grad_norm_([p for g in opt.param_groups for p in g["params"]], qc.grad_clip)
+            opt.step()
+        enforce_scale_invariants(student, signs)
+        opt._afb_pending = False
+    if not sync:
+        return loss.detach()
     return float(loss.detach()), norm
 
 

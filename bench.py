@@ -33,10 +33,11 @@ METRIC = "decode tok/s @128 sessions (8xB200, spec K=4); p50 TPOT; QAD train tok
 
 def _reference_arm(args):
     ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    why = ("the reference's serving engine is a private sglang fork (only its patch set is in the tree) and its "
-           "INT3 MoE kernels come from a closed binary wheel (humming-kernels); neither can be installed offline")
-    if not os.path.isdir(ref) or not any(n.endswith(".dist-info") for n in os.listdir(ref)):
-        why = "baseline/_ref is not installed: " + why
+    why = ("pip reports the reference 'is not installable' (no setup.py or pyproject.toml anywhere in the tree); its "
+           "serving engine is a private sglang fork (only its patch set ships) and its INT3 MoE kernels come from a "
+           "closed binary wheel (humming-kernels), neither of which is in the offline wheelhouse")
+    if os.path.isdir(ref) and any(n.endswith(".dist-info") for n in os.listdir(ref)):
+        why = "baseline/_ref holds a package, but " + why
     line = {"impl": "reference", "unavailable": why, "n_gpus": args.gpus}
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(line))
@@ -106,7 +107,8 @@ def count_launches(fn):
         torch.cuda.synchronize()
     ours = ("gemm_bf16", "splitk_reduce", "moe_int3", "rmsnorm", "qk_norm_rope", "router_topk", "expert_sort",
             "quant_rows", "moe_combine", "swiglu", "embedding", "paged_attn", "attn_merge", "gdn_", "select_tokens",
-            "spec_accept", "build_window", "gather_rows")
+            "spec_accept", "build_window", "gather_rows", "expert_sort", "int3_dequant", "int3_scale_grad",
+            "fp8_block_fakequant", "topk_tail_kl", "adamw_kernel", "train_kernel")
     n_ours = n_all = 0
     for e in prof.events():
         if e.device_type.name == "CUDA" and not e.name.startswith("Memcpy") and not e.name.startswith("Memset"):
@@ -128,10 +130,17 @@ def main():
     ap.add_argument("--max-ctx", type=int, default=24576)
     ap.add_argument("--out-tokens", type=int, default=2048)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--mode", default="serve", choices=["serve", "qad"],
+                    help="serve: spec-decode serving (default); qad: QAD training step")
+    ap.add_argument("--seq-len", dest="seq_len", type=int, default=16384, help="qad: tokens per sequence")
+    ap.add_argument("--global-batch", dest="global_batch", type=int, default=32, help="qad: sequences per step")
+    ap.add_argument("--topk", type=int, default=64, help="qad: teacher top-k")
     args = ap.parse_args()
     if args.impl == "reference":
         _reference_arm(args)
         return
+    if args.mode == "qad":
+        return qad_main(args)
     if args.warmup < 3:
         args.warmup = 3
 
@@ -280,6 +289,120 @@ def main():
     if rank == 0:
         print(json.dumps(out))
     eng.graphs.clear()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+QAD_METRIC = "QAD train tok/s"
+QAD_BASELINE_TOKS = 19900.0  # reference, 4 x B200, fused gradient kernels
+
+
+def qad_main(args):
+    """QAD training throughput on the config-4 shape: the 48-layer student (320 INT3 experts with STE, FP8 QAT
+    dense), forward KL on top-``topk`` teacher targets, ``global_batch`` sequences of ``seq_len`` tokens per
+    optimizer step (one sequence per micro-batch, gradients accumulated), sharded bf16 AdamW over the ranks."""
+    if args.warmup < 3:
+        args.warmup = 3
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    from arc_forge_2026_b200.config import QADConfig, preset
+    from arc_forge_2026_b200.formats.topk_targets import synthetic_targets
+    from arc_forge_2026_b200.train.qad import build_optimizer, enforce_scale_invariants, train_step
+    from arc_forge_2026_b200.train.student import random_student
+
+    if args.global_batch % world:
+        raise SystemExit(f"--global-batch {args.global_batch} is not a multiple of {world} ranks")
+    micro = args.global_batch // world
+    cfg = preset("qwen3next_80b", num_layers=args.layers)
+    qc = QADConfig(seq_len=args.seq_len, topk=args.topk, direction="forward")
+    student = random_student(cfg, dev, seed=args.seed)
+    opt = build_optimizer(student, qc, sharded=True, group=dist.group.WORLD if world > 1 else None)
+    signs = enforce_scale_invariants(student, None)
+    g = torch.Generator().manual_seed(args.seed * 7919 + rank)
+    T = args.seq_len
+    # host-side inputs for every micro-batch (pinned), copied to the device inside the e2e timed region
+    host = []
+    for _ in range(micro):
+        ids = torch.randint(0, cfg.vocab_size, (1, T), generator=g, dtype=torch.int64)
+        t = synthetic_targets(T, args.topk, cfg.vocab_size, g)
+        host.append({"ids": ids.pin_memory(), "t_ids": t["ids"].int().pin_memory(),
+                     "lp": t["lp"].float().pin_memory(), "tail": t["tail"].float().pin_memory()})
+    dev_in = [{k: v.to(dev) for k, v in h.items()} for h in host]
+    h2d = sum(v.numel() * v.element_size() for h in host for v in h.values())
+
+    def one_step(inputs):
+        losses = []
+        for i, x in enumerate(inputs):
+            tg = {"ids": x["t_ids"], "lp": x["lp"], "tail": x["tail"]}
+            losses.append(train_step(student, opt, x["ids"], tg, qc, signs, accumulate=i < len(inputs) - 1,
+                                     sync=False, micro_batches=len(inputs), first=i == 0))
+        return torch.stack(losses).mean()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        one_step(dev_in)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record()
+        for _ in range(args.steps):
+            loss = one_step(dev_in)
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+
+    # end to end: pinned host -> device copies of every micro-batch and the loss read back, each step
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        inputs = [{k: v.to(dev, non_blocking=True) for k, v in h.items()} for h in host]
+        last_loss = float(one_step(inputs))
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms, e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e_ms = float(t[0]), float(t[1])
+    n_ours, n_all = count_launches(lambda: one_step(dev_in))
+    tokens = args.global_batch * T * args.steps
+    value = tokens / (ms / 1000.0)
+    out = {
+        "metric": QAD_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": round(value / QAD_BASELINE_TOKS, 3), "dtype": "bf16",
+        "data": "synthetic (random-init student; uniform random tokens; random valid top-k teacher targets)",
+        "config": {"model": "qwen3next_80b-shaped student, 48L, 320 INT3 experts (STE scales), FP8 QAT dense",
+                   "global_batch": args.global_batch, "seq_len": T, "parallelism": f"dp{world}+sharded-adamw",
+                   "loss": f"forward KL, teacher top-{args.topk} + tail", "layers": args.layers,
+                   "optimizer": "bf16-state AdamW", "l2": "inputs larger than L2 (weights and activations)"},
+        "loss": round(last_loss, 5),
+        "e2e": {"value": round(tokens / (e_ms / 1000.0), 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": n_ours * args.steps,
+        "gpu_launches_per_step": {"ours": n_ours, "all": n_all},
+        "peak_gib": round(torch.cuda.max_memory_allocated() / 2**30, 2),
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(out))
     if world > 1:
         dist.destroy_process_group()
 
