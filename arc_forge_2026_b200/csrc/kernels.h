@@ -71,6 +71,21 @@ struct GdnArgs {
 };
 int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cudaStream_t st);
 
+// gdn_chunk.cu: inter-chunk state scan of the chunked gated delta rule (training), fp32, contiguous
+struct GdnScanArgs {
+  const float* m1 = nullptr;      // [BH, n, C, Dk]
+  const float* m2 = nullptr;      // [BH, n, C, Dk]
+  const float* y = nullptr;       // [BH, n, C, Dv]
+  const float* qm = nullptr;      // [BH, n, Dk, Dv] (reverse only, optional)
+  const float* last = nullptr;    // [BH, n] log decay over the whole chunk
+  const float* init = nullptr;    // [BH, Dk, Dv] optional initial state
+  float* states = nullptr;        // [BH, n, Dk, Dv] state before each step
+  float* x = nullptr;             // [BH, n, C, Dv]
+  float* final_state = nullptr;   // [BH, Dk, Dv] optional
+  int BH = 0, n_chunks = 0, C = 64, Dk = 128, Dv = 128;
+};
+int gdn_chunk_scan(const GdnScanArgs& a, bool reverse, cudaStream_t st);
+
 // sampling.cu
 int select_tokens(const void* logits, int ld, int rows, int V, int* out, float temperature, uint64_t seed,
                   const int* step, uint32_t* status, cudaStream_t st);

@@ -227,6 +227,47 @@ void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const
   check_rc(afb::gdn_decode(a, (int)parity, num_sms(), status_ptr(mixed.get_device()), stream()), "gdn_decode");
 }
 
+void gdn_chunk_scan_op(const at::Tensor& m1, const at::Tensor& m2, const at::Tensor& y,
+                       const c10::optional<at::Tensor>& qm, const at::Tensor& last, const c10::optional<at::Tensor>& init,
+                       at::Tensor& states, at::Tensor& x, c10::optional<at::Tensor> final_state, bool reverse) {
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&m1, &m2, &y, &last, &states, &x}) {
+    AFB_CHECK_CUDA(*t);
+    AFB_CHECK_DT(*t, at::kFloat);
+    AFB_CHECK_CONTIG(*t);
+  }
+  TORCH_CHECK(m1.dim() == 4 && m2.sizes() == m1.sizes() && y.dim() == 4, "m1/m2 [BH, n, C, Dk], y [BH, n, C, Dv]");
+  afb::GdnScanArgs a;
+  a.BH = m1.size(0);
+  a.n_chunks = m1.size(1);
+  a.C = m1.size(2);
+  a.Dk = m1.size(3);
+  a.Dv = y.size(3);
+  TORCH_CHECK(y.size(0) == a.BH && y.size(1) == a.n_chunks && y.size(2) == a.C, "y shape");
+  TORCH_CHECK(last.numel() == (int64_t)a.BH * a.n_chunks, "last shape");
+  TORCH_CHECK(states.numel() == (int64_t)a.BH * a.n_chunks * a.Dk * a.Dv && x.sizes() == y.sizes(), "outputs");
+  for (const auto* o : std::initializer_list<const c10::optional<at::Tensor>*>{&qm, &init})
+    if (o->has_value()) {
+      AFB_CHECK_DT(o->value(), at::kFloat);
+      AFB_CHECK_CONTIG(o->value());
+    }
+  if (qm) TORCH_CHECK(qm->numel() == states.numel(), "qm shape");
+  if (init) TORCH_CHECK(init->numel() == (int64_t)a.BH * a.Dk * a.Dv, "init shape");
+  if (final_state) {
+    AFB_CHECK_CONTIG(final_state.value());
+    TORCH_CHECK(final_state->numel() == (int64_t)a.BH * a.Dk * a.Dv, "final shape");
+  }
+  a.m1 = ptr<float>(m1);
+  a.m2 = ptr<float>(m2);
+  a.y = ptr<float>(y);
+  a.qm = optr<float>(qm);
+  a.last = ptr<float>(last);
+  a.init = optr<float>(init);
+  a.states = ptr<float>(states);
+  a.x = ptr<float>(x);
+  a.final_state = optr<float>(final_state);
+  check_rc(afb::gdn_chunk_scan(a, reverse, stream()), "gdn_chunk_scan");
+}
+
 void select_tokens_op(const at::Tensor& logits, int64_t V, at::Tensor& out, double temperature, int64_t seed,
                       c10::optional<at::Tensor> step) {
   AFB_CHECK_DT(logits, at::kBFloat16);
@@ -372,6 +413,7 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("build_window", &build_window_op);
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
+  m.def("gdn_chunk_scan", &gdn_chunk_scan_op);
   m.def("paged_attention", &paged_attention_op);
   m.def("embedding", &embedding_op);
 }

@@ -16,49 +16,49 @@ namespace afb {
 
 // -------------------------------------------------------------------------------------------- INT3 STE forward
 // codes: tile layout [E, R/128, K/128, 128, 12]; scales fp32 [E, R, K/128]; out bf16 [E, R, K]
-__global__ void int3_dequant_kernel(const uint32_t* __restrict__ codes, const float* __restrict__ scales, int R, int K,
-                                    __nv_bfloat16* __restrict__ out) {
-  // one warp per (e, row, group): lane handles 4 codes
-  const size_t gw = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int KG = K / 128;
-  const size_t total = (size_t)gridDim.y * R * KG;
-  const size_t idx = gw + (size_t)blockIdx.y * R * KG;
-  if (gw >= (size_t)R * KG) return;
-  (void)total;
-  const int e = blockIdx.y;
-  const int row = (int)(gw / KG), g = (int)(gw % KG);
-  const uint32_t* w = codes + ((((size_t)e * (R / 128) + row / 128) * KG + g) * 128 + (row & 127)) * 12;
-  // lane owns codes 4*lane .. 4*lane+3 of the 128-code row: sub-group q = lane / 8, position 4*(lane % 8)
-  const int q = lane >> 3, p0 = (lane & 7) * 4;
-  const uint32_t L0 = w[3 * q], L1 = w[3 * q + 1], H = w[3 * q + 2];
-  const float s = __bfloat162float(__float2bfloat16(scales[((size_t)e * R + row) * KG + g]));
-  float v[4];
-#pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const int c = p0 + t;  // code index within the 32-code sub-group
-    int code;
-    if (c < 8)
-      code = (int)((L0 >> (4 * c)) & 3) | (int)(((H >> (4 * c + 2)) & 1) << 2);
-    else if (c < 16)
-      code = (int)((L0 >> (4 * (c - 8) + 2)) & 3) | (int)(((H >> (4 * (c - 8) + 3)) & 1) << 2);
-    else if (c < 24)
-      code = (int)((L1 >> (4 * (c - 16))) & 3) | (int)(((H >> (4 * (c - 16))) & 1) << 2);
-    else
-      code = (int)((L1 >> (4 * (c - 24) + 2)) & 3) | (int)(((H >> (4 * (c - 24) + 1)) & 1) << 2);
-    v[t] = __bfloat162float(__float2bfloat16((float)(code - 4) * s));
+// One thread per 32 codes (3 words -> 64 bytes of bf16, four 16-byte stores); consecutive threads walk along K so
+// a warp writes 2 KB of one row contiguously.
+AFB_DEV int code_at(uint32_t L0, uint32_t L1, uint32_t H, int n) {
+  const int m = n & 7;
+  switch (n >> 3) {
+    case 0: return (int)((L0 >> (4 * m)) & 3) | (int)(((H >> (4 * m + 2)) & 1) << 2);
+    case 1: return (int)((L0 >> (4 * m + 2)) & 3) | (int)(((H >> (4 * m + 3)) & 1) << 2);
+    case 2: return (int)((L1 >> (4 * m)) & 3) | (int)(((H >> (4 * m)) & 1) << 2);
+    default: return (int)((L1 >> (4 * m + 2)) & 3) | (int)(((H >> (4 * m + 1)) & 1) << 2);
   }
-  __nv_bfloat16* o = out + ((size_t)e * R + row) * K + g * 128 + q * 32 + p0;
-  *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
-  (void)idx;
+}
+
+__global__ void int3_dequant_kernel(const uint32_t* __restrict__ codes, const float* __restrict__ scales, int E, int R,
+                                    int K, __nv_bfloat16* __restrict__ out) {
+  const int KG = K / 128;
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid >= (size_t)E * R * KG * 4) return;
+  const int q = (int)(tid & 3);
+  const size_t rest = tid >> 2;
+  const int g = (int)(rest % KG);
+  const size_t er = rest / KG;  // e * R + row
+  const int e = (int)(er / R), row = (int)(er % R);
+  const uint32_t* w = codes + ((((size_t)e * (R / 128) + row / 128) * KG + g) * 128 + (row & 127)) * 12 + 3 * q;
+  const uint32_t L0 = __ldg(w), L1 = __ldg(w + 1), H = __ldg(w + 2);
+  const float s = __bfloat162float(__float2bfloat16(scales[er * KG + g]));
+  uint4* o = reinterpret_cast<uint4*>(out + er * K + g * 128 + q * 32);
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    uint32_t p[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int n = v * 8 + h * 2;
+      p[h] = pack_bf16x2((float)(code_at(L0, L1, H, n) - 4) * s, (float)(code_at(L0, L1, H, n + 1) - 4) * s);
+    }
+    o[v] = make_uint4(p[0], p[1], p[2], p[3]);
+  }
 }
 
 int int3_dequant(const void* codes, const float* scales, int E, int R, int K, void* out, cudaStream_t st) {
   if (R % 128 || K % 128) return 3;
-  const int warps = 8;
-  const size_t per_e = (size_t)R * (K / 128);
-  dim3 grid((unsigned)((per_e + warps - 1) / warps), E);
-  int3_dequant_kernel<<<grid, warps * 32, 0, st>>>((const uint32_t*)codes, scales, R, K, (__nv_bfloat16*)out);
+  const size_t threads = (size_t)E * R * (K / 128) * 4;
+  int3_dequant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>((const uint32_t*)codes, scales, E, R, K,
+                                                                         (__nv_bfloat16*)out);
   return (int)cudaGetLastError();
 }
 

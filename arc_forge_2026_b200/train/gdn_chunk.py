@@ -1,14 +1,107 @@
-"""Chunked gated delta rule for training (autograd-friendly, PyTorch ops).
+"""Chunked gated delta rule for training.
 
 The sequence is cut into chunks of C tokens; inside a chunk the delta-rule recurrence is solved in closed form
 (lower-triangular system on ``beta * k k^T`` weighted by the within-chunk decay), and a [Dk, Dv] state carries
 across chunks (the WY formulation of DeltaNet, Yang et al. 2024, with the gate of Gated DeltaNet). It computes
-exactly the recurrence of ``models.reference.gated_delta_rule`` (tests compare them); the GPU decode path uses
-the recurrent kernels in csrc/gdn.cu.
+exactly the recurrence of ``models.reference.gated_delta_rule`` (tests compare them).
+
+Work split (the reference trains through FlashQLA's chunk scan, ``train/preflight.py:280-365``):
+
+* everything inside a chunk (decay matrix, triangular solve, pseudo-values ``u``, decayed keys ``w``, the
+  intra-chunk attention, the outputs) is a handful of batched products over all chunks at once;
+* the only sequential part -- the state passed from chunk to chunk -- is one native kernel per direction
+  (``csrc/gdn_chunk.cu``): forward ``X_i = U_i - W_i S_i``, ``S_{i+1} = e^{last} S_i + Kd_i^T X_i``, and the
+  reverse pass of its gradient; :class:`_InterChunk` carries the hand-derived backward of that recurrence, so
+  autograd never unrolls a per-chunk loop.
+
+On CPU the same two recurrences run as a plain loop (the oracle the native kernel is tested against).
 """
 from __future__ import annotations
 
 import torch
+
+
+def _scan(m1, m2, y, qm, last, init, reverse: bool):
+    """X = Y + s1 * M1 St ; St <- e^{last} St (+ Qm) + s2 * M2^T X over chunks (forward, or reverse order).
+
+    m1, m2 [BH, n, C, Dk]; y [BH, n, C, Dv]; qm [BH, n, Dk, Dv] or None; last [BH, n]; init [BH, Dk, Dv] or None.
+    Returns (states before each step [BH, n, Dk, Dv], X [BH, n, C, Dv], final state [BH, Dk, Dv])."""
+    BH, n, C, Dk = m1.shape
+    Dv = y.shape[-1]
+    if m1.is_cuda:
+        from ..ops import C as ext
+        m1, m2, y, last = (t.float().contiguous() for t in (m1, m2, y, last))
+        qm = qm.float().contiguous() if qm is not None else None
+        init = init.float().contiguous() if init is not None else None
+        states = torch.empty(BH, n, Dk, Dv, device=m1.device, dtype=torch.float32)
+        x = torch.empty_like(y)
+        final = torch.empty(BH, Dk, Dv, device=m1.device, dtype=torch.float32)
+        ext().gdn_chunk_scan(m1, m2, y, qm, last, init, states, x, final, reverse)
+        return states, x, final
+    s1, s2 = (1.0, -1.0) if reverse else (-1.0, 1.0)
+    St = torch.zeros(BH, Dk, Dv, dtype=y.dtype) if init is None else init.clone()
+    states = torch.empty(BH, n, Dk, Dv, dtype=y.dtype)
+    x = torch.empty_like(y)
+    for i in (range(n - 1, -1, -1) if reverse else range(n)):
+        states[:, i] = St
+        xi = y[:, i] + s1 * (m1[:, i] @ St)
+        x[:, i] = xi
+        St = last[:, i].exp()[:, None, None] * St + s2 * (m2[:, i].transpose(-1, -2) @ xi)
+        if qm is not None:
+            St = St + qm[:, i]
+    return states, x, St
+
+
+class _InterChunk(torch.autograd.Function):
+    """o = (q e^{gc}) S_i + attn_i (u_i - w_i S_i), with the state S carried across chunks.
+
+    q, k, w [BH, n, C, Dk]; u [BH, n, C, Dv]; gc [BH, n, C] (within-chunk cumulative log decay)."""
+
+    @staticmethod
+    def _intra(q, k, gc):
+        C = q.shape[-2]
+        tri = torch.ones(C, C, dtype=torch.bool, device=q.device).tril()
+        D = (gc[..., :, None] - gc[..., None, :]).masked_fill(~tri, float("-inf")).exp()
+        attn = (q @ k.transpose(-1, -2)) * D
+        qd = q * gc.exp()[..., None]
+        last = gc[..., -1]
+        kd = k * (last[..., None] - gc).exp()[..., None]
+        return D, attn, qd, kd, last
+
+    @staticmethod
+    def forward(ctx, q, k, u, w, gc, init):
+        D, attn, qd, kd, last = _InterChunk._intra(q, k, gc)
+        states, vnew, final = _scan(w, kd, u, None, last, init, reverse=False)
+        o = qd @ states + attn @ vnew
+        ctx.save_for_backward(q, k, w, gc, states, vnew)
+        ctx.has_init = init is not None
+        return o, final
+
+    @staticmethod
+    def backward(ctx, do, dfinal):
+        q, k, w, gc, states, vnew = ctx.saved_tensors
+        D, attn, qd, kd, last = _InterChunk._intra(q, k, gc)
+        do = do.float().contiguous()
+        P = attn.transpose(-1, -2) @ do                      # attn^T dO
+        Qm = qd.transpose(-1, -2) @ do                       # qd^T dO
+        dnext, dv, dS0 = _scan(kd, w, P, Qm, last, dfinal if dfinal is not None else None, reverse=True)
+        # dnext[:, i] = dS_{i+1}; dv = dL/du = dL/d(vnew)
+        dw = -(dv @ states.transpose(-1, -2))
+        dqd = do @ states.transpose(-1, -2)
+        dq = dqd * gc.exp()[..., None]
+        dgc = (dqd * qd).sum(-1)
+        dattn = do @ vnew.transpose(-1, -2)                  # zero above the diagonal through D
+        G = dattn * attn
+        dq = dq + (dattn * D) @ k
+        dk = (dattn * D).transpose(-1, -2) @ q
+        dgc = dgc + G.sum(-1) - G.sum(-2)
+        dkd = vnew @ dnext.transpose(-1, -2)
+        dk = dk + dkd * (last[..., None] - gc).exp()[..., None]
+        E = (dkd * kd).sum(-1)
+        dgc = dgc - E
+        dlast = E.sum(-1) + last.exp() * (dnext * states).sum((-1, -2))
+        dgc = torch.cat([dgc[..., :-1], (dgc[..., -1] + dlast)[..., None]], -1)
+        return dq, dk, dv, dw, dgc, (dS0 if ctx.has_init else None)
 
 
 def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None):
@@ -26,29 +119,56 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None):
         g = torch.nn.functional.pad(g, (0, pad))
         beta = torch.nn.functional.pad(beta, (0, pad))
     n = q.shape[2] // chunk
-    q, k, v = (x.reshape(B, H, n, chunk, -1) for x in (q, k, v))
-    g, beta = g.reshape(B, H, n, chunk), beta.reshape(B, H, n, chunk)
-    v_beta = v * beta[..., None]
+    q, k, v = (x.reshape(B * H, n, chunk, -1) for x in (q, k, v))
+    g, beta = g.reshape(B * H, n, chunk), beta.reshape(B * H, n, chunk)
     k_beta = k * beta[..., None]
     gc = g.cumsum(-1)  # within-chunk cumulative log decay
-    tri_incl = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool, device=q.device))
-    tri_strict = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool, device=q.device), -1)
+    tri_incl = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril()
+    tri_strict = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(-1)
     decay = (gc[..., :, None] - gc[..., None, :]).masked_fill(~tri_incl, float("-inf")).exp()
     # A = (I + strict_lower(beta k k^T * decay))^-1
     a = -(k_beta @ k.transpose(-1, -2) * decay).masked_fill(~tri_strict, 0.0)
     eye = torch.eye(chunk, dtype=dt, device=q.device)
     A = torch.linalg.solve_triangular(eye - a, eye.expand_as(a), upper=False, unitriangular=True)
-    u = A @ v_beta                                   # pseudo-values
+    u = A @ (v * beta[..., None])                    # pseudo-values
     w = A @ (k_beta * gc.exp()[..., None])          # decayed keys
-    S = torch.zeros(B, H, Dk, Dv, dtype=dt, device=q.device) if state is None else state.to(dt).transpose(0, 0)
+    init = None if state is None else state.to(dt).reshape(B * H, Dk, Dv)
+    o, S = _InterChunk.apply(q, k, u, w, gc, init)
+    o = o.reshape(B, H, n * chunk, Dv)[:, :, :T]
+    return o.transpose(1, 2), S.reshape(B, H, Dk, Dv)
+
+
+def chunk_gated_delta_rule_loop(q, k, v, g, beta, chunk: int = 64, state=None):
+    """The same computation with the inter-chunk state as an autograd-unrolled loop (test oracle)."""
+    B, T, H, Dk = k.shape
+    Dv = v.shape[-1]
+    dt = torch.float32
+    pad = (chunk - T % chunk) % chunk
+    q, k, v = (x.transpose(1, 2).to(dt) for x in (q, k, v))
+    g, beta = g.transpose(1, 2).to(dt), beta.transpose(1, 2).to(dt)
+    if pad:
+        q, k, v = (torch.nn.functional.pad(x, (0, 0, 0, pad)) for x in (q, k, v))
+        g, beta = torch.nn.functional.pad(g, (0, pad)), torch.nn.functional.pad(beta, (0, pad))
+    n = q.shape[2] // chunk
+    q, k, v = (x.reshape(B, H, n, chunk, -1) for x in (q, k, v))
+    g, beta = g.reshape(B, H, n, chunk), beta.reshape(B, H, n, chunk)
+    k_beta = k * beta[..., None]
+    gc = g.cumsum(-1)
+    tri_incl = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril()
+    tri_strict = torch.ones(chunk, chunk, dtype=torch.bool, device=q.device).tril(-1)
+    decay = (gc[..., :, None] - gc[..., None, :]).masked_fill(~tri_incl, float("-inf")).exp()
+    a = -(k_beta @ k.transpose(-1, -2) * decay).masked_fill(~tri_strict, 0.0)
+    eye = torch.eye(chunk, dtype=dt, device=q.device)
+    A = torch.linalg.solve_triangular(eye - a, eye.expand_as(a), upper=False, unitriangular=True)
+    u = A @ (v * beta[..., None])
+    w = A @ (k_beta * gc.exp()[..., None])
+    S = torch.zeros(B, H, Dk, Dv, dtype=dt, device=q.device) if state is None else state.to(dt)
     outs = []
-    qk_mask = ~tri_incl
     for i in range(n):
         qi, ki = q[:, :, i], k[:, :, i]
-        attn = (qi @ ki.transpose(-1, -2) * decay[:, :, i]).masked_fill(qk_mask, 0.0)
+        attn = (qi @ ki.transpose(-1, -2) * decay[:, :, i]).masked_fill(~tri_incl, 0.0)
         v_new = u[:, :, i] - w[:, :, i] @ S
-        o_inter = (qi * gc[:, :, i].exp()[..., None]) @ S
-        outs.append(o_inter + attn @ v_new)
+        outs.append((qi * gc[:, :, i].exp()[..., None]) @ S + attn @ v_new)
         last = gc[:, :, i, -1]
         S = S * last.exp()[..., None, None] + (ki * (last[..., None] - gc[:, :, i]).exp()[..., None]).transpose(-1, -2) @ v_new
     o = torch.stack(outs, 2).reshape(B, H, n * chunk, Dv)[:, :, :T]

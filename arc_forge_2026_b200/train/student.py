@@ -44,6 +44,37 @@ def grouped_linear(x: torch.Tensor, w: torch.Tensor, counts: torch.Tensor) -> to
     return torch.cat(outs) if outs else x.new_zeros(0, w.shape[1])
 
 
+class _Permute(torch.autograd.Function):
+    """rows = x[perm] for a permutation ``perm`` (inverse ``inv``); the gradient is the inverse gather, so neither
+    direction needs an atomic scatter-add."""
+
+    @staticmethod
+    def forward(ctx, x, perm, inv):
+        ctx.save_for_backward(inv)
+        return x.index_select(0, perm)
+
+    @staticmethod
+    def backward(ctx, g):
+        (inv,) = ctx.saved_tensors
+        return g.index_select(0, inv), None, None
+
+
+class _Dispatch(torch.autograd.Function):
+    """xs = x[order // K]: every token once per routed expert, in expert order. The gradient gathers the K copies of
+    each token back with the inverse permutation and sums them (no scatter-add)."""
+
+    @staticmethod
+    def forward(ctx, x, order, inv, K):
+        ctx.save_for_backward(inv)
+        ctx.K = K
+        return x.index_select(0, torch.div(order, K, rounding_mode="floor"))
+
+    @staticmethod
+    def backward(ctx, g):
+        (inv,) = ctx.saved_tensors
+        return g.index_select(0, inv).view(-1, ctx.K, g.shape[-1]).sum(1), None, None, None
+
+
 class StudentMoE(nn.Module):
     def __init__(self, cfg: ModelConfig, router, w13_codes, w13_scales, w2_codes, w2_scales, shared_gate, shared_up,
                  shared_down, shared_expert_gate):
@@ -63,19 +94,22 @@ class StudentMoE(nn.Module):
         T, H = x.shape
         logits = x.float() @ self.router.t()
         w, ids = R.route(logits, c.num_experts_per_tok, c.norm_topk_prob)
+        K = c.num_experts_per_tok
         flat = ids.flatten()
-        order = torch.argsort(flat, stable=True)
+        order = torch.argsort(flat, stable=True)  # (token, k) entries sorted by expert
+        inv = torch.empty_like(order)
+        inv[order] = torch.arange(order.numel(), device=order.device)
         counts = torch.bincount(flat, minlength=c.num_experts)
-        tok = order // c.num_experts_per_tok
-        xs = x[tok]
+        xs = _Dispatch.apply(x, order, inv, K)
         W13 = int3_weight(self.w13_scales, self.w13_codes).to(x.dtype)
         h = grouped_linear(xs, W13, counts)
         I = c.moe_intermediate_size
         h = F.silu(h[:, :I].float()).to(x.dtype) * h[:, I:]
         W2 = int3_weight(self.w2_scales, self.w2_codes).to(x.dtype)
         y = grouped_linear(h, W2, counts)
-        y = y * w.flatten()[order][:, None].to(y.dtype)
-        out = torch.zeros_like(x).index_add(0, tok, y)
+        # back to (token, k) order, weighted by the router and summed over k
+        y = _Permute.apply(y, inv, order).view(T, K, H)
+        out = (y * w.to(y.dtype)[..., None]).sum(1)
         gu = x @ self.shared_w13.to(x.dtype).t()
         Is = c.shared_expert_intermediate_size
         sh = (F.silu(gu[:, :Is].float()).to(x.dtype) * gu[:, Is:]) @ self.shared_down.to(x.dtype).t()

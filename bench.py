@@ -19,6 +19,7 @@ With N GPUs (torchrun), the 128 sessions are split over N data-parallel engine r
 from __future__ import annotations
 
 import argparse
+import collections
 import json
 import os
 import statistics
@@ -96,7 +97,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
-def count_launches(fn):
+def count_launches(fn, census_out=None, time_out=None):
     """Kernels of this repository launched by one call of ``fn`` (kernel list from the profiler's trace; used
     only for counting, never for timing)."""
     import torch
@@ -110,11 +111,17 @@ def count_launches(fn):
             "spec_accept", "build_window", "gather_rows", "expert_sort", "int3_dequant", "int3_scale_grad",
             "fp8_block_fakequant", "topk_tail_kl", "adamw_kernel", "train_kernel")
     n_ours = n_all = 0
+    census = collections.Counter()
     for e in prof.events():
         if e.device_type.name == "CUDA" and not e.name.startswith("Memcpy") and not e.name.startswith("Memset"):
             n_all += 1
+            census[e.name[:90]] += 1
+            if time_out is not None:
+                time_out[e.name[:90]] += e.device_time_total
             if any(k in e.name for k in ours):
                 n_ours += 1
+    if census_out is not None:
+        census_out.update(census)
     return n_ours, n_all
 
 
@@ -342,7 +349,7 @@ def qad_main(args):
     def one_step(inputs):
         losses = []
         for i, x in enumerate(inputs):
-            tg = {"ids": x["t_ids"], "lp": x["lp"], "tail": x["tail"]}
+            tg = {"ids": x["t_ids"].long(), "lp": x["lp"], "tail": x["tail"]}  # int32 on the wire, as stored
             losses.append(train_step(student, opt, x["ids"], tg, qc, signs, accumulate=i < len(inputs) - 1,
                                      sync=False, micro_batches=len(inputs), first=i == 0))
         return torch.stack(losses).mean()
@@ -381,7 +388,13 @@ def qad_main(args):
         t = torch.tensor([ms, e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e_ms = float(t[0]), float(t[1])
-    n_ours, n_all = count_launches(lambda: one_step(dev_in))
+    census, ktime = collections.Counter(), collections.Counter()
+    n_ours, n_all = count_launches(lambda: one_step(dev_in), census, ktime)
+    if rank == 0:  # where one step's launches and kernel time go, for the log (profiler time: not a result)
+        for name, cnt in census.most_common(12):
+            print(f"launches/step {cnt:8d}  {name}", file=sys.stderr)
+        for name, us in ktime.most_common(25):
+            print(f"kernel ms/step {us / 1000:9.1f}  x{census[name]:6d}  {name}", file=sys.stderr)
     tokens = args.global_batch * T * args.steps
     value = tokens / (ms / 1000.0)
     out = {
