@@ -100,6 +100,7 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
 
 void register_kernel_ops(pybind11::module& m);  // defined in ops_bindings.cpp
 void register_runtime(pybind11::module& m);     // defined in runtime.cpp
+void register_symm(pybind11::module& m);        // defined in symm.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "arc_forge_2026_b200 native kernels (sm_100a)";
@@ -110,4 +111,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &gemm_plan);
   register_kernel_ops(m);
   register_runtime(m);
+  register_symm(m);
 }

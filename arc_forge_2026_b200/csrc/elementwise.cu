@@ -241,8 +241,8 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict
   for (int e = threadIdx.x; e < E; e += blockDim.x) ccount[e] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    int e = ids[i];
-    if (expert_map) e = expert_map[e];
+    int e = ids[i];  // < 0: empty slot (expert-parallel receive regions)
+    if (e >= 0 && expert_map) e = expert_map[e];
     if (e >= 0) atomicAdd(&ccount[e], 1);
   }
   __syncthreads();
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict
     int e = -1;
     if (i < n) {
       e = ids[i];
-      if (expert_map) e = expert_map[e];
+      if (e >= 0 && expert_map) e = expert_map[e];
     }
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_in_warp = __popc(peers & ((1u << lane) - 1));

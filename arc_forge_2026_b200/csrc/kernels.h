@@ -86,6 +86,30 @@ struct GdnScanArgs {
 };
 int gdn_chunk_scan(const GdnScanArgs& a, bool reverse, cudaStream_t st);
 
+// ep.cu: expert-parallel MoE exchange over peer memory (symmetric heap regions at equal offsets on every rank)
+constexpr int EP_MAX_RANKS = 8;
+constexpr int EP_DISPATCH = 0, EP_COMBINE = 1;
+struct EpArgs {
+  int world = 1, rank = 0;
+  int T = 0, T_cap = 0, H = 0, k = 0;      // local tokens this step, slots per rank, hidden, experts per token
+  uint8_t* peer[EP_MAX_RANKS] = {};        // heap base of every rank (own included)
+  // region offsets (bytes) inside every heap
+  size_t off_x = 0;      // e4m3 [world*T_cap, H]
+  size_t off_s = 0;      // fp32 [H/128, ld_s] (group-major)
+  size_t off_ids = 0;    // int32 [world*T_cap, k]
+  size_t off_w = 0;      // fp32 [world*T_cap, k]
+  size_t off_comb = 0;   // bf16 [T_cap*k, H] routed rows of this rank's tokens
+  size_t off_flags = 0;  // uint64 [2 types][EP_MAX_RANKS sources]
+  int ld_s = 0;
+  unsigned* done = nullptr;             // local [2] CTA-completion counters
+  unsigned long long* sent = nullptr;   // local [2] exchanges published
+  unsigned long long* expected = nullptr;  // local [2] exchanges consumed
+};
+int ep_dispatch(const EpArgs& a, const void* x, int ldx, const int* ids, const float* weights, cudaStream_t st);
+int ep_wait(const EpArgs& a, int type, uint32_t* status, cudaStream_t st);
+int ep_gather(const EpArgs& a, const int* row_token, const int* nrows_dev, int rows_cap, void* xq, float* xs,
+              int ld_xs, cudaStream_t st);
+
 // sampling.cu
 int select_tokens(const void* logits, int ld, int rows, int V, int* out, float temperature, uint64_t seed,
                   const int* step, uint32_t* status, cudaStream_t st);

@@ -27,6 +27,14 @@ struct MoeGemmArgs {
   const float* route_w = nullptr;  // !PAIR: routing weight per (token, slot) entry, or null
   const int* row_entry = nullptr;  // !PAIR: sorted row -> entry index
   long long* dbg = nullptr;        // optional profiling counters [grid, 4 roles, 3]: wait cycles, total, k-steps
+  // !PAIR under expert parallelism: row_entry indexes all ranks' (token, slot) entries; entry e belongs to rank
+  // e / ep_entries_per_rank and its routed row goes to that rank's combine region at (e % ep_entries_per_rank);
+  // the last CTA then publishes the combine exchange on every rank (flag protocol of ep.cu)
+  int ep_world = 0, ep_rank = 0, ep_entries_per_rank = 0;
+  uint8_t* ep_peer[8] = {};
+  size_t ep_off_comb = 0, ep_off_flags = 0;
+  unsigned* ep_done = nullptr;             // local CTA-completion counter of the combine exchange
+  unsigned long long* ep_sent = nullptr;   // local published-combine counter
 };
 
 int moe_int3_gemm(const MoeGemmArgs& a, int pair, int num_sms, uint32_t* status, cudaStream_t st);

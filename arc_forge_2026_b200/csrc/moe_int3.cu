@@ -342,7 +342,15 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
 #pragma unroll
           for (int i = 0; i < NH; ++i) {
             if (t0 + i >= cn) break;
-            const float w = args.route_w ? args.route_w[args.row_entry[crow + t0 + i]] : 1.f;
+            const int entry = args.row_entry ? args.row_entry[crow + t0 + i] : 0;  // -1: segment padding
+            if (args.ep_world > 0) {
+              if (entry < 0) continue;
+              const int dst = entry / args.ep_entries_per_rank, le = entry - dst * args.ep_entries_per_rank;
+              reinterpret_cast<__nv_bfloat16*>(args.ep_peer[dst] + args.ep_off_comb)[(size_t)le * args.out_ld + col] =
+                  __float2bfloat16(acc0[i] * args.route_w[entry]);
+              continue;
+            }
+            const float w = args.route_w ? (entry >= 0 ? args.route_w[entry] : 0.f) : 1.f;
             reinterpret_cast<__nv_bfloat16*>(args.out_bf16)[(size_t)(crow + t0 + i) * args.out_ld + col] =
                 __float2bfloat16(acc0[i] * w);
           }
@@ -363,6 +371,17 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+  if (!PAIR && args.ep_world > 0) {  // publish the combine exchange once every CTA's peer stores are out
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(args.ep_done, 1u) == gridDim.x - 1) {
+      *args.ep_done = 0;
+      __threadfence_system();
+      const uint64_t v = ++*args.ep_sent;
+      for (int p = 0; p < args.ep_world; ++p)
+        st_release_sys_u64(reinterpret_cast<uint64_t*>(args.ep_peer[p] + args.ep_off_flags) + 8 + args.ep_rank, v);
+    }
   }
 }
 

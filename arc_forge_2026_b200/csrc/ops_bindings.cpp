@@ -72,11 +72,66 @@ void quant_rows_e4m3_op(const at::Tensor& x, c10::optional<at::Tensor> row_token
 
 // INT3 grouped expert GEMM. pair=True: w13 with SwiGLU + e4m3 requant (out_q, out_scales group-major);
 // pair=False: w2 with the routing weight (out_bf16).
+// Expert-parallel exchange context: the region layout of the symmetric heap and the local counters.
+struct EpCtx {
+  afb::EpArgs a;
+  EpCtx(int64_t world, int64_t rank, int64_t T_cap, int64_t H, int64_t k, std::vector<int64_t> peers,
+        std::vector<int64_t> offsets, int64_t ld_s, const at::Tensor& done, const at::Tensor& sent,
+        const at::Tensor& expected) {
+    TORCH_CHECK(world >= 1 && world <= afb::EP_MAX_RANKS && (int64_t)peers.size() == world, "EpCtx: world/peers");
+    TORCH_CHECK(offsets.size() == 6, "EpCtx: offsets = (x, s, ids, w, comb, flags)");
+    AFB_CHECK_DT(done, at::kInt);
+    AFB_CHECK_DT(sent, at::kLong);
+    AFB_CHECK_DT(expected, at::kLong);
+    TORCH_CHECK(done.numel() >= 2 && sent.numel() >= 2 && expected.numel() >= 2, "EpCtx: counters");
+    a.world = (int)world;
+    a.rank = (int)rank;
+    a.T_cap = (int)T_cap;
+    a.H = (int)H;
+    a.k = (int)k;
+    for (int p = 0; p < world; ++p) a.peer[p] = reinterpret_cast<uint8_t*>((uintptr_t)peers[p]);
+    a.off_x = offsets[0];
+    a.off_s = offsets[1];
+    a.off_ids = offsets[2];
+    a.off_w = offsets[3];
+    a.off_comb = offsets[4];
+    a.off_flags = offsets[5];
+    a.ld_s = (int)ld_s;
+    a.done = reinterpret_cast<unsigned*>(done.data_ptr());
+    a.sent = reinterpret_cast<unsigned long long*>(sent.data_ptr());
+    a.expected = reinterpret_cast<unsigned long long*>(expected.data_ptr());
+  }
+  void dispatch(const at::Tensor& x, int64_t T, const at::Tensor& ids, const at::Tensor& w) {
+    AFB_CHECK_DT(x, at::kBFloat16);
+    AFB_CHECK_DT(ids, at::kInt);
+    AFB_CHECK_DT(w, at::kFloat);
+    TORCH_CHECK(x.stride(1) == 1 && x.size(1) == a.H && ids.size(1) == a.k, "ep dispatch shapes");
+    afb::EpArgs b = a;
+    b.T = (int)T;
+    check_rc(afb::ep_dispatch(b, x.data_ptr(), x.stride(0), ptr<int>(ids), ptr<float>(w), stream()), "ep_dispatch");
+  }
+  void wait(int64_t type) { check_rc(afb::ep_wait(a, (int)type, status_ptr(current_device()), stream()), "ep_wait"); }
+  void gather(const at::Tensor& row_token, const at::Tensor& nrows, at::Tensor& xq, at::Tensor& xs) {
+    AFB_CHECK_DT(row_token, at::kInt);
+    AFB_CHECK_DT(nrows, at::kInt);
+    AFB_CHECK_DT(xs, at::kFloat);
+    TORCH_CHECK(xq.size(1) == a.H && xq.size(0) <= row_token.size(0), "ep gather shapes");
+    check_rc(afb::ep_gather(a, ptr<int>(row_token), ptr<int>(nrows), xq.size(0), xq.data_ptr(), ptr<float>(xs),
+                            xs.stride(0), stream()),
+             "ep_gather");
+  }
+  static int current_device() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
+  }
+};
+
 void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& offsets,
                       const at::Tensor& x_q, const at::Tensor& x_scales, bool pair, c10::optional<at::Tensor> out_q,
                       c10::optional<at::Tensor> out_scales, c10::optional<at::Tensor> out_bf16,
                       c10::optional<at::Tensor> route_w, c10::optional<at::Tensor> row_entry,
-                      c10::optional<at::Tensor> dbg) {
+                      c10::optional<at::Tensor> dbg, const EpCtx* ep) {
   AFB_CHECK_DT(codes, at::kInt);
   AFB_CHECK_DT(scales, at::kBFloat16);
   AFB_CHECK_DT(offsets, at::kInt);
@@ -100,6 +155,7 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
   TORCH_CHECK(a.ld_xs % 4 == 0 && x_scales.size(1) >= a.num_rows_total + 32,
               "x_scales must be group-major [K/128, >= rows + 32] with a row stride divisible by 4");
   if (pair) {
+    TORCH_CHECK(!ep, "expert-parallel output is the w2 GEMM's");
     TORCH_CHECK(out_q.has_value() && out_scales.has_value(), "pair needs out_q and out_scales");
     a.out_q = optr<uint8_t>(out_q);
     a.out_scales = optr<float>(out_scales);
@@ -114,6 +170,17 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
     a.route_w = optr<float>(route_w);
     a.row_entry = optr<int>(row_entry);
     TORCH_CHECK(!a.route_w || a.row_entry, "route_w needs row_entry");
+    if (ep) {
+      TORCH_CHECK(a.route_w && a.row_entry && a.out_ld == ep->a.H, "expert-parallel w2 needs route_w and row_entry");
+      a.ep_world = ep->a.world;
+      a.ep_rank = ep->a.rank;
+      a.ep_entries_per_rank = ep->a.T_cap * ep->a.k;
+      for (int p = 0; p < ep->a.world; ++p) a.ep_peer[p] = ep->a.peer[p];
+      a.ep_off_comb = ep->a.off_comb;
+      a.ep_off_flags = ep->a.off_flags;
+      a.ep_done = ep->a.done + afb::EP_COMBINE;
+      a.ep_sent = ep->a.sent + afb::EP_COMBINE;
+    }
   }
   a.dbg = optr<long long>(dbg);
   check_rc(afb::moe_int3_gemm(a, pair, num_sms(), status_ptr(codes.get_device()), stream()), "moe_int3_gemm");
@@ -401,7 +468,13 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("moe_combine", &moe_combine_op);
   m.def("moe_int3_gemm", &moe_int3_gemm_op, py::arg("codes"), py::arg("scales"), py::arg("offsets"), py::arg("x_q"),
         py::arg("x_scales"), py::arg("pair"), py::arg("out_q"), py::arg("out_scales"), py::arg("out_bf16"),
-        py::arg("route_w"), py::arg("row_entry"), py::arg("dbg") = py::none());
+        py::arg("route_w"), py::arg("row_entry"), py::arg("dbg") = py::none(), py::arg("ep") = nullptr);
+  py::class_<EpCtx>(m, "EpCtx")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, std::vector<int64_t>, std::vector<int64_t>, int64_t,
+                    const at::Tensor&, const at::Tensor&, const at::Tensor&>())
+      .def("dispatch", &EpCtx::dispatch)
+      .def("wait", &EpCtx::wait)
+      .def("gather", &EpCtx::gather);
   m.def("swiglu", &swiglu_op);
   m.def("int3_dequant", &int3_dequant_op);
   m.def("int3_scale_grad", &int3_scale_grad_op);

@@ -25,6 +25,7 @@ from ..ops import C
 from ..ops.attention import PAGE, paged_attention
 from ..ops.gdn import GdnScratch, GdnShape, GdnState, gdn_decode
 from ..ops.moe import Int3ExpertBank, MoEWorkspace, moe_forward, router_weight_with_shared_gate
+from ..parallel.ep import EPMoEWorkspace, moe_forward_ep
 from .reference import HybridMoE, rope_cos_sin
 
 
@@ -88,11 +89,28 @@ class HybridModel:
                                   c.linear_value_head_dim)
         cos, sin = rope_cos_sin(torch.arange(1 << 17, device=self.device), c.rotary_dim, c.rope_theta)
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
+        self.ep = None  # ExpertParallel when the routed experts are split over ranks
+
+    def enable_expert_parallel(self, world: int, rank: int, T_cap: int, group=None):
+        """Split the routed experts over ``world`` ranks (keeps this rank's block) and route every MoE layer
+        through the peer-memory exchange. ``T_cap`` bounds the tokens of one forward on this rank."""
+        from ..parallel.ep import ExpertParallel, expert_range, local_bank
+        c = self.cfg
+        e0, e1 = expert_range(c.num_experts, world, rank)
+        for lw in self.layers:
+            if lw.bank.num_experts == c.num_experts:
+                lw.bank = local_bank(lw.bank, world, rank)
+            elif lw.bank.num_experts != e1 - e0:
+                raise ValueError(f"layer holds {lw.bank.num_experts} experts, expected {c.num_experts} or {e1 - e0}")
+        self.ep = ExpertParallel(world, rank, T_cap, c.hidden_size, c.num_experts_per_tok, c.num_experts,
+                                 self.device, group)
+        return self.ep
 
     # ------------------------------------------------------------------ construction
     @classmethod
-    def random(cls, cfg: ModelConfig, device, seed: int = 0, std: float | None = None):
-        """Random-init weights of ``cfg`` generated directly on the device (INT3 experts as random codes)."""
+    def random(cls, cfg: ModelConfig, device, seed: int = 0, std: float | None = None, ep_world: int = 1):
+        """Random-init weights of ``cfg`` generated directly on the device (INT3 experts as random codes).
+        With ``ep_world > 1`` only one rank's block of ``E / ep_world`` experts is made per layer."""
         std = cfg.init_std if std is None else std
         dev = torch.device(device)
         gen = torch.Generator(device=dev).manual_seed(seed)
@@ -124,6 +142,7 @@ class HybridModel:
                 lw.w_out = randn(H, gs.Hv * gs.Dv)
             E, I, Is = cfg.num_experts, cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
             lw.router_ext = router_weight_with_shared_gate(randn(E, H), randn(1, H))
+            E = E // ep_world
             lw.bank = Int3ExpertBank(
                 torch.randint(-2**31, 2**31 - 1, (E, 2 * I // 128, H // 128, 128, 12), dtype=torch.int32,
                               device=dev, generator=gen),
@@ -247,8 +266,12 @@ class HybridModel:
                 cC.gemm(o, lw.w_out, out=h, residual=h)
                 gi += 1
             cC.rmsnorm(h, None, lw.post_norm, y, c.rms_norm_eps, True)
-            moe_forward(y, h, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, c.num_experts_per_tok, ws.moe,
-                        out=h, renorm=c.norm_topk_prob)
+            if self.ep is not None:
+                moe_forward_ep(y, h, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, self.ep, ws.moe, out=h,
+                               renorm=c.norm_topk_prob)
+            else:
+                moe_forward(y, h, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, c.num_experts_per_tok, ws.moe,
+                            out=h, renorm=c.norm_topk_prob)
         cC.rmsnorm(h, None, self.final_norm, y, c.rms_norm_eps, True)
         return y
 
@@ -274,5 +297,8 @@ class Workspace:
         gs = model.gdn_shape
         self.mixed = torch.empty(max_tokens, gs.mixed_dim, **bf)
         self.gdn_out = torch.empty(max_tokens, gs.Hv * gs.Dv, **bf)
-        self.moe = MoEWorkspace(max_tokens, c.num_experts, c.num_experts_per_tok, H, c.moe_intermediate_size,
-                                c.shared_expert_intermediate_size, dev)
+        if model.ep is not None:
+            self.moe = EPMoEWorkspace(model.ep, c.moe_intermediate_size, c.shared_expert_intermediate_size, dev)
+        else:
+            self.moe = MoEWorkspace(max_tokens, c.num_experts, c.num_experts_per_tok, H, c.moe_intermediate_size,
+                                    c.shared_expert_intermediate_size, dev)

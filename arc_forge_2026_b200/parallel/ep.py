@@ -1,0 +1,156 @@
+"""Expert parallelism for serving: attention / GDN layers stay data-parallel (each rank keeps its own sessions),
+the routed experts are split in contiguous blocks of ``E / world`` per rank, and every MoE layer exchanges tokens
+through a symmetric device heap with the native kernels of ``csrc/ep.cu``:
+
+    router (local) -> ep_dispatch (e4m3 quantisation fused with the all-gather to every rank's receive region)
+    -> shared expert (local, overlaps the exchange) -> ep_wait -> expert_sort of all ranks' entries for the
+    local experts -> ep_gather -> w13 GEMM -> w2 GEMM whose epilogue stores each routed row into its token owner's
+    combine region and publishes the exchange -> ep_wait -> combine (k rows in slot order + shared + residual).
+
+The reference splits experts the same way (``--ep 4`` in its B200 server configs, ``training/run_records/A1/
+config/p30241.server.json:32``) and, on its L4 stack, dispatches by all-gather and combines by a reduce to the
+owner rows (``hostcomm.cu:525-700``); here both ends are stores into peer HBM over NVSwitch from inside the
+kernels that produce the data.
+
+Every rank must run the same MoE layers in the same order (the exchanges are barriers): the engine steps all
+ranks together, a rank with no tokens still joins each exchange with ``T = 0``.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import C
+from ..ops.moe import SEG_PAD, Int3ExpertBank
+
+EP_DISPATCH, EP_COMBINE = 0, 1
+MAX_RANKS = 8
+
+
+def _align(x: int, a: int = 256) -> int:
+    return (x + a - 1) // a * a
+
+
+def expert_range(E: int, world: int, rank: int) -> tuple[int, int]:
+    """[e0, e1) of the experts rank ``rank`` owns."""
+    if E % world:
+        raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    n = E // world
+    return rank * n, (rank + 1) * n
+
+
+def local_bank(bank: Int3ExpertBank, world: int, rank: int) -> Int3ExpertBank:
+    e0, e1 = expert_range(bank.num_experts, world, rank)
+    return Int3ExpertBank(bank.w13_codes[e0:e1].contiguous(), bank.w13_scales[e0:e1].contiguous(),
+                          bank.w2_codes[e0:e1].contiguous(), bank.w2_scales[e0:e1].contiguous())
+
+
+class ExpertParallel:
+    """The exchange state of one EP group: symmetric heap, region views, counters and the native context.
+
+    ``T_cap`` is the most tokens one rank sends per MoE layer (its workspace capacity); the heap holds
+    ``world * T_cap`` receive slots and this rank's ``T_cap * k`` combine rows."""
+
+    def __init__(self, world: int, rank: int, T_cap: int, H: int, k: int, E: int, device, group=None):
+        if not 1 <= world <= MAX_RANKS:
+            raise ValueError(f"expert parallelism supports 1..{MAX_RANKS} ranks, got {world}")
+        self.world, self.rank, self.T_cap, self.H, self.k, self.E = world, rank, T_cap, H, k, E
+        self.e0, self.e1 = expert_range(E, world, rank)
+        self.E_local = self.e1 - self.e0
+        dev = torch.device(device)
+        rows = world * T_cap
+        self.ld_s = (rows + 32 + 3) // 4 * 4
+        off_x = 0
+        off_s = _align(off_x + rows * H)
+        off_ids = _align(off_s + (H // 128) * self.ld_s * 4)
+        off_w = _align(off_ids + rows * k * 4)
+        off_comb = _align(off_w + rows * k * 4)
+        off_flags = _align(off_comb + T_cap * k * H * 2)
+        total = _align(off_flags + 2 * MAX_RANKS * 8)
+        self.offsets = [off_x, off_s, off_ids, off_w, off_comb, off_flags]
+        ext = C()
+        self.heap = ext.SymmHeap(total, rank, world, dev.index if dev.index is not None else 0)
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, self.heap.handle(), group=group)
+            self.heap.open(handles)
+            dist.barrier(group=group)  # every heap is zeroed and mapped before any rank stores a flag
+        buf = self.heap.tensor()
+        self.recv_ids = buf[off_ids:off_ids + rows * k * 4].view(torch.int32).view(rows, k)
+        self.recv_w = buf[off_w:off_w + rows * k * 4].view(torch.float32)
+        self.comb = buf[off_comb:off_comb + T_cap * k * H * 2].view(torch.bfloat16).view(T_cap * k, H)
+        self.done = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.sent = torch.zeros(2, dtype=torch.int64, device=dev)
+        self.expected = torch.zeros(2, dtype=torch.int64, device=dev)
+        self.ctx = ext.EpCtx(world, rank, T_cap, H, k, list(self.heap.peers()), self.offsets, self.ld_s, self.done,
+                             self.sent, self.expected)
+        self.expert_map = torch.full((E,), -1, dtype=torch.int32, device=dev)
+        self.expert_map[self.e0:self.e1] = torch.arange(self.E_local, dtype=torch.int32, device=dev)
+        self.identity = torch.arange(T_cap * k, dtype=torch.int32, device=dev)  # combine rows are [t, slot]
+
+    def close(self):
+        if self.heap is not None:
+            self.heap.close()
+            self.heap = None
+
+
+class EPMoEWorkspace:
+    """Per-layer buffers of the expert-parallel MoE (fixed addresses: CUDA-graph safe)."""
+
+    def __init__(self, ep: ExpertParallel, I: int, Is: int, device):
+        dev = torch.device(device)
+        T, k, H, E_loc = ep.T_cap, ep.k, ep.H, ep.E_local
+        n = ep.world * T * k
+        R = n + (SEG_PAD - 1) * E_loc
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.n, self.rows = n, R
+        self.logits = torch.empty(T, ep.E + 8, dtype=torch.float32, device=dev)
+        self.ids = torch.empty(T, k, **i32)
+        self.weights = torch.empty(T, k, dtype=torch.float32, device=dev)
+        self.offsets = torch.empty(E_loc + 1, **i32)
+        self.row_token = torch.empty(R, **i32)
+        self.row_entry = torch.empty(R, **i32)
+        self.entry_row = torch.empty(n, **i32)
+        self.xq = torch.empty(R, H, dtype=torch.float8_e4m3fn, device=dev)
+        ld = (R + 32 + 3) // 4 * 4
+        self.xs = torch.zeros(H // 128, ld, dtype=torch.float32, device=dev)
+        self.hq = torch.empty(R, I, dtype=torch.float8_e4m3fn, device=dev)
+        self.hs = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
+        self.y = torch.empty(8, H, dtype=torch.bfloat16, device=dev)  # unused: w2 rows go to the combine regions
+        self.sh_gu = torch.empty(T, 2 * Is, dtype=torch.bfloat16, device=dev)
+        self.sh_h = torch.empty(T, Is, dtype=torch.bfloat16, device=dev)
+        self.sh_out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+
+
+def moe_forward_ep(x: torch.Tensor, resid: torch.Tensor, router_ext: torch.Tensor, bank: Int3ExpertBank,
+                   shared_w13: torch.Tensor, shared_w2: torch.Tensor, ep: ExpertParallel, ws: EPMoEWorkspace,
+                   out: torch.Tensor, renorm: bool = True) -> torch.Tensor:
+    """out = resid + MoE(x) for this rank's T tokens, with the routed experts spread over the EP group."""
+    c = C()
+    T, H = x.shape
+    k, E = ep.k, ep.E
+    if T > ep.T_cap:
+        raise ValueError(f"{T} tokens exceed the expert-parallel capacity {ep.T_cap}")
+    logits = ws.logits[:T]
+    ids, w = ws.ids[:T], ws.weights[:T]
+    if T > 0:
+        c.gemm(x, router_ext, out=logits, out_fp32=True)
+        c.router_topk(logits, E, k, renorm, ids, w)
+    ep.ctx.dispatch(x, T, ws.ids, ws.weights)
+    if T > 0:  # the shared expert runs while the peers' dispatch stores land
+        c.gemm(x, shared_w13, out=ws.sh_gu[:T])
+        c.swiglu(ws.sh_gu[:T], ws.sh_h[:T])
+        c.gemm(ws.sh_h[:T], shared_w2, out=ws.sh_out[:T])
+    ep.ctx.wait(EP_DISPATCH)
+    R = ws.rows
+    c.expert_sort(ep.recv_ids, ep.E_local, ep.expert_map, ws.offsets, ws.row_token, ws.row_entry, ws.entry_row,
+                  SEG_PAD)
+    ep.ctx.gather(ws.row_token, ws.offsets[ep.E_local:], ws.xq, ws.xs)
+    c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.offsets, ws.xq[:R], ws.xs, True, ws.hq[:R], ws.hs, None,
+                    None, None)
+    c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.offsets, ws.hq[:R], ws.hs, False, None, None, ep.comb,
+                    ep.recv_w, ws.row_entry[:R], None, ep.ctx)
+    ep.ctx.wait(EP_COMBINE)
+    if T > 0:
+        c.moe_combine(ep.comb, ep.identity[:T * k], k, ws.sh_out[:T], logits, E, resid, out)
+    return out

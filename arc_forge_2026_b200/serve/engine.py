@@ -1,4 +1,5 @@
-"""Speculative serving engine on one GPU (the EP variant in ``parallel/ep_engine.py`` reuses it per rank).
+"""Speculative serving engine on one GPU; under expert parallelism every rank runs one over its own sessions and
+the model's MoE layers exchange tokens with the other ranks (``parallel/ep.py``).
 
 One decode cycle for all resident sessions (fixed shapes, no host inputs, CUDA-graph replayable):
 
@@ -185,6 +186,9 @@ class SpecEngine:
     @torch.no_grad()
     def _prefill(self, sess: Session):
         cC, m = C(), self.model
+        if m.ep is not None and m.ep.world > 1:
+            raise NotImplementedError("prefill under expert parallelism needs every rank in the same forward; "
+                                      "this engine prefills one rank's session alone")
         dev = self.device
         L = len(sess.prompt)
         ids_all = torch.tensor(sess.prompt, dtype=torch.int32, device=dev)

@@ -109,7 +109,8 @@ def count_launches(fn, census_out=None, time_out=None):
     ours = ("gemm_bf16", "splitk_reduce", "moe_int3", "rmsnorm", "qk_norm_rope", "router_topk", "expert_sort",
             "quant_rows", "moe_combine", "swiglu", "embedding", "paged_attn", "attn_merge", "gdn_", "select_tokens",
             "spec_accept", "build_window", "gather_rows", "expert_sort", "int3_dequant", "int3_scale_grad",
-            "fp8_block_fakequant", "topk_tail_kl", "adamw_kernel", "train_kernel")
+            "fp8_block_fakequant", "topk_tail_kl", "adamw_kernel", "train_kernel", "ep_dispatch", "ep_wait",
+            "ep_gather", "gdn_chunk_scan")
     n_ours = n_all = 0
     census = collections.Counter()
     for e in prof.events():
@@ -173,7 +174,9 @@ def main():
     S_total = args.sessions
     S = S_total // world + (1 if rank < S_total % world else 0)
     K = 4
-    model = HybridModel.random(cfg, dev, seed=args.seed)
+    model = HybridModel.random(cfg, dev, seed=args.seed, ep_world=world)
+    if world > 1:  # attention/GDN data-parallel over sessions, routed experts split over the ranks
+        model.enable_expert_parallel(world, rank, T_cap=S * (K + 1))
     drafter = Drafter(drafter_preset("dflash_8l"), cfg.hidden_size, cfg.vocab_size, dev, seed=args.seed + 1)
     scfg = ServeConfig(spec_k=K, accept_mode="bernoulli", accept_prob=0.7, seed=args.seed + 7 * rank)
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
@@ -283,7 +286,8 @@ def main():
         "data": "synthetic (random-init weights; random tokens; contexts U[4k,24k] as random KV/GDN state)",
         "config": {"model": "qwen3next_80b-shaped hybrid MoE, 48L, 320 experts top-10 INT3 g128 + shared; "
                             "8-layer DFlash drafter", "global_batch": S_total, "seq_len": f"U[{args.min_ctx},"
-                            f"{args.max_ctx}] context + decode", "parallelism": f"dp{world}",
+                            f"{args.max_ctx}] context + decode",
+                   "parallelism": f"dp{world}-attn+ep{world}" if world > 1 else "dp1",
                    "spec_k": K, "acceptance": "seeded Bernoulli(0.7) per position", "layers": args.layers,
                    "l2": "inputs larger than L2 (weights 24 GB, KV > 40 GB streamed every cycle)"},
         "p50_tpot_ms": round(p50, 3) if p50 else None,
@@ -297,6 +301,9 @@ def main():
         print(json.dumps(out))
     eng.graphs.clear()
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank still reads a peer's heap
+        model.ep.close()
         dist.destroy_process_group()
 
 
