@@ -246,14 +246,39 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict
     if (e >= 0) atomicAdd(&ccount[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int e = 0; e < E; ++e) {
-      offsets[e] = acc;
-      cnt[e] = acc;
-      acc += (ccount[e] + pad - 1) / pad * pad;
+  {  // segment starts: block-wide exclusive scan of the padded counts (each thread owns `per` experts)
+    int* wsum = sm + 34 * E;  // [32]
+    const int per = (E + blockDim.x - 1) / blockDim.x, e0 = threadIdx.x * per;
+    int local = 0;
+    for (int i = 0; i < per; ++i)
+      if (e0 + i < E) local += (ccount[e0 + i] + pad - 1) / pad * pad;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
     }
-    offsets[E] = acc;
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int nw = blockDim.x >> 5;
+      int v = lane < nw ? wsum[lane] : 0, x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += u;
+      }
+      if (lane < nw) wsum[lane] = x - v;
+    }
+    __syncthreads();
+    int base = wsum[warp] + incl - local;
+    for (int i = 0; i < per; ++i)
+      if (e0 + i < E) {
+        offsets[e0 + i] = base;
+        cnt[e0 + i] = base;
+        base += (ccount[e0 + i] + pad - 1) / pad * pad;
+      }
+    if (threadIdx.x == blockDim.x - 1) offsets[E] = base;
   }
   __syncthreads();
   // pad rows
@@ -302,7 +327,7 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int* __restrict
 
 int expert_sort(const int* ids, int n, int E, const int* expert_map, int* offsets, int* row_token, int* row_entry,
                 int* entry_row, int k, int pad, cudaStream_t st) {
-  const size_t smem = (size_t)(34 * E) * sizeof(int);
+  const size_t smem = (size_t)(34 * E + 32) * sizeof(int);
   if (smem > 200 * 1024) return 3;
   static bool attr = false;
   if (!attr) {
@@ -365,46 +390,53 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
                                    const __nv_bfloat16* __restrict__ shared, const float* __restrict__ router_logits,
                                    int ld_logits, int sg_col, const __nv_bfloat16* __restrict__ resid,
                                    __nv_bfloat16* __restrict__ out, int T, int H) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
+  // one CTA per token, one thread per 8 columns; all k row loads of a thread are issued before the sums
+  const int t = blockIdx.x;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (t >= T || c >= H) return;
   float sg = 1.f;
   if (router_logits) sg = 1.f / (1.f + __expf(-router_logits[(size_t)t * ld_logits + sg_col]));
-  int rows[32];
-  for (int j = 0; j < k; ++j) rows[j] = entry_row[t * k + j];
-  for (int c = lane * 8; c < H; c += 256) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < k; ++j) {
-      if (rows[j] < 0) continue;
-      uint4 q = *reinterpret_cast<const uint4*>(y + (size_t)rows[j] * H + c);
-      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  constexpr int KB = 4;  // rows in flight per batch
+  for (int j0 = 0; j0 < k; j0 += KB) {
+    uint4 q[KB];
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {
+      const int r = j0 + u < k ? entry_row[t * k + j0 + u] : -1;
+      q[u] = r >= 0 ? *reinterpret_cast<const uint4*>(y + (size_t)r * H + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < KB; ++u) {  // slot order is kept: the sum is the same on every run and every rank count
+      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q[u]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
     }
-    if (shared) {
-      uint4 q = *reinterpret_cast<const uint4*>(shared + (size_t)t * H + c);
-      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += sg * __bfloat162float(hq[i]);
-    }
-    if (resid) {
-      uint4 q = *reinterpret_cast<const uint4*>(resid + (size_t)t * H + c);
-      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
-    }
-    *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = make_uint4(
-        pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
   }
+  if (shared) {
+    uint4 q = *reinterpret_cast<const uint4*>(shared + (size_t)t * H + c);
+    const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += sg * __bfloat162float(hq[i]);
+  }
+  if (resid) {
+    uint4 q = *reinterpret_cast<const uint4*>(resid + (size_t)t * H + c);
+    const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
+  }
+  *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = make_uint4(
+      pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
 }
 
 int moe_combine(const void* y, const int* entry_row, int k, const void* shared, const float* router_logits,
                 int ld_logits, int sg_col, const void* resid, void* out, int T, int H, cudaStream_t st) {
-  if (H % 8 || k > 32) return 3;
-  const int warps = 4;
-  moe_combine_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(
-      (const __nv_bfloat16*)y, entry_row, k, (const __nv_bfloat16*)shared, router_logits, ld_logits, sg_col,
-      (const __nv_bfloat16*)resid, (__nv_bfloat16*)out, T, H);
+  if (H % 8 || k > 64) return 3;
+  if (T <= 0) return 0;
+  const int threads = 256;
+  dim3 grid(T, (H / 8 + threads - 1) / threads);
+  moe_combine_kernel<<<grid, threads, 0, st>>>((const __nv_bfloat16*)y, entry_row, k, (const __nv_bfloat16*)shared,
+                                               router_logits, ld_logits, sg_col, (const __nv_bfloat16*)resid,
+                                               (__nv_bfloat16*)out, T, H);
   return (int)cudaGetLastError();
 }
 

@@ -143,6 +143,7 @@ def main():
     ap.add_argument("--seq-len", dest="seq_len", type=int, default=16384, help="qad: tokens per sequence")
     ap.add_argument("--global-batch", dest="global_batch", type=int, default=32, help="qad: sequences per step")
     ap.add_argument("--topk", type=int, default=64, help="qad: teacher top-k")
+    ap.add_argument("--census", action="store_true", help="print the kernel-time shares of one step (stderr)")
     args = ap.parse_args()
     if args.impl == "reference":
         _reference_arm(args)
@@ -262,7 +263,12 @@ def main():
     h2d = eng.bt_host.numel() * 4
     d2h = (eng.out_host.numel() + eng.cnt_host.numel()) * 4
 
-    n_ours, n_all = count_launches(eng.run_cycle)
+    census, ktime = collections.Counter(), collections.Counter()
+    n_ours, n_all = count_launches(eng.run_cycle, census, ktime)
+    if args.census and rank == 0:  # kernel-time shares of one cycle for the log (profiler time: not a result)
+        tot = sum(ktime.values())
+        for name, us in ktime.most_common(30):
+            print(f"kernel {us / 1000:8.3f} ms {100 * us / tot:5.1f}%  x{census[name]:5d}  {name}", file=sys.stderr)
 
     # ---------------- reduce over ranks (max time, summed tokens)
     if world > 1:
