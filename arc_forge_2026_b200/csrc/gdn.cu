@@ -287,20 +287,44 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
     float S[HK];
 #pragma unroll
     for (int k = 0; k < HK; ++k) S[k] = sm.state[b][(part * HK + k) * DV + v];
-    auto step = [&](int ts, float decay, float beta) {
-      const __nv_bfloat16* kk = sm.kq[b][ts][0] + part * HK;
-      const float vv = __bfloat162float(sm.v[b][ts][v]);
-      float mem = 0.f;
+    // this thread's 32 key (or query) values of a token row: four 16-byte shared loads, unpacked 8 at a time
+    auto load8 = [&](const __nv_bfloat16* row, int j, float* f) {
+      const uint4 u = reinterpret_cast<const uint4*>(row + part * HK)[j];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-      for (int k = 0; k < HK; ++k) {
-        S[k] *= decay;
-        mem = fmaf(__bfloat162float(kk[k]), S[k], mem);
+      for (int i = 0; i < 4; ++i) {
+        const float2 x = __bfloat1622float2(h2[i]);
+        f[2 * i] = x.x;
+        f[2 * i + 1] = x.y;
       }
+    };
+    auto step = [&](int ts, float decay, float beta) {
+      const __nv_bfloat16* kk = sm.kq[b][ts][0];
+      const float vv = __bfloat162float(sm.v[b][ts][v]);
+      float mem0 = 0.f, mem1 = 0.f;  // two chains halve the dependent-FMA latency
+#pragma unroll
+      for (int j = 0; j < HK / 8; ++j) {
+        float f[8];
+        load8(kk, j, f);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          S[8 * j + i] *= decay;
+          S[8 * j + i + 1] *= decay;
+          mem0 = fmaf(f[i], S[8 * j + i], mem0);
+          mem1 = fmaf(f[i + 1], S[8 * j + i + 1], mem1);
+        }
+      }
+      float mem = mem0 + mem1;
 #pragma unroll
       for (int o = 1; o < QT; o <<= 1) mem += __shfl_xor_sync(0xffffffffu, mem, o);
       const float delta = beta * (vv - mem);
 #pragma unroll
-      for (int k = 0; k < HK; ++k) S[k] = fmaf(__bfloat162float(kk[k]), delta, S[k]);
+      for (int j = 0; j < HK / 8; ++j) {
+        float f[8];
+        load8(kk, j, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) S[8 * j + i] = fmaf(f[i], delta, S[8 * j + i]);
+      }
     };
     for (int t = 0; t < np; ++t) step(t, __expf(sm.gb[b][0][2 * t]), sm.gb[b][0][2 * t + 1]);
     float* sp = a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV + (size_t)(part * HK) * DV + v;
@@ -308,10 +332,18 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
     for (int k = 0; k < HK; ++k) sp[(size_t)k * DV] = S[k];  // the committed state
     for (int t = 0; t < T; ++t) {
       step(MAXT + t, __expf(sm.gb[b][1][2 * t]), sm.gb[b][1][2 * t + 1]);
-      const __nv_bfloat16* qq = sm.kq[b][MAXT + t][1] + part * HK;
-      float o = 0.f;
+      float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-      for (int k = 0; k < HK; ++k) o = fmaf(__bfloat162float(qq[k]), S[k], o);
+      for (int j = 0; j < HK / 8; ++j) {
+        float f[8];
+        load8(sm.kq[b][MAXT + t][1], j, f);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          o0 = fmaf(f[i], S[8 * j + i], o0);
+          o1 = fmaf(f[i + 1], S[8 * j + i + 1], o1);
+        }
+      }
+      float o = o0 + o1;
 #pragma unroll
       for (int x = 1; x < QT; x <<= 1) o += __shfl_xor_sync(0xffffffffu, o, x);
       const float ssq = warp_sum(part ? 0.f : o * o);
