@@ -1,0 +1,371 @@
+"""OpenAI-compatible HTTP server over a serving engine (the GPU ``SpecEngine`` or the CPU reference engine).
+
+Routes (the surface the reference's agents use through its sglang fork: chat/completions, the Responses API with
+server-side sessions and ``/close_session``, usage accounting):
+
+    GET  /health                 liveness
+    GET  /v1/models              the served model
+    POST /v1/completions         {"prompt": str | [int], "max_tokens", "stream"}
+    POST /v1/chat/completions    {"messages": [...], "max_tokens", "stream"}
+    POST /v1/responses           {"input": str | [messages], "session_id"?, "max_output_tokens", "stream"}
+                                 a session keeps its transcript (and, on engines that can extend a session, its
+                                 KV / recurrent state) until /close_session
+    POST /close_session          {"session_id"}
+    GET  /metrics                Prometheus text (requests, tokens, active sessions, step latency)
+
+One engine thread owns the engine: it admits queued requests when a session slot is free, runs ``engine.step()``
+while any request is live and hands emitted tokens to the waiting HTTP handlers through their event loops.
+
+    python -m arc_forge_2026_b200.serve.server --preset tiny_cpu --port 8000          # CPU reference engine
+    python -m arc_forge_2026_b200.serve.server --preset tiny_gpu --gpu --port 8000    # native engine
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import collections
+import itertools
+import json
+import threading
+import time
+import uuid
+from dataclasses import dataclass, field
+
+from .tokenizer import ByteTokenizer
+
+
+@dataclass
+class Request:
+    prompt: list[int]
+    max_new: int
+    loop: asyncio.AbstractEventLoop
+    queue: asyncio.Queue
+    session_key: str | None = None
+    extend: list[int] | None = None   # continuation tokens for an existing session
+    sid: int = -1
+    n_out: int = 0
+    t0: float = field(default_factory=time.perf_counter)
+
+
+class EngineLoop:
+    """Runs the engine on one thread; requests come in through ``submit`` and tokens go out per request."""
+
+    def __init__(self, engine, eos_id: int | None = None, metrics=None):
+        self.engine = engine
+        self.eos_id = eos_id
+        self.metrics = metrics
+        self.cv = threading.Condition()
+        self.pending: collections.deque[Request] = collections.deque()
+        self.live: dict[int, Request] = {}
+        self.keyed: dict[str, int] = {}          # session_id -> engine sid (kept until /close_session)
+        self.transcripts: dict[str, list[int]] = {}
+        self._sids = itertools.count(1)
+        self._stop = False
+        self.thread = threading.Thread(target=self._run, name="afb-engine", daemon=True)
+        self.thread.start()
+
+    def submit(self, req: Request):
+        with self.cv:
+            self.pending.append(req)
+            self.cv.notify()
+
+    def close_session(self, key: str) -> bool:
+        with self.cv:
+            sid = self.keyed.pop(key, None)
+            self.transcripts.pop(key, None)
+            if sid is not None and sid not in self.live and sid in self.engine.sessions:
+                self.engine.release(sid)
+            return sid is not None
+
+    def shutdown(self):
+        with self.cv:
+            self._stop = True
+            self.cv.notify()
+        self.thread.join(timeout=10)
+
+    # ---------------------------------------------------------------- engine thread
+    def _emit(self, req: Request, item):
+        req.loop.call_soon_threadsafe(req.queue.put_nowait, item)
+
+    def _admit(self, req: Request):
+        eng = self.engine
+        key = req.session_key
+        try:
+            if key is not None and key in self.keyed:
+                sid = self.keyed[key]
+                if hasattr(eng, "extend_session") and sid in eng.sessions:
+                    sess = eng.extend_session(sid, req.extend or [], req.max_new)
+                else:  # engine without continuation: re-prefill the whole transcript
+                    if sid in eng.sessions:
+                        eng.release(sid)
+                    sess = eng.add_session(sid, self.transcripts[key] + (req.extend or []), req.max_new)
+            else:
+                sid = next(self._sids)
+                sess = eng.add_session(sid, req.prompt, req.max_new)
+                if key is not None:
+                    self.keyed[key] = sid
+        except Exception as e:  # noqa: BLE001 - reported to the client
+            self._emit(req, ("error", str(e)))
+            return
+        req.sid = sid
+        self.live[sid] = req
+        self._deliver(req, list(sess.generated))
+
+    def _deliver(self, req: Request, toks: list[int]):
+        for t in toks:
+            if req.n_out >= req.max_new:
+                break
+            req.n_out += 1
+            self._emit(req, ("token", t))
+            if self.metrics:
+                self.metrics["tokens"].inc()
+            if self.eos_id is not None and t == self.eos_id:
+                req.n_out = req.max_new
+                break
+        if req.n_out >= req.max_new:
+            self._finish(req)
+
+    def _finish(self, req: Request):
+        self.live.pop(req.sid, None)
+        eng = self.engine
+        if req.session_key is None:
+            if req.sid in eng.sessions:
+                eng.release(req.sid)
+        else:
+            s = eng.sessions.get(req.sid)
+            if s is not None:
+                self.transcripts[req.session_key] = list(s.prompt) + list(s.generated)
+                s.done = True
+                if hasattr(s, "row") and hasattr(eng, "active"):
+                    eng.active[s.row] = 0  # keep the session's pages, stop decoding it
+        self._emit(req, ("done", None))
+        if self.metrics:
+            self.metrics["latency"].observe(time.perf_counter() - req.t0)
+
+    def _run(self):
+        while True:
+            with self.cv:
+                while not self._stop and not self.pending and not self.live:
+                    self.cv.wait()
+                if self._stop:
+                    return
+                admit = []
+                free = self._free_slots()
+                while self.pending:
+                    req = self.pending[0]
+                    reuse = req.session_key is not None and req.session_key in self.keyed
+                    if not reuse and free <= 0:
+                        break
+                    admit.append(self.pending.popleft())
+                    free -= 0 if reuse else 1
+            for req in admit:
+                self._admit(req)
+            if self.live:
+                t0 = time.perf_counter()
+                out = self.engine.step()
+                if self.metrics:
+                    self.metrics["step"].observe(time.perf_counter() - t0)
+                for sid, toks in out.items():
+                    req = self.live.get(sid)
+                    if req is not None:
+                        self._deliver(req, toks)
+                for sid, req in list(self.live.items()):  # engine-side completion (its own max_new)
+                    s = self.engine.sessions.get(sid)
+                    if s is not None and s.done and req.n_out < req.max_new:
+                        self._finish(req)
+            if self.metrics:
+                self.metrics["active"].set(len(self.live))
+            if not self.live and self.pending and not admit:
+                time.sleep(0.001)  # full: wait for a slot
+
+    def _free_slots(self) -> int:
+        eng = self.engine
+        if hasattr(eng, "free_slots"):
+            return eng.free_slots
+        if hasattr(eng, "free_rows"):
+            return len(eng.free_rows)
+        return 1
+
+
+def _metrics():
+    from prometheus_client import CollectorRegistry, Counter, Gauge, Histogram
+    reg = CollectorRegistry()
+    return reg, {
+        "requests": Counter("afb_requests_total", "HTTP generation requests", ["route"], registry=reg),
+        "tokens": Counter("afb_generated_tokens_total", "tokens sent to clients", registry=reg),
+        "active": Gauge("afb_active_requests", "requests being decoded", registry=reg),
+        "step": Histogram("afb_engine_step_seconds", "engine.step() wall time", registry=reg),
+        "latency": Histogram("afb_request_seconds", "request wall time", registry=reg),
+    }
+
+
+def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200"):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+    tok = tokenizer or ByteTokenizer()
+    registry, metrics = _metrics()
+    loop_ = EngineLoop(engine, getattr(tok, "eos_id", None), metrics)
+    from contextlib import asynccontextmanager
+
+    @asynccontextmanager
+    async def lifespan(_app):
+        yield
+        loop_.shutdown()
+
+    app = FastAPI(title="arc_forge_2026_b200", lifespan=lifespan)
+    app.state.engine_loop = loop_
+
+    async def _generate(prompt, max_new, key=None, extend=None):
+        loop = asyncio.get_running_loop()
+        req = Request(prompt, max_new, loop, asyncio.Queue(), key, extend)
+        loop_.submit(req)
+        while True:
+            kind, val = await req.queue.get()
+            if kind == "error":
+                raise HTTPException(400, val)
+            if kind == "done":
+                return
+            yield val
+
+    async def _collect(gen):
+        return [t async for t in gen]
+
+    def _usage(p, c):
+        return {"prompt_tokens": p, "completion_tokens": c, "total_tokens": p + c}
+
+    def _sse(chunks):
+        async def body():
+            async for c in chunks:
+                yield f"data: {json.dumps(c)}\n\n"
+            yield "data: [DONE]\n\n"
+        return StreamingResponse(body(), media_type="text/event-stream")
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "arc_forge_2026_b200"}]}
+
+    @app.get("/metrics")
+    async def prom():
+        from prometheus_client import generate_latest
+        return PlainTextResponse(generate_latest(registry).decode())
+
+    @app.post("/v1/completions")
+    async def completions(body: dict):
+        metrics["requests"].labels("completions").inc()
+        prompt = body.get("prompt", "")
+        ids = list(prompt) if isinstance(prompt, list) else tok.encode(prompt)
+        max_new = int(body.get("max_tokens", 16))
+        rid = "cmpl-" + uuid.uuid4().hex[:24]
+        if body.get("stream"):
+            async def chunks():
+                async for t in _generate(ids, max_new):
+                    yield {"id": rid, "object": "text_completion", "model": model_name,
+                           "choices": [{"index": 0, "text": tok.decode([t]), "token_ids": [t], "finish_reason": None}]}
+            return _sse(chunks())
+        out = await _collect(_generate(ids, max_new))
+        return {"id": rid, "object": "text_completion", "created": int(time.time()), "model": model_name,
+                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": "length"
+                             if len(out) >= max_new else "stop"}],
+                "usage": _usage(len(ids), len(out))}
+
+    @app.post("/v1/chat/completions")
+    async def chat(body: dict):
+        metrics["requests"].labels("chat").inc()
+        ids = tok.chat(body.get("messages", []))
+        max_new = int(body.get("max_tokens", body.get("max_completion_tokens", 16)))
+        rid = "chatcmpl-" + uuid.uuid4().hex[:24]
+        if body.get("stream"):
+            async def chunks():
+                async for t in _generate(ids, max_new):
+                    yield {"id": rid, "object": "chat.completion.chunk", "model": model_name,
+                           "choices": [{"index": 0, "delta": {"content": tok.decode([t])}, "finish_reason": None}]}
+            return _sse(chunks())
+        out = await _collect(_generate(ids, max_new))
+        return {"id": rid, "object": "chat.completion", "created": int(time.time()), "model": model_name,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},
+                             "finish_reason": "length" if len(out) >= max_new else "stop"}],
+                "usage": _usage(len(ids), len(out))}
+
+    @app.post("/v1/responses")
+    async def responses(body: dict):
+        metrics["requests"].labels("responses").inc()
+        inp = body.get("input", "")
+        msgs = [{"role": "user", "content": inp}] if isinstance(inp, str) else list(inp)
+        key = body.get("session_id")
+        max_new = int(body.get("max_output_tokens", 16))
+        if key is not None and key in loop_.keyed:
+            ext = tok.encode("".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}\n" for m in msgs)
+                             + "<|assistant|>") if isinstance(tok, ByteTokenizer) else tok.chat(msgs)
+            prompt_len = len(loop_.transcripts.get(key, [])) + len(ext)
+            gen = _generate([], max_new, key, ext)
+        else:
+            ids = tok.chat(msgs)
+            prompt_len = len(ids)
+            gen = _generate(ids, max_new, key)
+        out = await _collect(gen)
+        text = tok.decode(out)
+        return {"id": "resp_" + uuid.uuid4().hex[:24], "object": "response", "created_at": int(time.time()),
+                "model": model_name, "status": "completed", "session_id": key,
+                "output": [{"type": "message", "role": "assistant",
+                            "content": [{"type": "output_text", "text": text}]}],
+                "output_text": text,
+                "usage": {"input_tokens": prompt_len, "output_tokens": len(out),
+                          "total_tokens": prompt_len + len(out)}}
+
+    @app.post("/close_session")
+    async def close_session(body: dict):
+        key = body.get("session_id")
+        if key is None:
+            raise HTTPException(400, "session_id is required")
+        return JSONResponse({"session_id": key, "closed": loop_.close_session(key)})
+
+    return app
+
+
+def _build_engine(args):
+    import torch
+    from ..config import ServeConfig, drafter_preset, preset
+    cfg = preset(args.preset)
+    if not args.gpu:
+        from ..models.reference import build_reference
+        from .cpu_engine import CPUEngine
+        return CPUEngine(build_reference(cfg, seed=args.seed), args.sessions, args.max_context), cfg
+    from ..models.drafter import Drafter
+    from ..models.hybrid import HybridModel
+    from .engine import SpecEngine
+    dev = torch.device("cuda", 0)
+    model = HybridModel.random(cfg, dev, seed=args.seed)
+    drafter = Drafter(drafter_preset(args.drafter), cfg.hidden_size, cfg.vocab_size, dev, seed=args.seed + 1)
+    eng = SpecEngine(model, drafter, ServeConfig(spec_k=args.spec_k), args.sessions, args.max_context)
+    return eng, cfg
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="tiny_cpu")
+    ap.add_argument("--gpu", action="store_true", help="native engine on cuda:0 (random-init weights)")
+    ap.add_argument("--drafter", default="tiny")
+    ap.add_argument("--spec-k", dest="spec_k", type=int, default=4)
+    ap.add_argument("--sessions", type=int, default=8)
+    ap.add_argument("--max-context", dest="max_context", type=int, default=4096)
+    ap.add_argument("--tokenizer", default=None, help="local Hugging Face tokenizer directory (default: bytes)")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    args = ap.parse_args(argv)
+    import uvicorn
+    from .tokenizer import HFTokenizer
+    engine, cfg = _build_engine(args)
+    tok = HFTokenizer(args.tokenizer) if args.tokenizer else ByteTokenizer()
+    if not args.tokenizer and cfg.vocab_size < ByteTokenizer.vocab_size:
+        raise SystemExit(f"vocab {cfg.vocab_size} is smaller than the byte tokenizer's {ByteTokenizer.vocab_size}")
+    uvicorn.run(create_app(engine, tok, cfg.name), host=args.host, port=args.port, log_level="info")
+
+
+if __name__ == "__main__":
+    main()
