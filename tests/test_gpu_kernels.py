@@ -141,3 +141,25 @@ def test_router_sort_quant_combine():
     ref = x.float() + torch.sigmoid(logits[:, E:E + 1]) * shared.float() + y.float()[entry_row.long()].view(T, k, H).sum(1)
     assert _rel(out, ref) < 5e-3
     check_status()
+
+
+def test_peer_wait_gives_up_with_status_and_the_context_survives():
+    """A peer flag that nothing raises: the bounded wait returns after ~2 s with the timeout bit set; the device
+    keeps working. A dispatch followed by its own wait (one rank) does not time out."""
+    from arc_forge_2026_b200.parallel.ep import EP_COMBINE, EP_DISPATCH, ExpertParallel
+    check_status()
+    ep = ExpertParallel(1, 0, 8, 256, 2, 4, "cuda")
+    x = torch.randn(8, 256, device="cuda").bfloat16()
+    ids = torch.zeros(8, 2, dtype=torch.int32, device="cuda")
+    w = torch.ones(8, 2, device="cuda")
+    ep.ctx.dispatch(x, 8, ids, w)
+    ep.ctx.wait(EP_DISPATCH)
+    torch.cuda.synchronize()
+    assert check_status() == 0
+    ep.ctx.wait(EP_COMBINE)  # nothing publishes a combine: gives up
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="peer wait timed out"):
+        check_status()
+    y = torch.ones(4, device="cuda")
+    assert float((y * 2).sum()) == 8.0
+    ep.close()
