@@ -75,9 +75,10 @@ __global__ void __launch_bounds__(256, 1)
   const int QR = a.q_per_seq * group;  // query rows of this CTA (<= 64)
   const int seq_len = a.seq_lens[seq];
   const int past = seq_len - a.q_per_seq;
-  const int npages = (seq_len + attn::PAGE - 1) / attn::PAGE;
+  const bool sparse = a.sp_count != nullptr;  // QSA: the block-table row is this sequence's page union
+  const int npages = sparse ? a.sp_count[seq] : (seq_len + attn::PAGE - 1) / attn::PAGE;
   // sliding window: query t sees keys [past + t + 1 - window, past + t]
-  const int kv_lo = a.window > 0 ? max(0, past + 1 - a.window) : 0;
+  const int kv_lo = a.window > 0 && !sparse ? max(0, past + 1 - a.window) : 0;
   const int pbeg = kv_lo / attn::PAGE;
   const int p0 = pbeg + split * a.pages_per_split;
   const int p1 = min(npages, p0 + a.pages_per_split);
@@ -168,7 +169,10 @@ __global__ void __launch_bounds__(256, 1)
         }
       }
       // ---- mask + online softmax (log2 domain)
-      const int kbase = (p0 + i) * attn::PAGE + kh * 32;
+      const size_t ui = (size_t)(a.bt_row ? a.bt_row[seq] : seq) * a.max_pages + p0 + i;  // union entry (sparse)
+      const int kbase = (sparse ? a.sp_lpage[ui] : p0 + i) * attn::PAGE + kh * 32;
+      const uint32_t rmask = sparse ? a.sp_mask[ui] : 0xffffffffu;
+      const bool see0 = (rmask >> min(t0, 31)) & 1u, see1 = (rmask >> min(t1, 31)) & 1u;
       float mx0 = m0, mx1 = m1;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -176,8 +180,10 @@ __global__ void __launch_bounds__(256, 1)
         for (int e = 0; e < 2; ++e) {
           const int key = kbase + j * 8 + (lane & 3) * 2 + e;
           float v0 = sc[j][e] * a.scale_log2, v1 = sc[j][2 + e] * a.scale_log2;
-          if (key >= past + t0 + 1 || r0 >= QR || (a.window > 0 && key < past + t0 + 1 - a.window)) v0 = -INFINITY;
-          if (key >= past + t1 + 1 || r1 >= QR || (a.window > 0 && key < past + t1 + 1 - a.window)) v1 = -INFINITY;
+          if (key >= past + t0 + 1 || r0 >= QR || !see0 || (a.window > 0 && key < past + t0 + 1 - a.window))
+            v0 = -INFINITY;
+          if (key >= past + t1 + 1 || r1 >= QR || !see1 || (a.window > 0 && key < past + t1 + 1 - a.window))
+            v1 = -INFINITY;
           sc[j][e] = v0;
           sc[j][2 + e] = v1;
           mx0 = fmaxf(mx0, v0);

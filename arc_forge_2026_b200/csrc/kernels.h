@@ -44,8 +44,56 @@ struct AttnArgs {
   __nv_bfloat16* out = nullptr;         // [num_tokens, Hq, D]
   float* part_o = nullptr;              // [splits, num_tokens, Hq, D]
   float* part_lse = nullptr;            // [splits, num_tokens, Hq]
+  // QSA sparse mode (all null: dense). block_table rows then hold each sequence's page union (max_pages = union
+  // capacity); sp_count[seq] entries are live, sp_lpage gives each entry's page index in the sequence (key
+  // positions) and sp_mask the bitmask of verify rows that attend to it.
+  const int* sp_count = nullptr;
+  const int* sp_lpage = nullptr;
+  const uint8_t* sp_mask = nullptr;
 };
 int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st);
+
+// qsa.cu: QSA indexer, page selection and union for block-sparse verify attention (block = one 64-token page)
+constexpr int QSA_MAX_LAYERS = 64;
+struct QsaArgs {
+  int Hi = 4, Di = 128, rot = 64;           // index heads, head dim, RoPE dims
+  float eps = 1e-6f;
+  const __nv_bfloat16* q_norm = nullptr;    // [Di] (zero-centred weight: x * (1 + w))
+  const float* cos_t = nullptr;             // [positions, rot/2]
+  const float* sin_t = nullptr;
+  __nv_bfloat16* idx_q = nullptr;           // [tokens, Hi, Di]
+  __nv_bfloat16* idx_raw = nullptr;         // [num_pages * 64, Di] per-token raw index keys (by KV slot)
+  const __nv_bfloat16* idx_key = nullptr;   // [num_pages, Di] pooled keys of finalised pages
+};
+struct QsaSelectArgs {
+  const int* block_table = nullptr;  // [S, max_pages]
+  int max_pages = 0, max_blocks = 0;
+  const int* fin = nullptr;          // [S] finalised pages per session
+  const int* seq_lens = nullptr;     // [S] tokens including this cycle's W verify rows
+  int W = 1, K = 32;
+  int* u_page = nullptr;             // [S, ucap] physical pages of the union
+  int* u_lpage = nullptr;            // [S, ucap] page index in the sequence
+  uint8_t* u_mask = nullptr;         // [S, ucap] rows that attend to the page
+  int* u_count = nullptr;            // [S]
+  int ucap = 0;
+};
+struct QsaFinalizeArgs {
+  const __nv_bfloat16* idx_raw[QSA_MAX_LAYERS] = {};
+  __nv_bfloat16* idx_key[QSA_MAX_LAYERS] = {};
+  const __nv_bfloat16* k_norm[QSA_MAX_LAYERS] = {};
+  const int* block_table = nullptr;  // [S, max_pages]
+  int max_pages = 0;
+  int* fin = nullptr;                // [S] in: finalised so far; out: ctx / 64
+  const int* ctx = nullptr;          // [S] committed tokens
+  const float* cos_t = nullptr;
+  const float* sin_t = nullptr;
+  int rot = 64;
+  float eps = 1e-6f;
+};
+int qsa_prep(const QsaArgs& a, const void* proj, int ld, int T, const int* positions, const int* slots,
+             cudaStream_t st);
+int qsa_finalize(const QsaFinalizeArgs& f, int S, int layers, cudaStream_t st);
+int qsa_select(const QsaArgs& a, const QsaSelectArgs& sa, int S, uint32_t* status, cudaStream_t st);
 
 // gdn.cu
 struct GdnArgs {

@@ -201,7 +201,9 @@ void moe_combine_op(const at::Tensor& y, const at::Tensor& entry_row, int64_t k,
 void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at::Tensor& vcache,
                         const at::Tensor& block_table, const at::Tensor& seq_lens, int64_t q_per_seq, double scale,
                         at::Tensor& out, c10::optional<at::Tensor> gate, int64_t gate_ld, int64_t gate_head_stride,
-                        int64_t splits, int64_t pages_per_split, int64_t window, c10::optional<at::Tensor> bt_row) {
+                        int64_t splits, int64_t pages_per_split, int64_t window, c10::optional<at::Tensor> bt_row,
+                        c10::optional<at::Tensor> sp_count, c10::optional<at::Tensor> sp_lpage,
+                        c10::optional<at::Tensor> sp_mask) {
   AFB_CHECK_DT(q, at::kBFloat16);
   AFB_CHECK_CONTIG(q);
   AFB_CHECK_CONTIG(kcache);
@@ -228,6 +230,18 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
   a.pages_per_split = (int)pages_per_split;
   a.window = (int)window;
   a.bt_row = optr<int>(bt_row);
+  if (sp_count.has_value()) {  // QSA sparse mode: block_table rows are page unions
+    TORCH_CHECK(sp_lpage.has_value() && sp_mask.has_value(), "sparse attention needs sp_count, sp_lpage and sp_mask");
+    AFB_CHECK_DT(sp_count.value(), at::kInt);
+    AFB_CHECK_DT(sp_lpage.value(), at::kInt);
+    AFB_CHECK_DT(sp_mask.value(), at::kByte);
+    TORCH_CHECK(sp_lpage->sizes() == block_table.sizes() && sp_mask->sizes() == block_table.sizes(),
+                "sp_lpage / sp_mask must match the block table");
+    TORCH_CHECK(q_per_seq <= 8 && window == 0, "sparse mode: at most 8 verify rows, no window");
+    a.sp_count = ptr<int>(sp_count.value());
+    a.sp_lpage = ptr<int>(sp_lpage.value());
+    a.sp_mask = ptr<uint8_t>(sp_mask.value());
+  }
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   if (gate.has_value()) {
     a.gate = reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr());
@@ -242,6 +256,84 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
     a.part_lse = ptr<float>(pl);
   }
   check_rc(afb::paged_attention(a, (int)splits, status_ptr(q.get_device()), stream()), "paged_attention");
+}
+
+// QSA (see qsa.cu). proj: projection rows whose columns [idx_off, idx_off + (Hi + 1) * 128) hold the index
+// query heads then the raw index key.
+void qsa_prep_op(const at::Tensor& proj, int64_t idx_off, const at::Tensor& positions, const at::Tensor& slots,
+                 const at::Tensor& q_norm, const at::Tensor& cos_t, const at::Tensor& sin_t, double eps, int64_t Hi,
+                 int64_t rot, at::Tensor& idx_q, at::Tensor& idx_raw) {
+  AFB_CHECK_DT(proj, at::kBFloat16);
+  AFB_CHECK_DT(idx_q, at::kBFloat16);
+  AFB_CHECK_DT(idx_raw, at::kBFloat16);
+  TORCH_CHECK(proj.stride(1) == 1 && idx_off % 4 == 0 && proj.size(1) >= idx_off + (Hi + 1) * 128, "qsa proj");
+  TORCH_CHECK(idx_q.numel() >= proj.size(0) * Hi * 128 && idx_raw.size(-1) == 128, "qsa outputs");
+  afb::QsaArgs a;
+  a.Hi = (int)Hi;
+  a.rot = (int)rot;
+  a.eps = (float)eps;
+  a.q_norm = reinterpret_cast<const __nv_bfloat16*>(q_norm.data_ptr());
+  a.cos_t = ptr<float>(cos_t);
+  a.sin_t = ptr<float>(sin_t);
+  a.idx_q = reinterpret_cast<__nv_bfloat16*>(idx_q.data_ptr());
+  a.idx_raw = reinterpret_cast<__nv_bfloat16*>(idx_raw.data_ptr());
+  const auto* base = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()) + idx_off;
+  check_rc(afb::qsa_prep(a, base, proj.stride(0), proj.size(0), ptr<int>(positions), ptr<int>(slots), stream()),
+           "qsa_prep");
+}
+
+void qsa_select_op(const at::Tensor& idx_q, const at::Tensor& idx_key, const at::Tensor& block_table,
+                   const at::Tensor& fin, const at::Tensor& seq_lens, int64_t W, int64_t K, int64_t Hi,
+                   at::Tensor& u_page, at::Tensor& u_lpage, at::Tensor& u_mask, at::Tensor& u_count) {
+  AFB_CHECK_DT(idx_q, at::kBFloat16);
+  AFB_CHECK_DT(idx_key, at::kBFloat16);
+  AFB_CHECK_DT(block_table, at::kInt);
+  AFB_CHECK_DT(u_mask, at::kByte);
+  const int S = seq_lens.size(0);
+  TORCH_CHECK(idx_q.numel() >= (int64_t)S * W * Hi * 128, "idx_q rows");
+  TORCH_CHECK(u_page.size(0) >= S && u_page.sizes() == u_lpage.sizes() && u_page.sizes() == u_mask.sizes(),
+              "union buffers");
+  afb::QsaArgs a;
+  a.Hi = (int)Hi;
+  a.idx_q = reinterpret_cast<__nv_bfloat16*>(idx_q.data_ptr());
+  a.idx_key = reinterpret_cast<const __nv_bfloat16*>(idx_key.data_ptr());
+  afb::QsaSelectArgs sa;
+  sa.block_table = ptr<int>(block_table);
+  sa.max_pages = block_table.size(1);
+  sa.max_blocks = block_table.size(1);
+  sa.fin = ptr<int>(fin);
+  sa.seq_lens = ptr<int>(seq_lens);
+  sa.W = (int)W;
+  sa.K = (int)K;
+  sa.u_page = ptr<int>(u_page);
+  sa.u_lpage = ptr<int>(u_lpage);
+  sa.u_mask = ptr<uint8_t>(u_mask);
+  sa.u_count = ptr<int>(u_count);
+  sa.ucap = u_page.size(1);
+  check_rc(afb::qsa_select(a, sa, S, status_ptr(idx_q.get_device()), stream()), "qsa_select");
+}
+
+void qsa_finalize_op(const std::vector<at::Tensor>& idx_raw, const std::vector<at::Tensor>& idx_key,
+                     const std::vector<at::Tensor>& k_norm, const at::Tensor& block_table, at::Tensor& fin,
+                     const at::Tensor& ctx, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t rot, double eps) {
+  const int L = idx_raw.size();
+  TORCH_CHECK(L >= 1 && L <= afb::QSA_MAX_LAYERS && (int)idx_key.size() == L && (int)k_norm.size() == L,
+              "qsa_finalize: one raw cache, key cache and norm per layer");
+  afb::QsaFinalizeArgs f;
+  for (int l = 0; l < L; ++l) {
+    f.idx_raw[l] = reinterpret_cast<const __nv_bfloat16*>(idx_raw[l].data_ptr());
+    f.idx_key[l] = reinterpret_cast<__nv_bfloat16*>(idx_key[l].data_ptr());
+    f.k_norm[l] = reinterpret_cast<const __nv_bfloat16*>(k_norm[l].data_ptr());
+  }
+  f.block_table = ptr<int>(block_table);
+  f.max_pages = block_table.size(1);
+  f.fin = ptr<int>(fin);
+  f.ctx = ptr<int>(ctx);
+  f.cos_t = ptr<float>(cos_t);
+  f.sin_t = ptr<float>(sin_t);
+  f.rot = (int)rot;
+  f.eps = (float)eps;
+  check_rc(afb::qsa_finalize(f, fin.size(0), L, stream()), "qsa_finalize");
 }
 
 // GDN decode/verify (see gdn.cu). pend: (pend_in, pend_qk, pend_v, pend_gb) with a leading parity dim of 2.
@@ -487,6 +579,13 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
   m.def("gdn_chunk_scan", &gdn_chunk_scan_op);
-  m.def("paged_attention", &paged_attention_op);
+  m.def("paged_attention", &paged_attention_op, py::arg("q"), py::arg("kcache"), py::arg("vcache"),
+        py::arg("block_table"), py::arg("seq_lens"), py::arg("q_per_seq"), py::arg("scale"), py::arg("out"),
+        py::arg("gate"), py::arg("gate_ld"), py::arg("gate_head_stride"), py::arg("splits"),
+        py::arg("pages_per_split"), py::arg("window"), py::arg("bt_row"), py::arg("sp_count") = py::none(),
+        py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none());
+  m.def("qsa_prep", &qsa_prep_op);
+  m.def("qsa_select", &qsa_select_op);
+  m.def("qsa_finalize", &qsa_finalize_op);
   m.def("embedding", &embedding_op);
 }

@@ -1,0 +1,126 @@
+"""QSA block-sparse verify attention on the native kernels (``csrc/qsa.cu`` + the sparse mode of
+``csrc/attention.cu``), plus fp32 PyTorch oracles of every step.
+
+Block = one 64-token KV page. Per full-attention layer:
+
+* ``qsa_prep`` -- index queries (RMSNorm + RoPE, ``Hi`` heads of 128) for this step's tokens, and each token's raw
+  index key stored at its KV slot;
+* ``qsa_finalize`` -- pooled index keys of pages whose 64 tokens are all committed (mean, RMSNorm, RoPE at the
+  page's first position), once per page;
+* ``qsa_attention`` -- per session: scores of its W verify rows over its finalised pages, top-K per row, the union
+  of the rows' pages plus the local (not yet finalised) pages with a row mask per page, then paged attention over
+  that union (one pass for all rows of the session; GQA rows and the output gate as in the dense kernel).
+
+The reference's QSA (``training/work/qwen38fn_lora/sparse_qsa.py:83-153``) scores 4-token blocks with a 4-head
+128-dim indexer and keeps 512 of them (2,048 tokens); BASELINE config 5 asks for 64-token blocks and top-32 (the
+same 2,048-token budget), which makes a block one page.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ..models.reference import apply_rope
+from ._ext import C
+
+PAGE = 64
+
+
+class QsaWorkspace:
+    """Union buffers for up to ``S`` sessions of ``W`` verify rows and top-``K`` (fixed addresses)."""
+
+    def __init__(self, S: int, W: int, K: int, max_pages: int, Hi: int, device, local_pages: int = 3):
+        dev = torch.device(device)
+        self.ucap = W * K + local_pages
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.u_page = torch.zeros(S, self.ucap, **i32)
+        self.u_lpage = torch.zeros(S, self.ucap, **i32)
+        self.u_mask = torch.zeros(S, self.ucap, dtype=torch.uint8, device=dev)
+        self.u_count = torch.zeros(S, **i32)
+        self.idx_q = torch.zeros(S * W, Hi, 128, dtype=torch.bfloat16, device=dev)
+        self.W, self.K, self.Hi, self.max_pages = W, K, Hi, max_pages
+
+
+def qsa_attention(q, kcache, vcache, block_table, seq_lens, fin, idx_key, ws: QsaWorkspace, out, gate=None,
+                  gate_ld=0, gate_head_stride=0, splits: int = 1):
+    """q [S*W, Hq, D] (already normed / RoPE'd), ws.idx_q filled by ``qsa_prep`` for the same rows."""
+    c = C()
+    S = seq_lens.shape[0]
+    c.qsa_select(ws.idx_q, idx_key, block_table, fin, seq_lens, ws.W, ws.K, ws.Hi, ws.u_page[:S], ws.u_lpage[:S],
+                 ws.u_mask[:S], ws.u_count[:S])
+    D = q.shape[-1]
+    pps = math.ceil(ws.ucap / splits)
+    c.paged_attention(q, kcache, vcache, ws.u_page[:S], seq_lens, ws.W, 1.0 / math.sqrt(D), out, gate, gate_ld,
+                      gate_head_stride, math.ceil(ws.ucap / pps), pps, 0, None, ws.u_count[:S], ws.u_lpage[:S],
+                      ws.u_mask[:S])
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ oracles
+def rms(x, w, eps=1e-6):
+    x = x.float()
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + w.float())
+
+
+def prep_reference(proj_idx, positions, q_norm, cos_t, sin_t, Hi, rot, eps=1e-6):
+    """proj_idx [T, (Hi+1)*128] -> (idx_q [T, Hi, 128] fp32, raw [T, 128] fp32)."""
+    T = proj_idx.shape[0]
+    q = rms(proj_idx[:, :Hi * 128].view(T, Hi, 128), q_norm, eps)
+    half = rot // 2
+    cos, sin = cos_t[positions.long(), :half], sin_t[positions.long(), :half]
+    q = apply_rope(q.unsqueeze(0), cos.unsqueeze(0), sin.unsqueeze(0))[0]
+    return q, proj_idx[:, Hi * 128:(Hi + 1) * 128].float()
+
+
+def pooled_key_reference(raw_page, page_index, k_norm, cos_t, sin_t, rot, eps=1e-6):
+    """raw_page [64, 128] (bf16 values) -> the page's index key (fp32)."""
+    m = raw_page.float().mean(0).bfloat16().float()
+    x = rms(m, k_norm, eps)
+    half = rot // 2
+    pos = torch.tensor([page_index * PAGE])
+    cos, sin = cos_t[pos, :half], sin_t[pos, :half]
+    return apply_rope(x.view(1, 1, 128), cos, sin).view(128)
+
+
+def select_reference(idx_q, keys, fin, seq_len, W, K):
+    """One session: idx_q [W, Hi, 128], keys [F, 128] (finalised pages, logical order) -> per row the sorted list
+    of logical pages it attends (top-K finalised by score, ties to the lower index, plus local pages)."""
+    F = fin
+    last = (seq_len - 1) // PAGE
+    rows = []
+    for r in range(W):
+        pos = seq_len - W + r
+        if F <= K:
+            chosen = list(range(F))
+        else:
+            sc = torch.relu(idx_q[r].float() @ keys[:F].float().t()).sum(0) / math.sqrt(128)
+            # top-K with ties to the lower index: sort by (-score, index)
+            order = sorted(range(F), key=lambda b: (-float(sc[b]), b))
+            chosen = sorted(order[:K])
+        local = [p for p in range(F, last + 1) if pos >= p * PAGE]
+        rows.append(chosen + local)
+    return rows
+
+
+def attention_reference(q, kcache, vcache, bt_row, seq_len, W, rows_pages, gate=None):
+    """One session's W verify rows: q [W, Hq, D]; each row attends to the keys of its pages up to its position."""
+    Hq, D = q.shape[1], q.shape[2]
+    Hkv = kcache.shape[1]
+    g = Hq // Hkv
+    out = torch.zeros(W, Hq, D)
+    for r in range(W):
+        pos = seq_len - W + r
+        toks = [p * PAGE + j for p in rows_pages[r] for j in range(PAGE) if p * PAGE + j <= pos]
+        toks = torch.tensor(toks)
+        pages = bt_row[(toks // PAGE).long()].long()
+        k = kcache[pages, :, (toks % PAGE).long()].float()  # [n, Hkv, D]
+        v = vcache[pages, :, (toks % PAGE).long()].float()
+        for h in range(Hq):
+            s = (k[:, h // g] @ q[r, h].float()) / math.sqrt(D)
+            p = torch.softmax(s, 0)
+            o = p @ v[:, h // g]
+            if gate is not None:
+                o = o * torch.sigmoid(gate[r, h].float())
+            out[r, h] = o
+    return out
