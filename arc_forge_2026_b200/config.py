@@ -76,6 +76,8 @@ class ModelConfig:
             raise ValueError("GDN value heads must be a multiple of key heads")
         if not 1 <= self.num_experts_per_tok <= self.num_experts:
             raise ValueError("invalid top-k")
+        if self.qsa_topk and (self.qsa_block != 64 or self.qsa_indexer_dim != 128 or not 1 <= self.qsa_indexer_heads <= 4):
+            raise ValueError("QSA needs 64-token blocks (one KV page), 128-dim index heads and 1..4 of them")
         rot = self.rotary_dim
         if rot <= 0 or rot % 2:
             raise ValueError("rotary dimension must be positive and even")
@@ -91,6 +93,11 @@ class ModelConfig:
     @property
     def rotary_dim(self) -> int:
         return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
+    def qsa_proj_dim(self) -> int:
+        """Columns the attention projection carries for the QSA indexer (index query heads + raw key), 0 if off."""
+        return (self.qsa_indexer_heads + 1) * self.qsa_indexer_dim if self.qsa_topk else 0
 
     @property
     def gdn_conv_dim(self) -> int:
@@ -149,6 +156,7 @@ class ServeConfig:
     seed: int = 0
     cuda_graphs: bool = True
     temperature: float = 0.0
+    qsa_splits: int = 4  # KV splits of the QSA union (per session: W*K + local pages)
     hisparse: bool = False
     hisparse_hot_blocks: int = 0
     parallel: str = "single"  # single | ep (EP over the world, DP attention)

@@ -27,7 +27,7 @@ void qk_norm_rope_store_op(const at::Tensor& qkv, int64_t Hq, int64_t Hkv, int64
   AFB_CHECK_DT(slots, at::kInt);
   AFB_CHECK_DT(cos_t, at::kFloat);
   const int T = qkv.size(0);
-  TORCH_CHECK(qkv.size(1) == Hq * 2 * D + 2 * Hkv * D, "qkv width");
+  TORCH_CHECK(qkv.size(1) >= Hq * 2 * D + 2 * Hkv * D, "qkv width (extra columns, e.g. the QSA indexer, follow)");
   TORCH_CHECK(qkv.stride(1) == 1, "qkv inner stride");
   const int page_size = kcache.size(2);
   check_rc(afb::qk_norm_rope_store(qkv.data_ptr(), qkv.stride(0), T, Hq, Hkv, D, rot, qw.data_ptr(), kw.data_ptr(),

@@ -25,6 +25,7 @@ from ..ops import C
 from ..ops.attention import PAGE, paged_attention
 from ..ops.gdn import GdnScratch, GdnShape, GdnState, gdn_decode
 from ..ops.moe import Int3ExpertBank, MoEWorkspace, moe_forward, router_weight_with_shared_gate
+from ..ops.qsa import qsa_attention
 from ..parallel.ep import EPMoEWorkspace, moe_forward_ep
 from .reference import HybridMoE, rope_cos_sin
 
@@ -39,6 +40,8 @@ class LayerWeights:
     q_norm: torch.Tensor | None = None
     k_norm: torch.Tensor | None = None
     w_o: torch.Tensor | None = None
+    qsa_q_norm: torch.Tensor | None = None  # QSA indexer norms (w_qkv then also holds the index projection rows)
+    qsa_k_norm: torch.Tensor | None = None
     # GDN
     w_in: torch.Tensor | None = None
     conv_w: torch.Tensor | None = None
@@ -127,7 +130,10 @@ class HybridModel:
                               torch.zeros(H, dtype=torch.bfloat16, device=dev))
             if kind == FULL:
                 D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_kv_heads
-                lw.w_qkv = randn(Hq * 2 * D + 2 * Hkv * D, H)
+                lw.w_qkv = randn(Hq * 2 * D + 2 * Hkv * D + cfg.qsa_proj_dim, H)
+                if cfg.qsa_topk:
+                    lw.qsa_q_norm = torch.zeros(cfg.qsa_indexer_dim, dtype=torch.bfloat16, device=dev)
+                    lw.qsa_k_norm = torch.zeros(cfg.qsa_indexer_dim, dtype=torch.bfloat16, device=dev)
                 lw.q_norm = torch.zeros(D, dtype=torch.bfloat16, device=dev)
                 lw.k_norm = torch.zeros(D, dtype=torch.bfloat16, device=dev)
                 lw.w_o = randn(H, Hq * D)
@@ -216,6 +222,12 @@ class HybridModel:
         return [(torch.zeros(shape, dtype=torch.bfloat16, device=self.device),
                  torch.zeros(shape, dtype=torch.bfloat16, device=self.device)) for _ in range(c.num_attention_layers)]
 
+    def new_qsa_cache(self, num_pages: int):
+        """Per full-attention layer: raw index keys by KV slot [pages*64, 128] and pooled page keys [pages, 128]."""
+        z = dict(dtype=torch.bfloat16, device=self.device)
+        return [(torch.zeros(num_pages * PAGE, self.cfg.qsa_indexer_dim, **z),
+                 torch.zeros(num_pages, self.cfg.qsa_indexer_dim, **z)) for _ in range(self.cfg.num_attention_layers)]
+
     def new_gdn_states(self, slots: int, max_q: int):
         return [GdnState(self.gdn_shape, slots, max_q, self.device) for _ in range(self.cfg.num_gdn_layers)]
 
@@ -223,8 +235,10 @@ class HybridModel:
         return Workspace(self, max_tokens)
 
     # ------------------------------------------------------------------ forward
-    def forward(self, b: StepBatch, kv, gdn, ws: "Workspace", gdn_scratch: GdnScratch | None = None):
-        """Runs the stack over b.ids; returns the final-normed hidden rows [N, H] (a view into the workspace)."""
+    def forward(self, b: StepBatch, kv, gdn, ws: "Workspace", gdn_scratch: GdnScratch | None = None, qsa=None):
+        """Runs the stack over b.ids; returns the final-normed hidden rows [N, H] (a view into the workspace).
+        ``qsa`` (a ``QsaState``): the full-attention layers store index keys and, on verify batches, attend to
+        their QSA page selection instead of the whole context."""
         c, cC = self.cfg, C()
         N, H = b.num_tokens, c.hidden_size
         h = ws.h[:N]
@@ -244,7 +258,15 @@ class HybridModel:
                 attn = ws.attn[:N]
                 row_len = qkv.shape[1]
                 gate = qkv[:, D:]
-                if b.attn_bt_row is not None:
+                if qsa is not None:
+                    raw, key = qsa.cache[ai]
+                    cC.qsa_prep(qkv, Hq * 2 * D + 2 * Hkv * D, b.positions, b.slots, lw.qsa_q_norm, self.rope_cos,
+                                self.rope_sin, c.rms_norm_eps, c.qsa_indexer_heads, c.rotary_dim, qsa.ws.idx_q, raw)
+                if qsa is not None and b.attn_bt_row is None:
+                    qsa_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, qsa.fin, key, qsa.ws,
+                                  attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
+                                  splits=qsa.splits)
+                elif b.attn_bt_row is not None:
                     # prefill: virtual rows of attn_q_per_seq queries; rows past N are padding (scratch)
                     qp = b.attn_q_per_seq
                     nv = b.attn_bt_row.shape[0]
@@ -291,7 +313,7 @@ class Workspace:
         self.h = torch.empty(max_tokens, H, **bf)
         self.y = torch.empty(max_tokens, H, **bf)
         D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_kv_heads
-        self.qkv = torch.empty(max_tokens + 8, Hq * 2 * D + 2 * Hkv * D, **bf)
+        self.qkv = torch.empty(max_tokens + 8, Hq * 2 * D + 2 * Hkv * D + c.qsa_proj_dim, **bf)
         self.q = torch.empty(max_tokens + 8, Hq * D, **bf)
         self.attn = torch.empty(max_tokens + 8, Hq * D, **bf)
         gs = model.gdn_shape

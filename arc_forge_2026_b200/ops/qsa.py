@@ -28,9 +28,11 @@ PAGE = 64
 
 
 class QsaWorkspace:
-    """Union buffers for up to ``S`` sessions of ``W`` verify rows and top-``K`` (fixed addresses)."""
+    """Union buffers for up to ``S`` sessions of ``W`` verify rows and top-``K`` (fixed addresses); ``idx_q`` holds
+    ``q_rows`` index-query rows (prefill chunks write there too)."""
 
-    def __init__(self, S: int, W: int, K: int, max_pages: int, Hi: int, device, local_pages: int = 3):
+    def __init__(self, S: int, W: int, K: int, max_pages: int, Hi: int, device, local_pages: int = 3,
+                 q_rows: int = 0):
         dev = torch.device(device)
         self.ucap = W * K + local_pages
         i32 = dict(dtype=torch.int32, device=dev)
@@ -38,8 +40,27 @@ class QsaWorkspace:
         self.u_lpage = torch.zeros(S, self.ucap, **i32)
         self.u_mask = torch.zeros(S, self.ucap, dtype=torch.uint8, device=dev)
         self.u_count = torch.zeros(S, **i32)
-        self.idx_q = torch.zeros(S * W, Hi, 128, dtype=torch.bfloat16, device=dev)
+        self.idx_q = torch.zeros(max(S * W, q_rows), Hi, 128, dtype=torch.bfloat16, device=dev)
         self.W, self.K, self.Hi, self.max_pages = W, K, Hi, max_pages
+
+
+class QsaState:
+    """What a serving engine keeps for QSA: per-layer index caches, finalised pages per session, the workspace."""
+
+    def __init__(self, model, S: int, W: int, num_pages: int, max_pages: int, q_rows: int, splits: int = 1):
+        c = model.cfg
+        self.cache = model.new_qsa_cache(num_pages)
+        self.fin = torch.zeros(S, dtype=torch.int32, device=model.device)
+        self.ws = QsaWorkspace(S, W, c.qsa_topk, max_pages, c.qsa_indexer_heads, model.device, q_rows=q_rows)
+        self.k_norms = [lw.qsa_k_norm for lw in model.layers if lw.qsa_k_norm is not None]
+        self.model = model
+        self.splits = splits
+
+    def finalize(self, block_table, ctx_len):
+        """Pooled keys for every page whose tokens are all committed (ctx_len), in every QSA layer."""
+        m = self.model
+        C().qsa_finalize([r for r, _ in self.cache], [k for _, k in self.cache], self.k_norms, block_table, self.fin,
+                         ctx_len, m.rope_cos, m.rope_sin, m.cfg.rotary_dim, m.cfg.rms_norm_eps)
 
 
 def qsa_attention(q, kcache, vcache, block_table, seq_lens, fin, idx_key, ws: QsaWorkspace, out, gate=None,

@@ -107,16 +107,22 @@ class SpecEngine:
             self.cond = torch.empty(S, model.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
         self.mode = {"greedy": 0, "rejection": 0, "bernoulli": 1}[scfg.accept_mode]
         self.gdn_scratch = GdnScratch(model.gdn_shape, 1, PREFILL_CHUNK, dev)
+        self.qsa = None
+        if model.cfg.qsa_topk:
+            from ..ops.qsa import QsaState
+            self.qsa = QsaState(model, S, W, num_pages, self.maxp, max(S * W, PREFILL_CHUNK), splits=scfg.qsa_splits)
 
     # ------------------------------------------------------------------ one cycle (device only)
     def _cycle(self, parity: int):
         cC, m = C(), self.model
         S, K, W = self.S, self.K, self.W
+        if self.qsa is not None:  # pooled index keys of the pages the last cycle completed
+            self.qsa.finalize(self.block_table, self.ctx_len)
         cC.build_window(self.anchor, self.drafts if K else None, 0, self.ctx_len, self.block_table, self.win_ids,
                         self.win_pos, self.win_slots, self.attn_len, self.step_ctr, W, 0)
         b = StepBatch(self.win_ids, self.win_pos, self.win_slots, self.block_table, self.attn_len, self.seq_slot,
                       self.n_commit, W, parity, max_pages=self.maxp)
-        hidden = m.forward(b, self.kv, self.gdn, self.ws)
+        hidden = m.forward(b, self.kv, self.gdn, self.ws, qsa=self.qsa)
         logits = self.logits[: S * W]
         m.logits(hidden, out=logits)
         cC.select_tokens(logits, m.cfg.vocab_size, self.tgt_tok, float(self.scfg.temperature), self.scfg.seed,
@@ -208,7 +214,7 @@ class SpecEngine:
                           self.n_commit, T, 0, commit_current=True, max_pages=self.maxp,
                           attn_bt_row=torch.full((nv,), sess.row, dtype=torch.int32, device=dev),
                           attn_seq_lens=vlen, attn_q_per_seq=8)
-            hidden = m.forward(b, self.kv, self.gdn, self.ws, self.gdn_scratch)
+            hidden = m.forward(b, self.kv, self.gdn, self.ws, self.gdn_scratch, qsa=self.qsa)
             if self.drafter is not None:
                 keep = max(0, T - (self.drafter.cfg.window + 64))
                 dslots = (self.d_block_table[sess.row, (pos.long() // PAGE)] * PAGE + pos.long() % PAGE).int()
@@ -221,6 +227,9 @@ class SpecEngine:
         cC.select_tokens(logits, m.cfg.vocab_size, tok, 0.0, 0, None)
         r = sess.row
         self.ctx_len[r] = L
+        if self.qsa is not None:  # the prompt's complete pages get their pooled index keys now
+            self.qsa.fin[r] = 0
+            self.qsa.finalize(self.block_table, self.ctx_len)
         self.anchor[r] = tok[0]
         self.n_commit[r] = 0
         self.active[r] = 1

@@ -30,6 +30,8 @@ import time
 
 BASELINE_TOKS = 2141.0  # reference deployed stack, 128 sessions, DFlash K=4 (paper §8.3, p. 33)
 METRIC = "decode tok/s @128 sessions (8xB200, spec K=4); p50 TPOT; QAD train tok/s"
+QSA_METRIC = "decode tok/s @110 sessions, 64k contexts, QSA top-32 x 64-token blocks (spec K=4)"
+QSA_BASELINE_TOKS = 1461.0  # reference, HiSparse + session cache, 110 sessions (paper Table 10 / section 8.2)
 
 
 def _reference_arm(args):
@@ -132,14 +134,15 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--sessions", type=int, default=128)
+    ap.add_argument("--sessions", type=int, default=None, help="default 128 (serve), 110 (qsa)")
     ap.add_argument("--layers", type=int, default=48)
-    ap.add_argument("--min-ctx", type=int, default=4096)
-    ap.add_argument("--max-ctx", type=int, default=24576)
-    ap.add_argument("--out-tokens", type=int, default=2048)
+    ap.add_argument("--min-ctx", type=int, default=None, help="default 4096 (serve), 65536 (qsa)")
+    ap.add_argument("--max-ctx", type=int, default=None, help="default 24576 (serve), 65536 (qsa)")
+    ap.add_argument("--out-tokens", type=int, default=None, help="default 2048 (serve), 4096 (qsa)")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--mode", default="serve", choices=["serve", "qad"],
-                    help="serve: spec-decode serving (default); qad: QAD training step")
+    ap.add_argument("--mode", default="serve", choices=["serve", "qad", "qsa"],
+                    help="serve: spec-decode serving (default, configs 2+3); qsa: long-context serving with QSA "
+                         "block-sparse attention (config 5); qad: QAD training step (config 4)")
     ap.add_argument("--seq-len", dest="seq_len", type=int, default=16384, help="qad: tokens per sequence")
     ap.add_argument("--global-batch", dest="global_batch", type=int, default=32, help="qad: sequences per step")
     ap.add_argument("--topk", type=int, default=64, help="qad: teacher top-k")
@@ -150,6 +153,11 @@ def main():
         return
     if args.mode == "qad":
         return qad_main(args)
+    qsa = args.mode == "qsa"
+    for k, serve_v, qsa_v in (("sessions", 128, 110), ("min_ctx", 4096, 65536), ("max_ctx", 24576, 65536),
+                              ("out_tokens", 2048, 4096)):
+        if getattr(args, k) is None:
+            setattr(args, k, qsa_v if qsa else serve_v)
     if args.warmup < 3:
         args.warmup = 3
 
@@ -171,7 +179,7 @@ def main():
     from arc_forge_2026_b200.serve.engine import SpecEngine
 
     dev = torch.device("cuda", local)
-    cfg = preset("qwen3next_80b", num_layers=args.layers)
+    cfg = preset("qwen3next_80b", num_layers=args.layers, **(dict(qsa_block=64, qsa_topk=32) if qsa else {}))
     S_total = args.sessions
     S = S_total // world + (1 if rank < S_total % world else 0)
     K = 4
@@ -208,6 +216,11 @@ def main():
         eng.anchor.copy_(torch.randint(0, cfg.vocab_size, (S,), generator=g).int().to(dev))
         eng.drafts.copy_(torch.randint(0, cfg.vocab_size, (S, K), generator=g).int().to(dev))
         eng.active.fill_(1)
+        if eng.qsa is not None:  # indexer state of the synthetic contexts: random raw and pooled keys
+            for raw, key in eng.qsa.cache:
+                raw.normal_(0, 1.0)
+                key.normal_(0, 1.0)
+            eng.qsa.fin.copy_((ctx // PAGE).int().to(dev))
     torch.cuda.synchronize()
     eng.capture()
     check_status()
@@ -286,15 +299,18 @@ def main():
     value = emitted / (ms / 1000.0)
     e2e = e_tokens / (e_ms / 1000.0)
     out = {
-        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": round(value / BASELINE_TOKS, 3), "dtype": "bf16",
-        "data": "synthetic (random-init weights; random tokens; contexts U[4k,24k] as random KV/GDN state)",
+        "metric": QSA_METRIC if qsa else METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": round(value / (QSA_BASELINE_TOKS if qsa else BASELINE_TOKS), 3), "dtype": "bf16",
+        "data": f"synthetic (random-init weights; random tokens; contexts U[{args.min_ctx},{args.max_ctx}] as random "
+                f"KV/GDN/indexer state)",
         "config": {"model": "qwen3next_80b-shaped hybrid MoE, 48L, 320 experts top-10 INT3 g128 + shared; "
                             "8-layer DFlash drafter", "global_batch": S_total, "seq_len": f"U[{args.min_ctx},"
                             f"{args.max_ctx}] context + decode",
                    "parallelism": f"dp{world}-attn+ep{world}" if world > 1 else "dp1",
                    "spec_k": K, "acceptance": "seeded Bernoulli(0.7) per position", "layers": args.layers,
+                   "attention": "QSA top-32 of 64-token blocks (+ local pages)" if qsa else "dense",
                    "l2": "inputs larger than L2 (weights 24 GB, KV > 40 GB streamed every cycle)"},
         "p50_tpot_ms": round(p50, 3) if p50 else None,
         "accepted_per_cycle": round(emitted / (args.steps * S_total), 3),

@@ -78,3 +78,28 @@ def test_bernoulli_acceptance_and_graph_replay():
     per_cycle = emitted / (40 * 8)
     expected = 1 + 0.7 + 0.7**2 + 0.7**3 + 0.7**4
     assert abs(per_cycle - expected) < 0.25, per_cycle
+
+
+def test_qsa_engine_equals_dense_while_all_pages_fit_and_runs_sparse_beyond():
+    cfg = preset("tiny_gpu", qsa_block=64, qsa_topk=4)
+    model = HybridModel.random(cfg, dev, seed=3)
+    with torch.no_grad():
+        model.lm_head.mul_(40.0)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (100, 150)]
+    scfg = ServeConfig(spec_k=0, accept_mode="greedy")
+    dense = SpecEngine(model, None, scfg, 2, 1024)
+    dense.qsa = None
+    out_dense = dense.generate(prompts, 30)
+    sparse = SpecEngine(model, None, scfg, 2, 1024)
+    assert sparse.qsa is not None
+    out_qsa = sparse.generate(prompts, 30)  # <= 3 finalised pages < top-4: QSA selects everything
+    torch.cuda.synchronize()
+    check_status()
+    assert out_qsa == out_dense
+    long_prompt = torch.randint(0, cfg.vocab_size, (700,), generator=g).tolist()  # 10 pages > top-4: sparse
+    out = sparse.generate([long_prompt], 20)
+    torch.cuda.synchronize()
+    check_status()
+    assert len(out[0]) == 20 and all(0 <= t < cfg.vocab_size for t in out[0])
+    assert int(sparse.qsa.fin[0]) >= 10
