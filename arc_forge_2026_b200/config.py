@@ -157,8 +157,9 @@ class ServeConfig:
     cuda_graphs: bool = True
     temperature: float = 0.0
     qsa_splits: int = 4  # KV splits of the QSA union (per session: W*K + local pages)
-    hisparse: bool = False
-    hisparse_hot_blocks: int = 0
+    hisparse: bool = False  # KV history of the QSA layers in pinned host memory (needs QSA)
+    hisparse_hot_blocks: int = 0  # GPU cache slots per session and layer (0: W * qsa_topk + 32)
+    hisparse_fp8: bool = False  # host pool in e4m3 with per-(page, head) scales (half the host memory)
     parallel: str = "single"  # single | ep (EP over the world, DP attention)
     fused_comm: bool = True  # EP dispatch/combine in our peer-memory kernels (False = NCCL baseline)
 

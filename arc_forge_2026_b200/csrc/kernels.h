@@ -63,7 +63,7 @@ struct QsaArgs {
   const float* sin_t = nullptr;
   __nv_bfloat16* idx_q = nullptr;           // [tokens, Hi, Di]
   __nv_bfloat16* idx_raw = nullptr;         // [num_pages * 64, Di] per-token raw index keys (by KV slot)
-  const __nv_bfloat16* idx_key = nullptr;   // [num_pages, Di] pooled keys of finalised pages
+  const __nv_bfloat16* idx_key = nullptr;   // [S * max_pages, Di] pooled keys of finalised pages (session, page)
 };
 struct QsaSelectArgs {
   const int* block_table = nullptr;  // [S, max_pages]
@@ -94,6 +94,35 @@ int qsa_prep(const QsaArgs& a, const void* proj, int ld, int T, const int* posit
              cudaStream_t st);
 int qsa_finalize(const QsaFinalizeArgs& f, int S, int layers, cudaStream_t st);
 int qsa_select(const QsaArgs& a, const QsaSelectArgs& sa, int S, uint32_t* status, cudaStream_t st);
+
+// hisparse.cu: host-memory KV pool with per-session GPU page caches (QSA layers)
+struct HsArgs {
+  int S = 0, max_pages = 0, C = 0, R = 4, Hkv = 0, D = 0;
+  int fp8 = 0;            // host pool in e4m3 with per-(page, head) scales
+  int* cycle = nullptr;   // device cycle counter (stamps of the cache slots)
+};
+struct HsLayer {
+  uint8_t* gpu_k = nullptr;   // GPU page pool of the layer, bf16 [pages, Hkv, 64, D]
+  uint8_t* gpu_v = nullptr;
+  uint8_t* host_k = nullptr;  // device pointer of the mapped host pool [S * max_pages] pages (bf16 or e4m3)
+  uint8_t* host_v = nullptr;
+  float* host_sk = nullptr;   // e4m3 scales [S * max_pages, Hkv]
+  float* host_sv = nullptr;
+  int* res = nullptr;         // [S, max_pages] cache slot of each page, -1 if not resident
+  int* slot_page = nullptr;   // [S, C] page held by each slot, -1 if empty
+  int* stamp = nullptr;       // [S, C] cycle of last use, -1 if never
+  __nv_bfloat16* raw = nullptr;  // optional raw index-key cache [pages * 64, 128] (moved with ring pages)
+};
+struct HsLayers {
+  HsLayer l[QSA_MAX_LAYERS];
+};
+int hs_cycle_start(const HsArgs& a, int* block_table, const int* ctx, int W, cudaStream_t st);
+int hs_writeback(const HsArgs& a, const HsLayers& Ls, int layers, const int* block_table, const int* fin,
+                 const int* ctx, cudaStream_t st);
+int hs_after_prefill(const HsArgs& a, const HsLayers& Ls, int layers, const int* block_table, int s, int p0, int p1,
+                     int p2, cudaStream_t st);
+int hs_fetch(const HsArgs& a, const HsLayer& L, int* u_page, const int* u_lpage, const int* u_count, int ucap,
+             const int* fin, uint32_t* status, cudaStream_t st);
 
 // gdn.cu
 struct GdnArgs {

@@ -336,6 +336,60 @@ void qsa_finalize_op(const std::vector<at::Tensor>& idx_raw, const std::vector<a
   check_rc(afb::qsa_finalize(f, fin.size(0), L, stream()), "qsa_finalize");
 }
 
+// HiSparse (see hisparse.cu): the host pools, GPU pools and residency tables of every QSA layer.
+struct HsCtx {
+  afb::HsArgs a;
+  afb::HsLayers L;
+  int layers = 0;
+  // per layer: (gpu_k, gpu_v, host_k, host_v, host_sk, host_sv, res, slot_page, stamp, raw) as raw addresses (0 = none)
+  HsCtx(int64_t S, int64_t max_pages, int64_t C, int64_t R, int64_t Hkv, int64_t D, bool fp8, const at::Tensor& cycle,
+        const std::vector<std::vector<int64_t>>& ptrs) {
+    TORCH_CHECK(ptrs.size() >= 1 && ptrs.size() <= afb::QSA_MAX_LAYERS, "HsCtx: 1..64 layers");
+    AFB_CHECK_DT(cycle, at::kInt);
+    a.S = (int)S;
+    a.max_pages = (int)max_pages;
+    a.C = (int)C;
+    a.R = (int)R;
+    a.Hkv = (int)Hkv;
+    a.D = (int)D;
+    a.fp8 = fp8 ? 1 : 0;
+    a.cycle = ptr<int>(cycle);
+    layers = (int)ptrs.size();
+    for (int l = 0; l < layers; ++l) {
+      TORCH_CHECK(ptrs[l].size() == 10, "HsCtx: 10 addresses per layer");
+      auto u8 = [&](int i) { return reinterpret_cast<uint8_t*>((uintptr_t)ptrs[l][i]); };
+      L.l[l].gpu_k = u8(0);
+      L.l[l].gpu_v = u8(1);
+      L.l[l].host_k = u8(2);
+      L.l[l].host_v = u8(3);
+      L.l[l].host_sk = reinterpret_cast<float*>(u8(4));
+      L.l[l].host_sv = reinterpret_cast<float*>(u8(5));
+      L.l[l].res = reinterpret_cast<int*>(u8(6));
+      L.l[l].slot_page = reinterpret_cast<int*>(u8(7));
+      L.l[l].stamp = reinterpret_cast<int*>(u8(8));
+      L.l[l].raw = reinterpret_cast<__nv_bfloat16*>(u8(9));
+    }
+  }
+  void cycle_start(at::Tensor& block_table, const at::Tensor& ctx, int64_t W) {
+    check_rc(afb::hs_cycle_start(a, ptr<int>(block_table), ptr<int>(ctx), (int)W, stream()), "hs_cycle_start");
+  }
+  void writeback(const at::Tensor& block_table, const at::Tensor& fin, const at::Tensor& ctx) {
+    check_rc(afb::hs_writeback(a, L, layers, ptr<int>(block_table), ptr<int>(fin), ptr<int>(ctx), stream()),
+             "hs_writeback");
+  }
+  void after_prefill(const at::Tensor& block_table, int64_t s, int64_t p0, int64_t p1, int64_t p2) {
+    check_rc(afb::hs_after_prefill(a, L, layers, ptr<int>(block_table), (int)s, (int)p0, (int)p1, (int)p2, stream()),
+             "hs_after_prefill");
+  }
+  void fetch(int64_t layer, at::Tensor& u_page, const at::Tensor& u_lpage, const at::Tensor& u_count,
+             const at::Tensor& fin) {
+    TORCH_CHECK(layer >= 0 && layer < layers, "hs fetch: layer");
+    check_rc(afb::hs_fetch(a, L.l[layer], ptr<int>(u_page), ptr<int>(u_lpage), ptr<int>(u_count), u_page.size(1),
+                           ptr<int>(fin), status_ptr(u_page.get_device()), stream()),
+             "hs_fetch");
+  }
+};
+
 // GDN decode/verify (see gdn.cu). pend: (pend_in, pend_qk, pend_v, pend_gb) with a leading parity dim of 2.
 void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const at::Tensor& conv_w,
                    at::Tensor& conv_state, at::Tensor& ssm_state, at::Tensor& pend_in, at::Tensor& pend_qk,
@@ -585,6 +639,13 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("pages_per_split"), py::arg("window"), py::arg("bt_row"), py::arg("sp_count") = py::none(),
         py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none());
   m.def("qsa_prep", &qsa_prep_op);
+  py::class_<HsCtx>(m, "HsCtx")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, bool, const at::Tensor&,
+                    const std::vector<std::vector<int64_t>>&>())
+      .def("cycle_start", &HsCtx::cycle_start)
+      .def("writeback", &HsCtx::writeback)
+      .def("after_prefill", &HsCtx::after_prefill)
+      .def("fetch", &HsCtx::fetch);
   m.def("qsa_select", &qsa_select_op);
   m.def("qsa_finalize", &qsa_finalize_op);
   m.def("embedding", &embedding_op);

@@ -3,7 +3,8 @@
 // Semantics (the reference's QSA, training/work/qwen38fn_lora/sparse_qsa.py:83-153, with the block equal to one
 // 64-token KV page so a selected block is exactly one page to fetch):
 //   index query  q[t, h]  = RoPE_t(RMSNorm_q(x_t W_iq,h))                         (Hi heads of Di dims)
-//   index key    k[b]     = RoPE_{64 b}(RMSNorm_k(mean_{j<64} x_{64b+j} W_ik))     (one key per finalised page)
+//   index key    k[b]     = RoPE_{64 b}(RMSNorm_k(mean_{j<64} x_{64b+j} W_ik))     (one key per finalised page,
+//                                                                             stored by (session row, page index))
 //   score[t, b] = sum_h relu(q[t,h] . k[b]) / sqrt(Di)
 //   a verify row attends to the top-K finalised pages by score (all of them when there are <= K) plus the
 //   "local" pages from the first non-finalised page through its own position (causal inside).
@@ -115,7 +116,7 @@ __global__ void qsa_finalize_kernel(QsaFinalizeArgs f) {
       const float cs = f.cos_t[(size_t)pos * half + fi], sn = f.sin_t[(size_t)pos * half + fi];
       o = d < half ? x * cs - buf[d + half] * sn : x * cs + buf[d - half] * sn;
     }
-    key[(size_t)page * qsa::DI + d] = __float2bfloat16(o);
+    key[((size_t)s * f.max_pages + p) * qsa::DI + d] = __float2bfloat16(o);
     __syncthreads();  // red / buf are reused by the next page
   }
 }
@@ -165,7 +166,7 @@ __global__ void __launch_bounds__(qsa::THREADS) qsa_select_kernel(QsaArgs a, Qsa
     __syncthreads();
     const float rs = rsqrtf((float)qsa::DI);
     for (int b = tid; b < F; b += blockDim.x) {
-      const uint4* kr = reinterpret_cast<const uint4*>(a.idx_key + (size_t)bt[b] * qsa::DI);
+      const uint4* kr = reinterpret_cast<const uint4*>(a.idx_key + ((size_t)s * sa.max_pages + b) * qsa::DI);
       float acc[qsa::MAXW * qsa::MAXH];
 #pragma unroll
       for (int i = 0; i < qsa::MAXW * qsa::MAXH; ++i) acc[i] = 0.f;

@@ -87,9 +87,44 @@ class SymmHeap {
   std::vector<int64_t> peers_;
 };
 
+// Pinned, device-mapped host memory of an exact size (the torch pinned allocator rounds large blocks up to a power
+// of two, which for a ~100 GB KV pool would double the host memory). Kernels read and write it through
+// device_ptr(); the host sees it as a uint8 tensor.
+class HostPool {
+ public:
+  explicit HostPool(int64_t bytes) : bytes_(bytes) {
+    if (bytes <= 0) throw std::invalid_argument("HostPool: size must be positive");
+    check(cudaHostAlloc(&host_, (size_t)bytes, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc");
+    check(cudaHostGetDevicePointer(&dev_, host_, 0), "cudaHostGetDevicePointer");
+  }
+  ~HostPool() { close(); }
+  void close() {
+    if (host_) cudaFreeHost(host_);
+    host_ = nullptr;
+    dev_ = nullptr;
+  }
+  int64_t device_ptr() const { return (int64_t)(uintptr_t)dev_; }
+  int64_t bytes() const { return bytes_; }
+  at::Tensor tensor() const {
+    if (!host_) throw std::runtime_error("HostPool: closed");
+    return torch::from_blob(host_, {bytes_}, [](void*) {}, torch::TensorOptions().dtype(torch::kUInt8));
+  }
+
+ private:
+  int64_t bytes_;
+  void* host_ = nullptr;
+  void* dev_ = nullptr;
+};
+
 }  // namespace
 
 void register_symm(pybind11::module& m) {
+  pybind11::class_<HostPool>(m, "HostPool")
+      .def(pybind11::init<int64_t>(), pybind11::arg("bytes"))
+      .def("device_ptr", &HostPool::device_ptr)
+      .def("tensor", &HostPool::tensor)
+      .def("close", &HostPool::close)
+      .def_property_readonly("bytes", &HostPool::bytes);
   pybind11::class_<SymmHeap>(m, "SymmHeap")
       .def(pybind11::init<int64_t, int64_t, int64_t, int64_t>(), pybind11::arg("bytes"), pybind11::arg("rank"),
            pybind11::arg("world"), pybind11::arg("device"))

@@ -222,11 +222,13 @@ class HybridModel:
         return [(torch.zeros(shape, dtype=torch.bfloat16, device=self.device),
                  torch.zeros(shape, dtype=torch.bfloat16, device=self.device)) for _ in range(c.num_attention_layers)]
 
-    def new_qsa_cache(self, num_pages: int):
-        """Per full-attention layer: raw index keys by KV slot [pages*64, 128] and pooled page keys [pages, 128]."""
+    def new_qsa_cache(self, num_pages: int, sessions: int, max_pages: int):
+        """Per full-attention layer: raw index keys by KV slot [pages*64, 128] and pooled page keys by (session
+        row, page index) [sessions * max_pages, 128]."""
         z = dict(dtype=torch.bfloat16, device=self.device)
         return [(torch.zeros(num_pages * PAGE, self.cfg.qsa_indexer_dim, **z),
-                 torch.zeros(num_pages, self.cfg.qsa_indexer_dim, **z)) for _ in range(self.cfg.num_attention_layers)]
+                 torch.zeros(sessions * max_pages, self.cfg.qsa_indexer_dim, **z))
+                for _ in range(self.cfg.num_attention_layers)]
 
     def new_gdn_states(self, slots: int, max_q: int):
         return [GdnState(self.gdn_shape, slots, max_q, self.device) for _ in range(self.cfg.num_gdn_layers)]
@@ -265,7 +267,7 @@ class HybridModel:
                 if qsa is not None and b.attn_bt_row is None:
                     qsa_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, qsa.fin, key, qsa.ws,
                                   attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
-                                  splits=qsa.splits)
+                                  splits=qsa.splits, hs=qsa.hs, layer=ai)
                 elif b.attn_bt_row is not None:
                     # prefill: virtual rows of attn_q_per_seq queries; rows past N are padding (scratch)
                     qp = b.attn_q_per_seq

@@ -49,12 +49,13 @@ class QsaState:
 
     def __init__(self, model, S: int, W: int, num_pages: int, max_pages: int, q_rows: int, splits: int = 1):
         c = model.cfg
-        self.cache = model.new_qsa_cache(num_pages)
+        self.cache = model.new_qsa_cache(num_pages, S, max_pages)
         self.fin = torch.zeros(S, dtype=torch.int32, device=model.device)
         self.ws = QsaWorkspace(S, W, c.qsa_topk, max_pages, c.qsa_indexer_heads, model.device, q_rows=q_rows)
         self.k_norms = [lw.qsa_k_norm for lw in model.layers if lw.qsa_k_norm is not None]
         self.model = model
         self.splits = splits
+        self.hs = None  # HiSparseState when the KV history lives in host memory
 
     def finalize(self, block_table, ctx_len):
         """Pooled keys for every page whose tokens are all committed (ctx_len), in every QSA layer."""
@@ -64,12 +65,15 @@ class QsaState:
 
 
 def qsa_attention(q, kcache, vcache, block_table, seq_lens, fin, idx_key, ws: QsaWorkspace, out, gate=None,
-                  gate_ld=0, gate_head_stride=0, splits: int = 1):
-    """q [S*W, Hq, D] (already normed / RoPE'd), ws.idx_q filled by ``qsa_prep`` for the same rows."""
+                  gate_ld=0, gate_head_stride=0, splits: int = 1, hs=None, layer: int = 0):
+    """q [S*W, Hq, D] (already normed / RoPE'd), ws.idx_q filled by ``qsa_prep`` for the same rows. With ``hs``
+    (a ``HiSparseState``) the selected finalised pages are first made resident from the host pool."""
     c = C()
     S = seq_lens.shape[0]
     c.qsa_select(ws.idx_q, idx_key, block_table, fin, seq_lens, ws.W, ws.K, ws.Hi, ws.u_page[:S], ws.u_lpage[:S],
                  ws.u_mask[:S], ws.u_count[:S])
+    if hs is not None:
+        hs.ctx.fetch(layer, ws.u_page, ws.u_lpage, ws.u_count, fin)
     D = q.shape[-1]
     pps = math.ceil(ws.ucap / splits)
     c.paged_attention(q, kcache, vcache, ws.u_page[:S], seq_lens, ws.W, 1.0 / math.sqrt(D), out, gate, gate_ld,

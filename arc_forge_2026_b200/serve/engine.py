@@ -54,6 +54,13 @@ class SpecEngine:
         W = self.W = K + 1
         self.max_context = max_context
         self.maxp = math.ceil((max_context + 2 * W + 8) / PAGE)
+        self.hs_slots = 0
+        if scfg.hisparse:  # GPU pages: per-session caches and rings, prefill staging, scratch (the host holds history)
+            if not model.cfg.qsa_topk:
+                raise ValueError("HiSparse offload needs QSA attention (cfg.qsa_topk > 0)")
+            from ..ops.hisparse import gpu_pages
+            self.hs_slots = scfg.hisparse_hot_blocks or W * model.cfg.qsa_topk + 32
+            num_pages = gpu_pages(S, self.maxp, self.hs_slots, 4) - 1
         num_pages = (num_pages or S * self.maxp) + 1
         # the last page is a scratch sink: rows without a session point at it, so their (ignored) window
         # writes never land in another session's pages
@@ -111,11 +118,19 @@ class SpecEngine:
         if model.cfg.qsa_topk:
             from ..ops.qsa import QsaState
             self.qsa = QsaState(model, S, W, num_pages, self.maxp, max(S * W, PREFILL_CHUNK), splits=scfg.qsa_splits)
+        self.hs = None
+        if scfg.hisparse:
+            from ..ops.hisparse import HiSparseState
+            self.hs = HiSparseState(self.kv, self.qsa.cache, S, self.maxp, self.hs_slots, 4, fp8=scfg.hisparse_fp8)
+            self.qsa.hs = self.hs
 
     # ------------------------------------------------------------------ one cycle (device only)
     def _cycle(self, parity: int):
         cC, m = C(), self.model
         S, K, W = self.S, self.K, self.W
+        if self.hs is not None:  # ring pages for this window; pages the last cycle completed go to the host pool
+            self.hs.ctx.cycle_start(self.block_table, self.ctx_len, W)
+            self.hs.ctx.writeback(self.block_table, self.qsa.fin, self.ctx_len)
         if self.qsa is not None:  # pooled index keys of the pages the last cycle completed
             self.qsa.finalize(self.block_table, self.ctx_len)
         cC.build_window(self.anchor, self.drafts if K else None, 0, self.ctx_len, self.block_table, self.win_ids,
@@ -184,8 +199,12 @@ class SpecEngine:
         row = self.free_rows.pop(0)
         sess = Session(sid, row, list(prompt), max_new_tokens)
         self.sessions[sid] = sess
-        self.alloc.ensure(sid, len(prompt) + 2 * self.W + 8)
-        self._sync_pages([row])
+        if self.hs is not None:  # the prompt is prefilled into the staging pages
+            self.bt_host[row] = torch.arange(self.hs.staging_base, self.hs.staging_base + self.maxp, dtype=torch.int32)
+            self.block_table[row].copy_(self.bt_host[row])
+        else:
+            self.alloc.ensure(sid, len(prompt) + 2 * self.W + 8)
+            self._sync_pages([row])
         self._prefill(sess)
         return sess
 
@@ -198,7 +217,8 @@ class SpecEngine:
         dev = self.device
         L = len(sess.prompt)
         ids_all = torch.tensor(sess.prompt, dtype=torch.int32, device=dev)
-        pages = torch.tensor(self.alloc.pages(sess.sid), dtype=torch.int64, device=dev)
+        pages = (self.block_table[sess.row].long() if self.hs is not None else
+                 torch.tensor(self.alloc.pages(sess.sid), dtype=torch.int64, device=dev))
         slot_row = torch.tensor([sess.row], dtype=torch.int32, device=dev)
         for st in self.gdn:  # fresh recurrent state for this row
             st.conv[sess.row].zero_()
@@ -230,6 +250,14 @@ class SpecEngine:
         if self.qsa is not None:  # the prompt's complete pages get their pooled index keys now
             self.qsa.fin[r] = 0
             self.qsa.finalize(self.block_table, self.ctx_len)
+        if self.hs is not None:  # complete pages -> host pool, the partial page -> its ring page
+            full, part = L // PAGE, L % PAGE
+            self.hs.ctx.after_prefill(self.block_table, r, 0, full, full + (1 if part else 0))
+            self.bt_host[r] = self.scratch_page
+            if part:
+                self.bt_host[r, full] = self.hs.ring_page(r, full)
+            self.block_table[r].copy_(self.bt_host[r])
+            self.hs.reset_session(r)
         self.anchor[r] = tok[0]
         self.n_commit[r] = 0
         self.active[r] = 1
@@ -240,15 +268,19 @@ class SpecEngine:
     def release(self, sid: int):
         sess = self.sessions.pop(sid)
         self.active[sess.row] = 0
-        self.alloc.release(sid)
+        if self.hs is None:
+            self.alloc.release(sid)
         self.bt_host[sess.row] = self.scratch_page
+        if self.hs is not None:
+            self.block_table[sess.row].copy_(self.bt_host[sess.row])
         self.free_rows.append(sess.row)
 
     def step(self) -> dict[int, list[int]]:
         """One cycle for every session + host bookkeeping; returns the tokens emitted per session."""
-        for s in self.sessions.values():  # pages for this cycle's window (at most W new tokens)
-            self.alloc.ensure(s.sid, len(s.prompt) + len(s.generated) + 2 * self.W + 8)
-        self._sync_pages()
+        if self.hs is None:  # pages for this cycle's window (at most W new tokens); HiSparse maps them on device
+            for s in self.sessions.values():
+                self.alloc.ensure(s.sid, len(s.prompt) + len(s.generated) + 2 * self.W + 8)
+            self._sync_pages()
         self.run_cycle()
         self.out_host.copy_(self.out_tokens, non_blocking=True)
         self.cnt_host.copy_(self.out_count, non_blocking=True)

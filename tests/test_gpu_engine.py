@@ -103,3 +103,28 @@ def test_qsa_engine_equals_dense_while_all_pages_fit_and_runs_sparse_beyond():
     check_status()
     assert len(out[0]) == 20 and all(0 <= t < cfg.vocab_size for t in out[0])
     assert int(sparse.qsa.fin[0]) >= 10
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_hisparse_offload_equals_on_device_qsa(fp8):
+    """Same QSA engine with the KV history in pinned host memory (bf16: exact; e4m3 pool: runs, close)."""
+    cfg = preset("tiny_gpu", qsa_block=64, qsa_topk=2)
+    model = HybridModel.random(cfg, dev, seed=4)
+    with torch.no_grad():
+        model.lm_head.mul_(40.0)
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (700, 450)]
+    base = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy"), 2, 1024)
+    out_base = base.generate(prompts, 80)  # crosses page boundaries: write-back and fetch both run
+    off = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy", hisparse=True, hisparse_fp8=fp8,
+                                              hisparse_hot_blocks=4), 2, 1024)
+    out_off = off.generate(prompts, 80)
+    torch.cuda.synchronize()
+    check_status()
+    assert int(off.hs.cycle.item()) >= 79  # the first token comes from the prefill
+    if not fp8:
+        assert out_off == out_base
+    else:
+        agree = sum(a == b for x, y in zip(out_off, out_base) for a, b in zip(x, y)) / (2 * 80)
+        assert agree > 0.5
+    off.hs.close()
