@@ -147,6 +147,9 @@ def main():
     ap.add_argument("--global-batch", dest="global_batch", type=int, default=32, help="qad: sequences per step")
     ap.add_argument("--topk", type=int, default=64, help="qad: teacher top-k")
     ap.add_argument("--census", action="store_true", help="print the kernel-time shares of one step (stderr)")
+    ap.add_argument("--hisparse", action="store_true", help="qsa: KV history in pinned host memory (HiSparse)")
+    ap.add_argument("--hisparse-fp8", dest="hisparse_fp8", action="store_true",
+                    help="qsa: host pool in e4m3 with per-(page, head) scales")
     args = ap.parse_args()
     if args.impl == "reference":
         _reference_arm(args)
@@ -187,7 +190,8 @@ def main():
     if world > 1:  # attention/GDN data-parallel over sessions, routed experts split over the ranks
         model.enable_expert_parallel(world, rank, T_cap=S * (K + 1))
     drafter = Drafter(drafter_preset("dflash_8l"), cfg.hidden_size, cfg.vocab_size, dev, seed=args.seed + 1)
-    scfg = ServeConfig(spec_k=K, accept_mode="bernoulli", accept_prob=0.7, seed=args.seed + 7 * rank)
+    scfg = ServeConfig(spec_k=K, accept_mode="bernoulli", accept_prob=0.7, seed=args.seed + 7 * rank,
+                       hisparse=bool(qsa and args.hisparse), hisparse_fp8=bool(args.hisparse_fp8))
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
     ctx = torch.randint(args.min_ctx, args.max_ctx + 1, (S,), generator=g)
     need_pages = int(sum((int(c) + args.out_tokens + 2 * (K + 1) + 8 + PAGE - 1) // PAGE for c in ctx))
@@ -210,8 +214,21 @@ def main():
             sess = Session(i, i, [0] * int(ctx[i]), 10**9)
             eng.sessions[i] = sess
             eng.free_rows.remove(i)
-            eng.alloc.ensure(i, int(ctx[i]) + args.out_tokens + 2 * (K + 1) + 8)
-        eng._sync_pages()
+            if eng.hs is None:
+                eng.alloc.ensure(i, int(ctx[i]) + args.out_tokens + 2 * (K + 1) + 8)
+        if eng.hs is None:
+            eng._sync_pages()
+        else:  # host pools: random valid values (e4m3 or bf16 of N(0, 1)), written in chunks from the device
+            for hk, hv in eng.hs.host_tensors():
+                for host in (hk, hv):
+                    step = 1 << 28
+                    for o in range(0, host.numel(), step):
+                        n = min(step, host.numel() - o)
+                        if args.hisparse_fp8:
+                            src = torch.randn(n, device=dev).to(torch.float8_e4m3fn).view(torch.uint8)
+                        else:
+                            src = torch.randn(n // 2, device=dev).bfloat16().view(torch.uint8)
+                        host[o:o + n].copy_(src)
         eng.ctx_len.copy_(ctx.int().to(dev))
         eng.anchor.copy_(torch.randint(0, cfg.vocab_size, (S,), generator=g).int().to(dev))
         eng.drafts.copy_(torch.randint(0, cfg.vocab_size, (S, K), generator=g).int().to(dev))
@@ -311,6 +328,8 @@ def main():
                    "parallelism": f"dp{world}-attn+ep{world}" if world > 1 else "dp1",
                    "spec_k": K, "acceptance": "seeded Bernoulli(0.7) per position", "layers": args.layers,
                    "attention": "QSA top-32 of 64-token blocks (+ local pages)" if qsa else "dense",
+                   "kv_offload": ("HiSparse host pool " + ("e4m3" if args.hisparse_fp8 else "bf16"))
+                   if scfg.hisparse else "none (all KV on the GPU)",
                    "l2": "inputs larger than L2 (weights 24 GB, KV > 40 GB streamed every cycle)"},
         "p50_tpot_ms": round(p50, 3) if p50 else None,
         "accepted_per_cycle": round(emitted / (args.steps * S_total), 3),
