@@ -229,11 +229,32 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
               dst[dq] = dq < SW_WORDS ? reinterpret_cast<const uint32_t*>(st + L::SW_OFF)[dq]
                                       : reinterpret_cast<const uint32_t*>(st + L::SX_OFF)[dq - SW_WORDS];
           }
-#pragma unroll 2
-          for (int task = dq; task < TASKS; task += NT) {
-            const int t = task >> 9, r = (task >> 2) & 127, sq = task & 3;
-            dequant_task(reinterpret_cast<const uint32_t*>(st + L::C_OFF + t * moe::CODE_TILE) + r * 12,
-                         at + t * moe::A_TILE, r, sq);
+          {  // all code words of this thread's tasks are loaded first (independent loads in flight), then decoded
+            constexpr int PER = (TASKS + NT - 1) / NT;
+            uint32_t w[PER][3];
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+              const int task = dq + i * NT;
+              if (task < TASKS) {
+                const int t = task >> 9, r = (task >> 2) & 127, sq = task & 3;
+                const uint32_t* rw = reinterpret_cast<const uint32_t*>(st + L::C_OFF + t * moe::CODE_TILE) + r * 12;
+                w[i][0] = rw[3 * sq];
+                w[i][1] = rw[3 * sq + 1];
+                w[i][2] = rw[3 * sq + 2];
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+              const int task = dq + i * NT;
+              if (task < TASKS) {
+                const int t = task >> 9, r = (task >> 2) & 127, sq = task & 3;
+                uint32_t o[8];
+                decode32(w[i][0], w[i][1], w[i][2], o);
+                uint8_t* tile = at + t * moe::A_TILE;
+                *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * sq)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * sq + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+              }
+            }
           }
           fence_proxy_async_smem();  // generic-proxy smem writes -> visible to the tensor core
           __syncwarp();
