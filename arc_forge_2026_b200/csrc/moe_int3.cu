@@ -307,6 +307,19 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
         for (int i = 0; i < NH; ++i) acc0[i] = 0.f;
 #pragma unroll
         for (int i = 0; i < (PAIR ? NH : 1); ++i) acc1[i] = 0.f;
+        // w2: the chunk's entry indices and routing weights are fetched now, as independent loads, so they are in
+        // registers when the K loop ends (fetched inside the store loop they were a chain of dependent misses)
+        int ent[PAIR ? 1 : NH];
+        float rwt[PAIR ? 1 : NH];
+        if constexpr (!PAIR) {
+#pragma unroll
+          for (int i = 0; i < NH; ++i) {
+            const int row = crow + half * NH + i;
+            ent[i] = (half * NH + i < cn && args.row_entry) ? args.row_entry[row] : -1;
+          }
+#pragma unroll
+          for (int i = 0; i < NH; ++i) rwt[i] = args.route_w ? (ent[i] >= 0 ? args.route_w[ent[i]] : 0.f) : 1.f;
+        }
         for (int g = 0; g < KG; ++g, ++kstep) {
           const int b = kstep % NBUF;
           const uint32_t ph = (kstep / NBUF) & 1;
@@ -363,17 +376,16 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
 #pragma unroll
           for (int i = 0; i < NH; ++i) {
             if (t0 + i >= cn) break;
-            const int entry = args.row_entry ? args.row_entry[crow + t0 + i] : 0;  // -1: segment padding
+            const int entry = ent[PAIR ? 0 : i];  // -1: segment padding
             if (args.ep_world > 0) {
               if (entry < 0) continue;
               const int dst = entry / args.ep_entries_per_rank, le = entry - dst * args.ep_entries_per_rank;
               reinterpret_cast<__nv_bfloat16*>(args.ep_peer[dst] + args.ep_off_comb)[(size_t)le * args.out_ld + col] =
-                  __float2bfloat16(acc0[i] * args.route_w[entry]);
+                  __float2bfloat16(acc0[i] * rwt[PAIR ? 0 : i]);
               continue;
             }
-            const float w = args.route_w ? (entry >= 0 ? args.route_w[entry] : 0.f) : 1.f;
             reinterpret_cast<__nv_bfloat16*>(args.out_bf16)[(size_t)(crow + t0 + i) * args.out_ld + col] =
-                __float2bfloat16(acc0[i] * w);
+                __float2bfloat16(acc0[i] * rwt[PAIR ? 0 : i]);
           }
         }
       }
