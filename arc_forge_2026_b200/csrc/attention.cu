@@ -53,7 +53,9 @@ struct AttnSmem {
   static constexpr uint32_t STAGE = 2 * KV_BYTES;
   static constexpr uint32_t Q_OFF = 2 * STAGE;
   static constexpr uint32_t BAR_OFF = Q_OFF + Q_BYTES;
-  static constexpr uint32_t TOTAL = BAR_OFF + 64 + 1024;
+  static constexpr int SBT = 1024;                             // block-table entries staged in shared memory
+  static constexpr uint32_t SBT_OFF = BAR_OFF + 64;
+  static constexpr uint32_t TOTAL = SBT_OFF + SBT * 4 + 1024;
 };
 
 template <int D>
@@ -92,6 +94,9 @@ __global__ void __launch_bounds__(256, 1)
     }
     fence_mbar_init();
   }
+  // this split's page ids, staged once: the TMA issue of each page then needs no global load on its path
+  int* sbt = reinterpret_cast<int*>(smem + S::SBT_OFF);
+  for (int i = threadIdx.x; i < min(n, S::SBT); i += blockDim.x) sbt[i] = bt[p0 + i];
   // Q rows -> smem (swizzled); rows >= QR are zero
   for (int idx = threadIdx.x; idx < 64 * (D / 8); idx += blockDim.x) {
     const int r = idx / (D / 8), cc = idx % (D / 8);
@@ -108,7 +113,7 @@ __global__ void __launch_bounds__(256, 1)
 
   auto issue = [&](int i) {
     const int s = i & 1;
-    const int page = bt[p0 + i];
+    const int page = i < S::SBT ? sbt[i] : bt[p0 + i];
     const int row = (page * a.Hkv + kvh) * attn::PAGE;
     uint8_t* st = smem + s * S::STAGE;
     mbar_arrive_expect_tx(&full[s], 2 * S::KV_BYTES);
