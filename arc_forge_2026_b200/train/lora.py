@@ -1,0 +1,128 @@
+"""LoRA adapters for RL / SFT on the QAD student, and the merged export serving loads.
+
+Adapters sit on the dense projections (attention q/k/v/o, GDN in_proj_qkvz / in_proj_ba / out_proj): the frozen
+base output (block-FP8 QAT weight where the deployed model runs FP8) plus ``scale * (x A^T) B^T`` computed in fp32,
+``scale = alpha / r`` (the reference's LoRABF16, ``training/work/qwen38fn_lora/trainer_kernels.py:167-213``).
+
+Merged export, ``fn-lora-merged-v2`` (the reference's ``merged_export.py:1-40``)::
+
+    <dir>/model.safetensors      merged adapted projections only, under the model's keys:
+                                 FP8-served ones as e4m3 ``<key>`` + fp32 ``<key minus .weight>.weight_scale_inv``
+                                 [N/128, K/128], the rest bf16
+    <dir>/merged_manifest.json   format, weight_version, lora rank / alpha / scale, per-tensor sha256 of base and
+                                 merged bytes, changed-element counts
+    <dir>/DONE                   written last; <dir>.tmp -> <dir> rename before it
+
+Merge: ``(W + scale * B @ A)`` in fp32 from the original base, rounded once (so rounding never compounds across
+publishes).
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+import os
+from pathlib import Path
+
+import torch
+from torch import nn
+
+from ..quant.fp8 import quantize_weight_block
+
+FORMAT = "fn-lora-merged-v2"
+FP8_PROJ = ("q_proj", "k_proj", "v_proj", "in_proj_qkvz", "out_proj")
+DEFAULT_TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "in_proj_qkvz", "in_proj_ba", "out_proj")
+
+
+class LoRAAdapter(nn.Module):
+    def __init__(self, in_features: int, out_features: int, r: int, alpha: float, device, generator=None):
+        super().__init__()
+        self.r, self.alpha, self.scale = r, alpha, alpha / r
+        self.A = nn.Parameter(torch.randn(r, in_features, generator=generator, device=device) / math.sqrt(in_features))
+        self.B = nn.Parameter(torch.zeros(out_features, r, device=device))
+
+    def forward(self, x):
+        return ((x.float() @ self.A.t()) @ self.B.t()) * self.scale
+
+    def delta(self) -> torch.Tensor:
+        return (self.B.float() @ self.A.float()) * self.scale
+
+
+def attach_lora(student, r: int = 16, alpha: float = 32.0, targets=DEFAULT_TARGETS, seed: int = 0):
+    """Freeze every student parameter and attach adapters to the ``targets`` projections of every layer.
+    Returns the adapter parameters (the only trainable ones)."""
+    for p in student.parameters():
+        p.requires_grad_(False)
+    g = torch.Generator(device=next(student.parameters()).device).manual_seed(seed)
+    params = []
+    for layer in student.layers:
+        for name in targets:
+            w = getattr(layer, name, None)
+            if w is None:
+                continue
+            ad = LoRAAdapter(w.shape[1], w.shape[0], r, alpha, w.device, g)
+            layer.lora[name] = ad
+            params += [ad.A, ad.B]
+    return params
+
+
+def lora_state(student) -> dict[str, torch.Tensor]:
+    return {f"layers.{i}.{n}.{k}": getattr(ad, k).detach().cpu()
+            for i, layer in enumerate(student.layers) for n, ad in layer.lora.items() for k in ("A", "B")}
+
+
+def load_lora_state(student, state: dict[str, torch.Tensor]):
+    with torch.no_grad():
+        for i, layer in enumerate(student.layers):
+            for n, ad in layer.lora.items():
+                ad.A.copy_(state[f"layers.{i}.{n}.A"])
+                ad.B.copy_(state[f"layers.{i}.{n}.B"])
+
+
+def _sha(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def merged_tensors(student, key_prefix: str = "model.layers") -> tuple[dict, dict]:
+    """{package key: tensor} of the merged adapted projections and a manifest entry per tensor."""
+    out, info = {}, {}
+    for i, layer in enumerate(student.layers):
+        for name, ad in layer.lora.items():
+            base = getattr(layer, name).detach().float().cpu()
+            merged = (base + ad.delta().detach().float().cpu()).to(torch.bfloat16)
+            key = f"{key_prefix}.{i}.{name}.weight"
+            base_b = base.to(torch.bfloat16)
+            if name in FP8_PROJ:
+                q, s = quantize_weight_block(merged.float())
+                out[key], out[key[: -len(".weight")] + ".weight_scale_inv"] = q, s
+                stored = q
+            else:
+                out[key] = merged
+                stored = merged
+            info[key] = {"sha256_base": _sha(base_b), "sha256_merged": _sha(stored),
+                         "changed": int((merged != base_b).sum()), "dtype": str(stored.dtype)}
+    return out, info
+
+
+def export_merged(student, out_dir, weight_version: int, meta: dict | None = None) -> Path:
+    from safetensors.torch import save_file
+    target = Path(out_dir)
+    tmp = target.with_name(target.name + ".tmp")
+    if target.exists() or tmp.exists():
+        raise FileExistsError(target)
+    tmp.mkdir(parents=True)
+    tensors, info = merged_tensors(student)
+    save_file(tensors, str(tmp / "model.safetensors"))
+    from safetensors.torch import load_file
+    back = load_file(str(tmp / "model.safetensors"))  # read back bitwise before publishing
+    for k, t in tensors.items():
+        if not torch.equal(back[k].view(torch.uint8), t.contiguous().view(torch.uint8)):
+            raise RuntimeError(f"read-back mismatch for {k}")
+    ads = [ad for layer in student.layers for ad in layer.lora.values()]
+    manifest = {"format": FORMAT, "weight_version": weight_version, "fp8_format": "fp8_e4m3_block128",
+                "lora_rank": ads[0].r if ads else None, "lora_alpha": ads[0].alpha if ads else None,
+                "scale": ads[0].scale if ads else None, "tensors": info, **(meta or {})}
+    (tmp / "merged_manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+    os.replace(tmp, target)
+    (target / "DONE").write_text("")
+    return target

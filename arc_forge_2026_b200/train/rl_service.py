@@ -1,0 +1,227 @@
+"""RL trainer service: HTTP-driven optimizer steps on the student with LoRA adapters (the reference's
+``training/work/qwen38fn_lora/train_rl_service.py:1-61``).
+
+Rank 0 serves HTTP; each request becomes one command that every rank executes (the command is broadcast over a
+gloo group with ``broadcast_object_list``, so the GPU process group carries only gradients). Routes:
+
+    GET  /health                       {ok, step, weight_version, busy}
+    POST /train   {batch | batch_path, algo?, clip?, cap?}
+                                       one optimizer step: forward, per-token log-probabilities under logits / T,
+                                       BPO (clipped ratio) or MIS (truncated importance weight) loss, backward into
+                                       the adapters, gradients averaged over ranks, global-norm clip, AdamW
+    POST /publish {weight_version}     merged adapters -> <out>/merged/v<version:06d> (``fn-lora-merged-v2``); versions
+                                       must increase
+    POST /save                         <out>/checkpoint-<step>/ (adapters + optimizer state + step), via .tmp rename
+    POST /stop
+
+Batch (``batch`` inline or a ``torch.save`` file at ``batch_path``): ``ids`` [B, T] int64 input tokens, ``labels``
+[B, T] int64 next tokens, ``mask`` [B, T] (1 = trained), ``advantages`` [B, T] or [B], ``behavior_logp`` [B, T]
+(the sampler's log-probabilities), optional ``temperature`` (default 1.0) and ``routing`` [B*T, layers, top_k]
+(routing replay, forced).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import threading
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+from ..parallel.shard_optim import average_gradients
+from .lora import attach_lora, export_merged, load_lora_state, lora_state
+from .losses import bpo_loss, mis_loss, selective_logprob
+from .optim import AdamWBF16, clip_grad_norm_
+from .routing_replay import RoutingReplay
+
+
+class RLTrainer:
+    def __init__(self, student, out_dir, lr: float = 2e-5, r: int = 16, alpha: float = 32.0, max_norm: float = 1.0,
+                 group=None):
+        self.student = student
+        self.out = Path(out_dir)
+        self.params = attach_lora(student, r, alpha)
+        self.opt = AdamWBF16([{"params": self.params, "lr": lr}])
+        self.max_norm = max_norm
+        self.group = group
+        self.step = 0
+        self.weight_version = 0
+        self.replay = None
+        self.busy = False
+
+    def _batch(self, cmd):
+        if "batch_path" in cmd:
+            return torch.load(cmd["batch_path"], map_location="cpu", weights_only=False)
+        return {k: torch.tensor(v) if isinstance(v, list) else v for k, v in cmd["batch"].items()}
+
+    def train(self, cmd: dict) -> dict:
+        b = self._batch(cmd)
+        dev = self.student.embed.device
+        ids, labels = b["ids"].long().to(dev), b["labels"].long().to(dev)
+        mask = b["mask"].float().to(dev).reshape(-1)
+        adv = b["advantages"].float().to(dev)
+        if adv.dim() == 1:
+            adv = adv[:, None].expand_as(ids)
+        adv = adv.reshape(-1)
+        beh = b["behavior_logp"].float().to(dev).reshape(-1)
+        T = float(b.get("temperature", 1.0))
+        if "routing" in b:
+            if self.replay is None:
+                c = self.student.cfg
+                self.replay = RoutingReplay("force", len(self.student.layers), c.num_experts_per_tok)
+                self.replay.install(self.student)
+            self.replay.set_routing(b["routing"].long())
+        t0 = time.perf_counter()
+        self.opt.zero_grad(set_to_none=True)
+        h = self.student.hidden(ids).reshape(ids.numel(), -1)
+        logp, ent = selective_logprob(h, self.student.lm_head, labels.reshape(-1), T)
+        algo = cmd.get("algo", "bpo")
+        if algo == "bpo":
+            loss = bpo_loss(logp, beh, adv, mask, clip=tuple(cmd.get("clip", (0.2, 0.28))))
+        elif algo == "mis":
+            loss = mis_loss(logp, beh, adv, mask, cap=float(cmd.get("cap", 2.0)))
+        else:
+            raise ValueError(f"unknown RL loss {algo!r}")
+        loss.backward()
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            average_gradients(self.params, self.group)
+        norm = clip_grad_norm_(self.params, self.max_norm)
+        self.opt.step()
+        self.step += 1
+        with torch.no_grad():
+            ratio = torch.exp(logp.detach() - beh)
+            m = mask > 0
+            report = {"step": self.step, "loss": float(loss.detach()), "grad_norm": float(norm),
+                      "tokens": int(m.sum()), "ratio_mean": float(ratio[m].mean()) if m.any() else None,
+                      "entropy": float(ent.detach()[m].mean()) if m.any() else None,
+                      "seconds": round(time.perf_counter() - t0, 4)}
+            if self.replay is not None:
+                st = self.replay.stats
+                report["routing_equal_frac"] = sum(st["equal"]) / max(1, sum(st["rows"]))
+        return report
+
+    def publish(self, cmd: dict) -> dict:
+        v = int(cmd["weight_version"])
+        if v <= self.weight_version:
+            raise ValueError(f"weight_version {v} must exceed the last published {self.weight_version}")
+        path = export_merged(self.student, self.out / "merged" / f"v{v:06d}", v, {"optimizer_step": self.step})
+        self.weight_version = v
+        return {"path": str(path), "weight_version": v}
+
+    def save(self, cmd: dict) -> dict:
+        target = self.out / f"checkpoint-{self.step}"
+        tmp = target.with_name(target.name + ".tmp")
+        tmp.mkdir(parents=True, exist_ok=False)
+        torch.save({"lora": lora_state(self.student), "opt": self.opt.state_dict(), "step": self.step,
+                    "weight_version": self.weight_version}, tmp / "trainer_state.pt")
+        os.replace(tmp, target)
+        return {"path": str(target)}
+
+    def load(self, path):
+        st = torch.load(Path(path) / "trainer_state.pt", map_location="cpu", weights_only=False)
+        load_lora_state(self.student, st["lora"])
+        self.opt.load_state_dict(st["opt"])
+        self.step, self.weight_version = st["step"], st["weight_version"]
+
+    def execute(self, cmd: dict) -> dict:
+        """Run one command on this rank (every rank runs the same commands in the same order)."""
+        op = cmd["op"]
+        if op == "train":
+            return self.train(cmd)
+        if op == "publish":
+            return self.publish(cmd) if not dist.is_initialized() or dist.get_rank() == 0 else {}
+        if op == "save":
+            return self.save(cmd) if not dist.is_initialized() or dist.get_rank() == 0 else {}
+        raise ValueError(f"unknown command {op!r}")
+
+
+def create_app(trainer: RLTrainer, control_group=None):
+    """Rank 0's HTTP front; with ``control_group`` (gloo) every command is broadcast to the other ranks first."""
+    from fastapi import FastAPI, HTTPException
+
+    app = FastAPI(title="arc_forge_2026_b200 RL trainer")
+    lock = threading.Lock()
+
+    def run(cmd):
+        with lock:
+            trainer.busy = True
+            try:
+                if control_group is not None:
+                    dist.broadcast_object_list([cmd], src=0, group=control_group)
+                return trainer.execute(cmd)
+            except Exception as e:  # noqa: BLE001
+                raise HTTPException(500, f"{type(e).__name__}: {e}") from e
+            finally:
+                trainer.busy = False
+
+    @app.get("/health")
+    def health():
+        return {"ok": True, "step": trainer.step, "weight_version": trainer.weight_version, "busy": trainer.busy}
+
+    @app.post("/train")
+    def train(body: dict):
+        return run({"op": "train", **body})
+
+    @app.post("/publish")
+    def publish(body: dict):
+        return run({"op": "publish", **body})
+
+    @app.post("/save")
+    def save(body: dict | None = None):
+        return run({"op": "save"})
+
+    return app
+
+
+def follower_loop(trainer: RLTrainer, control_group):
+    """Ranks > 0: execute the commands rank 0 broadcasts until a stop command."""
+    while True:
+        box = [None]
+        dist.broadcast_object_list(box, src=0, group=control_group)
+        cmd = box[0]
+        if cmd is None or cmd.get("op") == "stop":
+            return
+        trainer.execute(cmd)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="tiny_cpu")
+    ap.add_argument("--out", type=Path, required=True)
+    ap.add_argument("--lr", type=float, default=2e-5)
+    ap.add_argument("--lora-rank", dest="lora_rank", type=int, default=16)
+    ap.add_argument("--lora-alpha", dest="lora_alpha", type=float, default=32.0)
+    ap.add_argument("--port", type=int, default=8100)
+    ap.add_argument("--resume", type=Path)
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args(argv)
+    from ..config import preset
+    from .student import random_student
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))) if torch.cuda.is_available() else "cpu"
+    control = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
+                                timeout=datetime.timedelta(seconds=600))
+        control = dist.new_group(backend="gloo")
+    student = random_student(preset(args.preset), dev, seed=args.seed)
+    trainer = RLTrainer(student, args.out, args.lr, args.lora_rank, args.lora_alpha)
+    if args.resume:
+        trainer.load(args.resume)
+    if rank != 0:
+        follower_loop(trainer, control)
+        return
+    import uvicorn
+    args.out.mkdir(parents=True, exist_ok=True)
+    (args.out / "trainer_endpoint.json").write_text(json.dumps({"host": "127.0.0.1", "port": args.port}) + "\n")
+    uvicorn.run(create_app(trainer, control), host="127.0.0.1", port=args.port, log_level="info")
+    if control is not None:
+        dist.broadcast_object_list([{"op": "stop"}], src=0, group=control)
+
+
+if __name__ == "__main__":
+    main()

@@ -88,12 +88,17 @@ class StudentMoE(nn.Module):
         self.shared_w13 = _master(torch.cat([shared_gate, shared_up]))
         self.shared_down = _master(shared_down)
         self.shared_expert_gate = _master(shared_expert_gate)
+        self.replay = None  # (RoutingReplay, layer index) when the rollout's expert choices are forced
 
     def forward(self, x):
         c = self.cfg
         T, H = x.shape
         logits = x.float() @ self.router.t()
-        w, ids = R.route(logits, c.num_experts_per_tok, c.norm_topk_prob)
+        if self.replay is not None:
+            rep, index = self.replay
+            w, ids = rep.route(index, logits, c.num_experts_per_tok, c.norm_topk_prob)
+        else:
+            w, ids = R.route(logits, c.num_experts_per_tok, c.norm_topk_prob)
         K = c.num_experts_per_tok
         flat = ids.flatten()
         order = torch.argsort(flat, stable=True)  # (token, k) entries sorted by expert
@@ -185,6 +190,15 @@ class StudentLayer(nn.Module):
                 buf(n)
         self.moe = StudentMoE(cfg, t["router"], t["w13_codes"], t["w13_scales"], t["w2_codes"], t["w2_scales"],
                               t["shared_gate"], t["shared_up"], t["shared_down"], t["shared_expert_gate"])
+        self.lora = nn.ModuleDict()  # optional adapters by projection name (train/lora.py)
+
+    def _lin(self, name: str, x, fp8: bool):
+        """x @ W^T for projection ``name`` (block-FP8 QAT weight when ``fp8``), plus its LoRA adapter if attached."""
+        w = getattr(self, name)
+        y = F.linear(x, (fp8_weight(w) if fp8 else w).to(x.dtype))
+        if name in self.lora:
+            y = y + self.lora[name](x).to(y.dtype)
+        return y
 
     def groups(self):
         g = {k: [] for k in GROUPS}
@@ -202,22 +216,22 @@ class StudentLayer(nn.Module):
     def _attn(self, x, B, T):
         c = self.cfg
         D = c.head_dim
-        qg = F.linear(x, fp8_weight(self.q_proj).to(x.dtype)).view(B, T, c.num_attention_heads, 2 * D)
+        qg = self._lin("q_proj", x, True).view(B, T, c.num_attention_heads, 2 * D)
         q, gate = qg[..., :D], qg[..., D:].reshape(B, T, -1)
-        k = F.linear(x, fp8_weight(self.k_proj).to(x.dtype)).view(B, T, c.num_kv_heads, D)
-        v = F.linear(x, fp8_weight(self.v_proj).to(x.dtype)).view(B, T, c.num_kv_heads, D)
+        k = self._lin("k_proj", x, True).view(B, T, c.num_kv_heads, D)
+        v = self._lin("v_proj", x, True).view(B, T, c.num_kv_heads, D)
         q, k = R.rms_norm(q, self.q_norm, c.rms_norm_eps), R.rms_norm(k, self.k_norm, c.rms_norm_eps)
         cos, sin = R.rope_cos_sin(torch.arange(T, device=x.device), c.rotary_dim, c.rope_theta)
         q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
         o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
                                            enable_gqa=True).transpose(1, 2).reshape(B, T, -1)
         o = o * torch.sigmoid(gate.float()).to(o.dtype)
-        return F.linear(o, self.o_proj.to(o.dtype))
+        return self._lin("o_proj", o, False)
 
     def _gdn(self, x, B, T):
         c = self.cfg
-        qkvz = F.linear(x, fp8_weight(self.in_proj_qkvz).to(x.dtype))
-        ba = F.linear(x, self.in_proj_ba.to(x.dtype))
+        qkvz = self._lin("in_proj_qkvz", x, True)
+        ba = self._lin("in_proj_ba", x, False)
         mixed, z = qkvz[..., : c.gdn_conv_dim], qkvz[..., c.gdn_conv_dim:]
         b, a = ba[..., : c.linear_num_value_heads], ba[..., c.linear_num_value_heads:]
         mixed, _ = R.causal_conv1d(mixed, self.conv1d)
@@ -231,7 +245,7 @@ class StudentLayer(nn.Module):
         g, beta = R.gdn_gates(b, a, self.A_log, self.dt_bias)
         o, _ = chunk_gated_delta_rule(q, k, v, g, beta)
         o = R.gated_rms_norm(o.to(x.dtype), z.reshape(B, T, c.linear_num_value_heads, -1), self.g_norm, c.rms_norm_eps)
-        return F.linear(o.reshape(B, T, -1), fp8_weight(self.out_proj).to(o.dtype))
+        return self._lin("out_proj", o.reshape(B, T, -1), True)
 
     def forward(self, x):
         c = self.cfg
