@@ -1,0 +1,137 @@
+"""DFlash drafter training: a differentiable PyTorch twin of the serving drafter (``models/drafter.py``, same
+parameters and math), trained on target hidden states, and its export into the serving drafter.
+
+Per training sequence (tokens x[0..T), the target's hidden states h[0..T) -- h[t] after reading x[t]) and a set of
+anchor positions a:
+
+* context K/V of every layer come from the fusions ``f_t = E[x_t] + fc(h_t)`` through the layer's ``ctx_norm`` and
+  k/v projections (injected context: no trunk pass over the context);
+* the block at anchor a is ``[x_a, mask, ..., mask]`` (K slots at positions a..a+K-1), each slot plus
+  ``fc(h_{a-1})``; it runs through the layers attending to the context keys before a inside the window and
+  causally to the block's own earlier slots (gated attention, q/k RMSNorm, full-dim RoPE);
+* slot i predicts x[a+i+1] over the draft vocabulary.
+
+Objectives (the reference's ``training/work/qwen38fn_dflash/objective.py``): ``ce`` (next-token cross-entropy on
+every slot) and, with teacher logits, ``kl`` (forward KL to the target's distribution restricted to the draft
+vocabulary), mixed by ``kl_weight``.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ..config import DrafterConfig
+from ..models.reference import apply_rope, rms_norm, rope_cos_sin
+
+
+class DrafterTrain(nn.Module):
+    def __init__(self, cfg: DrafterConfig, target_hidden: int, vocab_size: int, draft_vocab: torch.Tensor,
+                 device="cpu", seed: int = 0, std: float = 0.02):
+        super().__init__()
+        self.cfg = cfg
+        g = torch.Generator(device=device).manual_seed(seed)
+        H, D, Hq, Hkv, I = cfg.hidden_size, cfg.head_dim, cfg.num_attention_heads, cfg.num_kv_heads, cfg.intermediate_size
+
+        def p(*shape):
+            return nn.Parameter(torch.randn(*shape, generator=g, device=device) * std)
+
+        def z(*shape):
+            return nn.Parameter(torch.zeros(*shape, device=device))
+        self.vocab_size, self.mask_id = vocab_size, vocab_size
+        self.embed = p(vocab_size + 1, H)
+        self.fc = p(H, target_hidden)
+        self.layers = nn.ModuleList()
+        for _ in range(cfg.num_layers):
+            m = nn.Module()
+            m.in_norm, m.ctx_norm, m.post_norm = z(H), z(H), z(H)
+            m.w_qkv = p(Hq * 2 * D + 2 * Hkv * D, H)
+            m.q_norm, m.k_norm = z(D), z(D)
+            m.w_o, m.w13, m.w2 = p(H, Hq * D), p(2 * I, H), p(H, I)
+            self.layers.append(m)
+        self.final_norm = z(H)
+        self.register_buffer("draft_vocab", draft_vocab.long().to(device))
+        self.lm_head = p(len(draft_vocab), H)
+        to_draft = torch.full((vocab_size,), -1, dtype=torch.long)
+        to_draft[draft_vocab.long().cpu()] = torch.arange(len(draft_vocab))
+        self.register_buffer("to_draft", to_draft.to(device))
+
+    def _rope(self, x, pos):
+        cos, sin = rope_cos_sin(pos, self.cfg.head_dim, self.cfg.rope_theta)
+        return apply_rope(x, cos, sin)
+
+    def block_logits(self, tokens: torch.Tensor, hidden: torch.Tensor, anchors: torch.Tensor) -> torch.Tensor:
+        """tokens [T], hidden [T, Ht], anchors [A] (1 <= a, a + K <= T - 1) -> draft-vocab logits [A, K, Vd]."""
+        c = self.cfg
+        K, D, Hq, Hkv = c.k, c.head_dim, c.num_attention_heads, c.num_kv_heads
+        T, A = tokens.shape[0], anchors.shape[0]
+        dev = tokens.device
+        fus = self.embed[tokens] + hidden.float() @ self.fc.t()                      # [T, H]
+        blk_ids = torch.full((A, K), self.mask_id, dtype=torch.long, device=dev)
+        blk_ids[:, 0] = tokens[anchors]
+        x = self.embed[blk_ids] + (hidden[anchors - 1].float() @ self.fc.t())[:, None]  # [A, K, H]
+        pos_b = anchors[:, None] + torch.arange(K, device=dev)[None]                  # [A, K]
+        pos_c = torch.arange(T, device=dev)
+        # visibility: context key p for block row (a, i) if p < a and p > a + i - window; block key (a, j) if j <= i
+        qpos = pos_b.reshape(-1)
+        ctx_ok = (pos_c[None] < anchors.repeat_interleave(K)[:, None]) & (pos_c[None] > qpos[:, None] - c.window)
+        same = torch.arange(A, device=dev).repeat_interleave(K)
+        blk_ok = (same[:, None] == same[None]) & (torch.arange(K, device=dev).repeat(A)[None] <=
+                                                  torch.arange(K, device=dev).repeat(A)[:, None])
+        mask = torch.cat([ctx_ok, blk_ok], 1)                                         # [A*K, T + A*K]
+        for m in self.layers:
+            kv_c = rms_norm(fus, m.ctx_norm, c.rms_norm_eps) @ m.w_qkv[Hq * 2 * D:].t()
+            kc = rms_norm(kv_c[:, :Hkv * D].view(T, Hkv, D), m.k_norm, c.rms_norm_eps)
+            kc = self._rope(kc.unsqueeze(0), pos_c[None])[0]
+            vc = kv_c[:, Hkv * D:].view(T, Hkv, D)
+            y = rms_norm(x, m.in_norm, c.rms_norm_eps).reshape(A * K, -1)
+            qkv = y @ m.w_qkv.t()
+            qg = qkv[:, :Hq * 2 * D].view(A * K, Hq, 2 * D)
+            q, gate = qg[..., :D], qg[..., D:]
+            kb = qkv[:, Hq * 2 * D:Hq * 2 * D + Hkv * D].view(A * K, Hkv, D)
+            vb = qkv[:, Hq * 2 * D + Hkv * D:].view(A * K, Hkv, D)
+            q = self._rope(rms_norm(q, m.q_norm, c.rms_norm_eps).unsqueeze(0), qpos[None])[0]
+            kb = self._rope(rms_norm(kb, m.k_norm, c.rms_norm_eps).unsqueeze(0), qpos[None])[0]
+            keys = torch.cat([kc, kb], 0).repeat_interleave(Hq // Hkv, 1)            # [T + A*K, Hq, D]
+            vals = torch.cat([vc, vb], 0).repeat_interleave(Hq // Hkv, 1)
+            s = torch.einsum("qhd,khd->hqk", q.float(), keys.float()) / math.sqrt(D)
+            s = s.masked_fill(~mask[None], float("-inf"))
+            o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vals.float())
+            o = (o * torch.sigmoid(gate.float())).reshape(A * K, Hq * D)
+            x = x + (o @ m.w_o.t()).view(A, K, -1)
+            y = rms_norm(x, m.post_norm, c.rms_norm_eps)
+            gu = y @ m.w13.t()
+            I = c.intermediate_size
+            x = x + (F.silu(gu[..., :I]) * gu[..., I:]) @ m.w2.t()
+        return rms_norm(x, self.final_norm, c.rms_norm_eps) @ self.lm_head.t()
+
+    def loss(self, tokens, hidden, anchors, teacher_logits=None, kl_weight: float = 0.0):
+        """Mean CE of every slot's next token (tokens outside the draft vocabulary are skipped), plus
+        ``kl_weight`` x forward KL to ``teacher_logits`` [T, V] of the target at the predicted positions."""
+        K = self.cfg.k
+        logits = self.block_logits(tokens, hidden, anchors)                           # [A, K, Vd]
+        tgt_pos = anchors[:, None] + 1 + torch.arange(K, device=tokens.device)[None]
+        tgt = self.to_draft[tokens[tgt_pos]]
+        ce = F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), tgt.reshape(-1), ignore_index=-1)
+        if teacher_logits is None or kl_weight == 0:
+            return ce
+        # the target's logits that predict position a+i+1 are those read at a+i
+        t = teacher_logits[tgt_pos - 1][..., self.draft_vocab].float()
+        kl = F.kl_div(torch.log_softmax(logits.float(), -1), torch.log_softmax(t, -1), log_target=True,
+                      reduction="batchmean")
+        return ce + kl_weight * kl
+
+    @torch.no_grad()
+    def export_to(self, drafter):
+        """Copy the trained weights (bf16) into a serving ``models.drafter.Drafter`` of the same shape."""
+        dt = torch.bfloat16
+        drafter.embed.copy_(self.embed.to(dt))
+        drafter.fc.copy_(self.fc.to(dt))
+        for m, lw in zip(self.layers, drafter.layers):
+            for n in ("in_norm", "ctx_norm", "post_norm", "w_qkv", "q_norm", "k_norm", "w_o", "w13", "w2"):
+                lw[n].copy_(getattr(m, n).to(dt))
+        drafter.final_norm.copy_(self.final_norm.to(dt))
+        drafter.lm_head.copy_(self.lm_head.to(dt))
+        drafter.draft_vocab.copy_(self.draft_vocab.int())

@@ -128,3 +128,35 @@ def test_hisparse_offload_equals_on_device_qsa(fp8):
         agree = sum(a == b for x, y in zip(out_off, out_base) for a, b in zip(x, y)) / (2 * 80)
         assert agree > 0.5
     off.hs.close()
+
+
+def test_trained_drafter_export_matches_serving_proposals():
+    """The PyTorch drafter twin and the serving drafter (native kernels) propose the same block after export."""
+    from arc_forge_2026_b200.train.drafter_train import DrafterTrain
+    dcfg = drafter_preset("tiny")
+    V, Ht, Lc = 4096, 256, 70
+    g = torch.Generator().manual_seed(7)
+    serving = Drafter(dcfg, Ht, V, dev, draft_vocab=V)
+    twin = DrafterTrain(dcfg, Ht, V, serving.draft_vocab.long().cpu(), seed=3)
+    with torch.no_grad():
+        twin.lm_head.mul_(50.0)  # peaky logits: argmax far from bf16 ties
+    twin.export_to(serving)
+    tokens = torch.randint(0, V, (Lc + dcfg.k + 1,), generator=g)
+    hidden = torch.randn(Lc + dcfg.k + 1, Ht, generator=g) * 0.5
+    with torch.no_grad():
+        want = twin.draft_vocab[twin.block_logits(tokens, hidden.bfloat16().float(),
+                                                  torch.tensor([Lc])).argmax(-1)[0]].tolist()
+    kv = serving.new_kv_cache(4)
+    ws = serving.new_workspace(128)
+    i32 = dict(dtype=torch.int32, device=dev)
+    pos = torch.arange(Lc, **i32)
+    serving.inject(tokens[:Lc].int().to(dev), hidden[:Lc].bfloat16().to(dev), pos, pos.clone(), kv, ws)
+    blk = torch.full((dcfg.k,), serving.mask_id, **i32)
+    blk[0] = int(tokens[Lc])
+    bpos = torch.arange(Lc, Lc + dcfg.k, **i32)
+    out = torch.zeros(1, dcfg.k, **i32)
+    serving.propose(blk, hidden[Lc - 1:Lc].bfloat16().to(dev), bpos, bpos.clone(), torch.arange(4, **i32).view(1, 4),
+                    torch.tensor([Lc + dcfg.k], **i32), kv, ws, out, 1, max_pages=4)
+    torch.cuda.synchronize()
+    check_status()
+    assert out[0].tolist() == want
