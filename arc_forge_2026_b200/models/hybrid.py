@@ -205,6 +205,45 @@ class HybridModel:
         return cls(cfg, layers, ref.embed_tokens.weight.detach().to(**bf), ref.norm.weight.detach().to(**bf),
                    ref.lm_head.weight.detach().to(**bf), dev)
 
+    @classmethod
+    def from_package(cls, pkg_dir, device, verify: bool = True):
+        """Load an INT3 deploy package (``formats/int3_package.py``): uint3 expert packs are re-tiled for the
+        expert GEMM, block-FP8 dense modules dequantised to bf16 for the dense GEMMs."""
+        from ..formats.int3_package import dense_weight, expert_codes, read_package
+        cfg, t = read_package(pkg_dir, verify)
+        dev = torch.device(device)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        layers = []
+        for i, kind in enumerate(cfg.layer_types):
+            p = f"model.layers.{i}"
+            lw = LayerWeights(kind, t[f"{p}.input_layernorm.weight"].to(**bf),
+                              t[f"{p}.post_attention_layernorm.weight"].to(**bf))
+            if kind == FULL:
+                a = f"{p}.self_attn"
+                lw.w_qkv = torch.cat([dense_weight(t, f"{a}.{n}") for n in ("q_proj", "k_proj", "v_proj")]).to(**bf)
+                lw.q_norm = t[f"{a}.q_norm.weight"].to(**bf)
+                lw.k_norm = t[f"{a}.k_norm.weight"].to(**bf)
+                lw.w_o = dense_weight(t, f"{a}.o_proj").to(**bf).contiguous()
+            else:
+                g = f"{p}.linear_attn"
+                lw.w_in = torch.cat([dense_weight(t, f"{g}.in_proj_qkvz"), dense_weight(t, f"{g}.in_proj_ba")]).to(**bf)
+                lw.conv_w = t[f"{g}.conv1d.weight"].float().to(dev).contiguous()
+                lw.A_log = t[f"{g}.A_log"].float().to(dev)
+                lw.dt_bias = t[f"{g}.dt_bias"].float().to(dev)
+                lw.g_norm = t[f"{g}.norm.weight"].to(**bf)
+                lw.w_out = dense_weight(t, f"{g}.out_proj").to(**bf).contiguous()
+            m = f"{p}.mlp"
+            lw.router_ext = router_weight_with_shared_gate(dense_weight(t, f"{m}.gate").to(**bf),
+                                                           dense_weight(t, f"{m}.shared_expert_gate").to(**bf))
+            c13, s13, c2, s2 = expert_codes(t, i, cfg)
+            lw.bank = Int3ExpertBank.from_codes(c13, s13, c2, s2, dev)
+            lw.shared_w13 = torch.cat([dense_weight(t, f"{m}.shared_expert.gate_proj"),
+                                       dense_weight(t, f"{m}.shared_expert.up_proj")]).to(**bf)
+            lw.shared_w2 = dense_weight(t, f"{m}.shared_expert.down_proj").to(**bf).contiguous()
+            layers.append(lw)
+        return cls(cfg, layers, t["model.embed_tokens.weight"].to(**bf), t["model.norm.weight"].to(**bf),
+                   t["lm_head.weight"].to(**bf), dev)
+
     def nbytes(self) -> int:
         tot = self.embed.nbytes + self.lm_head.nbytes
         for lw in self.layers:

@@ -160,3 +160,21 @@ def test_trained_drafter_export_matches_serving_proposals():
     torch.cuda.synchronize()
     check_status()
     assert out[0].tolist() == want
+
+
+def test_model_from_package_equals_model_from_reference(tmp_path):
+    from arc_forge_2026_b200.formats.int3_package import package_tensors, write_package
+    from arc_forge_2026_b200.quant.int3_tiles import tiles_to_codes, tiles_to_scales
+    cfg, ref, model = _models(5)
+    cs = [(tiles_to_codes(lw.bank.w13_codes.cpu()), tiles_to_scales(lw.bank.w13_scales.cpu()),
+           tiles_to_codes(lw.bank.w2_codes.cpu()), tiles_to_scales(lw.bank.w2_scales.cpu())) for lw in model.layers]
+    d = write_package(package_tensors(ref, cs, dense_fp8=False), cfg, tmp_path / "pkg", dense_fp8=False)
+    loaded = HybridModel.from_package(d, dev)
+    prompt = torch.randint(0, cfg.vocab_size, (90,), generator=torch.Generator().manual_seed(5)).tolist()
+    outs = []
+    for m in (model, loaded):
+        eng = SpecEngine(m, None, ServeConfig(spec_k=0, accept_mode="greedy"), 1, 1024)
+        outs.append(eng.generate([prompt], 12))
+    torch.cuda.synchronize()
+    check_status()
+    assert outs[0] == outs[1]
