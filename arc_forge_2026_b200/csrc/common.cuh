@@ -56,6 +56,14 @@ AFB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// 1-D bulk copy global -> shared completing on an mbarrier (no multicast); dst/src 16-byte aligned, bytes % 16 == 0
+AFB_DEV void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // system-scope release store / acquire load (flags that peers on other GPUs write or read)
 AFB_DEV void st_release_sys_u64(uint64_t* p, uint64_t v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");

@@ -23,10 +23,12 @@ namespace gck {
 constexpr int C = 64, SL = 32, THREADS = 256;
 template <int DK>
 struct Smem {
-  float m1[C][DK];
-  float m2[C][DK];
+  float m1[2][C][DK];  // double buffer: chunk i+1 lands by bulk copy while chunk i is computed
+  float m2[2][C][DK];
   float st[DK][SL];
   float x[C][SL];
+  uint64_t full[2];
+  int ok;
 };
 }  // namespace gck
 
@@ -48,27 +50,44 @@ __global__ void __launch_bounds__(gck::THREADS) gdn_chunk_scan_kernel(GdnScanArg
 #pragma unroll
   for (int j = 0; j < RPT; ++j) sm.st[rg * RPT + j][c] = S[j];
 
-  for (int step = 0; step < n; ++step) {
+  if (t == 0) {
+    mbar_init(&sm.full[0], 1);
+    mbar_init(&sm.full[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int step, int b) {  // thread 0: chunk of this step -> buffer b
     const int i = REV ? n - 1 - step : step;
     const size_t ci = (size_t)bh * n + i;
-    // ---- stage chunk i: M1, M2 [C, DK] and the Y slice [C, SL]
-    {
-      const float4* g1 = reinterpret_cast<const float4*>(a.m1 + ci * C * DK);
-      const float4* g2 = reinterpret_cast<const float4*>(a.m2 + ci * C * DK);
-      float4* d1 = reinterpret_cast<float4*>(&sm.m1[0][0]);
-      float4* d2 = reinterpret_cast<float4*>(&sm.m2[0][0]);
-#pragma unroll
-      for (int v = t; v < C * DK / 4; v += THREADS) {
-        d1[v] = g1[v];
-        d2[v] = g2[v];
-      }
-#pragma unroll
-      for (int r = rg; r < C; r += 8) sm.x[r][c] = a.y[(ci * C + r) * Dv + c0 + c];
+    mbar_arrive_expect_tx(&sm.full[b], 2u * C * DK * 4);
+    bulk_load_1d(&sm.m1[b][0][0], a.m1 + ci * C * DK, C * DK * 4, &sm.full[b]);
+    bulk_load_1d(&sm.m2[b][0][0], a.m2 + ci * C * DK, C * DK * 4, &sm.full[b]);
+  };
+  int issued = 0;
+  if (t == 0) {
+    issue(0, 0);
+    issued = 1;
+  }
+  int step = 0;
+  for (; step < n; ++step) {
+    const int i = REV ? n - 1 - step : step;
+    const size_t ci = (size_t)bh * n + i;
+    const int b = step & 1;
+    // the other buffer was last read by the previous step, which every thread has finished
+    if (t == 0 && step + 1 < n) {
+      issue(step + 1, b ^ 1);
+      ++issued;
     }
+#pragma unroll
+    for (int r = rg; r < C; r += 8) sm.x[r][c] = a.y[(ci * C + r) * Dv + c0 + c];
     // the state before this step (forward: S_i, reverse: dS_{i+1})
 #pragma unroll
     for (int j = 0; j < RPT; ++j) a.states[(ci * DK + rg * RPT + j) * Dv + c0 + c] = S[j];
+    if (t == 0) sm.ok = mbar_wait(&sm.full[b], (step >> 1) & 1, a.status) ? 1 : 0;
     __syncthreads();
+    if (!sm.ok) break;
+    const float(*m1)[DK] = sm.m1[b];
+    const float(*m2)[DK] = sm.m2[b];
     // ---- X[r][c] = Y + s1 * sum_k M1[r][k] St[k][c], rows r = rg + 8 * j
     {
       float acc[8];
@@ -79,7 +98,7 @@ __global__ void __launch_bounds__(gck::THREADS) gdn_chunk_scan_kernel(GdnScanArg
         const float s0 = sm.st[k][c], sa = sm.st[k + 1][c], sb = sm.st[k + 2][c], sc = sm.st[k + 3][c];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 m = *reinterpret_cast<const float4*>(&sm.m1[rg + 8 * j][k]);
+          const float4 m = *reinterpret_cast<const float4*>(&m1[rg + 8 * j][k]);
           acc[j] = fmaf(m.x, s0, fmaf(m.y, sa, fmaf(m.z, sb, fmaf(m.w, sc, acc[j]))));
         }
       }
@@ -102,7 +121,7 @@ __global__ void __launch_bounds__(gck::THREADS) gdn_chunk_scan_kernel(GdnScanArg
 #pragma unroll 2
       for (int r = 0; r < C; ++r) {
         const float xv = sm.x[r][c];
-        const float4* mr = reinterpret_cast<const float4*>(&sm.m2[r][rg * RPT]);
+        const float4* mr = reinterpret_cast<const float4*>(&m2[r][rg * RPT]);
 #pragma unroll
         for (int q = 0; q < RPT / 4; ++q) {
           const float4 m = mr[q];
@@ -121,6 +140,8 @@ __global__ void __launch_bounds__(gck::THREADS) gdn_chunk_scan_kernel(GdnScanArg
     }
     __syncthreads();
   }
+  if (step < n && t == 0)  // a wait gave up: let the copies still in flight land before the CTA exits (bounded)
+    for (int j = step + 1; j < issued; ++j) mbar_wait(&sm.full[j & 1], (j >> 1) & 1, a.status);
   if (a.final_state)
 #pragma unroll
     for (int j = 0; j < RPT; ++j) a.final_state[((size_t)bh * DK + rg * RPT + j) * Dv + c0 + c] = S[j];

@@ -159,6 +159,7 @@ struct GdnScanArgs {
   float* states = nullptr;        // [BH, n, Dk, Dv] state before each step
   float* x = nullptr;             // [BH, n, C, Dv]
   float* final_state = nullptr;   // [BH, Dk, Dv] optional
+  uint32_t* status = nullptr;     // bounded-wait error bits
   int BH = 0, n_chunks = 0, C = 64, Dk = 128, Dv = 128;
 };
 int gdn_chunk_scan(const GdnScanArgs& a, bool reverse, cudaStream_t st);

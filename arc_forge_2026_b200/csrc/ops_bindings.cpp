@@ -478,6 +478,7 @@ void gdn_chunk_scan_op(const at::Tensor& m1, const at::Tensor& m2, const at::Ten
   a.states = ptr<float>(states);
   a.x = ptr<float>(x);
   a.final_state = optr<float>(final_state);
+  a.status = status_ptr(m1.get_device());
   check_rc(afb::gdn_chunk_scan(a, reverse, stream()), "gdn_chunk_scan");
 }
 
