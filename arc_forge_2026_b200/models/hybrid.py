@@ -96,7 +96,8 @@ class HybridModel:
 
     def enable_expert_parallel(self, world: int, rank: int, T_cap: int, group=None):
         """Split the routed experts over ``world`` ranks (keeps this rank's block) and route every MoE layer
-        through the peer-memory exchange. ``T_cap`` bounds the tokens of one forward on this rank."""
+        through the peer-memory exchange. ``T_cap`` bounds the tokens of one forward on any rank and must be the same
+        on every rank (the exchange regions are laid out by it; the constructor checks)."""
         from ..parallel.ep import ExpertParallel, expert_range, local_bank
         c = self.cfg
         e0, e1 = expert_range(c.num_experts, world, rank)

@@ -54,6 +54,12 @@ class ExpertParallel:
     def __init__(self, world: int, rank: int, T_cap: int, H: int, k: int, E: int, device, group=None):
         if not 1 <= world <= MAX_RANKS:
             raise ValueError(f"expert parallelism supports 1..{MAX_RANKS} ranks, got {world}")
+        if world > 1:  # the region layout (slot = rank * T_cap + t, entry owner = entry // (T_cap * k)) must agree
+            shapes = [None] * world
+            dist.all_gather_object(shapes, (T_cap, H, k, E), group=group)
+            if any(sh != shapes[0] for sh in shapes):
+                raise ValueError(f"expert-parallel shapes differ across ranks (T_cap, H, k, E): {shapes}; every rank "
+                                 f"must use the same capacity (the largest per-rank token count)")
         self.world, self.rank, self.T_cap, self.H, self.k, self.E = world, rank, T_cap, H, k, E
         self.e0, self.e1 = expert_range(E, world, rank)
         self.E_local = self.e1 - self.e0

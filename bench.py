@@ -188,7 +188,8 @@ def main():
     K = 4
     model = HybridModel.random(cfg, dev, seed=args.seed, ep_world=world)
     if world > 1:  # attention/GDN data-parallel over sessions, routed experts split over the ranks
-        model.enable_expert_parallel(world, rank, T_cap=S * (K + 1))
+        # one capacity on every rank (sessions need not split evenly): the exchange layout depends on it
+        model.enable_expert_parallel(world, rank, T_cap=-(-S_total // world) * (K + 1))
     drafter = Drafter(drafter_preset("dflash_8l"), cfg.hidden_size, cfg.vocab_size, dev, seed=args.seed + 1)
     scfg = ServeConfig(spec_k=K, accept_mode="bernoulli", accept_prob=0.7, seed=args.seed + 7 * rank,
                        hisparse=bool(qsa and args.hisparse), hisparse_fp8=bool(args.hisparse_fp8))
