@@ -91,3 +91,29 @@ def test_sections_accumulate():
             sum(range(1000))
     r = s.report()
     assert r["a"]["calls"] == 3 and r["a"]["ms"] >= 0
+
+
+def _ep_worker(rank, world, port, q):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    from arc_forge_2026_b200.parallel.ep import ExpertParallel
+    try:  # rank 1 asks for a different capacity: both ranks must refuse before any device memory is touched
+        ExpertParallel(world, rank, 80 if rank == 0 else 70, 256, 2, 8, "cpu")
+        q.put((rank, "built"))
+    except ValueError as e:
+        q.put((rank, "refused" if "differ across ranks" in str(e) else f"other: {e}"))
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_refuses_mismatched_shapes():
+    world, port = 2, _port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=60) for _ in range(world))
+    for p in ps:
+        p.join(timeout=30)
+    assert res == {0: "refused", 1: "refused"}
