@@ -12,7 +12,11 @@ sides, timed with CUDA events on the launching stream; the max over ranks is rep
 ``e2e`` = the same metric through the engine's public ``step()`` API, which each cycle uploads the page table from
 pinned host memory and reads back the emitted tokens.
 
-With N GPUs (torchrun), the 128 sessions are split over N data-parallel engine replicas (one per GPU).
+With N GPUs (torchrun), attention / GDN / drafter run data-parallel: the 128 sessions (contexts drawn once) are dealt
+to the ranks in snake order of decreasing length, so every rank holds 128/N sessions and nearly the same KV; the
+routed experts are split over the ranks (expert parallelism, fused peer-memory dispatch / combine).
+``--mode qsa`` runs BASELINE config 5 (110 sessions, 64k contexts, QSA top-32 of 64-token blocks; ``--hisparse``
+keeps the KV history in pinned host memory); ``--mode qad`` the QAD training step (config 4).
 ``--impl reference`` runs the unmodified reference when it is installed under baseline/_ref, else prints its
 ``unavailable`` line.
 """
@@ -184,7 +188,14 @@ def main():
     dev = torch.device("cuda", local)
     cfg = preset("qwen3next_80b", num_layers=args.layers, **(dict(qsa_block=64, qsa_topk=32) if qsa else {}))
     S_total = args.sessions
-    S = S_total // world + (1 if rank < S_total % world else 0)
+    # contexts of all sessions drawn once, dealt to ranks in snake order of decreasing length (equal counts,
+    # near-equal KV per rank: the placement a serving scheduler makes so no rank gates the per-layer exchanges)
+    ctx_all = torch.randint(args.min_ctx, args.max_ctx + 1, (S_total,), generator=torch.Generator().manual_seed(
+        args.seed * 1000 + 17))
+    order = torch.argsort(ctx_all, descending=True, stable=True).tolist()
+    mine = [order[i] for i in range(S_total) if (i // world) % 2 == 0 and i % world == rank or
+            (i // world) % 2 == 1 and world - 1 - i % world == rank]
+    S = len(mine)
     K = 4
     model = HybridModel.random(cfg, dev, seed=args.seed, ep_world=world)
     if world > 1:  # attention/GDN data-parallel over sessions, routed experts split over the ranks
@@ -194,7 +205,7 @@ def main():
     scfg = ServeConfig(spec_k=K, accept_mode="bernoulli", accept_prob=0.7, seed=args.seed + 7 * rank,
                        hisparse=bool(qsa and args.hisparse), hisparse_fp8=bool(args.hisparse_fp8))
     g = torch.Generator().manual_seed(args.seed * 1000 + rank)
-    ctx = torch.randint(args.min_ctx, args.max_ctx + 1, (S,), generator=g)
+    ctx = ctx_all[mine]
     need_pages = int(sum((int(c) + args.out_tokens + 2 * (K + 1) + 8 + PAGE - 1) // PAGE for c in ctx))
     max_context = args.max_ctx + args.out_tokens + 64
     eng = SpecEngine(model, drafter, scfg, S, max_context, num_pages=need_pages)
@@ -327,6 +338,7 @@ def main():
                             "8-layer DFlash drafter", "global_batch": S_total, "seq_len": f"U[{args.min_ctx},"
                             f"{args.max_ctx}] context + decode",
                    "parallelism": f"dp{world}-attn+ep{world}" if world > 1 else "dp1",
+                   "placement": "sessions dealt to ranks in snake order of context length" if world > 1 else None,
                    "spec_k": K, "acceptance": "seeded Bernoulli(0.7) per position", "layers": args.layers,
                    "attention": "QSA top-32 of 64-token blocks (+ local pages)" if qsa else "dense",
                    "kv_offload": ("HiSparse host pool " + ("e4m3" if args.hisparse_fp8 else "bf16"))
