@@ -240,16 +240,35 @@ static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, in
 }
 
 // Tile/split choice: fill 148 SMs (two CTAs fit per SM at BN<=128 with 3-4 stages).
+// Tile width and split-K count by a small cost model: the grid runs in ceil(CTAs / SMs) waves and each CTA streams
+// its B slice (bn x K/splits weights from DRAM) plus the A slice (128 x K/splits, mostly L2 hits, weighted 1/4);
+// split-K adds the fp32 partials written and read back (M x N x 4 x (splits + 1)). This keeps skinny decode GEMMs
+// (M <= 128, weights streamed once) on whole waves instead of a mostly-empty second wave.
 GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
-  GemmPlan p;
+  GemmPlan best;
+  double best_cost = 1e300;
   const int mt = (M + 127) / 128;
-  const int t128 = mt * ((N + 127) / 128);
-  p.bn = (t128 >= num_sms) ? 128 : 64;
-  const int tiles = mt * ((N + p.bn - 1) / p.bn);
   const int kb = (K + 63) / 64;
-  p.splits = 1;
-  while (tiles * p.splits * 2 <= 2 * num_sms && kb / (p.splits * 2) >= 4 && p.splits < 8) p.splits *= 2;
-  return p;
+  const int bns[3] = {64, 128, 256};
+  const int sps[6] = {1, 2, 3, 4, 6, 8};
+  for (int bn : bns) {
+    const long long tiles = (long long)mt * ((N + bn - 1) / bn);
+    for (int sp : sps) {
+      if (sp > 1 && kb / sp < 4) continue;
+      const long long ctas = tiles * sp;
+      const long long waves = (ctas + num_sms - 1) / num_sms;
+      const double kper = (double)((kb + sp - 1) / sp) * 64.0;
+      const double per_cta = (bn + 0.25 * 128.0) * kper * 2.0;
+      double cost = (double)waves * per_cta * num_sms;
+      if (sp > 1) cost += (double)M * N * 4.0 * (sp + 1);
+      if (cost < best_cost * 0.97) {  // prefer fewer splits / narrower tiles unless clearly cheaper
+        best_cost = cost;
+        best.bn = bn;
+        best.splits = sp;
+      }
+    }
+  }
+  return best;
 }
 
 int gemm_bf16_tn(const void* A, int lda, const void* B, int ldb, int M, int N, int K, const GemmEpilogue& epi,
