@@ -26,6 +26,10 @@ struct MoeGemmArgs {
   int out_ld = 0;
   const float* route_w = nullptr;  // !PAIR: routing weight per (token, slot) entry, or null
   const int* row_entry = nullptr;  // !PAIR: sorted row -> entry index
+  // block-FP8 experts instead of INT3 (the teacher): e4m3 weights [E, rows, K] and fp32 scales per 128 x 128 block
+  // [E, rows/128, K/128]; codes / scales above are then unused
+  const uint8_t* fp8_w = nullptr;
+  const float* fp8_scales = nullptr;
   long long* dbg = nullptr;        // optional profiling counters [grid, 4 roles, 3]: wait cycles, total, k-steps
   // !PAIR under expert parallelism: row_entry indexes all ranks' (token, slot) entries; entry e belongs to rank
   // e / ep_entries_per_rank and its routed row goes to that rank's combine region at (e % ep_entries_per_rank);

@@ -48,22 +48,25 @@ constexpr int MAX_E = 1024;               // experts whose segment offsets are s
 
 // Rings: raw stages (codes, weight scales, activation tile and scales, all moved by bulk/TMA copies), dequantised
 // e4m3 A tiles (dequant -> MMA), and per TMEM accumulator buffer a copy of the group's scales (dequant -> epilogue).
-template <bool PAIR>
+template <bool PAIR, bool F8 = false>
 struct Layout {
   static constexpr int T = PAIR ? 2 : 1;  // weight tiles per k-step
   static constexpr uint32_t X_OFF = 0;    // 1024-aligned (TMA 128-byte swizzle)
+  // INT3: code tiles (bulk copies), then per-row bf16 scales. F8: the e4m3 weight tiles themselves (TMA, swizzled:
+  // they are the MMA's A operand as they land) -- their fp32 block scales are read by the scale warps.
+  static constexpr uint32_t WA_OFF = X_OFF + X_TILE;
   static constexpr uint32_t C_OFF = X_OFF + X_TILE;
-  static constexpr uint32_t SW_OFF = C_OFF + T * CODE_TILE;
-  static constexpr uint32_t SX_OFF = SW_OFF + T * 128 * 2;
+  static constexpr uint32_t SW_OFF = F8 ? WA_OFF + T * A_TILE : C_OFF + T * CODE_TILE;
+  static constexpr uint32_t SX_OFF = SW_OFF + (F8 ? 0 : T * 128 * 2);
   static constexpr uint32_t RAW_BYTES = SX_OFF + NTOK * 4;
   static constexpr uint32_t RAW = (RAW_BYTES + 1023) & ~1023u;
-  // w13 (PAIR): one CTA per SM; w2: two CTAs per SM (half the shared memory and TMEM each)
   static constexpr int CTAS_PER_SM = 1;
-  static constexpr int RS = PAIR ? 6 : 8;     // raw stages
-  static constexpr int AS = PAIR ? 3 : 4;     // dequantised stages
+  static constexpr int RS = F8 ? (PAIR ? 5 : 8) : (PAIR ? 6 : 8);  // raw stages
+  static constexpr int AS = PAIR ? 3 : 4;     // dequantised stages (F8: no A ring, barriers only)
   static constexpr int NBUF = PAIR ? 8 : 16;  // TMEM accumulator buffers (T * 32 columns each)
-  static constexpr uint32_t ESC = 640;        // per-buffer copy of the group's scales: T*128 bf16 s_w + 32 fp32 s_x
-  static constexpr uint32_t A_STAGE = T * A_TILE;
+  static constexpr uint32_t ESC = 640;        // per-buffer copy of the group's scales (INT3: T*128 bf16 s_w, then
+                                              // 32 fp32 s_x; F8: T fp32 block scales, s_x at byte 16)
+  static constexpr uint32_t A_STAGE = F8 ? 0 : T * A_TILE;
   static constexpr uint32_t A_OFF = RS * RAW;
   static constexpr uint32_t ESC_OFF = A_OFF + AS * A_STAGE;         // scale ring [NBUF][ESC]
   static constexpr uint32_t OFFS_OFF = ESC_OFF + NBUF * ESC;         // int offsets[MAX_E + 1]
@@ -115,10 +118,11 @@ AFB_DEV void dequant_task(const uint32_t* row_words, uint8_t* tile, int r, int q
   *reinterpret_cast<uint4*>(tile + sw128_offset(r, 2 * q + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
-template <bool PAIR>
+template <bool PAIR, bool F8>
 __global__ void __launch_bounds__(moe::THREADS, 1)
-    moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmX, MoeGemmArgs args, uint32_t* status) {
-  using L = moe::Layout<PAIR>;
+    moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                         MoeGemmArgs args, uint32_t* status) {
+  using L = moe::Layout<PAIR, F8>;
   constexpr int RS = L::RS, AS = L::AS, NBUF = L::NBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -186,17 +190,22 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
               break;
             }
             uint8_t* st = smem + s * L::RAW;
-            mbar_arrive_expect_tx(&full[s], L::T * (moe::CODE_TILE + 256) + moe::X_TILE + moe::NTOK * 4);
+            mbar_arrive_expect_tx(&full[s], F8 ? L::T * moe::A_TILE + moe::X_TILE + moe::NTOK * 4
+                                               : L::T * (moe::CODE_TILE + 256) + moe::X_TILE + moe::NTOK * 4);
             // activation scales of this group for the chunk's 32 rows (group-major, segment starts 8-aligned)
             bulk_g2s(st + L::SX_OFF, args.x_scales + (size_t)g * args.ld_xs + crow, moe::NTOK * 4, &full[s]);
 #pragma unroll
             for (int t = 0; t < L::T; ++t) {
               const int rb = PAIR ? (t == 0 ? j : NB + j) : j;  // gate block j, up block NB + j
-              const size_t tile = ((size_t)e * (args.rows / 128) + rb) * KG + g;
-              bulk_g2s(st + L::C_OFF + t * moe::CODE_TILE, args.codes + tile * (moe::CODE_TILE / 4), moe::CODE_TILE,
-                       &full[s]);
-              bulk_g2s(st + L::SW_OFF + t * 256, reinterpret_cast<const uint16_t*>(args.scales) + tile * 128, 256,
-                       &full[s]);
+              if constexpr (F8) {
+                tma_load_2d(st + L::WA_OFF + t * moe::A_TILE, &tmW, &full[s], g * 128, e * args.rows + rb * 128);
+              } else {
+                const size_t tile = ((size_t)e * (args.rows / 128) + rb) * KG + g;
+                bulk_g2s(st + L::C_OFF + t * moe::CODE_TILE, args.codes + tile * (moe::CODE_TILE / 4),
+                         moe::CODE_TILE, &full[s]);
+                bulk_g2s(st + L::SW_OFF + t * 256, reinterpret_cast<const uint16_t*>(args.scales) + tile * 128, 256,
+                         &full[s]);
+              }
             }
             tma_load_2d(st + L::X_OFF, &tmX, &full[s], g * 128, crow);
           }
@@ -222,6 +231,22 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           }
           const uint8_t* st = smem + s * L::RAW;
           uint8_t* at = smem + L::A_OFF + as * L::A_STAGE;
+          if constexpr (F8) {  // nothing to decode: only the scales move to the epilogue's slot b
+            float* dst = reinterpret_cast<float*>(smem + L::ESC_OFF + b * L::ESC);
+            if (dq < L::T) {
+              const int rb = PAIR ? (dq == 0 ? j : NB + j) : j;
+              dst[dq] = args.fp8_scales[((size_t)e * (args.rows / 128) + rb) * KG + g];
+            } else if (dq >= 32 && dq < 32 + moe::NTOK) {
+              dst[4 + dq - 32] = reinterpret_cast<const float*>(st + L::SX_OFF)[dq - 32];
+            }
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(&afull[as]);
+              mbar_arrive(&sready[b]);
+              mbar_arrive(&empty[s]);
+            }
+            continue;
+          }
           {  // the group's scales move to the epilogue's ring slot b, so the raw stage can be refilled early
             constexpr int SW_WORDS = L::T * 64, WORDS = SW_WORDS + moe::NTOK;
             uint32_t* dst = reinterpret_cast<uint32_t*>(smem + L::ESC_OFF + b * L::ESC);
@@ -280,7 +305,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           tc_fence_after();
           if (lane == 0) {
             const uint8_t* st = smem + s * L::RAW;
-            const uint8_t* at = smem + L::A_OFF + as * L::A_STAGE;
+            const uint8_t* at = F8 ? st + L::WA_OFF : smem + L::A_OFF + as * L::A_STAGE;
             const uint64_t dx = sw128_desc(smem_u32(st + L::X_OFF));
 #pragma unroll
             for (int t = 0; t < L::T; ++t) {
@@ -328,10 +353,13 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint8_t* esc = smem + L::ESC_OFF + b * L::ESC;  // [T][128] bf16 s_w, then [32] fp32 s_x
-          const float* sx = reinterpret_cast<const float*>(esc + L::T * 256) + half * NH;
-          const float sw0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(esc)[r]);
-          const float sw1 = PAIR ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(esc + 256)[r]) : 0.f;
+          const uint8_t* esc = smem + L::ESC_OFF + b * L::ESC;  // INT3: [T][128] bf16 s_w, [32] fp32 s_x
+          const float* sx = reinterpret_cast<const float*>(esc + (F8 ? 16 : L::T * 256)) + half * NH;
+          const float sw0 = F8 ? reinterpret_cast<const float*>(esc)[0]
+                               : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(esc)[r]);
+          const float sw1 = !PAIR ? 0.f
+                            : F8 ? reinterpret_cast<const float*>(esc)[1]
+                                 : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(esc + 256)[r]);
           const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * L::T * moe::NTOK + half * NH);
           float d[NH];  // one 16-column load at a time keeps the role inside 128 registers
           tmem_ld16(ta, d);
@@ -418,33 +446,38 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
   }
 }
 
+template <bool PAIR, bool F8>
+static int launch_moe(const CUtensorMap& tx, const CUtensorMap& tw, const MoeGemmArgs& a, int grid, uint32_t* status,
+                      cudaStream_t st) {
+  using L = moe::Layout<PAIR, F8>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(moe_int3_gemm_kernel<PAIR, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    attr = true;
+  }
+  moe_int3_gemm_kernel<PAIR, F8><<<grid, moe::THREADS, L::TOTAL, st>>>(tx, tw, a, status);
+  return (int)cudaGetLastError();
+}
+
 int moe_int3_gemm(const MoeGemmArgs& a, int pair, int num_sms, uint32_t* status, cudaStream_t st) {
   if (a.K % 128 || a.rows % (pair ? 256 : 128) || a.num_experts > moe::MAX_E) return 3;
   if (a.num_rows_total <= 0) return 0;
-  CUtensorMap tx;
+  CUtensorMap tx, tw;
   int rc = make_tmap_2d(&tx, a.x_q, 1, a.K, a.num_rows_total, (uint64_t)a.K, 128, moe::NTOK, 1);
   if (rc) return 1000 + rc;
-  const int units = a.num_experts * (a.rows / 128 / (pair ? 2 : 1));
-  const int slots = num_sms * (pair ? moe::Layout<true>::CTAS_PER_SM : moe::Layout<false>::CTAS_PER_SM);
-  const int grid = units < slots ? units : slots;
-  if (pair) {
-    using L = moe::Layout<true>;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(moe_int3_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-      attr = true;
-    }
-    moe_int3_gemm_kernel<true><<<grid, moe::THREADS, L::TOTAL, st>>>(tx, a, status);
+  if (a.fp8_w) {  // e4m3 weights [E * rows, K]: 128 x 128 tiles, 128-byte swizzle (the MMA's A layout)
+    if (!a.fp8_scales) return 3;
+    rc = make_tmap_2d(&tw, a.fp8_w, 1, a.K, (uint64_t)a.num_experts * a.rows, (uint64_t)a.K, 128, 128, 1);
+    if (rc) return 2000 + rc;
   } else {
-    using L = moe::Layout<false>;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(moe_int3_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-      attr = true;
-    }
-    moe_int3_gemm_kernel<false><<<grid, moe::THREADS, L::TOTAL, st>>>(tx, a, status);
+    tw = tx;  // unused by the INT3 kernels
   }
-  return (int)cudaGetLastError();
+  const int units = a.num_experts * (a.rows / 128 / (pair ? 2 : 1));
+  const int grid = units < num_sms ? units : num_sms;
+  if (a.fp8_w) return pair ? launch_moe<true, true>(tx, tw, a, grid, status, st)
+                           : launch_moe<false, true>(tx, tw, a, grid, status, st);
+  return pair ? launch_moe<true, false>(tx, tw, a, grid, status, st)
+              : launch_moe<false, false>(tx, tw, a, grid, status, st);
 }
 
 }  // namespace afb

@@ -132,19 +132,32 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
                       c10::optional<at::Tensor> out_scales, c10::optional<at::Tensor> out_bf16,
                       c10::optional<at::Tensor> route_w, c10::optional<at::Tensor> row_entry,
                       c10::optional<at::Tensor> dbg, const EpCtx* ep) {
-  AFB_CHECK_DT(codes, at::kInt);
-  AFB_CHECK_DT(scales, at::kBFloat16);
   AFB_CHECK_DT(offsets, at::kInt);
   AFB_CHECK_CONTIG(codes);
   AFB_CHECK_CONTIG(scales);
   AFB_CHECK_CONTIG(x_q);
-  TORCH_CHECK(codes.dim() == 5 && codes.size(3) == 128 && codes.size(4) == 12, "codes must be tile layout");
   afb::MoeGemmArgs a;
-  a.codes = ptr<int32_t>(codes);
-  a.scales = scales.data_ptr();
-  a.num_experts = codes.size(0);
-  a.rows = codes.size(1) * 128;
-  a.K = codes.size(2) * 128;
+  if (codes.scalar_type() == at::kFloat8_e4m3fn) {  // block-FP8 experts: weights [E, rows, K], scales [E, rows/128, K/128]
+    AFB_CHECK_DT(scales, at::kFloat);
+    TORCH_CHECK(codes.dim() == 3 && codes.size(1) % 128 == 0 && codes.size(2) % 128 == 0, "fp8 experts [E, R, K]");
+    TORCH_CHECK(scales.dim() == 3 && scales.size(0) == codes.size(0) && scales.size(1) == codes.size(1) / 128 &&
+                    scales.size(2) == codes.size(2) / 128,
+                "fp8 block scales [E, R/128, K/128]");
+    a.fp8_w = reinterpret_cast<const uint8_t*>(codes.data_ptr());
+    a.fp8_scales = ptr<float>(scales);
+    a.num_experts = codes.size(0);
+    a.rows = codes.size(1);
+    a.K = codes.size(2);
+  } else {
+    AFB_CHECK_DT(codes, at::kInt);
+    AFB_CHECK_DT(scales, at::kBFloat16);
+    TORCH_CHECK(codes.dim() == 5 && codes.size(3) == 128 && codes.size(4) == 12, "codes must be tile layout");
+    a.codes = ptr<int32_t>(codes);
+    a.scales = scales.data_ptr();
+    a.num_experts = codes.size(0);
+    a.rows = codes.size(1) * 128;
+    a.K = codes.size(2) * 128;
+  }
   TORCH_CHECK(offsets.numel() == a.num_experts + 1, "offsets must have E+1 entries");
   TORCH_CHECK(x_q.size(1) == a.K, "x_q width");
   a.expert_offsets = ptr<int>(offsets);
@@ -183,7 +196,8 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
     }
   }
   a.dbg = optr<long long>(dbg);
-  check_rc(afb::moe_int3_gemm(a, pair, num_sms(), status_ptr(codes.get_device()), stream()), "moe_int3_gemm");
+  check_rc(afb::moe_int3_gemm(a, pair, num_sms(), status_ptr(codes.get_device()), stream()),
+           a.fp8_w ? "moe_fp8_gemm" : "moe_int3_gemm");
 }
 
 void moe_combine_op(const at::Tensor& y, const at::Tensor& entry_row, int64_t k, c10::optional<at::Tensor> shared,

@@ -79,6 +79,48 @@ class Int3ExpertBank:
                                                           self.w2_scales))
 
 
+@dataclass
+class Fp8ExpertBank:
+    """One layer's routed experts in block FP8 (the teacher's format): e4m3 weights and one fp32 scale per 128 x 128
+    block (``weight_scale_inv``). The expert kernels take it in place of an ``Int3ExpertBank``."""
+    w13_codes: torch.Tensor   # e4m3 [E, 2I, H]
+    w13_scales: torch.Tensor  # fp32 [E, 2I/128, H/128]
+    w2_codes: torch.Tensor    # e4m3 [E, H, I]
+    w2_scales: torch.Tensor   # fp32 [E, H/128, I/128]
+
+    @property
+    def num_experts(self) -> int:
+        return self.w13_codes.shape[0]
+
+    @property
+    def hidden(self) -> int:
+        return self.w13_codes.shape[2]
+
+    @property
+    def inter(self) -> int:
+        return self.w2_codes.shape[2]
+
+    @classmethod
+    def from_weights(cls, w13: torch.Tensor, w2: torch.Tensor, device=None):
+        """Block-quantise fp32/bf16 expert weights [E, 2I, H] / [E, H, I]."""
+        def q(w):
+            qs = [fp8q.quantize_weight_block(w[e].float()) for e in range(w.shape[0])]
+            return torch.stack([a for a, _ in qs]), torch.stack([b for _, b in qs])
+        a, sa = q(w13)
+        b, sb = q(w2)
+        t = cls(a, sa.float(), b, sb.float())
+        return t.to(device) if device is not None else t
+
+    def to(self, device):
+        return Fp8ExpertBank(*(t.to(device) for t in (self.w13_codes, self.w13_scales, self.w2_codes,
+                                                         self.w2_scales)))
+
+    def dequant(self, dtype=torch.float32):
+        def dq(w, s):
+            return torch.stack([fp8q.dequant_weight_block(w[e], s[e]) for e in range(w.shape[0])]).to(dtype)
+        return dq(self.w13_codes, self.w13_scales), dq(self.w2_codes, self.w2_scales)
+
+
 SEG_PAD = 8  # expert segments start on multiples of 8 rows (16-byte bulk copies of per-row scales)
 
 

@@ -58,3 +58,24 @@ def test_int3_gemm_single_expert_exact_inputs():
     hh = torch.nn.functional.silu(h[:, :I]) * h[:, I:]
     got = hq.float() * hs[:, :T].t().repeat_interleave(128, -1)
     assert _rel(got, hh) < 4e-2  # e4m3 output quantisation (3 mantissa bits)
+
+
+@pytest.mark.parametrize("E,H,I,k,T", [(8, 256, 256, 2, 37), (64, 1024, 512, 8, 300)])
+def test_fp8_block_experts_match_oracle(E, H, I, k, T):
+    """Block-FP8 experts (the teacher's format) through the same expert kernels: W8A8 with 128x128 weight scales."""
+    from arc_forge_2026_b200.ops.moe import Fp8ExpertBank
+    g = torch.Generator(device="cpu").manual_seed(E + T + 1)
+    bank = Fp8ExpertBank.from_weights(torch.randn(E, 2 * I, H, generator=g) * 0.02,
+                                      torch.randn(E, H, I, generator=g) * 0.02, dev)
+    rext = router_weight_with_shared_gate((torch.randn(E, H, generator=g) * 0.02).bfloat16().to(dev),
+                                          (torch.randn(1, H, generator=g) * 0.02).bfloat16().to(dev))
+    sw13 = (torch.randn(2 * 128, H, generator=g) * 0.02).bfloat16().to(dev)
+    sw2 = (torch.randn(H, 128, generator=g) * 0.02).bfloat16().to(dev)
+    x = torch.randn(T, H, generator=g).bfloat16().to(dev)
+    resid = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+    ws = MoEWorkspace(T, E, k, H, I, 128, dev)
+    out = moe_forward(x, resid, rext, bank, sw13, sw2, k, ws)
+    torch.cuda.synchronize()
+    check_status()
+    ref = moe_reference(x, resid, rext, bank, sw13, sw2, k)
+    assert _rel(out, ref) < 2e-2
