@@ -24,7 +24,7 @@ from ..config import FULL, ModelConfig
 from ..ops import C
 from ..ops.attention import PAGE, paged_attention
 from ..ops.gdn import GdnScratch, GdnShape, GdnState, gdn_decode
-from ..ops.moe import Int3ExpertBank, MoEWorkspace, moe_forward, router_weight_with_shared_gate
+from ..ops.moe import Fp8ExpertBank, Int3ExpertBank, MoEWorkspace, moe_forward, router_weight_with_shared_gate
 from ..ops.qsa import qsa_attention
 from ..parallel.ep import EPMoEWorkspace, moe_forward_ep
 from .reference import HybridMoE, rope_cos_sin
@@ -150,6 +150,20 @@ class HybridModel:
             E, I, Is = cfg.num_experts, cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
             lw.router_ext = router_weight_with_shared_gate(randn(E, H), randn(1, H))
             E = E // ep_world
+            if cfg.expert_format == "fp8":  # block-FP8 experts (the QAD teacher): e4m3 of N(0, 1), scale std / 1
+                def fp8w(rows, k):
+                    w = torch.empty(E, rows, k, dtype=torch.float8_e4m3fn, device=dev)
+                    for e0 in range(0, E, 32):  # in slices: the fp32 draw of a whole bank would not fit
+                        e1 = min(E, e0 + 32)
+                        w[e0:e1] = torch.randn(e1 - e0, rows, k, generator=gen, device=dev).to(torch.float8_e4m3fn)
+                    return w, torch.full((E, rows // 128, k // 128), std, dtype=torch.float32, device=dev)
+                a, sa = fp8w(2 * I, H)
+                b, sb = fp8w(H, I)
+                lw.bank = Fp8ExpertBank(a, sa, b, sb)
+                lw.shared_w13 = randn(2 * Is, H)
+                lw.shared_w2 = randn(H, Is)
+                layers.append(lw)
+                continue
             lw.bank = Int3ExpertBank(
                 torch.randint(-2**31, 2**31 - 1, (E, 2 * I // 128, H // 128, 128, 12), dtype=torch.int32,
                               device=dev, generator=gen),

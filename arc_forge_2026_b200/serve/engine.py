@@ -191,7 +191,7 @@ class SpecEngine:
                 self.bt_host[s.row, n:] = self.scratch_page
         self.block_table.copy_(self.bt_host, non_blocking=True)
 
-    def add_session(self, sid: int, prompt: list[int], max_new_tokens: int):
+    def add_session(self, sid: int, prompt: list[int], max_new_tokens: int, on_chunk=None):
         if not self.free_rows:
             raise RuntimeError("no free session slot")
         if len(prompt) + max_new_tokens + 2 * self.W > self.max_context:
@@ -205,11 +205,19 @@ class SpecEngine:
         else:
             self.alloc.ensure(sid, len(prompt) + 2 * self.W + 8)
             self._sync_pages([row])
-        self._prefill(sess)
+        self._prefill(sess, on_chunk)
         return sess
 
     @torch.no_grad()
-    def _prefill(self, sess: Session):
+    def score(self, tokens: list[int], fn):
+        """Run ``tokens`` through the target model as one temporary session, chunk by chunk, calling
+        ``fn(hidden_rows [T, H], start)`` with the final-normed hidden states of every chunk (teacher scoring)."""
+        sid = -(1 << 30)
+        sess = self.add_session(sid, tokens, 1, on_chunk=fn)
+        self.release(sess.sid)
+
+    @torch.no_grad()
+    def _prefill(self, sess: Session, on_chunk=None):
         cC, m = C(), self.model
         if m.ep is not None and m.ep.world > 1:
             raise NotImplementedError("prefill under expert parallelism needs every rank in the same forward; "
@@ -235,6 +243,8 @@ class SpecEngine:
                           attn_bt_row=torch.full((nv,), sess.row, dtype=torch.int32, device=dev),
                           attn_seq_lens=vlen, attn_q_per_seq=8)
             hidden = m.forward(b, self.kv, self.gdn, self.ws, self.gdn_scratch, qsa=self.qsa)
+            if on_chunk is not None:
+                on_chunk(hidden[:T], c0)
             if self.drafter is not None:
                 keep = max(0, T - (self.drafter.cfg.window + 64))
                 dslots = (self.d_block_table[sess.row, (pos.long() // PAGE)] * PAGE + pos.long() % PAGE).int()

@@ -158,6 +158,9 @@ def main(argv=None):
     ap.add_argument("--resume", action="store_true")
     ap.add_argument("--export", type=Path)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--teacher-preset", dest="teacher_preset", default="",
+                    help="teacher mode on a GPU: run this (block-FP8) preset on the serving kernels, e.g. "
+                         "qwen3next_80b_teacher; empty: score with the student itself")
     args = ap.parse_args(argv)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -190,14 +193,26 @@ def main(argv=None):
         if args.out is None:
             raise SystemExit("--out is required in teacher mode")
         w = TopKWriter(args.out, "train", args.topk)
+        native = None
+        if dev.type == "cuda" and args.teacher_preset:  # the block-FP8 teacher on the serving kernels
+            from ..models.hybrid import HybridModel
+            from .teacher import NativeTeacher
+            tkw = {"num_layers": args.layers} if args.layers else {}
+            native = NativeTeacher(HybridModel.random(preset(args.teacher_preset, **tkw), dev, seed=args.seed + 101),
+                                   args.seq_len)
         with torch.no_grad():
             for step in range(args.steps):
                 ids, _ = batch(step)
+                if native is not None:
+                    for row in ids:
+                        t_ids, t_lp, t_tail = native.targets(row, args.topk)
+                        w.append(t_ids, t_lp, t_tail, row)
+                    continue
                 h = student.hidden(ids).reshape(ids.numel(), -1)
                 z = (h @ student.lm_head.t()).float()
                 t_ids, t_lp, t_tail = teacher_topk(z, args.topk)
                 w.append(t_ids, t_lp, t_tail, ids.reshape(-1))
-        w.close({"source": "trainer-prefill", "teacher": args.preset})
+        w.close({"source": "trainer-prefill", "teacher": args.teacher_preset if native is not None else args.preset})
         return
 
     opt = build_optimizer(student, qc, sharded=True, group=dist.group.WORLD if world > 1 else None)

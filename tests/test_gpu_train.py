@@ -133,3 +133,24 @@ def test_chunked_gdn_gradients_on_gpu_match_unrolled_loop():
         grads.append([o.detach()] + [t.grad for t in ins])
     for a, b in zip(*grads):
         assert _rel(a, b) < 1e-4
+
+
+def test_native_fp8_teacher_targets_agree_with_its_prefill():
+    from arc_forge_2026_b200.config import ServeConfig, preset
+    from arc_forge_2026_b200.models.hybrid import HybridModel
+    from arc_forge_2026_b200.serve.engine import SpecEngine
+    from arc_forge_2026_b200.train.teacher import NativeTeacher
+    cfg = preset("tiny_gpu", expert_format="fp8")
+    model = HybridModel.random(cfg, dev, seed=1)
+    with torch.no_grad():
+        model.lm_head.mul_(20.0)
+    ids = torch.randint(0, cfg.vocab_size, (300,), generator=torch.Generator().manual_seed(3))
+    t_ids, t_lp, t_tail = NativeTeacher(model, 300).targets(ids, 8)
+    torch.cuda.synchronize()
+    check_status()
+    assert t_ids.shape == (300, 8) and torch.all(t_lp[:, :-1] >= t_lp[:, 1:])
+    total = torch.logsumexp(torch.cat([t_lp, t_tail[:, None]], 1), 1)
+    assert torch.allclose(total, torch.zeros_like(total), atol=1e-4)  # top-k + tail is the whole distribution
+    eng = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy"), 1, 400)
+    eng.add_session(0, ids.tolist(), 2)
+    assert eng.sessions[0].generated[0] == int(t_ids[-1, 0])
