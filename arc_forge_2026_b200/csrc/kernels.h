@@ -188,6 +188,28 @@ int ep_wait(const EpArgs& a, int type, uint32_t* status, cudaStream_t st);
 int ep_gather(const EpArgs& a, const int* row_token, const int* nrows_dev, int rows_cap, void* xq, float* xs,
               int ld_xs, cudaStream_t st);
 
+// zero_comm.cu: ZeRO-style optimizer step over peer memory (symmetric heap)
+constexpr int ZERO_GRADS = 0, ZERO_NORM = 1, ZERO_PARAMS = 2;
+struct ZeroArgs {
+  int world = 1, rank = 0;
+  uint8_t* peer[EP_MAX_RANKS] = {};
+  size_t off_flags = 0;  // uint64 [3 types][EP_MAX_RANKS sources]
+  size_t off_norm = 0;   // float [EP_MAX_RANKS] sums of squares by rank
+  unsigned long long* sent = nullptr;      // local [3]
+  unsigned long long* expected = nullptr;  // local [3]
+  float* norm_out = nullptr;               // local scalar: the global gradient norm of the last step
+};
+int zero_signal(const ZeroArgs& a, int type, cudaStream_t st);
+int zero_wait(const ZeroArgs& a, int type, uint32_t* status, cudaStream_t st);
+int zero_rs(const ZeroArgs& a, size_t grad_off, size_t chunk, float scale, float* shard, float* partials, int blocks,
+            cudaStream_t st);
+int zero_norm_publish(const ZeroArgs& a, const float* partials, int n, cudaStream_t st);
+int zero_adamw(const ZeroArgs& a, size_t param_off, size_t chunk, const float* g, void* m, void* v, size_t n_valid,
+               float lr, float b1, float b2, float eps, float wd, int step, float max_norm, int blocks,
+               cudaStream_t st);
+int zero_ag(const ZeroArgs& a, size_t param_off, size_t chunk, int blocks, cudaStream_t st);
+
+
 // sampling.cu
 int select_tokens(const void* logits, int ld, int rows, int V, int* out, float temperature, uint64_t seed,
                   const int* step, uint32_t* status, cudaStream_t st);

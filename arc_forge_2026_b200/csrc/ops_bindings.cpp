@@ -350,6 +350,55 @@ void qsa_finalize_op(const std::vector<at::Tensor>& idx_raw, const std::vector<a
   check_rc(afb::qsa_finalize(f, fin.size(0), L, stream()), "qsa_finalize");
 }
 
+// ZeRO step over peer memory (see zero_comm.cu)
+struct ZeroCtx {
+  afb::ZeroArgs a;
+  ZeroCtx(int64_t world, int64_t rank, std::vector<int64_t> peers, int64_t off_flags, int64_t off_norm,
+          const at::Tensor& sent, const at::Tensor& expected, const at::Tensor& norm_out) {
+    TORCH_CHECK(world >= 1 && world <= afb::EP_MAX_RANKS && (int64_t)peers.size() == world, "ZeroCtx: world");
+    AFB_CHECK_DT(sent, at::kLong);
+    AFB_CHECK_DT(expected, at::kLong);
+    AFB_CHECK_DT(norm_out, at::kFloat);
+    a.world = (int)world;
+    a.rank = (int)rank;
+    for (int p = 0; p < world; ++p) a.peer[p] = reinterpret_cast<uint8_t*>((uintptr_t)peers[p]);
+    a.off_flags = off_flags;
+    a.off_norm = off_norm;
+    a.sent = reinterpret_cast<unsigned long long*>(sent.data_ptr());
+    a.expected = reinterpret_cast<unsigned long long*>(expected.data_ptr());
+    a.norm_out = ptr<float>(norm_out);
+  }
+  void signal(int64_t type) { check_rc(afb::zero_signal(a, (int)type, stream()), "zero_signal"); }
+  void wait(int64_t type) {
+    int d = 0;
+    cudaGetDevice(&d);
+    check_rc(afb::zero_wait(a, (int)type, status_ptr(d), stream()), "zero_wait");
+  }
+  void rs(int64_t grad_off, int64_t chunk, double scale, at::Tensor& shard, at::Tensor& partials) {
+    AFB_CHECK_DT(shard, at::kFloat);
+    AFB_CHECK_DT(partials, at::kFloat);
+    TORCH_CHECK(shard.numel() >= chunk, "rs shard");
+    check_rc(afb::zero_rs(a, grad_off, chunk, (float)scale, ptr<float>(shard), ptr<float>(partials), partials.numel(),
+                          stream()),
+             "zero_rs");
+  }
+  void norm_publish(const at::Tensor& partials) {
+    check_rc(afb::zero_norm_publish(a, ptr<float>(partials), partials.numel(), stream()), "zero_norm_publish");
+  }
+  void adamw(int64_t param_off, int64_t chunk, const at::Tensor& g, at::Tensor& m, at::Tensor& v, int64_t n_valid,
+             double lr, double b1, double b2, double eps, double wd, int64_t step, double max_norm, int64_t blocks) {
+    AFB_CHECK_DT(m, at::kBFloat16);
+    AFB_CHECK_DT(v, at::kBFloat16);
+    check_rc(afb::zero_adamw(a, param_off, chunk, ptr<float>(g), m.data_ptr(), v.data_ptr(), n_valid, (float)lr,
+                             (float)b1, (float)b2, (float)eps, (float)wd, (int)step, (float)max_norm, (int)blocks,
+                             stream()),
+             "zero_adamw");
+  }
+  void ag(int64_t param_off, int64_t chunk, int64_t blocks) {
+    check_rc(afb::zero_ag(a, param_off, chunk, (int)blocks, stream()), "zero_ag");
+  }
+};
+
 // HiSparse (see hisparse.cu): the host pools, GPU pools and residency tables of every QSA layer.
 struct HsCtx {
   afb::HsArgs a;
@@ -654,6 +703,15 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("pages_per_split"), py::arg("window"), py::arg("bt_row"), py::arg("sp_count") = py::none(),
         py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none());
   m.def("qsa_prep", &qsa_prep_op);
+  py::class_<ZeroCtx>(m, "ZeroCtx")
+      .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, const at::Tensor&, const at::Tensor&,
+                    const at::Tensor&>())
+      .def("signal", &ZeroCtx::signal)
+      .def("wait", &ZeroCtx::wait)
+      .def("rs", &ZeroCtx::rs)
+      .def("norm_publish", &ZeroCtx::norm_publish)
+      .def("adamw", &ZeroCtx::adamw)
+      .def("ag", &ZeroCtx::ag);
   py::class_<HsCtx>(m, "HsCtx")
       .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, bool, const at::Tensor&,
                     const std::vector<std::vector<int64_t>>&>())

@@ -36,6 +36,8 @@ def average_gradients(params, group=None):
 class ShardedAdamW:
     """ZeRO-style AdamW over parameter groups ``[{"params": [...], "lr": x}, ...]`` of fp32 masters."""
 
+    sharded = True
+
     def __init__(self, groups, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, group=None):
         self.pg = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1

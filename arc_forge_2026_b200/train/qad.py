@@ -42,10 +42,19 @@ def lr_for(group: str, qc: QADConfig) -> float:
     return {"scale": qc.lr_scale, "router": qc.lr_router}.get(group, qc.lr_dense)
 
 
-def build_optimizer(student: QADStudent, qc: QADConfig, sharded: bool = False, group=None):
+def build_optimizer(student: QADStudent, qc: QADConfig, sharded: bool = False, group=None, fused: bool | None = None):
+    """``sharded``: ZeRO-style over the ranks of ``group``; ``fused`` (default: on CUDA with several ranks) runs its
+    reduce-scatter, clip, update and all-gather in the peer-memory kernels of ``parallel/zero.py`` instead of NCCL."""
     groups = student.param_groups()
     spec = [{"params": groups[g], "lr": lr_for(g, qc), "name": g} for g in groups if groups[g]]
     if sharded:
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        on_gpu = spec[0]["params"][0].is_cuda
+        if fused is None:
+            fused = on_gpu and world > 1
+        if fused:
+            from ..parallel.zero import FusedShardedAdamW
+            return FusedShardedAdamW(spec, betas=qc.betas, weight_decay=qc.weight_decay, group=group)
         return ShardedAdamW(spec, betas=qc.betas, weight_decay=qc.weight_decay, group=group)
     return AdamWBF16(spec, betas=qc.betas, weight_decay=qc.weight_decay)
 
@@ -79,7 +88,7 @@ def train_step(student: QADStudent, opt, ids: torch.Tensor, targets: dict, qc: Q
     (gradients are zeroed at the first one, ``first`` defaults to "the optimizer has no pending gradients"); the
     loss is divided by ``micro_batches`` so the step sees the mean over the whole global batch.
     Returns (mean loss, grad norm) as floats when ``sync``, else the loss as a device tensor (no host sync)."""
-    sharded = isinstance(opt, ShardedAdamW)
+    sharded = getattr(opt, "sharded", False)
     if first is None:
         first = not getattr(opt, "_afb_pending", False)
     if first:
@@ -93,7 +102,9 @@ def train_step(student: QADStudent, opt, ids: torch.Tensor, targets: dict, qc: Q
     norm = None
     if not accumulate:
         mask_zero_scale_grads(student, signs)
-        if sharded:
+        if sharded and not sync and getattr(opt, "async_step", False):
+            opt.step(qc.grad_clip, sync=False)
+        elif sharded:
             norm = opt.step(qc.grad_clip)
         else:
             norm = clip_grad_norm_([p for g in opt.param_groups for p in g["params"]], qc.grad_clip)

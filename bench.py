@@ -472,7 +472,7 @@ def qad_main(args):
         "scaling": "strong", "vs_baseline": round(value / QAD_BASELINE_TOKS, 3), "dtype": "bf16",
         "data": "synthetic (random-init student; uniform random tokens; random valid top-k teacher targets)",
         "config": {"model": "qwen3next_80b-shaped student, 48L, 320 INT3 experts (STE scales), FP8 QAT dense",
-                   "global_batch": args.global_batch, "seq_len": T, "parallelism": f"dp{world}+sharded-adamw",
+                   "global_batch": args.global_batch, "seq_len": T, "parallelism": f"dp{world}+" + ("fused-zero-adamw" if type(opt).__name__ == "FusedShardedAdamW" else "sharded-adamw"),
                    "loss": f"forward KL, teacher top-{args.topk} + tail", "layers": args.layers,
                    "optimizer": "bf16-state AdamW", "l2": "inputs larger than L2 (weights and activations)"},
         "loss": round(last_loss, 5),

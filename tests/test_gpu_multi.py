@@ -23,3 +23,9 @@ def test_expert_parallel_moe_matches_single_gpu_on_two_ranks():
     r = _torchrun("tests/ep_worker.py", 2)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("rel_err") == 2
+
+
+def test_fused_zero_optimizer_matches_nccl_sharded_adamw_on_two_ranks():
+    r = _torchrun("tests/zero_worker.py", 2)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("ms_fused") == 2
