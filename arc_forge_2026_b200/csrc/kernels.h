@@ -207,7 +207,6 @@ int zero_norm_publish(const ZeroArgs& a, const float* partials, int n, cudaStrea
 int zero_adamw(const ZeroArgs& a, size_t param_off, size_t chunk, const float* g, void* m, void* v, size_t n_valid,
                float lr, float b1, float b2, float eps, float wd, int step, float max_norm, int blocks,
                cudaStream_t st);
-int zero_ag(const ZeroArgs& a, size_t param_off, size_t chunk, int blocks, cudaStream_t st);
 
 
 // sampling.cu

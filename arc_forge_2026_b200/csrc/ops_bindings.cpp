@@ -394,9 +394,6 @@ struct ZeroCtx {
                              stream()),
              "zero_adamw");
   }
-  void ag(int64_t param_off, int64_t chunk, int64_t blocks) {
-    check_rc(afb::zero_ag(a, param_off, chunk, (int)blocks, stream()), "zero_ag");
-  }
 };
 
 // HiSparse (see hisparse.cu): the host pools, GPU pools and residency tables of every QSA layer.
@@ -710,8 +707,7 @@ void register_kernel_ops(pybind11::module& m) {
       .def("wait", &ZeroCtx::wait)
       .def("rs", &ZeroCtx::rs)
       .def("norm_publish", &ZeroCtx::norm_publish)
-      .def("adamw", &ZeroCtx::adamw)
-      .def("ag", &ZeroCtx::ag);
+      .def("adamw", &ZeroCtx::adamw);
   py::class_<HsCtx>(m, "HsCtx")
       .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, bool, const at::Tensor&,
                     const std::vector<std::vector<int64_t>>&>())

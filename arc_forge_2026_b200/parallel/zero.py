@@ -17,7 +17,7 @@ from ..ops._ext import C, check_status
 from .ep import MAX_RANKS, _align
 
 ZERO_GRADS, ZERO_NORM, ZERO_PARAMS = 0, 1, 2
-RS_BLOCKS = 296  # blocks of the reduce-scatter / update / all-gather grids (2 per SM)
+RS_BLOCKS = 148 * 8  # blocks of the reduce-scatter and update grids: a full SM of 256-thread blocks each
 
 
 class FusedShardedAdamW:
@@ -36,7 +36,7 @@ class FusedShardedAdamW:
         for g in groups:
             params = list(g["params"])
             n = sum(p.numel() for p in params)
-            chunk = (math.ceil(n / self.world) + 3) // 4 * 4  # 16-byte vectors in the all-gather
+            chunk = (math.ceil(n / self.world) + 3) // 4 * 4  # 16-byte vectors in the exchange kernels
             size = chunk * self.world * 4
             specs.append((params, g["lr"], n, chunk, off, off + _align(size)))
             off += 2 * _align(size)
@@ -104,10 +104,8 @@ class FusedShardedAdamW:
             g["step"] += 1
             c.adamw(g["p_off"], g["chunk"], g["shard"], g["m"], g["v"], g["n"], g["lr"], b1, b2, self.eps, self.wd,
                     g["step"], max_norm, RS_BLOCKS)
-        c.signal(ZERO_PARAMS)
+        c.signal(ZERO_PARAMS)  # the update stored every rank's new shard into every heap
         c.wait(ZERO_PARAMS)
-        for g in self.groups:
-            c.ag(g["p_off"], g["chunk"], RS_BLOCKS)
         if not sync:
             return self.norm
         norm = float(self.norm.item())

@@ -453,12 +453,17 @@ def qad_main(args):
     n_ours, n_all = count_launches(lambda: one_step(dev_in), census, ktime)
     if args.census and rank == 0:  # device time by framework op (which PyTorch ops the elementwise kernels are)
         from torch.profiler import ProfilerActivity, profile
-        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
             one_step(dev_in)
             torch.cuda.synchronize()
         rows = sorted(prof.key_averages(), key=lambda e: -e.self_device_time_total)[:30]
         for e in rows:
             print(f"op ms/step {e.self_device_time_total / 1000:9.1f}  x{e.count:6d}  {e.key[:80]}", file=sys.stderr)
+        rows = sorted(prof.key_averages(group_by_input_shape=True), key=lambda e: -e.self_device_time_total)[:60]
+        for e in rows:
+            if e.key.startswith("aten::"):
+                print(f"op+shape ms/step {e.self_device_time_total / 1000:9.1f}  x{e.count:6d}  {e.key[:40]}  "
+                      f"{str(e.input_shapes)[:140]}", file=sys.stderr)
     if rank == 0:  # where one step's launches and kernel time go, for the log (profiler time: not a result)
         for name, cnt in census.most_common(12):
             print(f"launches/step {cnt:8d}  {name}", file=sys.stderr)
