@@ -161,8 +161,14 @@ struct GdnScanArgs {
   float* final_state = nullptr;   // [BH, Dk, Dv] optional
   uint32_t* status = nullptr;     // bounded-wait error bits
   int BH = 0, n_chunks = 0, C = 64, Dk = 128, Dv = 128;
+  // tensor-core path (Dk = 128): m1 / m2 as bf16 [BH, n, 64, 128] tiles in the XOR-swizzled layout of
+  // gdn_pack_tiles (16-byte chunk cc of row r stored at chunk cc ^ (r & 7)); null selects the fp32 SIMT path
+  const __nv_bfloat16* m1h = nullptr;
+  const __nv_bfloat16* m2h = nullptr;
 };
 int gdn_chunk_scan(const GdnScanArgs& a, bool reverse, cudaStream_t st);
+// fp32 [tiles, 64, 128] -> bf16 swizzled tiles for the tensor-core scan
+int gdn_pack_tiles(const float* src, __nv_bfloat16* dst, int64_t tiles, cudaStream_t st);
 
 // ep.cu: expert-parallel MoE exchange over peer memory (symmetric heap regions at equal offsets on every rank)
 constexpr int EP_MAX_RANKS = 8;

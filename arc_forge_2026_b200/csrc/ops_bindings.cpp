@@ -502,7 +502,8 @@ void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const
 
 void gdn_chunk_scan_op(const at::Tensor& m1, const at::Tensor& m2, const at::Tensor& y,
                        const c10::optional<at::Tensor>& qm, const at::Tensor& last, const c10::optional<at::Tensor>& init,
-                       at::Tensor& states, at::Tensor& x, c10::optional<at::Tensor> final_state, bool reverse) {
+                       at::Tensor& states, at::Tensor& x, c10::optional<at::Tensor> final_state, bool reverse,
+                       bool precise) {
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&m1, &m2, &y, &last, &states, &x}) {
     AFB_CHECK_CUDA(*t);
     AFB_CHECK_DT(*t, at::kFloat);
@@ -539,6 +540,16 @@ void gdn_chunk_scan_op(const at::Tensor& m1, const at::Tensor& m2, const at::Ten
   a.x = ptr<float>(x);
   a.final_state = optr<float>(final_state);
   a.status = status_ptr(m1.get_device());
+  at::Tensor m1h, m2h;
+  if (!precise && a.Dk == 128 && a.C == 64 && a.Dv % 32 == 0) {  // tensor-core path: bf16 swizzled M1 / M2 tiles
+    const int64_t tiles = (int64_t)a.BH * a.n_chunks;
+    m1h = at::empty({tiles, 64, 128}, m1.options().dtype(at::kBFloat16));
+    m2h = at::empty_like(m1h);
+    check_rc(afb::gdn_pack_tiles(a.m1, ptr<__nv_bfloat16>(m1h), tiles, stream()), "gdn_pack_tiles");
+    check_rc(afb::gdn_pack_tiles(a.m2, ptr<__nv_bfloat16>(m2h), tiles, stream()), "gdn_pack_tiles");
+    a.m1h = ptr<__nv_bfloat16>(m1h);
+    a.m2h = ptr<__nv_bfloat16>(m2h);
+  }
   check_rc(afb::gdn_chunk_scan(a, reverse, stream()), "gdn_chunk_scan");
 }
 
@@ -693,7 +704,9 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("build_window", &build_window_op);
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
-  m.def("gdn_chunk_scan", &gdn_chunk_scan_op);
+  m.def("gdn_chunk_scan", &gdn_chunk_scan_op, py::arg("m1"), py::arg("m2"), py::arg("y"), py::arg("qm"),
+        py::arg("last"), py::arg("init"), py::arg("states"), py::arg("x"), py::arg("final_state"), py::arg("reverse"),
+        py::arg("precise") = false);
   m.def("paged_attention", &paged_attention_op, py::arg("q"), py::arg("kcache"), py::arg("vcache"),
         py::arg("block_table"), py::arg("seq_lens"), py::arg("q_per_seq"), py::arg("scale"), py::arg("out"),
         py::arg("gate"), py::arg("gate_ld"), py::arg("gate_head_stride"), py::arg("splits"),

@@ -21,11 +21,13 @@ from __future__ import annotations
 import torch
 
 
-def _scan(m1, m2, y, qm, last, init, reverse: bool):
+def _scan(m1, m2, y, qm, last, init, reverse: bool, precise: bool = False):
     """X = Y + s1 * M1 St ; St <- e^{last} St (+ Qm) + s2 * M2^T X over chunks (forward, or reverse order).
 
     m1, m2 [BH, n, C, Dk]; y [BH, n, C, Dv]; qm [BH, n, Dk, Dv] or None; last [BH, n]; init [BH, Dk, Dv] or None.
-    Returns (states before each step [BH, n, Dk, Dv], X [BH, n, C, Dv], final state [BH, Dk, Dv])."""
+    Returns (states before each step [BH, n, Dk, Dv], X [BH, n, C, Dv], final state [BH, Dk, Dv]).
+    On CUDA with Dk = 128 the scan runs on tensor cores with bf16 operands and fp32 accumulation (the precision
+    class of the chunk kernels the reference trains with); ``precise`` selects the fp32 SIMT kernel."""
     BH, n, C, Dk = m1.shape
     Dv = y.shape[-1]
     if m1.is_cuda:
@@ -36,7 +38,7 @@ def _scan(m1, m2, y, qm, last, init, reverse: bool):
         states = torch.empty(BH, n, Dk, Dv, device=m1.device, dtype=torch.float32)
         x = torch.empty_like(y)
         final = torch.empty(BH, Dk, Dv, device=m1.device, dtype=torch.float32)
-        ext().gdn_chunk_scan(m1, m2, y, qm, last, init, states, x, final, reverse)
+        ext().gdn_chunk_scan(m1, m2, y, qm, last, init, states, x, final, reverse, precise)
         return states, x, final
     s1, s2 = (1.0, -1.0) if reverse else (-1.0, 1.0)
     St = torch.zeros(BH, Dk, Dv, dtype=y.dtype) if init is None else init.clone()
@@ -69,9 +71,10 @@ class _InterChunk(torch.autograd.Function):
         return D, attn, qd, kd, last
 
     @staticmethod
-    def forward(ctx, q, k, u, w, gc, init):
+    def forward(ctx, q, k, u, w, gc, init, precise=False):
         D, attn, qd, kd, last = _InterChunk._intra(q, k, gc)
-        states, vnew, final = _scan(w, kd, u, None, last, init, reverse=False)
+        states, vnew, final = _scan(w, kd, u, None, last, init, reverse=False, precise=precise)
+        ctx.precise = precise
         o = qd @ states + attn @ vnew
         ctx.save_for_backward(q, k, w, gc, states, vnew)
         ctx.has_init = init is not None
@@ -84,7 +87,8 @@ class _InterChunk(torch.autograd.Function):
         do = do.float().contiguous()
         P = attn.transpose(-1, -2) @ do                      # attn^T dO
         Qm = qd.transpose(-1, -2) @ do                       # qd^T dO
-        dnext, dv, dS0 = _scan(kd, w, P, Qm, last, dfinal if dfinal is not None else None, reverse=True)
+        dnext, dv, dS0 = _scan(kd, w, P, Qm, last, dfinal if dfinal is not None else None, reverse=True,
+                               precise=ctx.precise)
         # dnext[:, i] = dS_{i+1}; dv = dL/du = dL/d(vnew)
         dw = -(dv @ states.transpose(-1, -2))
         dqd = do @ states.transpose(-1, -2)
@@ -101,11 +105,13 @@ class _InterChunk(torch.autograd.Function):
         dgc = dgc - E
         dlast = E.sum(-1) + last.exp() * (dnext * states).sum((-1, -2))
         dgc = torch.cat([dgc[..., :-1], (dgc[..., -1] + dlast)[..., None]], -1)
-        return dq, dk, dv, dw, dgc, (dS0 if ctx.has_init else None)
+        return dq, dk, dv, dw, dgc, (dS0 if ctx.has_init else None), None
 
 
-def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None):
-    """q, k [B, T, H, Dk] (normalised, q scaled), v [B, T, H, Dv], g/beta [B, T, H] -> (o [B,T,H,Dv], state)."""
+def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None, precise: bool = False):
+    """q, k [B, T, H, Dk] (normalised, q scaled), v [B, T, H, Dv], g/beta [B, T, H] -> (o [B,T,H,Dv], state).
+
+    ``precise`` keeps the inter-chunk scan in fp32 on CUDA (default: tensor cores, bf16 operands)."""
     B, T, H, Dk = k.shape
     Dv = v.shape[-1]
     dt = torch.float32
@@ -133,7 +139,7 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None):
     u = A @ (v * beta[..., None])                    # pseudo-values
     w = A @ (k_beta * gc.exp()[..., None])          # decayed keys
     init = None if state is None else state.to(dt).reshape(B * H, Dk, Dv)
-    o, S = _InterChunk.apply(q, k, u, w, gc, init)
+    o, S = _InterChunk.apply(q, k, u, w, gc, init, precise)
     o = o.reshape(B, H, n * chunk, Dv)[:, :, :T]
     return o.transpose(1, 2), S.reshape(B, H, Dk, Dv)
 

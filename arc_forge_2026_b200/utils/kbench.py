@@ -2,6 +2,7 @@
 
     python -m arc_forge_2026_b200.utils.kbench moe      # INT3 w13/w2 expert GEMMs at the verify-step shape
     python -m arc_forge_2026_b200.utils.kbench gemm     # dense bf16 GEMMs of the decode step
+    python -m arc_forge_2026_b200.utils.kbench gdn_scan # chunked-GDN inter-chunk scan at the QAD shape
 
 Prints one JSON line per kernel: time, bytes, FLOPs and the fraction of MEASURED_PEAKS.json.
 """
@@ -157,9 +158,40 @@ def bench_attn(S=128, T=5, seed=0):
              "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)}]
 
 
+def bench_gdn_scan(BH=32, n=256, steps=(False, True)):
+    """Inter-chunk scan of one GDN layer at seq 16,384 (256 chunks of 64), 32 value heads, Dk = Dv = 128: the
+    tensor-core kernel and the fp32 SIMT kernel, forward and reverse (the reverse adds the Qm term)."""
+    from ..ops import C
+    peaks = load_peaks()
+    dev = "cuda"
+    Dk = Dv = 128
+    m1 = torch.randn(BH, n, 64, Dk, device=dev) * 0.05
+    m2 = torch.randn(BH, n, 64, Dk, device=dev) * 0.05
+    y = torch.randn(BH, n, 64, Dv, device=dev)
+    qm = torch.randn(BH, n, Dk, Dv, device=dev)
+    last = -torch.rand(BH, n, device=dev)
+    states = torch.empty(BH, n, Dk, Dv, device=dev)
+    x = torch.empty_like(y)
+    fin = torch.empty(BH, Dk, Dv, device=dev)
+    c = C()
+    res = []
+    flops = 2 * 2 * BH * n * 64 * Dk * Dv
+    for reverse in steps:
+        for precise in (False, True):
+            q = qm if reverse else None
+            ms = time_cuda(lambda: c.gdn_chunk_scan(m1, m2, y, q, last, None, states, x, fin, reverse, precise),
+                           iters=5)
+            byts = m1.nbytes + m2.nbytes + y.nbytes + x.nbytes + states.nbytes + (qm.nbytes if reverse else 0)
+            res.append({"kernel": "gdn_chunk_scan" + ("_fp32" if precise else "_tc") + ("_rev" if reverse else ""),
+                        "BH": BH, "chunks": n, "ms": round(ms, 4), "us_per_step": round(ms * 1000 / n, 2),
+                        "tflops": round(flops / ms / 1e9, 1), "gbs": round(byts / ms / 1e6, 1),
+                        "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)})
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "all"])
     ap.add_argument("--T", type=int, default=640)
     a = ap.parse_args()
     res = []
@@ -171,6 +203,8 @@ def main():
         res += bench_gdn()
     if a.what in ("attn", "all"):
         res += bench_attn()
+    if a.what in ("gdn_scan", "all"):
+        res += bench_gdn_scan()
     for r in res:
         print(json.dumps(r))
 

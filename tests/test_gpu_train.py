@@ -98,6 +98,7 @@ def test_tiny_qad_training_on_gpu():
 
 
 def test_gdn_chunk_scan_kernel_matches_cpu_scan():
+    """fp32 SIMT kernel to 1e-5; the tensor-core kernel (bf16 operands, fp32 accumulation) to 2e-2."""
     from arc_forge_2026_b200.train.gdn_chunk import _scan
     g = torch.Generator().manual_seed(11)
     BH, n, Cc, Dk, Dv = 3, 5, 64, 128, 128
@@ -109,10 +110,12 @@ def test_gdn_chunk_scan_kernel_matches_cpu_scan():
     init = torch.randn(BH, Dk, Dv, generator=g)
     for reverse, q in ((False, None), (True, qm)):
         ref = _scan(m1, m2, y, q, last, init, reverse)
-        got = _scan(m1.to(dev), m2.to(dev), y.to(dev), None if q is None else q.to(dev), last.to(dev), init.to(dev),
-                    reverse)
-        for a, b in zip(got, ref):
-            assert _rel(a.cpu(), b) < 1e-5
+        for precise, tol in ((True, 1e-5), (False, 2e-2)):
+            got = _scan(m1.to(dev), m2.to(dev), y.to(dev), None if q is None else q.to(dev), last.to(dev),
+                        init.to(dev), reverse, precise=precise)
+            for a, b in zip(got, ref):
+                assert _rel(a.cpu(), b) < tol, (reverse, precise, _rel(a.cpu(), b))
+    check_status()
 
 
 def test_chunked_gdn_gradients_on_gpu_match_unrolled_loop():
@@ -125,14 +128,16 @@ def test_chunked_gdn_gradients_on_gpu_match_unrolled_loop():
     gate = -torch.rand(B, T, H, generator=g) * 0.3
     beta = torch.rand(B, T, H, generator=g)
     dout = torch.randn(B, T, H, Dv, generator=g)
-    grads = []
-    for fn in (chunk_gated_delta_rule, chunk_gated_delta_rule_loop):
+
+    def run(fn, **kw):
         ins = [t.to(dev).requires_grad_(True) for t in (q, k, v, gate, beta)]
-        o, _ = fn(*ins)
+        o, _ = fn(*ins, **kw)
         (o * dout.to(dev)).sum().backward()
-        grads.append([o.detach()] + [t.grad for t in ins])
-    for a, b in zip(*grads):
-        assert _rel(a, b) < 1e-4
+        return [o.detach()] + [t.grad for t in ins]
+    ref = run(chunk_gated_delta_rule_loop)
+    for precise, tol in ((True, 1e-4), (False, 3e-2)):
+        for a, b in zip(run(chunk_gated_delta_rule, precise=precise), ref):
+            assert _rel(a, b) < tol, (precise, _rel(a, b))
 
 
 def test_native_fp8_teacher_targets_agree_with_its_prefill():
