@@ -170,6 +170,45 @@ int gdn_chunk_scan(const GdnScanArgs& a, bool reverse, cudaStream_t st);
 // fp32 [tiles, 64, 128] -> bf16 swizzled tiles for the tensor-core scan
 int gdn_pack_tiles(const float* src, __nv_bfloat16* dst, int64_t tiles, cudaStream_t st);
 
+// gdn_chunk_train.cu: the per-chunk work of the chunked gated delta rule for training (Dk = Dv = 128, chunk 64),
+// forward and backward, around the inter-chunk scan above. Grouped values: value head h reads key head h / (Hv/Hk).
+struct GdnTrainArgs {
+  const __nv_bfloat16* q = nullptr;  // [B, T, Hk, 128] (normalised, scaled)
+  const __nv_bfloat16* k = nullptr;  // [B, T, Hk, 128] (normalised)
+  const __nv_bfloat16* v = nullptr;  // [B, T, Hv, 128]
+  const float* g = nullptr;          // [B, T, Hv] log decay
+  const float* beta = nullptr;       // [B, T, Hv]
+  int B = 0, T = 0, Hk = 0, Hv = 0, n = 0;  // n = ceil(T / 64) chunks
+  // forward products (per sequence-head bh = b * Hv + h and chunk)
+  __nv_bfloat16* w_tiles = nullptr;   // [BH, n, 64, 128] swizzled (scan operand)
+  __nv_bfloat16* kd_tiles = nullptr;  // [BH, n, 64, 128] swizzled
+  float* u = nullptr;                 // [BH, n, 64, 128]
+  float* gc = nullptr;                // [BH, n, 64] within-chunk cumulative log decay
+  float* last = nullptr;              // [BH, n]
+  float* A = nullptr;                 // [BH, n, 64, 64] (I + beta k k^T decay, strictly lower)^-1
+  const float* states = nullptr;      // [BH, n, 128, 128] state before each chunk (from the scan)
+  const float* vnew = nullptr;        // [BH, n, 64, 128] u - w S (from the scan)
+  __nv_bfloat16* o = nullptr;         // [B, T, Hv, 128]
+  // backward
+  const __nv_bfloat16* dout = nullptr;  // [B, T, Hv, 128]
+  float* P = nullptr;                   // [BH, n, 64, 128] attn^T dO
+  float* Qm = nullptr;                  // [BH, n, 128, 128] (q e^{gc})^T dO
+  const float* dnext = nullptr;         // [BH, n, 128, 128] dL/dS after each chunk (reverse scan states)
+  const float* du = nullptr;            // [BH, n, 64, 128] dL/du (reverse scan X)
+  float* dw = nullptr;                  // [BH, n, 64, 128]
+  float* dgc = nullptr;                 // [BH, n, 64] dL/dgc of the inter-chunk part
+  float* dq = nullptr;                  // [B, T, Hv, 128] per value head
+  float* dk = nullptr;                  // [B, T, Hv, 128] per value head (inter-chunk part, then final)
+  float* dv = nullptr;                  // [B, T, Hv, 128]
+  float* dg = nullptr;                  // [B, T, Hv]
+  float* dbeta = nullptr;               // [B, T, Hv]
+};
+int gdn_train_fwd_prep(const GdnTrainArgs& a, cudaStream_t st);
+int gdn_train_fwd_out(const GdnTrainArgs& a, cudaStream_t st);
+int gdn_train_bwd_prep(const GdnTrainArgs& a, cudaStream_t st);
+int gdn_train_bwd_inter(const GdnTrainArgs& a, cudaStream_t st);
+int gdn_train_bwd_wy(const GdnTrainArgs& a, cudaStream_t st);
+
 // ep.cu: expert-parallel MoE exchange over peer memory (symmetric heap regions at equal offsets on every rank)
 constexpr int EP_MAX_RANKS = 8;
 constexpr int EP_DISPATCH = 0, EP_COMBINE = 1;

@@ -553,6 +553,118 @@ void gdn_chunk_scan_op(const at::Tensor& m1, const at::Tensor& m2, const at::Ten
   check_rc(afb::gdn_chunk_scan(a, reverse, stream()), "gdn_chunk_scan");
 }
 
+// chunked-GDN training stages (gdn_chunk_train.cu). `t` holds, in order (None where a stage does not use it):
+// q, k, v, g, beta, w_tiles, kd_tiles, u, gc, last, A, states, vnew, o, dout, P, Qm, dnext, du, dw, dgc, dq, dk, dv,
+// dg, dbeta
+void gdn_train_op(int64_t stage, const std::vector<c10::optional<at::Tensor>>& t, int64_t B, int64_t T, int64_t Hk,
+                  int64_t Hv) {
+  TORCH_CHECK(t.size() == 26, "gdn_train: 26 tensor slots");
+  for (const auto& x : t)
+    if (x.has_value()) {
+      AFB_CHECK_CUDA(x.value());
+      AFB_CHECK_CONTIG(x.value());
+    }
+  auto bf = [&](int i) -> __nv_bfloat16* {
+    if (!t[i].has_value()) return nullptr;
+    TORCH_CHECK(t[i]->scalar_type() == at::kBFloat16, "gdn_train: slot ", i, " must be bf16");
+    return ptr<__nv_bfloat16>(t[i].value());
+  };
+  auto f32 = [&](int i) -> float* {
+    if (!t[i].has_value()) return nullptr;
+    TORCH_CHECK(t[i]->scalar_type() == at::kFloat, "gdn_train: slot ", i, " must be fp32");
+    return ptr<float>(t[i].value());
+  };
+  afb::GdnTrainArgs a;
+  a.q = bf(0);
+  a.k = bf(1);
+  a.v = bf(2);
+  a.g = f32(3);
+  a.beta = f32(4);
+  a.w_tiles = bf(5);
+  a.kd_tiles = bf(6);
+  a.u = f32(7);
+  a.gc = f32(8);
+  a.last = f32(9);
+  a.A = f32(10);
+  a.states = f32(11);
+  a.vnew = f32(12);
+  a.o = bf(13);
+  a.dout = bf(14);
+  a.P = f32(15);
+  a.Qm = f32(16);
+  a.dnext = f32(17);
+  a.du = f32(18);
+  a.dw = f32(19);
+  a.dgc = f32(20);
+  a.dq = f32(21);
+  a.dk = f32(22);
+  a.dv = f32(23);
+  a.dg = f32(24);
+  a.dbeta = f32(25);
+  a.B = (int)B;
+  a.T = (int)T;
+  a.Hk = (int)Hk;
+  a.Hv = (int)Hv;
+  a.n = (int)((T + 63) / 64);
+  TORCH_CHECK(Hk >= 1 && Hv % Hk == 0, "gdn_train: Hv must be a multiple of Hk");
+  // every slot a stage reads or writes must be present
+  static const std::vector<std::vector<int>> need = {
+      {1, 2, 3, 4, 5, 6, 7, 8, 9, 10},          // fwd_prep
+      {0, 1, 8, 11, 12, 13},                    // fwd_out
+      {0, 1, 8, 14, 15, 16},                    // bwd_prep
+      {0, 1, 8, 11, 12, 14, 17, 18, 19, 20, 21, 22},  // bwd_inter
+      {1, 2, 4, 8, 10, 18, 19, 20, 22, 23, 24, 25}};  // bwd_wy
+  TORCH_CHECK(stage >= 0 && stage < 5, "gdn_train: stage 0..4");
+  for (int i : need[stage]) TORCH_CHECK(t[i].has_value(), "gdn_train stage ", stage, ": slot ", i, " missing");
+  int rc = 0;
+  switch (stage) {
+    case 0: rc = afb::gdn_train_fwd_prep(a, stream()); break;
+    case 1: rc = afb::gdn_train_fwd_out(a, stream()); break;
+    case 2: rc = afb::gdn_train_bwd_prep(a, stream()); break;
+    case 3: rc = afb::gdn_train_bwd_inter(a, stream()); break;
+    default: rc = afb::gdn_train_bwd_wy(a, stream()); break;
+  }
+  check_rc(rc, "gdn_train");
+}
+
+// the tensor-core scan on pre-swizzled bf16 tiles (written by the gdn_train forward prep)
+void gdn_chunk_scan_tiles_op(const at::Tensor& m1h, const at::Tensor& m2h, const at::Tensor& y,
+                             const c10::optional<at::Tensor>& qm, const at::Tensor& last,
+                             const c10::optional<at::Tensor>& init, at::Tensor& states, at::Tensor& x,
+                             c10::optional<at::Tensor> final_state, bool reverse) {
+  AFB_CHECK_DT(m1h, at::kBFloat16);
+  AFB_CHECK_DT(m2h, at::kBFloat16);
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&y, &last, &states, &x}) {
+    AFB_CHECK_CUDA(*t);
+    AFB_CHECK_DT(*t, at::kFloat);
+    AFB_CHECK_CONTIG(*t);
+  }
+  TORCH_CHECK(y.dim() == 4 && y.size(2) == 64 && y.size(3) % 32 == 0, "y [BH, n, 64, Dv]");
+  afb::GdnScanArgs a;
+  a.BH = y.size(0);
+  a.n_chunks = y.size(1);
+  a.C = 64;
+  a.Dk = 128;
+  a.Dv = y.size(3);
+  TORCH_CHECK(m1h.numel() == (int64_t)a.BH * a.n_chunks * 64 * 128 && m2h.numel() == m1h.numel(), "tile shapes");
+  TORCH_CHECK(last.numel() == (int64_t)a.BH * a.n_chunks, "last shape");
+  TORCH_CHECK(states.numel() == (int64_t)a.BH * a.n_chunks * 128 * a.Dv && x.sizes() == y.sizes(), "outputs");
+  if (qm) TORCH_CHECK(qm->numel() == states.numel() && qm->scalar_type() == at::kFloat, "qm");
+  if (init) TORCH_CHECK(init->numel() == (int64_t)a.BH * 128 * a.Dv && init->scalar_type() == at::kFloat, "init");
+  if (final_state) TORCH_CHECK(final_state->numel() == (int64_t)a.BH * 128 * a.Dv, "final shape");
+  a.m1h = ptr<__nv_bfloat16>(m1h);
+  a.m2h = ptr<__nv_bfloat16>(m2h);
+  a.y = ptr<float>(y);
+  a.qm = optr<float>(qm);
+  a.last = ptr<float>(last);
+  a.init = optr<float>(init);
+  a.states = ptr<float>(states);
+  a.x = ptr<float>(x);
+  a.final_state = optr<float>(final_state);
+  a.status = status_ptr(y.get_device());
+  check_rc(afb::gdn_chunk_scan(a, reverse, stream()), "gdn_chunk_scan_tiles");
+}
+
 void select_tokens_op(const at::Tensor& logits, int64_t V, at::Tensor& out, double temperature, int64_t seed,
                       c10::optional<at::Tensor> step) {
   AFB_CHECK_DT(logits, at::kBFloat16);
@@ -704,6 +816,8 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("build_window", &build_window_op);
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
+  m.def("gdn_train", &gdn_train_op);
+  m.def("gdn_chunk_scan_tiles", &gdn_chunk_scan_tiles_op);
   m.def("gdn_chunk_scan", &gdn_chunk_scan_op, py::arg("m1"), py::arg("m2"), py::arg("y"), py::arg("qm"),
         py::arg("last"), py::arg("init"), py::arg("states"), py::arg("x"), py::arg("final_state"), py::arg("reverse"),
         py::arg("precise") = false);

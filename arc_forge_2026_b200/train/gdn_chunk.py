@@ -108,10 +108,94 @@ class _InterChunk(torch.autograd.Function):
         return dq, dk, dv, dw, dgc, (dS0 if ctx.has_init else None), None
 
 
-def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None, precise: bool = False):
-    """q, k [B, T, H, Dk] (normalised, q scaled), v [B, T, H, Dv], g/beta [B, T, H] -> (o [B,T,H,Dv], state).
+class _GdnChunkNative(torch.autograd.Function):
+    """The whole chunked rule in native kernels (``csrc/gdn_chunk_train.cu`` around the tensor-core scan of
+    ``csrc/gdn_chunk.cu``): q, k [B, T, Hk, 128] bf16, v [B, T, Hv, 128] bf16 (value head h reads key head
+    h // (Hv / Hk): no repeat of q / k), g, beta [B, T, Hv] fp32 -> o [B, T, Hv, 128] bf16, final state
+    [B, Hv, 128, 128] fp32. Backward: attn^T dO / Qm, the reverse scan, then the inter-chunk and WY gradients."""
 
-    ``precise`` keeps the inter-chunk scan in fp32 on CUDA (default: tensor cores, bf16 operands)."""
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta):
+        from ..ops import C as ext
+        B, T, Hk, D = q.shape
+        Hv = v.shape[2]
+        n, BH = (T + 63) // 64, B * Hv
+        dev = q.device
+        f32 = dict(device=dev, dtype=torch.float32)
+        w_t = torch.empty(BH, n, 64, 128, device=dev, dtype=torch.bfloat16)
+        kd_t = torch.empty_like(w_t)
+        u = torch.empty(BH, n, 64, 128, **f32)
+        gc = torch.empty(BH, n, 64, **f32)
+        last = torch.empty(BH, n, **f32)
+        A = torch.empty(BH, n, 64, 64, **f32)
+        slots = [None] * 26
+        slots[0:11] = [q, k, v, g, beta, w_t, kd_t, u, gc, last, A]
+        c = ext()
+        c.gdn_train(0, slots, B, T, Hk, Hv)
+        states = torch.empty(BH, n, 128, 128, **f32)
+        vnew = torch.empty_like(u)
+        final = torch.empty(BH, 128, 128, **f32)
+        c.gdn_chunk_scan_tiles(w_t, kd_t, u, None, last, None, states, vnew, final, False)
+        o = torch.empty(B, T, Hv, 128, device=dev, dtype=torch.bfloat16)
+        slots[11:14] = [states, vnew, o]
+        c.gdn_train(1, slots, B, T, Hk, Hv)
+        ctx.save_for_backward(q, k, v, g, beta, w_t, kd_t, gc, last, A, states, vnew)
+        ctx.dims = (B, T, Hk, Hv)
+        return o, final.view(B, Hv, 128, 128)
+
+    @staticmethod
+    def backward(ctx, do, dfinal):
+        from ..ops import C as ext
+        q, k, v, g, beta, w_t, kd_t, gc, last, A, states, vnew = ctx.saved_tensors
+        B, T, Hk, Hv = ctx.dims
+        BH = B * Hv
+        c = ext()
+        do = (torch.zeros(B, T, Hv, 128, device=q.device, dtype=torch.bfloat16) if do is None
+              else do.to(torch.bfloat16).contiguous())
+        P, Qm = torch.empty_like(vnew), torch.empty_like(states)
+        slots = [None] * 26
+        slots[0:5] = [q, k, v, g, beta]
+        slots[8], slots[10], slots[11], slots[12] = gc, A, states, vnew
+        slots[14], slots[15], slots[16] = do, P, Qm
+        c.gdn_train(2, slots, B, T, Hk, Hv)
+        dnext, du = torch.empty_like(states), torch.empty_like(vnew)
+        ds0 = torch.empty(BH, 128, 128, device=q.device, dtype=torch.float32)
+        init = None if dfinal is None else dfinal.float().reshape(BH, 128, 128).contiguous()
+        c.gdn_chunk_scan_tiles(kd_t, w_t, P, Qm, last, init, dnext, du, ds0, True)
+        del P, Qm
+        f32 = dict(device=q.device, dtype=torch.float32)
+        dq = torch.empty(B, T, Hv, 128, **f32)
+        dk, dv = torch.empty_like(dq), torch.empty_like(dq)
+        dw, dgc = torch.empty_like(vnew), torch.empty_like(gc)
+        dg, dbeta = torch.empty(B, T, Hv, **f32), torch.empty(B, T, Hv, **f32)
+        slots[17:26] = [dnext, du, dw, dgc, dq, dk, dv, dg, dbeta]
+        c.gdn_train(3, slots, B, T, Hk, Hv)
+        c.gdn_train(4, slots, B, T, Hk, Hv)
+        rep = Hv // Hk
+        if rep > 1:
+            dq = dq.view(B, T, Hk, rep, 128).sum(3)
+            dk = dk.view(B, T, Hk, rep, 128).sum(3)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg, dbeta
+
+
+def _native_ok(q, k, v, g, chunk, state, precise) -> bool:
+    return (q.is_cuda and not precise and state is None and chunk == 64 and q.shape[-1] == 128
+            and v.shape[-1] == 128 and v.shape[2] % k.shape[2] == 0)
+
+
+def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None, precise: bool = False):
+    """q, k [B, T, Hk, Dk] (normalised, q scaled), v [B, T, Hv, Dv], g/beta [B, T, Hv] -> (o [B,T,Hv,Dv], state).
+
+    Grouped values: value head h uses key head h // (Hv / Hk). On CUDA with Dk = Dv = 128 and no initial state the
+    whole rule runs in the native kernels (bf16 operands, fp32 accumulation, o in bf16); ``precise`` keeps the
+    fp32 torch path with the fp32 scan."""
+    if _native_ok(q, k, v, g, chunk, state, precise):
+        bf = torch.bfloat16
+        return _GdnChunkNative.apply(q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(),
+                                     g.float().contiguous(), beta.float().contiguous())
+    if k.shape[2] != v.shape[2]:
+        rep = v.shape[2] // k.shape[2]
+        q, k = q.repeat_interleave(rep, 2), k.repeat_interleave(rep, 2)
     B, T, H, Dk = k.shape
     Dv = v.shape[-1]
     dt = torch.float32

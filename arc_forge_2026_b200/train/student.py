@@ -239,9 +239,8 @@ class StudentLayer(nn.Module):
         q = mixed[..., :nk].reshape(B, T, c.linear_num_key_heads, -1)
         k = mixed[..., nk:2 * nk].reshape(B, T, c.linear_num_key_heads, -1)
         v = mixed[..., 2 * nk:].reshape(B, T, c.linear_num_value_heads, -1)
-        rep = c.linear_num_value_heads // c.linear_num_key_heads
-        q = (R.l2norm(q) * c.linear_key_head_dim ** -0.5).repeat_interleave(rep, 2)
-        k = R.l2norm(k).repeat_interleave(rep, 2)
+        q = R.l2norm(q) * c.linear_key_head_dim ** -0.5  # grouped values: chunk_gated_delta_rule maps heads
+        k = R.l2norm(k)
         g, beta = R.gdn_gates(b, a, self.A_log, self.dt_bias)
         o, _ = chunk_gated_delta_rule(q, k, v, g, beta)
         o = R.gated_rms_norm(o.to(x.dtype), z.reshape(B, T, c.linear_num_value_heads, -1), self.g_norm, c.rms_norm_eps)

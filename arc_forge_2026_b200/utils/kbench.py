@@ -3,6 +3,7 @@
     python -m arc_forge_2026_b200.utils.kbench moe      # INT3 w13/w2 expert GEMMs at the verify-step shape
     python -m arc_forge_2026_b200.utils.kbench gemm     # dense bf16 GEMMs of the decode step
     python -m arc_forge_2026_b200.utils.kbench gdn_scan # chunked-GDN inter-chunk scan at the QAD shape
+    python -m arc_forge_2026_b200.utils.kbench gdn_train # chunked-GDN layer forward + backward at the QAD shape
 
 Prints one JSON line per kernel: time, bytes, FLOPs and the fraction of MEASURED_PEAKS.json.
 """
@@ -189,9 +190,39 @@ def bench_gdn_scan(BH=32, n=256, steps=(False, True)):
     return res
 
 
+def bench_gdn_train(B=1, T=16384, Hk=16, Hv=32):
+    """One GDN layer's chunked rule, forward and forward + backward, at seq 16,384 (the QAD shape): the native
+    kernels against the torch path with the fp32 scan."""
+    from ..train.gdn_chunk import chunk_gated_delta_rule
+    dev = "cuda"
+    D = 128
+    q = (torch.nn.functional.normalize(torch.randn(B, T, Hk, D, device=dev), dim=-1) * D ** -0.5).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, device=dev), dim=-1).bfloat16()
+    v = torch.randn(B, T, Hv, D, device=dev).bfloat16()
+    gate = -torch.rand(B, T, Hv, device=dev) * 0.3
+    beta = torch.rand(B, T, Hv, device=dev)
+    dout = torch.randn(B, T, Hv, D, device=dev).bfloat16()
+    res = []
+    for precise in (False, True):
+        ins = [t.clone().requires_grad_(True) for t in (q, k, v, gate, beta)]
+
+        def fwd():
+            with torch.no_grad():
+                chunk_gated_delta_rule(*ins, precise=precise)
+
+        def fwd_bwd():
+            o, _ = chunk_gated_delta_rule(*ins, precise=precise)
+            o.backward(dout.to(o.dtype))
+        ms_f = time_cuda(fwd, iters=5, flush_bytes=1 << 20)
+        ms_fb = time_cuda(fwd_bwd, iters=5, flush_bytes=1 << 20)
+        res.append({"kernel": "gdn_chunk_layer" + ("_torch_fp32scan" if precise else "_native"), "T": T, "Hv": Hv,
+                    "ms_fwd": round(ms_f, 3), "ms_fwd_bwd": round(ms_fb, 3)})
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "all"])
     ap.add_argument("--T", type=int, default=640)
     a = ap.parse_args()
     res = []
@@ -205,6 +236,8 @@ def main():
         res += bench_attn()
     if a.what in ("gdn_scan", "all"):
         res += bench_gdn_scan()
+    if a.what in ("gdn_train", "all"):
+        res += bench_gdn_train()
     for r in res:
         print(json.dumps(r))
 

@@ -140,6 +140,38 @@ def test_chunked_gdn_gradients_on_gpu_match_unrolled_loop():
             assert _rel(a, b) < tol, (precise, _rel(a, b))
 
 
+def test_native_chunked_gdn_matches_fp32_oracle():
+    """The native chunk kernels (grouped values, T not a multiple of 64, B > 1, a final-state gradient) against the
+    fp32 recurrence on the same bf16-rounded inputs: outputs and every input gradient."""
+    from arc_forge_2026_b200.train.gdn_chunk import chunk_gated_delta_rule, chunk_gated_delta_rule_loop
+    g = torch.Generator().manual_seed(13)
+    B, T, Hk, Hv, D = 2, 200, 2, 4, 128
+    rep = Hv // Hk
+    q = (torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1) * D ** -0.5).bfloat16().float()
+    k = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1).bfloat16().float()
+    v = torch.randn(B, T, Hv, D, generator=g).bfloat16().float()
+    gate = -torch.rand(B, T, Hv, generator=g) * 0.3
+    beta = torch.rand(B, T, Hv, generator=g)
+    dout = torch.randn(B, T, Hv, D, generator=g)
+    dS = torch.randn(B, Hv, D, D, generator=g) * 0.1
+
+    def run(native):
+        ins = [t.to(dev).requires_grad_(True) for t in (q, k, v, gate, beta)]
+        if native:
+            o, S = chunk_gated_delta_rule(ins[0].bfloat16(), ins[1].bfloat16(), ins[2].bfloat16(), ins[3], ins[4])
+        else:
+            o, S = chunk_gated_delta_rule_loop(ins[0].repeat_interleave(rep, 2), ins[1].repeat_interleave(rep, 2),
+                                               ins[2], ins[3], ins[4])
+        ((o.float() * dout.to(dev)).sum() + (S.float() * dS.to(dev)).sum()).backward()
+        return [o.detach().float(), S.detach().float()] + [t.grad.float() for t in ins]
+    got, ref = run(True), run(False)
+    torch.cuda.synchronize()
+    check_status()
+    names = ["o", "state", "dq", "dk", "dv", "dg", "dbeta"]
+    errs = {n: round(_rel(a, b), 5) for n, a, b in zip(names, got, ref)}
+    assert all(e < 3e-2 for e in errs.values()), errs
+
+
 def test_native_fp8_teacher_targets_agree_with_its_prefill():
     from arc_forge_2026_b200.config import ServeConfig, preset
     from arc_forge_2026_b200.models.hybrid import HybridModel
