@@ -209,6 +209,28 @@ int gdn_train_bwd_prep(const GdnTrainArgs& a, cudaStream_t st);
 int gdn_train_bwd_inter(const GdnTrainArgs& a, cudaStream_t st);
 int gdn_train_bwd_wy(const GdnTrainArgs& a, cudaStream_t st);
 
+// train_fused.cu: fused forward / backward of the student's element-wise and row-wise ops (bf16 I/O, fp32 math)
+int conv_silu_fwd(const void* x, int64_t ldx, const float* w, void* y, int B, int T, int Cc, cudaStream_t st);
+int conv_silu_bwd(const void* x, int64_t ldx, const float* w, const void* dy, void* dx, int B, int T, int Cc,
+                  cudaStream_t st);
+// row r of a strided view: (r / inner) * ld_outer + (r % inner) * ld_inner elements
+struct RowMap {
+  int64_t inner = 1, ld_outer = 0, ld_inner = 0;
+};
+// z null: y = x rstd (1 + w); z given: y = x rstd w silu(z) (then dz is written in the backward); H = 128 .. 2048
+// (powers of two); x / z rows may be strided views, y / dy / dx / dz are contiguous
+int rmsnorm_train_fwd(const void* x, RowMap mx, const void* z, RowMap mz, const float* w, float eps, void* y,
+                      float* rstd, int64_t rows, int H, cudaStream_t st);
+int rmsnorm_train_bwd(const void* x, RowMap mx, const void* z, RowMap mz, const float* w, const float* rstd,
+                      const void* dy, void* dx, void* dz, int64_t rows, int H, cudaStream_t st);
+int swiglu_train_fwd(const void* gu, void* h, int64_t rows, int I, cudaStream_t st);
+int swiglu_train_bwd(const void* gu, const void* dh, void* dgu, int64_t rows, int I, cudaStream_t st);
+int moe_combine_train_fwd(const void* y, const int64_t* inv, const float* w, int K, void* out, int64_t T, int H,
+                          cudaStream_t st);
+int moe_combine_train_bwd(const void* y, const int64_t* inv, const float* w, int K, const void* dout, void* dy,
+                          float* dw, int64_t T, int H, cudaStream_t st);
+int moe_dispatch_train_bwd(const void* g, const int64_t* inv, int K, void* dx, int64_t T, int H, cudaStream_t st);
+
 // ep.cu: expert-parallel MoE exchange over peer memory (symmetric heap regions at equal offsets on every rank)
 constexpr int EP_MAX_RANKS = 8;
 constexpr int EP_DISPATCH = 0, EP_COMBINE = 1;

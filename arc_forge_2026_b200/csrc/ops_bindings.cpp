@@ -665,6 +665,127 @@ void gdn_chunk_scan_tiles_op(const at::Tensor& m1h, const at::Tensor& m2h, const
   check_rc(afb::gdn_chunk_scan(a, reverse, stream()), "gdn_chunk_scan_tiles");
 }
 
+// ---- fused training ops (train_fused.cu); row strides of the (possibly strided) inputs are taken from the tensors
+static void check_rows(const at::Tensor& t, const char* what) {
+  AFB_CHECK_CUDA(t);
+  AFB_CHECK_DT(t, at::kBFloat16);
+  TORCH_CHECK(t.stride(-1) == 1 && t.size(-1) % 4 == 0, what, ": inner stride must be 1");
+}
+// rows of a view [outer dims..., inner, H]: the outer dims must collapse to one stride
+static afb::RowMap row_map(const at::Tensor& t, const char* what) {
+  check_rows(t, what);
+  afb::RowMap m;
+  const int d = t.dim();
+  TORCH_CHECK(d >= 2, what, ": at least 2 dims");
+  m.inner = t.size(d - 2);
+  m.ld_inner = t.stride(d - 2);
+  m.ld_outer = d >= 3 ? t.stride(d - 3) : m.inner * m.ld_inner;
+  for (int i = 0; i + 3 < d; ++i)
+    TORCH_CHECK(t.stride(i) == t.stride(i + 1) * t.size(i + 1), what, ": outer dims must collapse");
+  TORCH_CHECK(m.ld_inner % 4 == 0 && m.ld_outer % 4 == 0, what, ": row strides must keep 8-byte alignment");
+  return m;
+}
+
+void conv_silu_op(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, c10::optional<at::Tensor> dy,
+                  c10::optional<at::Tensor> dx) {
+  check_rows(x, "conv_silu x");
+  TORCH_CHECK(x.dim() == 3 && x.stride(0) == x.size(1) * x.stride(1), "x [B, T, C] with evenly strided rows");
+  AFB_CHECK_DT(w, at::kFloat);
+  AFB_CHECK_CONTIG(w);
+  TORCH_CHECK(w.size(0) == x.size(2) && w.size(1) == 4, "w [C, 4]");
+  const int B = x.size(0), T = x.size(1), Cc = x.size(2);
+  if (dy) {
+    AFB_CHECK_CONTIG(dy.value());
+    AFB_CHECK_CONTIG(dx.value());
+    check_rc(afb::conv_silu_bwd(x.data_ptr(), x.stride(1), ptr<float>(w), dy->data_ptr(), dx->data_ptr(), B, T, Cc,
+                                stream()),
+             "conv_silu_bwd");
+  } else {
+    AFB_CHECK_CONTIG(y);
+    check_rc(afb::conv_silu_fwd(x.data_ptr(), x.stride(1), ptr<float>(w), y.data_ptr(), B, T, Cc, stream()),
+             "conv_silu_fwd");
+  }
+}
+
+void rmsnorm_train_op(const at::Tensor& x, c10::optional<at::Tensor> z, const at::Tensor& w, double eps,
+                      at::Tensor& y, at::Tensor& rstd, c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dx,
+                      c10::optional<at::Tensor> dz) {
+  const afb::RowMap mx = row_map(x, "rmsnorm x");
+  afb::RowMap mz;
+  if (z) {
+    mz = row_map(z.value(), "rmsnorm z");
+    TORCH_CHECK(z->sizes() == x.sizes(), "rmsnorm: z shape");
+  }
+  AFB_CHECK_DT(w, at::kFloat);
+  AFB_CHECK_CONTIG(w);
+  AFB_CHECK_DT(rstd, at::kFloat);
+  const int H = x.size(-1);
+  const int64_t rows = x.numel() / H;
+  TORCH_CHECK(w.numel() == H && rstd.numel() == rows, "rmsnorm shapes");
+  const void* zp = z ? z->data_ptr() : nullptr;
+  if (dy) {
+    AFB_CHECK_CONTIG(dy.value());
+    AFB_CHECK_CONTIG(dx.value());
+    if (z) AFB_CHECK_CONTIG(dz.value());
+    check_rc(afb::rmsnorm_train_bwd(x.data_ptr(), mx, zp, mz, ptr<float>(w), ptr<float>(rstd), dy->data_ptr(),
+                                    dx->data_ptr(), dz ? dz->data_ptr() : nullptr, rows, H, stream()),
+             "rmsnorm_train_bwd");
+  } else {
+    AFB_CHECK_CONTIG(y);
+    check_rc(afb::rmsnorm_train_fwd(x.data_ptr(), mx, zp, mz, ptr<float>(w), (float)eps, y.data_ptr(),
+                                    ptr<float>(rstd), rows, H, stream()),
+             "rmsnorm_train_fwd");
+  }
+}
+
+void swiglu_train_op(const at::Tensor& gu, at::Tensor& out, c10::optional<at::Tensor> dh) {
+  AFB_CHECK_DT(gu, at::kBFloat16);
+  AFB_CHECK_CONTIG(gu);
+  AFB_CHECK_CONTIG(out);
+  const int I = gu.size(-1) / 2;
+  const int64_t rows = gu.numel() / (2 * I);
+  if (dh) {
+    AFB_CHECK_CONTIG(dh.value());
+    check_rc(afb::swiglu_train_bwd(gu.data_ptr(), dh->data_ptr(), out.data_ptr(), rows, I, stream()), "swiglu_bwd");
+  } else {
+    check_rc(afb::swiglu_train_fwd(gu.data_ptr(), out.data_ptr(), rows, I, stream()), "swiglu_fwd");
+  }
+}
+
+void moe_combine_train_op(const at::Tensor& y, const at::Tensor& inv, const at::Tensor& w, at::Tensor& out,
+                          c10::optional<at::Tensor> dout, c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dw) {
+  AFB_CHECK_DT(y, at::kBFloat16);
+  AFB_CHECK_CONTIG(y);
+  AFB_CHECK_DT(inv, at::kLong);
+  AFB_CHECK_CONTIG(inv);
+  AFB_CHECK_DT(w, at::kFloat);
+  AFB_CHECK_CONTIG(w);
+  const int64_t T = w.size(0);
+  const int K = w.size(1), H = y.size(-1);
+  TORCH_CHECK(inv.numel() == T * K && y.size(0) == T * K, "combine shapes");
+  if (dout) {
+    check_rc(afb::moe_combine_train_bwd(y.data_ptr(), ptr<int64_t>(inv), ptr<float>(w), K, dout->data_ptr(),
+                                        dy->data_ptr(), ptr<float>(dw.value()), T, H, stream()),
+             "moe_combine_bwd");
+  } else {
+    check_rc(afb::moe_combine_train_fwd(y.data_ptr(), ptr<int64_t>(inv), ptr<float>(w), K, out.data_ptr(), T, H,
+                                        stream()),
+             "moe_combine_fwd");
+  }
+}
+
+void moe_dispatch_bwd_op(const at::Tensor& g, const at::Tensor& inv, int64_t K, at::Tensor& dx) {
+  AFB_CHECK_DT(g, at::kBFloat16);
+  AFB_CHECK_CONTIG(g);
+  AFB_CHECK_CONTIG(dx);
+  AFB_CHECK_DT(inv, at::kLong);
+  const int64_t T = dx.size(0);
+  TORCH_CHECK(inv.numel() == T * K && g.size(0) == T * K, "dispatch shapes");
+  check_rc(afb::moe_dispatch_train_bwd(g.data_ptr(), ptr<int64_t>(inv), (int)K, dx.data_ptr(), T, dx.size(-1),
+                                       stream()),
+           "moe_dispatch_bwd");
+}
+
 void select_tokens_op(const at::Tensor& logits, int64_t V, at::Tensor& out, double temperature, int64_t seed,
                       c10::optional<at::Tensor> step) {
   AFB_CHECK_DT(logits, at::kBFloat16);
@@ -817,6 +938,11 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
   m.def("gdn_train", &gdn_train_op);
+  m.def("conv_silu", &conv_silu_op);
+  m.def("rmsnorm_train", &rmsnorm_train_op);
+  m.def("swiglu_train", &swiglu_train_op);
+  m.def("moe_combine_train", &moe_combine_train_op);
+  m.def("moe_dispatch_bwd", &moe_dispatch_bwd_op);
   m.def("gdn_chunk_scan_tiles", &gdn_chunk_scan_tiles_op);
   m.def("gdn_chunk_scan", &gdn_chunk_scan_op, py::arg("m1"), py::arg("m2"), py::arg("y"), py::arg("qm"),
         py::arg("last"), py::arg("init"), py::arg("states"), py::arg("x"), py::arg("final_state"), py::arg("reverse"),

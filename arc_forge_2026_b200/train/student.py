@@ -21,6 +21,7 @@ from torch.utils.checkpoint import checkpoint
 from ..config import FULL, ModelConfig
 from ..models import reference as R
 from ..quant.int3_tiles import codes_to_tiles
+from . import fused
 from .fakequant import fp8_weight, int3_weight
 from .gdn_chunk import chunk_gated_delta_rule
 
@@ -42,21 +43,6 @@ def grouped_linear(x: torch.Tensor, w: torch.Tensor, counts: torch.Tensor) -> to
             outs.append(x[o:o + c] @ w[e].t())
         o += c
     return torch.cat(outs) if outs else x.new_zeros(0, w.shape[1])
-
-
-class _Permute(torch.autograd.Function):
-    """rows = x[perm] for a permutation ``perm`` (inverse ``inv``); the gradient is the inverse gather, so neither
-    direction needs an atomic scatter-add."""
-
-    @staticmethod
-    def forward(ctx, x, perm, inv):
-        ctx.save_for_backward(inv)
-        return x.index_select(0, perm)
-
-    @staticmethod
-    def backward(ctx, g):
-        (inv,) = ctx.saved_tensors
-        return g.index_select(0, inv), None, None
 
 
 class _Dispatch(torch.autograd.Function):
@@ -105,19 +91,17 @@ class StudentMoE(nn.Module):
         inv = torch.empty_like(order)
         inv[order] = torch.arange(order.numel(), device=order.device)
         counts = torch.bincount(flat, minlength=c.num_experts)
-        xs = _Dispatch.apply(x, order, inv, K)
+        xs = fused.moe_dispatch(x, order, inv, K)
+        if xs is None:
+            xs = _Dispatch.apply(x, order, inv, K)
         W13 = int3_weight(self.w13_scales, self.w13_codes).to(x.dtype)
-        h = grouped_linear(xs, W13, counts)
-        I = c.moe_intermediate_size
-        h = F.silu(h[:, :I].float()).to(x.dtype) * h[:, I:]
+        h = fused.swiglu(grouped_linear(xs, W13, counts))
         W2 = int3_weight(self.w2_scales, self.w2_codes).to(x.dtype)
         y = grouped_linear(h, W2, counts)
         # back to (token, k) order, weighted by the router and summed over k
-        y = _Permute.apply(y, inv, order).view(T, K, H)
-        out = (y * w.to(y.dtype)[..., None]).sum(1)
+        out = fused.moe_combine(y, inv, w)
         gu = x @ self.shared_w13.to(x.dtype).t()
-        Is = c.shared_expert_intermediate_size
-        sh = (F.silu(gu[:, :Is].float()).to(x.dtype) * gu[:, Is:]) @ self.shared_down.to(x.dtype).t()
+        sh = fused.swiglu(gu) @ self.shared_down.to(x.dtype).t()
         sg = torch.sigmoid(x.float() @ self.shared_expert_gate.t()).to(x.dtype)
         return out + sg * sh
 
@@ -220,7 +204,7 @@ class StudentLayer(nn.Module):
         q, gate = qg[..., :D], qg[..., D:].reshape(B, T, -1)
         k = self._lin("k_proj", x, True).view(B, T, c.num_kv_heads, D)
         v = self._lin("v_proj", x, True).view(B, T, c.num_kv_heads, D)
-        q, k = R.rms_norm(q, self.q_norm, c.rms_norm_eps), R.rms_norm(k, self.k_norm, c.rms_norm_eps)
+        q, k = fused.rms_norm(q, self.q_norm, c.rms_norm_eps), fused.rms_norm(k, self.k_norm, c.rms_norm_eps)
         cos, sin = R.rope_cos_sin(torch.arange(T, device=x.device), c.rotary_dim, c.rope_theta)
         q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
         o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
@@ -234,7 +218,7 @@ class StudentLayer(nn.Module):
         ba = self._lin("in_proj_ba", x, False)
         mixed, z = qkvz[..., : c.gdn_conv_dim], qkvz[..., c.gdn_conv_dim:]
         b, a = ba[..., : c.linear_num_value_heads], ba[..., c.linear_num_value_heads:]
-        mixed, _ = R.causal_conv1d(mixed, self.conv1d)
+        mixed = fused.conv_silu(mixed, self.conv1d)
         nk = c.linear_num_key_heads * c.linear_key_head_dim
         q = mixed[..., :nk].reshape(B, T, c.linear_num_key_heads, -1)
         k = mixed[..., nk:2 * nk].reshape(B, T, c.linear_num_key_heads, -1)
@@ -243,15 +227,16 @@ class StudentLayer(nn.Module):
         k = R.l2norm(k)
         g, beta = R.gdn_gates(b, a, self.A_log, self.dt_bias)
         o, _ = chunk_gated_delta_rule(q, k, v, g, beta)
-        o = R.gated_rms_norm(o.to(x.dtype), z.reshape(B, T, c.linear_num_value_heads, -1), self.g_norm, c.rms_norm_eps)
+        o = fused.gated_rms_norm(o.to(x.dtype), z.reshape(B, T, c.linear_num_value_heads, -1), self.g_norm,
+                                 c.rms_norm_eps)
         return self._lin("out_proj", o.reshape(B, T, -1), True)
 
     def forward(self, x):
         c = self.cfg
         B, T, H = x.shape
-        y = R.rms_norm(x, self.in_norm, c.rms_norm_eps)
+        y = fused.rms_norm(x, self.in_norm, c.rms_norm_eps)
         x = x + (self._attn(y, B, T) if self.kind == FULL else self._gdn(y, B, T))
-        y = R.rms_norm(x, self.post_norm, c.rms_norm_eps)
+        y = fused.rms_norm(x, self.post_norm, c.rms_norm_eps)
         return x + self.moe(y.reshape(B * T, H)).reshape(B, T, H)
 
 
@@ -289,7 +274,7 @@ class QADStudent(nn.Module):
                 x = checkpoint(L, x, use_reentrant=False)
             else:
                 x = L(x)
-        return R.rms_norm(x, self.final_norm, self.cfg.rms_norm_eps)
+        return fused.rms_norm(x, self.final_norm, self.cfg.rms_norm_eps)
 
 
 def random_student(cfg: ModelConfig, device, seed: int = 0, checkpoint_layers=True) -> "QADStudent":

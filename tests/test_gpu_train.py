@@ -172,6 +172,61 @@ def test_native_chunked_gdn_matches_fp32_oracle():
     assert all(e < 3e-2 for e in errs.values()), errs
 
 
+def test_fused_training_ops_match_torch():
+    """conv+SiLU (strided input), RMSNorm (H 2048 and a strided H 256 view), gated RMSNorm (H 128, strided z),
+    SwiGLU, MoE combine and dispatch: outputs and input gradients against the plain-torch math."""
+    from arc_forge_2026_b200.models import reference as R
+    from arc_forge_2026_b200.train import fused
+    g = torch.Generator().manual_seed(21)
+
+    def grads(fn, *ts):
+        ins = [t.detach().clone().requires_grad_(t.is_floating_point() and t.dtype != torch.float32 or
+                                                 getattr(t, "_want_grad", False)) for t in ts]
+        out = fn(*ins)
+        dout = torch.randn(out.shape, generator=torch.Generator().manual_seed(99)).to(dev).to(out.dtype)
+        (out.float() * dout.float()).sum().backward()
+        return [out.detach().float()] + [i.grad.float() for i in ins if i.grad is not None]
+
+    def check(name, fast, ref, *ts, tol=2e-2):
+        a, b = grads(fast, *ts), grads(ref, *ts)
+        assert len(a) == len(b), name
+        for i, (x, y) in enumerate(zip(a, b)):
+            assert _rel(x, y) < tol, (name, i, _rel(x, y))
+
+    B, T, C = 2, 150, 256
+    base = torch.randn(B, T, C + 64, generator=g).bfloat16().to(dev)
+    w4 = (torch.randn(C, 4, generator=g) * 0.3).to(dev)
+    check("conv", lambda x: fused.conv_silu(x[..., :C], w4), lambda x: R.causal_conv1d(x[..., :C], w4)[0], base)
+    x = torch.randn(B, T, 2048, generator=g).bfloat16().to(dev)
+    wn = (torch.randn(2048, generator=g) * 0.1).to(dev)
+    check("rms2048", lambda x: fused.rms_norm(x, wn, 1e-6), lambda x: R.rms_norm(x, wn, 1e-6), x)
+    qg = torch.randn(B, T, 4, 512, generator=g).bfloat16().to(dev)
+    w256 = (torch.randn(256, generator=g) * 0.1).to(dev)
+    check("rms256view", lambda q: fused.rms_norm(q[..., :256], w256, 1e-6),
+          lambda q: R.rms_norm(q[..., :256], w256, 1e-6), qg)
+    o = torch.randn(B, T, 4, 128, generator=g).bfloat16().to(dev)
+    zq = torch.randn(B, T, 64 + 4 * 128, generator=g).bfloat16().to(dev)
+    w128 = (1 + torch.randn(128, generator=g) * 0.1).to(dev)
+    check("gated128", lambda o, z: fused.gated_rms_norm(o, z[..., 64:].reshape(B, T, 4, 128), w128, 1e-6),
+          lambda o, z: R.gated_rms_norm(o, z[..., 64:].reshape(B, T, 4, 128), w128, 1e-6), o, zq)
+    gu = torch.randn(300, 1024, generator=g).bfloat16().to(dev)
+    check("swiglu", fused.swiglu, lambda t: torch.nn.functional.silu(t[:, :512].float()).bfloat16() * t[:, 512:], gu)
+    Tk, K, H = 97, 10, 2048
+    y = torch.randn(Tk * K, H, generator=g).bfloat16().to(dev)
+    inv = torch.randperm(Tk * K, generator=g).to(dev)
+    wt = torch.rand(Tk, K, generator=g).to(dev)
+    wt._want_grad = True
+
+    def comb_ref(y, w):
+        return (y.index_select(0, inv).view(Tk, K, H) * w.to(y.dtype)[..., None]).sum(1)
+    check("combine", lambda y, w: fused.moe_combine(y, inv, w), comb_ref, y, wt)
+    xt = torch.randn(Tk, H, generator=g).bfloat16().to(dev)
+    order = torch.argsort(inv)
+    check("dispatch", lambda x: fused.moe_dispatch(x, order, inv, K),
+          lambda x: x.index_select(0, torch.div(order, K, rounding_mode="floor")), xt)
+    check_status()
+
+
 def test_native_fp8_teacher_targets_agree_with_its_prefill():
     from arc_forge_2026_b200.config import ServeConfig, preset
     from arc_forge_2026_b200.models.hybrid import HybridModel
