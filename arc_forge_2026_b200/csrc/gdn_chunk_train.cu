@@ -81,25 +81,43 @@ AFB_DEV uint4 pack8(const float* f, float s) {
   return o;
 }
 
-// 64 rows (tokens t0..) of head h of a [B, T, H, 128] bf16 tensor -> padded tile; rows past T are zero
+// 64 rows (tokens t0..) of head h of a [B, T, H, 128] bf16 tensor -> padded tile; rows past T are zero. Every
+// thread issues all of its loads before its first shared-memory store (memory-level parallelism).
+constexpr int RV = C * 16 / THREADS;  // 16-byte row vectors per thread
 AFB_DEV void load_rows(bf16* dst, const bf16* src, int b, int t0, int T, int H, int h) {
-  for (int q = threadIdx.x; q < C * 16; q += THREADS) {
-    const int r = q >> 4, cc = q & 15, t = t0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (t < T) v = *reinterpret_cast<const uint4*>(src + (((size_t)b * T + t) * H + h) * D + cc * 8);
-    *reinterpret_cast<uint4*>(dst + r * PW + cc * 8) = v;
+  uint4 v[RV];
+#pragma unroll
+  for (int u = 0; u < RV; ++u) {
+    const int q = threadIdx.x + u * THREADS, r = q >> 4, cc = q & 15, t = t0 + r;
+    v[u] = make_uint4(0, 0, 0, 0);
+    if (t < T) v[u] = *reinterpret_cast<const uint4*>(src + (((size_t)b * T + t) * H + h) * D + cc * 8);
+  }
+#pragma unroll
+  for (int u = 0; u < RV; ++u) {
+    const int q = threadIdx.x + u * THREADS;
+    *reinterpret_cast<uint4*>(dst + (q >> 4) * PW + (q & 15) * 8) = v[u];
   }
 }
-// contiguous fp32 [ROWS x 128] -> padded bf16 tile
+// contiguous fp32 [ROWS x 128] -> padded bf16 tile, 8 loads in flight per thread
 template <int ROWS>
 AFB_DEV void load_f32(bf16* dst, const float* src) {
-  for (int q = threadIdx.x; q < ROWS * 32; q += THREADS) {
-    const int r = q >> 5, c4 = q & 31;
-    const float4 v = reinterpret_cast<const float4*>(src + (size_t)r * D)[c4];
-    uint2 o;
-    o.x = pack_bf16x2(v.x, v.y);
-    o.y = pack_bf16x2(v.z, v.w);
-    *reinterpret_cast<uint2*>(dst + r * PW + c4 * 4) = o;
+  constexpr int N = ROWS * 32 / THREADS;
+#pragma unroll
+  for (int b0 = 0; b0 < N; b0 += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = threadIdx.x + (b0 + u) * THREADS;
+      v[u] = reinterpret_cast<const float4*>(src + (size_t)(q >> 5) * D)[q & 31];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int q = threadIdx.x + (b0 + u) * THREADS;
+      uint2 o;
+      o.x = pack_bf16x2(v[u].x, v[u].y);
+      o.y = pack_bf16x2(v[u].z, v[u].w);
+      *reinterpret_cast<uint2*>(dst + (q >> 5) * PW + (q & 31) * 4) = o;
+    }
   }
 }
 
@@ -181,22 +199,30 @@ __global__ void __launch_bounds__(THREADS) gdn_train_fwd_prep_kernel(GdnTrainArg
   __syncthreads();
   const float last = sm.gc[C - 1];
   uint8_t* kd_tile = reinterpret_cast<uint8_t*>(a.kd_tiles + c.ci * C * D);
-  for (int q = tid; q < C * 16; q += THREADS) {
-    const int r = q >> 4, cc = q & 15, t = c.t0 + r;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (t < a.T) {
-      kv = *reinterpret_cast<const uint4*>(a.k + (((size_t)c.b * a.T + t) * a.Hk + c.hk) * D + cc * 8);
-      vv = *reinterpret_cast<const uint4*>(a.v + (((size_t)c.b * a.T + t) * a.Hv + c.h) * D + cc * 8);
+  {
+    uint4 kv[RV], vv[RV];
+#pragma unroll
+    for (int u = 0; u < RV; ++u) {
+      const int q = tid + u * THREADS, r = q >> 4, cc = q & 15, t = c.t0 + r;
+      kv[u] = vv[u] = make_uint4(0, 0, 0, 0);
+      if (t < a.T) {
+        kv[u] = *reinterpret_cast<const uint4*>(a.k + (((size_t)c.b * a.T + t) * a.Hk + c.hk) * D + cc * 8);
+        vv[u] = *reinterpret_cast<const uint4*>(a.v + (((size_t)c.b * a.T + t) * a.Hv + c.h) * D + cc * 8);
+      }
     }
-    float kf[8], vf[8];
-    unpack8(kv, kf);
-    unpack8(vv, vf);
-    const float be = sm.beta[r];
-    *reinterpret_cast<uint4*>(&sm.kr[r * PW + cc * 8]) = kv;
-    *reinterpret_cast<uint4*>(&sm.kb[r * PW + cc * 8]) = pack8(kf, be);
-    *reinterpret_cast<uint4*>(&sm.kbg[r * PW + cc * 8]) = pack8(kf, be * sm.egc[r]);
-    *reinterpret_cast<uint4*>(&sm.vb[r * PW + cc * 8]) = pack8(vf, be);
-    *reinterpret_cast<uint4*>(kd_tile + tile_byte(r, cc * 8)) = pack8(kf, __expf(last - sm.gc[r]));
+#pragma unroll
+    for (int u = 0; u < RV; ++u) {
+      const int q = tid + u * THREADS, r = q >> 4, cc = q & 15;
+      float kf[8], vf[8];
+      unpack8(kv[u], kf);
+      unpack8(vv[u], vf);
+      const float be = sm.beta[r];
+      *reinterpret_cast<uint4*>(&sm.kr[r * PW + cc * 8]) = kv[u];
+      *reinterpret_cast<uint4*>(&sm.kb[r * PW + cc * 8]) = pack8(kf, be);
+      *reinterpret_cast<uint4*>(&sm.kbg[r * PW + cc * 8]) = pack8(kf, be * sm.egc[r]);
+      *reinterpret_cast<uint4*>(&sm.vb[r * PW + cc * 8]) = pack8(vf, be);
+      *reinterpret_cast<uint4*>(kd_tile + tile_byte(r, cc * 8)) = pack8(kf, __expf(last - sm.gc[r]));
+    }
   }
   __syncthreads();
   const int mt = w & 3, nh = w >> 2;
@@ -342,13 +368,12 @@ __global__ void __launch_bounds__(THREADS) gdn_train_bwd_prep_kernel(GdnTrainArg
   load_rows(sm.ks, a.k, c.b, c.t0, a.T, a.Hk, c.hk);
   load_rows(sm.dos, a.dout, c.b, c.t0, a.T, a.Hv, c.h);
   __syncthreads();
-  for (int q = tid; q < C * 16; q += THREADS) {  // q and q e^{gc}
-    const int r = q >> 4, cc = q & 15, t = c.t0 + r;
-    uint4 qv = make_uint4(0, 0, 0, 0);
-    if (t < a.T) qv = *reinterpret_cast<const uint4*>(a.q + (((size_t)c.b * a.T + t) * a.Hk + c.hk) * D + cc * 8);
+  load_rows(sm.qs, a.q, c.b, c.t0, a.T, a.Hk, c.hk);
+  __syncthreads();
+  for (int q = tid; q < C * 16; q += THREADS) {  // q e^{gc}
+    const int r = q >> 4, cc = q & 15;
     float f[8];
-    unpack8(qv, f);
-    *reinterpret_cast<uint4*>(&sm.qs[r * PW + cc * 8]) = qv;
+    unpack8(*reinterpret_cast<const uint4*>(&sm.qs[r * PW + cc * 8]), f);
     *reinterpret_cast<uint4*>(&sm.qd[r * PW + cc * 8]) = pack8(f, __expf(sm.gc[r]));
   }
   __syncthreads();
@@ -408,18 +433,28 @@ __global__ void __launch_bounds__(THREADS) gdn_train_bwd_inter_kernel(GdnTrainAr
   {
     const float* S = a.states + c.ci * D * D;
     const float* N = a.dnext + c.ci * D * D;
-    for (int q = tid; q < D * 32; q += THREADS) {
-      const int r = q >> 5, c4 = q & 31;
-      const float4 s4 = reinterpret_cast<const float4*>(S + (size_t)r * D)[c4];
-      const float4 n4 = reinterpret_cast<const float4*>(N + (size_t)r * D)[c4];
-      sdot += s4.x * n4.x + s4.y * n4.y + s4.z * n4.z + s4.w * n4.w;
-      uint2 o;
-      o.x = pack_bf16x2(s4.x, s4.y);
-      o.y = pack_bf16x2(s4.z, s4.w);
-      *reinterpret_cast<uint2*>(&sm.ss[r * PW + c4 * 4]) = o;
-      o.x = pack_bf16x2(n4.x, n4.y);
-      o.y = pack_bf16x2(n4.z, n4.w);
-      *reinterpret_cast<uint2*>(&sm.dns[r * PW + c4 * 4]) = o;
+    constexpr int NQ = D * 32 / THREADS;
+#pragma unroll
+    for (int b0 = 0; b0 < NQ; b0 += 4) {
+      float4 s4[4], n4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = tid + (b0 + u) * THREADS;
+        s4[u] = reinterpret_cast<const float4*>(S + (size_t)(q >> 5) * D)[q & 31];
+        n4[u] = reinterpret_cast<const float4*>(N + (size_t)(q >> 5) * D)[q & 31];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = tid + (b0 + u) * THREADS, r = q >> 5, c4 = q & 31;
+        sdot += s4[u].x * n4[u].x + s4[u].y * n4[u].y + s4[u].z * n4[u].z + s4[u].w * n4[u].w;
+        uint2 o;
+        o.x = pack_bf16x2(s4[u].x, s4[u].y);
+        o.y = pack_bf16x2(s4[u].z, s4[u].w);
+        *reinterpret_cast<uint2*>(&sm.ss[r * PW + c4 * 4]) = o;
+        o.x = pack_bf16x2(n4[u].x, n4[u].y);
+        o.y = pack_bf16x2(n4[u].z, n4[u].w);
+        *reinterpret_cast<uint2*>(&sm.dns[r * PW + c4 * 4]) = o;
+      }
     }
   }
   sdot = warp_sum(sdot);
@@ -564,31 +599,47 @@ __global__ void __launch_bounds__(THREADS) gdn_train_bwd_wy_kernel(GdnTrainArgs 
   }
   load_f32<C>(sm.dus, a.du + c.ci * C * D);
   load_f32<C>(sm.dws, a.dw + c.ci * C * D);
-  for (int q = tid; q < C * C / 4; q += THREADS) {  // A -> bf16
-    const int r = q >> 4, c4 = q & 15;
-    const float4 v = reinterpret_cast<const float4*>(a.A + (c.ci * C + r) * C)[c4];
-    uint2 o;
-    o.x = pack_bf16x2(v.x, v.y);
-    o.y = pack_bf16x2(v.z, v.w);
-    *reinterpret_cast<uint2*>(&sm.As[r * PN + c4 * 4]) = o;
+  {  // A -> bf16
+    float4 v[C * C / 4 / THREADS];
+#pragma unroll
+    for (int u = 0; u < C * C / 4 / THREADS; ++u) {
+      const int q = tid + u * THREADS;
+      v[u] = reinterpret_cast<const float4*>(a.A + (c.ci * C + (q >> 4)) * C)[q & 15];
+    }
+#pragma unroll
+    for (int u = 0; u < C * C / 4 / THREADS; ++u) {
+      const int q = tid + u * THREADS;
+      uint2 o;
+      o.x = pack_bf16x2(v[u].x, v[u].y);
+      o.y = pack_bf16x2(v[u].z, v[u].w);
+      *reinterpret_cast<uint2*>(&sm.As[(q >> 4) * PN + (q & 15) * 4]) = o;
+    }
   }
   __syncthreads();
-  for (int q = tid; q < C * 16; q += THREADS) {
-    const int r = q >> 4, cc = q & 15, t = c.t0 + r;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (t < a.T) {
-      kv = *reinterpret_cast<const uint4*>(a.k + (((size_t)c.b * a.T + t) * a.Hk + c.hk) * D + cc * 8);
-      vv = *reinterpret_cast<const uint4*>(a.v + (((size_t)c.b * a.T + t) * a.Hv + c.h) * D + cc * 8);
+  {
+    uint4 kv[RV], vv[RV];
+#pragma unroll
+    for (int u = 0; u < RV; ++u) {
+      const int q = tid + u * THREADS, r = q >> 4, cc = q & 15, t = c.t0 + r;
+      kv[u] = vv[u] = make_uint4(0, 0, 0, 0);
+      if (t < a.T) {
+        kv[u] = *reinterpret_cast<const uint4*>(a.k + (((size_t)c.b * a.T + t) * a.Hk + c.hk) * D + cc * 8);
+        vv[u] = *reinterpret_cast<const uint4*>(a.v + (((size_t)c.b * a.T + t) * a.Hv + c.h) * D + cc * 8);
+      }
     }
-    float kf[8], vf[8];
-    unpack8(kv, kf);
-    unpack8(vv, vf);
-    const float be = sm.beta[r];
-    *reinterpret_cast<uint4*>(&sm.ks[r * PW + cc * 8]) = kv;
-    *reinterpret_cast<uint4*>(&sm.vs[r * PW + cc * 8]) = vv;
-    *reinterpret_cast<uint4*>(&sm.kb[r * PW + cc * 8]) = pack8(kf, be);
-    *reinterpret_cast<uint4*>(&sm.kbg[r * PW + cc * 8]) = pack8(kf, be * sm.egc[r]);
-    *reinterpret_cast<uint4*>(&sm.vb[r * PW + cc * 8]) = pack8(vf, be);
+#pragma unroll
+    for (int u = 0; u < RV; ++u) {
+      const int q = tid + u * THREADS, r = q >> 4, cc = q & 15;
+      float kf[8], vf[8];
+      unpack8(kv[u], kf);
+      unpack8(vv[u], vf);
+      const float be = sm.beta[r];
+      *reinterpret_cast<uint4*>(&sm.ks[r * PW + cc * 8]) = kv[u];
+      *reinterpret_cast<uint4*>(&sm.vs[r * PW + cc * 8]) = vv[u];
+      *reinterpret_cast<uint4*>(&sm.kb[r * PW + cc * 8]) = pack8(kf, be);
+      *reinterpret_cast<uint4*>(&sm.kbg[r * PW + cc * 8]) = pack8(kf, be * sm.egc[r]);
+      *reinterpret_cast<uint4*>(&sm.vb[r * PW + cc * 8]) = pack8(vf, be);
+    }
   }
   __syncthreads();
   {  // dA = du Vb^T + dw Kbg^T

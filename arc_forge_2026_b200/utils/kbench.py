@@ -224,6 +224,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "all"])
     ap.add_argument("--T", type=int, default=640)
+    ap.add_argument("--seq", type=int, default=16384, help="sequence length of the gdn_scan / gdn_train cases")
     a = ap.parse_args()
     res = []
     if a.what in ("moe", "all"):
@@ -235,9 +236,9 @@ def main():
     if a.what in ("attn", "all"):
         res += bench_attn()
     if a.what in ("gdn_scan", "all"):
-        res += bench_gdn_scan()
+        res += bench_gdn_scan(n=(a.seq + 63) // 64)
     if a.what in ("gdn_train", "all"):
-        res += bench_gdn_train()
+        res += bench_gdn_train(T=a.seq)
     for r in res:
         print(json.dumps(r))
 
