@@ -2,13 +2,15 @@
 //
 // * int3_dequant: W[e, n, k] = bf16((c - 4) * bf16(s[e, n, k/128])) from the INT3 tile layout and fp32 master
 //   scales -- the STE forward of trainable group scales (codes frozen), the same product the serving pack holds.
-// * int3_scale_grad: dS[e, n, g] = sum_{k in g} (c - 4) * dW[e, n, k] (one warp per (e, n, g)), the gradient of the
+// * int3_scale_grad: dS[e, n, g] = sum_{k in g} (c - 4) * dW[e, n, k] (one half-warp per (e, n, g)), the gradient of the
 //   scales given dW; fixed-order reduction, bitwise reproducible.
 // * fp8_block_fakequant: W -> dequant(quant_e4m3(W)) with one scale per 128x128 block (scale = amax / 448), the
 //   STE forward of the dense block-FP8 projections (one CTA per block).
 // * topk_tail_kl: per row of fp32 logits z (one CTA per row): log-sum-exp over the vocabulary and over the
 //   non-top-k tail, the loss of the (k + 1)-class coarsening (forward or reverse KL), and dL/dz written as bf16.
 // * adamw: fused AdamW on fp32 masters with bf16 moment states; writes the bf16 compute copy of the weights.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -63,45 +65,72 @@ int int3_dequant(const void* codes, const float* scales, int E, int R, int K, vo
 }
 
 // dS[e, n, g] = sum_k (c - 4) * dW[e, n, g*128 + k]; dW bf16 [E, R, K]; codes as above; dS fp32 [E, R, K/128]
-__global__ void int3_scale_grad_kernel(const uint32_t* __restrict__ codes, const __nv_bfloat16* __restrict__ dW, int R,
-                                       int K, float* __restrict__ dS) {
-  const size_t gw = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+// dS[e, r, g] = sum_{k in group g} (code[e, r, k] - 4) * dW[e, r, k]. A half-warp owns one (row, group) pair: lane
+// l of the half takes the 8 codes 8l..8l+7 (quad q = l / 4, sub-block j = l % 4 of the 12-word tile row) and one
+// 16-byte vector of dW; every thread has 4 pairs' loads in flight before it reduces (persistent grid).
+AFB_DEV int code8_word_lo(int j) { return j < 2 ? 0 : 1; }
+__global__ void __launch_bounds__(256) int3_scale_grad_kernel(const uint32_t* __restrict__ codes,
+                                                              const __nv_bfloat16* __restrict__ dW, int E, int R,
+                                                              int K, float* __restrict__ dS) {
+  constexpr int U = 4;
   const int KG = K / 128;
-  if (gw >= (size_t)R * KG) return;
-  const int e = blockIdx.y;
-  const int row = (int)(gw / KG), g = (int)(gw % KG);
-  const uint32_t* w = codes + ((((size_t)e * (R / 128) + row / 128) * KG + g) * 128 + (row & 127)) * 12;
-  const int q = lane >> 3, p0 = (lane & 7) * 4;
-  const uint32_t L0 = w[3 * q], L1 = w[3 * q + 1], H = w[3 * q + 2];
-  const __nv_bfloat16* d = dW + ((size_t)e * R + row) * K + g * 128 + q * 32 + p0;
-  uint2 raw = *reinterpret_cast<const uint2*>(d);
-  const __nv_bfloat16* dh = reinterpret_cast<const __nv_bfloat16*>(&raw);
-  float acc = 0.f;
+  const int64_t pairs = (int64_t)E * R * KG;
+  const int hl = threadIdx.x & 15;                 // lane within the half-warp
+  const int q = hl >> 2, j = hl & 3;               // quad and 8-code sub-block
+  const int64_t half = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int64_t halves = ((int64_t)gridDim.x * blockDim.x) >> 4;
+  for (int64_t p0 = half; p0 < pairs; p0 += halves * U) {
+    uint4 dv[U];
+    uint32_t lw[U], hw[U];
 #pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const int c = p0 + t;
-    int code;
-    if (c < 8)
-      code = (int)((L0 >> (4 * c)) & 3) | (int)(((H >> (4 * c + 2)) & 1) << 2);
-    else if (c < 16)
-      code = (int)((L0 >> (4 * (c - 8) + 2)) & 3) | (int)(((H >> (4 * (c - 8) + 3)) & 1) << 2);
-    else if (c < 24)
-      code = (int)((L1 >> (4 * (c - 16))) & 3) | (int)(((H >> (4 * (c - 16))) & 1) << 2);
-    else
-      code = (int)((L1 >> (4 * (c - 24) + 2)) & 3) | (int)(((H >> (4 * (c - 24) + 1)) & 1) << 2);
-    acc = fmaf((float)(code - 4), __bfloat162float(dh[t]), acc);
+    for (int u = 0; u < U; ++u) {
+      const int64_t p = p0 + u * halves;
+      dv[u] = make_uint4(0, 0, 0, 0);
+      lw[u] = hw[u] = 0;
+      if (p < pairs) {
+        const int64_t er = p / KG;                 // e * R + row
+        const int g = (int)(p % KG), row = (int)(er % R);
+        const int64_t e = er / R;
+        const uint32_t* w = codes + (((e * (R / 128) + row / 128) * KG + g) * 128 + (row & 127)) * 12;
+        lw[u] = w[3 * q + code8_word_lo(j)];
+        hw[u] = w[3 * q + 2];
+        dv[u] = *reinterpret_cast<const uint4*>(dW + er * K + g * 128 + hl * 8);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const __nv_bfloat16* dh = reinterpret_cast<const __nv_bfloat16*>(&dv[u]);
+      float acc = 0.f;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {  // code c = 8j + t within the quad (bit layout of quant/int3_tiles.py)
+        int code;
+        if (j == 0)
+          code = (int)((lw[u] >> (4 * t)) & 3) | (int)(((hw[u] >> (4 * t + 2)) & 1) << 2);
+        else if (j == 1)
+          code = (int)((lw[u] >> (4 * t + 2)) & 3) | (int)(((hw[u] >> (4 * t + 3)) & 1) << 2);
+        else if (j == 2)
+          code = (int)((lw[u] >> (4 * t)) & 3) | (int)(((hw[u] >> (4 * t)) & 1) << 2);
+        else
+          code = (int)((lw[u] >> (4 * t + 2)) & 3) | (int)(((hw[u] >> (4 * t + 1)) & 1) << 2);
+        acc = fmaf((float)(code - 4), __bfloat162float(dh[t]), acc);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);  // within the half-warp
+      const int64_t p = p0 + u * halves;
+      if (hl == 0 && p < pairs) dS[p] = acc;
+    }
   }
-  acc = warp_sum(acc);
-  if (lane == 0) dS[((size_t)e * R + row) * KG + g] = acc;
 }
 
 int int3_scale_grad(const void* codes, const void* dW, int E, int R, int K, float* dS, cudaStream_t st) {
   if (R % 128 || K % 128) return 3;
-  const int warps = 8;
-  const size_t per_e = (size_t)R * (K / 128);
-  dim3 grid((unsigned)((per_e + warps - 1) / warps), E);
-  int3_scale_grad_kernel<<<grid, warps * 32, 0, st>>>((const uint32_t*)codes, (const __nv_bfloat16*)dW, R, K, dS);
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t halves = (int64_t)E * R * (K / 128);
+  const int64_t blocks = std::min<int64_t>((halves * 16 + 255) / 256, (int64_t)sms * 8);
+  int3_scale_grad_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint32_t*)codes, (const __nv_bfloat16*)dW, E, R, K,
+                                                           dS);
   return (int)cudaGetLastError();
 }
 
