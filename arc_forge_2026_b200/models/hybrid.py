@@ -259,6 +259,40 @@ class HybridModel:
         return cls(cfg, layers, t["model.embed_tokens.weight"].to(**bf), t["model.norm.weight"].to(**bf),
                    t["lm_head.weight"].to(**bf), dev)
 
+    def tensors(self):
+        """(name, tensor) of every weight the forward reads (layer fields, expert-bank fields, embeddings)."""
+        yield "embed", self.embed
+        yield "final_norm", self.final_norm
+        yield "lm_head", self.lm_head
+        for i, lw in enumerate(self.layers):
+            for k, v in vars(lw).items():
+                if isinstance(v, torch.Tensor):
+                    yield f"layers.{i}.{k}", v
+                elif v is not None and hasattr(v, "__dict__"):
+                    for bk, bv in vars(v).items():
+                        if isinstance(bv, torch.Tensor):
+                            yield f"layers.{i}.{k}.{bk}", bv
+
+    @torch.no_grad()
+    def update_from_package(self, pkg_dir) -> dict:
+        """Replace the weights by those of a deploy package of the same architecture, copying into the existing
+        tensors (addresses unchanged: captured CUDA graphs stay valid). Expert-parallel models keep their block of
+        experts. Raises before writing anything if any tensor differs in shape or dtype."""
+        new = HybridModel.from_package(pkg_dir, self.device)
+        if self.ep is not None:
+            from ..parallel.ep import local_bank
+            for lw in new.layers:
+                lw.bank = local_bank(lw.bank, self.ep.world, self.ep.rank)
+        mine, theirs = dict(self.tensors()), dict(new.tensors())
+        if mine.keys() != theirs.keys():
+            raise ValueError(f"package tensors differ: {sorted(set(mine) ^ set(theirs))[:8]}")
+        for k, t in mine.items():
+            if t.shape != theirs[k].shape or t.dtype != theirs[k].dtype:
+                raise ValueError(f"{k}: {tuple(theirs[k].shape)} {theirs[k].dtype} vs {tuple(t.shape)} {t.dtype}")
+        for k, t in mine.items():
+            t.copy_(theirs[k])
+        return {"tensors": len(mine)}
+
     def nbytes(self) -> int:
         tot = self.embed.nbytes + self.lm_head.nbytes
         for lw in self.layers:

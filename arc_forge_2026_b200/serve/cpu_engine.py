@@ -35,6 +35,18 @@ class CPUEngine:
         return self.S - len(self.sessions)
 
     @torch.no_grad()
+    def update_weights(self, path) -> dict:
+        """Load a state dict of the reference model (``.pt`` or ``.safetensors``) in place."""
+        path = str(path)
+        if path.endswith(".safetensors"):
+            from safetensors.torch import load_file
+            sd = load_file(path)
+        else:
+            sd = torch.load(path, map_location="cpu", weights_only=True)
+        self.model.load_state_dict(sd, strict=True)
+        return {"tensors": len(sd)}
+
+    @torch.no_grad()
     def _feed(self, s: CPUSession, toks: list[int]):
         ids = torch.tensor([toks], dtype=torch.long)
         s.logits = self.model(ids, s.cache, s.pos)[0, -1]

@@ -275,6 +275,11 @@ class SpecEngine:
             self.drafts[r].fill_(0)
         sess.generated.append(int(tok.item()))
 
+    def update_weights(self, pkg_dir) -> dict:
+        """Swap in the weights of a deploy package between steps (in place: the captured graphs stay valid)."""
+        torch.cuda.synchronize(self.model.device)
+        return self.model.update_from_package(pkg_dir)
+
     def release(self, sid: int):
         sess = self.sessions.pop(sid)
         self.active[sess.row] = 0

@@ -11,6 +11,10 @@ server-side sessions and ``/close_session``, usage accounting):
                                  a session keeps its transcript (and, on engines that can extend a session, its
                                  KV / recurrent state) until /close_session
     POST /close_session          {"session_id"}
+    POST /abort_request          {"rid"}: stop a queued or running request (its response ends with finish_reason
+                                 "abort"); generation routes accept an optional "rid" to name the request
+    POST /update_weights_from_disk {"model_path"}: load new weights between engine steps, in place (a deploy
+                                 package for the native engine, a state-dict file for the CPU engine)
     GET  /metrics                Prometheus text (requests, tokens, active sessions, step latency)
 
 One engine thread owns the engine: it admits queued requests when a session slot is free, runs ``engine.step()``
@@ -45,6 +49,8 @@ class Request:
     sid: int = -1
     n_out: int = 0
     t0: float = field(default_factory=time.perf_counter)
+    rid: str = ""
+    aborted: bool = False
 
 
 class EngineLoop:
@@ -59,6 +65,8 @@ class EngineLoop:
         self.live: dict[int, Request] = {}
         self.keyed: dict[str, int] = {}          # session_id -> engine sid (kept until /close_session)
         self.transcripts: dict[str, list[int]] = {}
+        self.by_rid: dict[str, Request] = {}
+        self.commands: collections.deque = collections.deque()  # (fn, concurrent Future) run between steps
         self._sids = itertools.count(1)
         self._stop = False
         self.thread = threading.Thread(target=self._run, name="afb-engine", daemon=True)
@@ -67,7 +75,32 @@ class EngineLoop:
     def submit(self, req: Request):
         with self.cv:
             self.pending.append(req)
+            if req.rid:
+                self.by_rid[req.rid] = req
             self.cv.notify()
+
+    def abort(self, rid: str) -> bool:
+        """Queued: dropped now; running: finished by the engine thread before its next step."""
+        with self.cv:
+            req = self.by_rid.get(rid)
+            if req is None:
+                return False
+            req.aborted = True
+            if req in self.pending:
+                self.pending.remove(req)
+                self.by_rid.pop(rid, None)
+                self._emit(req, ("done", "abort"))
+            self.cv.notify()
+            return True
+
+    def call(self, fn):
+        """Run ``fn(engine)`` on the engine thread between steps; returns a concurrent future."""
+        import concurrent.futures
+        fut = concurrent.futures.Future()
+        with self.cv:
+            self.commands.append((fn, fut))
+            self.cv.notify()
+        return fut
 
     def close_session(self, key: str) -> bool:
         with self.cv:
@@ -125,8 +158,9 @@ class EngineLoop:
         if req.n_out >= req.max_new:
             self._finish(req)
 
-    def _finish(self, req: Request):
+    def _finish(self, req: Request, reason: str | None = None):
         self.live.pop(req.sid, None)
+        self.by_rid.pop(req.rid, None)
         eng = self.engine
         if req.session_key is None:
             if req.sid in eng.sessions:
@@ -138,17 +172,28 @@ class EngineLoop:
                 s.done = True
                 if hasattr(s, "row") and hasattr(eng, "active"):
                     eng.active[s.row] = 0  # keep the session's pages, stop decoding it
-        self._emit(req, ("done", None))
+        self._emit(req, ("done", reason))
         if self.metrics:
             self.metrics["latency"].observe(time.perf_counter() - req.t0)
 
     def _run(self):
         while True:
             with self.cv:
-                while not self._stop and not self.pending and not self.live:
+                while not self._stop and not self.pending and not self.live and not self.commands:
                     self.cv.wait()
                 if self._stop:
                     return
+                commands = list(self.commands)
+                self.commands.clear()
+                aborted = [r for r in self.live.values() if r.aborted]
+            for fn, fut in commands:
+                try:
+                    fut.set_result(fn(self.engine))
+                except Exception as e:  # noqa: BLE001 - reported to the caller
+                    fut.set_exception(e)
+            for req in aborted:
+                self._finish(req, "abort")
+            with self.cv:
                 admit = []
                 free = self._free_slots()
                 while self.pending:
@@ -216,17 +261,22 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200"):
     app = FastAPI(title="arc_forge_2026_b200", lifespan=lifespan)
     app.state.engine_loop = loop_
 
-    async def _generate(prompt, max_new, key=None, extend=None):
+    async def _generate(prompt, max_new, key=None, extend=None, rid=None, state=None):
         loop = asyncio.get_running_loop()
-        req = Request(prompt, max_new, loop, asyncio.Queue(), key, extend)
+        req = Request(prompt, max_new, loop, asyncio.Queue(), key, extend, rid=rid or "")
         loop_.submit(req)
         while True:
             kind, val = await req.queue.get()
             if kind == "error":
                 raise HTTPException(400, val)
             if kind == "done":
+                if state is not None and val:
+                    state["reason"] = val
                 return
             yield val
+
+    def _reason(state, n, max_new):
+        return state.get("reason") or ("length" if n >= max_new else "stop")
 
     async def _collect(gen):
         return [t async for t in gen]
@@ -260,17 +310,18 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200"):
         prompt = body.get("prompt", "")
         ids = list(prompt) if isinstance(prompt, list) else tok.encode(prompt)
         max_new = int(body.get("max_tokens", 16))
-        rid = "cmpl-" + uuid.uuid4().hex[:24]
+        rid = body.get("rid") or "cmpl-" + uuid.uuid4().hex[:24]
+        st = {}
         if body.get("stream"):
             async def chunks():
-                async for t in _generate(ids, max_new):
+                async for t in _generate(ids, max_new, rid=rid, state=st):
                     yield {"id": rid, "object": "text_completion", "model": model_name,
                            "choices": [{"index": 0, "text": tok.decode([t]), "token_ids": [t], "finish_reason": None}]}
             return _sse(chunks())
-        out = await _collect(_generate(ids, max_new))
+        out = await _collect(_generate(ids, max_new, rid=rid, state=st))
         return {"id": rid, "object": "text_completion", "created": int(time.time()), "model": model_name,
-                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": "length"
-                             if len(out) >= max_new else "stop"}],
+                "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out,
+                             "finish_reason": _reason(st, len(out), max_new)}],
                 "usage": _usage(len(ids), len(out))}
 
     @app.post("/v1/chat/completions")
@@ -278,17 +329,18 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200"):
         metrics["requests"].labels("chat").inc()
         ids = tok.chat(body.get("messages", []))
         max_new = int(body.get("max_tokens", body.get("max_completion_tokens", 16)))
-        rid = "chatcmpl-" + uuid.uuid4().hex[:24]
+        rid = body.get("rid") or "chatcmpl-" + uuid.uuid4().hex[:24]
+        st = {}
         if body.get("stream"):
             async def chunks():
-                async for t in _generate(ids, max_new):
+                async for t in _generate(ids, max_new, rid=rid, state=st):
                     yield {"id": rid, "object": "chat.completion.chunk", "model": model_name,
                            "choices": [{"index": 0, "delta": {"content": tok.decode([t])}, "finish_reason": None}]}
             return _sse(chunks())
-        out = await _collect(_generate(ids, max_new))
+        out = await _collect(_generate(ids, max_new, rid=rid, state=st))
         return {"id": rid, "object": "chat.completion", "created": int(time.time()), "model": model_name,
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},
-                             "finish_reason": "length" if len(out) >= max_new else "stop"}],
+                             "finish_reason": _reason(st, len(out), max_new)}],
                 "usage": _usage(len(ids), len(out))}
 
     @app.post("/v1/responses")
@@ -298,19 +350,22 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200"):
         msgs = [{"role": "user", "content": inp}] if isinstance(inp, str) else list(inp)
         key = body.get("session_id")
         max_new = int(body.get("max_output_tokens", 16))
+        rid = body.get("rid") or "resp_" + uuid.uuid4().hex[:24]
+        st = {}
         if key is not None and key in loop_.keyed:
             ext = tok.encode("".join(f"<|{m.get('role', 'user')}|>{m.get('content', '')}\n" for m in msgs)
                              + "<|assistant|>") if isinstance(tok, ByteTokenizer) else tok.chat(msgs)
             prompt_len = len(loop_.transcripts.get(key, [])) + len(ext)
-            gen = _generate([], max_new, key, ext)
+            gen = _generate([], max_new, key, ext, rid=rid, state=st)
         else:
             ids = tok.chat(msgs)
             prompt_len = len(ids)
-            gen = _generate(ids, max_new, key)
+            gen = _generate(ids, max_new, key, rid=rid, state=st)
         out = await _collect(gen)
         text = tok.decode(out)
-        return {"id": "resp_" + uuid.uuid4().hex[:24], "object": "response", "created_at": int(time.time()),
-                "model": model_name, "status": "completed", "session_id": key,
+        return {"id": rid, "object": "response", "created_at": int(time.time()),
+                "model": model_name, "status": "incomplete" if st.get("reason") == "abort" else "completed",
+                "session_id": key,
                 "output": [{"type": "message", "role": "assistant",
                             "content": [{"type": "output_text", "text": text}]}],
                 "output_text": text,
@@ -323,6 +378,25 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200"):
         if key is None:
             raise HTTPException(400, "session_id is required")
         return JSONResponse({"session_id": key, "closed": loop_.close_session(key)})
+
+    @app.post("/abort_request")
+    async def abort_request(body: dict):
+        rid = body.get("rid")
+        if not rid:
+            raise HTTPException(400, "rid is required")
+        return {"rid": rid, "aborted": loop_.abort(rid)}
+
+    @app.post("/update_weights_from_disk")
+    async def update_weights(body: dict):
+        path = body.get("model_path")
+        if not path:
+            raise HTTPException(400, "model_path is required")
+        fut = loop_.call(lambda eng: eng.update_weights(path))
+        try:
+            info = await asyncio.wrap_future(fut)
+        except Exception as e:  # noqa: BLE001 - reported to the client
+            return JSONResponse({"success": False, "message": str(e)}, status_code=400)
+        return {"success": True, "message": "weights updated", **(info or {})}
 
     return app
 

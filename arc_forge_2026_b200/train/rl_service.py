@@ -9,6 +9,11 @@ gloo group with ``broadcast_object_list``, so the GPU process group carries only
                                        one optimizer step: forward, per-token log-probabilities under logits / T,
                                        BPO (clipped ratio) or MIS (truncated importance weight) loss, backward into
                                        the adapters, gradients averaged over ranks, global-norm clip, AdamW
+    POST /begin                        start a step accumulated over several calls (zeroes the gradients)
+    POST /accumulate {batch | batch_path, algo?, clip?, cap?}
+                                       forward + backward of one micro-batch; gradients add up (token-weighted)
+    POST /step                         apply the accumulated step: gradients / tokens of the step, averaged over
+                                       ranks, clipped, AdamW
     POST /publish {weight_version}     merged adapters -> <out>/merged/v<version:06d> (``fn-lora-merged-v2``); versions
                                        must increase
     POST /save                         <out>/checkpoint-<step>/ (adapters + optimizer state + step), via .tmp rename
@@ -57,7 +62,16 @@ class RLTrainer:
             return torch.load(cmd["batch_path"], map_location="cpu", weights_only=False)
         return {k: torch.tensor(v) if isinstance(v, list) else v for k, v in cmd["batch"].items()}
 
-    def train(self, cmd: dict) -> dict:
+    def begin(self, cmd: dict | None = None) -> dict:
+        self.opt.zero_grad(set_to_none=True)
+        self.acc = {"tokens": 0, "loss_sum": 0.0, "batches": 0, "ratio_sum": 0.0, "ent_sum": 0.0, "t0": time.perf_counter()}
+        return {"step": self.step, "begun": True}
+
+    def accumulate(self, cmd: dict) -> dict:
+        """Forward + backward of one micro-batch; the loss enters as a token sum (divided by the step's tokens at
+        ``step``), so a step over several calls equals one call over their concatenation."""
+        if getattr(self, "acc", None) is None:
+            raise RuntimeError("accumulate before begin")
         b = self._batch(cmd)
         dev = self.student.embed.device
         ids, labels = b["ids"].long().to(dev), b["labels"].long().to(dev)
@@ -74,8 +88,6 @@ class RLTrainer:
                 self.replay = RoutingReplay("force", len(self.student.layers), c.num_experts_per_tok)
                 self.replay.install(self.student)
             self.replay.set_routing(b["routing"].long())
-        t0 = time.perf_counter()
-        self.opt.zero_grad(set_to_none=True)
         h = self.student.hidden(ids).reshape(ids.numel(), -1)
         logp, ent = selective_logprob(h, self.student.lm_head, labels.reshape(-1), T)
         algo = cmd.get("algo", "bpo")
@@ -85,23 +97,48 @@ class RLTrainer:
             loss = mis_loss(logp, beh, adv, mask, cap=float(cmd.get("cap", 2.0)))
         else:
             raise ValueError(f"unknown RL loss {algo!r}")
-        loss.backward()
+        m = mask > 0
+        n = int(m.sum())
+        (loss * n).backward()
+        with torch.no_grad():
+            ratio = torch.exp(logp.detach() - beh)
+            self.acc["tokens"] += n
+            self.acc["loss_sum"] += float(loss.detach()) * n
+            self.acc["ratio_sum"] += float(ratio[m].sum()) if n else 0.0
+            self.acc["ent_sum"] += float(ent.detach()[m].sum()) if n else 0.0
+            self.acc["batches"] += 1
+        return {"step": self.step, "batches": self.acc["batches"], "tokens": self.acc["tokens"],
+                "loss": float(loss.detach())}
+
+    def step_opt(self, cmd: dict | None = None) -> dict:
+        acc = getattr(self, "acc", None)
+        if acc is None or acc["batches"] == 0:
+            raise RuntimeError("step without accumulated batches")
+        tokens = max(1, acc["tokens"])
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             average_gradients(self.params, self.group)
+        with torch.no_grad():
+            for p in self.params:
+                if p.grad is not None:
+                    p.grad.div_(tokens)
         norm = clip_grad_norm_(self.params, self.max_norm)
         self.opt.step()
         self.step += 1
-        with torch.no_grad():
-            ratio = torch.exp(logp.detach() - beh)
-            m = mask > 0
-            report = {"step": self.step, "loss": float(loss.detach()), "grad_norm": float(norm),
-                      "tokens": int(m.sum()), "ratio_mean": float(ratio[m].mean()) if m.any() else None,
-                      "entropy": float(ent.detach()[m].mean()) if m.any() else None,
-                      "seconds": round(time.perf_counter() - t0, 4)}
-            if self.replay is not None:
-                st = self.replay.stats
-                report["routing_equal_frac"] = sum(st["equal"]) / max(1, sum(st["rows"]))
+        report = {"step": self.step, "loss": acc["loss_sum"] / tokens, "grad_norm": float(norm), "tokens": acc["tokens"],
+                  "batches": acc["batches"], "ratio_mean": acc["ratio_sum"] / tokens if acc["tokens"] else None,
+                  "entropy": acc["ent_sum"] / tokens if acc["tokens"] else None,
+                  "seconds": round(time.perf_counter() - acc["t0"], 4)}
+        if self.replay is not None:
+            st = self.replay.stats
+            report["routing_equal_frac"] = sum(st["equal"]) / max(1, sum(st["rows"]))
+        self.acc = None
         return report
+
+    def train(self, cmd: dict) -> dict:
+        """One optimizer step on one batch (begin + accumulate + step)."""
+        self.begin()
+        self.accumulate(cmd)
+        return self.step_opt()
 
     def publish(self, cmd: dict) -> dict:
         v = int(cmd["weight_version"])
@@ -131,6 +168,12 @@ class RLTrainer:
         op = cmd["op"]
         if op == "train":
             return self.train(cmd)
+        if op == "begin":
+            return self.begin(cmd)
+        if op == "accumulate":
+            return self.accumulate(cmd)
+        if op == "step":
+            return self.step_opt(cmd)
         if op == "publish":
             return self.publish(cmd) if not dist.is_initialized() or dist.get_rank() == 0 else {}
         if op == "save":
@@ -164,6 +207,18 @@ def create_app(trainer: RLTrainer, control_group=None):
     @app.post("/train")
     def train(body: dict):
         return run({"op": "train", **body})
+
+    @app.post("/begin")
+    def begin(body: dict | None = None):
+        return run({"op": "begin"})
+
+    @app.post("/accumulate")
+    def accumulate(body: dict):
+        return run({"op": "accumulate", **body})
+
+    @app.post("/step")
+    def step(body: dict | None = None):
+        return run({"op": "step"})
 
     @app.post("/publish")
     def publish(body: dict):

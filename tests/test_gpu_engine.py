@@ -178,3 +178,26 @@ def test_model_from_package_equals_model_from_reference(tmp_path):
     torch.cuda.synchronize()
     check_status()
     assert outs[0] == outs[1]
+
+
+def test_update_weights_in_place_matches_fresh_load(tmp_path):
+    """A running engine swaps to another package's weights in place (same tensor addresses) and then decodes what
+    an engine built on that package decodes."""
+    from arc_forge_2026_b200.formats.int3_package import package_tensors, write_package
+    from arc_forge_2026_b200.quant.int3_tiles import tiles_to_codes, tiles_to_scales
+    cfg, ref, model = _models(6)
+    cs = [(tiles_to_codes(lw.bank.w13_codes.cpu()), tiles_to_scales(lw.bank.w13_scales.cpu()),
+           tiles_to_codes(lw.bank.w2_codes.cpu()), tiles_to_scales(lw.bank.w2_scales.cpu())) for lw in model.layers]
+    d = write_package(package_tensors(ref, cs, dense_fp8=False), cfg, tmp_path / "pkg", dense_fp8=False)
+    _, _, other = _models(9)
+    ptrs = [t.data_ptr() for _, t in other.tensors()]
+    prompt = torch.randint(0, cfg.vocab_size, (70,), generator=torch.Generator().manual_seed(6)).tolist()
+    eng = SpecEngine(other, None, ServeConfig(spec_k=0, accept_mode="greedy"), 1, 1024)
+    assert eng.update_weights(d)["tensors"] == len(ptrs)
+    assert [t.data_ptr() for _, t in other.tensors()] == ptrs
+    got = eng.generate([prompt], 10)
+    want = SpecEngine(HybridModel.from_package(d, dev), None, ServeConfig(spec_k=0, accept_mode="greedy"), 1,
+                      1024).generate([prompt], 10)
+    torch.cuda.synchronize()
+    check_status()
+    assert got == want

@@ -125,3 +125,29 @@ def test_rl_service_steps_publish_save(tmp_path):
         assert (tmp_path / "merged" / "v000001" / "DONE").exists()
         assert c.post("/publish", json={"weight_version": 1}).status_code == 500  # versions must increase
         assert c.post("/save").json()["path"].endswith("checkpoint-7")
+
+
+def test_rl_step_accumulated_over_calls_equals_one_call(tmp_path):
+    """begin + accumulate(half) + accumulate(other half) + step gives the adapters of one /train over both halves
+    (token-weighted gradient accumulation)."""
+    from arc_forge_2026_b200.train.lora import lora_state
+    from arc_forge_2026_b200.train.rl_service import RLTrainer
+    g = torch.Generator().manual_seed(3)
+    c = preset("tiny_cpu")
+    B, T = 2, 12
+    batch = {"ids": torch.randint(0, c.vocab_size, (B, T), generator=g),
+             "labels": torch.randint(0, c.vocab_size, (B, T), generator=g),
+             "mask": torch.tensor([[1] * T, [1] * 7 + [0] * 5]),
+             "advantages": torch.tensor([0.5, -1.0]), "behavior_logp": -torch.rand(B, T, generator=g) * 3}
+    one, acc = RLTrainer(_student(4), tmp_path / "a", lr=1e-2), RLTrainer(_student(4), tmp_path / "b", lr=1e-2)
+    r1 = one.train({"batch": batch})
+    acc.begin()
+    for i in range(B):
+        acc.accumulate({"batch": {k: v[i:i + 1] for k, v in batch.items()}})
+    r2 = acc.step_opt()
+    assert r2["tokens"] == r1["tokens"] == 19 and r2["batches"] == 2
+    assert abs(r1["loss"] - r2["loss"]) < 1e-5 and abs(r1["grad_norm"] - r2["grad_norm"]) < 1e-4 * (1 + r1["grad_norm"])
+    s1, s2 = lora_state(one.student), lora_state(acc.student)
+    assert all(torch.allclose(s1[k].float(), s2[k].float(), atol=1e-6) for k in s1)
+    with pytest.raises(RuntimeError):
+        acc.step_opt()

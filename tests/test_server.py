@@ -73,3 +73,45 @@ def test_concurrent_requests_beyond_slots_and_metrics(setup):
     m = client.get("/metrics").text
     assert "afb_generated_tokens_total" in m and "afb_engine_step_seconds" in m
     assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+
+
+def test_abort_request_ends_a_running_generation(setup):
+    client, _ = setup
+    import concurrent.futures as cf
+    import time
+    with cf.ThreadPoolExecutor(2) as ex:
+        fut = ex.submit(client.post, "/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 3000, "rid": "r-abort"})
+        aborted = False
+        for _ in range(200):  # the request may still be queued on the first tries
+            time.sleep(0.05)
+            if client.post("/abort_request", json={"rid": "r-abort"}).json()["aborted"]:
+                aborted = True
+                break
+        r = fut.result(timeout=120)
+    assert aborted and r.status_code == 200, r.text
+    ch = r.json()["choices"][0]
+    assert ch["finish_reason"] == "abort" and len(ch["token_ids"]) < 3000
+    assert client.post("/abort_request", json={"rid": "r-abort"}).json()["aborted"] is False
+    ok = client.post("/v1/completions", json={"prompt": [1, 2], "max_tokens": 2})  # the engine keeps serving
+    assert ok.status_code == 200 and len(ok.json()["choices"][0]["token_ids"]) == 2
+
+
+def test_update_weights_from_disk_swaps_the_served_model(tmp_path):
+    cfg = preset("tiny_cpu")
+    a, b = build_reference(cfg, seed=0), build_reference(cfg, seed=7)
+    path = tmp_path / "b.pt"
+    torch.save(b.state_dict(), path)
+    app = create_app(CPUEngine(a, max_sessions=2), _NoEos(), "tiny")
+    prompt = [3, 1, 4, 1, 5]
+    with TestClient(app) as client:
+        r = client.post("/update_weights_from_disk", json={"model_path": str(path)})
+        assert r.status_code == 200 and r.json()["success"], r.text
+        out = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 4}).json()["choices"][0]
+        bad = client.post("/update_weights_from_disk", json={"model_path": str(tmp_path / "missing.pt")})
+        assert bad.status_code == 400 and bad.json()["success"] is False
+    ref = build_reference(cfg, seed=7).eval()
+    ids = list(prompt)
+    with torch.no_grad():
+        for _ in range(4):
+            ids.append(int(ref(torch.tensor([ids]))[0, -1].argmax()))
+    assert out["token_ids"] == ids[len(prompt):]
