@@ -12,7 +12,8 @@ Modes (the reference's ``training/work/qwen38fn_qad/train_qad.py:1-21``):
 Distributed: one process per GPU (torchrun). Every rank trains on its own sequences; the trainable masters live in
 a ZeRO-style sharded optimizer (``parallel/shard_optim.py``): gradients are reduce-scattered, each rank updates its
 shard, masters are all-gathered. Checkpoints hold the trainable masters and optimizer state per rank plus a
-``trainer.json`` with the step and the plan hash; resume refuses a different plan. ``--export`` writes the trained
+``trainer.json`` with the step and the plan hash (DCP storage: ``train/checkpoint.py``, resumable at another world
+size); resume refuses a different plan. ``--export`` writes the trained
 tensors as a ``gean320-qad-v2-delta``.
 
     python -m arc_forge_2026_b200.train.qad --mode train --preset qwen3next_80b --synthetic --steps 10
@@ -122,17 +123,17 @@ def plan_hash(args) -> str:
 
 
 def save_checkpoint(path: Path, student: QADStudent, opt, step: int, phash: str, rank: int):
-    path = Path(path)
-    path.mkdir(parents=True, exist_ok=True)
-    trainable = {n: p.detach() for n, p in student.named_parameters()}
-    torch.save({"params": trainable, "opt": opt.state_dict()}, path / f"rank{rank:03d}.pt.tmp")
-    os.replace(path / f"rank{rank:03d}.pt.tmp", path / f"rank{rank:03d}.pt")
-    if rank == 0:
-        (path / "trainer.json.tmp").write_text(json.dumps({"step": step, "plan": phash}) + "\n")
-        os.replace(path / "trainer.json.tmp", path / "trainer.json")
+    """DCP checkpoint (``train/checkpoint.py``): masters once, optimizer moments by owned range, loadable at another
+    world size."""
+    from .checkpoint import save_dcp
+    save_dcp(path, student, opt, step, phash)
 
 
 def load_checkpoint(path: Path, student: QADStudent, opt, phash: str, rank: int) -> int:
+    from .checkpoint import is_dcp, load_dcp
+    if is_dcp(path):
+        return load_dcp(path, student, opt, phash)
+    # per-rank torch.save files of earlier checkpoints (same world size only)
     meta = json.loads((Path(path) / "trainer.json").read_text())
     if meta["plan"] != phash:
         raise RuntimeError(f"checkpoint plan {meta['plan']} != this run's plan {phash}: refusing to resume")
