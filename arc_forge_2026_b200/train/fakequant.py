@@ -68,8 +68,14 @@ class FP8BlockSTE(torch.autograd.Function):
 
 
 def int3_weight(scales, codes):
+    from . import kernels
+    if scales.is_cuda:
+        kernels.hit("int3_weight", True)
     return Int3ScaleSTE.apply(scales, codes)
 
 
 def fp8_weight(master):
+    from . import kernels
+    if master.is_cuda:
+        kernels.hit("fp8_weight", True)
     return FP8BlockSTE.apply(master)

@@ -13,6 +13,7 @@ import torch
 import torch.nn.functional as F
 
 from ..models import reference as R
+from . import kernels
 
 _BF = torch.bfloat16
 _NORM_H = (128, 256, 512, 1024, 2048)
@@ -45,9 +46,12 @@ class _ConvSiLU(torch.autograd.Function):
 
 def conv_silu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Causal depthwise conv (kernel 4, zero history) + SiLU over x [B, T, C] (a strided view is fine); frozen w."""
-    if (_gpu_bf16(x) and x.dim() == 3 and w.shape[-1] == 4 and x.shape[-1] % 8 == 0 and x.stride(1) % 8 == 0
-            and x.stride(0) == x.shape[1] * x.stride(1) and not w.requires_grad):
+    if (kernels.use("conv_silu") and _gpu_bf16(x) and x.dim() == 3 and w.shape[-1] == 4 and x.shape[-1] % 8 == 0
+            and x.stride(1) % 8 == 0 and x.stride(0) == x.shape[1] * x.stride(1) and not w.requires_grad):
+        kernels.hit("conv_silu", True)
         return _ConvSiLU.apply(x, w.float().contiguous())
+    if x.is_cuda:
+        kernels.hit("conv_silu", False)
     return R.causal_conv1d(x, w)[0]
 
 
@@ -77,15 +81,21 @@ def _norm_ok(x, w) -> bool:
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     """Zero-centred RMSNorm ``x / rms(x) * (1 + w)`` (frozen w) of ``models.reference.rms_norm``."""
-    if _norm_ok(x, w):
+    if kernels.use("rms_norm") and _norm_ok(x, w):
+        kernels.hit("rms_norm", True)
         return _RMSNorm.apply(x, w.float().contiguous(), eps, None)
+    if x.is_cuda:
+        kernels.hit("rms_norm", False)
     return R.rms_norm(x, w, eps)
 
 
 def gated_rms_norm(x: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     """GDN output norm ``x / rms(x) * w * silu(z)`` (frozen w) of ``models.reference.gated_rms_norm``."""
-    if _norm_ok(x, w) and _gpu_bf16(z) and z.shape == x.shape:
+    if kernels.use("gated_rms_norm") and _norm_ok(x, w) and _gpu_bf16(z) and z.shape == x.shape:
+        kernels.hit("gated_rms_norm", True)
         return _RMSNorm.apply(x, w.float().contiguous(), eps, z)
+    if x.is_cuda:
+        kernels.hit("gated_rms_norm", False)
     return R.gated_rms_norm(x, z, w, eps)
 
 
@@ -109,8 +119,11 @@ class _SwiGLU(torch.autograd.Function):
 def swiglu(gu: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` of ``gu = [gate | up]`` along the last dim."""
     I = gu.shape[-1] // 2
-    if _gpu_bf16(gu) and gu.is_contiguous() and I % 8 == 0:
+    if kernels.use("swiglu") and _gpu_bf16(gu) and gu.is_contiguous() and I % 8 == 0:
+        kernels.hit("swiglu", True)
         return _SwiGLU.apply(gu)
+    if gu.is_cuda:
+        kernels.hit("swiglu", False)
     return F.silu(gu[..., :I].float()).to(gu.dtype) * gu[..., I:]
 
 
@@ -134,8 +147,11 @@ def moe_combine(y: torch.Tensor, inv: torch.Tensor, w: torch.Tensor) -> torch.Te
     """out[t] = sum_k w[t, k] y[inv[t*K + k]]: routed rows (expert order) back to their tokens, weighted."""
     T, K = w.shape
     H = y.shape[-1]
-    if _gpu_bf16(y) and y.is_contiguous() and H in (256, 512, 1024, 2048):
+    if kernels.use("moe_combine") and _gpu_bf16(y) and y.is_contiguous() and H in (256, 512, 1024, 2048):
+        kernels.hit("moe_combine", True)
         return _Combine.apply(y, inv.contiguous(), w.float().contiguous())
+    if y.is_cuda:
+        kernels.hit("moe_combine", False)
     yt = y.index_select(0, inv).view(T, K, H)
     return (yt * w.to(yt.dtype)[..., None]).sum(1)
 
@@ -160,6 +176,9 @@ class _Dispatch(torch.autograd.Function):
 
 
 def moe_dispatch(x: torch.Tensor, order: torch.Tensor, inv: torch.Tensor, K: int) -> torch.Tensor:
-    if _gpu_bf16(x) and x.shape[-1] in (256, 512, 1024, 2048):
+    if kernels.use("moe_dispatch") and _gpu_bf16(x) and x.shape[-1] in (256, 512, 1024, 2048):
+        kernels.hit("moe_dispatch", True)
         return _Dispatch.apply(x, order, inv.contiguous(), K)
+    if x.is_cuda:
+        kernels.hit("moe_dispatch", False)
     return None

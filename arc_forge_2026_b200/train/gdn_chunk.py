@@ -189,10 +189,14 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None, precis
     Grouped values: value head h uses key head h // (Hv / Hk). On CUDA with Dk = Dv = 128 and no initial state the
     whole rule runs in the native kernels (bf16 operands, fp32 accumulation, o in bf16); ``precise`` keeps the
     fp32 torch path with the fp32 scan."""
-    if _native_ok(q, k, v, g, chunk, state, precise):
+    from . import kernels
+    if kernels.use("gdn_chunk") and _native_ok(q, k, v, g, chunk, state, precise):
+        kernels.hit("gdn_chunk", True)
         bf = torch.bfloat16
         return _GdnChunkNative.apply(q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(),
                                      g.float().contiguous(), beta.float().contiguous())
+    if q.is_cuda and not precise:
+        kernels.hit("gdn_chunk", False)
     if k.shape[2] != v.shape[2]:
         rep = v.shape[2] // k.shape[2]
         q, k = q.repeat_interleave(rep, 2), k.repeat_interleave(rep, 2)

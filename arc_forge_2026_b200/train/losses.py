@@ -60,6 +60,9 @@ def fused_topk_tail_kl(hidden, weight, weight_t, ids, t_lp, t_tail, direction="f
     """Summed loss over rows (divide by the number of rows for the mean)."""
     if direction not in ("forward", "reverse"):
         raise ValueError(direction)
+    if hidden.is_cuda:
+        from . import kernels
+        kernels.hit("topk_tail_kl", True)
     return FusedTopKTailKL.apply(hidden, weight, weight_t, ids, t_lp, t_tail, direction == "reverse", chunk_rows)
 
 

@@ -168,12 +168,17 @@ def main(argv=None):
     ap.add_argument("--targets", type=Path, help="qad-topk-v1 root (train/score)")
     ap.add_argument("--out", type=Path, help="teacher: targets root; train: checkpoint directory")
     ap.add_argument("--resume", action="store_true")
+    ap.add_argument("--fast-kernels", dest="fast_kernels", default="all",
+                    help="native training kernels to use: all, none, or a comma list (train/kernels.py NAMES); on a "
+                         "GPU the first step then fails if an enabled kernel fell back to PyTorch")
     ap.add_argument("--export", type=Path)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--teacher-preset", dest="teacher_preset", default="",
                     help="teacher mode on a GPU: run this (block-FP8) preset on the serving kernels, e.g. "
                          "qwen3next_80b_teacher; empty: score with the student itself")
     args = ap.parse_args(argv)
+    from . import kernels
+    kernels.enable(args.fast_kernels)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -243,7 +248,10 @@ def main(argv=None):
                                                 qc.direction) / ids.numel())
             norm = 0.0
         else:
+            kernels.reset()
             loss, norm = train_step(student, opt, ids, t, qc, signs)
+            if step == start and dev.type == "cuda":
+                kernels.assert_step_calls(no_fallback=True)  # an enabled native kernel must not fall back
         if dev.type == "cuda":
             torch.cuda.synchronize()
         dt = time.perf_counter() - t0

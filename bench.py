@@ -419,8 +419,12 @@ def qad_main(args):
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
+    from arc_forge_2026_b200.train import kernels
+    for i in range(args.warmup):
+        if i == args.warmup - 1:
+            kernels.reset()
         one_step(dev_in)
+    kernels.assert_step_calls(no_fallback=True)  # every native training kernel ran; none fell back to PyTorch
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()

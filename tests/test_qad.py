@@ -1,4 +1,5 @@
 """QAD student, fused loss and optimizer on CPU (oracle paths) against the reference model and plain autograd."""
+import pytest
 import torch
 
 from arc_forge_2026_b200.config import preset
@@ -83,3 +84,26 @@ def test_gradient_accumulation_matches_one_batch():
     # (0.2% apart); every other gradient agrees to fp32 summation order
     for a, b in zip(*grads):
         assert ((a - b).norm() / b.norm().clamp_min(1e-30)).item() < 5e-3
+
+
+def test_kernel_registry_counts_and_rejects_fallbacks():
+    from arc_forge_2026_b200.train import kernels
+    old = set(kernels.NAMES)
+    try:
+        assert kernels.enable("rms_norm,swiglu") == {"rms_norm", "swiglu"}
+        assert kernels.use("rms_norm") and not kernels.use("gdn_chunk")
+        kernels.reset()
+        kernels.hit("rms_norm", True)
+        kernels.hit("rms_norm", True)
+        kernels.hit("gdn_chunk", False)  # disabled: a fallback there is allowed
+        assert kernels.assert_step_calls({"rms_norm": 2})["native"]["rms_norm"] == 2
+        kernels.hit("swiglu", False)
+        with pytest.raises(RuntimeError, match="swiglu"):
+            kernels.assert_step_calls()
+        with pytest.raises(RuntimeError, match="expected 3"):
+            kernels.assert_step_calls({"rms_norm": 3}, no_fallback=False)
+        with pytest.raises(ValueError):
+            kernels.enable("not_a_kernel")
+        assert kernels.enable("none") == set()
+    finally:
+        kernels.enable(sorted(old))
