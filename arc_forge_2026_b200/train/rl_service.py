@@ -21,7 +21,7 @@ gloo group with ``broadcast_object_list``, so the GPU process group carries only
 
 Batch (``batch`` inline or a ``torch.save`` file at ``batch_path``): ``ids`` [B, T] int64 input tokens, ``labels``
 [B, T] int64 next tokens, ``mask`` [B, T] (1 = trained), ``advantages`` [B, T] or [B], ``behavior_logp`` [B, T]
-(the sampler's log-probabilities), optional ``temperature`` (default 1.0) and ``routing`` [B*T, layers, top_k]
+(the sampler's log-probabilities; absent: on-policy), optional ``temperature`` (default 1.0) and ``routing`` [B*T, layers, top_k]
 (routing replay, forced).
 """
 from __future__ import annotations
@@ -80,7 +80,6 @@ class RLTrainer:
         if adv.dim() == 1:
             adv = adv[:, None].expand_as(ids)
         adv = adv.reshape(-1)
-        beh = b["behavior_logp"].float().to(dev).reshape(-1)
         T = float(b.get("temperature", 1.0))
         if "routing" in b:
             if self.replay is None:
@@ -90,6 +89,9 @@ class RLTrainer:
             self.replay.set_routing(b["routing"].long())
         h = self.student.hidden(ids).reshape(ids.numel(), -1)
         logp, ent = selective_logprob(h, self.student.lm_head, labels.reshape(-1), T)
+        # the sampler's log-probabilities; without them the batch is treated as on-policy (ratio 1)
+        beh = (b["behavior_logp"].float().to(dev).reshape(-1) if b.get("behavior_logp") is not None
+               else logp.detach())
         algo = cmd.get("algo", "bpo")
         if algo == "bpo":
             loss = bpo_loss(logp, beh, adv, mask, clip=tuple(cmd.get("clip", (0.2, 0.28))))
