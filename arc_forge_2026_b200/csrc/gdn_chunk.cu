@@ -75,6 +75,13 @@ __global__ void __launch_bounds__(gck::THREADS) gdn_chunk_scan_kernel(GdnScanArg
     const int i = REV ? n - 1 - step : step;
     const size_t ci = (size_t)bh * n + i;
     const int b = step & 1;
+    if (a.reset && (REV ? (i + 1 < n && a.reset[i + 1]) : a.reset[i])) {  // a new sequence starts here
+#pragma unroll
+      for (int j = 0; j < RPT; ++j) {
+        S[j] = 0.f;
+        sm.st[rg * RPT + j][c] = 0.f;
+      }
+    }
     // the other buffer was last read by the previous step, which every thread has finished
     if (t == 0 && step + 1 < n) {
       issue(step + 1, b ^ 1);
@@ -146,7 +153,8 @@ __global__ void __launch_bounds__(gck::THREADS) gdn_chunk_scan_kernel(GdnScanArg
     for (int j = step + 1; j < issued; ++j) mbar_wait(&sm.full[j & 1], (j >> 1) & 1, a.status);
   if (a.final_state)
 #pragma unroll
-    for (int j = 0; j < RPT; ++j) a.final_state[((size_t)bh * DK + rg * RPT + j) * Dv + c0 + c] = S[j];
+    for (int j = 0; j < RPT; ++j)
+      a.final_state[((size_t)bh * DK + rg * RPT + j) * Dv + c0 + c] = (REV && a.reset && a.reset[0]) ? 0.f : S[j];
 }
 
 template <bool REV, int DK>
@@ -307,6 +315,14 @@ __global__ void __launch_bounds__(gct::THREADS) gdn_chunk_scan_tc_kernel(GdnScan
   for (; step < n; ++step) {
     const size_t ci = chunk_of(step);
     const int b = step & 1;
+    const int ic = REV ? n - 1 - step : step;
+    if (a.reset && (REV ? (ic + 1 < n && a.reset[ic + 1]) : a.reset[ic])) {  // a new sequence starts here
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[j][e] = 0.f;
+      store_state_bf16();  // read by product 1 only after the barrier below
+    }
     float y[2][4], qm[4][4];
 #pragma unroll
     for (int j = 0; j < 2; ++j)
@@ -380,13 +396,15 @@ __global__ void __launch_bounds__(gct::THREADS) gdn_chunk_scan_tc_kernel(GdnScan
   }
   if (step < n && tid == 0)  // a wait gave up: let the copies still in flight land before the CTA exits (bounded)
     for (int j = step + 1; j < issued; ++j) mbar_wait(&sm.full[j & 1], (j >> 1) & 1, a.status);
-  if (a.final_state)
+  if (a.final_state) {
+    const float keep = (REV && a.reset && a.reset[0]) ? 0.f : 1.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
         *reinterpret_cast<float2*>(a.final_state + ((size_t)bh * DK + p2r + g + 8 * h) * Dv + c0 + 8 * j + 2 * t) =
-            make_float2(S[j][2 * h], S[j][2 * h + 1]);
+            make_float2(keep * S[j][2 * h], keep * S[j][2 * h + 1]);
+  }
 }
 
 template <bool REV>

@@ -165,6 +165,9 @@ struct GdnScanArgs {
   // gdn_pack_tiles (16-byte chunk cc of row r stored at chunk cc ^ (r & 7)); null selects the fp32 SIMT path
   const __nv_bfloat16* m1h = nullptr;
   const __nv_bfloat16* m2h = nullptr;
+  // optional [n] flags (packed sequences): chunk i starts a new sequence, so the state before it is zero; forward
+  // zeroes S before chunk i, reverse stops the gradient from flowing from chunk i into chunk i - 1
+  const int* reset = nullptr;
 };
 int gdn_chunk_scan(const GdnScanArgs& a, bool reverse, cudaStream_t st);
 // fp32 [tiles, 64, 128] -> bf16 swizzled tiles for the tensor-core scan
@@ -210,9 +213,11 @@ int gdn_train_bwd_inter(const GdnTrainArgs& a, cudaStream_t st);
 int gdn_train_bwd_wy(const GdnTrainArgs& a, cudaStream_t st);
 
 // train_fused.cu: fused forward / backward of the student's element-wise and row-wise ops (bf16 I/O, fp32 math)
-int conv_silu_fwd(const void* x, int64_t ldx, const float* w, void* y, int B, int T, int Cc, cudaStream_t st);
-int conv_silu_bwd(const void* x, int64_t ldx, const float* w, const void* dy, void* dx, int B, int T, int Cc,
+// pos (optional, [B * T] int32): position of each token inside its packed sequence (taps before its start read 0)
+int conv_silu_fwd(const void* x, int64_t ldx, const float* w, void* y, int B, int T, int Cc, const int* pos,
                   cudaStream_t st);
+int conv_silu_bwd(const void* x, int64_t ldx, const float* w, const void* dy, void* dx, int B, int T, int Cc,
+                  const int* pos, cudaStream_t st);
 // row r of a strided view: (r / inner) * ld_outer + (r % inner) * ld_inner elements
 struct RowMap {
   int64_t inner = 1, ld_outer = 0, ld_inner = 0;

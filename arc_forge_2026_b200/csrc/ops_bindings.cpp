@@ -503,7 +503,7 @@ void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const
 void gdn_chunk_scan_op(const at::Tensor& m1, const at::Tensor& m2, const at::Tensor& y,
                        const c10::optional<at::Tensor>& qm, const at::Tensor& last, const c10::optional<at::Tensor>& init,
                        at::Tensor& states, at::Tensor& x, c10::optional<at::Tensor> final_state, bool reverse,
-                       bool precise) {
+                       bool precise, const c10::optional<at::Tensor>& reset) {
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&m1, &m2, &y, &last, &states, &x}) {
     AFB_CHECK_CUDA(*t);
     AFB_CHECK_DT(*t, at::kFloat);
@@ -540,6 +540,11 @@ void gdn_chunk_scan_op(const at::Tensor& m1, const at::Tensor& m2, const at::Ten
   a.x = ptr<float>(x);
   a.final_state = optr<float>(final_state);
   a.status = status_ptr(m1.get_device());
+  if (reset) {
+    AFB_CHECK_DT(reset.value(), at::kInt);
+    TORCH_CHECK(reset->numel() == a.n_chunks, "reset: one flag per chunk");
+    a.reset = ptr<int>(reset.value());
+  }
   at::Tensor m1h, m2h;
   if (!precise && a.Dk == 128 && a.C == 64 && a.Dv % 32 == 0) {  // tensor-core path: bf16 swizzled M1 / M2 tiles
     const int64_t tiles = (int64_t)a.BH * a.n_chunks;
@@ -631,7 +636,8 @@ void gdn_train_op(int64_t stage, const std::vector<c10::optional<at::Tensor>>& t
 void gdn_chunk_scan_tiles_op(const at::Tensor& m1h, const at::Tensor& m2h, const at::Tensor& y,
                              const c10::optional<at::Tensor>& qm, const at::Tensor& last,
                              const c10::optional<at::Tensor>& init, at::Tensor& states, at::Tensor& x,
-                             c10::optional<at::Tensor> final_state, bool reverse) {
+                             c10::optional<at::Tensor> final_state, bool reverse,
+                             const c10::optional<at::Tensor>& reset) {
   AFB_CHECK_DT(m1h, at::kBFloat16);
   AFB_CHECK_DT(m2h, at::kBFloat16);
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&y, &last, &states, &x}) {
@@ -662,6 +668,11 @@ void gdn_chunk_scan_tiles_op(const at::Tensor& m1h, const at::Tensor& m2h, const
   a.x = ptr<float>(x);
   a.final_state = optr<float>(final_state);
   a.status = status_ptr(y.get_device());
+  if (reset) {
+    AFB_CHECK_DT(reset.value(), at::kInt);
+    TORCH_CHECK(reset->numel() == a.n_chunks, "reset: one flag per chunk");
+    a.reset = ptr<int>(reset.value());
+  }
   check_rc(afb::gdn_chunk_scan(a, reverse, stream()), "gdn_chunk_scan_tiles");
 }
 
@@ -687,22 +698,29 @@ static afb::RowMap row_map(const at::Tensor& t, const char* what) {
 }
 
 void conv_silu_op(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, c10::optional<at::Tensor> dy,
-                  c10::optional<at::Tensor> dx) {
+                  c10::optional<at::Tensor> dx, c10::optional<at::Tensor> pos) {
   check_rows(x, "conv_silu x");
   TORCH_CHECK(x.dim() == 3 && x.stride(0) == x.size(1) * x.stride(1), "x [B, T, C] with evenly strided rows");
   AFB_CHECK_DT(w, at::kFloat);
   AFB_CHECK_CONTIG(w);
   TORCH_CHECK(w.size(0) == x.size(2) && w.size(1) == 4, "w [C, 4]");
   const int B = x.size(0), T = x.size(1), Cc = x.size(2);
+  const int* pp = nullptr;
+  if (pos) {
+    AFB_CHECK_DT(pos.value(), at::kInt);
+    AFB_CHECK_CONTIG(pos.value());
+    TORCH_CHECK(pos->numel() == (int64_t)B * T, "pos: one position per token");
+    pp = ptr<int>(pos.value());
+  }
   if (dy) {
     AFB_CHECK_CONTIG(dy.value());
     AFB_CHECK_CONTIG(dx.value());
     check_rc(afb::conv_silu_bwd(x.data_ptr(), x.stride(1), ptr<float>(w), dy->data_ptr(), dx->data_ptr(), B, T, Cc,
-                                stream()),
+                                pp, stream()),
              "conv_silu_bwd");
   } else {
     AFB_CHECK_CONTIG(y);
-    check_rc(afb::conv_silu_fwd(x.data_ptr(), x.stride(1), ptr<float>(w), y.data_ptr(), B, T, Cc, stream()),
+    check_rc(afb::conv_silu_fwd(x.data_ptr(), x.stride(1), ptr<float>(w), y.data_ptr(), B, T, Cc, pp, stream()),
              "conv_silu_fwd");
   }
 }
@@ -938,15 +956,18 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
   m.def("gdn_train", &gdn_train_op);
-  m.def("conv_silu", &conv_silu_op);
+  m.def("conv_silu", &conv_silu_op, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("dy"), py::arg("dx"),
+        py::arg("pos") = py::none());
   m.def("rmsnorm_train", &rmsnorm_train_op);
   m.def("swiglu_train", &swiglu_train_op);
   m.def("moe_combine_train", &moe_combine_train_op);
   m.def("moe_dispatch_bwd", &moe_dispatch_bwd_op);
-  m.def("gdn_chunk_scan_tiles", &gdn_chunk_scan_tiles_op);
+  m.def("gdn_chunk_scan_tiles", &gdn_chunk_scan_tiles_op, py::arg("m1h"), py::arg("m2h"), py::arg("y"), py::arg("qm"),
+        py::arg("last"), py::arg("init"), py::arg("states"), py::arg("x"), py::arg("final_state"), py::arg("reverse"),
+        py::arg("reset") = py::none());
   m.def("gdn_chunk_scan", &gdn_chunk_scan_op, py::arg("m1"), py::arg("m2"), py::arg("y"), py::arg("qm"),
         py::arg("last"), py::arg("init"), py::arg("states"), py::arg("x"), py::arg("final_state"), py::arg("reverse"),
-        py::arg("precise") = false);
+        py::arg("precise") = false, py::arg("reset") = py::none());
   m.def("paged_attention", &paged_attention_op, py::arg("q"), py::arg("kcache"), py::arg("vcache"),
         py::arg("block_table"), py::arg("seq_lens"), py::arg("q_per_seq"), py::arg("scale"), py::arg("out"),
         py::arg("gate"), py::arg("gate_ld"), py::arg("gate_head_stride"), py::arg("splits"),

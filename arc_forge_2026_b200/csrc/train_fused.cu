@@ -40,9 +40,10 @@ using namespace tfu;
 
 // ------------------------------------------------------------------------------------------------ conv + SiLU
 // thread: 8 channels x RUN tokens of one sequence, sliding window over the 3 previous inputs
+// pos (optional, [B * T]): position of each token inside its packed sequence; taps before the sequence start read 0
 __global__ void __launch_bounds__(256) conv_silu_fwd_kernel(const bf16* __restrict__ x, int64_t ldx,
                                                             const float* __restrict__ w, bf16* __restrict__ y, int B,
-                                                            int T, int Cc) {
+                                                            int T, int Cc, const int* __restrict__ pos) {
   const int groups = Cc / 8, tiles = (T + RUN - 1) / RUN;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)B * tiles * groups) return;
@@ -69,9 +70,12 @@ __global__ void __launch_bounds__(256) conv_silu_fwd_kernel(const bf16* __restri
   for (int t = t0; t < t1; ++t) {
     float cur[8], out[8];
     unpack8(*reinterpret_cast<const uint4*>(x + ((int64_t)b * T + t) * ldx + c0), cur);
+    const int ps = pos ? pos[(int64_t)b * T + t] : 3;
+    const float m0 = ps >= 3 ? 1.f : 0.f, m1 = ps >= 2 ? 1.f : 0.f, m2 = ps >= 1 ? 1.f : 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float p = wk[i][0] * win[0][i] + wk[i][1] * win[1][i] + wk[i][2] * win[2][i] + wk[i][3] * cur[i];
+      const float p = m0 * wk[i][0] * win[0][i] + m1 * wk[i][1] * win[1][i] + m2 * wk[i][2] * win[2][i] +
+                      wk[i][3] * cur[i];
       out[i] = p * sigmoidf(p);
       win[0][i] = win[1][i];
       win[1][i] = win[2][i];
@@ -84,7 +88,8 @@ __global__ void __launch_bounds__(256) conv_silu_fwd_kernel(const bf16* __restri
 // dx[t] = sum_k w[k] dpre[t+3-k],  dpre = dy * silu'(pre): the thread recomputes pre for its tokens and the 3 after
 __global__ void __launch_bounds__(256) conv_silu_bwd_kernel(const bf16* __restrict__ x, int64_t ldx,
                                                             const float* __restrict__ w, const bf16* __restrict__ dy,
-                                                            bf16* __restrict__ dx, int B, int T, int Cc) {
+                                                            bf16* __restrict__ dx, int B, int T, int Cc,
+                                                            const int* __restrict__ pos) {
   const int groups = Cc / 8, tiles = (T + RUN - 1) / RUN;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)B * tiles * groups) return;
@@ -100,6 +105,7 @@ __global__ void __launch_bounds__(256) conv_silu_bwd_kernel(const bf16* __restri
     wk[i][3] = v.w;
   }
   float win[3][8], dp[3][8];  // x[s-3..s-1]; dpre[s-3..s-1]
+  int pw[3] = {3, 3, 3};      // positions of s-3..s-1 (with pos: the taps of those outputs that are live)
 #pragma unroll
   for (int s = 0; s < 3; ++s) {
     const int t = t0 - 3 + s;
@@ -119,19 +125,26 @@ __global__ void __launch_bounds__(256) conv_silu_bwd_kernel(const bf16* __restri
     }
     unpack8(xv, cur);
     unpack8(gv, g);
+    const int ps = (pos && s < T) ? pos[(int64_t)b * T + s] : 3;
+    const float m0 = ps >= 3 ? 1.f : 0.f, m1 = ps >= 2 ? 1.f : 0.f, m2 = ps >= 1 ? 1.f : 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float p = wk[i][0] * win[0][i] + wk[i][1] * win[1][i] + wk[i][2] * win[2][i] + wk[i][3] * cur[i];
+      const float p = m0 * wk[i][0] * win[0][i] + m1 * wk[i][1] * win[1][i] + m2 * wk[i][2] * win[2][i] +
+                      wk[i][3] * cur[i];
       const float sg = sigmoidf(p);
       dcur[i] = g[i] * sg * (1.f + p * (1.f - sg));
     }
-    if (s >= t0 + 3) {  // dx[s-3] complete
+    if (s >= t0 + 3) {  // dx[s-3] complete: output s-3+j used x[s-3] through tap 3-j when its position >= j
+      const float a1 = pw[1] >= 1 ? 1.f : 0.f, a2 = pw[2] >= 2 ? 1.f : 0.f;
       float out[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        out[i] = wk[i][3] * dp[0][i] + wk[i][2] * dp[1][i] + wk[i][1] * dp[2][i] + wk[i][0] * dcur[i];
+        out[i] = wk[i][3] * dp[0][i] + a1 * wk[i][2] * dp[1][i] + a2 * wk[i][1] * dp[2][i] + m0 * wk[i][0] * dcur[i];
       *reinterpret_cast<uint4*>(dx + ((int64_t)b * T + s - 3) * Cc + c0) = pack8(out);
     }
+    pw[0] = pw[1];
+    pw[1] = pw[2];
+    pw[2] = ps;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       win[0][i] = win[1][i];
@@ -144,18 +157,19 @@ __global__ void __launch_bounds__(256) conv_silu_bwd_kernel(const bf16* __restri
   }
 }
 
-int conv_silu_fwd(const void* x, int64_t ldx, const float* w, void* y, int B, int T, int Cc, cudaStream_t st) {
-  if (Cc % 8 || ldx % 8 || B < 1 || T < 1) return 3;
-  const int64_t n = (int64_t)B * ((T + RUN - 1) / RUN) * (Cc / 8);
-  conv_silu_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const bf16*)x, ldx, w, (bf16*)y, B, T, Cc);
-  return (int)cudaGetLastError();
-}
-int conv_silu_bwd(const void* x, int64_t ldx, const float* w, const void* dy, void* dx, int B, int T, int Cc,
+int conv_silu_fwd(const void* x, int64_t ldx, const float* w, void* y, int B, int T, int Cc, const int* pos,
                   cudaStream_t st) {
   if (Cc % 8 || ldx % 8 || B < 1 || T < 1) return 3;
   const int64_t n = (int64_t)B * ((T + RUN - 1) / RUN) * (Cc / 8);
+  conv_silu_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const bf16*)x, ldx, w, (bf16*)y, B, T, Cc, pos);
+  return (int)cudaGetLastError();
+}
+int conv_silu_bwd(const void* x, int64_t ldx, const float* w, const void* dy, void* dx, int B, int T, int Cc,
+                  const int* pos, cudaStream_t st) {
+  if (Cc % 8 || ldx % 8 || B < 1 || T < 1) return 3;
+  const int64_t n = (int64_t)B * ((T + RUN - 1) / RUN) * (Cc / 8);
   conv_silu_bwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const bf16*)x, ldx, w, (const bf16*)dy,
-                                                                    (bf16*)dx, B, T, Cc);
+                                                                    (bf16*)dx, B, T, Cc, pos);
   return (int)cudaGetLastError();
 }
 

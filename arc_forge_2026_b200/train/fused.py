@@ -30,29 +30,49 @@ def _gpu_bf16(*ts) -> bool:
 
 class _ConvSiLU(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w):
+    def forward(ctx, x, w, pos):
         y = torch.empty(x.shape, dtype=_BF, device=x.device)
-        _ext().conv_silu(x, w, y, None, None)
-        ctx.save_for_backward(x, w)
+        _ext().conv_silu(x, w, y, None, None, pos)
+        ctx.save_for_backward(x, w, pos)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        x, w = ctx.saved_tensors
+        x, w, pos = ctx.saved_tensors
         dx = torch.empty(x.shape, dtype=_BF, device=x.device)
-        _ext().conv_silu(x, w, dx, dy.to(_BF).contiguous(), dx)
-        return dx, None
+        _ext().conv_silu(x, w, dx, dy.to(_BF).contiguous(), dx, pos)
+        return dx, None, None
 
 
-def conv_silu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """Causal depthwise conv (kernel 4, zero history) + SiLU over x [B, T, C] (a strided view is fine); frozen w."""
+def conv_silu(x: torch.Tensor, w: torch.Tensor, pos: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal depthwise conv (kernel 4, zero history) + SiLU over x [B, T, C] (a strided view is fine); frozen w.
+    ``pos`` [B, T] (packed sequences): each token's position inside its sequence; taps before the start read 0."""
     if (kernels.use("conv_silu") and _gpu_bf16(x) and x.dim() == 3 and w.shape[-1] == 4 and x.shape[-1] % 8 == 0
             and x.stride(1) % 8 == 0 and x.stride(0) == x.shape[1] * x.stride(1) and not w.requires_grad):
         kernels.hit("conv_silu", True)
-        return _ConvSiLU.apply(x, w.float().contiguous())
+        return _ConvSiLU.apply(x, w.float().contiguous(), None if pos is None else pos.int().contiguous())
     if x.is_cuda:
         kernels.hit("conv_silu", False)
-    return R.causal_conv1d(x, w)[0]
+    if pos is None:
+        return R.causal_conv1d(x, w)[0]
+    return conv_silu_reference(x, w, pos)
+
+
+def conv_silu_reference(x, w, pos):
+    """Plain-torch causal conv + SiLU with per-token sequence positions (the packed-sequence oracle)."""
+    B, T, Cc = x.shape
+    K = w.shape[1]
+    xf = x.float()
+    pre = torch.zeros(B, T, Cc, dtype=torch.float32, device=x.device)
+    for k in range(K):
+        lag = K - 1 - k
+        if lag >= T:
+            continue
+        shifted = torch.zeros_like(xf)
+        shifted[:, lag:] = xf[:, : T - lag]
+        live = (pos >= lag).to(xf.dtype)[..., None]
+        pre = pre + w[:, k].float() * shifted * live
+    return F.silu(pre).to(x.dtype)
 
 
 class _RMSNorm(torch.autograd.Function):

@@ -21,13 +21,14 @@ from __future__ import annotations
 import torch
 
 
-def _scan(m1, m2, y, qm, last, init, reverse: bool, precise: bool = False):
+def _scan(m1, m2, y, qm, last, init, reverse: bool, precise: bool = False, reset=None):
     """X = Y + s1 * M1 St ; St <- e^{last} St (+ Qm) + s2 * M2^T X over chunks (forward, or reverse order).
 
     m1, m2 [BH, n, C, Dk]; y [BH, n, C, Dv]; qm [BH, n, Dk, Dv] or None; last [BH, n]; init [BH, Dk, Dv] or None.
     Returns (states before each step [BH, n, Dk, Dv], X [BH, n, C, Dv], final state [BH, Dk, Dv]).
     On CUDA with Dk = 128 the scan runs on tensor cores with bf16 operands and fp32 accumulation (the precision
-    class of the chunk kernels the reference trains with); ``precise`` selects the fp32 SIMT kernel."""
+    class of the chunk kernels the reference trains with); ``precise`` selects the fp32 SIMT kernel. ``reset`` [n]
+    int32 (packed sequences): chunk i starts a new sequence (zero state before it, no gradient across it)."""
     BH, n, C, Dk = m1.shape
     Dv = y.shape[-1]
     if m1.is_cuda:
@@ -38,19 +39,24 @@ def _scan(m1, m2, y, qm, last, init, reverse: bool, precise: bool = False):
         states = torch.empty(BH, n, Dk, Dv, device=m1.device, dtype=torch.float32)
         x = torch.empty_like(y)
         final = torch.empty(BH, Dk, Dv, device=m1.device, dtype=torch.float32)
-        ext().gdn_chunk_scan(m1, m2, y, qm, last, init, states, x, final, reverse, precise)
+        ext().gdn_chunk_scan(m1, m2, y, qm, last, init, states, x, final, reverse, precise, reset)
         return states, x, final
     s1, s2 = (1.0, -1.0) if reverse else (-1.0, 1.0)
     St = torch.zeros(BH, Dk, Dv, dtype=y.dtype) if init is None else init.clone()
     states = torch.empty(BH, n, Dk, Dv, dtype=y.dtype)
     x = torch.empty_like(y)
+    rs = None if reset is None else [bool(r) for r in reset.tolist()]
     for i in (range(n - 1, -1, -1) if reverse else range(n)):
+        if rs is not None and (rs[i + 1] if reverse and i + 1 < n else (rs[i] if not reverse else False)):
+            St = torch.zeros_like(St)
         states[:, i] = St
         xi = y[:, i] + s1 * (m1[:, i] @ St)
         x[:, i] = xi
         St = last[:, i].exp()[:, None, None] * St + s2 * (m2[:, i].transpose(-1, -2) @ xi)
         if qm is not None:
             St = St + qm[:, i]
+    if reverse and rs is not None and rs[0]:
+        St = torch.zeros_like(St)
     return states, x, St
 
 
@@ -71,10 +77,10 @@ class _InterChunk(torch.autograd.Function):
         return D, attn, qd, kd, last
 
     @staticmethod
-    def forward(ctx, q, k, u, w, gc, init, precise=False):
+    def forward(ctx, q, k, u, w, gc, init, precise=False, reset=None):
         D, attn, qd, kd, last = _InterChunk._intra(q, k, gc)
-        states, vnew, final = _scan(w, kd, u, None, last, init, reverse=False, precise=precise)
-        ctx.precise = precise
+        states, vnew, final = _scan(w, kd, u, None, last, init, reverse=False, precise=precise, reset=reset)
+        ctx.precise, ctx.reset = precise, reset
         o = qd @ states + attn @ vnew
         ctx.save_for_backward(q, k, w, gc, states, vnew)
         ctx.has_init = init is not None
@@ -88,7 +94,7 @@ class _InterChunk(torch.autograd.Function):
         P = attn.transpose(-1, -2) @ do                      # attn^T dO
         Qm = qd.transpose(-1, -2) @ do                       # qd^T dO
         dnext, dv, dS0 = _scan(kd, w, P, Qm, last, dfinal if dfinal is not None else None, reverse=True,
-                               precise=ctx.precise)
+                               precise=ctx.precise, reset=ctx.reset)
         # dnext[:, i] = dS_{i+1}; dv = dL/du = dL/d(vnew)
         dw = -(dv @ states.transpose(-1, -2))
         dqd = do @ states.transpose(-1, -2)
@@ -105,7 +111,7 @@ class _InterChunk(torch.autograd.Function):
         dgc = dgc - E
         dlast = E.sum(-1) + last.exp() * (dnext * states).sum((-1, -2))
         dgc = torch.cat([dgc[..., :-1], (dgc[..., -1] + dlast)[..., None]], -1)
-        return dq, dk, dv, dw, dgc, (dS0 if ctx.has_init else None), None
+        return dq, dk, dv, dw, dgc, (dS0 if ctx.has_init else None), None, None
 
 
 class _GdnChunkNative(torch.autograd.Function):
@@ -115,7 +121,7 @@ class _GdnChunkNative(torch.autograd.Function):
     [B, Hv, 128, 128] fp32. Backward: attn^T dO / Qm, the reverse scan, then the inter-chunk and WY gradients."""
 
     @staticmethod
-    def forward(ctx, q, k, v, g, beta):
+    def forward(ctx, q, k, v, g, beta, reset=None):
         from ..ops import C as ext
         B, T, Hk, D = q.shape
         Hv = v.shape[2]
@@ -135,12 +141,12 @@ class _GdnChunkNative(torch.autograd.Function):
         states = torch.empty(BH, n, 128, 128, **f32)
         vnew = torch.empty_like(u)
         final = torch.empty(BH, 128, 128, **f32)
-        c.gdn_chunk_scan_tiles(w_t, kd_t, u, None, last, None, states, vnew, final, False)
+        c.gdn_chunk_scan_tiles(w_t, kd_t, u, None, last, None, states, vnew, final, False, reset)
         o = torch.empty(B, T, Hv, 128, device=dev, dtype=torch.bfloat16)
         slots[11:14] = [states, vnew, o]
         c.gdn_train(1, slots, B, T, Hk, Hv)
         ctx.save_for_backward(q, k, v, g, beta, w_t, kd_t, gc, last, A, states, vnew)
-        ctx.dims = (B, T, Hk, Hv)
+        ctx.dims, ctx.reset = (B, T, Hk, Hv), reset
         return o, final.view(B, Hv, 128, 128)
 
     @staticmethod
@@ -161,7 +167,7 @@ class _GdnChunkNative(torch.autograd.Function):
         dnext, du = torch.empty_like(states), torch.empty_like(vnew)
         ds0 = torch.empty(BH, 128, 128, device=q.device, dtype=torch.float32)
         init = None if dfinal is None else dfinal.float().reshape(BH, 128, 128).contiguous()
-        c.gdn_chunk_scan_tiles(kd_t, w_t, P, Qm, last, init, dnext, du, ds0, True)
+        c.gdn_chunk_scan_tiles(kd_t, w_t, P, Qm, last, init, dnext, du, ds0, True, ctx.reset)
         del P, Qm
         f32 = dict(device=q.device, dtype=torch.float32)
         dq = torch.empty(B, T, Hv, 128, **f32)
@@ -175,7 +181,7 @@ class _GdnChunkNative(torch.autograd.Function):
         if rep > 1:
             dq = dq.view(B, T, Hk, rep, 128).sum(3)
             dk = dk.view(B, T, Hk, rep, 128).sum(3)
-        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg, dbeta
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg, dbeta, None
 
 
 def _native_ok(q, k, v, g, chunk, state, precise) -> bool:
@@ -183,18 +189,20 @@ def _native_ok(q, k, v, g, chunk, state, precise) -> bool:
             and v.shape[-1] == 128 and v.shape[2] % k.shape[2] == 0)
 
 
-def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None, precise: bool = False):
+def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None, precise: bool = False, chunk_reset=None):
     """q, k [B, T, Hk, Dk] (normalised, q scaled), v [B, T, Hv, Dv], g/beta [B, T, Hv] -> (o [B,T,Hv,Dv], state).
 
     Grouped values: value head h uses key head h // (Hv / Hk). On CUDA with Dk = Dv = 128 and no initial state the
     whole rule runs in the native kernels (bf16 operands, fp32 accumulation, o in bf16); ``precise`` keeps the
-    fp32 torch path with the fp32 scan."""
+    fp32 torch path with the fp32 scan. ``chunk_reset`` [ceil(T / chunk)] int32 (packed sequences aligned to
+    chunks, B = 1): chunk i starts a new sequence, so no state or gradient crosses into it."""
     from . import kernels
     if kernels.use("gdn_chunk") and _native_ok(q, k, v, g, chunk, state, precise):
         kernels.hit("gdn_chunk", True)
         bf = torch.bfloat16
         return _GdnChunkNative.apply(q.to(bf).contiguous(), k.to(bf).contiguous(), v.to(bf).contiguous(),
-                                     g.float().contiguous(), beta.float().contiguous())
+                                     g.float().contiguous(), beta.float().contiguous(),
+                                     None if chunk_reset is None else chunk_reset.int().contiguous())
     if q.is_cuda and not precise:
         kernels.hit("gdn_chunk", False)
     if k.shape[2] != v.shape[2]:
@@ -227,7 +235,8 @@ def chunk_gated_delta_rule(q, k, v, g, beta, chunk: int = 64, state=None, precis
     u = A @ (v * beta[..., None])                    # pseudo-values
     w = A @ (k_beta * gc.exp()[..., None])          # decayed keys
     init = None if state is None else state.to(dt).reshape(B * H, Dk, Dv)
-    o, S = _InterChunk.apply(q, k, u, w, gc, init, precise)
+    o, S = _InterChunk.apply(q, k, u, w, gc, init, precise,
+                             None if chunk_reset is None else chunk_reset.int().to(q.device).contiguous())
     o = o.reshape(B, H, n * chunk, Dv)[:, :, :T]
     return o.transpose(1, 2), S.reshape(B, H, Dk, Dv)
 

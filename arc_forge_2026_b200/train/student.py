@@ -61,6 +61,27 @@ class _Dispatch(torch.autograd.Function):
         return g.index_select(0, inv).view(-1, ctx.K, g.shape[-1]).sum(1), None, None, None
 
 
+def packed_attention(q, k, v, cu_seqlens, max_seqlen: int):
+    """Causal attention inside each segment of a packed row: q [T, Hq, D], k / v [T, Hkv, D] -> [T, Hq, D].
+    CUDA: the variable-length flash-attention kernel (library); otherwise one SDPA call per segment."""
+    if q.is_cuda:
+        try:
+            from flash_attn import flash_attn_varlen_func
+        except ImportError:  # pragma: no cover - the image ships flash_attn
+            flash_attn_varlen_func = None
+        if flash_attn_varlen_func is not None and q.dtype in (torch.bfloat16, torch.float16):
+            cu = cu_seqlens.to(device=q.device, dtype=torch.int32)
+            return flash_attn_varlen_func(q.contiguous(), k.contiguous(), v.contiguous(), cu, cu, max_seqlen,
+                                          max_seqlen, causal=True)
+    outs = []
+    bounds = cu_seqlens.tolist()
+    for s0, s1 in zip(bounds[:-1], bounds[1:]):
+        o = F.scaled_dot_product_attention(q[s0:s1].transpose(0, 1)[None], k[s0:s1].transpose(0, 1)[None],
+                                           v[s0:s1].transpose(0, 1)[None], is_causal=True, enable_gqa=True)
+        outs.append(o[0].transpose(0, 1))
+    return torch.cat(outs)
+
+
 class StudentMoE(nn.Module):
     def __init__(self, cfg: ModelConfig, router, w13_codes, w13_scales, w2_codes, w2_scales, shared_gate, shared_up,
                  shared_down, shared_expert_gate):
@@ -197,7 +218,7 @@ class StudentLayer(nn.Module):
             g["dense_bf16"].append(self.in_proj_ba)
         return g
 
-    def _attn(self, x, B, T):
+    def _attn(self, x, B, T, pack=None):
         c = self.cfg
         D = c.head_dim
         qg = self._lin("q_proj", x, True).view(B, T, c.num_attention_heads, 2 * D)
@@ -205,20 +226,24 @@ class StudentLayer(nn.Module):
         k = self._lin("k_proj", x, True).view(B, T, c.num_kv_heads, D)
         v = self._lin("v_proj", x, True).view(B, T, c.num_kv_heads, D)
         q, k = fused.rms_norm(q, self.q_norm, c.rms_norm_eps), fused.rms_norm(k, self.k_norm, c.rms_norm_eps)
-        cos, sin = R.rope_cos_sin(torch.arange(T, device=x.device), c.rotary_dim, c.rope_theta)
+        positions = torch.arange(T, device=x.device) if pack is None else pack["pos"][0]
+        cos, sin = R.rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
         q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
-        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
-                                           enable_gqa=True).transpose(1, 2).reshape(B, T, -1)
+        if pack is None:
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               is_causal=True, enable_gqa=True).transpose(1, 2).reshape(B, T, -1)
+        else:
+            o = packed_attention(q[0], k[0], v[0], pack["cu_seqlens"], pack["max_seqlen"]).reshape(B, T, -1)
         o = o * torch.sigmoid(gate.float()).to(o.dtype)
         return self._lin("o_proj", o, False)
 
-    def _gdn(self, x, B, T):
+    def _gdn(self, x, B, T, pack=None):
         c = self.cfg
         qkvz = self._lin("in_proj_qkvz", x, True)
         ba = self._lin("in_proj_ba", x, False)
         mixed, z = qkvz[..., : c.gdn_conv_dim], qkvz[..., c.gdn_conv_dim:]
         b, a = ba[..., : c.linear_num_value_heads], ba[..., c.linear_num_value_heads:]
-        mixed = fused.conv_silu(mixed, self.conv1d)
+        mixed = fused.conv_silu(mixed, self.conv1d, None if pack is None else pack["pos"])
         nk = c.linear_num_key_heads * c.linear_key_head_dim
         q = mixed[..., :nk].reshape(B, T, c.linear_num_key_heads, -1)
         k = mixed[..., nk:2 * nk].reshape(B, T, c.linear_num_key_heads, -1)
@@ -226,16 +251,18 @@ class StudentLayer(nn.Module):
         q = R.l2norm(q) * c.linear_key_head_dim ** -0.5  # grouped values: chunk_gated_delta_rule maps heads
         k = R.l2norm(k)
         g, beta = R.gdn_gates(b, a, self.A_log, self.dt_bias)
-        o, _ = chunk_gated_delta_rule(q, k, v, g, beta)
+        o, _ = chunk_gated_delta_rule(q, k, v, g, beta, chunk_reset=None if pack is None else pack["chunk_reset"])
         o = fused.gated_rms_norm(o.to(x.dtype), z.reshape(B, T, c.linear_num_value_heads, -1), self.g_norm,
                                  c.rms_norm_eps)
         return self._lin("out_proj", o.reshape(B, T, -1), True)
 
-    def forward(self, x):
+    def forward(self, x, pack=None):
         c = self.cfg
         B, T, H = x.shape
+        if pack is not None and B != 1:
+            raise ValueError("packed bins are single rows (B = 1)")
         y = fused.rms_norm(x, self.in_norm, c.rms_norm_eps)
-        x = x + (self._attn(y, B, T) if self.kind == FULL else self._gdn(y, B, T))
+        x = x + (self._attn(y, B, T, pack) if self.kind == FULL else self._gdn(y, B, T, pack))
         y = fused.rms_norm(x, self.post_norm, c.rms_norm_eps)
         return x + self.moe(y.reshape(B * T, H)).reshape(B, T, H)
 
@@ -267,13 +294,15 @@ class QADStudent(nn.Module):
                 g[k] += v
         return g
 
-    def hidden(self, ids):
+    def hidden(self, ids, pack: dict | None = None):
+        """Final hidden states of ``ids`` [B, T]; ``pack`` (``train/packing.py`` ``PackedBin.forward_args``) makes
+        the row a packed bin of several sequences (B = 1)."""
         x = F.embedding(ids, self.embed)
         for L in self.layers:
             if self.ckpt and torch.is_grad_enabled():
-                x = checkpoint(L, x, use_reentrant=False)
+                x = checkpoint(L, x, pack, use_reentrant=False)
             else:
-                x = L(x)
+                x = L(x, pack)
         return fused.rms_norm(x, self.final_norm, self.cfg.rms_norm_eps)
 
 
