@@ -14,10 +14,10 @@ import torch
 
 
 class _Offloaded:
-    __slots__ = ("host", "event", "device", "index", "prefetched", "ready")
+    __slots__ = ("host", "event", "device", "index", "stride", "prefetched", "ready")
 
-    def __init__(self, host, event, device, index):
-        self.host, self.event, self.device, self.index = host, event, device, index
+    def __init__(self, host, event, device, index, stride):
+        self.host, self.event, self.device, self.index, self.stride = host, event, device, index, stride
         self.prefetched = None
         self.ready = None
 
@@ -42,7 +42,7 @@ class CheckpointOffload(torch.autograd.graph.saved_tensors_hooks):
             ev = torch.cuda.Event()
             ev.record(self.stream)
         t.record_stream(self.stream)  # t's memory is not reused before the copy has read it
-        item = _Offloaded(host, ev, t.device, len(self.items))
+        item = _Offloaded(host, ev, t.device, len(self.items), t.stride())
         self.items.append(item)
         self.bytes_offloaded += t.numel() * t.element_size()
         return item
@@ -50,7 +50,10 @@ class CheckpointOffload(torch.autograd.graph.saved_tensors_hooks):
     def _fetch(self, item: _Offloaded):
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(item.event)
-            dev = item.host.to(item.device, non_blocking=True)
+            # the saved tensor's own layout (a transposed weight stays transposed): the backward then runs the same
+            # kernels on the same layout as without offload, so the gradients are bitwise identical
+            dev = torch.empty_strided(item.host.size(), item.stride, dtype=item.host.dtype, device=item.device)
+            dev.copy_(item.host, non_blocking=True)
             ready = torch.cuda.Event()
             ready.record(self.stream)
         item.prefetched, item.ready = dev, ready

@@ -63,7 +63,8 @@ class _Dispatch(torch.autograd.Function):
 
 def packed_attention(q, k, v, cu_seqlens, max_seqlen: int):
     """Causal attention inside each segment of a packed row: q [T, Hq, D], k / v [T, Hkv, D] -> [T, Hq, D].
-    CUDA: the variable-length flash-attention kernel (library); otherwise one SDPA call per segment."""
+    CUDA: the variable-length flash-attention kernel (library) with its deterministic backward (the gradients stay
+    bitwise reproducible); otherwise one SDPA call per segment."""
     if q.is_cuda:
         try:
             from flash_attn import flash_attn_varlen_func
@@ -72,7 +73,7 @@ def packed_attention(q, k, v, cu_seqlens, max_seqlen: int):
         if flash_attn_varlen_func is not None and q.dtype in (torch.bfloat16, torch.float16):
             cu = cu_seqlens.to(device=q.device, dtype=torch.int32)
             return flash_attn_varlen_func(q.contiguous(), k.contiguous(), v.contiguous(), cu, cu, max_seqlen,
-                                          max_seqlen, causal=True)
+                                          max_seqlen, causal=True, deterministic=True)
     outs = []
     bounds = cu_seqlens.tolist()
     for s0, s1 in zip(bounds[:-1], bounds[1:]):
