@@ -17,6 +17,10 @@ server-side sessions and ``/close_session``, usage accounting):
                                  package for the native engine, a state-dict file for the CPU engine)
     GET  /metrics                Prometheus text (requests, tokens, active sessions, step latency)
 
+With ``--session-ledger DIR`` every request is recorded in a TITO session ledger (``formats/tito.py``): a
+Responses-API session is one segment (each turn appends its new input tokens and its generated tokens; /close_session
+closes it), any other request a single-append segment.
+
 One engine thread owns the engine: it admits queued requests when a session slot is free, runs ``engine.step()``
 while any request is live and hands emitted tokens to the waiting HTTP handlers through their event loops.
 
@@ -51,13 +55,16 @@ class Request:
     t0: float = field(default_factory=time.perf_counter)
     rid: str = ""
     aborted: bool = False
+    out: list = field(default_factory=list)
 
 
 class EngineLoop:
     """Runs the engine on one thread; requests come in through ``submit`` and tokens go out per request."""
 
-    def __init__(self, engine, eos_id: int | None = None, metrics=None):
+    def __init__(self, engine, eos_id: int | None = None, metrics=None, ledger=None):
         self.engine = engine
+        self.ledger = ledger                      # formats.tito.LedgerWriter or None
+        self.ledger_segs: dict[str, int] = {}     # session_id -> open ledger segment
         self.eos_id = eos_id
         self.metrics = metrics
         self.cv = threading.Condition()
@@ -106,6 +113,9 @@ class EngineLoop:
         with self.cv:
             sid = self.keyed.pop(key, None)
             self.transcripts.pop(key, None)
+            seg = self.ledger_segs.pop(key, None)
+            if seg is not None:
+                self.ledger.close_segment(seg)
             if sid is not None and sid not in self.live and sid in self.engine.sessions:
                 self.engine.release(sid)
             return sid is not None
@@ -149,6 +159,7 @@ class EngineLoop:
             if req.n_out >= req.max_new:
                 break
             req.n_out += 1
+            req.out.append(int(t))
             self._emit(req, ("token", t))
             if self.metrics:
                 self.metrics["tokens"].inc()
@@ -158,9 +169,30 @@ class EngineLoop:
         if req.n_out >= req.max_new:
             self._finish(req)
 
+    def _record(self, req: Request, reason: str | None):
+        """The request's tokens into the session ledger (the tail: this turn's new input tokens)."""
+        lg = self.ledger
+        if lg is None:
+            return
+        stop = self.eos_id is not None and req.out and req.out[-1] == self.eos_id
+        fin = {"type": "abort" if reason == "abort" else ("stop" if stop else "length")}
+        if stop:
+            fin["matched"] = int(self.eos_id)
+        if req.session_key is None:
+            seg = lg.open_segment(None)
+            lg.append(seg, req.rid, req.prompt, req.out, fin, t0=None)
+            lg.close_segment(seg)
+            return
+        seg = self.ledger_segs.get(req.session_key)
+        first = seg is None
+        if first:
+            seg = self.ledger_segs[req.session_key] = lg.open_segment(req.session_key)
+        lg.append(seg, req.rid, req.prompt if first else (req.extend or []), req.out, fin)
+
     def _finish(self, req: Request, reason: str | None = None):
         self.live.pop(req.sid, None)
         self.by_rid.pop(req.rid, None)
+        self._record(req, reason)
         eng = self.engine
         if req.session_key is None:
             if req.sid in eng.sessions:
@@ -244,19 +276,21 @@ def _metrics():
     }
 
 
-def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200"):
+def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200", ledger=None):
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
     tok = tokenizer or ByteTokenizer()
     registry, metrics = _metrics()
-    loop_ = EngineLoop(engine, getattr(tok, "eos_id", None), metrics)
+    loop_ = EngineLoop(engine, getattr(tok, "eos_id", None), metrics, ledger)
     from contextlib import asynccontextmanager
 
     @asynccontextmanager
     async def lifespan(_app):
         yield
         loop_.shutdown()
+        if ledger is not None:
+            ledger.close()
 
     app = FastAPI(title="arc_forge_2026_b200", lifespan=lifespan)
     app.state.engine_loop = loop_
@@ -431,6 +465,8 @@ def main(argv=None):
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--session-ledger", dest="session_ledger", default=None,
+                    help="directory of the TITO session ledger (one instance subdirectory per server run)")
     args = ap.parse_args(argv)
     import uvicorn
     from .tokenizer import HFTokenizer
@@ -438,7 +474,11 @@ def main(argv=None):
     tok = HFTokenizer(args.tokenizer) if args.tokenizer else ByteTokenizer()
     if not args.tokenizer and cfg.vocab_size < ByteTokenizer.vocab_size:
         raise SystemExit(f"vocab {cfg.vocab_size} is smaller than the byte tokenizer's {ByteTokenizer.vocab_size}")
-    uvicorn.run(create_app(engine, tok, cfg.name), host=args.host, port=args.port, log_level="info")
+    ledger = None
+    if args.session_ledger:
+        from ..formats.tito import LedgerWriter
+        ledger = LedgerWriter(args.session_ledger, meta={"model": cfg.name, "vocab_size": cfg.vocab_size})
+    uvicorn.run(create_app(engine, tok, cfg.name, ledger), host=args.host, port=args.port, log_level="info")
 
 
 if __name__ == "__main__":
