@@ -19,6 +19,7 @@
 #define AFB_ERR_PEER_TIMEOUT 0x2u
 #define AFB_ERR_BOUNDS 0x4u
 #define AFB_ERR_TMEM 0x8u
+#define AFB_ERR_MISMATCH 0x10u  // a cross-rank agreement check found different values
 
 #ifndef AFB_WAIT_NS
 #define AFB_WAIT_NS 2000000000ull  // bounded waits give up after 2 s (globaltimer)

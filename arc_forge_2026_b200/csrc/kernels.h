@@ -260,6 +260,17 @@ int ep_wait(const EpArgs& a, int type, uint32_t* status, cudaStream_t st);
 int ep_gather(const EpArgs& a, const int* row_token, const int* nrows_dev, int rows_cap, void* xq, float* xs,
               int ld_xs, cudaStream_t st);
 
+// guard.cu: cross-rank agreement of small int64 packets over peer memory (device-side replica check)
+struct GuardArgs {
+  int world = 1, rank = 0, n_max = 0;
+  uint8_t* peer[EP_MAX_RANKS] = {};
+  size_t off_slots = 0;  // int64 [2 parities][EP_MAX_RANKS sources][n_max]
+  size_t off_flags = 0;  // uint64 [EP_MAX_RANKS sources]
+  unsigned long long* calls = nullptr;  // local: checks issued
+  int* mismatches = nullptr;            // local: running count of differing elements
+};
+int guard_check(const GuardArgs& a, const int64_t* packet, int n, uint32_t* status, cudaStream_t st);
+
 // zero_comm.cu: ZeRO-style optimizer step over peer memory (symmetric heap)
 constexpr int ZERO_GRADS = 0, ZERO_NORM = 1, ZERO_PARAMS = 2;
 struct ZeroArgs {

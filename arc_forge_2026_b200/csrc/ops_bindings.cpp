@@ -351,6 +351,32 @@ void qsa_finalize_op(const std::vector<at::Tensor>& idx_raw, const std::vector<a
 }
 
 // ZeRO step over peer memory (see zero_comm.cu)
+// cross-rank agreement check (guard.cu)
+struct GuardCtx {
+  afb::GuardArgs a;
+  GuardCtx(int64_t world, int64_t rank, std::vector<int64_t> peers, int64_t off_slots, int64_t off_flags, int64_t n_max,
+           const at::Tensor& calls, const at::Tensor& mismatches) {
+    TORCH_CHECK(world >= 1 && world <= afb::EP_MAX_RANKS && (int64_t)peers.size() == world, "GuardCtx: world");
+    AFB_CHECK_DT(calls, at::kLong);
+    AFB_CHECK_DT(mismatches, at::kInt);
+    a.world = (int)world;
+    a.rank = (int)rank;
+    a.n_max = (int)n_max;
+    for (int p = 0; p < world; ++p) a.peer[p] = reinterpret_cast<uint8_t*>((uintptr_t)peers[p]);
+    a.off_slots = off_slots;
+    a.off_flags = off_flags;
+    a.calls = reinterpret_cast<unsigned long long*>(calls.data_ptr());
+    a.mismatches = ptr<int>(mismatches);
+  }
+  void check(const at::Tensor& packet) {
+    AFB_CHECK_DT(packet, at::kLong);
+    AFB_CHECK_CONTIG(packet);
+    int d = 0;
+    cudaGetDevice(&d);
+    check_rc(afb::guard_check(a, ptr<int64_t>(packet), packet.numel(), status_ptr(d), stream()), "guard_check");
+  }
+};
+
 struct ZeroCtx {
   afb::ZeroArgs a;
   ZeroCtx(int64_t world, int64_t rank, std::vector<int64_t> peers, int64_t off_flags, int64_t off_norm,
@@ -974,6 +1000,10 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("pages_per_split"), py::arg("window"), py::arg("bt_row"), py::arg("sp_count") = py::none(),
         py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none());
   m.def("qsa_prep", &qsa_prep_op);
+  py::class_<GuardCtx>(m, "GuardCtx")
+      .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, const at::Tensor&,
+                    const at::Tensor&>())
+      .def("check", &GuardCtx::check);
   py::class_<ZeroCtx>(m, "ZeroCtx")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, const at::Tensor&, const at::Tensor&,
                     const at::Tensor&>())

@@ -355,7 +355,7 @@ class HybridModel:
                 if qsa is not None and b.attn_bt_row is None:
                     qsa_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, qsa.fin, key, qsa.ws,
                                   attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
-                                  splits=qsa.splits, hs=qsa.hs, layer=ai)
+                                  splits=qsa.splits, hs=qsa.hs, layer=ai, replay=qsa.replay)
                 elif b.attn_bt_row is not None:
                     # prefill: virtual rows of attn_q_per_seq queries; rows past N are padding (scratch)
                     qp = b.attn_q_per_seq

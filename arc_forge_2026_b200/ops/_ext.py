@@ -48,6 +48,7 @@ def check_status(device: int | None = None, clear: bool = True) -> int:
     if clear and word:
         st.zero_()
     if word:
-        names = {1: "mbarrier wait timed out", 2: "peer wait timed out", 4: "index out of bounds", 8: "TMEM"}
+        names = {1: "mbarrier wait timed out", 2: "peer wait timed out", 4: "index out of bounds", 8: "TMEM",
+                 16: "cross-rank mismatch"}
         raise RuntimeError("kernel status: " + ", ".join(v for k, v in names.items() if word & k))
     return word

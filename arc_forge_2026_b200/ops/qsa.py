@@ -56,6 +56,7 @@ class QsaState:
         self.model = model
         self.splits = splits
         self.hs = None  # HiSparseState when the KV history lives in host memory
+        self.replay = None  # DecisionReplay (record / force the selections; eager engine cycles only)
 
     def finalize(self, block_table, ctx_len):
         """Pooled keys for every page whose tokens are all committed (ctx_len), in every QSA layer."""
@@ -64,14 +65,54 @@ class QsaState:
                          ctx_len, m.rope_cos, m.rope_sin, m.cfg.rotary_dim, m.cfg.rms_norm_eps)
 
 
+class DecisionReplay:
+    """Record the sparse-attention decisions of every QSA call (the per-session page union, its logical pages and
+    row masks) or force recorded ones in place of the selection (the reference's decision replay,
+    ``training/work/qwen38fn_lora/decision_replay.py``): kernels and configurations are then compared on identical
+    selections. Calls are matched in order; the decisions hold physical pages, so a forced run must allocate pages as
+    the recorded one did (same engine, same inputs). Eager execution only (the log grows on the host)."""
+
+    def __init__(self, mode: str = "record", log=None):
+        if mode not in ("record", "force"):
+            raise ValueError(mode)
+        self.mode, self.log, self.cursor = mode, list(log or []), 0
+
+    def record(self, ws: QsaWorkspace, S: int):
+        self.log.append(tuple(t[:S].detach().clone() for t in (ws.u_page, ws.u_lpage, ws.u_mask, ws.u_count)))
+
+    def force(self, ws: QsaWorkspace, S: int):
+        if self.cursor >= len(self.log):
+            raise RuntimeError(f"decision replay: {len(self.log)} recorded calls, call {self.cursor + 1} asked")
+        rec = self.log[self.cursor]
+        self.cursor += 1
+        for dst, src in zip((ws.u_page, ws.u_lpage, ws.u_mask, ws.u_count), rec):
+            if src.shape[0] != S:
+                raise RuntimeError("decision replay: the forced call has a different number of sessions")
+            dst[:S].copy_(src)
+
+    def save(self, path):
+        torch.save([tuple(t.cpu() for t in rec) for rec in self.log], path)
+
+    @classmethod
+    def load(cls, path, device, mode: str = "force"):
+        return cls(mode, [tuple(t.to(device) for t in rec) for rec in torch.load(path, weights_only=True)])
+
+
 def qsa_attention(q, kcache, vcache, block_table, seq_lens, fin, idx_key, ws: QsaWorkspace, out, gate=None,
-                  gate_ld=0, gate_head_stride=0, splits: int = 1, hs=None, layer: int = 0):
+                  gate_ld=0, gate_head_stride=0, splits: int = 1, hs=None, layer: int = 0,
+                  replay: DecisionReplay | None = None):
     """q [S*W, Hq, D] (already normed / RoPE'd), ws.idx_q filled by ``qsa_prep`` for the same rows. With ``hs``
-    (a ``HiSparseState``) the selected finalised pages are first made resident from the host pool."""
+    (a ``HiSparseState``) the selected finalised pages are first made resident from the host pool; ``replay``
+    records or forces the selections."""
     c = C()
     S = seq_lens.shape[0]
-    c.qsa_select(ws.idx_q, idx_key, block_table, fin, seq_lens, ws.W, ws.K, ws.Hi, ws.u_page[:S], ws.u_lpage[:S],
-                 ws.u_mask[:S], ws.u_count[:S])
+    if replay is not None and replay.mode == "force":
+        replay.force(ws, S)
+    else:
+        c.qsa_select(ws.idx_q, idx_key, block_table, fin, seq_lens, ws.W, ws.K, ws.Hi, ws.u_page[:S],
+                     ws.u_lpage[:S], ws.u_mask[:S], ws.u_count[:S])
+        if replay is not None:
+            replay.record(ws, S)
     if hs is not None:
         hs.ctx.fetch(layer, ws.u_page, ws.u_lpage, ws.u_count, fin)
     D = q.shape[-1]

@@ -29,3 +29,9 @@ def test_fused_zero_optimizer_matches_nccl_sharded_adamw_on_two_ranks():
     r = _torchrun("tests/zero_worker.py", 2)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("\"ms_fused\":") == 2
+
+
+def test_replica_guard_detects_cross_rank_mismatch_on_two_ranks():
+    r = _torchrun("tests/guard_worker.py", 2)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count('"mismatch_raised": true') == 2

@@ -89,3 +89,39 @@ def test_select_and_sparse_attention_match_oracle(splits):
         assert lp == sorted(lp) and len(set(lp)) == n
         ref = attention_reference(q[s * W:(s + 1) * W], kc, vc, bt[s], lens[s], W, rows, gate[s * W:(s + 1) * W])
         assert _rel(out[s * W:(s + 1) * W].cpu(), ref) < 1e-2
+
+
+def test_decision_replay_forces_recorded_selections(tmp_path):
+    """A recorded run's page unions, forced into a second run with different index queries, reproduce the first
+    run's output exactly; the log survives a save / load."""
+    from arc_forge_2026_b200.ops.qsa import DecisionReplay
+    g = torch.Generator().manual_seed(5)
+    Hi, W, K, Hq, Hkv, D = 4, 5, 8, 16, 2, 256
+    lens = [900, 2000, 1500]
+    S = len(lens)
+    maxp = max((L + PAGE - 1) // PAGE for L in lens)
+    P = S * maxp + 3
+    bt = torch.randperm(P, generator=g)[:S * maxp].view(S, maxp).int().to(dev)
+    kc = torch.randn(P, Hkv, PAGE, D, generator=g).bfloat16().to(dev)
+    vc = torch.randn(P, Hkv, PAGE, D, generator=g).bfloat16().to(dev)
+    keys = torch.randn(S * maxp, 128, generator=g).bfloat16().to(dev)
+    q = torch.randn(S * W, Hq, D, generator=g).bfloat16().to(dev)
+    seq_lens = torch.tensor(lens, dtype=torch.int32).to(dev)
+    fin = torch.tensor([(L - W) // PAGE for L in lens], dtype=torch.int32).to(dev)
+    ws = QsaWorkspace(S, W, K, maxp, Hi, dev)
+    outs = []
+    rec = DecisionReplay("record")
+    for i, mode in enumerate((rec, None, "forced")):
+        ws.idx_q.copy_(torch.randn(S * W, Hi, 128, generator=torch.Generator().manual_seed(10 + min(i, 1))).bfloat16())
+        out = torch.zeros(S * W, Hq, D, dtype=torch.bfloat16, device=dev)
+        rp = mode
+        if mode == "forced":
+            rec.save(tmp_path / "dec.pt")
+            rp = DecisionReplay.load(tmp_path / "dec.pt", dev)
+        qsa_attention(q, kc, vc, bt, seq_lens, fin, keys, ws, out, replay=rp)
+        outs.append(out)
+    torch.cuda.synchronize()
+    check_status()
+    assert len(rec.log) == 1
+    assert not torch.equal(outs[0], outs[1])   # other index queries select other pages
+    assert torch.equal(outs[0], outs[2])       # forced: the recorded selection, bit for bit

@@ -117,3 +117,28 @@ def test_expert_parallel_refuses_mismatched_shapes():
     for p in ps:
         p.join(timeout=30)
     assert res == {0: "refused", 1: "refused"}
+
+
+def _host_check_worker(rank, world, port, out):
+    import os
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from arc_forge_2026_b200.parallel.guard import host_check
+    host_check([1, 2, 3])
+    try:
+        host_check([1, 2, rank])
+        ok = False
+    except RuntimeError:
+        ok = True
+    with open(f"{out}.{rank}", "w") as f:
+        f.write("1" if ok else "0")
+    dist.destroy_process_group()
+
+
+def test_host_replica_check_raises_on_every_rank(tmp_path):
+    import os
+    import torch.multiprocessing as mp
+    port = 29700 + os.getpid() % 200
+    mp.spawn(_host_check_worker, args=(2, port, str(tmp_path / "r")), nprocs=2, join=True)
+    assert (tmp_path / "r.0").read_text() == "1" and (tmp_path / "r.1").read_text() == "1"
