@@ -301,30 +301,23 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
     auto step = [&](int ts, float decay, float beta) {
       const __nv_bfloat16* kk = sm.kq[b][ts][0];
       const float vv = __bfloat162float(sm.v[b][ts][v]);
+      float f[HK];  // this thread's key values, converted once for both passes
+#pragma unroll
+      for (int j = 0; j < HK / 8; ++j) load8(kk, j, f + 8 * j);
       float mem0 = 0.f, mem1 = 0.f;  // two chains halve the dependent-FMA latency
 #pragma unroll
-      for (int j = 0; j < HK / 8; ++j) {
-        float f[8];
-        load8(kk, j, f);
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          S[8 * j + i] *= decay;
-          S[8 * j + i + 1] *= decay;
-          mem0 = fmaf(f[i], S[8 * j + i], mem0);
-          mem1 = fmaf(f[i + 1], S[8 * j + i + 1], mem1);
-        }
+      for (int i = 0; i < HK; i += 2) {
+        S[i] *= decay;
+        S[i + 1] *= decay;
+        mem0 = fmaf(f[i], S[i], mem0);
+        mem1 = fmaf(f[i + 1], S[i + 1], mem1);
       }
       float mem = mem0 + mem1;
 #pragma unroll
       for (int o = 1; o < QT; o <<= 1) mem += __shfl_xor_sync(0xffffffffu, mem, o);
       const float delta = beta * (vv - mem);
 #pragma unroll
-      for (int j = 0; j < HK / 8; ++j) {
-        float f[8];
-        load8(kk, j, f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) S[8 * j + i] = fmaf(f[i], delta, S[8 * j + i]);
-      }
+      for (int i = 0; i < HK; ++i) S[i] = fmaf(f[i], delta, S[i]);
     };
     for (int t = 0; t < np; ++t) step(t, __expf(sm.gb[b][0][2 * t]), sm.gb[b][0][2 * t + 1]);
     float* sp = a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV + (size_t)(part * HK) * DV + v;
@@ -349,9 +342,14 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
       const float ssq = warp_sum(part ? 0.f : o * o);
       if ((tid & 31) == 0) sm.red[tid >> 5] = ssq;
       __syncthreads();
-      float tot = 0.f;
+      float tot;
+      if constexpr (THREADS / 32 == 32) {
+        tot = warp_sum(sm.red[tid & 31]);  // one load per lane, not one per warp
+      } else {
+        tot = 0.f;
 #pragma unroll
-      for (int w = 0; w < THREADS / 32; ++w) tot += sm.red[w];
+        for (int w = 0; w < THREADS / 32; ++w) tot += sm.red[w];
+      }
       if (!part) {
         const size_t tok = (size_t)seq * T + t;
         const float z = __bfloat162float(sm.z[b][t][v]);
