@@ -60,6 +60,7 @@ class ModelConfig:
     # misc
     rms_norm_eps: float = 1.0e-6
     hc_count: int = 1  # hyper-connection branches; 1 = plain residual stream
+    hc_lowrank: int = 320  # rank of the hyper-connection mix projection
     init_std: float = 0.02
     # QSA sparse attention on the full-attention layers (0 = dense attention)
     qsa_block: int = 0

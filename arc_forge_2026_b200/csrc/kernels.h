@@ -260,6 +260,20 @@ int ep_wait(const EpArgs& a, int type, uint32_t* status, cudaStream_t st);
 int ep_gather(const EpArgs& a, const int* row_token, const int* nrows_dev, int rows_cap, void* xq, float* xs,
               int ld_xs, cudaStream_t st);
 
+// hc.cu: hyper-connection residual stream [rows, G, H] (bf16): grouped norm, branch mix, gated write-back, and
+// their dX-only backward; H in {256, 512, 1024, 2048, 2560}, G <= 8
+int hc_norm_fwd(const void* h, const float* w, void* zb, float* rstd, int64_t rows, int G, int H, float eps,
+                cudaStream_t st);
+int hc_norm_bwd(const void* h, const float* w, const float* rstd, const float* dzb, void* dh, int64_t rows, int G,
+                int H, cudaStream_t st);
+int hc_mix_fwd(const void* pre, const void* zb, void* x, int64_t rows, int G, int H, cudaStream_t st);
+int hc_mix_bwd(const void* pre, const void* zb, const void* dx, void* dpre, float* dzb, int64_t rows, int G, int H,
+               cudaStream_t st);
+int hc_inject_fwd(const void* h, const void* y, const void* gate, void* out, int64_t rows, int G, int H,
+                  cudaStream_t st);
+int hc_inject_bwd(const void* y, const void* gate, const void* dout, void* dy, float* dgate, int64_t rows, int G,
+                  int H, cudaStream_t st);
+
 // guard.cu: cross-rank agreement of small int64 packets over peer memory (device-side replica check)
 struct GuardArgs {
   int world = 1, rank = 0, n_max = 0;

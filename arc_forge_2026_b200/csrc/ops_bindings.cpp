@@ -830,6 +830,75 @@ void moe_dispatch_bwd_op(const at::Tensor& g, const at::Tensor& inv, int64_t K, 
            "moe_dispatch_bwd");
 }
 
+// ---- hyper-connections (hc.cu); the branch stream is [rows, G, H] contiguous bf16
+static void hc_shape(const at::Tensor& h, int64_t& rows, int& G, int& H) {
+  AFB_CHECK_DT(h, at::kBFloat16);
+  AFB_CHECK_CONTIG(h);
+  TORCH_CHECK(h.dim() >= 2, "hc: [..., G, H]");
+  H = h.size(-1);
+  G = h.size(-2);
+  rows = h.numel() / ((int64_t)G * H);
+}
+void hc_norm_op(const at::Tensor& h, const at::Tensor& w, double eps, at::Tensor& zb, at::Tensor& rstd,
+                c10::optional<at::Tensor> dzb, c10::optional<at::Tensor> dh) {
+  int64_t rows;
+  int G, H;
+  hc_shape(h, rows, G, H);
+  AFB_CHECK_DT(w, at::kFloat);
+  AFB_CHECK_DT(rstd, at::kFloat);
+  TORCH_CHECK(w.numel() == (int64_t)G * H && rstd.numel() == rows * G, "hc_norm shapes");
+  if (dzb) {
+    AFB_CHECK_DT(dzb.value(), at::kFloat);
+    AFB_CHECK_CONTIG(dzb.value());
+    AFB_CHECK_CONTIG(dh.value());
+    check_rc(afb::hc_norm_bwd(h.data_ptr(), ptr<float>(w), ptr<float>(rstd), ptr<float>(dzb.value()), dh->data_ptr(),
+                              rows, G, H, stream()),
+             "hc_norm_bwd");
+  } else {
+    AFB_CHECK_CONTIG(zb);
+    check_rc(afb::hc_norm_fwd(h.data_ptr(), ptr<float>(w), zb.data_ptr(), ptr<float>(rstd), rows, G, H, (float)eps,
+                              stream()),
+             "hc_norm_fwd");
+  }
+}
+void hc_mix_op(const at::Tensor& pre, const at::Tensor& zb, at::Tensor& x, c10::optional<at::Tensor> dx,
+               c10::optional<at::Tensor> dpre, c10::optional<at::Tensor> dzb) {
+  int64_t rows;
+  int G, H;
+  hc_shape(zb, rows, G, H);
+  AFB_CHECK_CONTIG(pre);
+  TORCH_CHECK(pre.numel() == zb.numel(), "hc_mix: pre and zb shapes");
+  if (dx) {
+    AFB_CHECK_CONTIG(dx.value());
+    check_rc(afb::hc_mix_bwd(pre.data_ptr(), zb.data_ptr(), dx->data_ptr(), dpre->data_ptr(), ptr<float>(dzb.value()),
+                             rows, G, H, stream()),
+             "hc_mix_bwd");
+  } else {
+    AFB_CHECK_CONTIG(x);
+    check_rc(afb::hc_mix_fwd(pre.data_ptr(), zb.data_ptr(), x.data_ptr(), rows, G, H, stream()), "hc_mix_fwd");
+  }
+}
+void hc_inject_op(const at::Tensor& h, const at::Tensor& y, const at::Tensor& gate, at::Tensor& out,
+                  c10::optional<at::Tensor> dout, c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dgate) {
+  int64_t rows;
+  int G, H;
+  hc_shape(h, rows, G, H);
+  AFB_CHECK_CONTIG(y);
+  AFB_CHECK_CONTIG(gate);
+  AFB_CHECK_DT(gate, at::kBFloat16);
+  TORCH_CHECK(y.numel() == rows * H && gate.numel() == rows * G, "hc_inject shapes");
+  if (dout) {
+    AFB_CHECK_CONTIG(dout.value());
+    check_rc(afb::hc_inject_bwd(y.data_ptr(), gate.data_ptr(), dout->data_ptr(), dy->data_ptr(),
+                                ptr<float>(dgate.value()), rows, G, H, stream()),
+             "hc_inject_bwd");
+  } else {
+    AFB_CHECK_CONTIG(out);
+    check_rc(afb::hc_inject_fwd(h.data_ptr(), y.data_ptr(), gate.data_ptr(), out.data_ptr(), rows, G, H, stream()),
+             "hc_inject_fwd");
+  }
+}
+
 void select_tokens_op(const at::Tensor& logits, int64_t V, at::Tensor& out, double temperature, int64_t seed,
                       c10::optional<at::Tensor> step) {
   AFB_CHECK_DT(logits, at::kBFloat16);
@@ -982,6 +1051,9 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
   m.def("gdn_train", &gdn_train_op);
+  m.def("hc_norm", &hc_norm_op);
+  m.def("hc_mix", &hc_mix_op);
+  m.def("hc_inject", &hc_inject_op);
   m.def("conv_silu", &conv_silu_op, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("dy"), py::arg("dx"),
         py::arg("pos") = py::none());
   m.def("rmsnorm_train", &rmsnorm_train_op);

@@ -92,7 +92,22 @@ def package_tensors(ref, codes_scales, dense_fp8: bool = True) -> dict[str, torc
         out[f"{p}.mlp.experts.w13_scales"] = s13.to(torch.bfloat16).contiguous()
         out[f"{p}.mlp.experts.w2_qweight"] = pack_uint3(c2)
         out[f"{p}.mlp.experts.w2_scales"] = s2.to(torch.bfloat16).contiguous()
+        if getattr(L, "hc", False):
+            for n in ("hc_attn", "hc_mlp"):
+                _put_hc(out, f"{p}.{n}", getattr(L, n))
+    if getattr(ref, "hc_final", None) is not None:
+        _put_hc(out, "model.hc_final", ref.hc_final)
     return out
+
+
+def _put_hc(out: dict, prefix: str, mod):
+    """Hyper-connection weights: the norm weight in fp32, the projections in bf16 (never FP8: the gate and the mix
+    feed every branch of the residual stream)."""
+    out[f"{prefix}.hc_norm.weight"] = mod.hc_norm.weight.detach().float().cpu()
+    for n in ("w_down", "w_up", "w_inject"):
+        w = getattr(mod, n, None)
+        if w is not None:
+            out[f"{prefix}.{n}"] = w.detach().cpu().to(torch.bfloat16).contiguous()
 
 
 def write_package(tensors: dict[str, torch.Tensor], cfg: ModelConfig, out_dir, shard_bytes: int = 5 << 30,

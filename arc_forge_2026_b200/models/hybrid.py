@@ -10,7 +10,8 @@ Weights live in the layouts the kernels want:
   expert as ``[gate; up]`` and ``down``.
 
 The residual stream is bf16 and is updated in place by the GEMM epilogues (``out = acc + residual``) and the MoE
-combine. A step over N tokens launches, per layer, 6-9 kernels; the whole decode step is CUDA-graph capturable
+combine. With hyper-connections (``hc_count > 1``) it is a stream of G branches ``[N, G, H]`` instead: every sub-layer
+reads a mix of the branches and writes its output back to each branch with a gate (``ops/hc.py``). A step over N tokens launches, per layer, 6-9 kernels; the whole decode step is CUDA-graph capturable
 (all shapes fixed by the batch layout, all indices on the device).
 """
 from __future__ import annotations
@@ -24,6 +25,7 @@ from ..config import FULL, ModelConfig
 from ..ops import C
 from ..ops.attention import PAGE, paged_attention
 from ..ops.gdn import GdnScratch, GdnShape, GdnState, gdn_decode
+from ..ops.hc import HCWeights, hc_inject_, hc_read
 from ..ops.moe import Fp8ExpertBank, Int3ExpertBank, MoEWorkspace, moe_forward, router_weight_with_shared_gate
 from ..ops.qsa import qsa_attention
 from ..parallel.ep import EPMoEWorkspace, moe_forward_ep
@@ -54,6 +56,9 @@ class LayerWeights:
     bank: Int3ExpertBank | None = None
     shared_w13: torch.Tensor | None = None
     shared_w2: torch.Tensor | None = None
+    # hyper-connections (hc_count > 1): the read before / write-back after each sub-layer
+    hc_attn: HCWeights | None = None
+    hc_mlp: HCWeights | None = None
 
 
 @dataclass
@@ -79,6 +84,12 @@ class StepBatch:
         return self.ids.shape[0]
 
 
+def _hc_from_package(t: dict, prefix: str, cfg: ModelConfig, dev) -> HCWeights:
+    inj = t.get(f"{prefix}.w_inject")
+    return HCWeights.from_tensors(t[f"{prefix}.hc_norm.weight"], t[f"{prefix}.w_down"], t[f"{prefix}.w_up"], inj,
+                                  cfg.rms_norm_eps, dev)
+
+
 class HybridModel:
     def __init__(self, cfg: ModelConfig, layers: list[LayerWeights], embed, final_norm, lm_head, device):
         self.cfg = cfg
@@ -93,6 +104,7 @@ class HybridModel:
         cos, sin = rope_cos_sin(torch.arange(1 << 17, device=self.device), c.rotary_dim, c.rope_theta)
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
         self.ep = None  # ExpertParallel when the routed experts are split over ranks
+        self.hc_final: HCWeights | None = None  # the final branch readout of a hyper-connection model
 
     def enable_expert_parallel(self, world: int, rank: int, T_cap: int, group=None):
         """Split the routed experts over ``world`` ranks (keeps this rank's block) and route every MoE layer
@@ -162,6 +174,9 @@ class HybridModel:
                 lw.bank = Fp8ExpertBank(a, sa, b, sb)
                 lw.shared_w13 = randn(2 * Is, H)
                 lw.shared_w2 = randn(H, Is)
+                if cfg.hc_count > 1:
+                    lw.hc_attn, lw.hc_mlp = (HCWeights.random(cfg.hc_count, H, cfg.hc_lowrank, std, cfg.rms_norm_eps,
+                                                              True, gen, dev) for _ in range(2))
                 layers.append(lw)
                 continue
             lw.bank = Int3ExpertBank(
@@ -176,9 +191,16 @@ class HybridModel:
             lw.shared_w13 = randn(2 * Is, H)
             lw.shared_w2 = randn(H, Is)
             layers.append(lw)
+        G = cfg.hc_count
+        if G > 1:
+            for lw in layers:
+                lw.hc_attn, lw.hc_mlp = (HCWeights.random(G, H, cfg.hc_lowrank, std, cfg.rms_norm_eps, True, gen, dev)
+                                         for _ in range(2))
         embed = randn(cfg.vocab_size, H)
-        return cls(cfg, layers, embed, torch.zeros(H, dtype=torch.bfloat16, device=dev),
-                   randn(cfg.vocab_size, H), dev)
+        m = cls(cfg, layers, embed, torch.zeros(H, dtype=torch.bfloat16, device=dev), randn(cfg.vocab_size, H), dev)
+        if G > 1:
+            m.hc_final = HCWeights.random(G, H, cfg.hc_lowrank, std, cfg.rms_norm_eps, False, gen, dev)
+        return m
 
     @classmethod
     def from_reference(cls, ref: HybridMoE, device, codes_scales: list | None = None):
@@ -216,9 +238,14 @@ class HybridModel:
             lw.bank = Int3ExpertBank.from_codes(c13, s13.to(torch.bfloat16), c2, s2.to(torch.bfloat16), dev)
             lw.shared_w13 = torch.cat([moe.shared_gate_proj.weight, moe.shared_up_proj.weight]).detach().to(**bf)
             lw.shared_w2 = moe.shared_down_proj.weight.detach().to(**bf).contiguous()
+            if getattr(L, "hc", False):
+                lw.hc_attn, lw.hc_mlp = HCWeights.from_module(L.hc_attn, dev), HCWeights.from_module(L.hc_mlp, dev)
             layers.append(lw)
-        return cls(cfg, layers, ref.embed_tokens.weight.detach().to(**bf), ref.norm.weight.detach().to(**bf),
-                   ref.lm_head.weight.detach().to(**bf), dev)
+        m = cls(cfg, layers, ref.embed_tokens.weight.detach().to(**bf), ref.norm.weight.detach().to(**bf),
+                ref.lm_head.weight.detach().to(**bf), dev)
+        if cfg.hc_count > 1:
+            m.hc_final = HCWeights.from_module(ref.hc_final, dev)
+        return m
 
     @classmethod
     def from_package(cls, pkg_dir, device, verify: bool = True):
@@ -255,15 +282,24 @@ class HybridModel:
             lw.shared_w13 = torch.cat([dense_weight(t, f"{m}.shared_expert.gate_proj"),
                                        dense_weight(t, f"{m}.shared_expert.up_proj")]).to(**bf)
             lw.shared_w2 = dense_weight(t, f"{m}.shared_expert.down_proj").to(**bf).contiguous()
+            if cfg.hc_count > 1:
+                lw.hc_attn, lw.hc_mlp = (_hc_from_package(t, f"{p}.{n}", cfg, dev) for n in ("hc_attn", "hc_mlp"))
             layers.append(lw)
-        return cls(cfg, layers, t["model.embed_tokens.weight"].to(**bf), t["model.norm.weight"].to(**bf),
-                   t["lm_head.weight"].to(**bf), dev)
+        m = cls(cfg, layers, t["model.embed_tokens.weight"].to(**bf), t["model.norm.weight"].to(**bf),
+                t["lm_head.weight"].to(**bf), dev)
+        if cfg.hc_count > 1:
+            m.hc_final = _hc_from_package(t, "model.hc_final", cfg, dev)
+        return m
 
     def tensors(self):
         """(name, tensor) of every weight the forward reads (layer fields, expert-bank fields, embeddings)."""
         yield "embed", self.embed
         yield "final_norm", self.final_norm
         yield "lm_head", self.lm_head
+        if self.hc_final is not None:
+            for k, v in vars(self.hc_final).items():
+                if isinstance(v, torch.Tensor):
+                    yield f"hc_final.{k}", v
         for i, lw in enumerate(self.layers):
             for k, v in vars(lw).items():
                 if isinstance(v, torch.Tensor):
@@ -294,14 +330,7 @@ class HybridModel:
         return {"tensors": len(mine)}
 
     def nbytes(self) -> int:
-        tot = self.embed.nbytes + self.lm_head.nbytes
-        for lw in self.layers:
-            for v in lw.__dict__.values():
-                if isinstance(v, torch.Tensor):
-                    tot += v.nbytes
-                elif isinstance(v, Int3ExpertBank):
-                    tot += v.nbytes()
-        return tot
+        return sum(t.nbytes for _, t in self.tensors())
 
     # ------------------------------------------------------------------ caches
     def new_kv_cache(self, num_pages: int):
@@ -336,8 +365,17 @@ class HybridModel:
         y = ws.y[:N]
         ai = gi = 0
         D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_kv_heads
+        G = c.hc_count
+        hs = None
+        if G > 1:  # branch stream; h becomes the sub-layer output buffer
+            hs = ws.hs[:N]
+            hs.copy_(h[:, None, :].expand(N, G, H))
         for lw in self.layers:
-            cC.rmsnorm(h, None, lw.in_norm, y, c.rms_norm_eps, True)
+            if hs is not None:
+                x, gate = hc_read(hs, lw.hc_attn, G)
+                cC.rmsnorm(x, None, lw.in_norm, y, c.rms_norm_eps, True)
+            else:
+                cC.rmsnorm(h, None, lw.in_norm, y, c.rms_norm_eps, True)
             if lw.kind == FULL:
                 qkv = ws.qkv[:N]
                 cC.gemm(y, lw.w_qkv, out=qkv)
@@ -367,7 +405,7 @@ class HybridModel:
                     paged_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, b.q_per_seq,
                                     attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
                                     max_pages=b.max_pages)
-                cC.gemm(attn, lw.w_o, out=h, residual=h)
+                cC.gemm(attn, lw.w_o, out=h, residual=None if hs is not None else h)
                 ai += 1
             else:
                 mixed = ws.mixed[:N]
@@ -375,15 +413,26 @@ class HybridModel:
                 o = ws.gdn_out[:N]
                 gdn_decode(mixed, self.gdn_shape, gdn[gi], lw.conv_w, lw.A_log, lw.dt_bias, lw.g_norm, b.n_commit,
                            b.seq_slot, o, b.q_per_seq, b.parity, b.commit_current, gdn_scratch, c.rms_norm_eps)
-                cC.gemm(o, lw.w_out, out=h, residual=h)
+                cC.gemm(o, lw.w_out, out=h, residual=None if hs is not None else h)
                 gi += 1
-            cC.rmsnorm(h, None, lw.post_norm, y, c.rms_norm_eps, True)
+            resid = h
+            if hs is not None:
+                hc_inject_(hs, h, gate)
+                x, gate = hc_read(hs, lw.hc_mlp, G)
+                cC.rmsnorm(x, None, lw.post_norm, y, c.rms_norm_eps, True)
+                resid = ws.zero[:N]
+            else:
+                cC.rmsnorm(h, None, lw.post_norm, y, c.rms_norm_eps, True)
             if self.ep is not None:
-                moe_forward_ep(y, h, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, self.ep, ws.moe, out=h,
+                moe_forward_ep(y, resid, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, self.ep, ws.moe, out=h,
                                renorm=c.norm_topk_prob)
             else:
-                moe_forward(y, h, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, c.num_experts_per_tok, ws.moe,
-                            out=h, renorm=c.norm_topk_prob)
+                moe_forward(y, resid, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, c.num_experts_per_tok,
+                            ws.moe, out=h, renorm=c.norm_topk_prob)
+            if hs is not None:
+                hc_inject_(hs, h, gate)
+        if hs is not None:
+            h = hc_read(hs, self.hc_final, G)[0]
         cC.rmsnorm(h, None, self.final_norm, y, c.rms_norm_eps, True)
         return y
 
@@ -402,6 +451,9 @@ class Workspace:
         self.max_tokens = max_tokens
         self.h = torch.empty(max_tokens, H, **bf)
         self.y = torch.empty(max_tokens, H, **bf)
+        if c.hc_count > 1:  # branch stream and the zero residual of the MoE output
+            self.hs = torch.empty(max_tokens, c.hc_count, H, **bf)
+            self.zero = torch.zeros(max_tokens, H, **bf)
         D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_kv_heads
         self.qkv = torch.empty(max_tokens + 8, Hq * 2 * D + 2 * Hkv * D + c.qsa_proj_dim, **bf)
         self.q = torch.empty(max_tokens + 8, Hq * D, **bf)

@@ -294,6 +294,45 @@ class MoE(nn.Module):
         return out.reshape(shape)
 
 
+class HyperConnection(nn.Module):
+    """Hyper-connection read of a residual stream of G branches h [..., G, H] (the reference model's gated residual,
+    ``training/work/qwen38fn_lora/hc_mix.py:1-20``):
+
+        zb   = rmsnorm_g(h) * (1 + w)               RMSNorm of every branch (H features), zero-centred weight [G*H]
+        du   = zb @ W_down^T, di = zb @ W_inject^T   [.., R], [.., G]
+        x    = mean_g(sigmoid(silu(du / 4) @ W_up^T) * zb)    the mixed sub-layer input [..., H]
+        gate = 2 sigmoid(di / 4)                    the write-back gate of every branch [..., G]
+
+    The write-back of the sub-layer's output y is ``h + y * gate`` per branch (:func:`hc_inject`). ``inject=False``
+    (the final readout) has no gate."""
+
+    def __init__(self, cfg: ModelConfig, inject: bool = True):
+        super().__init__()
+        G, H, R = cfg.hc_count, cfg.hidden_size, cfg.hc_lowrank
+        self.G, self.H, self.R, self.eps = G, H, R, cfg.rms_norm_eps
+        self.hc_norm = RMSNorm(G * H, cfg.rms_norm_eps)
+        self.w_down = nn.Parameter(torch.zeros(R, G * H))
+        self.w_up = nn.Parameter(torch.zeros(G * H, R))
+        self.w_inject = nn.Parameter(torch.zeros(G, G * H)) if inject else None
+
+    def forward(self, h):
+        G, H = self.G, self.H
+        hf = h.float()
+        zb = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + self.eps)
+        zb = zb.flatten(-2) * (1.0 + self.hc_norm.weight.float())
+        s = F.silu((zb @ self.w_down.float().t()) * 0.25)
+        pre = s @ self.w_up.float().t()
+        x = (torch.sigmoid(pre) * zb).unflatten(-1, (G, H)).mean(-2).to(h.dtype)
+        if self.w_inject is None:
+            return x, None
+        return x, (2.0 * torch.sigmoid((zb @ self.w_inject.float().t()) * 0.25)).to(h.dtype)
+
+
+def hc_inject(h, y, gate):
+    """h [..., G, H] + y [..., H] * gate [..., G] per branch."""
+    return (h.float() + y.float()[..., None, :] * gate.float()[..., :, None]).to(h.dtype)
+
+
 class DecoderLayer(nn.Module):
     def __init__(self, cfg: ModelConfig, kind: str, index: int):
         super().__init__()
@@ -303,8 +342,17 @@ class DecoderLayer(nn.Module):
         self.mixer = GatedAttention(cfg) if kind == FULL else GatedDeltaNet(cfg)
         self.mlp = MoE(cfg)
         self.mlp.layer_index = index
+        self.hc = cfg.hc_count > 1
+        if self.hc:  # hyper-connections: each sub-layer reads a mix of the branches and writes back gated
+            self.hc_attn = HyperConnection(cfg)
+            self.hc_mlp = HyperConnection(cfg)
 
     def forward(self, x, positions, cache=None):
+        if self.hc:  # x is the branch stream [B, T, G, H]
+            a, g = self.hc_attn(x)
+            x = hc_inject(x, self.mixer(self.input_layernorm(a), positions, cache), g)
+            a, g = self.hc_mlp(x)
+            return hc_inject(x, self.mlp(self.post_attention_layernorm(a)), g)
         x = x + self.mixer(self.input_layernorm(x), positions, cache)
         return x + self.mlp(self.post_attention_layernorm(x))
 
@@ -320,6 +368,7 @@ class HybridMoE(nn.Module):
         self.layers = nn.ModuleList([DecoderLayer(cfg, t, i) for i, t in enumerate(cfg.layer_types)])
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
         self.lm_head = nn.Linear(cfg.hidden_size, cfg.vocab_size, bias=False)
+        self.hc_final = HyperConnection(cfg, inject=False) if cfg.hc_count > 1 else None
 
     @torch.no_grad()
     def init_weights(self, seed: int = 0):
@@ -347,8 +396,12 @@ class HybridMoE(nn.Module):
         B, T = ids.shape
         positions = torch.arange(start_pos, start_pos + T, device=ids.device)
         x = self.embed_tokens(ids)
+        if self.hc_final is not None:  # every branch starts as the embedding
+            x = x[..., None, :].expand(*x.shape[:-1], self.cfg.hc_count, x.shape[-1]).contiguous()
         for i, layer in enumerate(self.layers):
             x = layer(x, positions, None if cache is None else cache[i])
+        if self.hc_final is not None:
+            x = self.hc_final(x)[0]
         return self.norm(x)
 
     def forward(self, ids, cache=None, start_pos: int = 0):

@@ -23,6 +23,7 @@ from ..models import reference as R
 from ..quant.int3_tiles import codes_to_tiles
 from . import fused
 from .fakequant import fp8_weight, int3_weight
+from .hc import hc_inject, hc_read
 from .gdn_chunk import chunk_gated_delta_rule
 
 GROUPS = ("scale", "router", "shared", "dense_fp8", "dense_bf16")
@@ -141,7 +142,28 @@ def layer_tensors_from_reference(L: R.DecoderLayer, codes_scales) -> dict:
     t.update(router=moe.gate.weight, w13_codes=codes_to_tiles(c13), w13_scales=s13, w2_codes=codes_to_tiles(c2),
              w2_scales=s2, shared_gate=moe.shared_gate_proj.weight, shared_up=moe.shared_up_proj.weight,
              shared_down=moe.shared_down_proj.weight, shared_expert_gate=moe.shared_expert_gate.weight)
-    return {k: v.detach() for k, v in t.items()}
+    out = {k: v.detach() for k, v in t.items()}
+    if getattr(L, "hc", False):  # hyper-connection weights (frozen)
+        out["hc_attn"] = {k: v.detach() for k, v in L.hc_attn.state_dict().items()}
+        out["hc_mlp"] = {k: v.detach() for k, v in L.hc_mlp.state_dict().items()}
+    return out
+
+
+def random_hc_tensors(cfg: ModelConfig, device, gen, inject: bool = True) -> dict:
+    G, H, R_ = cfg.hc_count, cfg.hidden_size, cfg.hc_lowrank
+    std = cfg.init_std
+    t = {"hc_norm.weight": torch.zeros(G * H, device=device),
+         "w_down": torch.randn(R_, G * H, generator=gen, device=device) * std,
+         "w_up": torch.randn(G * H, R_, generator=gen, device=device) * std}
+    if inject:
+        t["w_inject"] = torch.randn(G, G * H, generator=gen, device=device) * std
+    return t
+
+
+def _hc_module(cfg, state: dict, inject: bool, device):
+    m = R.HyperConnection(cfg, inject=inject)
+    m.load_state_dict({k: v.float() for k, v in state.items()})
+    return m.to(device).requires_grad_(False)
 
 
 def random_layer_tensors(cfg: ModelConfig, kind: str, device, gen: torch.Generator) -> dict:
@@ -172,6 +194,9 @@ def random_layer_tensors(cfg: ModelConfig, kind: str, device, gen: torch.Generat
                                     device=device, generator=gen),
              w2_scales=rn(E, H, I // 128, s=std / 2.3),
              shared_gate=rn(Is, H), shared_up=rn(Is, H), shared_down=rn(H, Is), shared_expert_gate=rn(1, H))
+    if cfg.hc_count > 1:
+        t["hc_attn"] = random_hc_tensors(cfg, device, gen)
+        t["hc_mlp"] = random_hc_tensors(cfg, device, gen)
     return t
 
 
@@ -197,6 +222,11 @@ class StudentLayer(nn.Module):
         self.moe = StudentMoE(cfg, t["router"], t["w13_codes"], t["w13_scales"], t["w2_codes"], t["w2_scales"],
                               t["shared_gate"], t["shared_up"], t["shared_down"], t["shared_expert_gate"])
         self.lora = nn.ModuleDict()  # optional adapters by projection name (train/lora.py)
+        self.hc_attn = self.hc_mlp = None
+        if cfg.hc_count > 1:  # hyper-connections: the layer reads a mix of the branches and writes back gated
+            dev = t["in_norm"].device
+            self.hc_attn = _hc_module(cfg, t["hc_attn"], True, dev)
+            self.hc_mlp = _hc_module(cfg, t["hc_mlp"], True, dev)
 
     def _lin(self, name: str, x, fp8: bool):
         """x @ W^T for projection ``name`` (block-FP8 QAT weight when ``fp8``), plus its LoRA adapter if attached."""
@@ -259,9 +289,16 @@ class StudentLayer(nn.Module):
 
     def forward(self, x, pack=None):
         c = self.cfg
-        B, T, H = x.shape
+        B, T, H = x.shape[0], x.shape[1], x.shape[-1]
         if pack is not None and B != 1:
             raise ValueError("packed bins are single rows (B = 1)")
+        if self.hc_attn is not None:  # x: the branch stream [B, T, G, H]
+            a, g = hc_read(x, self.hc_attn)
+            y = fused.rms_norm(a, self.in_norm, c.rms_norm_eps)
+            x = hc_inject(x, self._attn(y, B, T, pack) if self.kind == FULL else self._gdn(y, B, T, pack), g)
+            a, g = hc_read(x, self.hc_mlp)
+            y = fused.rms_norm(a, self.post_norm, c.rms_norm_eps)
+            return hc_inject(x, self.moe(y.reshape(B * T, H)).reshape(B, T, H), g)
         y = fused.rms_norm(x, self.in_norm, c.rms_norm_eps)
         x = x + (self._attn(y, B, T, pack) if self.kind == FULL else self._gdn(y, B, T, pack))
         y = fused.rms_norm(x, self.post_norm, c.rms_norm_eps)
@@ -280,6 +317,10 @@ class QADStudent(nn.Module):
         self.register_buffer("lm_head", ref.lm_head.weight.detach().to(compute_dtype).clone())
         self.layers = nn.ModuleList([StudentLayer(cfg, L.kind, layer_tensors_from_reference(L, codes_scales[i]))
                                      for i, L in enumerate(ref.layers)])
+        self.hc_final = None
+        if cfg.hc_count > 1:
+            self.hc_final = _hc_module(cfg, {k: v.detach() for k, v in ref.hc_final.state_dict().items()}, False,
+                                       self.embed.device)
         self._lm_head_t = None
 
     @property
@@ -299,11 +340,16 @@ class QADStudent(nn.Module):
         """Final hidden states of ``ids`` [B, T]; ``pack`` (``train/packing.py`` ``PackedBin.forward_args``) makes
         the row a packed bin of several sequences (B = 1)."""
         x = F.embedding(ids, self.embed)
+        hc = getattr(self, "hc_final", None)
+        if hc is not None:  # every branch starts as the embedding
+            x = x[..., None, :].expand(*x.shape[:-1], self.cfg.hc_count, x.shape[-1]).contiguous()
         for L in self.layers:
             if self.ckpt and torch.is_grad_enabled():
                 x = checkpoint(L, x, pack, use_reentrant=False)
             else:
                 x = L(x, pack)
+        if hc is not None:
+            x = hc_read(x, hc)[0]
         return fused.rms_norm(x, self.final_norm, self.cfg.rms_norm_eps)
 
 
@@ -320,4 +366,5 @@ def random_student(cfg: ModelConfig, device, seed: int = 0, checkpoint_layers=Tr
     st.register_buffer("lm_head", (torch.randn(V, H, generator=gen, device=dev) * cfg.init_std).to(torch.bfloat16))
     st.layers = nn.ModuleList([StudentLayer(cfg, kind, random_layer_tensors(cfg, kind, dev, gen))
                                for kind in cfg.layer_types])
+    st.hc_final = _hc_module(cfg, random_hc_tensors(cfg, dev, gen, inject=False), False, dev) if cfg.hc_count > 1 else None
     return st

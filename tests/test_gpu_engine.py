@@ -14,8 +14,8 @@ pytestmark = pytest.mark.gpu
 dev = "cuda"
 
 
-def _models(seed=0):
-    cfg = preset("tiny_gpu")
+def _models(seed=0, **over):
+    cfg = preset("tiny_gpu", **over)
     ref = build_reference(cfg, seed=seed)
     with torch.no_grad():
         ref.lm_head.weight.mul_(40.0)  # peaky logits: argmax far from ties
@@ -201,3 +201,28 @@ def test_update_weights_in_place_matches_fresh_load(tmp_path):
     torch.cuda.synchronize()
     check_status()
     assert got == want
+
+
+def test_hyper_connection_model_decodes_like_reference(tmp_path):
+    """A 4-branch hyper-connection model: the engine's greedy decode (plain and speculative) follows the reference,
+    and a deploy package carries the hyper-connection weights."""
+    from arc_forge_2026_b200.formats.int3_package import package_tensors, write_package
+    from arc_forge_2026_b200.quant.int3_tiles import tiles_to_codes, tiles_to_scales
+    cfg, ref, model = _models(7, hc_count=4, hc_lowrank=64)
+    assert model.hc_final is not None and model.layers[0].hc_attn is not None
+    g = torch.Generator().manual_seed(7)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (90, 33)]
+    plain = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy"), 2, 1024).generate(prompts, 16)
+    drafter = Drafter(drafter_preset("tiny"), cfg.hidden_size, cfg.vocab_size, dev, draft_vocab=4096)
+    spec = SpecEngine(model, drafter, ServeConfig(spec_k=4, accept_mode="greedy"), 2, 1024).generate(prompts, 16)
+    torch.cuda.synchronize()
+    check_status()
+    assert plain == spec
+    toks, _ = ref.greedy_decode(torch.tensor([prompts[0]]), 6)
+    assert toks[0].tolist()[:4] == plain[0][:4]
+    cs = [(tiles_to_codes(lw.bank.w13_codes.cpu()), tiles_to_scales(lw.bank.w13_scales.cpu()),
+           tiles_to_codes(lw.bank.w2_codes.cpu()), tiles_to_scales(lw.bank.w2_scales.cpu())) for lw in model.layers]
+    d = write_package(package_tensors(ref, cs, dense_fp8=False), cfg, tmp_path / "pkg", dense_fp8=False)
+    loaded = HybridModel.from_package(d, dev)
+    again = SpecEngine(loaded, None, ServeConfig(spec_k=0, accept_mode="greedy"), 2, 1024).generate(prompts, 16)
+    assert again == plain

@@ -287,6 +287,63 @@ def test_sft_packed_bins_with_checkpoint_offload_on_gpu(tmp_path, capsys):
     assert losses[0] == losses[1] and len(losses[0]) == 3, losses
 
 
+def test_hyper_connection_kernels_match_reference():
+    """Native hyper-connection read (norm, projections, mix, gate) and write-back against the fp32 reference
+    module: outputs and the gradient of the branch stream (weights frozen)."""
+    from arc_forge_2026_b200.config import preset
+    from arc_forge_2026_b200.models import reference as R
+    from arc_forge_2026_b200.train.hc import hc_inject, hc_read
+    cfg = preset("tiny_cpu", hc_count=4, hc_lowrank=32, hidden_size=256)
+    g = torch.Generator().manual_seed(31)
+    mod = R.HyperConnection(cfg).to(dev)
+    with torch.no_grad():
+        for p in (mod.w_down, mod.w_up, mod.w_inject):
+            p.copy_(torch.randn(p.shape, generator=g) * 0.05)
+        mod.hc_norm.weight.copy_(torch.randn(mod.hc_norm.weight.shape, generator=g) * 0.1)
+    mod.requires_grad_(False)
+    h0 = torch.randn(3, 37, 4, 256, generator=g).bfloat16().to(dev)
+    dx = torch.randn(3, 37, 256, generator=g).to(dev)
+    dg = torch.randn(3, 37, 4, generator=g).to(dev)
+    y0 = torch.randn(3, 37, 256, generator=g).bfloat16().to(dev)
+    dout = torch.randn(3, 37, 4, 256, generator=g).to(dev)
+
+    def run(native):
+        h = h0.clone().requires_grad_(True)
+        y = y0.clone().requires_grad_(True)
+        x, gate = hc_read(h, mod) if native else mod(h)
+        out = hc_inject(h, y, gate) if native else R.hc_inject(h, y, gate)
+        ((x.float() * dx).sum() + (gate.float() * dg).sum() + (out.float() * dout).sum()).backward()
+        return [x.detach().float(), gate.detach().float(), out.detach().float(), h.grad.float(), y.grad.float()]
+    got, ref = run(True), run(False)
+    errs = [round(_rel(a, b), 5) for a, b in zip(got, ref)]
+    assert all(e < 2e-2 for e in errs), errs
+    check_status()
+
+
+def test_hyper_connection_student_trains_on_native_kernels():
+    """A QAD student with 4 hyper-connection branches steps on the GPU with every HC read on the native path."""
+    from arc_forge_2026_b200.config import QADConfig, preset
+    from arc_forge_2026_b200.formats.topk_targets import synthetic_targets
+    from arc_forge_2026_b200.train import kernels
+    from arc_forge_2026_b200.train.qad import build_optimizer, enforce_scale_invariants, train_step
+    from arc_forge_2026_b200.train.student import random_student
+    cfg = preset("tiny_gpu", hc_count=4, hc_lowrank=64)
+    st = random_student(cfg, dev, seed=0)
+    qc = QADConfig(seq_len=256, topk=16, direction="reverse", lr_scale=1e-3, lr_router=1e-3, lr_dense=1e-3)
+    opt = build_optimizer(st, qc, sharded=True)
+    signs = enforce_scale_invariants(st, None)
+    gen = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (2, 256), generator=gen).to(dev)
+    t = synthetic_targets(ids.numel(), 16, cfg.vocab_size, gen, dev)
+    kernels.reset()
+    losses = [train_step(st, opt, ids, t, qc, signs)[0] for _ in range(4)]
+    torch.cuda.synchronize()
+    check_status()
+    c = kernels.counts()
+    assert c["native"].get("hc", 0) >= 4 * (2 * cfg.num_layers + 1) and "hc" not in c["fallback"], c
+    assert losses[-1] < losses[0], losses
+
+
 def test_native_fp8_teacher_targets_agree_with_its_prefill():
     from arc_forge_2026_b200.config import ServeConfig, preset
     from arc_forge_2026_b200.models.hybrid import HybridModel

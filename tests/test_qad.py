@@ -107,3 +107,29 @@ def test_kernel_registry_counts_and_rejects_fallbacks():
         assert kernels.enable("none") == set()
     finally:
         kernels.enable(sorted(old))
+
+
+def test_hyper_connection_student_matches_reference():
+    """A student of an HC model (4 branches) follows the reference model and takes gradients through the
+    frozen hyper-connection reads and write-backs."""
+    cfg = preset("tiny_cpu", hc_count=4, hc_lowrank=32)
+    ref = build_reference(cfg, seed=1)
+    cs = []
+    with torch.no_grad():
+        for moe in ref.moe_layers():
+            c13, s13 = rtn_quantize(moe.w13.float())
+            c2, s2 = rtn_quantize(moe.w2.float())
+            s13, s2 = s13.bfloat16().float(), s2.bfloat16().float()
+            moe.w13.copy_((c13.float() - 4) * s13.repeat_interleave(128, -1))
+            moe.w2.copy_((c2.float() - 4) * s2.repeat_interleave(128, -1))
+            cs.append((c13, s13, c2, s2))
+    st = QADStudent(cfg, ref, cs, compute_dtype=torch.float32, checkpoint_layers=False)
+    ids = torch.randint(0, cfg.vocab_size, (1, 30), generator=torch.Generator().manual_seed(2))
+    with torch.no_grad():
+        h_ref, h = ref.hidden(ids), st.hidden(ids)
+    rel = ((h - h_ref).norm() / h_ref.norm()).item()
+    assert rel < 0.2, rel
+    h = st.hidden(ids)
+    h.pow(2).mean().backward()
+    assert st.layers[0].moe.w13_scales.grad is not None
+    assert all(not p.requires_grad for p in st.layers[0].hc_attn.parameters())
