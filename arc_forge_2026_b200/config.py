@@ -138,6 +138,12 @@ class DrafterConfig:
     block_size: int = 5  # anchor + K proposal slots (verify width K=4)
     rms_norm_eps: float = 1.0e-6
     rope_theta: float = 1.0e7
+    # training variants (the serving drafter is plain / dense; train/drafter_tools.py converts the others)
+    residual: str = "plain"  # plain | hc (hyper-connection branch stream)
+    hc_count: int = 1
+    hc_lowrank: int = 64
+    ffn: str = "dense"  # dense | dense_shared (a dense SwiGLU plus a sigmoid-gated shared SwiGLU)
+    shared_intermediate_size: int = 0
 
     @property
     def k(self) -> int:

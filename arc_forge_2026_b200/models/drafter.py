@@ -61,6 +61,16 @@ class Drafter:
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
 
     @property
+    @classmethod
+    def from_dir(cls, path, device, verify: bool = True) -> "Drafter":
+        """Load a drafter directory (``train/drafter_tools.py`` layout: an export, a plain conversion, a layer
+        expansion or a deployment copy; block-FP8 linears are dequantised to bf16 for the serving GEMMs)."""
+        from ..train.drafter_tools import load_dir
+        twin = load_dir(path, verify=verify)
+        d = cls(twin.cfg, twin.fc.shape[1], twin.vocab_size, device, draft_vocab=len(twin.draft_vocab))
+        twin.export_to(d)
+        return d
+
     def kv_row_offset(self) -> int:
         c = self.cfg
         return c.num_attention_heads * 2 * c.head_dim

@@ -14,6 +14,12 @@ anchor positions a:
 Objectives (the reference's ``training/work/qwen38fn_dflash/objective.py``): ``ce`` (next-token cross-entropy on
 every slot) and, with teacher logits, ``kl`` (forward KL to the target's distribution restricted to the draft
 vocabulary), mixed by ``kl_weight``.
+
+Two training-only variants (the reference's ``Config.residual`` / ``ffn_type``, ``qwen38fn_dflash/model.py:20-91``,
+``:114 GatedResidual``): ``residual="hc"`` keeps G branches of the stream; each sub-layer reads the hyper-connection
+mix of the branches in place of its RMSNorm and writes back through per-branch gates, and a final readout mix
+replaces the final norm. ``ffn="dense_shared"`` adds a shared SwiGLU scaled by ``sigmoid(y . w_shared_gate)``.
+The serving drafter is plain and dense; ``train/drafter_tools.py`` converts the variants.
 """
 from __future__ import annotations
 
@@ -24,7 +30,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..config import DrafterConfig
-from ..models.reference import apply_rope, rms_norm, rope_cos_sin
+from ..models.reference import HyperConnection, apply_rope, hc_inject, rms_norm, rope_cos_sin
 
 
 class DrafterTrain(nn.Module):
@@ -41,17 +47,36 @@ class DrafterTrain(nn.Module):
         def z(*shape):
             return nn.Parameter(torch.zeros(*shape, device=device))
         self.vocab_size, self.mask_id = vocab_size, vocab_size
+        self.hc = cfg.residual == "hc"
+        if cfg.residual not in ("plain", "hc") or cfg.ffn not in ("dense", "dense_shared"):
+            raise ValueError(f"unknown drafter variant residual={cfg.residual!r} ffn={cfg.ffn!r}")
+
+        def hc_mod(inject):  # starts as a single stream in disguise: constant mix, unit gates
+            mod = HyperConnection(cfg, inject).to(device)
+            with torch.no_grad():
+                mod.w_down.copy_(torch.randn(mod.w_down.shape, generator=g, device=device) * std)
+            return mod
         self.embed = p(vocab_size + 1, H)
         self.fc = p(H, target_hidden)
         self.layers = nn.ModuleList()
         for _ in range(cfg.num_layers):
             m = nn.Module()
-            m.in_norm, m.ctx_norm, m.post_norm = z(H), z(H), z(H)
+            m.ctx_norm = z(H)
+            if self.hc:
+                m.hc_attn, m.hc_mlp = hc_mod(True), hc_mod(True)
+            else:
+                m.in_norm, m.post_norm = z(H), z(H)
             m.w_qkv = p(Hq * 2 * D + 2 * Hkv * D, H)
             m.q_norm, m.k_norm = z(D), z(D)
             m.w_o, m.w13, m.w2 = p(H, Hq * D), p(2 * I, H), p(H, I)
+            if cfg.ffn == "dense_shared":
+                Is = cfg.shared_intermediate_size
+                m.sw13, m.sw2, m.shared_gate = p(2 * Is, H), p(H, Is), p(1, H)
             self.layers.append(m)
-        self.final_norm = z(H)
+        if self.hc:
+            self.hc_final = hc_mod(False)
+        else:
+            self.final_norm = z(H)
         self.register_buffer("draft_vocab", draft_vocab.long().to(device))
         self.lm_head = p(len(draft_vocab), H)
         to_draft = torch.full((vocab_size,), -1, dtype=torch.long)
@@ -62,8 +87,33 @@ class DrafterTrain(nn.Module):
         cos, sin = rope_cos_sin(pos, self.cfg.head_dim, self.cfg.rope_theta)
         return apply_rope(x, cos, sin)
 
-    def block_logits(self, tokens: torch.Tensor, hidden: torch.Tensor, anchors: torch.Tensor) -> torch.Tensor:
-        """tokens [T], hidden [T, Ht], anchors [A] (1 <= a, a + K <= T - 1) -> draft-vocab logits [A, K, Vd]."""
+    def _read(self, site: str, x, norm_w, hc_mod, probe):
+        """The sub-layer input at ``site``: RMSNorm of the stream (plain) or the hyper-connection mix (hc)."""
+        if hc_mod is not None:
+            y, gate = hc_mod(x)
+        else:
+            y, gate = rms_norm(x, norm_w, self.cfg.rms_norm_eps), None
+        if probe is not None:
+            probe(site, x, y, gate)
+        return y, gate
+
+    def _ffn(self, m, y, i: int, probe):
+        I = self.cfg.intermediate_size
+        gu = y @ m.w13.t()
+        out = (F.silu(gu[..., :I]) * gu[..., I:]) @ m.w2.t()
+        if self.cfg.ffn == "dense_shared":
+            Is = self.cfg.shared_intermediate_size
+            logit = y @ m.shared_gate.t()
+            if probe is not None:
+                probe(f"shared{i}", None, logit, None)
+            sg = y @ m.sw13.t()
+            out = out + torch.sigmoid(logit) * ((F.silu(sg[..., :Is]) * sg[..., Is:]) @ m.sw2.t())
+        return out
+
+    def block_logits(self, tokens: torch.Tensor, hidden: torch.Tensor, anchors: torch.Tensor, probe=None) -> torch.Tensor:
+        """tokens [T], hidden [T, Ht], anchors [A] (1 <= a, a + K <= T - 1) -> draft-vocab logits [A, K, Vd].
+        ``probe(site, stream, sub-layer input, gate)`` is called at every read (sites ``attn<i>``, ``mlp<i>``,
+        ``final``; ``shared<i>`` with the shared-gate logits); it may raise to stop the forward early."""
         c = self.cfg
         K, D, Hq, Hkv = c.k, c.head_dim, c.num_attention_heads, c.num_kv_heads
         T, A = tokens.shape[0], anchors.shape[0]
@@ -81,12 +131,16 @@ class DrafterTrain(nn.Module):
         blk_ok = (same[:, None] == same[None]) & (torch.arange(K, device=dev).repeat(A)[None] <=
                                                   torch.arange(K, device=dev).repeat(A)[:, None])
         mask = torch.cat([ctx_ok, blk_ok], 1)                                         # [A*K, T + A*K]
-        for m in self.layers:
+        G = c.hc_count
+        if self.hc:  # every branch starts as the fusion
+            x = x[..., None, :].expand(A, K, G, x.shape[-1]).clone()
+        for i, m in enumerate(self.layers):
             kv_c = rms_norm(fus, m.ctx_norm, c.rms_norm_eps) @ m.w_qkv[Hq * 2 * D:].t()
             kc = rms_norm(kv_c[:, :Hkv * D].view(T, Hkv, D), m.k_norm, c.rms_norm_eps)
             kc = self._rope(kc.unsqueeze(0), pos_c[None])[0]
             vc = kv_c[:, Hkv * D:].view(T, Hkv, D)
-            y = rms_norm(x, m.in_norm, c.rms_norm_eps).reshape(A * K, -1)
+            y, gate_a = self._read(f"attn{i}", x, getattr(m, "in_norm", None), getattr(m, "hc_attn", None), probe)
+            y = y.reshape(A * K, -1)
             qkv = y @ m.w_qkv.t()
             qg = qkv[:, :Hq * 2 * D].view(A * K, Hq, 2 * D)
             q, gate = qg[..., :D], qg[..., D:]
@@ -100,12 +154,13 @@ class DrafterTrain(nn.Module):
             s = s.masked_fill(~mask[None], float("-inf"))
             o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vals.float())
             o = (o * torch.sigmoid(gate.float())).reshape(A * K, Hq * D)
-            x = x + (o @ m.w_o.t()).view(A, K, -1)
-            y = rms_norm(x, m.post_norm, c.rms_norm_eps)
-            gu = y @ m.w13.t()
-            I = c.intermediate_size
-            x = x + (F.silu(gu[..., :I]) * gu[..., I:]) @ m.w2.t()
-        return rms_norm(x, self.final_norm, c.rms_norm_eps) @ self.lm_head.t()
+            o = (o @ m.w_o.t()).view(A, K, -1)
+            x = hc_inject(x, o, gate_a) if self.hc else x + o
+            y, gate_m = self._read(f"mlp{i}", x, getattr(m, "post_norm", None), getattr(m, "hc_mlp", None), probe)
+            f = self._ffn(m, y, i, probe)
+            x = hc_inject(x, f, gate_m) if self.hc else x + f
+        y, _ = self._read("final", x, getattr(self, "final_norm", None), getattr(self, "hc_final", None), probe)
+        return y @ self.lm_head.t()
 
     def loss(self, tokens, hidden, anchors, teacher_logits=None, kl_weight: float = 0.0):
         """Mean CE of every slot's next token (tokens outside the draft vocabulary are skipped), plus
@@ -125,7 +180,10 @@ class DrafterTrain(nn.Module):
 
     @torch.no_grad()
     def export_to(self, drafter):
-        """Copy the trained weights (bf16) into a serving ``models.drafter.Drafter`` of the same shape."""
+        """Copy the trained weights (bf16) into a serving ``models.drafter.Drafter`` of the same shape (plain residual,
+        dense FFN; ``train/drafter_tools.py`` converts the other variants first)."""
+        if self.hc or self.cfg.ffn != "dense":
+            raise ValueError("the serving drafter is plain / dense: convert this variant first (drafter_tools)")
         dt = torch.bfloat16
         drafter.embed.copy_(self.embed.to(dt))
         drafter.fc.copy_(self.fc.to(dt))

@@ -226,3 +226,28 @@ def test_hyper_connection_model_decodes_like_reference(tmp_path):
     loaded = HybridModel.from_package(d, dev)
     again = SpecEngine(loaded, None, ServeConfig(spec_k=0, accept_mode="greedy"), 2, 1024).generate(prompts, 16)
     assert again == plain
+
+
+def test_converted_drafter_directory_serves(tmp_path):
+    """An HC dense-shared drafter converted to plain, expanded and written as a block-FP8 deployment copy loads into
+    the serving drafter (``Drafter.from_dir``); greedy speculative decoding with it equals plain greedy decoding."""
+    from arc_forge_2026_b200.train import drafter_tools as dtl
+    from arc_forge_2026_b200.train.drafter_train import DrafterTrain
+    cfg, ref, model = _models(3)
+    dcfg = drafter_preset("tiny", residual="hc", hc_count=4, hc_lowrank=16, ffn="dense_shared",
+                          shared_intermediate_size=128)
+    src = DrafterTrain(dcfg, cfg.hidden_size, cfg.vocab_size, torch.arange(cfg.vocab_size), seed=4)
+    g = torch.Generator().manual_seed(4)
+    calib = [(torch.randint(0, cfg.vocab_size, (80,), generator=g), torch.randn(80, cfg.hidden_size, generator=g),
+              torch.arange(1, 70, 7)) for _ in range(2)]
+    plain, _ = dtl.convert_plain(src, calib)
+    big = dtl.expand_layers(plain, [0, 1, 1])
+    d = dtl.save_dir(big, tmp_path / "dep", "deploy", fp8=("attn", "mlp"))
+    drafter = Drafter.from_dir(d, dev)
+    assert drafter.cfg.num_layers == 3 and drafter.cfg.intermediate_size == dcfg.intermediate_size + 128
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (60, 17)]
+    out_plain = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy"), 2, 1024).generate(prompts, 24)
+    out_spec = SpecEngine(model, drafter, ServeConfig(spec_k=4, accept_mode="greedy"), 2, 1024).generate(prompts, 24)
+    torch.cuda.synchronize()
+    check_status()
+    assert out_plain == out_spec
