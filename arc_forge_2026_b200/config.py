@@ -61,6 +61,16 @@ class ModelConfig:
     rms_norm_eps: float = 1.0e-6
     hc_count: int = 1  # hyper-connection branches; 1 = plain residual stream
     hc_lowrank: int = 320  # rank of the hyper-connection mix projection
+    # per-layer n-gram embeddings (PLE): layers (0-based) that add a gated n-gram embedding to the stream
+    ple_layer_ids: tuple = ()
+    ngram_size: int = 3
+    heads_per_ngram: int = 8
+    ngram_vocab_size_base: int = 20_000_000
+    ple_embed_dim: int = 2560
+    ple_conv_kernel: int = 4
+    ple_conv_dilation: int = 1
+    ngram_seed: int = 1234
+    eos_token_id: int = 2
     init_std: float = 0.02
     # QSA sparse attention on the full-attention layers (0 = dense attention)
     qsa_block: int = 0
@@ -84,12 +94,22 @@ class ModelConfig:
             raise ValueError("rotary dimension must be positive and even")
         if self.expert_format not in ("int3", "fp8", "bf16"):
             raise ValueError(f"expert_format {self.expert_format!r}")
+        self.ple_layer_ids = tuple(int(i) for i in self.ple_layer_ids)
+        if any(not 0 <= i < self.num_layers for i in self.ple_layer_ids):
+            raise ValueError(f"ple_layer_ids {self.ple_layer_ids} outside the {self.num_layers} layers")
+        if self.ple_layer_ids and (self.ngram_size < 2 or self.ple_embed_dim % self.ngram_heads
+                                   or (self.ple_embed_dim // self.ngram_heads) % 16):
+            raise ValueError("PLE: ple_embed_dim must split into ngram heads of a multiple of 16 dims")
         if self.expert_format == "int3" and (self.hidden_size % 128 or self.moe_intermediate_size % 128):
             raise ValueError("uint3 g128 experts need hidden and expert widths divisible by 128")
 
     @property
     def layer_types(self) -> list[str]:
         return [FULL if (i + 1) % self.full_attention_interval == 0 else LINEAR for i in range(self.num_layers)]
+
+    @property
+    def ngram_heads(self) -> int:
+        return (self.ngram_size - 1) * self.heads_per_ngram
 
     @property
     def rotary_dim(self) -> int:

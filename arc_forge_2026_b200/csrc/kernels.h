@@ -262,6 +262,32 @@ int ep_gather(const EpArgs& a, const int* row_token, const int* nrows_dev, int r
 
 // hc.cu: hyper-connection residual stream [rows, G, H] (bf16): grouped norm, branch mix, gated write-back, and
 // their dX-only backward; H in {256, 512, 1024, 2048, 2560}, G <= 8
+// ---- per-layer n-gram embedding lookup (ple.cu)
+constexpr int PLE_MAX_SHARDS = 8;
+struct PleLookupArgs {
+  const int32_t* ext;      // tokens with their history inline
+  int64_t ext_len;
+  const int64_t* pos;      // [rows] index of each row's token in ext
+  const int64_t* seg;      // [rows] index in ext of each row's segment start
+  int rows;
+  int n, hpn, head_dim;    // n-gram size, heads per order, dims per head
+  int32_t eos;
+  const int64_t* mult;     // [n]
+  const int64_t* mod;      // [(n-1) * hpn]
+  const int64_t* off;      // [(n-1) * hpn]
+  const int64_t* hot_idx;  // compact table: sorted kept buckets of every head (nullptr: full table)
+  const int64_t* hot_base; // [(n-1) * hpn]
+  const int32_t* hot_len;  // [(n-1) * hpn]
+  const void* shards[PLE_MAX_SHARDS];        // table rows [rows_per_shard, head_dim] per shard
+  const float* scale_shards[PLE_MAX_SHARDS]; // e4m3 tables: 128 x 128 block scales per shard
+  int64_t rows_per_shard, table_rows;
+  int scale_ld;            // scale columns (ceil(head_dim / 128))
+  void* out;               // bf16 [rows, heads * head_dim]
+  int64_t* ids_out;        // optional [rows, heads] table rows (-1: hot-table miss)
+  uint32_t* status;
+};
+int ple_lookup(const PleLookupArgs& a, bool fp8, cudaStream_t st);
+
 int hc_norm_fwd(const void* h, const float* w, void* zb, float* rstd, int64_t rows, int G, int H, float eps,
                 cudaStream_t st);
 int hc_norm_bwd(const void* h, const float* w, const float* rstd, const float* dzb, void* dh, int64_t rows, int G,

@@ -839,6 +839,63 @@ static void hc_shape(const at::Tensor& h, int64_t& rows, int& G, int& H) {
   G = h.size(-2);
   rows = h.numel() / ((int64_t)G * H);
 }
+// ``shard_ptrs`` / ``scale_ptrs``: device addresses of the table shards (this process's tensors or peers' buffers
+// mapped from a symmetric heap); the Python wrapper checks their shapes.
+void ple_lookup_op(const at::Tensor& ext, const at::Tensor& pos, const at::Tensor& seg, int64_t n, int64_t hpn,
+                   int64_t eos, const at::Tensor& mult, const at::Tensor& mod, const at::Tensor& off,
+                   std::vector<int64_t> shard_ptrs, std::vector<int64_t> scale_ptrs, bool fp8, int64_t head_dim,
+                   int64_t rows_per_shard, int64_t table_rows, at::Tensor& out, c10::optional<at::Tensor> ids_out,
+                   c10::optional<at::Tensor> hot_idx, c10::optional<at::Tensor> hot_base,
+                   c10::optional<at::Tensor> hot_len) {
+  AFB_CHECK_DT(ext, at::kInt);
+  for (const at::Tensor* t : {&pos, &seg, &mult, &mod, &off}) AFB_CHECK_DT((*t), at::kLong);
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&ext, &pos, &seg, &mult, &mod, &off, &out})
+    AFB_CHECK_CONTIG((*t));
+  AFB_CHECK_DT(out, at::kBFloat16);
+  TORCH_CHECK(!shard_ptrs.empty() && (int)shard_ptrs.size() <= afb::PLE_MAX_SHARDS, "ple_lookup: 1..8 shards");
+  TORCH_CHECK(!fp8 || scale_ptrs.size() == shard_ptrs.size(), "ple_lookup: one scale pointer per e4m3 shard");
+  const int heads = (int)((n - 1) * hpn);
+  TORCH_CHECK(mult.numel() == n && mod.numel() == heads && off.numel() == heads, "ple_lookup: hash shapes");
+  TORCH_CHECK(pos.numel() == seg.numel() && out.numel() == pos.numel() * heads * head_dim, "ple_lookup: out shape");
+  TORCH_CHECK((int64_t)shard_ptrs.size() * rows_per_shard >= table_rows, "ple_lookup: shards cover the table");
+  afb::PleLookupArgs a{};
+  a.ext = ext.data_ptr<int32_t>();
+  a.ext_len = ext.numel();
+  a.pos = pos.data_ptr<int64_t>();
+  a.seg = seg.data_ptr<int64_t>();
+  a.rows = (int)pos.numel();
+  a.n = (int)n;
+  a.hpn = (int)hpn;
+  a.head_dim = (int)head_dim;
+  a.eos = (int32_t)eos;
+  a.mult = mult.data_ptr<int64_t>();
+  a.mod = mod.data_ptr<int64_t>();
+  a.off = off.data_ptr<int64_t>();
+  for (size_t i = 0; i < shard_ptrs.size(); ++i) {
+    a.shards[i] = reinterpret_cast<const void*>((uintptr_t)shard_ptrs[i]);
+    if (fp8) a.scale_shards[i] = reinterpret_cast<const float*>((uintptr_t)scale_ptrs[i]);
+  }
+  a.rows_per_shard = rows_per_shard;
+  a.table_rows = table_rows;
+  a.scale_ld = (int)((head_dim + 127) / 128);
+  a.out = out.data_ptr();
+  if (ids_out) {
+    AFB_CHECK_DT(ids_out.value(), at::kLong);
+    TORCH_CHECK(ids_out->numel() == pos.numel() * heads, "ple_lookup: ids_out shape");
+    a.ids_out = ids_out->data_ptr<int64_t>();
+  }
+  if (hot_idx) {
+    AFB_CHECK_DT(hot_idx.value(), at::kLong);
+    AFB_CHECK_DT(hot_base.value(), at::kLong);
+    AFB_CHECK_DT(hot_len.value(), at::kInt);
+    TORCH_CHECK(hot_base->numel() == heads && hot_len->numel() == heads, "ple_lookup: hot index shapes");
+    a.hot_idx = hot_idx->data_ptr<int64_t>();
+    a.hot_base = hot_base->data_ptr<int64_t>();
+    a.hot_len = hot_len->data_ptr<int32_t>();
+  }
+  a.status = status_ptr(out.get_device());
+  check_rc(afb::ple_lookup(a, fp8, stream()), "ple_lookup");
+}
 void hc_norm_op(const at::Tensor& h, const at::Tensor& w, double eps, at::Tensor& zb, at::Tensor& rstd,
                 c10::optional<at::Tensor> dzb, c10::optional<at::Tensor> dh) {
   int64_t rows;
@@ -1051,6 +1108,7 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("gather_rows", &gather_rows_op);
   m.def("gdn_decode", &gdn_decode_op);
   m.def("gdn_train", &gdn_train_op);
+  m.def("ple_lookup", &ple_lookup_op);
   m.def("hc_norm", &hc_norm_op);
   m.def("hc_mix", &hc_mix_op);
   m.def("hc_inject", &hc_inject_op);

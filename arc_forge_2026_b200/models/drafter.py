@@ -60,7 +60,6 @@ class Drafter:
         cos, sin = rope_cos_sin(torch.arange(1 << 17, device=dev), D, cfg.rope_theta)
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
 
-    @property
     @classmethod
     def from_dir(cls, path, device, verify: bool = True) -> "Drafter":
         """Load a drafter directory (``train/drafter_tools.py`` layout: an export, a plain conversion, a layer
@@ -71,6 +70,7 @@ class Drafter:
         twin.export_to(d)
         return d
 
+    @property
     def kv_row_offset(self) -> int:
         c = self.cfg
         return c.num_attention_heads * 2 * c.head_dim

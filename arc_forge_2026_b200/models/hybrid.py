@@ -372,7 +372,7 @@ class HybridModel:
             hs.copy_(h[:, None, :].expand(N, G, H))
         for lw in self.layers:
             if hs is not None:
-                x, gate = hc_read(hs, lw.hc_attn, G)
+                x, hc_gate = hc_read(hs, lw.hc_attn, G)
                 cC.rmsnorm(x, None, lw.in_norm, y, c.rms_norm_eps, True)
             else:
                 cC.rmsnorm(h, None, lw.in_norm, y, c.rms_norm_eps, True)
@@ -417,8 +417,8 @@ class HybridModel:
                 gi += 1
             resid = h
             if hs is not None:
-                hc_inject_(hs, h, gate)
-                x, gate = hc_read(hs, lw.hc_mlp, G)
+                hc_inject_(hs, h, hc_gate)
+                x, hc_gate = hc_read(hs, lw.hc_mlp, G)
                 cC.rmsnorm(x, None, lw.post_norm, y, c.rms_norm_eps, True)
                 resid = ws.zero[:N]
             else:
@@ -430,7 +430,7 @@ class HybridModel:
                 moe_forward(y, resid, lw.router_ext, lw.bank, lw.shared_w13, lw.shared_w2, c.num_experts_per_tok,
                             ws.moe, out=h, renorm=c.norm_topk_prob)
             if hs is not None:
-                hc_inject_(hs, h, gate)
+                hc_inject_(hs, h, hc_gate)
         if hs is not None:
             h = hc_read(hs, self.hc_final, G)[0]
         cC.rmsnorm(h, None, self.final_norm, y, c.rms_norm_eps, True)

@@ -346,8 +346,38 @@ class DecoderLayer(nn.Module):
         if self.hc:  # hyper-connections: each sub-layer reads a mix of the branches and writes back gated
             self.hc_attn = HyperConnection(cfg)
             self.hc_mlp = HyperConnection(cfg)
+        from .ple import PLELayer
+        self.ple = PLELayer(cfg) if index in cfg.ple_layer_ids else None
 
-    def forward(self, x, positions, cache=None):
+    def _ple(self, x, tokens, cache):
+        """Add the per-layer n-gram embedding update (one sequence per batch row; ``cache`` keeps the last n-1 tokens
+        and the conv inputs of every row for incremental decoding)."""
+        ple = self.ple
+        xs = x if self.hc else x.unsqueeze(-2)
+        pad = (ple.k - 1) * ple.dil
+        hists = cache.get("ple_hist") if cache is not None else None
+        states = cache.get("ple_conv") if cache is not None else None
+        outs, new_h, new_s = [], [], []
+        for b in range(tokens.shape[0]):
+            hist = hists[b] if hists is not None else None
+            state = states[b] if states is not None else None
+            upd, c = ple.mix(xs[b], ple.embed(ple.hash.ids(tokens[b], history=hist)), conv_state=state)
+            outs.append(upd)
+            if cache is not None:
+                ext = tokens[b].long() if hist is None else torch.cat([hist, tokens[b].long()])
+                new_h.append(ext[-(ple.hash.n - 1):])
+                prev = torch.zeros(pad, c.shape[1], device=c.device) if state is None else state
+                new_s.append(torch.cat([prev, c])[-pad:] if pad else prev)
+        if cache is not None:
+            cache["ple_hist"], cache["ple_conv"] = new_h, new_s
+        upd = torch.stack(outs).to(x.dtype)
+        return x + (upd if self.hc else upd.squeeze(-2))
+
+    def forward(self, x, positions, cache=None, tokens=None):
+        if self.ple is not None:
+            if tokens is None:
+                raise ValueError("a PLE layer needs the token ids")
+            x = self._ple(x, tokens, cache)
         if self.hc:  # x is the branch stream [B, T, G, H]
             a, g = self.hc_attn(x)
             x = hc_inject(x, self.mixer(self.input_layernorm(a), positions, cache), g)
@@ -399,7 +429,7 @@ class HybridMoE(nn.Module):
         if self.hc_final is not None:  # every branch starts as the embedding
             x = x[..., None, :].expand(*x.shape[:-1], self.cfg.hc_count, x.shape[-1]).contiguous()
         for i, layer in enumerate(self.layers):
-            x = layer(x, positions, None if cache is None else cache[i])
+            x = layer(x, positions, None if cache is None else cache[i], ids)
         if self.hc_final is not None:
             x = self.hc_final(x)[0]
         return self.norm(x)

@@ -20,6 +20,7 @@ from torch.utils.checkpoint import checkpoint
 
 from ..config import FULL, ModelConfig
 from ..models import reference as R
+from ..models.ple import PLELayer
 from ..quant.int3_tiles import codes_to_tiles
 from . import fused
 from .fakequant import fp8_weight, int3_weight
@@ -143,6 +144,8 @@ def layer_tensors_from_reference(L: R.DecoderLayer, codes_scales) -> dict:
              w2_scales=s2, shared_gate=moe.shared_gate_proj.weight, shared_up=moe.shared_up_proj.weight,
              shared_down=moe.shared_down_proj.weight, shared_expert_gate=moe.shared_expert_gate.weight)
     out = {k: v.detach() for k, v in t.items()}
+    if getattr(L, "ple", None) is not None:  # per-layer n-gram embedding (frozen)
+        out["ple"] = {k: v.detach() for k, v in L.ple.state_dict().items()}
     if getattr(L, "hc", False):  # hyper-connection weights (frozen)
         out["hc_attn"] = {k: v.detach() for k, v in L.hc_attn.state_dict().items()}
         out["hc_mlp"] = {k: v.detach() for k, v in L.hc_mlp.state_dict().items()}
@@ -200,6 +203,13 @@ def random_layer_tensors(cfg: ModelConfig, kind: str, device, gen: torch.Generat
     return t
 
 
+def random_ple_tensors(cfg: ModelConfig, device, gen) -> dict:
+    """Random weights of one PLE layer (the n-gram table at ``init_std``)."""
+    m = PLELayer(cfg)
+    return {k: (torch.randn(v.shape, generator=gen, device=device) * cfg.init_std if v.dim() == 2
+                else torch.zeros(v.shape, device=device)) for k, v in m.state_dict().items()}
+
+
 class StudentLayer(nn.Module):
     def __init__(self, cfg: ModelConfig, kind: str, t: dict):
         super().__init__()
@@ -227,6 +237,37 @@ class StudentLayer(nn.Module):
             dev = t["in_norm"].device
             self.hc_attn = _hc_module(cfg, t["hc_attn"], True, dev)
             self.hc_mlp = _hc_module(cfg, t["hc_mlp"], True, dev)
+        self.ple = None
+        if "ple" in t:  # per-layer n-gram embedding, frozen; its table lookup is the native kernel on the GPU
+            self.ple = PLELayer(cfg)
+            self.ple.load_state_dict({k: v.float() for k, v in t["ple"].items()})
+            self.ple.to(t["in_norm"].device).requires_grad_(False)
+        self._ple_table = None
+
+    def _ple_update(self, x, tokens, pack):
+        """The PLE stream update of x ([B, T, H] or [B, T, G, H]) for token ids [B, T]."""
+        from . import kernels
+        ple = self.ple
+        B, T = tokens.shape
+        xs = x if self.hc_attn is not None else x.unsqueeze(-2)
+        seg = None
+        if pack is not None:  # each token's segment start in the packed row
+            seg = torch.arange(T, device=tokens.device) - pack["pos"].reshape(-1).long()
+        native = tokens.is_cuda and kernels.use("ple")
+        if native and self._ple_table is None:
+            from ..ops.ple import PleTable
+            self._ple_table = PleTable.from_weight(ple.hash, ple.table, tokens.device, fp8=True)
+        outs = []
+        for b in range(B):
+            if native:
+                e = self._ple_table.lookup_tokens(tokens[b], seg)
+            else:
+                e = ple.embed(ple.hash.ids(tokens[b], seg))
+            if tokens.is_cuda:
+                kernels.hit("ple", native)
+            outs.append(ple.mix(xs[b], e.float(), seg)[0])
+        upd = torch.stack(outs).to(x.dtype)
+        return upd if self.hc_attn is not None else upd.squeeze(-2)
 
     def _lin(self, name: str, x, fp8: bool):
         """x @ W^T for projection ``name`` (block-FP8 QAT weight when ``fp8``), plus its LoRA adapter if attached."""
@@ -287,11 +328,15 @@ class StudentLayer(nn.Module):
                                  c.rms_norm_eps)
         return self._lin("out_proj", o.reshape(B, T, -1), True)
 
-    def forward(self, x, pack=None):
+    def forward(self, x, pack=None, tokens=None):
         c = self.cfg
         B, T, H = x.shape[0], x.shape[1], x.shape[-1]
         if pack is not None and B != 1:
             raise ValueError("packed bins are single rows (B = 1)")
+        if self.ple is not None:
+            if tokens is None:
+                raise ValueError("a PLE layer needs the token ids")
+            x = x + self._ple_update(x, tokens, pack)
         if self.hc_attn is not None:  # x: the branch stream [B, T, G, H]
             a, g = hc_read(x, self.hc_attn)
             y = fused.rms_norm(a, self.in_norm, c.rms_norm_eps)
@@ -345,9 +390,9 @@ class QADStudent(nn.Module):
             x = x[..., None, :].expand(*x.shape[:-1], self.cfg.hc_count, x.shape[-1]).contiguous()
         for L in self.layers:
             if self.ckpt and torch.is_grad_enabled():
-                x = checkpoint(L, x, pack, use_reentrant=False)
+                x = checkpoint(L, x, pack, ids, use_reentrant=False)
             else:
-                x = L(x, pack)
+                x = L(x, pack, ids)
         if hc is not None:
             x = hc_read(x, hc)[0]
         return fused.rms_norm(x, self.final_norm, self.cfg.rms_norm_eps)
@@ -364,7 +409,12 @@ def random_student(cfg: ModelConfig, device, seed: int = 0, checkpoint_layers=Tr
     st.register_buffer("embed", (torch.randn(V, H, generator=gen, device=dev) * cfg.init_std).to(torch.bfloat16))
     st.register_buffer("final_norm", torch.zeros(H, device=dev))
     st.register_buffer("lm_head", (torch.randn(V, H, generator=gen, device=dev) * cfg.init_std).to(torch.bfloat16))
-    st.layers = nn.ModuleList([StudentLayer(cfg, kind, random_layer_tensors(cfg, kind, dev, gen))
-                               for kind in cfg.layer_types])
+    layers = []
+    for i, kind in enumerate(cfg.layer_types):
+        t = random_layer_tensors(cfg, kind, dev, gen)
+        if i in cfg.ple_layer_ids:
+            t["ple"] = random_ple_tensors(cfg, dev, gen)
+        layers.append(StudentLayer(cfg, kind, t))
+    st.layers = nn.ModuleList(layers)
     st.hc_final = _hc_module(cfg, random_hc_tensors(cfg, dev, gen, inject=False), False, dev) if cfg.hc_count > 1 else None
     return st

@@ -344,6 +344,32 @@ def test_hyper_connection_student_trains_on_native_kernels():
     assert losses[-1] < losses[0], losses
 
 
+def test_ple_student_trains_with_the_native_lookup():
+    """A QAD student with a PLE layer (and 2 hyper-connection branches) steps on the GPU; the n-gram lookup runs
+    on the native kernel."""
+    from arc_forge_2026_b200.config import QADConfig, preset
+    from arc_forge_2026_b200.formats.topk_targets import synthetic_targets
+    from arc_forge_2026_b200.train import kernels
+    from arc_forge_2026_b200.train.qad import build_optimizer, enforce_scale_invariants, train_step
+    from arc_forge_2026_b200.train.student import random_student
+    cfg = preset("tiny_gpu", ple_layer_ids=(1,), ngram_vocab_size_base=4001, ple_embed_dim=256, hc_count=2,
+                 hc_lowrank=64)
+    st = random_student(cfg, dev, seed=0)
+    qc = QADConfig(seq_len=256, topk=16, direction="reverse", lr_scale=1e-3, lr_router=1e-3, lr_dense=1e-3)
+    opt = build_optimizer(st, qc, sharded=True)
+    signs = enforce_scale_invariants(st, None)
+    gen = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (2, 256), generator=gen).to(dev)
+    t = synthetic_targets(ids.numel(), 16, cfg.vocab_size, gen, dev)
+    kernels.reset()
+    losses = [train_step(st, opt, ids, t, qc, signs)[0] for _ in range(4)]
+    torch.cuda.synchronize()
+    check_status()
+    c = kernels.counts()
+    assert c["native"].get("ple", 0) >= 4 * 2 and "ple" not in c["fallback"], c
+    assert losses[-1] < losses[0], losses
+
+
 def test_native_fp8_teacher_targets_agree_with_its_prefill():
     from arc_forge_2026_b200.config import ServeConfig, preset
     from arc_forge_2026_b200.models.hybrid import HybridModel
