@@ -35,3 +35,9 @@ def test_replica_guard_detects_cross_rank_mismatch_on_two_ranks():
     r = _torchrun("tests/guard_worker.py", 2)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count('"mismatch_raised": true') == 2
+
+
+def test_row_sharded_ple_lookup_over_peer_memory_on_two_ranks():
+    r = _torchrun("tests/ple_worker.py", 2)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("peer_vs_contract") == 2

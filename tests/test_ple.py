@@ -139,3 +139,38 @@ def test_student_with_ple_follows_reference():
     assert rel < 0.2, rel
     st.hidden(ids).pow(2).mean().backward()
     assert st.layers[0].moe.w13_scales.grad is not None
+
+
+def _shard_worker(rank, world, port, out):
+    import os
+    import torch.distributed as dist
+    from arc_forge_2026_b200.parallel.ple_shard import ShardedPleTable, shard_rows
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    cfg = _cfg()
+    h = P.NgramHash(cfg)
+    w = torch.randn(h.rows, 16, generator=torch.Generator().manual_seed(9))
+    per = shard_rows(h.rows, world)
+    t = ShardedPleTable(h, w[rank * per:(rank + 1) * per], rank, world, "cpu", fp8=True, group=None)
+    toks = torch.randint(0, cfg.vocab_size, (20 + 7 * rank,), generator=torch.Generator().manual_seed(rank))
+    got = t.lookup_tokens(toks)
+    # the unsharded table quantised per shard: every 128-row scale block lies inside one shard
+    full = torch.cat([w, w.new_zeros(per * world - h.rows, 16)])
+    from arc_forge_2026_b200.quant.fp8 import dequant_weight_block, quantize_weight_block
+    q, s = quantize_weight_block(full)
+    dense = dequant_weight_block(q, s)
+    want = dense[h.ids(toks)].flatten(-2)
+    torch.save({"err": (got - want).abs().max().item()}, f"{out}/r{rank}.pt")
+    dist.destroy_process_group()
+
+
+def test_row_sharded_table_over_gloo_ranks(tmp_path):
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_shard_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        assert torch.load(tmp_path / f"r{r}.pt")["err"] < 1e-6
