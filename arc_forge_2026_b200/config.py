@@ -175,7 +175,7 @@ class ServeConfig:
     max_sessions: int = 128
     page_size: int = 64
     max_context: int = 32768
-    kv_dtype: str = "bf16"  # bf16 | fp8
+    kv_dtype: str = "bf16"  # the paged KV cache holds bf16 (the only format the attention kernels read)
     gdn_state_dtype: str = "fp32"
     spec_k: int = 4  # 0 disables speculative decoding
     accept_mode: str = "rejection"  # rejection | greedy | bernoulli

@@ -91,3 +91,34 @@ def write_manifest(path: Path, drop: torch.Tensor, scores: torch.Tensor, meta: d
     tmp.write_text(json.dumps(doc, indent=1) + "\n")
     tmp.rename(path)
     return doc
+
+
+@torch.no_grad()
+def verify_pruned(pruned: HybridMoE, source: HybridMoE, manifest: dict) -> dict:
+    """Byte-identity provenance of a pruned model (the reference's
+    ``training/work/qwen38fn_eval/probes/verify_pruned_vs_incumbent.py``): every kept expert's w13 / w2 and router
+    row equal the source's at its original id (manifest ``keep`` lists), every other tensor is unchanged. Raises
+    on the first difference; returns counts of what was checked."""
+    keep = manifest["keep"]
+    src_moe, dst_moe = list(source.moe_layers()), list(pruned.moe_layers())
+    if len(keep) != len(src_moe) or len(dst_moe) != len(src_moe):
+        raise ValueError("manifest layers differ from the models'")
+    experts = 0
+    for layer, (a, b, ids) in enumerate(zip(src_moe, dst_moe, keep)):
+        if b.w13.shape[0] != len(ids) or ids != sorted(ids):
+            raise ValueError(f"layer {layer}: {b.w13.shape[0]} experts for {len(ids)} keep ids (ascending)")
+        for j, e in enumerate(ids):
+            for name in ("w13", "w2"):
+                if not torch.equal(getattr(b, name)[j], getattr(a, name)[e]):
+                    raise ValueError(f"layer {layer}: pruned expert {j} {name} differs from source expert {e}")
+            if not torch.equal(b.gate.weight[j], a.gate.weight[e]):
+                raise ValueError(f"layer {layer}: router row {j} differs from source row {e}")
+            experts += 1
+    moe_keys = (".mlp.w13", ".mlp.w2", ".mlp.gate.weight")
+    sd_a, sd_b = source.state_dict(), pruned.state_dict()
+    others = [k for k in sd_a if not k.endswith(moe_keys)]
+    for k in others:
+        if k not in sd_b or not torch.equal(sd_a[k], sd_b[k]):
+            raise ValueError(f"{k}: changed by pruning")
+    return {"experts": experts, "other_tensors": len(others)}
+

@@ -436,8 +436,14 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200", ledge
 
 
 def _build_engine(args):
+    """The serving engine of the command line (the reference's B200 launch script,
+    ``training/work/qwen38fn_eval/serve_qwen38fn_0520.sh:1-80``): a deploy package (``--package``) or random-init
+    weights of ``--preset``; a drafter directory (``--drafter-dir``) or a random drafter of ``--drafter``; the
+    speculative width, acceptance rule, KV / QSA / HiSparse options."""
     import torch
     from ..config import ServeConfig, drafter_preset, preset
+    if args.package and not args.gpu:
+        raise SystemExit("--package needs --gpu (the CPU engine serves the fp32 oracle of a preset)")
     cfg = preset(args.preset)
     if not args.gpu:
         from ..models.reference import build_reference
@@ -447,9 +453,18 @@ def _build_engine(args):
     from ..models.hybrid import HybridModel
     from .engine import SpecEngine
     dev = torch.device("cuda", 0)
-    model = HybridModel.random(cfg, dev, seed=args.seed)
-    drafter = Drafter(drafter_preset(args.drafter), cfg.hidden_size, cfg.vocab_size, dev, seed=args.seed + 1)
-    eng = SpecEngine(model, drafter, ServeConfig(spec_k=args.spec_k), args.sessions, args.max_context)
+    if args.package:
+        model = HybridModel.from_package(args.package, dev)
+        cfg = model.cfg
+    else:
+        model = HybridModel.random(cfg, dev, seed=args.seed)
+    drafter = None
+    if args.spec_k > 0:
+        drafter = (Drafter.from_dir(args.drafter_dir, dev) if args.drafter_dir else
+                   Drafter(drafter_preset(args.drafter), cfg.hidden_size, cfg.vocab_size, dev, seed=args.seed + 1))
+    scfg = ServeConfig(spec_k=args.spec_k, accept_mode=args.accept_mode, temperature=args.temperature,
+                       hisparse=args.hisparse, seed=args.seed)
+    eng = SpecEngine(model, drafter, scfg, args.sessions, args.max_context)
     return eng, cfg
 
 
@@ -457,8 +472,15 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="tiny_cpu")
     ap.add_argument("--gpu", action="store_true", help="native engine on cuda:0 (random-init weights)")
+    ap.add_argument("--package", default=None, help="INT3 deploy package directory (formats/int3_package.py)")
     ap.add_argument("--drafter", default="tiny")
+    ap.add_argument("--drafter-dir", dest="drafter_dir", default=None,
+                    help="drafter directory (train/drafter_tools.py layout) instead of a random drafter")
     ap.add_argument("--spec-k", dest="spec_k", type=int, default=4)
+    ap.add_argument("--accept-mode", dest="accept_mode", default="rejection",
+                    choices=["rejection", "greedy", "bernoulli"])
+    ap.add_argument("--temperature", type=float, default=0.0)
+    ap.add_argument("--hisparse", action="store_true", help="host KV pool for idle pages (QSA models)")
     ap.add_argument("--sessions", type=int, default=8)
     ap.add_argument("--max-context", dest="max_context", type=int, default=4096)
     ap.add_argument("--tokenizer", default=None, help="local Hugging Face tokenizer directory (default: bytes)")

@@ -1,4 +1,5 @@
 """CPU tests of the oracle model and the formats (tiny hybrid MoE, fp32, seed 0)."""
+import pytest
 import torch
 
 from arc_forge_2026_b200.config import preset
@@ -124,8 +125,15 @@ def test_config1_pipeline_prune_quantize_decode():
     drop = saliency.keep_mask(scores, 20)
     mass = saliency.retained_mass(scores, drop)
     assert 0.6 < mass["min"] <= mass["mean"] <= 1.0
+    source = build_reference(cfg, seed=0)
     saliency.prune_experts(model, drop)
     assert model.cfg.num_experts == 20 and model.layers[0].mlp.w13.shape[0] == 20
+    manifest = {"keep": [(~drop[i]).nonzero().flatten().tolist() for i in range(drop.shape[0])]}
+    got = saliency.verify_pruned(model, source, manifest)
+    assert got["experts"] == 20 * cfg.num_layers and got["other_tensors"] > 0
+    bad = {"keep": [list(reversed(k)) for k in manifest["keep"]]}
+    with pytest.raises(ValueError):
+        saliency.verify_pruned(model, source, bad)
 
     # GPTQ every expert of every layer with Hessians from its routed calibration rows
     packs = []
