@@ -95,6 +95,14 @@ def package_tensors(ref, codes_scales, dense_fp8: bool = True) -> dict[str, torc
         if getattr(L, "hc", False):
             for n in ("hc_attn", "hc_mlp"):
                 _put_hc(out, f"{p}.{n}", getattr(L, n))
+        if getattr(L, "ple", None) is not None:  # n-gram table in block FP8; projections bf16; norms, conv fp32
+            ple = L.ple
+            q, s = quantize_weight_block(ple.table.detach().float().cpu())
+            out[f"{p}.ple.table.weight"], out[f"{p}.ple.table.weight_scale_inv"] = q, s
+            for n in ("key_proj", "value_proj"):
+                out[f"{p}.ple.{n}"] = getattr(ple, n).detach().cpu().to(torch.bfloat16).contiguous()
+            for n in ("norm_key", "norm_query", "norm_conv", "conv"):
+                out[f"{p}.ple.{n}"] = getattr(ple, n).detach().float().cpu().contiguous()
     if getattr(ref, "hc_final", None) is not None:
         _put_hc(out, "model.hc_final", ref.hc_final)
     return out

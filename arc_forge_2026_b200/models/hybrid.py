@@ -26,6 +26,7 @@ from ..ops import C
 from ..ops.attention import PAGE, paged_attention
 from ..ops.gdn import GdnScratch, GdnShape, GdnState, gdn_decode
 from ..ops.hc import HCWeights, hc_inject_, hc_read
+from ..ops.ple import PleServeState, PleServeWeights, ple_serve
 from ..ops.moe import Fp8ExpertBank, Int3ExpertBank, MoEWorkspace, moe_forward, router_weight_with_shared_gate
 from ..ops.qsa import qsa_attention
 from ..parallel.ep import EPMoEWorkspace, moe_forward_ep
@@ -59,6 +60,8 @@ class LayerWeights:
     # hyper-connections (hc_count > 1): the read before / write-back after each sub-layer
     hc_attn: HCWeights | None = None
     hc_mlp: HCWeights | None = None
+    # per-layer n-gram embedding (the layers of cfg.ple_layer_ids)
+    ple: PleServeWeights | None = None
 
 
 @dataclass
@@ -82,6 +85,35 @@ class StepBatch:
     @property
     def num_tokens(self) -> int:
         return self.ids.shape[0]
+
+
+def _random_ple(cfg: ModelConfig, std: float, gen, dev) -> PleServeWeights:
+    from ..models.ple import NgramHash
+    from ..ops.ple import PleTable
+    h = NgramHash(cfg)
+    G, H, E = cfg.hc_count, cfg.hidden_size, cfg.ple_embed_dim
+    D = E // cfg.ngram_heads
+    # e4m3 rows drawn directly (a real table is ~51 GB: no fp32 staging), scale std per 128 x 128 block
+    rows = torch.randn(h.rows, D, generator=gen, device=dev).clamp_(-8, 8).to(torch.float8_e4m3fn)
+    scale = torch.full(((h.rows + 127) // 128, (D + 127) // 128), std, dtype=torch.float32, device=dev)
+
+    def rn(*s):
+        return torch.randn(*s, generator=gen, device=dev) * std
+    z = torch.zeros(G * H, device=dev)
+    return PleServeWeights(PleTable(h, rows, scale), rn(G * H, E), rn(H, E), z, z.clone(), z.clone(),
+                           rn(G * H, cfg.ple_conv_kernel), G, H, cfg.rms_norm_eps, cfg.ple_conv_dilation)
+
+
+def _ple_from_package(t: dict, prefix: str, cfg: ModelConfig, dev) -> PleServeWeights:
+    from ..models.ple import NgramHash
+    from ..ops.ple import PleTable
+    rows = t[f"{prefix}.table.weight"]
+    table = (PleTable(NgramHash(cfg), rows.to(dev), t[f"{prefix}.table.weight_scale_inv"].float().to(dev))
+             if rows.dtype == torch.float8_e4m3fn else PleTable(NgramHash(cfg), rows.to(dev, torch.bfloat16), None))
+    f = {n: t[f"{prefix}.{n}"].to(dev) for n in ("key_proj", "value_proj", "norm_key", "norm_query", "norm_conv",
+                                                  "conv")}
+    return PleServeWeights(table, f["key_proj"], f["value_proj"], f["norm_key"], f["norm_query"], f["norm_conv"],
+                           f["conv"], cfg.hc_count, cfg.hidden_size, cfg.rms_norm_eps, cfg.ple_conv_dilation)
 
 
 def _hc_from_package(t: dict, prefix: str, cfg: ModelConfig, dev) -> HCWeights:
@@ -196,6 +228,8 @@ class HybridModel:
             for lw in layers:
                 lw.hc_attn, lw.hc_mlp = (HCWeights.random(G, H, cfg.hc_lowrank, std, cfg.rms_norm_eps, True, gen, dev)
                                          for _ in range(2))
+        for i in cfg.ple_layer_ids:
+            layers[i].ple = _random_ple(cfg, std, gen, dev)
         embed = randn(cfg.vocab_size, H)
         m = cls(cfg, layers, embed, torch.zeros(H, dtype=torch.bfloat16, device=dev), randn(cfg.vocab_size, H), dev)
         if G > 1:
@@ -240,6 +274,8 @@ class HybridModel:
             lw.shared_w2 = moe.shared_down_proj.weight.detach().to(**bf).contiguous()
             if getattr(L, "hc", False):
                 lw.hc_attn, lw.hc_mlp = HCWeights.from_module(L.hc_attn, dev), HCWeights.from_module(L.hc_mlp, dev)
+            if getattr(L, "ple", None) is not None:
+                lw.ple = PleServeWeights.from_module(L.ple, dev)
             layers.append(lw)
         m = cls(cfg, layers, ref.embed_tokens.weight.detach().to(**bf), ref.norm.weight.detach().to(**bf),
                 ref.lm_head.weight.detach().to(**bf), dev)
@@ -284,6 +320,8 @@ class HybridModel:
             lw.shared_w2 = dense_weight(t, f"{m}.shared_expert.down_proj").to(**bf).contiguous()
             if cfg.hc_count > 1:
                 lw.hc_attn, lw.hc_mlp = (_hc_from_package(t, f"{p}.{n}", cfg, dev) for n in ("hc_attn", "hc_mlp"))
+            if i in cfg.ple_layer_ids:
+                lw.ple = _ple_from_package(t, f"{p}.ple", cfg, dev)
             layers.append(lw)
         m = cls(cfg, layers, t["model.embed_tokens.weight"].to(**bf), t["model.norm.weight"].to(**bf),
                 t["lm_head.weight"].to(**bf), dev)
@@ -347,6 +385,10 @@ class HybridModel:
                  torch.zeros(sessions * max_pages, self.cfg.qsa_indexer_dim, **z))
                 for _ in range(self.cfg.num_attention_layers)]
 
+    def new_ple_states(self, slots: int, max_q: int):
+        """Side state of every PLE layer (n-gram history, conv inputs, pending rows of the last window)."""
+        return [PleServeState(lw.ple, slots, max_q, self.device) for lw in self.layers if lw.ple is not None]
+
     def new_gdn_states(self, slots: int, max_q: int):
         return [GdnState(self.gdn_shape, slots, max_q, self.device) for _ in range(self.cfg.num_gdn_layers)]
 
@@ -354,10 +396,12 @@ class HybridModel:
         return Workspace(self, max_tokens)
 
     # ------------------------------------------------------------------ forward
-    def forward(self, b: StepBatch, kv, gdn, ws: "Workspace", gdn_scratch: GdnScratch | None = None, qsa=None):
+    def forward(self, b: StepBatch, kv, gdn, ws: "Workspace", gdn_scratch: GdnScratch | None = None, qsa=None,
+                ple=None):
         """Runs the stack over b.ids; returns the final-normed hidden rows [N, H] (a view into the workspace).
         ``qsa`` (a ``QsaState``): the full-attention layers store index keys and, on verify batches, attend to
-        their QSA page selection instead of the whole context."""
+        their QSA page selection instead of the whole context. ``ple``: the PLE side states (``new_ple_states``) when
+        the model has PLE layers."""
         c, cC = self.cfg, C()
         N, H = b.num_tokens, c.hidden_size
         h = ws.h[:N]
@@ -370,7 +414,12 @@ class HybridModel:
         if G > 1:  # branch stream; h becomes the sub-layer output buffer
             hs = ws.hs[:N]
             hs.copy_(h[:, None, :].expand(N, G, H))
+        pi = 0
         for lw in self.layers:
+            if lw.ple is not None:
+                ple_serve(hs if hs is not None else h.view(N, 1, H), b.ids, lw.ple, ple[pi], b.seq_slot, b.n_commit,
+                          b.q_per_seq, b.parity, b.commit_current)
+                pi += 1
             if hs is not None:
                 x, hc_gate = hc_read(hs, lw.hc_attn, G)
                 cC.rmsnorm(x, None, lw.in_norm, y, c.rms_norm_eps, True)

@@ -9,6 +9,8 @@ only the most used buckets of every head; a miss reads zeros.
 """
 from __future__ import annotations
 
+import math
+
 import numpy as np
 import torch
 
@@ -97,3 +99,110 @@ class PleTable:
         dense = self.dense_rows().cpu()
         dense = torch.cat([dense, torch.zeros(1, self.D)])           # row -1 -> zeros
         return dense[torch.where(ids < 0, torch.full_like(ids, dense.shape[0] - 1), ids)].flatten(-2)
+
+
+# ---------------------------------------------------------------------------------------------- serving
+def _group_rms(x: torch.Tensor, w: torch.Tensor, G: int, eps: float) -> torch.Tensor:
+    z = x.float().unflatten(-1, (G, -1))
+    z = z * torch.rsqrt(z.square().mean(-1, keepdim=True) + eps)
+    return z.flatten(-2) * (1.0 + w)
+
+
+class PleServeWeights:
+    """One PLE layer in the serving layout: the device table, bf16 projections for the tcgen05 GEMM, fp32 norms and
+    conv taps."""
+
+    def __init__(self, table: PleTable, key_proj, value_proj, norm_key, norm_query, norm_conv, conv, G: int, H: int,
+                 eps: float, dil: int):
+        bf = torch.bfloat16
+        self.table = table
+        self.key_proj, self.value_proj = key_proj.to(bf).contiguous(), value_proj.to(bf).contiguous()
+        self.norm_key, self.norm_query, self.norm_conv = (t.float().contiguous() for t in (norm_key, norm_query,
+                                                                                           norm_conv))
+        self.conv = conv.float().contiguous()
+        self.G, self.H, self.eps, self.dil = G, H, eps, dil
+        self.k = conv.shape[1]
+        self.pad = (self.k - 1) * dil
+
+    @classmethod
+    def from_module(cls, mod, device, fp8: bool = True) -> "PleServeWeights":
+        """From a ``models.ple.PLELayer``."""
+        dev = torch.device(device)
+        t = PleTable.from_weight(mod.hash, mod.table, dev, fp8=fp8)
+        return cls(t, mod.key_proj.detach().to(dev), mod.value_proj.detach().to(dev), mod.norm_key.detach().to(dev),
+                   mod.norm_query.detach().to(dev), mod.norm_conv.detach().to(dev), mod.conv.detach().to(dev),
+                   mod.G, mod.H, mod.eps, mod.dil)
+
+
+class PleServeState:
+    """Per slot: the last n-1 committed tokens (right-aligned, ``hist_len`` valid), the last (k-1)·dil committed conv
+    inputs, and the pending tokens / conv inputs of the last verify window (double-buffered by parity) that the next
+    cycle commits up to its accepted count — the deferred commit the GDN verify uses, applied to the PLE side state
+    (the reference's serving patch 0016 commits this state after verification)."""
+
+    def __init__(self, w: PleServeWeights, slots: int, max_q: int, device):
+        dev = torch.device(device)
+        n1 = w.table.hash.n - 1
+        C = w.G * w.H
+        self.n1, self.max_q = n1, max_q
+        self.hist = torch.zeros(slots, n1, dtype=torch.int64, device=dev)
+        self.hist_len = torch.zeros(slots, dtype=torch.int64, device=dev)
+        self.conv = torch.zeros(slots, w.pad, C, dtype=torch.float32, device=dev)
+        self.ptok = torch.zeros(2, slots, max_q, dtype=torch.int64, device=dev)
+        self.pconv = torch.zeros(2, slots, max_q, C, dtype=torch.float32, device=dev)
+
+    def reset(self, slot: int):
+        for t in (self.hist, self.hist_len, self.conv):
+            t[slot].zero_()
+
+
+def ple_serve(stream: torch.Tensor, tokens: torch.Tensor, w: PleServeWeights, st: PleServeState, seq_slot,
+              n_commit, q_per_seq: int, parity: int, commit_current: bool):
+    """Add the PLE update to ``stream`` [N, G, H] (bf16, in place) for a step of S = N / q_per_seq sequences of
+    ``q_per_seq`` rows. Device-side only (fixed shapes): CUDA-graph capturable."""
+    from . import C as _C
+    S, W = seq_slot.numel(), q_per_seq
+    N = S * W
+    n1, pad = st.n1, w.pad
+    slots = seq_slot.long()
+    dev = stream.device
+    if not commit_current:  # commit the previous window's accepted rows
+        prev = parity ^ 1
+        nc = n_commit.long()[slots]                                                     # [S]
+        ext_t = torch.cat([st.hist[slots], st.ptok[prev, slots]], 1)                   # [S, n1 + max_q]
+        st.hist[slots] = torch.gather(ext_t, 1, nc[:, None] + torch.arange(n1, device=dev))
+        st.hist_len[slots] = torch.clamp(st.hist_len[slots] + nc, max=n1)
+        if pad:
+            ext_c = torch.cat([st.conv[slots], st.pconv[prev, slots]], 1)             # [S, pad + max_q, C]
+            idx = (nc[:, None] + torch.arange(pad, device=dev))[..., None].expand(S, pad, ext_c.shape[2])
+            st.conv[slots] = torch.gather(ext_c, 1, idx)
+    hl = st.hist_len[slots]
+    toks = tokens.view(S, W).long()
+    ext = torch.cat([st.hist[slots], toks], 1)                                           # [S, n1 + W]
+    base = torch.arange(S, device=dev)[:, None] * (n1 + W)
+    pos = (base + n1 + torch.arange(W, device=dev)[None]).reshape(-1)
+    seg = (base + n1 - hl[:, None]).expand(S, W).reshape(-1)
+    e = w.table.lookup(ext.reshape(-1).int(), pos, seg)                                  # [N, E] bf16
+    c = _C()
+    G, H = w.G, w.H
+    k = _group_rms(c.gemm(e, w.key_proj), w.norm_key, G, w.eps).view(N, G, H)
+    q = _group_rms(stream.reshape(N, G * H), w.norm_query, G, w.eps).view(N, G, H)
+    g = (k * q).sum(-1, keepdim=True) / math.sqrt(H)
+    g = g.abs().clamp_min(1e-6).sqrt() * g.sign()
+    v = torch.sigmoid(g) * c.gemm(e, w.value_proj).float()[:, None, :]                 # [N, G, H]
+    cin = _group_rms(v.reshape(N, G * H), w.norm_conv, G, w.eps).view(S, W, G * H)
+    ext_c = torch.cat([st.conv[slots], cin], 1) if pad else cin                        # [S, pad + W, C]
+    out = torch.zeros_like(cin)
+    for j in range(w.k):
+        back = (w.k - 1 - j) * w.dil
+        out += ext_c[:, pad - back: pad - back + W] * w.conv[:, j]
+    stream += (v + out.view(N, G, H)).to(stream.dtype)
+    if commit_current:  # prefill: every row is final
+        both = torch.cat([st.hist[slots], toks], 1)
+        st.hist[slots] = both[:, -n1:]
+        st.hist_len[slots] = torch.clamp(hl + W, max=n1)
+        if pad:
+            st.conv[slots] = ext_c[:, -pad:]
+    else:
+        st.ptok[parity, slots, :W] = toks
+        st.pconv[parity, slots, :W] = cin

@@ -68,6 +68,7 @@ class SpecEngine:
         self.alloc = C().PageAllocator(num_pages - 1, PAGE)
         self.kv = model.new_kv_cache(num_pages)
         self.gdn = model.new_gdn_states(S, W)
+        self.ple = model.new_ple_states(S, W) if model.cfg.ple_layer_ids else None
         i32 = dict(dtype=torch.int32, device=dev)
         self.block_table = torch.full((S, self.maxp), self.scratch_page, **i32)
         self.bt_host = torch.full((S, self.maxp), self.scratch_page, dtype=torch.int32).pin_memory()
@@ -137,7 +138,7 @@ class SpecEngine:
                         self.win_pos, self.win_slots, self.attn_len, self.step_ctr, W, 0)
         b = StepBatch(self.win_ids, self.win_pos, self.win_slots, self.block_table, self.attn_len, self.seq_slot,
                       self.n_commit, W, parity, max_pages=self.maxp)
-        hidden = m.forward(b, self.kv, self.gdn, self.ws, qsa=self.qsa)
+        hidden = m.forward(b, self.kv, self.gdn, self.ws, qsa=self.qsa, ple=self.ple)
         logits = self.logits[: S * W]
         m.logits(hidden, out=logits)
         cC.select_tokens(logits, m.cfg.vocab_size, self.tgt_tok, float(self.scfg.temperature), self.scfg.seed,
@@ -231,6 +232,8 @@ class SpecEngine:
         for st in self.gdn:  # fresh recurrent state for this row
             st.conv[sess.row].zero_()
             st.ssm[sess.row].zero_()
+        for st in self.ple or ():
+            st.reset(sess.row)
         hidden_last = None
         for c0 in range(0, L, PREFILL_CHUNK):
             T = min(PREFILL_CHUNK, L - c0)
@@ -242,7 +245,7 @@ class SpecEngine:
                           self.n_commit, T, 0, commit_current=True, max_pages=self.maxp,
                           attn_bt_row=torch.full((nv,), sess.row, dtype=torch.int32, device=dev),
                           attn_seq_lens=vlen, attn_q_per_seq=8)
-            hidden = m.forward(b, self.kv, self.gdn, self.ws, self.gdn_scratch, qsa=self.qsa)
+            hidden = m.forward(b, self.kv, self.gdn, self.ws, self.gdn_scratch, qsa=self.qsa, ple=self.ple)
             if on_chunk is not None:
                 on_chunk(hidden[:T], c0)
             if self.drafter is not None:

@@ -19,6 +19,9 @@ def _models(seed=0, **over):
     ref = build_reference(cfg, seed=seed)
     with torch.no_grad():
         ref.lm_head.weight.mul_(40.0)  # peaky logits: argmax far from ties
+        for L in ref.layers:
+            if L.ple is not None:
+                L.ple.table.mul_(50.0)  # a PLE layer that visibly moves the stream
         qs = []
         for moe in ref.moe_layers():  # INT3 experts in both models
             c13, s13 = rtn_quantize(moe.w13.float())
@@ -267,3 +270,32 @@ def test_converted_drafter_directory_serves(tmp_path):
     torch.cuda.synchronize()
     check_status()
     assert out_plain == out_spec
+
+
+def test_ple_model_speculative_decoding_commits_side_state(tmp_path):
+    """A model with a PLE layer: greedy speculative decoding (partial acceptance: the n-gram history and conv inputs
+    of rejected rows must not be committed) equals plain greedy decoding; the first token follows the reference; a
+    deploy package carries the PLE layer."""
+    from arc_forge_2026_b200.formats.int3_package import package_tensors, write_package
+    from arc_forge_2026_b200.quant.int3_tiles import tiles_to_codes, tiles_to_scales
+    cfg, ref, model = _models(8, ple_layer_ids=(1,), ngram_vocab_size_base=4001, ple_embed_dim=256)
+    assert model.layers[1].ple is not None
+    g = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (70, 21, 5)]
+    prompts[0][30] = cfg.eos_token_id
+    plain = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy"), 3, 1024).generate(prompts, 30)
+    drafter = Drafter(drafter_preset("tiny"), cfg.hidden_size, cfg.vocab_size, dev, draft_vocab=4096)
+    spec_eng = SpecEngine(model, drafter, ServeConfig(spec_k=4, accept_mode="greedy"), 3, 1024)
+    spec = spec_eng.generate(prompts, 30)
+    torch.cuda.synchronize()
+    check_status()
+    assert plain == spec
+    with torch.no_grad():
+        for p, out in zip(prompts, plain):
+            assert out[0] in ref(torch.tensor([p]))[0, -1].topk(3).indices.tolist()
+    cs = [(tiles_to_codes(lw.bank.w13_codes.cpu()), tiles_to_scales(lw.bank.w13_scales.cpu()),
+           tiles_to_codes(lw.bank.w2_codes.cpu()), tiles_to_scales(lw.bank.w2_scales.cpu())) for lw in model.layers]
+    d = write_package(package_tensors(ref, cs, dense_fp8=False), cfg, tmp_path / "pkg", dense_fp8=False)
+    loaded = HybridModel.from_package(d, dev)
+    again = SpecEngine(loaded, None, ServeConfig(spec_k=0, accept_mode="greedy"), 3, 1024).generate(prompts, 30)
+    assert again == plain

@@ -174,3 +174,67 @@ def test_row_sharded_table_over_gloo_ranks(tmp_path):
     mp.spawn(_shard_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         assert torch.load(tmp_path / f"r{r}.pt")["err"] < 1e-6
+
+
+def test_serving_side_state_commit_matches_the_reference(monkeypatch):
+    """``ops.ple.ple_serve`` (prefill, then verify windows with partial acceptance and the deferred commit) gives
+    every accepted row the reference layer's update; the native GEMM and lookup are replaced by torch here."""
+    import arc_forge_2026_b200.ops as ops_pkg
+    from arc_forge_2026_b200.ops import ple as OP
+
+    class FakeC:
+        @staticmethod
+        def gemm(a, b):
+            return (a.float() @ b.float().t()).to(torch.bfloat16)
+
+    def fake_lookup(self, ext, pos, seg, ids_out=None):
+        rows = []
+        for p, s in zip(pos.tolist(), seg.tolist()):
+            rows.append(self.hash.ids(ext[s:p + 1].long())[-1])
+        ids = torch.stack(rows)
+        return self.dense_rows()[ids].flatten(-2).to(torch.bfloat16)
+    monkeypatch.setattr(ops_pkg, "C", lambda: FakeC())
+    monkeypatch.setattr(OP.PleTable, "lookup", fake_lookup)
+    cfg = _cfg(hc_count=2, hc_lowrank=32, ple_conv_dilation=1)
+    ref = build_reference(cfg, seed=5)
+    mod = ref.layers[1].ple
+    with torch.no_grad():
+        mod.table.mul_(20.0)
+    w = OP.PleServeWeights.from_module(mod, "cpu", fp8=False)
+    W, slots = 3, 2
+    st = OP.PleServeState(w, slots, W, "cpu")
+    g = torch.Generator().manual_seed(6)
+    T = 40
+    toks = torch.randint(0, cfg.vocab_size, (T,), generator=g)
+    toks[17] = cfg.eos_token_id
+    stream = torch.randn(T, 2, cfg.hidden_size, generator=g).bfloat16()
+    with torch.no_grad():
+        want = mod(stream.float(), toks)                        # [T, G, H] update of every position
+    got = torch.zeros(T, 2, cfg.hidden_size)
+    slot = torch.tensor([1])
+    n_commit = torch.zeros(slots, dtype=torch.int32)
+    # prefill 11 tokens
+    x = stream[:11].float()
+    OP.ple_serve(x, toks[:11].int(), w, st, slot, n_commit, 11, 0, True)
+    got[:11] = (x.float() - stream[:11].float())
+    pos, parity = 11, 0
+    while pos + W <= T:
+        x = stream[pos:pos + W].float()
+        OP.ple_serve(x, toks[pos:pos + W].int(), w, st, slot, n_commit, W, parity, False)
+        acc = int(torch.randint(1, W + 1, (1,), generator=g))  # rows accepted this cycle, committed by the next
+        got[pos:pos + acc] = (x.float() - stream[pos:pos + W].float())[:acc]
+        n_commit[1] = acc
+        pos += acc
+        parity ^= 1
+    rel = ((got[:pos] - want[:pos]).norm() / want[:pos].norm()).item()
+    assert rel < 1e-2, rel
+    # committing every row of a window (instead of the accepted ones) breaks the history: the check sees it
+    st2 = OP.PleServeState(w, slots, W, "cpu")
+    x = stream[:11].float()
+    OP.ple_serve(x, toks[:11].int(), w, st2, slot, torch.zeros(slots, dtype=torch.int32), 11, 0, True)
+    x = stream[11:14].float()
+    OP.ple_serve(x, torch.tensor([5, 6, 7], dtype=torch.int32), w, st2, slot, n_commit, W, 0, False)
+    x = stream[11:14].float()
+    OP.ple_serve(x, toks[11:14].int(), w, st2, slot, torch.tensor([0, 3], dtype=torch.int32), W, 1, False)
+    bad = (x - stream[11:14].float())
+    assert ((bad - want[11:14]).norm() / want[11:14].norm()).item() > 5e-2
