@@ -19,6 +19,7 @@ row; GDN in commit-all mode) and injects the prompt tail into the drafter cache.
 from __future__ import annotations
 
 import math
+import time
 from dataclasses import dataclass, field
 
 import torch
@@ -41,6 +42,21 @@ class Session:
     max_new_tokens: int
     generated: list[int] = field(default_factory=list)
     done: bool = False
+    emitted: list[int] = field(default_factory=list)  # every token the target emitted (generated is capped)
+    last_used: float = 0.0
+
+
+@dataclass
+class Parked:
+    """An idle session whose slot was given away: its committed recurrent state in pinned host memory (GDN conv and
+    SSM rows, PLE history and conv rows, the drafter's ring pages, the QSA finalisation mark). Its KV pages stay
+    allocated on the device."""
+    sess: Session
+    committed: int
+    gdn: list
+    ple: list
+    dkv: list
+    qsa_fin: int | None
 
 
 class SpecEngine:
@@ -93,6 +109,8 @@ class SpecEngine:
         self.parity = 0
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.sessions: dict[int, Session] = {}
+        self.parked: dict[int, Parked] = {}
+        self.prefilled_tokens = 0  # tokens run through prefill (continuations prefill only their new tokens)
         self.free_rows = list(range(S))
         self.out_host = torch.zeros(S, W, dtype=torch.int32).pin_memory()
         self.cnt_host = torch.zeros(S, dtype=torch.int32).pin_memory()
@@ -192,9 +210,116 @@ class SpecEngine:
                 self.bt_host[s.row, n:] = self.scratch_page
         self.block_table.copy_(self.bt_host, non_blocking=True)
 
-    def add_session(self, sid: int, prompt: list[int], max_new_tokens: int, on_chunk=None):
-        if not self.free_rows:
+    # ------------------------------------------------------------------ session continuation and parking
+    @property
+    def free_slots(self) -> int:
+        """Rows a new session can take now: free rows plus idle sessions that can be parked to make room."""
+        return len(self.free_rows) + (0 if self.hs is not None else len(self._idle()))
+
+    def has_session(self, sid: int) -> bool:
+        return sid in self.sessions or sid in self.parked
+
+    def _idle(self):
+        return [s for s in self.sessions.values() if s.done]
+
+    def _make_room(self):
+        if self.free_rows:
+            return
+        idle = self._idle() if self.hs is None else []
+        if not idle:
             raise RuntimeError("no free session slot")
+        self.park(min(idle, key=lambda s: s.last_used).sid)
+
+    def _committed(self, r: int) -> int:
+        """Tokens of row r whose recurrent state is committed (the last cycle's accepted rows are still pending)."""
+        return int(self.ctx_len[r]) - int(self.n_commit[r])
+
+    @torch.no_grad()
+    def park(self, sid: int):
+        """Move an idle session's committed state to pinned host memory and free its row (the reference parks one
+        GDN snapshot per idle session in host memory; its KV stays where it is)."""
+        sess = self.sessions[sid]
+        if not sess.done:
+            raise RuntimeError(f"session {sid} is decoding; only idle sessions park")
+        if self.hs is not None:
+            raise NotImplementedError("parking with the HiSparse host pool")
+        r = sess.row
+        torch.cuda.synchronize(self.device)
+
+        def host(t):
+            return torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t)
+        gdn = [(host(st.conv[r]), host(st.ssm[r])) for st in self.gdn]
+        ple = [(host(st.hist[r]), host(st.hist_len[r]), host(st.conv[r])) for st in (self.ple or ())]
+        dkv = []
+        if self.drafter is not None:
+            pages = slice(r * self.ring, (r + 1) * self.ring)
+            dkv = [(host(k[pages]), host(v[pages])) for k, v in self.dkv]
+        fin = int(self.qsa.fin[r]) if self.qsa is not None else None
+        self.parked[sid] = Parked(sess, self._committed(r), gdn, ple, dkv, fin)
+        del self.sessions[sid]
+        self.active[r] = 0
+        self.n_commit[r] = 0
+        self.bt_host[r] = self.scratch_page
+        self.block_table[r].copy_(self.bt_host[r])
+        sess.row = -1
+        self.free_rows.append(r)
+
+    @torch.no_grad()
+    def _unpark(self, sid: int) -> Session:
+        self._make_room()
+        pk = self.parked.pop(sid)
+        sess = pk.sess
+        r = sess.row = self.free_rows.pop(0)
+        for st, (conv, ssm) in zip(self.gdn, pk.gdn):
+            st.conv[r].copy_(conv)
+            st.ssm[r].copy_(ssm)
+        for st, (hist, hl, conv) in zip(self.ple or (), pk.ple):
+            st.hist[r].copy_(hist)
+            st.hist_len[r].copy_(hl)
+            st.conv[r].copy_(conv)
+        if pk.dkv:
+            pages = slice(r * self.ring, (r + 1) * self.ring)
+            for (k, v), (hk, hv) in zip(self.dkv, pk.dkv):
+                k[pages].copy_(hk)
+                v[pages].copy_(hv)
+        if pk.qsa_fin is not None:
+            self.qsa.fin[r] = pk.qsa_fin
+        self.ctx_len[r] = pk.committed
+        self.n_commit[r] = 0
+        self.sessions[sid] = sess
+        self._sync_pages([r])
+        return sess
+
+    @torch.no_grad()
+    def continue_session(self, sid: int, tokens: list[int], max_new_tokens: int, on_chunk=None) -> Session:
+        """Next turn of an idle (or parked) session: ``tokens`` is its whole transcript so far plus the new input.
+        Only the part after the committed state is prefilled; a transcript that differs from what the engine
+        committed (or the HiSparse pool) falls back to prefilling it all."""
+        if len(tokens) + max_new_tokens + 2 * self.W > self.max_context:
+            raise ValueError("prompt + max_new_tokens exceed max_context")
+        if sid in self.parked:
+            self._unpark(sid)
+        sess = self.sessions[sid]
+        if not sess.done:
+            raise RuntimeError(f"session {sid} is still decoding")
+        r = sess.row
+        torch.cuda.synchronize(self.device)
+        committed = self._committed(r)
+        known = (sess.prompt + sess.emitted)[:committed]
+        if self.hs is not None or len(tokens) <= committed or list(tokens[:committed]) != known:
+            self.release(sid)
+            return self.add_session(sid, list(tokens), max_new_tokens, on_chunk)
+        sess.prompt, sess.generated, sess.emitted = list(tokens), [], []
+        sess.max_new_tokens, sess.done = max_new_tokens, False
+        self.alloc.ensure(sid, len(tokens) + 2 * self.W + 8)
+        self._sync_pages([r])
+        self.ctx_len[r] = committed
+        self.n_commit[r] = 0  # the last window's accepted rows are prefilled again below
+        self._prefill(sess, on_chunk, start=committed)
+        return sess
+
+    def add_session(self, sid: int, prompt: list[int], max_new_tokens: int, on_chunk=None):
+        self._make_room()
         if len(prompt) + max_new_tokens + 2 * self.W > self.max_context:
             raise ValueError("prompt + max_new_tokens exceed max_context")
         row = self.free_rows.pop(0)
@@ -218,7 +343,8 @@ class SpecEngine:
         self.release(sess.sid)
 
     @torch.no_grad()
-    def _prefill(self, sess: Session, on_chunk=None):
+    def _prefill(self, sess: Session, on_chunk=None, start: int = 0):
+        """Prefill ``sess.prompt[start:]`` (``start`` > 0: the recurrent state holds the first ``start`` tokens)."""
         cC, m = C(), self.model
         if m.ep is not None and m.ep.world > 1:
             raise NotImplementedError("prefill under expert parallelism needs every rank in the same forward; "
@@ -229,13 +355,15 @@ class SpecEngine:
         pages = (self.block_table[sess.row].long() if self.hs is not None else
                  torch.tensor(self.alloc.pages(sess.sid), dtype=torch.int64, device=dev))
         slot_row = torch.tensor([sess.row], dtype=torch.int32, device=dev)
-        for st in self.gdn:  # fresh recurrent state for this row
-            st.conv[sess.row].zero_()
-            st.ssm[sess.row].zero_()
-        for st in self.ple or ():
-            st.reset(sess.row)
+        if start == 0:
+            for st in self.gdn:  # fresh recurrent state for this row
+                st.conv[sess.row].zero_()
+                st.ssm[sess.row].zero_()
+            for st in self.ple or ():
+                st.reset(sess.row)
         hidden_last = None
-        for c0 in range(0, L, PREFILL_CHUNK):
+        self.prefilled_tokens += L - start
+        for c0 in range(start, L, PREFILL_CHUNK):
             T = min(PREFILL_CHUNK, L - c0)
             pos = torch.arange(c0, c0 + T, device=dev, dtype=torch.int32)
             slots = (pages[pos.long() // PAGE] * PAGE + (pos.long() % PAGE)).int()
@@ -277,6 +405,7 @@ class SpecEngine:
         if self.drafter is not None:  # first drafts: propose from the prefill's last hidden state
             self.drafts[r].fill_(0)
         sess.generated.append(int(tok.item()))
+        sess.emitted.append(sess.generated[-1])
 
     def update_weights(self, pkg_dir) -> dict:
         """Swap in the weights of a deploy package between steps (in place: the captured graphs stay valid)."""
@@ -284,6 +413,11 @@ class SpecEngine:
         return self.model.update_from_package(pkg_dir)
 
     def release(self, sid: int):
+        if sid in self.parked:  # its KV pages only
+            self.parked.pop(sid)
+            if self.hs is None:
+                self.alloc.release(sid)
+            return
         sess = self.sessions.pop(sid)
         self.active[sess.row] = 0
         if self.hs is None:
@@ -308,11 +442,19 @@ class SpecEngine:
             n = int(self.cnt_host[s.row])
             toks = self.out_host[s.row, :n].tolist()
             room = s.max_new_tokens - len(s.generated)
+            if not s.done and n > room:
+                # the turn ends inside this window: commit only the rows of the delivered tokens, so the state
+                # matches the transcript a later turn continues (the other accepted rows are dropped)
+                self.ctx_len[s.row] -= n - room
+                self.n_commit[s.row] -= n - room
             toks = toks[:room]
+            if not s.done:
+                s.emitted.extend(toks)
             s.generated.extend(toks)
             emitted[s.sid] = toks
-            if len(s.generated) >= s.max_new_tokens:
+            if len(s.generated) >= s.max_new_tokens and not s.done:
                 s.done = True
+                s.last_used = time.monotonic()
                 self.active[s.row] = 0
         return emitted
 

@@ -116,7 +116,9 @@ class EngineLoop:
             seg = self.ledger_segs.pop(key, None)
             if seg is not None:
                 self.ledger.close_segment(seg)
-            if sid is not None and sid not in self.live and sid in self.engine.sessions:
+            has = (self.engine.has_session(sid) if hasattr(self.engine, "has_session")
+                   else sid in self.engine.sessions)
+            if sid is not None and sid not in self.live and has:
                 self.engine.release(sid)
             return sid is not None
 
@@ -136,7 +138,10 @@ class EngineLoop:
         try:
             if key is not None and key in self.keyed:
                 sid = self.keyed[key]
-                if hasattr(eng, "extend_session") and sid in eng.sessions:
+                if hasattr(eng, "continue_session") and eng.has_session(sid):
+                    # only the tokens after the committed state are prefilled (a parked session is restored first)
+                    sess = eng.continue_session(sid, self.transcripts[key] + (req.extend or []), req.max_new)
+                elif hasattr(eng, "extend_session") and sid in eng.sessions:
                     sess = eng.extend_session(sid, req.extend or [], req.max_new)
                 else:  # engine without continuation: re-prefill the whole transcript
                     if sid in eng.sessions:
@@ -202,6 +207,7 @@ class EngineLoop:
             if s is not None:
                 self.transcripts[req.session_key] = list(s.prompt) + list(s.generated)
                 s.done = True
+                s.last_used = time.monotonic()
                 if hasattr(s, "row") and hasattr(eng, "active"):
                     eng.active[s.row] = 0  # keep the session's pages, stop decoding it
         self._emit(req, ("done", reason))
@@ -231,10 +237,12 @@ class EngineLoop:
                 while self.pending:
                     req = self.pending[0]
                     reuse = req.session_key is not None and req.session_key in self.keyed
-                    if not reuse and free <= 0:
+                    # a keyed session keeps its row between turns unless it was parked
+                    held = reuse and self.keyed[req.session_key] in getattr(self.engine, "sessions", {})
+                    if not held and free <= 0:
                         break
                     admit.append(self.pending.popleft())
-                    free -= 0 if reuse else 1
+                    free -= 1  # a new / parked session takes a row; a held idle one stops counting as parkable
             for req in admit:
                 self._admit(req)
             if self.live:

@@ -299,3 +299,49 @@ def test_ple_model_speculative_decoding_commits_side_state(tmp_path):
     loaded = HybridModel.from_package(d, dev)
     again = SpecEngine(loaded, None, ServeConfig(spec_k=0, accept_mode="greedy"), 3, 1024).generate(prompts, 30)
     assert again == plain
+
+
+def test_session_continuation_and_parking_match_fresh_prefill():
+    """Multi-turn sessions on 2 rows: a turn continues from the committed GDN / PLE state (only new tokens are
+    prefilled); a third session parks the least recently used idle one (its state to pinned host memory, its row
+    freed) and the parked session later resumes from the snapshot. Greedy outputs equal fresh sessions prefilling
+    the whole transcript."""
+    cfg, ref, model = _models(9, ple_layer_ids=(1,), ngram_vocab_size_base=4001, ple_embed_dim=256)
+    drafter = Drafter(drafter_preset("tiny"), cfg.hidden_size, cfg.vocab_size, dev, draft_vocab=4096)
+    scfg = ServeConfig(spec_k=4, accept_mode="greedy")
+    eng = SpecEngine(model, drafter, scfg, 2, 1024)
+    g = torch.Generator().manual_seed(9)
+
+    def rnd(n):
+        return torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist()
+
+    def run(sess_id, tokens, n, cont):
+        s = eng.continue_session(sess_id, tokens, n) if cont else eng.add_session(sess_id, tokens, n)
+        while not s.done:
+            eng.step()
+        return list(s.prompt) + s.generated[:n]
+
+    def fresh(tokens, n):
+        e = SpecEngine(model, drafter, scfg, 1, 1024)
+        return tokens + e.generate([tokens], n)[0]
+
+    ta = run(1, rnd(60), 12, False)
+    tb = run(2, rnd(45), 9, False)
+    assert eng.free_slots == 2 and not eng.free_rows
+    ta2 = ta + rnd(7)
+    before = eng.prefilled_tokens
+    assert run(1, ta2, 10, True) == fresh(ta2, 10)          # continuation in place
+    assert eng.prefilled_tokens - before <= 7 + eng.W       # the new tokens and the uncommitted tail only
+    tc = run(3, rnd(33), 8, False)                           # parks session 2 (the least recently used)
+    assert 2 in eng.parked and 3 in eng.sessions
+    tb2 = tb + rnd(5)
+    before = eng.prefilled_tokens
+    got = run(2, tb2, 11, True)                              # restores 2, parks 1
+    assert 1 in eng.parked and got == fresh(tb2, 11)
+    assert eng.prefilled_tokens - before <= 5 + eng.W
+    assert tc == fresh(tc[:33], 8)
+    for sid in (1, 2, 3):
+        eng.release(sid)
+    assert not eng.parked and len(eng.free_rows) == 2
+    torch.cuda.synchronize()
+    check_status()
