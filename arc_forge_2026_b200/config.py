@@ -175,7 +175,7 @@ class ServeConfig:
     max_sessions: int = 128
     page_size: int = 64
     max_context: int = 32768
-    kv_dtype: str = "bf16"  # the paged KV cache holds bf16 (the only format the attention kernels read)
+    kv_dtype: str = "bf16"  # target KV cache: bf16 | nvfp4 (e2m1 + e4m3 per 16 elements: 3.6x the tokens per byte)
     gdn_state_dtype: str = "fp32"
     spec_k: int = 4  # 0 disables speculative decoding
     accept_mode: str = "rejection"  # rejection | greedy | bernoulli

@@ -9,7 +9,16 @@
 // Causality inside the verify window: position t sees keys < past_len + t + 1.
 // With one split the output is written directly as bf16 * sigmoid(gate); with several, each split writes
 // (O, log-sum-exp) partials and attn_merge_kernel combines them in split order (deterministic).
+//
+// NVFP4 KV (FP4 = true): a page-head holds 64 x D/2 bytes of e2m1 pairs and 64 x D/16 e4m3 scales (one per 16
+// elements), both contiguous, so each arrives by one 1-D bulk copy per tensor into a 2-deep ring (3.6x fewer bytes
+// than bf16). All 256 threads dequantise a landed page into the same swizzled bf16 tiles the MMA path reads
+// (e2m1 x e4m3 has at most 5 significant bits, so the bf16 tile holds the dequantised values exactly); block-wide
+// barriers order the dequantisation against the previous page's MMAs, and the stage is refilled right after it.
 #include <cudaTypedefs.h>
+#include <cuda_fp4.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -41,11 +50,63 @@ struct AttnSmem {
   static constexpr uint32_t TOTAL = SBT_OFF + SBT * 4 + 1024;
 };
 
+// NVFP4 layout: 2 stages of packed K, packed V, K scales, V scales, then one bf16 K + V tile pair (the MMA operands)
 template <int D>
+struct AttnSmemFp4 {
+  static constexpr uint32_t PK = attn::PAGE * D / 2;           // e2m1 bytes of one page-head
+  static constexpr uint32_t PS = attn::PAGE * D / 16;          // e4m3 scale bytes of one page-head
+  static constexpr uint32_t KV_BYTES = attn::PAGE * D * 2;     // one dequantised bf16 tile
+  static constexpr uint32_t STAGE = 2 * PK + 2 * PS;
+  static constexpr uint32_t BF_OFF = 2 * STAGE;
+  static constexpr uint32_t Q_BYTES = 64 * D * 2;
+  static constexpr uint32_t Q_OFF = BF_OFF + 2 * KV_BYTES;
+  static constexpr uint32_t BAR_OFF = Q_OFF + Q_BYTES;
+  static constexpr int SBT = 1024;
+  static constexpr uint32_t SBT_OFF = BAR_OFF + 64;
+  static constexpr uint32_t TOTAL = SBT_OFF + SBT * 4 + 1024;
+  static_assert(BF_OFF % 1024 == 0 && Q_OFF % 1024 == 0, "swizzled tiles need 1 KB alignment");
+  static_assert(BF_OFF >= 4 * 16 * D * 4 + 64 * 2 * 4 || Q_OFF >= 4 * 16 * D * 4 + 64 * 2 * 4,
+                "the half-merge scratch must fit below Q");
+};
+
+// one landed NVFP4 page-head pair (packed + scales at `st`) -> swizzled bf16 K and V tiles at `bf`
+template <int D>
+AFB_DEV void dequant_fp4_page(const uint8_t* st, uint8_t* bf) {
+  using S = AttnSmemFp4<D>;
+  constexpr int PC = D / 32;  // 16-byte packed chunks per row (32 elements, 2 scales)
+  for (int q = threadIdx.x; q < 2 * attn::PAGE * PC; q += blockDim.x) {
+    const int m = q / (attn::PAGE * PC), rq = q % (attn::PAGE * PC);
+    const int row = rq / PC, pc = rq % PC;
+    const uint8_t* pk = st + m * S::PK + row * (D / 2) + pc * 16;
+    const uint8_t* sc = st + 2 * S::PK + m * S::PS + row * (D / 16) + pc * 2;
+    const uint4 v = *reinterpret_cast<const uint4*>(pk);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+    uint8_t* dst = bf + m * S::KV_BYTES;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {  // 16 elements share one scale
+      const __half_raw sh = __nv_cvt_fp8_to_halfraw(sc[half], __NV_E4M3);
+      const float s = __half2float(__half(sh));
+#pragma unroll
+      for (int c8 = 0; c8 < 2; ++c8) {  // two 8-element bf16 chunks
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __half2_raw h2 = __nv_cvt_fp4x2_to_halfraw2(b[half * 8 + c8 * 4 + j], __NV_E2M1);
+          const float2 f = __half22float2(__half2(h2));
+          w[j] = pack_bf16x2(f.x * s, f.y * s);
+        }
+        const int cc = pc * 4 + half * 2 + c8;
+        *reinterpret_cast<uint4*>(dst + sw_off<attn::PAGE>(row, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
+template <int D, bool FP4>
 __global__ void __launch_bounds__(256, 1)
     paged_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       AttnArgs a, uint32_t* status) {
-  using S = AttnSmem<D>;
+  using S = typename std::conditional<FP4, AttnSmemFp4<D>, AttnSmem<D>>::type;
   constexpr int NT_O = D / 8;  // output n-tiles per row tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -99,17 +160,28 @@ __global__ void __launch_bounds__(256, 1)
     const int page = i < S::SBT ? sbt[i] : bt[p0 + i];
     const int row = (page * a.Hkv + kvh) * attn::PAGE;
     uint8_t* st = smem + s * S::STAGE;
-    mbar_arrive_expect_tx(&full[s], 2 * S::KV_BYTES);
+    if constexpr (FP4) {  // contiguous page-heads: one plain bulk copy per tensor (no tensor map)
+      const size_t ph = (size_t)page * a.Hkv + kvh;
+      mbar_arrive_expect_tx(&full[s], S::STAGE);
+      bulk_load_1d(st, reinterpret_cast<const uint8_t*>(a.kcache) + ph * S::PK, S::PK, &full[s]);
+      bulk_load_1d(st + S::PK, reinterpret_cast<const uint8_t*>(a.vcache) + ph * S::PK, S::PK, &full[s]);
+      bulk_load_1d(st + 2 * S::PK, a.kscale + ph * S::PS, S::PS, &full[s]);
+      bulk_load_1d(st + 2 * S::PK + S::PS, a.vscale + ph * S::PS, S::PS, &full[s]);
+    } else {
+      mbar_arrive_expect_tx(&full[s], 2 * S::KV_BYTES);
 #pragma unroll
-    for (int c = 0; c < D / 64; ++c) {
-      tma_load_2d(st + c * attn::PAGE * 128, &tmK, &full[s], c * 64, row);
-      tma_load_2d(st + S::KV_BYTES + c * attn::PAGE * 128, &tmV, &full[s], c * 64, row);
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(st + c * attn::PAGE * 128, &tmK, &full[s], c * 64, row);
+        tma_load_2d(st + S::KV_BYTES + c * attn::PAGE * 128, &tmV, &full[s], c * 64, row);
+      }
     }
   };
   int issued = 0;  // meaningful in thread 0 only
   if (threadIdx.x == 0) {
-    prefetch_tmap(&tmK);
-    prefetch_tmap(&tmV);
+    if constexpr (!FP4) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+    }
     for (int i = 0; i < min(2, n); ++i) issue(i);
     issued = min(2, n);
   }
@@ -127,11 +199,29 @@ __global__ void __launch_bounds__(256, 1)
 
   for (int i = 0; i < n && ok; ++i) {
     const int s = i & 1;
-    if (!mbar_wait(&full[s], (i >> 1) & 1, status)) {
-      ok = false;
-      break;
+    uint32_t k_base;
+    if constexpr (FP4) {
+      // every thread waits (bounded), then one block-wide vote keeps the exit uniform; the barrier also orders the
+      // previous page's MMA reads of the bf16 tiles before they are overwritten
+      const bool landed = mbar_wait(&full[s], (i >> 1) & 1, status);
+      if (!__syncthreads_and(landed)) {
+        ok = false;
+        break;
+      }
+      dequant_fp4_page<D>(smem + s * S::STAGE, smem + S::BF_OFF);
+      __syncthreads();
+      if (threadIdx.x == 0 && i + 2 < n) {  // the stage is consumed: refill it now
+        issue(i + 2);
+        ++issued;
+      }
+      k_base = smem_u32(smem + S::BF_OFF);
+    } else {
+      if (!mbar_wait(&full[s], (i >> 1) & 1, status)) {
+        ok = false;
+        break;
+      }
+      k_base = smem_u32(smem + s * S::STAGE);
     }
-    const uint32_t k_base = smem_u32(smem + s * S::STAGE);
     const uint32_t v_base = k_base + S::KV_BYTES;
     if (active) {
       // ---- S = Q K^T for 32 keys (4 n-tiles of 8)
@@ -221,14 +311,16 @@ __global__ void __launch_bounds__(256, 1)
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if (threadIdx.x == 0 && i + 2 < n) {
-      if (!mbar_wait(&empty[s], (i >> 1) & 1, status)) {
-        ok = false;
-      } else {
-        issue(i + 2);
-        ++issued;
+    if constexpr (!FP4) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (threadIdx.x == 0 && i + 2 < n) {
+        if (!mbar_wait(&empty[s], (i >> 1) & 1, status)) {
+          ok = false;
+        } else {
+          issue(i + 2);
+          ++issued;
+        }
       }
     }
   }
@@ -338,22 +430,29 @@ __global__ void attn_merge_kernel(AttnArgs a, int splits) {
   }
 }
 
-template <int D>
+template <int D, bool FP4>
 static int launch_attn(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st) {
-  using S = AttnSmem<D>;
-  CUtensorMap tk, tv;
-  const uint64_t rows = (uint64_t)a.num_pages * a.Hkv * attn::PAGE;
-  int rc = make_tmap_2d(&tk, a.kcache, 2, D, rows, (uint64_t)D * 2, 64, attn::PAGE, 1);
-  if (rc) return 1000 + rc;
-  rc = make_tmap_2d(&tv, a.vcache, 2, D, rows, (uint64_t)D * 2, 64, attn::PAGE, 1);
-  if (rc) return 1000 + rc;
+  using S = typename std::conditional<FP4, AttnSmemFp4<D>, AttnSmem<D>>::type;
+  CUtensorMap tk{}, tv{};
+  int rc;
+  if (!FP4) {
+    const uint64_t rows = (uint64_t)a.num_pages * a.Hkv * attn::PAGE;
+    rc = make_tmap_2d(&tk, a.kcache, 2, D, rows, (uint64_t)D * 2, 64, attn::PAGE, 1);
+    if (rc) return 1000 + rc;
+    rc = make_tmap_2d(&tv, a.vcache, 2, D, rows, (uint64_t)D * 2, 64, attn::PAGE, 1);
+    if (rc) return 1000 + rc;
+  } else if (!a.kscale || !a.vscale || (reinterpret_cast<uintptr_t>(a.kcache) | reinterpret_cast<uintptr_t>(a.vcache) |
+                                         reinterpret_cast<uintptr_t>(a.kscale) |
+                                         reinterpret_cast<uintptr_t>(a.vscale)) % 16) {
+    return 5;  // bulk copies need 16-byte aligned sources
+  }
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(paged_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+    cudaFuncSetAttribute(paged_attn_kernel<D, FP4>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
     attr = true;
   }
   dim3 grid(a.num_seqs * a.Hkv, splits);
-  paged_attn_kernel<D><<<grid, 256, S::TOTAL, st>>>(tk, tv, a, status);
+  paged_attn_kernel<D, FP4><<<grid, 256, S::TOTAL, st>>>(tk, tv, a, status);
   rc = (int)cudaGetLastError();
   if (rc || splits == 1) return rc;
   attn_merge_kernel<D><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
@@ -364,8 +463,9 @@ int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_
   if (a.q_per_seq * (a.Hq / a.Hkv) > 64) return 3;
   if (splits > 1 && (!a.part_o || !a.part_lse)) return 4;
   if (a.num_seqs == 0) return 0;
-  if (a.D == 256) return launch_attn<256>(a, splits, status, st);
-  if (a.D == 128) return launch_attn<128>(a, splits, status, st);
+  const bool fp4 = a.kscale != nullptr;
+  if (a.D == 256) return fp4 ? launch_attn<256, true>(a, splits, status, st) : launch_attn<256, false>(a, splits, status, st);
+  if (a.D == 128) return fp4 ? launch_attn<128, true>(a, splits, status, st) : launch_attn<128, false>(a, splits, status, st);
   return 3;
 }
 

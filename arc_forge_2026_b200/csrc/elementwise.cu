@@ -3,6 +3,8 @@
 // expert GEMMs, SwiGLU, the top-k combine with the shared expert, and the embedding gather.
 // Each is one pass over HBM with vectorised 16-byte accesses; reductions are per warp in a fixed order,
 // so results are bitwise reproducible run to run.
+#include <cuda_fp4.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -77,14 +79,36 @@ int rmsnorm(const void* x, void* residual, const void* w, void* y, int rows, int
 // the paged cache at slots[t] (page = slot / page_size): cache layout [num_pages, Hkv, page_size, D].
 // cos/sin come from a table [max_pos, rot/2] built in fp64 on the host. One warp per (token, head);
 // the head vector is staged in shared memory so each lane can read its rotation partner.
+// NVFP4 cache (kscale / vscale given): k and v rows are stored as e2m1 pairs [.., D/2] with one e4m3 scale per 16
+// elements [.., D/16]: scale = e4m3(amax / 6), codes = e2m1(x / scale) rounded to nearest, saturating at +-6.
+AFB_DEV void store_nvfp4_row(const float* x, int D, int lane, uint8_t* packed, uint8_t* scales) {
+  if (lane < D / 16) {
+    const float* blk = x + lane * 16;
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(blk[i]));
+    const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(amax / 6.f, __NV_SATFINITE, __NV_E4M3);
+    const float sd = __half2float(__half(__nv_cvt_fp8_to_halfraw(s8, __NV_E4M3)));
+    const float inv = sd > 0.f ? 1.f / sd : 0.f;
+    uint8_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      b[i] = __nv_cvt_float2_to_fp4x2(make_float2(blk[2 * i] * inv, blk[2 * i + 1] * inv), __NV_E2M1,
+                                      cudaRoundNearest);
+    *reinterpret_cast<uint2*>(packed + lane * 8) = *reinterpret_cast<const uint2*>(b);
+    scales[lane] = s8;
+  }
+}
+
 __global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv, int ld, int T, int Hq, int Hkv, int D,
                                           int rot, const __nv_bfloat16* __restrict__ qw,
                                           const __nv_bfloat16* __restrict__ kw, const int* __restrict__ positions,
                                           const int* __restrict__ slots, const float* __restrict__ cos_t,
                                           const float* __restrict__ sin_t, float eps, __nv_bfloat16* __restrict__ q_out,
                                           __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache,
-                                          int page_size) {
+                                          int page_size, uint8_t* __restrict__ kscale, uint8_t* __restrict__ vscale) {
   __shared__ float buf[8][256];
+  __shared__ float obuf[8][256];
   const int wi = threadIdx.x >> 5;
   const int gw = blockIdx.x * (blockDim.x >> 5) + wi;
   const int lane = threadIdx.x & 31;
@@ -106,12 +130,20 @@ __global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv,
   }
   const int slot = slots[t];
   const int page = slot / page_size, tok = slot % page_size;
+  const bool fp4 = kscale != nullptr;
+  float* b = buf[wi];
   if (kind == 2) {
-    __nv_bfloat16* dst = vcache + (((size_t)page * Hkv + (h - Hq - Hkv)) * page_size + tok) * D;
+    const size_t row = ((size_t)page * Hkv + (h - Hq - Hkv)) * page_size + tok;
+    if (fp4) {
+      for (int j = lane; j < D; j += 32) b[j] = __bfloat162float(src[j]);
+      __syncwarp();
+      store_nvfp4_row(b, D, lane, reinterpret_cast<uint8_t*>(vcache) + row * (D / 2), vscale + row * (D / 16));
+      return;
+    }
+    __nv_bfloat16* dst = vcache + row * D;
     for (int j = lane; j < D; j += 32) dst[j] = src[j];
     return;
   }
-  float* b = buf[wi];
   float ss = 0.f;
   for (int j = lane; j < D; j += 32) {
     const float f = __bfloat162float(src[j]);
@@ -125,8 +157,10 @@ __global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv,
   __syncwarp();
   const int half = rot / 2;
   const int p = positions[t];
-  __nv_bfloat16* dst = kind == 0 ? q_out + ((size_t)t * Hq + h) * D
-                                 : kcache + (((size_t)page * Hkv + (h - Hq)) * page_size + tok) * D;
+  const size_t krow = ((size_t)page * Hkv + (h - Hq)) * page_size + tok;
+  const bool k_fp4 = fp4 && kind == 1;
+  __nv_bfloat16* dst = kind == 0 ? q_out + ((size_t)t * Hq + h) * D : kcache + krow * D;
+  float* ob = obuf[wi];
   for (int j = lane; j < D; j += 32) {
     float o = b[j];
     if (j < rot) {
@@ -134,20 +168,29 @@ __global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv,
       const float cs = cos_t[(size_t)p * half + fi], sn = sin_t[(size_t)p * half + fi];
       o = j < half ? b[j] * cs - b[j + half] * sn : b[j] * cs + b[j - half] * sn;
     }
-    dst[j] = __float2bfloat16(o);
+    if (k_fp4)
+      ob[j] = o;
+    else
+      dst[j] = __float2bfloat16(o);
+  }
+  if (k_fp4) {
+    __syncwarp();
+    store_nvfp4_row(ob, D, lane, reinterpret_cast<uint8_t*>(kcache) + krow * (D / 2), kscale + krow * (D / 16));
   }
 }
 
 int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, int rot, const void* qw, const void* kw,
                        const int* positions, const int* slots, const float* cos_t, const float* sin_t, float eps,
-                       void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st) {
-  if (D > 256 || rot > D || rot % 2) return 3;
+                       void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st, uint8_t* kscale,
+                       uint8_t* vscale) {
+  if (D > 256 || rot > D || rot % 2 || (kscale && D % 32)) return 3;
   if (!T) return 0;
   const int warps = 8;
   const int total = T * (Hq + 2 * Hkv);
   qk_norm_rope_store_kernel<<<(total + warps - 1) / warps, warps * 32, 0, st>>>(
       (const __nv_bfloat16*)qkv, ld, T, Hq, Hkv, D, rot, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, positions,
-      slots, cos_t, sin_t, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)kcache, (__nv_bfloat16*)vcache, page_size);
+      slots, cos_t, sin_t, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)kcache, (__nv_bfloat16*)vcache, page_size,
+      kscale, vscale);
   return (int)cudaGetLastError();
 }
 

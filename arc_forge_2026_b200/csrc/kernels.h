@@ -12,7 +12,8 @@ int rmsnorm(const void* x, void* residual, const void* w, void* y, int rows, int
             cudaStream_t st);
 int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, int rot, const void* qw, const void* kw,
                        const int* positions, const int* slots, const float* cos_t, const float* sin_t, float eps,
-                       void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st);
+                       void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st,
+                       uint8_t* kscale = nullptr, uint8_t* vscale = nullptr);  // scales given: NVFP4 cache
 int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, int* ids, float* weights,
                 cudaStream_t st);
 int expert_sort(const int* ids, int n, int E, const int* expert_map, int* offsets, int* row_token, int* row_entry,
@@ -27,8 +28,10 @@ int embedding(const int* ids, const void* table, void* out, int T, int H, int V,
 // attention.cu
 struct AttnArgs {
   const __nv_bfloat16* q = nullptr;  // [num_tokens, Hq, D], num_tokens = num_seqs * q_per_seq
-  const void* kcache = nullptr;      // [num_pages, Hkv, 64, D] bf16
+  const void* kcache = nullptr;      // [num_pages, Hkv, 64, D] bf16, or NVFP4: [num_pages, Hkv, 64, D/2] e2m1 pairs
   const void* vcache = nullptr;
+  const uint8_t* kscale = nullptr;   // NVFP4 only: [num_pages, Hkv, 64, D/16] e4m3, one scale per 16 elements
+  const uint8_t* vscale = nullptr;
   int num_pages = 0;
   const int* block_table = nullptr;  // [num_seqs, max_pages]
   int max_pages = 0;

@@ -19,10 +19,24 @@ void rmsnorm_op(const at::Tensor& x, c10::optional<at::Tensor> residual, const a
            "rmsnorm");
 }
 
+// NVFP4 KV cache: the e2m1 pairs [pages, Hkv, 64, D/2] (uint8) and their e4m3 scales [pages, Hkv, 64, D/16] (uint8)
+uint8_t* kv_scale_ptr(const c10::optional<at::Tensor>& scale, const at::Tensor& cache, int64_t D) {
+  if (!scale.has_value()) return nullptr;
+  AFB_CHECK_CONTIG(scale.value());
+  AFB_CHECK_CONTIG(cache);
+  TORCH_CHECK(cache.scalar_type() == at::kByte && scale->scalar_type() == at::kByte, "NVFP4 cache and scales: uint8");
+  TORCH_CHECK(cache.dim() == 4 && cache.size(2) == 64 && cache.size(3) * 2 == D && scale->dim() == 4 &&
+                  scale->size(0) == cache.size(0) && scale->size(1) == cache.size(1) && scale->size(2) == 64 &&
+                  scale->size(3) * 16 == D,
+              "NVFP4 cache must be [pages, Hkv, 64, D/2] with scales [pages, Hkv, 64, D/16]");
+  return scale->data_ptr<uint8_t>();
+}
+
 void qk_norm_rope_store_op(const at::Tensor& qkv, int64_t Hq, int64_t Hkv, int64_t D, int64_t rot,
                            const at::Tensor& qw, const at::Tensor& kw, const at::Tensor& positions,
                            const at::Tensor& slots, const at::Tensor& cos_t, const at::Tensor& sin_t, double eps,
-                           at::Tensor& q_out, at::Tensor& kcache, at::Tensor& vcache) {
+                           at::Tensor& q_out, at::Tensor& kcache, at::Tensor& vcache,
+                           c10::optional<at::Tensor> kscale, c10::optional<at::Tensor> vscale) {
   AFB_CHECK_DT(positions, at::kInt);
   AFB_CHECK_DT(slots, at::kInt);
   AFB_CHECK_DT(cos_t, at::kFloat);
@@ -33,7 +47,7 @@ void qk_norm_rope_store_op(const at::Tensor& qkv, int64_t Hq, int64_t Hkv, int64
   check_rc(afb::qk_norm_rope_store(qkv.data_ptr(), qkv.stride(0), T, Hq, Hkv, D, rot, qw.data_ptr(), kw.data_ptr(),
                                    ptr<int>(positions), ptr<int>(slots), ptr<float>(cos_t), ptr<float>(sin_t),
                                    (float)eps, q_out.data_ptr(), kcache.data_ptr(), vcache.data_ptr(), page_size,
-                                   stream()),
+                                   stream(), kv_scale_ptr(kscale, kcache, D), kv_scale_ptr(vscale, vcache, D)),
            "qk_norm_rope_store");
 }
 
@@ -217,7 +231,8 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
                         at::Tensor& out, c10::optional<at::Tensor> gate, int64_t gate_ld, int64_t gate_head_stride,
                         int64_t splits, int64_t pages_per_split, int64_t window, c10::optional<at::Tensor> bt_row,
                         c10::optional<at::Tensor> sp_count, c10::optional<at::Tensor> sp_lpage,
-                        c10::optional<at::Tensor> sp_mask) {
+                        c10::optional<at::Tensor> sp_mask, c10::optional<at::Tensor> kscale,
+                        c10::optional<at::Tensor> vscale) {
   AFB_CHECK_DT(q, at::kBFloat16);
   AFB_CHECK_CONTIG(q);
   AFB_CHECK_CONTIG(kcache);
@@ -231,8 +246,14 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
   a.vcache = vcache.data_ptr();
   a.num_pages = kcache.size(0);
   a.Hkv = kcache.size(1);
-  a.D = kcache.size(3);
+  a.D = kcache.size(3) * (kscale.has_value() ? 2 : 1);
   a.Hq = q.size(1);
+  TORCH_CHECK(q.size(2) == a.D, "q head dim must match the cache");
+  if (kscale.has_value()) {  // NVFP4 cache
+    TORCH_CHECK(vscale.has_value(), "NVFP4 attention needs both scale tensors");
+    a.kscale = kv_scale_ptr(kscale, kcache, a.D);
+    a.vscale = kv_scale_ptr(vscale, vcache, a.D);
+  }
   a.block_table = ptr<int>(block_table);
   a.max_pages = block_table.size(1);
   a.seq_lens = ptr<int>(seq_lens);
@@ -1082,7 +1103,10 @@ void embedding_op(const at::Tensor& ids, const at::Tensor& table, at::Tensor& ou
 
 void register_kernel_ops(pybind11::module& m) {
   m.def("rmsnorm", &rmsnorm_op);
-  m.def("qk_norm_rope_store", &qk_norm_rope_store_op);
+  m.def("qk_norm_rope_store", &qk_norm_rope_store_op, py::arg("qkv"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"),
+        py::arg("rot"), py::arg("qw"), py::arg("kw"), py::arg("positions"), py::arg("slots"), py::arg("cos_t"),
+        py::arg("sin_t"), py::arg("eps"), py::arg("q_out"), py::arg("kcache"), py::arg("vcache"),
+        py::arg("kscale") = py::none(), py::arg("vscale") = py::none());
   m.def("router_topk", &router_topk_op);
   m.def("expert_sort", &expert_sort_op);
   m.def("quant_rows_e4m3", &quant_rows_e4m3_op);
@@ -1128,7 +1152,8 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("block_table"), py::arg("seq_lens"), py::arg("q_per_seq"), py::arg("scale"), py::arg("out"),
         py::arg("gate"), py::arg("gate_ld"), py::arg("gate_head_stride"), py::arg("splits"),
         py::arg("pages_per_split"), py::arg("window"), py::arg("bt_row"), py::arg("sp_count") = py::none(),
-        py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none());
+        py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none(), py::arg("kscale") = py::none(),
+        py::arg("vscale") = py::none());
   m.def("qsa_prep", &qsa_prep_op);
   py::class_<GuardCtx>(m, "GuardCtx")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, const at::Tensor&,

@@ -371,8 +371,16 @@ class HybridModel:
         return sum(t.nbytes for _, t in self.tensors())
 
     # ------------------------------------------------------------------ caches
-    def new_kv_cache(self, num_pages: int):
+    def new_kv_cache(self, num_pages: int, kv_dtype: str = "bf16"):
+        """Per attention layer (k, v) bf16 pages, or with ``kv_dtype="nvfp4"`` (k, v, kscale, vscale): e2m1 codes
+        and e4m3 scales per 16 elements (``ops/attention.py`` ``new_nvfp4_kv``)."""
         c = self.cfg
+        if kv_dtype == "nvfp4":
+            from ..ops.attention import new_nvfp4_kv
+            return [new_nvfp4_kv(num_pages, c.num_kv_heads, c.head_dim, self.device)
+                    for _ in range(c.num_attention_layers)]
+        if kv_dtype != "bf16":
+            raise ValueError(f"kv_dtype {kv_dtype!r}: bf16 or nvfp4")
         shape = (num_pages, c.num_kv_heads, PAGE, c.head_dim)
         return [(torch.zeros(shape, dtype=torch.bfloat16, device=self.device),
                  torch.zeros(shape, dtype=torch.bfloat16, device=self.device)) for _ in range(c.num_attention_layers)]
@@ -428,10 +436,12 @@ class HybridModel:
             if lw.kind == FULL:
                 qkv = ws.qkv[:N]
                 cC.gemm(y, lw.w_qkv, out=qkv)
-                kc, vc = kv[ai]
+                kc, vc, *kvs = kv[ai]  # kvs: the NVFP4 scales, or empty for a bf16 cache
+                kvs = tuple(kvs) or None
                 q = ws.q[:N]
                 cC.qk_norm_rope_store(qkv, Hq, Hkv, D, c.rotary_dim, lw.q_norm, lw.k_norm, b.positions, b.slots,
-                                      self.rope_cos, self.rope_sin, c.rms_norm_eps, q, kc, vc)
+                                      self.rope_cos, self.rope_sin, c.rms_norm_eps, q, kc, vc,
+                                      *(kvs or (None, None)))
                 attn = ws.attn[:N]
                 row_len = qkv.shape[1]
                 gate = qkv[:, D:]
@@ -442,18 +452,18 @@ class HybridModel:
                 if qsa is not None and b.attn_bt_row is None:
                     qsa_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, qsa.fin, key, qsa.ws,
                                   attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
-                                  splits=qsa.splits, hs=qsa.hs, layer=ai, replay=qsa.replay)
+                                  splits=qsa.splits, hs=qsa.hs, layer=ai, replay=qsa.replay, kv_scales=kvs)
                 elif b.attn_bt_row is not None:
                     # prefill: virtual rows of attn_q_per_seq queries; rows past N are padding (scratch)
                     qp = b.attn_q_per_seq
                     nv = b.attn_bt_row.shape[0]
                     paged_attention(ws.q[: nv * qp].view(-1, Hq, D), kc, vc, b.block_table, b.attn_seq_lens, qp,
                                     ws.attn[: nv * qp].view(-1, Hq, D), gate=ws.qkv[: nv * qp, D:], gate_ld=row_len,
-                                    gate_head_stride=2 * D, max_pages=b.max_pages, bt_row=b.attn_bt_row)
+                                    gate_head_stride=2 * D, max_pages=b.max_pages, bt_row=b.attn_bt_row, kv_scales=kvs)
                 else:
                     paged_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, b.q_per_seq,
                                     attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
-                                    max_pages=b.max_pages)
+                                    max_pages=b.max_pages, kv_scales=kvs)
                 cC.gemm(attn, lw.w_o, out=h, residual=None if hs is not None else h)
                 ai += 1
             else:

@@ -100,10 +100,10 @@ class DecisionReplay:
 
 def qsa_attention(q, kcache, vcache, block_table, seq_lens, fin, idx_key, ws: QsaWorkspace, out, gate=None,
                   gate_ld=0, gate_head_stride=0, splits: int = 1, hs=None, layer: int = 0,
-                  replay: DecisionReplay | None = None):
+                  replay: DecisionReplay | None = None, kv_scales=None):
     """q [S*W, Hq, D] (already normed / RoPE'd), ws.idx_q filled by ``qsa_prep`` for the same rows. With ``hs``
     (a ``HiSparseState``) the selected finalised pages are first made resident from the host pool; ``replay``
-    records or forces the selections."""
+    records or forces the selections. ``kv_scales``: (kscale, vscale) of an NVFP4 cache."""
     c = C()
     S = seq_lens.shape[0]
     if replay is not None and replay.mode == "force":
@@ -119,7 +119,7 @@ def qsa_attention(q, kcache, vcache, block_table, seq_lens, fin, idx_key, ws: Qs
     pps = math.ceil(ws.ucap / splits)
     c.paged_attention(q, kcache, vcache, ws.u_page[:S], seq_lens, ws.W, 1.0 / math.sqrt(D), out, gate, gate_ld,
                       gate_head_stride, math.ceil(ws.ucap / pps), pps, 0, None, ws.u_count[:S], ws.u_lpage[:S],
-                      ws.u_mask[:S])
+                      ws.u_mask[:S], *(kv_scales or (None, None)))
     return out
 
 

@@ -82,7 +82,9 @@ class SpecEngine:
         # writes never land in another session's pages
         self.scratch_page = num_pages - 1
         self.alloc = C().PageAllocator(num_pages - 1, PAGE)
-        self.kv = model.new_kv_cache(num_pages)
+        if scfg.kv_dtype == "nvfp4" and scfg.hisparse:
+            raise ValueError("the HiSparse host pool holds bf16 / e4m3 pages: use kv_dtype='bf16' with hisparse")
+        self.kv = model.new_kv_cache(num_pages, scfg.kv_dtype)
         self.gdn = model.new_gdn_states(S, W)
         self.ple = model.new_ple_states(S, W) if model.cfg.ple_layer_ids else None
         i32 = dict(dtype=torch.int32, device=dev)

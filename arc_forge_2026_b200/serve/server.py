@@ -471,7 +471,7 @@ def _build_engine(args):
         drafter = (Drafter.from_dir(args.drafter_dir, dev) if args.drafter_dir else
                    Drafter(drafter_preset(args.drafter), cfg.hidden_size, cfg.vocab_size, dev, seed=args.seed + 1))
     scfg = ServeConfig(spec_k=args.spec_k, accept_mode=args.accept_mode, temperature=args.temperature,
-                       hisparse=args.hisparse, seed=args.seed)
+                       kv_dtype=args.kv_dtype, hisparse=args.hisparse, seed=args.seed)
     eng = SpecEngine(model, drafter, scfg, args.sessions, args.max_context)
     return eng, cfg
 
@@ -489,6 +489,8 @@ def main(argv=None):
                     choices=["rejection", "greedy", "bernoulli"])
     ap.add_argument("--temperature", type=float, default=0.0)
     ap.add_argument("--hisparse", action="store_true", help="host KV pool for idle pages (QSA models)")
+    ap.add_argument("--kv-dtype", dest="kv_dtype", default="bf16", choices=["bf16", "nvfp4"],
+                    help="target KV cache format (nvfp4: e2m1 with e4m3 scales per 16 elements)")
     ap.add_argument("--sessions", type=int, default=8)
     ap.add_argument("--max-context", dest="max_context", type=int, default=4096)
     ap.add_argument("--tokenizer", default=None, help="local Hugging Face tokenizer directory (default: bytes)")

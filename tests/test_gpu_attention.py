@@ -61,3 +61,56 @@ def test_paged_attention_window_and_virtual_rows(window):
     check_status()
     ref = paged_attention_reference(q, kc, vc, bt.expand(3, maxp), seq_lens, qp, window=window)
     assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("D,splits", [(256, None), (128, 3)])
+def test_nvfp4_kv_store_and_attention(D, splits):
+    """The KV store writes e2m1 codes with e4m3 scales per 16 elements (close to the bf16 rows); attention over the
+    NVFP4 cache (bulk-copied packed pages dequantised in shared memory) equals attention over the same values in
+    bf16 pages."""
+    from arc_forge_2026_b200.ops import C
+    from arc_forge_2026_b200.ops.attention import new_nvfp4_kv, nvfp4_dequant
+    from arc_forge_2026_b200.models.reference import rope_cos_sin
+    g = torch.Generator(device="cpu").manual_seed(D)
+    Hq, Hkv, qp, rot = 16, 2, 5, 64
+    lens = [70, 333, 1200]
+    S = len(lens)
+    maxp = max((L + 63) // 64 for L in lens)
+    P = S * maxp + 2
+    bt = torch.randperm(P, generator=g)[: S * maxp].view(S, maxp).int().to(dev)
+    kc = torch.zeros(P, Hkv, 64, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    k4, v4, ks, vs = new_nvfp4_kv(P, Hkv, D, dev)
+    cos, sin = rope_cos_sin(torch.arange(4096, device=dev), rot, 1e7)
+    qw = (torch.randn(D, generator=g) * 0.1).bfloat16().to(dev)
+    kw = (torch.randn(D, generator=g) * 0.1).bfloat16().to(dev)
+    width = Hq * 2 * D + 2 * Hkv * D
+    for s, L in enumerate(lens):  # the whole context through the store kernel, both formats
+        qkv = (torch.randn(L, width, generator=g) * 2).bfloat16().to(dev)
+        pos = torch.arange(L, dtype=torch.int32, device=dev)
+        slots = (bt[s, pos.long() // 64] * 64 + pos % 64).int()
+        qo = torch.empty(L, Hq, D, dtype=torch.bfloat16, device=dev)
+        C().qk_norm_rope_store(qkv, Hq, Hkv, D, rot, qw, kw, pos, slots, cos.contiguous(), sin.contiguous(), 1e-6,
+                               qo, kc, vc)
+        C().qk_norm_rope_store(qkv, Hq, Hkv, D, rot, qw, kw, pos, slots, cos.contiguous(), sin.contiguous(), 1e-6,
+                               qo, k4, v4, kscale=ks, vscale=vs)
+    torch.cuda.synchronize()
+    check_status()
+    kd, vd = nvfp4_dequant(k4, ks), nvfp4_dequant(v4, vs)
+    used = bt.reshape(-1).long()
+    for deq, ref in ((kd, kc), (vd, vc)):
+        err = _rel(deq[used], ref[used])
+        assert 0 < err < 0.15, err  # e2m1: one mantissa bit
+    seq_lens = torch.tensor(lens, dtype=torch.int32, device=dev)
+    q = torch.randn(S * qp, Hq, D, generator=g).bfloat16().to(dev)
+    gate = torch.randn(S * qp, Hq, 2 * D, generator=g).bfloat16().to(dev)
+    out4, outb = torch.empty_like(q), torch.empty_like(q)
+    paged_attention(q, k4, v4, bt, seq_lens, qp, out4, gate=gate[..., D:], gate_ld=Hq * 2 * D, gate_head_stride=2 * D,
+                    splits=splits, kv_scales=(ks, vs))
+    paged_attention(q, kd.bfloat16(), vd.bfloat16(), bt, seq_lens, qp, outb, gate=gate[..., D:], gate_ld=Hq * 2 * D,
+                    gate_head_stride=2 * D, splits=splits)
+    torch.cuda.synchronize()
+    check_status()
+    assert _rel(out4, outb) < 1e-3, _rel(out4, outb)
+    ref = paged_attention_reference(q, kd.bfloat16(), vd.bfloat16(), bt, seq_lens, qp, gate=gate[..., D:])
+    assert _rel(out4, ref) < 1e-2

@@ -345,3 +345,22 @@ def test_session_continuation_and_parking_match_fresh_prefill():
     assert not eng.parked and len(eng.free_rows) == 2
     torch.cuda.synchronize()
     check_status()
+
+
+def test_nvfp4_kv_engine_speculative_equals_plain():
+    """The engine with an NVFP4 target KV cache: greedy speculative decoding equals plain greedy decoding, and the
+    first token is among the reference's best."""
+    cfg, ref, model = _models(10)
+    g = torch.Generator().manual_seed(10)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (150, 40)]
+    plain = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy", kv_dtype="nvfp4"), 2,
+                       1024).generate(prompts, 24)
+    drafter = Drafter(drafter_preset("tiny"), cfg.hidden_size, cfg.vocab_size, dev, draft_vocab=4096)
+    spec = SpecEngine(model, drafter, ServeConfig(spec_k=4, accept_mode="greedy", kv_dtype="nvfp4"), 2,
+                      1024).generate(prompts, 24)
+    torch.cuda.synchronize()
+    check_status()
+    assert plain == spec
+    with torch.no_grad():
+        for p, out in zip(prompts, plain):
+            assert out[0] in ref(torch.tensor([p]))[0, -1].topk(3).indices.tolist()
