@@ -860,6 +860,32 @@ static void hc_shape(const at::Tensor& h, int64_t& rows, int& G, int& H) {
   G = h.size(-2);
   rows = h.numel() / ((int64_t)G * H);
 }
+// LoRA: rows_times(P [T, K] bf16, W [R, K] fp32) -> [T, R] fp32; tgrad(P [T, M] bf16, Q [T, R] fp32) -> [M, R] fp32
+at::Tensor lora_rows_times_op(const at::Tensor& P, const at::Tensor& W) {
+  AFB_CHECK_DT(P, at::kBFloat16);
+  AFB_CHECK_DT(W, at::kFloat);
+  AFB_CHECK_CONTIG(W);
+  TORCH_CHECK(P.dim() == 2 && P.stride(1) == 1 && W.dim() == 2 && W.size(1) == P.size(1), "lora_rows_times shapes");
+  const int T = P.size(0), K = P.size(1), R = W.size(0);
+  at::Tensor out = torch::empty({T, R}, W.options());
+  check_rc(afb::lora_rows_times(P.data_ptr(), P.stride(0), ptr<float>(W), T, K, R, ptr<float>(out), stream()),
+           "lora_rows_times");
+  return out;
+}
+at::Tensor lora_tgrad_op(const at::Tensor& P, const at::Tensor& Q, int64_t splits) {
+  AFB_CHECK_DT(P, at::kBFloat16);
+  AFB_CHECK_DT(Q, at::kFloat);
+  AFB_CHECK_CONTIG(Q);
+  TORCH_CHECK(P.dim() == 2 && P.stride(1) == 1 && Q.dim() == 2 && Q.size(0) == P.size(0), "lora_tgrad shapes");
+  const int T = P.size(0), M = P.size(1), R = Q.size(1);
+  at::Tensor part = torch::empty({splits, M, R}, Q.options());
+  at::Tensor out = torch::empty({M, R}, Q.options());
+  check_rc(afb::lora_tgrad(P.data_ptr(), P.stride(0), ptr<float>(Q), T, M, R, (int)splits, ptr<float>(part),
+                           ptr<float>(out), stream()),
+           "lora_tgrad");
+  return out;
+}
+
 // ``shard_ptrs`` / ``scale_ptrs``: device addresses of the table shards (this process's tensors or peers' buffers
 // mapped from a symmetric heap); the Python wrapper checks their shapes.
 void ple_lookup_op(const at::Tensor& ext, const at::Tensor& pos, const at::Tensor& seg, int64_t n, int64_t hpn,
@@ -1133,6 +1159,8 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("gdn_decode", &gdn_decode_op);
   m.def("gdn_train", &gdn_train_op);
   m.def("ple_lookup", &ple_lookup_op);
+  m.def("lora_rows_times", &lora_rows_times_op);
+  m.def("lora_tgrad", &lora_tgrad_op);
   m.def("hc_norm", &hc_norm_op);
   m.def("hc_mix", &hc_mix_op);
   m.def("hc_inject", &hc_inject_op);

@@ -34,6 +34,42 @@ FP8_PROJ = ("q_proj", "k_proj", "v_proj", "in_proj_qkvz", "out_proj")
 DEFAULT_TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "in_proj_qkvz", "in_proj_ba", "out_proj")
 
 
+def _tgrad_splits(T: int, M: int) -> int:
+    """T splits of the native tgrad: about 4 CTAs per SM, no split longer than 2,048 rows (long fp32 sums drift)."""
+    tiles = max(1, (M + 127) // 128)
+    return max(1, min((T + 63) // 64, max(-(-148 * 4 // tiles), -(-T // 2048))))
+
+
+class _LoRANative(torch.autograd.Function):
+    """``scale * (x A^T) B^T`` with the native LoRA kernels (``csrc/lora.cu``): the bf16 activations and output
+    gradients are read once in bf16, never copied to fp32; the rank-r expansions (s B^T, ds A) stay fp32 GEMMs."""
+
+    @staticmethod
+    def forward(ctx, x, A, B, scale):
+        from ..ops import C
+        lead = x.shape[:-1]
+        xb = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
+        s = C().lora_rows_times(xb, A.detach().float().contiguous())            # [T, r]
+        ctx.save_for_backward(xb, s, A, B)
+        ctx.scale, ctx.lead, ctx.xdtype = scale, lead, x.dtype
+        return ((s @ B.float().t()) * scale).view(*lead, B.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import kernels
+        from ..ops import C
+        xb, s, A, B = ctx.saved_tensors
+        c = C()
+        dyb = dy.reshape(-1, dy.shape[-1]).to(torch.bfloat16).contiguous()
+        T = dyb.shape[0]
+        dB = c.lora_tgrad(dyb, s, _tgrad_splits(T, dyb.shape[1])) * ctx.scale              # [N, r]
+        ds = c.lora_rows_times(dyb, B.detach().float().t().contiguous()) * ctx.scale      # [T, r]
+        dA = c.lora_tgrad(xb, ds.contiguous(), _tgrad_splits(T, xb.shape[1])).t()         # [r, K]
+        dx = (ds @ A.float()).to(ctx.xdtype).view(*ctx.lead, A.shape[1])
+        kernels.hit("lora_grad", True)
+        return dx, dA, dB, None
+
+
 class LoRAAdapter(nn.Module):
     def __init__(self, in_features: int, out_features: int, r: int, alpha: float, device, generator=None):
         super().__init__()
@@ -42,6 +78,12 @@ class LoRAAdapter(nn.Module):
         self.B = nn.Parameter(torch.zeros(out_features, r, device=device))
 
     def forward(self, x):
+        from . import kernels
+        if (x.is_cuda and kernels.use("lora_grad") and self.r in (8, 16, 32, 64) and x.shape[-1] % 8 == 0
+                and self.B.shape[0] % 8 == 0):
+            return _LoRANative.apply(x, self.A, self.B, self.scale)
+        if x.is_cuda:
+            kernels.hit("lora_grad", False)
         return ((x.float() @ self.A.t()) @ self.B.t()) * self.scale
 
     def delta(self) -> torch.Tensor:

@@ -155,8 +155,21 @@ def bench_attn(S=128, T=5, seed=0):
     out = torch.empty_like(q)
     ms = time_cuda(lambda: paged_attention(q, kc, vc, bt, seq_lens, T, out, max_pages=maxp), flush_bytes=1 << 20)
     byts = int(lens.sum()) * 2 * 2 * 256 * 2
-    return [{"kernel": "paged_attn_verify", "S": S, "T": T, "ms": round(ms, 4), "kv_bytes": byts,
-             "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)}]
+    res = [{"kernel": "paged_attn_verify", "S": S, "T": T, "ms": round(ms, 4), "kv_bytes": byts,
+            "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)}]
+    # the same contexts in an NVFP4 cache (random codes, unit scales): 0.5625 bytes per element
+    del kc, vc
+    k4 = torch.randint(0, 256, (P, 2, 64, 128), dtype=torch.uint8, device=dev)
+    v4 = torch.randint(0, 256, (P, 2, 64, 128), dtype=torch.uint8, device=dev)
+    ks = torch.full((P, 2, 64, 16), 0x38, dtype=torch.uint8, device=dev)  # e4m3 1.0
+    vs = ks.clone()
+    ms4 = time_cuda(lambda: paged_attention(q, k4, v4, bt, seq_lens, T, out, max_pages=maxp, kv_scales=(ks, vs)),
+                    flush_bytes=1 << 20)
+    b4 = int(lens.sum()) * 2 * 2 * (128 + 16)
+    res.append({"kernel": "paged_attn_verify_nvfp4", "S": S, "T": T, "ms": round(ms4, 4), "kv_bytes": b4,
+                "gbs": round(b4 / ms4 / 1e6, 1), "frac_hbm_of_measured": round(b4 / ms4 / 1e6 / peaks["hbm_gbs"], 3),
+                "speedup_vs_bf16": round(ms / ms4, 2)})
+    return res
 
 
 def bench_gdn_scan(BH=32, n=256, steps=(False, True)):
@@ -224,6 +237,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "all"])
     ap.add_argument("--T", type=int, default=640)
+    ap.add_argument("--S", type=int, default=128, help="sessions of the attn case")
     ap.add_argument("--seq", type=int, default=16384, help="sequence length of the gdn_scan / gdn_train cases")
     a = ap.parse_args()
     res = []
@@ -234,7 +248,7 @@ def main():
     if a.what in ("gdn", "all"):
         res += bench_gdn()
     if a.what in ("attn", "all"):
-        res += bench_attn()
+        res += bench_attn(S=a.S)
     if a.what in ("gdn_scan", "all"):
         res += bench_gdn_scan(n=(a.seq + 63) // 64)
     if a.what in ("gdn_train", "all"):

@@ -125,3 +125,35 @@ def test_decision_replay_forces_recorded_selections(tmp_path):
     assert len(rec.log) == 1
     assert not torch.equal(outs[0], outs[1])   # other index queries select other pages
     assert torch.equal(outs[0], outs[2])       # forced: the recorded selection, bit for bit
+
+
+def test_sparse_attention_over_an_nvfp4_cache():
+    """QSA sparse verify attention reading an NVFP4 cache equals the same selection over the dequantised bf16
+    pages."""
+    from arc_forge_2026_b200.ops.attention import nvfp4_dequant
+    g = torch.Generator().manual_seed(5)
+    Hi, W, K, Hq, Hkv, D = 4, 5, 8, 16, 2, 256
+    lens = [300, 3000, 2050]
+    S = len(lens)
+    maxp = max((L + PAGE - 1) // PAGE for L in lens)
+    P = S * maxp + 3
+    bt = torch.randperm(P, generator=g)[:S * maxp].view(S, maxp).int().to(dev)
+    codes = [torch.randint(0, 256, (P, Hkv, PAGE, D // 2), generator=g, dtype=torch.uint8).to(dev) for _ in range(2)]
+    scales = [(torch.rand(P, Hkv, PAGE, D // 16, generator=g) * 0.75 + 0.25).to(torch.float8_e4m3fn)
+              .view(torch.uint8).to(dev) for _ in range(2)]
+    kd, vd = (nvfp4_dequant(c, s).bfloat16() for c, s in zip(codes, scales))
+    keys = torch.randn(S * maxp, 128, generator=g).bfloat16().to(dev)
+    idx_q = torch.randn(S * W, Hi, 128, generator=g).bfloat16().to(dev)
+    q = torch.randn(S * W, Hq, D, generator=g).bfloat16().to(dev)
+    seq_lens = torch.tensor(lens, dtype=torch.int32, device=dev)
+    fin = torch.tensor([(L - W) // PAGE for L in lens], dtype=torch.int32, device=dev)
+    outs = []
+    for kv in ((codes[0], codes[1], (scales[0], scales[1])), (kd, vd, None)):
+        ws = QsaWorkspace(S, W, K, maxp, Hi, dev)
+        ws.idx_q.copy_(idx_q)
+        out = torch.zeros(S * W, Hq, D, dtype=torch.bfloat16, device=dev)
+        qsa_attention(q, kv[0], kv[1], bt, seq_lens, fin, keys, ws, out, None, 0, 0, splits=2, kv_scales=kv[2])
+        outs.append(out)
+    torch.cuda.synchronize()
+    check_status()
+    assert _rel(outs[0], outs[1]) < 1e-3

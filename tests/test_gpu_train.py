@@ -389,3 +389,33 @@ def test_native_fp8_teacher_targets_agree_with_its_prefill():
     eng = SpecEngine(model, None, ServeConfig(spec_k=0, accept_mode="greedy"), 1, 400)
     eng.add_session(0, ids.tolist(), 2)
     assert eng.sessions[0].generated[0] == int(t_ids[-1, 0])
+
+
+@pytest.mark.parametrize("r", [16, 64])
+def test_lora_native_products_match_fp32(r):
+    """The native LoRA products (bf16 big operand, fp32 small operand as bf16 hi + lo) against fp64 torch: forward
+    output and the gradients of x, A and B; T and N not multiples of the tiles."""
+    from arc_forge_2026_b200.train import kernels
+    from arc_forge_2026_b200.train.lora import LoRAAdapter
+    g = torch.Generator().manual_seed(r)
+    T, K, N = 3001, 2048, 1000
+    ad = LoRAAdapter(K, N, r, 32.0, dev)
+    with torch.no_grad():
+        ad.B.copy_(torch.randn(N, r, generator=g) * 0.05)
+    x = torch.randn(T, K, generator=g).bfloat16().to(dev).requires_grad_(True)
+    dy = torch.randn(T, N, generator=g).bfloat16().float().to(dev)
+    kernels.reset()
+    y = ad(x)
+    y.backward(dy)
+    assert kernels.counts()["native"].get("lora_grad", 0) == 1
+    xd, A, B = x.detach().double(), ad.A.detach().double(), ad.B.detach().double()
+    s = xd @ A.t()
+    ref_y = (s @ B.t()) * ad.scale
+    dyd = dy.double()
+    ref_dB = (dyd.t() @ s) * ad.scale
+    ds = (dyd @ B) * ad.scale
+    ref_dA = ds.t() @ xd
+    ref_dx = ds @ A
+    for got, ref in ((y, ref_y), (ad.B.grad, ref_dB), (ad.A.grad, ref_dA), (x.grad, ref_dx)):
+        assert _rel(got.double(), ref) < (5e-3 if got is x.grad else 1e-4), _rel(got.double(), ref)
+    check_status()
