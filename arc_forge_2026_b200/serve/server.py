@@ -479,7 +479,7 @@ def _build_engine(args):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="tiny_cpu")
-    ap.add_argument("--gpu", action="store_true", help="native engine on cuda:0 (random-init weights)")
+    ap.add_argument("--gpu", action="store_true", help="native engine on cuda:0 (random-init weights unless --package)")
     ap.add_argument("--package", default=None, help="INT3 deploy package directory (formats/int3_package.py)")
     ap.add_argument("--drafter", default="tiny")
     ap.add_argument("--drafter-dir", dest="drafter_dir", default=None,
