@@ -12,9 +12,11 @@
 //
 // NVFP4 KV (FP4 = true): a page-head holds 64 x D/2 bytes of e2m1 pairs and 64 x D/16 e4m3 scales (one per 16
 // elements), both contiguous, so each arrives by one 1-D bulk copy per tensor into a 2-deep ring (3.6x fewer bytes
-// than bf16). All 256 threads dequantise a landed page into the same swizzled bf16 tiles the MMA path reads
-// (e2m1 x e4m3 has at most 5 significant bits, so the bf16 tile holds the dequantised values exactly); block-wide
-// barriers order the dequantisation against the previous page's MMAs, and the stage is refilled right after it.
+// than bf16). All 256 threads dequantise a landed page into swizzled f16 tiles: one e2m1x2 -> f16x2 conversion and
+// one f16x2 multiply by the block scale per element pair (e2m1 x e4m3 has at most 6 significant bits and stays
+// within f16's range, so the tile holds the dequantised values exactly). This variant runs its MMAs in f16 (Q and
+// the softmax probabilities converted to f16; fp32 accumulation). Block-wide barriers order the dequantisation
+// against the previous page's MMAs, and the stage is refilled right after it.
 #include <cudaTypedefs.h>
 #include <cuda_fp4.h>
 
@@ -48,18 +50,22 @@ struct AttnSmem {
   static constexpr int SBT = 1024;                             // block-table entries staged in shared memory
   static constexpr uint32_t SBT_OFF = BAR_OFF + 64;
   static constexpr uint32_t TOTAL = SBT_OFF + SBT * 4 + 1024;
+  static constexpr int NS = 2;  // TMA stages
 };
 
-// NVFP4 layout: 2 stages of packed K, packed V, K scales, V scales, then one bf16 K + V tile pair (the MMA operands)
+// NVFP4 layout: NS stages of packed K, packed V, K scales, V scales, then two f16 K + V tile pairs (the MMA operands
+// of page i and page i + 1)
 template <int D>
 struct AttnSmemFp4 {
+  static constexpr int NS = 3;
   static constexpr uint32_t PK = attn::PAGE * D / 2;           // e2m1 bytes of one page-head
   static constexpr uint32_t PS = attn::PAGE * D / 16;          // e4m3 scale bytes of one page-head
-  static constexpr uint32_t KV_BYTES = attn::PAGE * D * 2;     // one dequantised bf16 tile
+  static constexpr uint32_t KV_BYTES = attn::PAGE * D * 2;     // one dequantised f16 tile
+  static constexpr uint32_t BUF = 2 * KV_BYTES;                // one K + V pair
   static constexpr uint32_t STAGE = 2 * PK + 2 * PS;
-  static constexpr uint32_t BF_OFF = 2 * STAGE;
+  static constexpr uint32_t BF_OFF = NS * STAGE;
   static constexpr uint32_t Q_BYTES = 64 * D * 2;
-  static constexpr uint32_t Q_OFF = BF_OFF + 2 * KV_BYTES;
+  static constexpr uint32_t Q_OFF = BF_OFF + 2 * BUF;
   static constexpr uint32_t BAR_OFF = Q_OFF + Q_BYTES;
   static constexpr int SBT = 1024;
   static constexpr uint32_t SBT_OFF = BAR_OFF + 64;
@@ -69,7 +75,30 @@ struct AttnSmemFp4 {
                 "the half-merge scratch must fit below Q");
 };
 
-// one landed NVFP4 page-head pair (packed + scales at `st`) -> swizzled bf16 K and V tiles at `bf`
+AFB_DEV void mma_f16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <bool F16>
+AFB_DEV void mma_kv(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (F16)
+    mma_f16(c, a0, a1, a2, a3, b0, b1);
+  else
+    mma_bf16(c, a0, a1, a2, a3, b0, b1);
+}
+template <bool F16>
+AFB_DEV uint32_t pack_kv(float a, float b) {
+  if constexpr (F16) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    return pack_bf16x2(a, b);
+  }
+}
+
+// one landed NVFP4 page-head pair (packed + scales at `st`) -> swizzled f16 K and V tiles at `bf`
 template <int D>
 AFB_DEV void dequant_fp4_page(const uint8_t* st, uint8_t* bf) {
   using S = AttnSmemFp4<D>;
@@ -84,16 +113,14 @@ AFB_DEV void dequant_fp4_page(const uint8_t* st, uint8_t* bf) {
     uint8_t* dst = bf + m * S::KV_BYTES;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {  // 16 elements share one scale
-      const __half_raw sh = __nv_cvt_fp8_to_halfraw(sc[half], __NV_E4M3);
-      const float s = __half2float(__half(sh));
+      const __half2 s2 = __half2half2(__half(__nv_cvt_fp8_to_halfraw(sc[half], __NV_E4M3)));
 #pragma unroll
-      for (int c8 = 0; c8 < 2; ++c8) {  // two 8-element bf16 chunks
+      for (int c8 = 0; c8 < 2; ++c8) {  // two 8-element f16 chunks
         uint32_t w[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const __half2_raw h2 = __nv_cvt_fp4x2_to_halfraw2(b[half * 8 + c8 * 4 + j], __NV_E2M1);
-          const float2 f = __half22float2(__half2(h2));
-          w[j] = pack_bf16x2(f.x * s, f.y * s);
+          const __half2 h2 = __hmul2(__half2(__nv_cvt_fp4x2_to_halfraw2(b[half * 8 + c8 * 4 + j], __NV_E2M1)), s2);
+          w[j] = *reinterpret_cast<const uint32_t*>(&h2);
         }
         const int cc = pc * 4 + half * 2 + c8;
         *reinterpret_cast<uint4*>(dst + sw_off<attn::PAGE>(row, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -112,7 +139,7 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + S::Q_OFF;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-  uint64_t* empty = full + 2;
+  uint64_t* empty = full + S::NS;  // bf16 path only
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = blockIdx.x / a.Hkv, kvh = blockIdx.x % a.Hkv;
@@ -132,9 +159,9 @@ __global__ void __launch_bounds__(256, 1)
   const int* bt = a.block_table + (size_t)(a.bt_row ? a.bt_row[seq] : seq) * a.max_pages;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < S::NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], attn::WARPS);
+      if (!FP4) mbar_init(&empty[s], attn::WARPS);
     }
     fence_mbar_init();
   }
@@ -150,13 +177,20 @@ __global__ void __launch_bounds__(256, 1)
       const __nv_bfloat16* src =
           a.q + ((size_t)(seq * a.q_per_seq + t) * a.Hq + kvh * group + h) * D + cc * 8;
       v = *reinterpret_cast<const uint4*>(src);
+      if constexpr (FP4) {  // the f16 MMA path: queries to f16
+        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&v);
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = pack_kv<true>(__low2float(hb[j]), __high2float(hb[j]));
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
     }
     *reinterpret_cast<uint4*>(sQ + sw_off<64>(r, cc)) = v;
   }
   __syncthreads();
 
   auto issue = [&](int i) {
-    const int s = i & 1;
+    const int s = i % S::NS;
     const int page = i < S::SBT ? sbt[i] : bt[p0 + i];
     const int row = (page * a.Hkv + kvh) * attn::PAGE;
     uint8_t* st = smem + s * S::STAGE;
@@ -182,8 +216,8 @@ __global__ void __launch_bounds__(256, 1)
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
     }
-    for (int i = 0; i < min(2, n); ++i) issue(i);
-    issued = min(2, n);
+    for (int i = 0; i < min(S::NS, n); ++i) issue(i);
+    issued = min(S::NS, n);
   }
 
   const int mt = warp >> 1, kh = warp & 1;
@@ -201,20 +235,20 @@ __global__ void __launch_bounds__(256, 1)
     const int s = i & 1;
     uint32_t k_base;
     if constexpr (FP4) {
-      // every thread waits (bounded), then one block-wide vote keeps the exit uniform; the barrier also orders the
-      // previous page's MMA reads of the bf16 tiles before they are overwritten
-      const bool landed = mbar_wait(&full[s], (i >> 1) & 1, status);
-      if (!__syncthreads_and(landed)) {
-        ok = false;
-        break;
+      if (i == 0) {  // page 0 -> f16 buffer 0. Every thread waits (bounded); one block-wide vote keeps exits uniform
+        const bool landed = mbar_wait(&full[0], 0, status);
+        if (!__syncthreads_and(landed)) {
+          ok = false;
+          break;
+        }
+        dequant_fp4_page<D>(smem, smem + S::BF_OFF);
+        __syncthreads();
+        if (threadIdx.x == 0 && S::NS < n) {  // stage 0 is consumed: refill it
+          issue(S::NS);
+          ++issued;
+        }
       }
-      dequant_fp4_page<D>(smem + s * S::STAGE, smem + S::BF_OFF);
-      __syncthreads();
-      if (threadIdx.x == 0 && i + 2 < n) {  // the stage is consumed: refill it now
-        issue(i + 2);
-        ++issued;
-      }
-      k_base = smem_u32(smem + S::BF_OFF);
+      k_base = smem_u32(smem + S::BF_OFF + (i & 1) * S::BUF);
     } else {
       if (!mbar_wait(&full[s], (i >> 1) & 1, status)) {
         ok = false;
@@ -242,8 +276,8 @@ __global__ void __launch_bounds__(256, 1)
           const int key = kh * 32 + np * 16 + (lane & 7) + ((lane >> 4) << 3);
           const int cc = ks * 2 + ((lane >> 3) & 1);
           ldsm_x4(k_base + sw_off<attn::PAGE>(key, cc), b0, b1, b2, b3);
-          mma_bf16(sc[np * 2], a0, a1, a2, a3, b0, b1);
-          mma_bf16(sc[np * 2 + 1], a0, a1, a2, a3, b2, b3);
+          mma_kv<FP4>(sc[np * 2], a0, a1, a2, a3, b0, b1);
+          mma_kv<FP4>(sc[np * 2 + 1], a0, a1, a2, a3, b2, b3);
         }
       }
       // ---- mask + online softmax (log2 domain)
@@ -284,8 +318,8 @@ __global__ void __launch_bounds__(256, 1)
         const float e2 = exp2f(sc[j][2] - base1), e3 = exp2f(sc[j][3] - base1);
         rs0 += e0 + e1;
         rs1 += e2 + e3;
-        p[j][0] = pack_bf16x2(e0, e1);
-        p[j][1] = pack_bf16x2(e2, e3);
+        p[j][0] = pack_kv<FP4>(e0, e1);
+        p[j][1] = pack_kv<FP4>(e2, e3);
       }
       l0 = l0 * c0 + rs0;
       l1 = l1 * c1 + rs1;
@@ -306,12 +340,29 @@ __global__ void __launch_bounds__(256, 1)
           const int key = kh * 32 + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
           const int cc = dp * 2 + (lane >> 4);
           ldsm_x4_t(v_base + sw_off<attn::PAGE>(key, cc), b0, b1, b2, b3);
-          mma_bf16(o[dp * 2], pa0, pa1, pa2, pa3, b0, b1);
-          mma_bf16(o[dp * 2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+          mma_kv<FP4>(o[dp * 2], pa0, pa1, pa2, pa3, b0, b1);
+          mma_kv<FP4>(o[dp * 2 + 1], pa0, pa1, pa2, pa3, b2, b3);
         }
       }
     }
-    if constexpr (!FP4) {
+    if constexpr (FP4) {
+      // page i + 1 -> the other f16 buffer, right after this warp's MMAs on page i (warps with fewer rows start
+      // early); that buffer's last reader, page i - 1, finished before the previous barrier
+      bool landed = true;
+      if (i + 1 < n) {
+        const int s1 = (i + 1) % S::NS;
+        landed = mbar_wait(&full[s1], ((i + 1) / S::NS) & 1, status);
+        if (landed) dequant_fp4_page<D>(smem + s1 * S::STAGE, smem + S::BF_OFF + ((i + 1) & 1) * S::BUF);
+      }
+      if (!__syncthreads_and(landed)) {
+        ok = false;
+        break;
+      }
+      if (threadIdx.x == 0 && i + 1 + S::NS < n) {  // the stage of page i + 1 is consumed: refill it
+        issue(i + 1 + S::NS);
+        ++issued;
+      }
+    } else {
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
       if (threadIdx.x == 0 && i + 2 < n) {
@@ -326,7 +377,7 @@ __global__ void __launch_bounds__(256, 1)
   }
   // drain copies still in flight before the smem is reused (bounded)
   if (threadIdx.x == 0) {
-    for (int i = max(0, issued - 2); i < issued; ++i) mbar_wait(&full[i & 1], (i >> 1) & 1, status);
+    for (int i = max(0, issued - S::NS); i < issued; ++i) mbar_wait(&full[i % S::NS], (i / S::NS) & 1, status);
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);

@@ -66,8 +66,8 @@ def test_paged_attention_window_and_virtual_rows(window):
 @pytest.mark.parametrize("D,splits", [(256, None), (128, 3)])
 def test_nvfp4_kv_store_and_attention(D, splits):
     """The KV store writes e2m1 codes with e4m3 scales per 16 elements (close to the bf16 rows); attention over the
-    NVFP4 cache (bulk-copied packed pages dequantised in shared memory) equals attention over the same values in
-    bf16 pages."""
+    NVFP4 cache (bulk-copied packed pages dequantised in shared memory, f16 MMAs) agrees with attention over the same
+    values in bf16 pages and with the fp32 oracle."""
     from arc_forge_2026_b200.ops import C
     from arc_forge_2026_b200.ops.attention import new_nvfp4_kv, nvfp4_dequant
     from arc_forge_2026_b200.models.reference import rope_cos_sin
@@ -111,6 +111,6 @@ def test_nvfp4_kv_store_and_attention(D, splits):
                     gate_head_stride=2 * D, splits=splits)
     torch.cuda.synchronize()
     check_status()
-    assert _rel(out4, outb) < 1e-3, _rel(out4, outb)
+    assert _rel(out4, outb) < 1e-2, _rel(out4, outb)
     ref = paged_attention_reference(q, kd.bfloat16(), vd.bfloat16(), bt, seq_lens, qp, gate=gate[..., D:])
     assert _rel(out4, ref) < 1e-2
