@@ -91,6 +91,51 @@ at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tens
   return o;
 }
 
+// Grouped GEMM over the experts of a MoE layer (modes of afb::GemmGroups). ROWS: a [R, K] rows sorted by group,
+// b [E * group_rows, K], out [R, group_rows]. REDUCE: a [group_rows, R_pad], b [Kd, R_pad], out [E, group_rows, Kd],
+// seg entries multiples of 64.
+void gemm_grouped(const at::Tensor& a, const at::Tensor& b, const at::Tensor& seg, c10::optional<at::Tensor> tiles,
+                  int64_t mode, int64_t group_rows, int64_t max_tiles, at::Tensor& out) {
+  CHECK_CUDA(a);
+  CHECK_DT(a, at::kBFloat16);
+  CHECK_DT(b, at::kBFloat16);
+  CHECK_ROWMAJOR(a);
+  CHECK_ROWMAJOR(b);
+  CHECK_ROWMAJOR(out);
+  TORCH_CHECK(seg.scalar_type() == at::kInt && seg.is_contiguous(), "gemm_grouped: seg int32");
+  TORCH_CHECK(a.size(1) == b.size(1), "gemm_grouped: K mismatch");
+  c10::cuda::CUDAGuard g(a.device());
+  afb::GemmEpilogue epi;
+  epi.out = out.data_ptr();
+  epi.out_fp32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(epi.out_fp32 || out.scalar_type() == at::kBFloat16, "gemm_grouped: bf16 or fp32 out");
+  afb::GemmGroups grp;
+  grp.mode = (int)mode;
+  grp.seg = seg.data_ptr<int>();
+  grp.E = (int)seg.numel() - 1;
+  grp.group_rows = (int)group_rows;
+  int N;
+  if (mode == 1) {
+    TORCH_CHECK(tiles.has_value() && tiles->scalar_type() == at::kInt && tiles->numel() == seg.numel(),
+                "gemm_grouped ROWS: tiles int32 [E + 1]");
+    TORCH_CHECK(b.size(0) == (int64_t)grp.E * group_rows && out.size(0) == a.size(0) && out.size(1) == group_rows,
+                "gemm_grouped ROWS shapes");
+    grp.tiles = tiles->data_ptr<int>();
+    N = (int)group_rows;
+    epi.ldo = out.stride(0);
+  } else {
+    TORCH_CHECK(out.dim() == 3 && out.size(0) == grp.E && out.size(1) == group_rows && out.size(2) == b.size(0) &&
+                    a.size(0) == group_rows,
+                "gemm_grouped REDUCE shapes");
+    N = (int)b.size(0);
+    epi.ldo = (int)out.size(2);
+    grp.group_out_stride = (int64_t)group_rows * out.size(2);
+  }
+  check_rc(afb::gemm_bf16_grouped(a.data_ptr(), a.stride(0), a.size(0), b.data_ptr(), b.stride(0), b.size(0), N,
+                                  a.size(1), epi, grp, (int)max_tiles, status_ptr(a.get_device()), stream()),
+           "gemm_grouped");
+}
+
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
   afb::GemmPlan p = afb::plan_gemm(M, N, K, num_sms());
   return {p.bn, p.splits};
@@ -105,6 +150,8 @@ void register_symm(pybind11::module& m);        // defined in symm.cpp
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "arc_forge_2026_b200 native kernels (sm_100a)";
   m.def("status_tensor", &status_tensor, "per-device kernel status words (int32[16])");
+  m.def("gemm_grouped", &gemm_grouped, py::arg("a"), py::arg("b"), py::arg("seg"), py::arg("tiles"), py::arg("mode"),
+        py::arg("group_rows"), py::arg("max_tiles"), py::arg("out"));
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM: out = alpha * a @ b.T (+ residual)", py::arg("a"), py::arg("b"),
         py::arg("out") = py::none(), py::arg("residual") = py::none(), py::arg("alpha") = 1.0,
         py::arg("out_fp32") = false, py::arg("bn") = 0, py::arg("splits") = 0);

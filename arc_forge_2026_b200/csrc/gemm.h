@@ -16,6 +16,21 @@ struct GemmEpilogue {
   void* partial = nullptr;         // split-K scratch: fp32 [splits, M, N]
 };
 
+// Grouped GEMMs (the experts of a MoE layer), two forms:
+//  ROWS (mode 1):   C[r, :] = A[r, :] @ B_e^T for the rows r of group e: rows [seg[e], seg[e+1]) of A, B_e = rows
+//                   [e * group_rows, (e + 1) * group_rows) of B. tiles[e] = sum over groups before e of
+//                   ceil(rows / 128) (prefix over E + 1 entries); the grid covers an upper bound, surplus CTAs exit.
+//  REDUCE (mode 2): C_e = A[:, seg[e]:seg[e+1]] @ B[:, seg[e]:seg[e+1]]^T, written at C + e * group_out_stride;
+//                   seg entries are multiples of 64 (the K block), so no block mixes two groups.
+struct GemmGroups {
+  int mode = 0;
+  const int* seg = nullptr;     // [E + 1]
+  const int* tiles = nullptr;   // [E + 1] (ROWS)
+  int E = 0;
+  int group_rows = 0;           // ROWS: rows of B per group; REDUCE: rows of A (= rows of each C_e)
+  int64_t group_out_stride = 0; // REDUCE: elements between consecutive C_e
+};
+
 struct GemmPlan {
   int bn = 128;
   int splits = 1;
@@ -24,6 +39,9 @@ struct GemmPlan {
 GemmPlan plan_gemm(int M, int N, int K, int num_sms);
 int gemm_bf16_tn(const void* A, int lda, const void* B, int ldb, int M, int N, int K, const GemmEpilogue& epi, int bn,
                  int splits, uint32_t* status, cudaStream_t stream);
+int gemm_bf16_grouped(const void* A, int lda, int rows_a, const void* B, int ldb, int rows_b, int N, int K,
+                      const GemmEpilogue& epi, const GemmGroups& g, int max_tiles, uint32_t* status,
+                      cudaStream_t stream);
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype_bytes, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle128);
 

@@ -5,6 +5,8 @@
 //   warp 1      allocates TMEM and one elected thread issues tcgen05.mma (M=128, N=BN, K=16 per op)
 //   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, convert, optional residual add, store
 // Split-K (gridDim.z > 1) writes fp32 partials that a reduce kernel sums in a fixed order.
+// Grouped forms (GemmGroups, gemm.h) run the experts of a MoE layer in one launch: each CTA maps its tile to a
+// group (and to that group's A rows / B rows, or to its K range) before the usual pipeline.
 // Used for every dense projection of the serving and training paths (QKV/in_proj, o_proj/out_proj,
 // shared expert, router, LM head) in place of the reference's cuBLAS/CUTLASS dense GEMMs.
 #include <cudaTypedefs.h>
@@ -24,10 +26,10 @@ struct GemmSmem {
   static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int GMODE = 0>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                        int K, GemmEpilogue epi, uint32_t* status) {
+                        int K, GemmEpilogue epi, uint32_t* status, GemmGroups grp = GemmGroups()) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -46,8 +48,28 @@ __global__ void __launch_bounds__(192, 1)
   const int num_kb_total = (K + S::BK - 1) / S::BK;
   const int splits = gridDim.z;
   const int kb_per = (num_kb_total + splits - 1) / splits;
-  const int kb0 = blockIdx.z * kb_per;
-  const int kb1 = min(num_kb_total, kb0 + kb_per);
+  int kb0 = blockIdx.z * kb_per;
+  int kb1 = min(num_kb_total, kb0 + kb_per);
+  int a_row0 = tile_m * S::BM, b_row0 = tile_n * BN, m_end = M, col0_base = tile_n * BN;
+  if constexpr (GMODE == 1) {  // rows of group e: find e with tiles[e] <= tile_m < tiles[e + 1]
+    if (tile_m >= grp.tiles[grp.E]) return;  // surplus CTA of the upper-bound grid (before any barrier / TMEM)
+    int lo = 0, hi = grp.E;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (grp.tiles[mid] <= tile_m) lo = mid; else hi = mid;
+    }
+    a_row0 = grp.seg[lo] + (tile_m - grp.tiles[lo]) * S::BM;
+    m_end = grp.seg[lo + 1];
+    b_row0 = lo * grp.group_rows + tile_n * BN;
+  } else if constexpr (GMODE == 2) {  // group e = tile_m / m-tiles; its K range is its segment
+    const int mt_per = (grp.group_rows + S::BM - 1) / S::BM;
+    const int e = tile_m / mt_per;
+    a_row0 = (tile_m % mt_per) * S::BM;
+    m_end = grp.group_rows;
+    kb0 = grp.seg[e] / S::BK;
+    kb1 = grp.seg[e + 1] / S::BK;
+    epi.out = reinterpret_cast<uint8_t*>(epi.out) + (size_t)e * grp.group_out_stride * (epi.out_fp32 ? 4 : 2);
+  }
   const int num_kb = max(0, kb1 - kb0);
 
   if (threadIdx.x == 0) {
@@ -74,8 +96,8 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ph = (i / STAGES) & 1;
         if (i >= STAGES && !mbar_wait(&empty[s], ph ^ 1, status)) break;
         mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
-        tma_load_2d(sA + s * S::A_BYTES, &tmA, &full[s], (kb0 + i) * S::BK, tile_m * S::BM);
-        tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], (kb0 + i) * S::BK, tile_n * BN);
+        tma_load_2d(sA + s * S::A_BYTES, &tmA, &full[s], (kb0 + i) * S::BK, a_row0);
+        tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], (kb0 + i) * S::BK, b_row0);
         ++issued;
       }
       // drain: every issued copy has landed before the CTA may exit (bounded)
@@ -104,15 +126,15 @@ __global__ void __launch_bounds__(192, 1)
     const int quad = warp & 3;
     const bool ok = mbar_wait(done, 0, status);
     tc_fence_after();
-    const int row = tile_m * S::BM + quad * 32 + lane;
+    const int row = a_row0 + quad * 32 + lane;
     const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16);
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       float v[32];
       tmem_ld32(taddr + c, v);
       tmem_ld_wait();
-      const int col0 = tile_n * BN + c;
-      if (!ok || row >= M || col0 >= N) continue;
+      const int col0 = col0_base + c;
+      if (!ok || row >= m_end || col0 >= N) continue;
       if (num_kb == 0) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = 0.f;  // an empty split-K slice contributes zeros
@@ -235,7 +257,45 @@ static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, in
     attr = true;
   }
   dim3 grid((M + S::BM - 1) / S::BM, (N + BN - 1) / BN, splits);
-  kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, M, N, K, epi, status);
+  kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, M, N, K, epi, status, GemmGroups());
+  return (int)cudaGetLastError();
+}
+
+// Grouped launch (one tile width: 128; no split-K). A ROWS grid covers max_tiles m-tiles (an upper bound of
+// sum ceil(rows_e / 128)); a REDUCE grid covers E x ceil(group_rows / 128).
+int gemm_bf16_grouped(const void* A, int lda, int rows_a, const void* B, int ldb, int rows_b, int N, int K,
+                      const GemmEpilogue& epi, const GemmGroups& g, int max_tiles, uint32_t* status,
+                      cudaStream_t stream) {
+  constexpr int BN = 128, STAGES = 3;
+  using S = GemmSmem<BN, STAGES>;
+  if (g.mode != 1 && g.mode != 2) return 3;
+  if ((K % 8) || (lda % 8) || (ldb % 8) || (N % 8) || epi.partial) return 3;
+  if (rows_a <= 0 || rows_b <= 0 || N <= 0 || g.E <= 0) return 0;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, 2, K, rows_a, (uint64_t)lda * 2, S::BK, S::BM, 1);
+  if (rc) return 1000 + rc;
+  rc = make_tmap_2d(&tb, B, 2, K, rows_b, (uint64_t)ldb * 2, S::BK, BN, 1);
+  if (rc) return 2000 + rc;
+  dim3 grid;
+  if (g.mode == 1) {
+    auto kern = gemm_bf16_tn_kernel<BN, STAGES, 1>;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+      attr = true;
+    }
+    grid = dim3(max_tiles, (N + BN - 1) / BN, 1);
+    kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, rows_a, N, K, epi, status, g);
+  } else {
+    auto kern = gemm_bf16_tn_kernel<BN, STAGES, 2>;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+      attr = true;
+    }
+    grid = dim3(g.E * ((g.group_rows + S::BM - 1) / S::BM), (N + BN - 1) / BN, 1);
+    kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, rows_a, N, K, epi, status, g);
+  }
   return (int)cudaGetLastError();
 }
 

@@ -20,7 +20,8 @@ import os
 import threading
 
 NAMES = ("gdn_chunk", "conv_silu", "rms_norm", "gated_rms_norm", "swiglu", "moe_combine", "moe_dispatch",
-         "int3_weight", "fp8_weight", "topk_tail_kl", "hc", "ple", "lora_grad")
+         "int3_weight", "fp8_weight", "topk_tail_kl", "hc", "ple", "lora_grad",
+         "grouped_gemm")
 
 _lock = threading.Lock()
 _enabled: set[str] = set(NAMES)

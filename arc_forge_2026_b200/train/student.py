@@ -35,7 +35,16 @@ def _master(t: torch.Tensor) -> nn.Parameter:
 
 
 def grouped_linear(x: torch.Tensor, w: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
-    """x [R, K] rows sorted by expert, w [E, N, K], counts [E] -> [R, N]."""
+    """x [R, K] rows sorted by expert, w [E, N, K], counts [E] -> [R, N]. CUDA: the grouped tcgen05 GEMM
+    (``train/grouped.py``; forward, dX and dW native); CPU: one GEMM per expert."""
+    from . import kernels
+    if x.is_cuda and kernels.use("grouped_gemm") and x.dtype == torch.bfloat16 and x.shape[1] % 8 == 0 \
+            and w.shape[1] % 8 == 0:
+        from .grouped import GroupedLinear
+        kernels.hit("grouped_gemm", True)
+        return GroupedLinear.apply(x, w, counts)
+    if x.is_cuda:
+        kernels.hit("grouped_gemm", False)
     if x.is_cuda and hasattr(torch, "_grouped_mm"):
         offs = counts.cumsum(0).to(torch.int32)
         return torch._grouped_mm(x, w.transpose(-2, -1), offs=offs)

@@ -419,3 +419,33 @@ def test_lora_native_products_match_fp32(r):
     for got, ref in ((y, ref_y), (ad.B.grad, ref_dB), (ad.A.grad, ref_dA), (x.grad, ref_dx)):
         assert _rel(got.double(), ref) < (5e-3 if got is x.grad else 1e-4), _rel(got.double(), ref)
     check_status()
+
+
+def test_grouped_expert_gemm_matches_per_expert_gemms():
+    """The grouped tcgen05 GEMM (ROWS for the forward and dX, REDUCE for dW) against one fp32 GEMM per expert, with
+    empty experts and segment lengths that are not multiples of the tiles."""
+    from arc_forge_2026_b200.train.grouped import GroupedLinear
+    g = torch.Generator().manual_seed(21)
+    E, K, N = 9, 512, 384
+    counts = torch.tensor([0, 5, 200, 1, 0, 130, 64, 63, 300])
+    R = int(counts.sum())
+    x = torch.randn(R, K, generator=g).bfloat16().to(dev).requires_grad_(True)
+    w = (torch.randn(E, N, K, generator=g) * 0.05).bfloat16().to(dev).requires_grad_(True)
+    dy = torch.randn(R, N, generator=g).bfloat16().to(dev)
+    for _ in range(2):  # twice: the second call reuses the kernel's cached state
+        x.grad = w.grad = None
+        y = GroupedLinear.apply(x, w, counts.to(dev))
+        y.backward(dy)
+    torch.cuda.synchronize()
+    check_status()
+    xs, ws, dys = x.detach().float(), w.detach().float(), dy.float()
+    ys, dxs, dws, o = [], [], [], 0
+    for e, c in enumerate(counts.tolist()):
+        ys.append(xs[o:o + c] @ ws[e].t())
+        dxs.append(dys[o:o + c] @ ws[e])
+        dws.append(dys[o:o + c].t() @ xs[o:o + c])
+        o += c
+    assert _rel(y, torch.cat(ys)) < 1e-2
+    assert _rel(x.grad, torch.cat(dxs)) < 1e-2
+    assert _rel(w.grad, torch.stack(dws)) < 1e-2
+    assert w.grad[0].abs().max() == 0 and w.grad[4].abs().max() == 0  # empty experts: zero gradient
