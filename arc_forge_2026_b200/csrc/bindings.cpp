@@ -101,7 +101,11 @@ void gemm_grouped(const at::Tensor& a, const at::Tensor& b, const at::Tensor& se
   CHECK_DT(b, at::kBFloat16);
   CHECK_ROWMAJOR(a);
   CHECK_ROWMAJOR(b);
-  CHECK_ROWMAJOR(out);
+  if (mode == 1) {
+    CHECK_ROWMAJOR(out);
+  } else {
+    TORCH_CHECK(out.is_contiguous(), "gemm_grouped REDUCE: contiguous [E, group_rows, Kd] out");
+  }
   TORCH_CHECK(seg.scalar_type() == at::kInt && seg.is_contiguous(), "gemm_grouped: seg int32");
   TORCH_CHECK(a.size(1) == b.size(1), "gemm_grouped: K mismatch");
   c10::cuda::CUDAGuard g(a.device());
