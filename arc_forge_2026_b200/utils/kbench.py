@@ -172,6 +172,35 @@ def bench_attn(S=128, T=5, seed=0):
     return res
 
 
+def bench_grouped(E=320, T=16384, k=10, H=2048, I=512, seed=0):
+    """Grouped expert GEMMs of one QAD layer (w13: K=H, N=2I; w2: K=I, N=H; routed rows T*k): the native grouped
+    tcgen05 GEMM (forward, dX, dW) against torch._grouped_mm."""
+    from ..train.grouped import grouped_reduce, grouped_rows
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(seed)
+    ids = torch.randint(0, E, (T * k,), generator=g, device=dev)
+    counts = torch.bincount(ids, minlength=E)
+    offs = counts.cumsum(0).int()
+    res = []
+    for name, K, N in (("w13", H, 2 * I), ("w2", I, H)):
+        x = torch.randn(T * k, K, generator=g, device=dev).bfloat16()
+        w = (torch.randn(E, N, K, generator=g, device=dev) * 0.02).bfloat16()
+        dy = torch.randn(T * k, N, generator=g, device=dev).bfloat16()
+        cases = {
+            "fwd_native": lambda: grouped_rows(x, w, counts),
+            "fwd_library": lambda: torch._grouped_mm(x, w.transpose(-2, -1), offs=offs),
+            "dx_native": lambda: grouped_rows(dy, w.transpose(1, 2).contiguous(), counts),
+            "dx_library": lambda: torch._grouped_mm(dy, w, offs=offs),
+            "dw_native": lambda: grouped_reduce(dy, x, counts),
+            "dw_library": lambda: torch._grouped_mm(dy.t(), x, offs=offs),
+        }
+        for cname, fn in cases.items():
+            ms = time_cuda(fn, flush_bytes=1 << 20)
+            res.append({"kernel": f"grouped_{name}_{cname}", "ms": round(ms, 4),
+                        "tflops": round(2 * T * k * K * N / ms / 1e9, 1)})
+    return res
+
+
 def bench_gdn_scan(BH=32, n=256, steps=(False, True)):
     """Inter-chunk scan of one GDN layer at seq 16,384 (256 chunks of 64), 32 value heads, Dk = Dv = 128: the
     tensor-core kernel and the fp32 SIMT kernel, forward and reverse (the reverse adds the Qm term)."""
@@ -235,7 +264,7 @@ def bench_gdn_train(B=1, T=16384, Hk=16, Hv=32):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "grouped", "all"])
     ap.add_argument("--T", type=int, default=640)
     ap.add_argument("--S", type=int, default=128, help="sessions of the attn case")
     ap.add_argument("--seq", type=int, default=16384, help="sequence length of the gdn_scan / gdn_train cases")
@@ -251,6 +280,8 @@ def main():
         res += bench_attn(S=a.S)
     if a.what in ("gdn_scan", "all"):
         res += bench_gdn_scan(n=(a.seq + 63) // 64)
+    if a.what in ("grouped", "all"):
+        res += bench_grouped()
     if a.what in ("gdn_train", "all"):
         res += bench_gdn_train(T=a.seq)
     for r in res:
