@@ -32,7 +32,7 @@ import sys
 import threading
 import time
 
-BASELINE_TOKS = 2141.0  # reference deployed stack, 128 sessions, DFlash K=4 (paper §8.3, p. 33)
+BASELINE_TOKS = 2141.0  # reference deployed stack, 128 sessions, DFlash K=4 (its paper, §8.3, p. 33)
 METRIC = "decode tok/s @128 sessions (8xB200, spec K=4); p50 TPOT; QAD train tok/s"
 QSA_METRIC = "decode tok/s @110 sessions, 64k contexts, QSA top-32 x 64-token blocks (spec K=4)"
 QSA_BASELINE_TOKS = 1461.0  # reference, HiSparse + session cache, 110 sessions (paper Table 10 / section 8.2)
