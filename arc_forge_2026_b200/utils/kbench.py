@@ -201,6 +201,28 @@ def bench_grouped(E=320, T=16384, k=10, H=2048, I=512, seed=0):
     return res
 
 
+def bench_ple(T=16384, base=250_000, seed=0):
+    """PLE lookup of one packed 16k-token row: 16 heads (2- and 3-grams x 8) of 160 e4m3 dims from a table of
+    ~4M rows (a quarter-size stand-in of the 20M-bucket heads; the gather is random either way)."""
+    from ..config import preset
+    from ..models.ple import NgramHash
+    from ..ops.ple import PleTable
+    peaks = load_peaks()
+    dev = "cuda"
+    cfg = preset("tiny_cpu", vocab_size=248320, ple_layer_ids=(1,), ngram_vocab_size_base=base, ple_embed_dim=2560)
+    h = NgramHash(cfg)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    rows = torch.randint(-120, 120, (h.rows, 160), generator=g, device=dev, dtype=torch.int8).view(torch.float8_e4m3fn)
+    scale = torch.full(((h.rows + 127) // 128, 2), 0.01, device=dev)
+    table = PleTable(h, rows, scale)
+    toks = torch.randint(0, cfg.vocab_size, (T,), generator=g, device=dev)
+    seg = torch.zeros(T, dtype=torch.long, device=dev)
+    ms = time_cuda(lambda: table.lookup_tokens(toks, seg), flush_bytes=1 << 20)
+    byts = T * 16 * (160 + 320) + T * 16 * 4  # e4m3 rows read, bf16 rows written, scales
+    return [{"kernel": "ple_lookup", "T": T, "table_rows": h.rows, "ms": round(ms, 4), "bytes": byts,
+             "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)}]
+
+
 def bench_gdn_scan(BH=32, n=256, steps=(False, True)):
     """Inter-chunk scan of one GDN layer at seq 16,384 (256 chunks of 64), 32 value heads, Dk = Dv = 128: the
     tensor-core kernel and the fp32 SIMT kernel, forward and reverse (the reverse adds the Qm term)."""
@@ -264,7 +286,7 @@ def bench_gdn_train(B=1, T=16384, Hk=16, Hv=32):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "grouped", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "grouped", "ple", "all"])
     ap.add_argument("--T", type=int, default=640)
     ap.add_argument("--S", type=int, default=128, help="sessions of the attn case")
     ap.add_argument("--seq", type=int, default=16384, help="sequence length of the gdn_scan / gdn_train cases")
@@ -280,6 +302,8 @@ def main():
         res += bench_attn(S=a.S)
     if a.what in ("gdn_scan", "all"):
         res += bench_gdn_scan(n=(a.seq + 63) // 64)
+    if a.what in ("ple", "all"):
+        res += bench_ple()
     if a.what in ("grouped", "all"):
         res += bench_grouped()
     if a.what in ("gdn_train", "all"):
