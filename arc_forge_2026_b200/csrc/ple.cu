@@ -15,7 +15,8 @@
 // reduce-scatter of rows. A hot (compact) table maps each head's kept buckets through a sorted index (binary
 // search); a miss reads zeros.
 //
-// One warp per (row, head): every lane computes the hash (a few integer ops), then lane l copies 16 table bytes.
+// One warp per token: lane h hashes head h (the 64-bit modulo of each head runs once, in parallel across lanes),
+// then the 32 lanes copy the token's heads x 16-byte chunks, each taking its head's row id by a shuffle.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -29,51 +30,57 @@ AFB_DEV int64_t wrap_mul(int64_t a, int64_t b) {
 
 template <bool FP8>
 __global__ void __launch_bounds__(256) ple_lookup_kernel(PleLookupArgs a) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // one warp per token
   const int lane = threadIdx.x & 31;
-  const int heads = (a.n - 1) * a.hpn;
-  if (warp >= a.rows * heads) return;
-  const int r = warp / heads, h = warp % heads;
-  const int order = 2 + h / a.hpn;
+  const int heads = (a.n - 1) * a.hpn;  // <= 32 (checked at launch): lane h hashes head h
+  if (r >= a.rows) return;
   const int64_t p = a.pos[r];
   const int64_t seg = a.seg[r];
   const bool bad = p < 0 || p >= a.ext_len || seg < 0 || seg > p;
   if (bad && lane == 0) flag_error(a.status, AFB_ERR_BOUNDS);  // bad index: recorded, the row reads zeros
-  int64_t mix = bad ? 0 : wrap_mul((int64_t)a.ext[p], a.mult[0]);
-  bool ok = !bad;
-  for (int s = 1; s < order && !bad; ++s) {
-    const int64_t q = p - s;
-    ok = ok && q >= seg && a.ext[q] != a.eos;
-    const int64_t tok = ok ? (int64_t)a.ext[q] : (int64_t)a.eos;
-    mix ^= wrap_mul(tok, a.mult[s]);
-  }
-  int64_t m = mix % a.mod[h];
-  if (m < 0) m += a.mod[h];
-  int64_t row = bad ? -1 : m + a.off[h];
-  if (a.hot_idx && !bad) {  // compact table: binary search of the bucket among this head's kept ones
-    const int64_t* b = a.hot_idx + a.hot_base[h];
-    int lo = 0, hi = a.hot_len[h];
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (b[mid] < m) lo = mid + 1; else hi = mid;
+  long long row = -1;
+  if (lane < heads && !bad) {
+    const int h = lane;
+    const int order = 2 + h / a.hpn;
+    int64_t mix = wrap_mul((int64_t)a.ext[p], a.mult[0]);
+    bool ok = true;
+    for (int s = 1; s < order; ++s) {
+      const int64_t q = p - s;
+      ok = ok && q >= seg && a.ext[q] != a.eos;
+      mix ^= wrap_mul(ok ? (int64_t)a.ext[q] : (int64_t)a.eos, a.mult[s]);
     }
-    row = (lo < a.hot_len[h] && b[lo] == m) ? a.hot_base[h] + lo : -1;
+    int64_t m = mix % a.mod[h];
+    if (m < 0) m += a.mod[h];
+    row = m + a.off[h];
+    if (a.hot_idx) {  // compact table: binary search of the bucket among this head's kept ones
+      const int64_t* b = a.hot_idx + a.hot_base[h];
+      int lo = 0, hi = a.hot_len[h];
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (b[mid] < m) lo = mid + 1; else hi = mid;
+      }
+      row = (lo < a.hot_len[h] && b[lo] == m) ? a.hot_base[h] + lo : -1;
+    }
   }
+  if (a.ids_out && lane < heads) a.ids_out[(int64_t)r * heads + lane] = row;
   const int D = a.head_dim;
-  bf16* out = reinterpret_cast<bf16*>(a.out) + (int64_t)r * heads * D + (int64_t)h * D;
-  if (a.ids_out && lane == 0) a.ids_out[(int64_t)r * heads + h] = row;
-  const int chunks = FP8 ? D / 16 : D / 8;  // 16-byte chunks of the table row
-  for (int c = lane; c < chunks; c += 32) {
+  const int C = FP8 ? D / 16 : D / 8;  // 16-byte chunks of one table row
+  bf16* out = reinterpret_cast<bf16*>(a.out) + (int64_t)r * heads * D;
+  for (int base = 0; base < heads * C; base += 32) {  // uniform trip count: every lane joins each shuffle
+    const int t = base + lane;
+    const int h = min(t / C, heads - 1), c = t % C;
+    const long long rh = __shfl_sync(0xffffffffu, row, h);
+    if (t >= heads * C) continue;
     uint4 o0, o1;
-    if (row < 0 || row >= a.table_rows) {
+    if (rh < 0 || rh >= a.table_rows) {
       o0 = make_uint4(0, 0, 0, 0);
       o1 = o0;
     } else {
-      const int shard = (int)(row / a.rows_per_shard);
-      const int64_t lr = row - (int64_t)shard * a.rows_per_shard;
+      const int shard = (int)(rh / a.rows_per_shard);
+      const int64_t lr = rh - (int64_t)shard * a.rows_per_shard;
       if (FP8) {
-        const uint8_t* t = reinterpret_cast<const uint8_t*>(a.shards[shard]) + lr * D + c * 16;
-        const uint4 v = *reinterpret_cast<const uint4*>(t);
+        const uint8_t* tp = reinterpret_cast<const uint8_t*>(a.shards[shard]) + lr * D + c * 16;
+        const uint4 v = *reinterpret_cast<const uint4*>(tp);
         const float sc = a.scale_shards[shard][(lr / 128) * a.scale_ld + (c * 16) / 128];
         const __nv_fp8x4_e4m3* e = reinterpret_cast<const __nv_fp8x4_e4m3*>(&v);
         float f[16];
@@ -90,24 +97,26 @@ __global__ void __launch_bounds__(256) ple_lookup_kernel(PleLookupArgs a) {
         o1 = make_uint4(pack_bf16x2(f[8], f[9]), pack_bf16x2(f[10], f[11]), pack_bf16x2(f[12], f[13]),
                         pack_bf16x2(f[14], f[15]));
       } else {
-        const bf16* t = reinterpret_cast<const bf16*>(a.shards[shard]) + lr * D + c * 8;
-        o0 = *reinterpret_cast<const uint4*>(t);
+        const bf16* tp = reinterpret_cast<const bf16*>(a.shards[shard]) + lr * D + c * 8;
+        o0 = *reinterpret_cast<const uint4*>(tp);
       }
     }
+    bf16* dst = out + (int64_t)h * D;
     if (FP8) {
-      reinterpret_cast<uint4*>(out + c * 16)[0] = o0;
-      reinterpret_cast<uint4*>(out + c * 16)[1] = o1;
+      reinterpret_cast<uint4*>(dst + c * 16)[0] = o0;
+      reinterpret_cast<uint4*>(dst + c * 16)[1] = o1;
     } else {
-      reinterpret_cast<uint4*>(out + c * 8)[0] = o0;
+      reinterpret_cast<uint4*>(dst + c * 8)[0] = o0;
     }
   }
 }
 }  // namespace pled
 
 int ple_lookup(const PleLookupArgs& a, bool fp8, cudaStream_t st) {
-  if (a.n < 2 || a.n > 8 || a.hpn < 1 || a.head_dim % 16 || a.rows_per_shard <= 0 || a.rows_per_shard % 128)
+  if (a.n < 2 || a.n > 8 || a.hpn < 1 || (a.n - 1) * a.hpn > 32 || a.head_dim % 16 || a.rows_per_shard <= 0 ||
+      a.rows_per_shard % 128)
     return 3;
-  const int64_t warps = (int64_t)a.rows * (a.n - 1) * a.hpn;
+  const int64_t warps = a.rows;
   if (warps == 0) return 0;
   const int64_t blocks = (warps * 32 + 255) / 256;
   if (fp8)
