@@ -88,8 +88,11 @@ def test_gradient_accumulation_matches_one_batch():
 
 def test_kernel_registry_counts_and_rejects_fallbacks():
     from arc_forge_2026_b200.train import kernels
-    old = set(kernels.NAMES)
+    old = {n for n in kernels.NAMES if kernels.enabled(n)}
     try:
+        everything = kernels.enable("all")
+        assert "grouped_gemm" in kernels.OPT_IN and not everything & kernels.OPT_IN and "gdn_chunk" in everything
+        assert "grouped_gemm" in kernels.enable("gdn_chunk,grouped_gemm")  # opt-in kernels run when named
         assert kernels.enable("rms_norm,swiglu") == {"rms_norm", "swiglu"}
         assert kernels.use("rms_norm") and not kernels.use("gdn_chunk")
         kernels.reset()
