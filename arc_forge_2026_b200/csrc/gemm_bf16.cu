@@ -261,12 +261,13 @@ static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, in
   return (int)cudaGetLastError();
 }
 
-// Grouped launch (one tile width: 128; no split-K). A ROWS grid covers max_tiles m-tiles (an upper bound of
+// Grouped launch (one tile width: 256; no split-K). A ROWS grid covers max_tiles m-tiles (an upper bound of
 // sum ceil(rows_e / 128)); a REDUCE grid covers E x ceil(group_rows / 128).
 int gemm_bf16_grouped(const void* A, int lda, int rows_a, const void* B, int ldb, int rows_b, int N, int K,
                       const GemmEpilogue& epi, const GemmGroups& g, int max_tiles, uint32_t* status,
                       cudaStream_t stream) {
-  constexpr int BN = 128, STAGES = 3;
+  constexpr int BN = 256, STAGES = 4;  // 128 x 256 tiles: half the CTAs of 128-wide ones (each CTA's setup and
+                                       // pipeline fill is paid once per tile; REDUCE tiles have few K blocks)
   using S = GemmSmem<BN, STAGES>;
   if (g.mode != 1 && g.mode != 2) return 3;
   if ((K % 8) || (lda % 8) || (ldb % 8) || (N % 8) || epi.partial) return 3;

@@ -265,6 +265,10 @@ int ep_gather(const EpArgs& a, const int* row_token, const int* nrows_dev, int r
 
 // hc.cu: hyper-connection residual stream [rows, G, H] (bf16): grouped norm, branch mix, gated write-back, and
 // their dX-only backward; H in {256, 512, 1024, 2048, 2560}, G <= 8
+// ---- batched bf16 transpose with an optional row -> column remap (train_kernels.cu)
+int transpose_bf16(const void* src, int64_t R, int64_t C, int64_t lds, int64_t batch, int64_t src_batch,
+                   const int64_t* dst, void* out, int64_t ldo, int64_t out_batch, cudaStream_t st);
+
 // ---- LoRA adapter products (lora.cu): R in {8, 16, 32, 64}; the small operand is fp32 (split into bf16 hi + lo)
 int lora_rows_times(const void* P, int64_t ldp, const float* W, int T, int K, int R, float* out, cudaStream_t st);
 int lora_tgrad(const void* P, int64_t ldp, const float* Q, int T, int M, int R, int splits, float* part, float* out,

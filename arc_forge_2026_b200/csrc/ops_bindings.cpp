@@ -860,6 +860,27 @@ static void hc_shape(const at::Tensor& h, int64_t& rows, int& G, int& H) {
   G = h.size(-2);
   rows = h.numel() / ((int64_t)G * H);
 }
+// out[b, c, dst[r]] = src[b, r, c]: src [B, R, C] (or [R, C]) bf16 rows of unit inner stride, out [B, C, ldo]
+void transpose_bf16_op(const at::Tensor& src, c10::optional<at::Tensor> dst, at::Tensor& out) {
+  AFB_CHECK_DT(src, at::kBFloat16);
+  AFB_CHECK_DT(out, at::kBFloat16);
+  AFB_CHECK_CONTIG(out);
+  TORCH_CHECK(src.stride(-1) == 1 && (src.dim() == 2 || src.dim() == 3) && out.dim() == src.dim(), "transpose shapes");
+  const int64_t B = src.dim() == 3 ? src.size(0) : 1;
+  const int64_t R = src.size(-2), C = src.size(-1);
+  TORCH_CHECK(out.size(-2) == C && (src.dim() == 2 || out.size(0) == B), "transpose: out rows must be src columns");
+  const int64_t ldo = out.size(-1);
+  if (dst) {
+    AFB_CHECK_DT(dst.value(), at::kLong);
+    TORCH_CHECK(dst->numel() == R, "transpose: dst has one column per source row");
+  } else {
+    TORCH_CHECK(ldo >= R, "transpose: out too narrow");
+  }
+  check_rc(afb::transpose_bf16(src.data_ptr(), R, C, src.stride(-2), B, src.dim() == 3 ? src.stride(0) : 0,
+                               dst ? dst->data_ptr<int64_t>() : nullptr, out.data_ptr(), ldo, C * ldo, stream()),
+           "transpose_bf16");
+}
+
 // LoRA: rows_times(P [T, K] bf16, W [R, K] fp32) -> [T, R] fp32; tgrad(P [T, M] bf16, Q [T, R] fp32) -> [M, R] fp32
 at::Tensor lora_rows_times_op(const at::Tensor& P, const at::Tensor& W) {
   AFB_CHECK_DT(P, at::kBFloat16);
@@ -1160,6 +1181,7 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("gdn_train", &gdn_train_op);
   m.def("ple_lookup", &ple_lookup_op);
   m.def("lora_rows_times", &lora_rows_times_op);
+  m.def("transpose_bf16", &transpose_bf16_op, py::arg("src"), py::arg("dst"), py::arg("out"));
   m.def("lora_tgrad", &lora_tgrad_op);
   m.def("hc_norm", &hc_norm_op);
   m.def("hc_mix", &hc_mix_op);

@@ -325,3 +325,45 @@ int adamw(float* p, const float* g, void* m, void* v, void* w, size_t n, float l
 }
 
 }  // namespace afb
+
+namespace afb {
+// ------------------------------------------------------------------------------------------ tiled transpose
+// out[b][col_map(c)... ] : out[b][c][dst(r)] = src[b][r][c] for a batch of [R, C] bf16 matrices, through 64 x 64
+// shared-memory tiles (reads and writes coalesced). dst (optional, [R]) remaps rows of src to columns of out: the
+// grouped expert GEMM's dW operands are the activations transposed into 64-row-aligned expert segments.
+namespace tpd {
+constexpr int TILE = 64;
+}
+__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, int64_t R,
+                                                             int64_t C, int64_t lds, int64_t src_batch,
+                                                             const int64_t* __restrict__ dst,
+                                                             __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                                             int64_t out_batch) {
+  __shared__ __nv_bfloat16 t[tpd::TILE][tpd::TILE + 2];
+  const int64_t r0 = (int64_t)blockIdx.y * tpd::TILE, c0 = (int64_t)blockIdx.x * tpd::TILE;
+  const __nv_bfloat16* s = src + (int64_t)blockIdx.z * src_batch;
+  __nv_bfloat16* o = out + (int64_t)blockIdx.z * out_batch;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4 threads
+  for (int i = ty; i < tpd::TILE; i += 4) {
+    const int64_t r = r0 + i, c = c0 + tx;
+    t[i][tx] = (r < R && c < C) ? s[r * lds + c] : __float2bfloat16(0.f);
+  }
+  __syncthreads();
+  const int64_t r = r0 + tx;
+  if (r >= R) return;
+  const int64_t col = dst ? dst[r] : r;
+  for (int i = ty; i < tpd::TILE; i += 4) {
+    const int64_t c = c0 + i;
+    if (c < C) o[c * ldo + col] = t[tx][i];
+  }
+}
+
+int transpose_bf16(const void* src, int64_t R, int64_t C, int64_t lds, int64_t batch, int64_t src_batch,
+                   const int64_t* dst, void* out, int64_t ldo, int64_t out_batch, cudaStream_t st) {
+  if (R <= 0 || C <= 0 || batch <= 0) return 0;
+  dim3 grid((unsigned)((C + tpd::TILE - 1) / tpd::TILE), (unsigned)((R + tpd::TILE - 1) / tpd::TILE), (unsigned)batch);
+  transpose_bf16_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(src), R, C, lds, src_batch, dst,
+                                              reinterpret_cast<__nv_bfloat16*>(out), ldo, out_batch);
+  return (int)cudaGetLastError();
+}
+}  // namespace afb

@@ -48,12 +48,23 @@ def grouped_reduce(dy: torch.Tensor, x: torch.Tensor, counts: torch.Tensor) -> t
     rows = (R + 64 * E + 63) // 64 * 64  # upper bound of the padded rows (no host sync); 16-byte row pitch
     owner = torch.repeat_interleave(torch.arange(E, device=dev), counts, output_size=R)
     dst = (torch.arange(R, device=dev) - seg[owner] + pseg[owner]).long()
-    xp = torch.zeros(rows, K, dtype=_BF, device=dev)
-    dyp = torch.zeros(rows, N, dtype=_BF, device=dev)
-    xp.index_copy_(0, dst, x.to(_BF))
-    dyp.index_copy_(0, dst, dy.to(_BF))
+    c = C()
+    # X^T and dY^T with every expert's rows at its 64-aligned column segment (one native transpose each)
+    xt = torch.zeros(K, rows, dtype=_BF, device=dev)
+    dyt = torch.zeros(N, rows, dtype=_BF, device=dev)
+    c.transpose_bf16(x.to(_BF).contiguous(), dst, xt)
+    c.transpose_bf16(dy.to(_BF).contiguous(), dst, dyt)
     out = torch.empty(E, N, K, dtype=_BF, device=dev)
-    C().gemm_grouped(dyp.t().contiguous(), xp.t().contiguous(), pseg, None, 2, N, 0, out)
+    c.gemm_grouped(dyt, xt, pseg, None, 2, N, 0, out)
+    return out
+
+
+def transposed_bank(w: torch.Tensor) -> torch.Tensor:
+    """[E, N, K] bf16 -> [E, K, N] (native tiled transpose)."""
+    from ..ops import C
+    E, N, K = w.shape
+    out = torch.empty(E, K, N, dtype=_BF, device=w.device)
+    C().transpose_bf16(w.contiguous(), None, out)
     return out
 
 
@@ -68,6 +79,6 @@ class GroupedLinear(torch.autograd.Function):
     def backward(ctx, dy):
         xb, wb, counts = ctx.saved_tensors
         dy = dy.to(_BF).contiguous()
-        dx = grouped_rows(dy, wb.transpose(1, 2).contiguous(), counts) if ctx.needs_input_grad[0] else None
+        dx = grouped_rows(dy, transposed_bank(wb), counts) if ctx.needs_input_grad[0] else None
         dw = grouped_reduce(dy, xb, counts) if ctx.needs_input_grad[1] else None
         return dx, dw, None

@@ -175,7 +175,7 @@ def bench_attn(S=128, T=5, seed=0):
 def bench_grouped(E=320, T=16384, k=10, H=2048, I=512, seed=0):
     """Grouped expert GEMMs of one QAD layer (w13: K=H, N=2I; w2: K=I, N=H; routed rows T*k): the native grouped
     tcgen05 GEMM (forward, dX, dW) against torch._grouped_mm."""
-    from ..train.grouped import grouped_reduce, grouped_rows
+    from ..train.grouped import grouped_reduce, grouped_rows, transposed_bank
     dev = "cuda"
     g = torch.Generator(device=dev).manual_seed(seed)
     ids = torch.randint(0, E, (T * k,), generator=g, device=dev)
@@ -189,7 +189,7 @@ def bench_grouped(E=320, T=16384, k=10, H=2048, I=512, seed=0):
         cases = {
             "fwd_native": lambda: grouped_rows(x, w, counts),
             "fwd_library": lambda: torch._grouped_mm(x, w.transpose(-2, -1), offs=offs),
-            "dx_native": lambda: grouped_rows(dy, w.transpose(1, 2).contiguous(), counts),
+            "dx_native": lambda: grouped_rows(dy, transposed_bank(w), counts),
             "dx_library": lambda: torch._grouped_mm(dy, w, offs=offs),
             "dw_native": lambda: grouped_reduce(dy, x, counts),
             "dw_library": lambda: torch._grouped_mm(dy.t(), x, offs=offs),
