@@ -51,3 +51,38 @@ def test_package_detects_tampering(tmp_path):
     f.write_bytes(bytes(data))
     with pytest.raises(RuntimeError, match="sha256"):
         read_package(d)
+
+
+def test_package_round_trip_of_hyper_connections_and_ple(tmp_path):
+    """A model with 2 hyper-connection branches and a PLE layer: the package carries the HC projections (bf16), the
+    PLE table (block FP8) and the PLE projections / norms / conv, and the serving model loaded from it (on the CPU:
+    loading runs no kernel) holds the reference's values."""
+    import torch
+    from arc_forge_2026_b200.config import preset
+    from arc_forge_2026_b200.formats.int3_package import package_tensors, write_package
+    from arc_forge_2026_b200.models.hybrid import HybridModel
+    from arc_forge_2026_b200.models.reference import build_reference
+    from arc_forge_2026_b200.quant.fp8 import dequant_weight_block, quantize_weight_block
+    from arc_forge_2026_b200.quant.gptq import rtn_quantize
+    cfg = preset("tiny_cpu", hc_count=2, hc_lowrank=32, ple_layer_ids=(1,), ngram_vocab_size_base=997,
+                 ple_embed_dim=256)
+    ref = build_reference(cfg, seed=3)
+    cs = []
+    for moe in ref.moe_layers():
+        c13, s13 = rtn_quantize(moe.w13.detach().float())
+        c2, s2 = rtn_quantize(moe.w2.detach().float())
+        cs.append((c13, s13, c2, s2))
+    d = write_package(package_tensors(ref, cs, dense_fp8=False), cfg, tmp_path / "pkg", dense_fp8=False)
+    m = HybridModel.from_package(d, "cpu")
+    assert m.cfg.hc_count == 2 and m.cfg.ple_layer_ids == (1,)
+    hc = ref.layers[0].hc_attn
+    R = hc.w_down.shape[0]
+    assert torch.equal(m.layers[0].hc_attn.wcat[:R], hc.w_down.detach().bfloat16())
+    assert torch.equal(m.layers[0].hc_attn.wcat[R:R + 2], hc.w_inject.detach().bfloat16())
+    assert m.layers[0].hc_attn.wcat.shape[0] % 8 == 0 and m.hc_final is not None and not m.hc_final.inject
+    lw = m.layers[1].ple
+    assert lw is not None and m.layers[0].ple is None
+    q, s = quantize_weight_block(ref.layers[1].ple.table.detach().float())
+    assert torch.equal(dequant_weight_block(lw.table.rows, lw.table.scale), dequant_weight_block(q, s))
+    assert torch.equal(lw.conv, ref.layers[1].ple.conv.detach().float())
+    assert torch.equal(lw.key_proj, ref.layers[1].ple.key_proj.detach().bfloat16())
