@@ -497,11 +497,8 @@ static int launch_attn(const AttnArgs& a, int splits, uint32_t* status, cudaStre
                                          reinterpret_cast<uintptr_t>(a.vscale)) % 16) {
     return 5;  // bulk copies need 16-byte aligned sources
   }
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(paged_attn_kernel<D, FP4>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)paged_attn_kernel<D, FP4>, S::TOTAL)) return e;
   dim3 grid(a.num_seqs * a.Hkv, splits);
   paged_attn_kernel<D, FP4><<<grid, 256, S::TOTAL, st>>>(tk, tv, a, status);
   rc = (int)cudaGetLastError();

@@ -15,6 +15,10 @@
 //    current); make that first call before any stream capture;
 //  * all calls share the one array and it keeps the previous call's contents: every partial a call reads is
 //    written by the same call first, and calls that overlap on the GPU (other streams, other threads) race;
+//  * a bounded wait inside the attention kernel that gives up (a TMA page copy that never lands) sets a bit in a
+//    second fixed device word instead of faulting; the call itself has already returned 0 by then, so after
+//    synchronising the stream read the word with afb_paged_attention_noalloc_status (0 = every call since the last
+//    reset finished its waits; any other value means some output of those calls is not valid);
 //  * it allocates nothing: no cudaMalloc, no cudaFree, no allocating library routine.
 #pragma once
 #include <cuda_runtime.h>
@@ -28,6 +32,8 @@ extern "C" {
 #define AFB_ATTN_NOALLOC_BAD_ARGS (-1)
 #define AFB_ATTN_NOALLOC_TOO_LARGE (-2)
 #define AFB_ATTN_NOALLOC_SETUP_FAILED (-3)
+#define AFB_ATTN_NOALLOC_TMAP_FAILED (-4)    // the K/V cache could not be described to the TMA unit (alignment)
+#define AFB_ATTN_NOALLOC_UNSUPPORTED (-5)    // the launcher refused a shape the argument check let through
 
 typedef struct afb_attn_noalloc_params {
   const void* q;            // bf16 [num_seqs * q_per_seq, Hq, D]
@@ -46,8 +52,15 @@ typedef struct afb_attn_noalloc_params {
   void* out;                // bf16 [num_seqs * q_per_seq, Hq, D]
 } afb_attn_noalloc_params;
 
-// Returns AFB_ATTN_NOALLOC_OK, a negative AFB_ATTN_NOALLOC_* code, or a positive launch error code.
+// Returns AFB_ATTN_NOALLOC_OK, a negative AFB_ATTN_NOALLOC_* code, or a positive cudaError_t from the launch.
+// Argument errors (D not 128 or 256, Hq not a multiple of Hkv, more than 64 query rows per KV head and sequence,
+// i.e. q_per_seq * Hq / Hkv > 64, null pointers) return AFB_ATTN_NOALLOC_BAD_ARGS before anything is launched.
 int afb_paged_attention_noalloc(const afb_attn_noalloc_params* p, cudaStream_t stream);
+
+// Reads the current device's kernel status word into *status (0 = clean) and clears it when `reset` is non-zero.
+// Synchronous (it copies one word from the device): call it after the attention calls' stream has finished.
+// Returns 0, AFB_ATTN_NOALLOC_SETUP_FAILED or a positive cudaError_t.
+int afb_paged_attention_noalloc_status(unsigned int* status, int reset);
 
 #ifdef __cplusplus
 }

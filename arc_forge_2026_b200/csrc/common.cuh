@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define AFB_DEV __device__ __forceinline__
 
 // status word bits (written with atomicOr; read by the host after a launch)
@@ -26,6 +28,21 @@
 #endif
 
 namespace afb {
+
+// Raise a kernel's dynamic shared-memory limit once per device. The attribute belongs to the current device's
+// context, so every GPU a process launches on needs its own call; `done` (one per call site) keeps a bit per
+// device. Returns 0 or the cudaError_t of the failed call.
+inline int smem_attr_once(std::atomic<uint64_t>& done, const void* fn, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return 0;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return (int)e;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return 0;
+}
 
 AFB_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 

@@ -372,11 +372,8 @@ int expert_sort(const int* ids, int n, int E, const int* expert_map, int* offset
                 int* entry_row, int k, int pad, cudaStream_t st) {
   const size_t smem = (size_t)(34 * E + 32) * sizeof(int);
   if (smem > 200 * 1024) return 3;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(expert_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)expert_sort_kernel, 200 * 1024)) return e;
   expert_sort_kernel<<<1, 1024, smem, st>>>(ids, n, E, expert_map, offsets, row_token, row_entry, entry_row, k,
                                               pad < 1 ? 1 : pad);
   return (int)cudaGetLastError();

@@ -374,11 +374,8 @@ int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cuda
     gdn_conv_prep_kernel<128><<<dim3(a.num_seqs, C / 128), 128, 0, st>>>(a, parity);
     if (!a.commit_current && a.max_q <= gdnp::MAXT && a.max_q % 2 == 0 && a.num_seqs <= gdnp::MAXS && num_sms > 0) {
       const size_t smem = sizeof(gdnp::Smem) + 128;
-      static bool attr = false;
-      if (!attr) {
-        cudaFuncSetAttribute(gdn_verify_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-      }
+      static std::atomic<uint64_t> attr_devs{0};
+      if (const int e = smem_attr_once(attr_devs, (const void*)gdn_verify_persistent_kernel, (int)smem)) return e;
       const int items = a.num_seqs * a.Hv;
       gdn_verify_persistent_kernel<<<items < num_sms ? items : num_sms, gdnp::THREADS, smem, st>>>(a, parity, status);
       return (int)cudaGetLastError();

@@ -160,11 +160,8 @@ __global__ void __launch_bounds__(gck::THREADS) gdn_chunk_scan_kernel(GdnScanArg
 template <bool REV, int DK>
 static int launch_scan(const GdnScanArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(gck::Smem<DK>) + 16;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(gdn_chunk_scan_kernel<REV, DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)gdn_chunk_scan_kernel<REV, DK>, (int)smem)) return e;
   gdn_chunk_scan_kernel<REV, DK><<<dim3(a.BH, a.Dv / gck::SL), gck::THREADS, smem, st>>>(a);
   return (int)cudaGetLastError();
 }
@@ -410,11 +407,8 @@ __global__ void __launch_bounds__(gct::THREADS) gdn_chunk_scan_tc_kernel(GdnScan
 template <bool REV>
 static int launch_scan_tc(const GdnScanArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(gct::Smem) + 128;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(gdn_chunk_scan_tc_kernel<REV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)gdn_chunk_scan_tc_kernel<REV>, (int)smem)) return e;
   gdn_chunk_scan_tc_kernel<REV><<<dim3(a.BH, a.Dv / gct::SL), gct::THREADS, smem, st>>>(a);
   return (int)cudaGetLastError();
 }

@@ -251,11 +251,8 @@ static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, in
   rc = make_tmap_2d(&tb, B, 2, K, N, (uint64_t)ldb * 2, S::BK, BN, 1);
   if (rc) return 2000 + rc;
   auto kern = gemm_bf16_tn_kernel<BN, STAGES>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)kern, S::TOTAL)) return e;
   dim3 grid((M + S::BM - 1) / S::BM, (N + BN - 1) / BN, splits);
   kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, M, N, K, epi, status, GemmGroups());
   return (int)cudaGetLastError();
@@ -280,20 +277,14 @@ int gemm_bf16_grouped(const void* A, int lda, int rows_a, const void* B, int ldb
   dim3 grid;
   if (g.mode == 1) {
     auto kern = gemm_bf16_tn_kernel<BN, STAGES, 1>;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-      attr = true;
-    }
+    static std::atomic<uint64_t> attr_devs{0};
+    if (const int e = smem_attr_once(attr_devs, (const void*)kern, S::TOTAL)) return e;
     grid = dim3(max_tiles, (N + BN - 1) / BN, 1);
     kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, rows_a, N, K, epi, status, g);
   } else {
     auto kern = gemm_bf16_tn_kernel<BN, STAGES, 2>;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-      attr = true;
-    }
+    static std::atomic<uint64_t> attr_devs{0};
+    if (const int e = smem_attr_once(attr_devs, (const void*)kern, S::TOTAL)) return e;
     grid = dim3(g.E * ((g.group_rows + S::BM - 1) / S::BM), (N + BN - 1) / BN, 1);
     kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, rows_a, N, K, epi, status, g);
   }

@@ -450,11 +450,8 @@ template <bool PAIR, bool F8>
 static int launch_moe(const CUtensorMap& tx, const CUtensorMap& tw, const MoeGemmArgs& a, int grid, uint32_t* status,
                       cudaStream_t st) {
   using L = moe::Layout<PAIR, F8>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(moe_int3_gemm_kernel<PAIR, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)moe_int3_gemm_kernel<PAIR, F8>, L::TOTAL)) return e;
   moe_int3_gemm_kernel<PAIR, F8><<<grid, moe::THREADS, L::TOTAL, st>>>(tx, tw, a, status);
   return (int)cudaGetLastError();
 }

@@ -277,11 +277,8 @@ int qsa_select(const QsaArgs& a, const QsaSelectArgs& sa, int S, uint32_t* statu
   const size_t smem = (size_t)qsa::MAXW * qsa::MAXH * qsa::DI * 4 + (size_t)qsa::MAXW * sa.max_blocks * 4 +
                       (size_t)sa.max_blocks * 4;
   if (smem > 220 * 1024) return 3;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(qsa_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)qsa_select_kernel, 220 * 1024)) return e;
   qsa_select_kernel<<<S, qsa::THREADS, smem, st>>>(a, sa, status);
   return (int)cudaGetLastError();
 }

@@ -48,8 +48,9 @@ def pack_uint3(codes: torch.Tensor) -> torch.Tensor:
 def unpack_uint3(qweight: torch.Tensor, k: int) -> torch.Tensor:
     """int32 [..., 3k/32] -> uint8 codes [..., k]."""
     if qweight.dtype != torch.int32 or k % 32 or qweight.shape[-1] * 32 != 3 * k:
-        raise ValueError(f"uint3 stream needs int32 [..., 3k/32] with k % 32 == 0, got {tuple(qweight.shape)} "
-                         f"for k={k}")
+        raise ValueError(f"cannot unpack {k} three-bit codes per row from a {qweight.dtype} tensor of shape "
+                         f"{tuple(qweight.shape)}: rows hold k codes in 3*k/32 int32 words, so k must be a "
+                         f"multiple of 32")
     lead = qweight.shape[:-1]
     w = qweight.reshape(-1, k // 32, 3).to(torch.int64) & 0xFFFFFFFF
     out = torch.empty(w.shape[0], k // 32, 32, dtype=torch.uint8, device=qweight.device)

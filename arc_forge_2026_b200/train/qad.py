@@ -122,6 +122,30 @@ def plan_hash(args) -> str:
     return hashlib.sha256(json.dumps({k: getattr(args, k) for k in keys}, sort_keys=True).encode()).hexdigest()[:16]
 
 
+def _start_profile(dev):
+    from torch.profiler import ProfilerActivity, profile
+    acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if dev.type == "cuda" else [])
+    prof = profile(activities=acts, record_shapes=True)
+    prof.__enter__()
+    return prof
+
+
+def _finish_profile(prof, out: Path, step: int, rank: int):
+    """Stop the profiler and write, for this rank, the op table sorted by device time (self and total), the same
+    grouped by input shape, and a Chrome trace. Profiled steps run slower: their tok/s is not a result."""
+    prof.__exit__(None, None, None)
+    out.mkdir(parents=True, exist_ok=True)
+    base = out / f"profile_step{step}_rank{rank}"
+    ka = prof.key_averages()
+    dev_key = "self_device_time_total" if torch.cuda.is_available() else "self_cpu_time_total"
+    tot_key = "device_time_total" if torch.cuda.is_available() else "cpu_time_total"
+    with open(f"{base}.txt", "w") as f:
+        f.write(ka.table(sort_by=dev_key, row_limit=60) + "\n")
+        f.write(ka.table(sort_by=tot_key, row_limit=60) + "\n")
+        f.write(prof.key_averages(group_by_input_shape=True).table(sort_by=dev_key, row_limit=60) + "\n")
+    prof.export_chrome_trace(f"{base}.trace.json")
+
+
 def save_checkpoint(path: Path, student: QADStudent, opt, step: int, phash: str, rank: int):
     """DCP checkpoint (``train/checkpoint.py``): masters once, optimizer moments by owned range, loadable at another
     world size."""
@@ -168,6 +192,11 @@ def main(argv=None):
     ap.add_argument("--targets", type=Path, help="qad-topk-v1 root (train/score)")
     ap.add_argument("--out", type=Path, help="teacher: targets root; train: checkpoint directory")
     ap.add_argument("--resume", action="store_true")
+    ap.add_argument("--save-every", dest="save_every", type=int, default=0,
+                    help="train: write a checkpoint every N steps (0: only after the last step)")
+    ap.add_argument("--profile-step", dest="profile_step", type=int, default=-1,
+                    help="profile this step with torch.profiler: device-time tables by op and by input shape and a "
+                         "Chrome trace, written under --out (or the working directory) as profile_step<N>.*")
     ap.add_argument("--fast-kernels", dest="fast_kernels", default="all",
                     help="native training kernels to use: all, none, or a comma list (train/kernels.py NAMES); on a "
                          "GPU the first step then fails if an enabled kernel fell back to PyTorch")
@@ -240,6 +269,7 @@ def main(argv=None):
         start = load_checkpoint(args.out, student, opt, phash, rank)
     for step in range(start, args.steps):
         ids, t = batch(step)
+        prof = _start_profile(dev) if step == args.profile_step else None
         t0 = time.perf_counter()
         if args.mode == "score":
             with torch.no_grad():
@@ -255,12 +285,15 @@ def main(argv=None):
         if dev.type == "cuda":
             torch.cuda.synchronize()
         dt = time.perf_counter() - t0
+        if prof is not None:
+            _finish_profile(prof, args.out or Path("."), step, rank)
         if rank == 0:
             print(json.dumps({"step": step, "loss": round(loss, 6), "grad_norm": round(norm, 4),
                               "tok_s": round(ids.numel() * world / dt, 1),
                               "peak_gib": round(torch.cuda.max_memory_allocated() / 2**30, 2)
                               if dev.type == "cuda" else None}), flush=True)
-        if args.out and args.mode == "train":
+        last = step == args.steps - 1
+        if args.out and args.mode == "train" and (last or (args.save_every > 0 and (step + 1) % args.save_every == 0)):
             save_checkpoint(args.out, student, opt, step + 1, phash, rank)
     if args.export and rank == 0:
         export(student, args.export, {"preset": args.preset, "plan": phash})

@@ -32,10 +32,14 @@ import sys
 import threading
 import time
 
-BASELINE_TOKS = 2141.0  # reference deployed stack, 128 sessions, DFlash K=4 (its paper, §8.3, p. 33)
 METRIC = "decode tok/s @128 sessions (8xB200, spec K=4); p50 TPOT; QAD train tok/s"
 QSA_METRIC = "decode tok/s @110 sessions, 64k contexts, QSA top-32 x 64-token blocks (spec K=4)"
-QSA_BASELINE_TOKS = 1461.0  # reference, HiSparse + session cache, 110 sessions (paper Table 10 / section 8.2)
+# The reference publishes no decode number for this model on B200: its 128-session figures (2,141 / 2,343 tok/s,
+# paper section 8.3 and Table 10) are for 4 x L4 over PCIe, so no published number is comparable and vs_baseline
+# stays null for the serving modes.
+SERVE_BASELINE_NOTE = ("no comparable published number: the reference's 128-session decode figures are 4xL4/PCIe "
+                       "(2,141 tok/s, paper section 8.3); its B200 figure is a 41 ms cycle for its own 2560-hidden "
+                       "HC4/PLE model at 64 sessions (paper App. E.11)")
 
 
 def _reference_arm(args):
@@ -258,6 +262,21 @@ def main():
         if world > 1:
             dist.barrier()
 
+    # The timed cycles sample the whole decode span: they run in G groups, group g starting with every session's
+    # context advanced by (g + 1/2) * out_tokens / G tokens (midpoints of G equal slices of the output), so the KV
+    # read per cycle averages over the span instead of its first tokens. The pages of the full span were
+    # allocated above; the jump is one device copy of the context lengths (and the QSA finalisation mark).
+    ctx_dev = ctx.int().to(dev)
+    G = 1 if scfg.hisparse else max(1, min(4, args.steps))
+    offsets = [int((g + 0.5) * args.out_tokens / G) for g in range(G)]
+
+    def at_offset(i, n):
+        g = i * G // n
+        if i == 0 or g != (i - 1) * G // n:
+            eng.ctx_len.copy_(ctx_dev + offsets[g])
+            if eng.qsa is not None:
+                eng.qsa.fin.copy_((ctx_dev + offsets[g]) // PAGE)
+
     # ---------------- device-timed: K graph replays
     for _ in range(args.warmup):
         eng.run_cycle()
@@ -270,6 +289,7 @@ def main():
     with ClockSampler(local) as clocks:
         ev[0].record()
         for i in range(args.steps):
+            at_offset(i, args.steps)
             eng.run_cycle()
             counts[i].copy_(eng.out_count)
             ev[i + 1].record()
@@ -296,7 +316,8 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_tokens = 0
     e0.record()
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        at_offset(i, args.steps)
         e_tokens += sum(len(v) for v in eng.step().values())
     e1.record()
     torch.cuda.synchronize()
@@ -331,7 +352,7 @@ def main():
         "metric": QSA_METRIC if qsa else METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
         "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": round(value / (QSA_BASELINE_TOKS if qsa else BASELINE_TOKS), 3), "dtype": "bf16",
+        "vs_baseline": None, "baseline_note": SERVE_BASELINE_NOTE, "dtype": "bf16",
         "data": f"synthetic (random-init weights; random tokens; contexts U[{args.min_ctx},{args.max_ctx}] as random "
                 f"KV/GDN/indexer state)",
         "config": {"model": "qwen3next_80b-shaped hybrid MoE, 48L, 320 experts top-10 INT3 g128 + shared; "
@@ -343,7 +364,9 @@ def main():
                    "attention": "QSA top-32 of 64-token blocks (+ local pages)" if qsa else "dense",
                    "kv_offload": ("HiSparse host pool " + ("e4m3" if args.hisparse_fp8 else "bf16"))
                    if scfg.hisparse else "none (all KV on the GPU)",
-                   "l2": "inputs larger than L2 (weights 24 GB, KV > 40 GB streamed every cycle)"},
+                   "l2": "inputs larger than L2 (weights 24 GB, KV > 40 GB streamed every cycle)",
+                   "decode_span": f"timed cycles in {G} groups at context + {offsets} of {args.out_tokens} output "
+                                  f"tokens"},
         "p50_tpot_ms": round(p50, 3) if p50 else None,
         "accepted_per_cycle": round(emitted / (args.steps * S_total), 3),
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -478,7 +501,9 @@ def qad_main(args):
     out = {
         "metric": QAD_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": round(value / QAD_BASELINE_TOKS, 3), "dtype": "bf16",
+        "scaling": "strong", "dtype": "bf16",
+        # the published 19.9k tok/s is a 4 x B200 figure: compared only at the same GPU count
+        "vs_baseline": round(value / QAD_BASELINE_TOKS, 3) if world == 4 else None,
         "data": "synthetic (random-init student; uniform random tokens; random valid top-k teacher targets)",
         "config": {"model": "qwen3next_80b-shaped student, 48L, 320 INT3 experts (STE scales), FP8 QAT dense",
                    "global_batch": args.global_batch, "seq_len": T, "parallelism": f"dp{world}+" + ("fused-zero-adamw" if type(opt).__name__ == "FusedShardedAdamW" else "sharded-adamw"),

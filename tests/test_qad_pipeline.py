@@ -109,3 +109,23 @@ def test_sharded_adamw_matches_single_process(tmp_path):
         opt.step()
     torch.testing.assert_close(got["p1"], p1.detach(), rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(got["p2"], p2.detach(), rtol=1e-5, atol=1e-6)
+
+
+def test_trainer_cli_save_interval_and_profile_step(tmp_path, monkeypatch):
+    """--save-every writes a checkpoint only every N steps (and after the last); --profile-step writes the op tables
+    and a Chrome trace of that one step."""
+    from arc_forge_2026_b200.train import qad as qad_mod
+    saved = []
+    real = qad_mod.save_checkpoint
+    monkeypatch.setattr(qad_mod, "save_checkpoint", lambda path, st, opt, step, ph, rank: (saved.append(step),
+                                                                                          real(path, st, opt, step, ph,
+                                                                                               rank)))
+    common = ["--preset", "tiny_cpu", "--seq-len", "32", "--batch", "1", "--topk", "8", "--synthetic"]
+    ck = tmp_path / "ckpt"
+    qad_mod.main(["--mode", "train", "--steps", "5", "--save-every", "2", "--profile-step", "1", "--out", str(ck)]
+                 + common)
+    assert saved == [2, 4, 5]
+    assert json.loads((ck / "trainer.json").read_text())["step"] == 5
+    table = (ck / "profile_step1_rank0.txt").read_text()
+    assert "aten::" in table
+    assert json.loads((ck / "profile_step1_rank0.trace.json").read_text())
