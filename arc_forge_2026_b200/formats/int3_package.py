@@ -157,13 +157,18 @@ def write_package(tensors: dict[str, torch.Tensor], cfg: ModelConfig, out_dir, s
                 "payload_bytes": sum(t.numel() * t.element_size() for t in tensors.values()),
                 "files": {f: {"bytes": (partial / f).stat().st_size, "sha256": _file_sha(partial / f)}
                           for f in files + ["config.json", "model.safetensors.index.json"]}, **(meta or {})}
-    (partial / "deploy_manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+    # the reference's byte form (json indent 2 + newline): RL overlays rebuild this file and hash it
+    (partial / "deploy_manifest.json").write_text(json.dumps(manifest, indent=2) + "\n")
     (partial / "DONE").write_text("")
     os.replace(partial, target)
     return target
 
 
-def read_package(pkg_dir, verify: bool = True) -> tuple[ModelConfig, dict[str, torch.Tensor]]:
+def read_package(pkg_dir, verify: bool = True, weight_patch=None,
+                 merged=None) -> tuple[ModelConfig, dict[str, torch.Tensor]]:
+    """(config, tensors) of a package. ``weight_patch``: a ``arcforge.kaggle.weight_patch.v1`` directory made against
+    this package, whose tensors replace the package's; ``merged``: a ``fn-lora-merged-v2`` directory whose tensors
+    replace the package's under the same names (what a server's update from disk loads)."""
     from safetensors.torch import load_file
     d = Path(pkg_dir)
     if not (d / "DONE").exists():
@@ -183,7 +188,36 @@ def read_package(pkg_dir, verify: bool = True) -> tuple[ModelConfig, dict[str, t
     tensors = {}
     for f in sorted(set(index["weight_map"].values())):
         tensors.update(load_file(str(d / f)))
+    if weight_patch is not None:
+        from .weight_patch import WeightPatch
+        tensors = WeightPatch(weight_patch, _file_sha(d / "deploy_manifest.json")).apply(tensors)
+    if merged is not None:
+        tensors = apply_merged(tensors, merged)
     return cfg, tensors
+
+
+def apply_merged(tensors: dict[str, torch.Tensor], merged_dir) -> dict[str, torch.Tensor]:
+    """``tensors`` with a published merged version's tensors substituted (same names, dtypes and shapes; every
+    merged tensor checked against the manifest's sha256)."""
+    from safetensors.torch import load_file
+    from .weight_patch import MERGED_FORMAT, tensor_sha
+    m = Path(merged_dir)
+    if not (m / "DONE").exists():
+        raise RuntimeError(f"{m} is not published (no DONE)")
+    man = json.loads((m / "merged_manifest.json").read_text())
+    if man.get("format") != MERGED_FORMAT:
+        raise ValueError(f"{m}: format {man.get('format')!r}")
+    new = load_file(str(m / "model.safetensors"))
+    out = dict(tensors)
+    for k, t in new.items():
+        if k not in out:
+            raise KeyError(f"{k} of {m} is not in the package")
+        if t.dtype != out[k].dtype or t.shape != out[k].shape:
+            raise ValueError(f"{k}: merged {t.dtype}{tuple(t.shape)}, package {out[k].dtype}{tuple(out[k].shape)}")
+        if tensor_sha(t) != man["keys"][k]["merged_sha256"]:
+            raise RuntimeError(f"{k}: bytes differ from {m}/merged_manifest.json")
+        out[k] = t
+    return out
 
 
 def dense_weight(tensors: dict[str, torch.Tensor], key: str, dtype=torch.bfloat16) -> torch.Tensor:

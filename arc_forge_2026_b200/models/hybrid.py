@@ -284,11 +284,12 @@ class HybridModel:
         return m
 
     @classmethod
-    def from_package(cls, pkg_dir, device, verify: bool = True):
+    def from_package(cls, pkg_dir, device, verify: bool = True, weight_patch=None, merged=None):
         """Load an INT3 deploy package (``formats/int3_package.py``): uint3 expert packs are re-tiled for the
-        expert GEMM, block-FP8 dense modules dequantised to bf16 for the dense GEMMs."""
+        expert GEMM, block-FP8 dense modules dequantised to bf16 for the dense GEMMs. ``weight_patch`` / ``merged``:
+        an RL weight patch or merged version served over the unchanged package (``read_package``)."""
         from ..formats.int3_package import dense_weight, expert_codes, read_package
-        cfg, t = read_package(pkg_dir, verify)
+        cfg, t = read_package(pkg_dir, verify, weight_patch=weight_patch, merged=merged)
         dev = torch.device(device)
         bf = dict(dtype=torch.bfloat16, device=dev)
         layers = []
@@ -327,6 +328,7 @@ class HybridModel:
                 t["lm_head.weight"].to(**bf), dev)
         if cfg.hc_count > 1:
             m.hc_final = _hc_from_package(t, "model.hc_final", cfg, dev)
+        m.pkg_dir = str(pkg_dir)
         return m
 
     def tensors(self):
@@ -350,9 +352,21 @@ class HybridModel:
     @torch.no_grad()
     def update_from_package(self, pkg_dir) -> dict:
         """Replace the weights by those of a deploy package of the same architecture, copying into the existing
-        tensors (addresses unchanged: captured CUDA graphs stay valid). Expert-parallel models keep their block of
-        experts. Raises before writing anything if any tensor differs in shape or dtype."""
-        new = HybridModel.from_package(pkg_dir, self.device)
+        tensors (addresses unchanged: captured CUDA graphs stay valid). ``pkg_dir`` may also be an RL weight patch
+        (``patch.json``) or a merged version (``merged_manifest.json``): it is then applied over the package this
+        model was loaded from. Expert-parallel models keep their block of experts. Raises before writing anything if
+        any tensor differs in shape or dtype."""
+        from pathlib import Path
+        d = Path(pkg_dir)
+        base = getattr(self, "pkg_dir", None)
+        if (d / "patch.json").exists() or (d / "merged_manifest.json").exists():
+            if base is None:
+                raise ValueError(f"{d} patches a package, but this model was not loaded from one")
+            kw = {"weight_patch": d} if (d / "patch.json").exists() else {"merged": d}
+            new = HybridModel.from_package(base, self.device, **kw)
+        else:
+            new = HybridModel.from_package(pkg_dir, self.device)
+            base = str(pkg_dir)
         if self.ep is not None:
             from ..parallel.ep import local_bank
             for lw in new.layers:
@@ -365,6 +379,7 @@ class HybridModel:
                 raise ValueError(f"{k}: {tuple(theirs[k].shape)} {theirs[k].dtype} vs {tuple(t.shape)} {t.dtype}")
         for k, t in mine.items():
             t.copy_(theirs[k])
+        self.pkg_dir = base
         return {"tensors": len(mine)}
 
     def nbytes(self) -> int:

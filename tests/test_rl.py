@@ -7,7 +7,7 @@ import torch
 import torch.nn.functional as F
 
 from arc_forge_2026_b200.config import preset
-from arc_forge_2026_b200.formats.weight_patch import apply_patch, write_patch
+from arc_forge_2026_b200.formats import weight_patch as wp
 from arc_forge_2026_b200.train.lora import attach_lora, export_merged, merged_tensors
 from arc_forge_2026_b200.train.routing_replay import RoutingReplay
 from arc_forge_2026_b200.train.student import random_student
@@ -38,33 +38,72 @@ def test_lora_identity_gradients_and_merge():
     ref = F.linear(x, layer.in_proj_ba + ad.delta())
     assert torch.allclose(y, ref, atol=1e-5)
     tensors, info = merged_tensors(st)
-    key = "model.layers.0.in_proj_ba.weight"
-    assert tensors[key].dtype == torch.bfloat16 and info[key]["changed"] > 0
-    assert tensors["model.layers.0.in_proj_qkvz.weight"].dtype == torch.float8_e4m3fn
-    assert "model.layers.0.in_proj_qkvz.weight_scale_inv" in tensors
+    key = "model.layers.0.linear_attn.in_proj_ba.weight"
+    assert tensors[key].dtype == torch.bfloat16 and info[key]["changed_elements"] > 0
+    assert info[key]["format"] == "bf16"
+    fk = "model.layers.0.linear_attn.in_proj_qkvz.weight"
+    assert tensors[fk].dtype == torch.float8_e4m3fn and info[fk]["format"] == "fp8_e4m3_block128"
+    assert info[fk]["scale_key"] == "model.layers.0.linear_attn.in_proj_qkvz.weight_scale_inv"
+    assert info[info[fk]["scale_key"]]["format"] == "fp32_scale_inv"
 
 
-def test_merged_export_and_weight_patch(tmp_path):
-    st = _student(1)
+def _package(tmp_path, seed=0):
+    from arc_forge_2026_b200.formats.int3_package import package_tensors, write_package
+    from arc_forge_2026_b200.models.reference import build_reference
+    from arc_forge_2026_b200.quant.gptq import rtn_quantize
+    from arc_forge_2026_b200.train.student import QADStudent
+    cfg = preset("tiny_cpu")
+    ref = build_reference(cfg, seed=seed)
+    cs = []
+    for moe in ref.moe_layers():
+        c13, s13 = rtn_quantize(moe.w13.detach().float())
+        c2, s2 = rtn_quantize(moe.w2.detach().float())
+        cs.append((c13, s13.bfloat16(), c2, s2.bfloat16()))
+    pkg = write_package(package_tensors(ref, cs), cfg, tmp_path / "pkg", shard_bytes=1 << 20)
+    return pkg, QADStudent(cfg, ref, cs, checkpoint_layers=False)
+
+
+def test_merged_export_overlay_and_weight_patch_in_the_reference_layout(tmp_path):
+    """A merged RL version -> overlay (arcforge.kaggle.model_overlay.v1) -> weight patch
+    (arcforge.kaggle.weight_patch.v1, per-shard patch-<shard> + patch.json): reading the package with the patch gives
+    exactly the merged tensors, the untouched tensors stay the package's, and a tampered base is refused."""
+    from arc_forge_2026_b200.formats.int3_package import read_package
+    pkg, st = _package(tmp_path)
     attach_lora(st, r=4, alpha=8.0)
     with torch.no_grad():
         for layer in st.layers:
             for ad in layer.lora.values():
-                ad.B.normal_(0, 0.01)
-    d = export_merged(st, tmp_path / "v000001", 1)
-    assert (d / "DONE").exists()
+                ad.B.normal_(0, 0.05)
+    d = export_merged(st, tmp_path / "v000003", 3, {"optimizer_step": 3, "run": "test"})
     man = json.loads((d / "merged_manifest.json").read_text())
-    assert man["format"] == "fn-lora-merged-v2" and man["weight_version"] == 1 and man["lora_rank"] == 4
+    assert man["format"] == "fn-lora-merged-v2" and man["weight_version"] == "3" and man["lora_rank"] == 4
+    assert man["tensors"] == len(man["keys"]) and all("merged_sha256" in e for e in man["keys"].values())
     with pytest.raises(FileExistsError):
-        export_merged(st, tmp_path / "v000001", 2)
-    base = {"a": torch.randn(4, 4).bfloat16(), "b": torch.randn(3).bfloat16(), "c": torch.zeros(2)}
-    new = dict(base, b=base["b"] + 1)
-    p = write_patch(base, new, tmp_path / "patch")
-    assert json.loads((p / "patch_manifest.json").read_text())["changed"] == 1
-    out = apply_patch(base, p)
-    assert torch.equal(out["b"], new["b"]) and out["a"] is base["a"]
-    with pytest.raises(RuntimeError):
-        apply_patch(dict(base, b=base["b"] * 2), p)
+        export_merged(st, tmp_path / "v000003", 4)
+    sha = wp.file_sha(pkg / "deploy_manifest.json")
+    ov = wp.build_overlay(pkg, sha, d, tmp_path / "overlay")
+    assert ov["schema"] == "arcforge.kaggle.model_overlay.v1" and ov["report"]["replaced"] == man["tensors"]
+    assert (tmp_path / "overlay" / "DONE").exists() and ov["rl_merged"]["optimizer_step"] == 3
+    patch = wp.build_patch(pkg, tmp_path / "overlay", tmp_path / "patch")
+    pdir = tmp_path / "patch"
+    assert patch["schema"] == "arcforge.kaggle.weight_patch.v1"
+    assert all(f.startswith("patch-model-") for f in patch["files"]) and (pdir / "patch.json").exists()
+    assert 0 < len(patch["tensors"]) <= man["tensors"]
+    _, base = read_package(pkg)
+    _, viapatch = read_package(pkg, weight_patch=pdir)
+    _, viamerged = read_package(pkg, merged=d)
+    for k in base:
+        assert torch.equal(viapatch[k].view(torch.uint8), viamerged[k].view(torch.uint8)), k
+    assert any(not torch.equal(viapatch[k].view(torch.uint8), base[k].view(torch.uint8)) for k in patch["tensors"])
+    # a patch is bound to its base package
+    with pytest.raises(ValueError, match="patches the package"):
+        wp.WeightPatch(pdir, "0" * 64)
+    with pytest.raises(FileExistsError):
+        wp.build_patch(pkg, tmp_path / "overlay", tmp_path / "patch")
+    # the overlay names the base manifest it was made from: a package with other shard bytes is refused
+    other, _ = _package(tmp_path / "b", seed=1)
+    with pytest.raises(RuntimeError, match="hashes to"):
+        wp.build_patch(other, tmp_path / "overlay", tmp_path / "patch2")
 
 
 def test_routing_replay_forces_recorded_experts():
