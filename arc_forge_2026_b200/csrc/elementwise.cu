@@ -197,8 +197,12 @@ int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, i
 // ------------------------------------------------------------------------------------------ router
 // logits [T, ld] fp32 (first E columns are experts). softmax -> top-k (ties: lower id) -> renorm.
 // One warp per token; lane i owns experts i, i+32, ... (E <= 1024).
+// With `cnt` / `list` given (cnt zeroed before the launch) every (token, slot) entry e = t * k + j is also appended
+// to its expert's list: list[expert * cap + pos] = e, pos from an atomic counter cnt[expert] (the order inside a list
+// is arbitrary; the expert kernels' results do not depend on it). cap >= T: a token picks an expert once.
 __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int k, int renorm,
-                                   int* __restrict__ ids, float* __restrict__ weights) {
+                                   int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ cnt,
+                                   int* __restrict__ list, int cap) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -253,14 +257,25 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
   if (lane < k) {
     ids[(size_t)t * k + lane] = isel;
     weights[(size_t)t * k + lane] = renorm ? wsel / picked_sum : wsel;
+    if (cnt) {
+      const int pos = atomicAdd(&cnt[isel], 1);
+      list[(size_t)isel * cap + pos] = t * k + lane;
+    }
   }
 }
 
 int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, int* ids, float* weights,
-                cudaStream_t st) {
+                cudaStream_t st, int* cnt, int* list, int cap) {
   if (E > 1024 || k > 32) return 3;
+  if (cnt && (!list || cap < T)) return 3;
   const int warps = 4;
-  router_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(logits, ld, T, E, k, renorm, ids, weights);
+  if (cnt) {
+    const cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t)E * sizeof(int), st);
+    if (e != cudaSuccess) return (int)e;
+  }
+  if (T <= 0) return 0;
+  router_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(logits, ld, T, E, k, renorm, ids, weights, cnt,
+                                                                      list, cap);
   return (int)cudaGetLastError();
 }
 
@@ -422,61 +437,149 @@ int quant_rows_e4m3(const void* x, int ldx, const int* row_token, const int* nro
   return (int)cudaGetLastError();
 }
 
+// out_q[r, :] = e4m3(x[src(r), :] * (1 / s)) with ONE scale per row, s = max(amax of the row, 1e-30) / 448: the
+// reference's W3A8 activation rule (training/work/qwen38fn_lora/int3_moe.py:108-118, Humming's per-row input
+// quantisation). One warp per row; the second pass over the row re-reads it from L1/L2.
+__global__ void quant_rows_e4m3_row_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                                           const int* __restrict__ row_token, const int* __restrict__ nrows_dev,
+                                           int nrows, int K, uint8_t* __restrict__ q, float* __restrict__ scales) {
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int n = nrows_dev ? min(*nrows_dev, nrows) : nrows;
+  if (r >= n) return;
+  const int src = row_token ? row_token[r] : r;
+  const uint4* p = reinterpret_cast<const uint4*>(x + (size_t)src * ldx);
+  const int nv = K / 8;
+  float a = 0.f;
+  for (int v = lane; v < nv; v += 32) {
+    const uint4 raw = p[v];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      a = fmaxf(a, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  a = warp_max(a);
+  const float s = fmaxf(a, 1e-30f) / 448.f;
+  const float inv = 1.f / s;
+  uint2* out = reinterpret_cast<uint2*>(q + (size_t)r * K);
+  for (int v = lane; v < nv; v += 32) {
+    const uint4 raw = p[v];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __bfloat1622float2(h[i]);
+      f[2 * i] = t.x * inv;
+      f[2 * i + 1] = t.y * inv;
+    }
+    const __nv_fp8x4_e4m3 lo(make_float4(f[0], f[1], f[2], f[3])), hi(make_float4(f[4], f[5], f[6], f[7]));
+    out[v] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+  }
+  if (lane == 0) scales[r] = s;
+}
+
+int quant_rows_e4m3_row(const void* x, int ldx, const int* row_token, const int* nrows_dev, int nrows, int K, void* q,
+                        float* scales, cudaStream_t st) {
+  if (K % 8 || ldx % 8) return 3;
+  if (nrows <= 0) return 0;
+  const int warps = 8;
+  quant_rows_e4m3_row_kernel<<<(nrows + warps - 1) / warps, warps * 32, 0, st>>>(
+      (const __nv_bfloat16*)x, ldx, row_token, nrows_dev, nrows, K, (uint8_t*)q, scales);
+  return (int)cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------------------ MoE combine
 // out[t] = x_res[t] + sigmoid(sg[t]) * shared[t] + sum_j y[entry_row[t*k+j]]   (y already carries the route weight)
 // sg is read from column `sg_col` of the router logits (the shared-expert gate rides along the router GEMM).
-// One warp per token, 8 bf16 per lane per step; rows of y absent on this rank (entry_row < 0) are skipped.
+// entry_row null: y rows are the entries themselves (row t*k + j). Rows of y absent on this rank (entry_row < 0) are
+// skipped. With `ew` (expert parallelism) every CTA first waits, bounded, until every rank has published this
+// exchange's combine rows into this rank's region, and the last CTA counts the exchange consumed.
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ entry_row, int k,
                                    const __nv_bfloat16* __restrict__ shared, const float* __restrict__ router_logits,
                                    int ld_logits, int sg_col, const __nv_bfloat16* __restrict__ resid,
-                                   __nv_bfloat16* __restrict__ out, int T, int H) {
+                                   __nv_bfloat16* __restrict__ out, int T, int H, EpArgs ew, uint32_t* status) {
   // one CTA per token, one thread per 8 columns; all k row loads of a thread are issued before the sums
   const int t = blockIdx.x;
   const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
-  if (t >= T || c >= H) return;
-  float sg = 1.f;
-  if (router_logits) sg = 1.f / (1.f + __expf(-router_logits[(size_t)t * ld_logits + sg_col]));
-  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  constexpr int KB = 4;  // rows in flight per batch
-  for (int j0 = 0; j0 < k; j0 += KB) {
-    uint4 q[KB];
-#pragma unroll
-    for (int u = 0; u < KB; ++u) {
-      const int r = j0 + u < k ? entry_row[t * k + j0 + u] : -1;
-      q[u] = r >= 0 ? *reinterpret_cast<const uint4*>(y + (size_t)r * H + c) : make_uint4(0, 0, 0, 0);
+  const bool waiting = ew.world > 0;
+  if (waiting) {
+    if (threadIdx.x == 0) {
+      const uint64_t want = ew.expected[1] + 1;
+      for (int p = 0; p < ew.world; ++p) {
+        const uint64_t* f = reinterpret_cast<const uint64_t*>(ew.peer[ew.rank] + ew.off_flags) + EP_MAX_RANKS + p;
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t polls = 0;
+        while (ld_acquire_sys_u64(f) < want) {
+          if ((++polls & 63) == 0 && globaltimer_ns() - t0 > AFB_WAIT_NS) {
+            flag_error(status, AFB_ERR_PEER_TIMEOUT);
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
     }
+    __syncthreads();
+  }
+  if (t < T && c < H) {
+    float sg = 1.f;
+    if (router_logits) sg = 1.f / (1.f + __expf(-router_logits[(size_t)t * ld_logits + sg_col]));
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    constexpr int KB = 4;  // rows in flight per batch
+    for (int j0 = 0; j0 < k; j0 += KB) {
+      uint4 q[KB];
 #pragma unroll
-    for (int u = 0; u < KB; ++u) {  // slot order is kept: the sum is the same on every run and every rank count
-      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q[u]);
+      for (int u = 0; u < KB; ++u) {
+        const int r = j0 + u < k ? (entry_row ? entry_row[t * k + j0 + u] : t * k + j0 + u) : -1;
+        q[u] = r >= 0 ? *reinterpret_cast<const uint4*>(y + (size_t)r * H + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < KB; ++u) {  // slot order is kept: the sum is the same on every run and every rank count
+        const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q[u]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
+      }
+    }
+    if (shared) {
+      uint4 q = *reinterpret_cast<const uint4*>(shared + (size_t)t * H + c);
+      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += sg * __bfloat162float(hq[i]);
+    }
+    if (resid) {
+      uint4 q = *reinterpret_cast<const uint4*>(resid + (size_t)t * H + c);
+      const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
     }
+    *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = make_uint4(
+        pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
   }
-  if (shared) {
-    uint4 q = *reinterpret_cast<const uint4*>(shared + (size_t)t * H + c);
-    const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] += sg * __bfloat162float(hq[i]);
+  if (waiting && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&ew.wait_done[1], 1u) == gridDim.x * gridDim.y - 1) {
+      ew.wait_done[1] = 0;
+      ew.expected[1] += 1;
+    }
   }
-  if (resid) {
-    uint4 q = *reinterpret_cast<const uint4*>(resid + (size_t)t * H + c);
-    const __nv_bfloat16* hq = reinterpret_cast<const __nv_bfloat16*>(&q);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(hq[i]);
-  }
-  *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = make_uint4(
-      pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
 }
 
 int moe_combine(const void* y, const int* entry_row, int k, const void* shared, const float* router_logits,
-                int ld_logits, int sg_col, const void* resid, void* out, int T, int H, cudaStream_t st) {
+                int ld_logits, int sg_col, const void* resid, void* out, int T, int H, cudaStream_t st,
+                const EpArgs* wait_combine, uint32_t* status) {
   if (H % 8 || k > 64) return 3;
-  if (T <= 0) return 0;
+  EpArgs ew;
+  if (wait_combine) ew = *wait_combine;
+  else ew.world = 0;
+  // a rank with no tokens still joins the exchange: one CTA waits and counts it consumed
+  const int rows = T > 0 ? T : (wait_combine ? 1 : 0);
+  if (rows <= 0) return 0;
   const int threads = 256;
-  dim3 grid(T, (H / 8 + threads - 1) / threads);
+  dim3 grid(rows, (H / 8 + threads - 1) / threads);
   moe_combine_kernel<<<grid, threads, 0, st>>>((const __nv_bfloat16*)y, entry_row, k, (const __nv_bfloat16*)shared,
                                                router_logits, ld_logits, sg_col, (const __nv_bfloat16*)resid,
-                                               (__nv_bfloat16*)out, T, H);
+                                               (__nv_bfloat16*)out, T, H, ew, status);
   return (int)cudaGetLastError();
 }
 

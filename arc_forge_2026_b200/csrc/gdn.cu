@@ -101,6 +101,10 @@ __global__ void __launch_bounds__(DK) gdn_conv_prep_kernel(GdnArgs a, int parity
   }
 }
 
+// float offset of row kk (0..31) of thread t's slice in the swizzled state layout (DK = DV = 128, 4 threads per
+// column; see the persistent verify kernel)
+AFB_DEV int gdn_state_off(int t, int kk) { return t * 32 + ((((kk >> 2) ^ (t & 7))) << 2) + (kk & 3); }
+
 // QT threads per value column (adjacent lanes), each holding DK/QT state rows in registers; dot products over DK
 // are reduced with log2(QT) shuffles. QT=4 (512 threads) doubles the warps per SM over one thread pair per column,
 // so the strided state loads of some warps overlap the recurrence of others.
@@ -119,9 +123,14 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
   __shared__ float red[32];
 
   float S[HK];
-  float* sp = a.ssm_state + (((size_t)slot * a.Hv + h) * DK + part * HK) * DV + v;
+  // DK = DV = 128 with 4 threads per column: the swizzled thread-major layout the persistent verify kernel uses
+  // (thread t = QT * v + part owns its 32 rows contiguously); other shapes: plain [Dk, Dv]
+  constexpr bool SWZ = DK == 128 && DV == 128 && QT == 4;
+  float* sp = SWZ ? a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV
+                  : a.ssm_state + (((size_t)slot * a.Hv + h) * DK + part * HK) * DV + v;
+  auto sidx = [&](int k) -> size_t { return SWZ ? (size_t)gdn_state_off(threadIdx.x, k) : (size_t)k * DV; };
 #pragma unroll
-  for (int k = 0; k < HK; ++k) S[k] = sp[(size_t)k * DV];
+  for (int k = 0; k < HK; ++k) S[k] = sp[sidx(k)];
 
   auto load_kq = [&](int par, int t) {
     const size_t base = ((size_t)par * a.pend_slots + ps) * a.max_q + t;
@@ -161,7 +170,7 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
     const int nprev = a.n_commit[slot];
     for (int t = 0; t < nprev; ++t) update(load_kq(prev, t));
 #pragma unroll
-    for (int k = 0; k < HK; ++k) sp[(size_t)k * DV] = S[k];
+    for (int k = 0; k < HK; ++k) sp[sidx(k)] = S[k];
   }
   for (int t = 0; t < T; ++t) {
     update(load_kq(cur, t));
@@ -185,25 +194,39 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
   }
   if (a.commit_current) {
 #pragma unroll
-    for (int k = 0; k < HK; ++k) sp[(size_t)k * DV] = S[k];
+    for (int k = 0; k < HK; ++k) sp[sidx(k)] = S[k];
   }
 }
 
 // ------------------------------------------------------------------------------------------ persistent verify path
 // One CTA (512 threads, 4 per value column) per SM loops over (sequence, value head) items. While it runs the
-// recurrence of item i from registers, bulk copies (no multicast) stage item i+1 into the other half of a shared
-// memory double buffer: its 64 KB committed state, the k (and q) rows of the previous cycle's and this cycle's
-// tokens, their v rows, gates and the z rows of the output gate. So the token steps never wait on global memory,
-// and the state loads of the next item overlap the math of the current one.
+// recurrence of item i, bulk copies (no multicast) stage item i+1 into the other half of a shared-memory double
+// buffer: its 64 KB committed state, the k (and q) rows of the previous cycle's and this cycle's tokens, their v rows,
+// gates and the z rows of the output gate.
+//
+// Per item:
+//   * keys and queries are converted once to fp32 into part-padded rows (conflict-free 16-byte loads);
+//   * the recurrence keeps S / Gamma in registers, Gamma = the product of the decays since the item started, so a
+//     step is two FMA passes (the dot k.S and the rank-1 update) instead of three -- the decay is applied to the
+//     scalar, S_true = Gamma * S. When log Gamma falls below -60 the registers are rescaled and Gamma restarts at 1;
+//   * after the accepted tokens of the previous cycle the committed state Gamma * S goes back into its shared-memory
+//     slot and one bulk copy stores the 64 KB (the state is not rewritten when no token was accepted);
+//   * this cycle's raw outputs go to shared memory; one pass then applies the gated RMSNorm per token.
+// State layout (DK = DV = 128, per (slot, head)): thread t = 4 * v + part owns rows part*32 .. part*32+31 of column v
+// and stores them contiguously, 16-byte chunk c at chunk position c ^ (t & 7) -- so every thread moves its slice
+// with 16-byte accesses and no two lanes of a quarter warp touch the same bank.
 namespace gdnp {
 constexpr int DK = 128, DV = 128, QT = 4, HK = DK / QT, THREADS = QT * DV, MAXT = 8, MAXS = 1024;
+constexpr int KP = HK + 4;  // padded fp32 slice of a key / query row per part
 struct Smem {
   float state[2][DK * DV];
   __nv_bfloat16 kq[2][2 * MAXT][2][DK];  // token slots 0..7: previous cycle (k only), 8..15: this cycle (k, q)
   __nv_bfloat16 v[2][2 * MAXT][DV];
   __nv_bfloat16 z[2][MAXT][DV];
   float gb[2][2][2 * MAXT];              // [buf][previous / this cycle][token * 2 + (g, beta)]
-  float red[THREADS / 32];
+  float kf[2 * MAXT][QT * KP];           // this item's keys, fp32, compact token order (accepted, then new)
+  float qf[MAXT][QT * KP];               // this item's queries, fp32
+  float o[MAXT][DV];                     // raw outputs of this cycle's tokens
   int slot[MAXS], ncommit[MAXS];
   uint64_t full[2];
 };
@@ -215,6 +238,14 @@ AFB_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
+AFB_DEV void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+               "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+AFB_DEV void bulk_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+AFB_DEV void bulk_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel(GdnArgs a, int parity,
                                                                                   uint32_t* status) {
@@ -238,131 +269,184 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
   }
   __syncthreads();
 
-  auto issue = [&](int item, int b) {  // thread 0 only
+  // warp 0 stages an item: lane 0 arms the barrier, then every lane issues a share of the bulk copies (one lane per
+  // copy, so the warp is not held back by a serial issue loop)
+  auto issue = [&](int item, int b) {
     const int seq = item / a.Hv, h = item % a.Hv;
     const int slot = sm.slot[seq], np = sm.ncommit[seq];
     const int kh = h / (a.Hv / a.Hk);
-    const uint32_t bytes = DK * DV * 4 + np * (DK + DV) * 2 + T * (2 * DK + 2 * DV) * 2 + 2 * a.max_q * 8;
-    mbar_arrive_expect_tx(&sm.full[b], bytes);
-    bulk_copy(sm.state[b], a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV, DK * DV * 4, &sm.full[b]);
-    for (int t = 0; t < np; ++t) {
-      const size_t base = ((size_t)prev * a.pend_slots + slot) * a.max_q + t;
-      bulk_copy(sm.kq[b][t][0], a.pend_qk + base * (2 * nq) + nq + kh * DK, DK * 2, &sm.full[b]);
-      bulk_copy(sm.v[b][t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
+    const int lane = tid & 31;
+    if (lane == 0) {
+      bulk_store_wait_read();  // the committed-state store of two items ago has finished reading buffer b
+      const uint32_t bytes = DK * DV * 4 + np * (DK + DV) * 2 + T * (2 * DK + 2 * DV) * 2 + 2 * a.max_q * 8;
+      mbar_arrive_expect_tx(&sm.full[b], bytes);
     }
-    for (int t = 0; t < T; ++t) {
-      const size_t base = ((size_t)cur * a.pend_slots + slot) * a.max_q + t;
-      bulk_copy(sm.kq[b][MAXT + t][0], a.pend_qk + base * (2 * nq) + nq + kh * DK, DK * 2, &sm.full[b]);
-      bulk_copy(sm.kq[b][MAXT + t][1], a.pend_qk + base * (2 * nq) + kh * DK, DK * 2, &sm.full[b]);
-      bulk_copy(sm.v[b][MAXT + t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
-      bulk_copy(sm.z[b][t], a.mixed + ((size_t)seq * T + t) * a.mixed_ld + a.z_off + h * DV, DV * 2, &sm.full[b]);
+    __syncwarp();
+    // copy list: 0 state, 1 gb prev, 2 gb cur, then per accepted token (k, v), then per new token (k, q, v, z)
+    const int ncopies = 3 + 2 * np + 4 * T;
+    for (int c = lane; c < ncopies; c += 32) {
+      if (c == 0) {
+        bulk_copy(sm.state[b], a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV, DK * DV * 4, &sm.full[b]);
+      } else if (c <= 2) {
+        const int par = c == 1 ? prev : cur;
+        bulk_copy(sm.gb[b][c - 1], a.pend_gb + (((size_t)par * a.pend_slots + slot) * a.Hv + h) * a.max_q * 2,
+                  a.max_q * 8, &sm.full[b]);
+      } else if (c < 3 + 2 * np) {
+        const int t = (c - 3) >> 1;
+        const size_t base = ((size_t)prev * a.pend_slots + slot) * a.max_q + t;
+        if (((c - 3) & 1) == 0)
+          bulk_copy(sm.kq[b][t][0], a.pend_qk + base * (2 * nq) + nq + kh * DK, DK * 2, &sm.full[b]);
+        else
+          bulk_copy(sm.v[b][t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
+      } else {
+        const int t = (c - 3 - 2 * np) >> 2, w = (c - 3 - 2 * np) & 3;
+        const size_t base = ((size_t)cur * a.pend_slots + slot) * a.max_q + t;
+        if (w == 0)
+          bulk_copy(sm.kq[b][MAXT + t][0], a.pend_qk + base * (2 * nq) + nq + kh * DK, DK * 2, &sm.full[b]);
+        else if (w == 1)
+          bulk_copy(sm.kq[b][MAXT + t][1], a.pend_qk + base * (2 * nq) + kh * DK, DK * 2, &sm.full[b]);
+        else if (w == 2)
+          bulk_copy(sm.v[b][MAXT + t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
+        else
+          bulk_copy(sm.z[b][t], a.mixed + ((size_t)seq * T + t) * a.mixed_ld + a.z_off + h * DV, DV * 2,
+                    &sm.full[b]);
+      }
     }
-    bulk_copy(sm.gb[b][0], a.pend_gb + (((size_t)prev * a.pend_slots + slot) * a.Hv + h) * a.max_q * 2,
-              a.max_q * 8, &sm.full[b]);
-    bulk_copy(sm.gb[b][1], a.pend_gb + (((size_t)cur * a.pend_slots + slot) * a.Hv + h) * a.max_q * 2,
-              a.max_q * 8, &sm.full[b]);
   };
 
   int issued = 0, done = 0;
-  if (tid == 0 && blockIdx.x < items) {
+  if (tid < 32 && blockIdx.x < items) {
     issue(blockIdx.x, 0);
     issued = 1;
   }
-  bool ok = true;
   int i = 0;
-  for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++i) {
+  for (int item = blockIdx.x; item < items; item += gridDim.x, ++i) {
     const int b = i & 1;
     const int next = item + gridDim.x;
-    if (tid == 0 && next < items) {
+    if (tid < 32 && next < items) {  // buffer b ^ 1 was released by every thread at the end of the last item
       issue(next, b ^ 1);
       ++issued;
     }
-    if (!mbar_wait(&sm.full[b], (i >> 1) & 1, status)) {
-      ok = false;
-      break;
-    }
+    // every thread acquires the copies through the barrier; the vote makes a timeout (flagged in the status word)
+    // end the loop on every thread together
+    const bool ok = __syncthreads_and(mbar_wait(&sm.full[b], (i >> 1) & 1, status));
+    if (!ok) break;
     ++done;
     const int seq = item / a.Hv, h = item % a.Hv;
     const int slot = sm.slot[seq], np = sm.ncommit[seq];
+    const int L = np + T;  // tokens of this item: the accepted ones of the previous cycle, then this cycle's
+
+    // ---- keys / queries -> fp32, part-padded (token order: accepted 0..np-1, then new np..np+T-1)
+    for (int idx = tid; idx < (L + T) * (DK / 2); idx += THREADS) {
+      const int row = idx / (DK / 2), c2 = (idx % (DK / 2)) * 2;
+      const __nv_bfloat16* src;
+      float* dst;
+      if (row < L) {
+        src = sm.kq[b][row < np ? row : MAXT + row - np][0] + c2;
+        dst = sm.kf[row];
+      } else {
+        src = sm.kq[b][MAXT + row - L][1] + c2;
+        dst = sm.qf[row - L];
+      }
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
+      const int pc = (c2 / HK) * KP + (c2 % HK);
+      dst[pc] = f.x;
+      dst[pc + 1] = f.y;
+    }
+    // ---- this thread's 32 state values
     float S[HK];
 #pragma unroll
-    for (int k = 0; k < HK; ++k) S[k] = sm.state[b][(part * HK + k) * DV + v];
-    // this thread's 32 key (or query) values of a token row: four 16-byte shared loads, unpacked 8 at a time
-    auto load8 = [&](const __nv_bfloat16* row, int j, float* f) {
-      const uint4 u = reinterpret_cast<const uint4*>(row + part * HK)[j];
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 x = __bfloat1622float2(h2[i]);
-        f[2 * i] = x.x;
-        f[2 * i + 1] = x.y;
-      }
-    };
-    auto step = [&](int ts, float decay, float beta) {
-      const __nv_bfloat16* kk = sm.kq[b][ts][0];
-      const float vv = __bfloat162float(sm.v[b][ts][v]);
-      float f[HK];  // this thread's key values, converted once for both passes
-#pragma unroll
-      for (int j = 0; j < HK / 8; ++j) load8(kk, j, f + 8 * j);
-      float mem0 = 0.f, mem1 = 0.f;  // two chains halve the dependent-FMA latency
-#pragma unroll
-      for (int i = 0; i < HK; i += 2) {
-        S[i] *= decay;
-        S[i + 1] *= decay;
-        mem0 = fmaf(f[i], S[i], mem0);
-        mem1 = fmaf(f[i + 1], S[i + 1], mem1);
-      }
-      float mem = mem0 + mem1;
-#pragma unroll
-      for (int o = 1; o < QT; o <<= 1) mem += __shfl_xor_sync(0xffffffffu, mem, o);
-      const float delta = beta * (vv - mem);
-#pragma unroll
-      for (int i = 0; i < HK; ++i) S[i] = fmaf(f[i], delta, S[i]);
-    };
-    for (int t = 0; t < np; ++t) step(t, __expf(sm.gb[b][0][2 * t]), sm.gb[b][0][2 * t + 1]);
-    float* sp = a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV + (size_t)(part * HK) * DV + v;
-#pragma unroll
-    for (int k = 0; k < HK; ++k) sp[(size_t)k * DV] = S[k];  // the committed state
-    for (int t = 0; t < T; ++t) {
-      step(MAXT + t, __expf(sm.gb[b][1][2 * t]), sm.gb[b][1][2 * t + 1]);
-      float o0 = 0.f, o1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < HK / 8; ++j) {
-        float f[8];
-        load8(sm.kq[b][MAXT + t][1], j, f);
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          o0 = fmaf(f[i], S[8 * j + i], o0);
-          o1 = fmaf(f[i + 1], S[8 * j + i + 1], o1);
-        }
-      }
-      float o = o0 + o1;
-#pragma unroll
-      for (int x = 1; x < QT; x <<= 1) o += __shfl_xor_sync(0xffffffffu, o, x);
-      const float ssq = warp_sum(part ? 0.f : o * o);
-      if ((tid & 31) == 0) sm.red[tid >> 5] = ssq;
-      __syncthreads();
-      float tot;
-      if constexpr (THREADS / 32 == 32) {
-        tot = warp_sum(sm.red[tid & 31]);  // one load per lane, not one per warp
-      } else {
-        tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < THREADS / 32; ++w) tot += sm.red[w];
-      }
-      if (!part) {
-        const size_t tok = (size_t)seq * T + t;
-        const float z = __bfloat162float(sm.z[b][t][v]);
-        const float y = o * rsqrtf(tot / DV + a.eps) * __bfloat162float(a.norm_w[v]) * silu(z);
-        a.out[tok * (a.Hv * DV) + h * DV + v] = __float2bfloat16(y);
-      }
-      __syncthreads();  // red is rewritten by the next token
+    for (int c = 0; c < HK / 4; ++c) {
+      const float4 x = *reinterpret_cast<const float4*>(&sm.state[b][tid * 32 + ((c ^ (tid & 7)) << 2)]);
+      S[4 * c] = x.x;
+      S[4 * c + 1] = x.y;
+      S[4 * c + 2] = x.z;
+      S[4 * c + 3] = x.w;
     }
-    __syncthreads();  // buffer b is refilled two items later
+    __syncthreads();  // fp32 keys / queries ready
+
+    float lg = 0.f;  // log Gamma
+    // partial dot of this thread's slice with an fp32 row (four FMA chains), summed over the QT lanes of a column
+    auto dot = [&](const float* row) {
+      const float4* r4 = reinterpret_cast<const float4*>(row + part * KP);
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+      for (int c = 0; c < HK / 4; ++c) {
+        const float4 x = r4[c];
+        d0 = fmaf(x.x, S[4 * c], d0);
+        d1 = fmaf(x.y, S[4 * c + 1], d1);
+        d2 = fmaf(x.z, S[4 * c + 2], d2);
+        d3 = fmaf(x.w, S[4 * c + 3], d3);
+      }
+      float d = (d0 + d1) + (d2 + d3);
+#pragma unroll
+      for (int o = 1; o < QT; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      return d;
+    };
+    // one token of the gated delta rule on S / Gamma: decay g (log), gate beta, value vv, key row kr
+    auto step = [&](float g, float beta, float vv, const float* kr) {
+      float lgn = lg + g;
+      const float mem = __expf(lgn) * dot(kr);
+      if (lgn < -60.f) {  // uniform over the CTA: the gates are per (token, head)
+        const float f = __expf(lgn);
+#pragma unroll
+        for (int k = 0; k < HK; ++k) S[k] *= f;
+        lgn = 0.f;
+      }
+      lg = lgn;
+      const float c = beta * (vv - mem) * __expf(-lg);  // delta / Gamma
+      const float4* r4 = reinterpret_cast<const float4*>(kr + part * KP);
+#pragma unroll
+      for (int q = 0; q < HK / 4; ++q) {
+        const float4 x = r4[q];
+        S[4 * q] = fmaf(x.x, c, S[4 * q]);
+        S[4 * q + 1] = fmaf(x.y, c, S[4 * q + 1]);
+        S[4 * q + 2] = fmaf(x.z, c, S[4 * q + 2]);
+        S[4 * q + 3] = fmaf(x.w, c, S[4 * q + 3]);
+      }
+    };
+    for (int t = 0; t < np; ++t)
+      step(sm.gb[b][0][2 * t], sm.gb[b][0][2 * t + 1], __bfloat162float(sm.v[b][t][v]), sm.kf[t]);
+    if (np > 0) {  // the committed state Gamma * S back into its slot, stored by one bulk copy
+      const float gam = __expf(lg);
+#pragma unroll
+      for (int c = 0; c < HK / 4; ++c)
+        *reinterpret_cast<float4*>(&sm.state[b][tid * 32 + ((c ^ (tid & 7)) << 2)]) =
+            make_float4(gam * S[4 * c], gam * S[4 * c + 1], gam * S[4 * c + 2], gam * S[4 * c + 3]);
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) bulk_store(a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV, sm.state[b], DK * DV * 4);
+    }
+    for (int t = 0; t < T; ++t) {
+      step(sm.gb[b][1][2 * t], sm.gb[b][1][2 * t + 1], __bfloat162float(sm.v[b][MAXT + t][v]), sm.kf[np + t]);
+      const float o = __expf(lg) * dot(sm.qf[t]);
+      if (part == 0) sm.o[t][v] = o;
+    }
+    __syncthreads();  // raw outputs complete
+    // ---- gated RMSNorm per token: warp w takes token w, lane l columns 4l .. 4l+3
+    {
+      const int w = tid >> 5, l = tid & 31;
+      if (w < T) {
+        const float4 o4 = *reinterpret_cast<const float4*>(&sm.o[w][4 * l]);
+        const float rstd = rsqrtf(warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w) / DV + a.eps);
+        const uint2 zr = *reinterpret_cast<const uint2*>(&sm.z[b][w][4 * l]);
+        const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zr);
+        const float2 za = __bfloat1622float2(z2[0]), zb = __bfloat1622float2(z2[1]);
+        const float2 na = make_float2(__bfloat162float(a.norm_w[4 * l]), __bfloat162float(a.norm_w[4 * l + 1]));
+        const float2 nb = make_float2(__bfloat162float(a.norm_w[4 * l + 2]), __bfloat162float(a.norm_w[4 * l + 3]));
+        const size_t tok = (size_t)seq * T + w;
+        *reinterpret_cast<uint2*>(a.out + tok * (a.Hv * DV) + h * DV + 4 * l) =
+            make_uint2(pack_bf16x2(o4.x * rstd * na.x * silu(za.x), o4.y * rstd * na.y * silu(za.y)),
+                       pack_bf16x2(o4.z * rstd * nb.x * silu(zb.x), o4.w * rstd * nb.y * silu(zb.y)));
+      }
+    }
+    __syncthreads();  // o / kf / qf are rewritten by the next item; buffer b is refilled two items later
   }
-  // drain copies still in flight (only after a failed wait), bounded
-  if (tid == 0)
+  // drain copies still in flight (only after a failed wait), bounded; then the last committed-state stores
+  if (tid == 0) {
     for (int j = done; j < issued; ++j) mbar_wait(&sm.full[j & 1], (j >> 1) & 1, status);
+    bulk_store_wait_all();
+  }
 }
 
 int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cudaStream_t st) {

@@ -15,13 +15,17 @@ int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, i
                        void* q_out, void* kcache, void* vcache, int page_size, cudaStream_t st,
                        uint8_t* kscale = nullptr, uint8_t* vscale = nullptr);  // scales given: NVFP4 cache
 int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, int* ids, float* weights,
-                cudaStream_t st);
+                cudaStream_t st, int* cnt = nullptr, int* list = nullptr, int cap = 0);
 int expert_sort(const int* ids, int n, int E, const int* expert_map, int* offsets, int* row_token, int* row_entry,
                 int* entry_row, int k, int pad, cudaStream_t st);
 int quant_rows_e4m3(const void* x, int ldx, const int* row_token, const int* nrows_dev, int nrows, int K, void* q,
                     float* scales, int ld_s, cudaStream_t st);
+// one scale per row, s = max(amax, 1e-30) / 448 (the INT3 experts' W3A8 activation rule); K % 8 == 0
+int quant_rows_e4m3_row(const void* x, int ldx, const int* row_token, const int* nrows_dev, int nrows, int K, void* q,
+                        float* scales, cudaStream_t st);
 int moe_combine(const void* y, const int* entry_row, int k, const void* shared, const float* router_logits,
-                int ld_logits, int sg_col, const void* resid, void* out, int T, int H, cudaStream_t st);
+                int ld_logits, int sg_col, const void* resid, void* out, int T, int H, cudaStream_t st,
+                const struct EpArgs* wait_combine = nullptr, uint32_t* status = nullptr);
 int swiglu(const void* x, void* y, int T, int I, cudaStream_t st);
 int embedding(const int* ids, const void* table, void* out, int T, int H, int V, uint32_t* status, cudaStream_t st);
 
@@ -248,20 +252,29 @@ struct EpArgs {
   uint8_t* peer[EP_MAX_RANKS] = {};        // heap base of every rank (own included)
   // region offsets (bytes) inside every heap
   size_t off_x = 0;      // e4m3 [world*T_cap, H]
-  size_t off_s = 0;      // fp32 [H/128, ld_s] (group-major)
+  size_t off_s = 0;      // fp32 [world*T_cap] one scale per row
   size_t off_ids = 0;    // int32 [world*T_cap, k]
   size_t off_w = 0;      // fp32 [world*T_cap, k]
   size_t off_comb = 0;   // bf16 [T_cap*k, H] routed rows of this rank's tokens
   size_t off_flags = 0;  // uint64 [2 types][EP_MAX_RANKS sources]
+  size_t off_rcnt = 0;   // int [world sources][E_local]: how many of each source's entries go to each local expert
+  size_t off_rlist = 0;  // int [world sources][E_local][T_cap]: those entries (global entry = src*T_cap*k + t*k + j)
   int ld_s = 0;
+  int E_local = 0;       // experts per rank (expert e lives on rank e / E_local)
   unsigned* done = nullptr;             // local [2] CTA-completion counters
   unsigned long long* sent = nullptr;   // local [2] exchanges published
   unsigned long long* expected = nullptr;  // local [2] exchanges consumed
+  unsigned* wait_done = nullptr;        // local [2] CTA-completion counters of the kernels that consume an exchange
+  // dispatch: this rank's per-expert entry lists from the router (cnt [E], list [E, T_cap], local entry indices)
+  const int* lcnt = nullptr;
+  const int* llist = nullptr;
 };
 int ep_dispatch(const EpArgs& a, const void* x, int ldx, const int* ids, const float* weights, cudaStream_t st);
 int ep_wait(const EpArgs& a, int type, uint32_t* status, cudaStream_t st);
-int ep_gather(const EpArgs& a, const int* row_token, const int* nrows_dev, int rows_cap, void* xq, float* xs,
-              int ld_xs, cudaStream_t st);
+// e4m3 per-row quantisation of the entry rows x [rows, K] that this rank's routing lists name (h between the expert
+// GEMMs under expert parallelism): one warp per list slot, empty slots exit at once
+int quant_routed_rows(const void* x, int K, const int* cnt, const int* list, int srcs, int E, int cap, void* q,
+                      float* scales, cudaStream_t st);
 
 // hc.cu: hyper-connection residual stream [rows, G, H] (bf16): grouped norm, branch mix, gated write-back, and
 // their dX-only backward; H in {256, 512, 1024, 2048, 2560}, G <= 8

@@ -51,14 +51,22 @@ void qk_norm_rope_store_op(const at::Tensor& qkv, int64_t Hq, int64_t Hkv, int64
            "qk_norm_rope_store");
 }
 
+// Optional per-expert entry lists: cnt int [E] (cleared by the launcher), list int [E, cap], cap >= tokens.
 void router_topk_op(const at::Tensor& logits, int64_t E, int64_t k, bool renorm, at::Tensor& ids,
-                    at::Tensor& weights) {
+                    at::Tensor& weights, c10::optional<at::Tensor> cnt, c10::optional<at::Tensor> list) {
   AFB_CHECK_DT(logits, at::kFloat);
   AFB_CHECK_DT(ids, at::kInt);
   AFB_CHECK_DT(weights, at::kFloat);
   TORCH_CHECK(logits.stride(1) == 1, "router logits need unit inner stride");
+  int cap = 0;
+  if (cnt.has_value()) {
+    TORCH_CHECK(list.has_value() && cnt->numel() >= E && list->dim() == 2 && list->size(0) >= E &&
+                    list->is_contiguous(),
+                "router lists: cnt [E], list [E, cap]");
+    cap = list->size(1);
+  }
   check_rc(afb::router_topk(ptr<float>(logits), logits.stride(0), logits.size(0), E, k, renorm, ptr<int>(ids),
-                            ptr<float>(weights), stream()),
+                            ptr<float>(weights), stream(), optr<int>(cnt), optr<int>(list), cap),
            "router_topk");
 }
 
@@ -71,6 +79,20 @@ void expert_sort_op(const at::Tensor& ids, int64_t E, c10::optional<at::Tensor> 
   check_rc(afb::expert_sort(ptr<int>(ids), ids.numel(), E, optr<int>(expert_map), ptr<int>(offsets),
                             ptr<int>(row_token), ptr<int>(row_entry), ptr<int>(entry_row), k, (int)pad, stream()),
            "expert_sort");
+}
+
+// per-row e4m3 (the INT3 experts' activation format): q [>= rows, K], scales fp32 [>= rows]
+void quant_rows_e4m3_row_op(const at::Tensor& x, c10::optional<at::Tensor> row_token,
+                            c10::optional<at::Tensor> nrows_dev, int64_t nrows, at::Tensor& q, at::Tensor& scales) {
+  AFB_CHECK_DT(x, at::kBFloat16);
+  AFB_CHECK_DT(scales, at::kFloat);
+  TORCH_CHECK(x.stride(-1) == 1 && x.stride(0) % 8 == 0, "x rows must be contiguous and 16-byte aligned");
+  const int K = x.size(1);
+  TORCH_CHECK(q.size(1) == K && q.stride(0) == K && q.size(0) >= nrows && scales.size(0) >= nrows,
+              "quant_rows_e4m3_row shapes");
+  check_rc(afb::quant_rows_e4m3_row(x.data_ptr(), x.stride(0), optr<int>(row_token), optr<int>(nrows_dev), nrows, K,
+                                    q.data_ptr(), ptr<float>(scales), stream()),
+           "quant_rows_e4m3_row");
 }
 
 void quant_rows_e4m3_op(const at::Tensor& x, c10::optional<at::Tensor> row_token, c10::optional<at::Tensor> nrows_dev,
@@ -89,20 +111,23 @@ void quant_rows_e4m3_op(const at::Tensor& x, c10::optional<at::Tensor> row_token
 // Expert-parallel exchange context: the region layout of the symmetric heap and the local counters.
 struct EpCtx {
   afb::EpArgs a;
-  EpCtx(int64_t world, int64_t rank, int64_t T_cap, int64_t H, int64_t k, std::vector<int64_t> peers,
+  EpCtx(int64_t world, int64_t rank, int64_t T_cap, int64_t H, int64_t k, int64_t E_local, std::vector<int64_t> peers,
         std::vector<int64_t> offsets, int64_t ld_s, const at::Tensor& done, const at::Tensor& sent,
-        const at::Tensor& expected) {
+        const at::Tensor& expected, const at::Tensor& wait_done) {
     TORCH_CHECK(world >= 1 && world <= afb::EP_MAX_RANKS && (int64_t)peers.size() == world, "EpCtx: world/peers");
-    TORCH_CHECK(offsets.size() == 6, "EpCtx: offsets = (x, s, ids, w, comb, flags)");
+    TORCH_CHECK(offsets.size() == 8, "EpCtx: offsets = (x, s, ids, w, comb, flags, rcnt, rlist)");
     AFB_CHECK_DT(done, at::kInt);
     AFB_CHECK_DT(sent, at::kLong);
     AFB_CHECK_DT(expected, at::kLong);
-    TORCH_CHECK(done.numel() >= 2 && sent.numel() >= 2 && expected.numel() >= 2, "EpCtx: counters");
+    AFB_CHECK_DT(wait_done, at::kInt);
+    TORCH_CHECK(done.numel() >= 2 && sent.numel() >= 2 && expected.numel() >= 2 && wait_done.numel() >= 2,
+                "EpCtx: counters");
     a.world = (int)world;
     a.rank = (int)rank;
     a.T_cap = (int)T_cap;
     a.H = (int)H;
     a.k = (int)k;
+    a.E_local = (int)E_local;
     for (int p = 0; p < world; ++p) a.peer[p] = reinterpret_cast<uint8_t*>((uintptr_t)peers[p]);
     a.off_x = offsets[0];
     a.off_s = offsets[1];
@@ -110,29 +135,54 @@ struct EpCtx {
     a.off_w = offsets[3];
     a.off_comb = offsets[4];
     a.off_flags = offsets[5];
+    a.off_rcnt = offsets[6];
+    a.off_rlist = offsets[7];
     a.ld_s = (int)ld_s;
     a.done = reinterpret_cast<unsigned*>(done.data_ptr());
     a.sent = reinterpret_cast<unsigned long long*>(sent.data_ptr());
     a.expected = reinterpret_cast<unsigned long long*>(expected.data_ptr());
+    a.wait_done = reinterpret_cast<unsigned*>(wait_done.data_ptr());
   }
-  void dispatch(const at::Tensor& x, int64_t T, const at::Tensor& ids, const at::Tensor& w) {
+  // lcnt / llist: this rank's router lists (int [E], [E, T_cap]) of local entry indices
+  void dispatch(const at::Tensor& x, int64_t T, const at::Tensor& ids, const at::Tensor& w, const at::Tensor& lcnt,
+                const at::Tensor& llist) {
     AFB_CHECK_DT(x, at::kBFloat16);
     AFB_CHECK_DT(ids, at::kInt);
     AFB_CHECK_DT(w, at::kFloat);
+    AFB_CHECK_DT(lcnt, at::kInt);
+    AFB_CHECK_DT(llist, at::kInt);
     TORCH_CHECK(x.stride(1) == 1 && x.size(1) == a.H && ids.size(1) == a.k, "ep dispatch shapes");
+    TORCH_CHECK(lcnt.numel() >= (int64_t)a.E_local * a.world && llist.dim() == 2 && llist.size(1) == a.T_cap &&
+                    llist.is_contiguous(),
+                "ep dispatch lists: cnt [E], list [E, T_cap]");
     afb::EpArgs b = a;
     b.T = (int)T;
+    b.lcnt = ptr<int>(lcnt);
+    b.llist = ptr<int>(llist);
     check_rc(afb::ep_dispatch(b, x.data_ptr(), x.stride(0), ptr<int>(ids), ptr<float>(w), stream()), "ep_dispatch");
   }
   void wait(int64_t type) { check_rc(afb::ep_wait(a, (int)type, status_ptr(current_device()), stream()), "ep_wait"); }
-  void gather(const at::Tensor& row_token, const at::Tensor& nrows, at::Tensor& xq, at::Tensor& xs) {
-    AFB_CHECK_DT(row_token, at::kInt);
-    AFB_CHECK_DT(nrows, at::kInt);
-    AFB_CHECK_DT(xs, at::kFloat);
-    TORCH_CHECK(xq.size(1) == a.H && xq.size(0) <= row_token.size(0), "ep gather shapes");
-    check_rc(afb::ep_gather(a, ptr<int>(row_token), ptr<int>(nrows), xq.size(0), xq.data_ptr(), ptr<float>(xs),
-                            xs.stride(0), stream()),
-             "ep_gather");
+  // per-row e4m3 of the entry rows h [world * T_cap * k, I] that this rank's lists name
+  void quant_routed(const at::Tensor& h, at::Tensor& q, at::Tensor& scales) {
+    AFB_CHECK_DT(h, at::kBFloat16);
+    AFB_CHECK_DT(scales, at::kFloat);
+    AFB_CHECK_CONTIG(h);
+    TORCH_CHECK(q.sizes() == h.sizes() && q.is_contiguous() && scales.numel() >= h.size(0), "quant_routed shapes");
+    const int* cnt = reinterpret_cast<const int*>(a.peer[a.rank] + a.off_rcnt);
+    const int* list = reinterpret_cast<const int*>(a.peer[a.rank] + a.off_rlist);
+    check_rc(afb::quant_routed_rows(h.data_ptr(), h.size(1), cnt, list, a.world, a.E_local, a.T_cap, q.data_ptr(),
+                                    ptr<float>(scales), stream()),
+             "quant_routed_rows");
+  }
+  // out[t] = resid[t] + sigmoid(gate) * shared[t] + the k routed rows of token t from the combine region; waits for
+  // every rank's combine rows first (in the kernel) and counts the exchange consumed
+  void combine(const at::Tensor& comb, c10::optional<at::Tensor> shared, c10::optional<at::Tensor> router_logits,
+               int64_t sg_col, c10::optional<at::Tensor> resid, at::Tensor& out, int64_t T) {
+    const int ld = router_logits.has_value() ? router_logits->stride(0) : 0;
+    check_rc(afb::moe_combine(comb.data_ptr(), nullptr, a.k, optr<void>(shared), optr<float>(router_logits), ld,
+                              sg_col, optr<void>(resid), out.data_ptr(), (int)T, a.H, stream(), &a,
+                              status_ptr(current_device())),
+             "moe_combine(ep)");
   }
   static int current_device() {
     int d = 0;
@@ -141,15 +191,23 @@ struct EpCtx {
   }
 };
 
-void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& offsets,
-                      const at::Tensor& x_q, const at::Tensor& x_scales, bool pair, c10::optional<at::Tensor> out_q,
-                      c10::optional<at::Tensor> out_scales, c10::optional<at::Tensor> out_bf16,
-                      c10::optional<at::Tensor> route_w, c10::optional<at::Tensor> row_entry,
-                      c10::optional<at::Tensor> dbg, const EpCtx* ep) {
-  AFB_CHECK_DT(offsets, at::kInt);
+// Routed-expert GEMM (INT3 tile layout, or block FP8 when codes is e4m3). route_cnt int [srcs, E] (or [E]),
+// route_list int [srcs, E, cap] (or [E, cap]): the entries of each expert; an entry's activation row is
+// entry / x_div. pair=True: w13 (INT3: bf16 h per entry in out_bf16; FP8: e4m3 h + group scales per entry);
+// pair=False: w2 with the routing weight per entry (out_bf16 per entry, or the expert-parallel combine scatter).
+// ep: the exchange context (w2: scatter + publish; w13 with ep_wait: wait for the dispatch in the prologue).
+void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const at::Tensor& route_cnt,
+                      const at::Tensor& route_list, int64_t x_div, const at::Tensor& x_q, const at::Tensor& x_scales,
+                      bool pair, c10::optional<at::Tensor> out_q, c10::optional<at::Tensor> out_scales,
+                      c10::optional<at::Tensor> out_bf16, c10::optional<at::Tensor> route_w,
+                      c10::optional<at::Tensor> dbg, const EpCtx* ep, bool ep_wait) {
+  AFB_CHECK_DT(route_cnt, at::kInt);
+  AFB_CHECK_DT(route_list, at::kInt);
   AFB_CHECK_CONTIG(codes);
   AFB_CHECK_CONTIG(scales);
   AFB_CHECK_CONTIG(x_q);
+  AFB_CHECK_CONTIG(route_cnt);
+  AFB_CHECK_CONTIG(route_list);
   afb::MoeGemmArgs a;
   if (codes.scalar_type() == at::kFloat8_e4m3fn) {  // block-FP8 experts: weights [E, rows, K], scales [E, rows/128, K/128]
     AFB_CHECK_DT(scales, at::kFloat);
@@ -172,33 +230,56 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
     a.rows = codes.size(1) * 128;
     a.K = codes.size(2) * 128;
   }
-  TORCH_CHECK(offsets.numel() == a.num_experts + 1, "offsets must have E+1 entries");
-  TORCH_CHECK(x_q.size(1) == a.K, "x_q width");
-  a.expert_offsets = ptr<int>(offsets);
+  const int E = a.num_experts;
+  const int srcs = route_cnt.dim() == 2 ? route_cnt.size(0) : 1;
+  TORCH_CHECK(route_cnt.numel() == (int64_t)srcs * E && route_list.dim() == route_cnt.dim() + 1 &&
+                  route_list.numel() % ((int64_t)srcs * E) == 0,
+              "route_cnt [srcs, E] and route_list [srcs, E, cap]");
+  a.route_cnt = ptr<int>(route_cnt);
+  a.route_list = ptr<int>(route_list);
+  a.route_srcs = srcs;
+  a.route_cap = route_list.size(-1);
+  a.x_div = (int)x_div;
+  TORCH_CHECK(x_q.size(1) == a.K && x_q.stride(0) == a.K, "x_q [rows, K]");
   a.x_q = x_q.data_ptr();
   a.x_scales = ptr<float>(x_scales);
-  a.ld_xs = x_scales.stride(0);
-  a.num_rows_total = x_q.size(0);
-  TORCH_CHECK(a.ld_xs % 4 == 0 && x_scales.size(1) >= a.num_rows_total + 32,
-              "x_scales must be group-major [K/128, >= rows + 32] with a row stride divisible by 4");
+  a.x_rows = x_q.size(0);
+  if (a.fp8_w) {  // 1 x 128 activation scales, group-major
+    a.ld_xs = x_scales.stride(0);
+    TORCH_CHECK(x_scales.dim() == 2 && x_scales.size(0) == a.K / 128 && x_scales.size(1) >= a.x_rows,
+                "fp8 experts: x_scales must be group-major [K/128, >= rows]");
+  } else {  // one activation scale per row
+    TORCH_CHECK(x_scales.dim() == 1 && x_scales.size(0) >= a.x_rows, "int3 experts: x_scales [rows]");
+  }
   if (pair) {
-    TORCH_CHECK(!ep, "expert-parallel output is the w2 GEMM's");
-    TORCH_CHECK(out_q.has_value() && out_scales.has_value(), "pair needs out_q and out_scales");
-    a.out_q = optr<uint8_t>(out_q);
-    a.out_scales = optr<float>(out_scales);
-    a.ld_os = out_scales->stride(0);
-    TORCH_CHECK(out_scales->size(1) >= a.num_rows_total, "out_scales capacity");
-    a.out_ld = out_q->stride(0);
-    TORCH_CHECK(out_q->size(1) == a.rows / 2, "out_q width must be I");
+    if (a.fp8_w) {  // e4m3 h with a scale per (entry, 128 columns), the next FP8 GEMM's input
+      TORCH_CHECK(out_q.has_value() && out_scales.has_value(), "fp8 pair needs out_q and out_scales");
+      a.out_q = optr<uint8_t>(out_q);
+      a.out_scales = optr<float>(out_scales);
+      a.ld_os = out_scales->stride(0);
+      a.out_ld = out_q->stride(0);
+      TORCH_CHECK(out_q->size(1) == a.rows / 2, "out_q width must be I");
+    } else {  // bf16 h (quantised per row again before w2)
+      TORCH_CHECK(out_bf16.has_value(), "int3 pair needs out_bf16 (h)");
+      AFB_CHECK_DT((*out_bf16), at::kBFloat16);
+      TORCH_CHECK(out_bf16->size(1) == a.rows / 2 && out_bf16->stride(1) == 1, "h must be bf16 [entries, I]");
+      a.out_bf16 = out_bf16->data_ptr();
+      a.out_ld = out_bf16->stride(0);
+    }
+    if (ep_wait) {
+      TORCH_CHECK(ep, "ep_wait needs the exchange context");
+      a.ep_wait_flags = reinterpret_cast<const uint64_t*>(ep->a.peer[ep->a.rank] + ep->a.off_flags);  // dispatch
+      a.ep_expected = ep->a.expected;
+      a.ep_wait_done = ep->a.wait_done;
+      TORCH_CHECK(srcs == ep->a.world, "expert-parallel lists have one row per rank");
+    }
   } else {
     TORCH_CHECK(out_bf16.has_value(), "w2 needs out_bf16");
     a.out_bf16 = out_bf16->data_ptr();
     a.out_ld = out_bf16->stride(0);
     a.route_w = optr<float>(route_w);
-    a.row_entry = optr<int>(row_entry);
-    TORCH_CHECK(!a.route_w || a.row_entry, "route_w needs row_entry");
     if (ep) {
-      TORCH_CHECK(a.route_w && a.row_entry && a.out_ld == ep->a.H, "expert-parallel w2 needs route_w and row_entry");
+      TORCH_CHECK(a.route_w && a.out_ld == ep->a.H, "expert-parallel w2 needs route_w");
       a.ep_world = ep->a.world;
       a.ep_rank = ep->a.rank;
       a.ep_entries_per_rank = ep->a.T_cap * ep->a.k;
@@ -214,12 +295,12 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
            a.fp8_w ? "moe_fp8_gemm" : "moe_int3_gemm");
 }
 
-void moe_combine_op(const at::Tensor& y, const at::Tensor& entry_row, int64_t k, c10::optional<at::Tensor> shared,
+void moe_combine_op(const at::Tensor& y, c10::optional<at::Tensor> entry_row, int64_t k, c10::optional<at::Tensor> shared,
                     c10::optional<at::Tensor> router_logits, int64_t sg_col, c10::optional<at::Tensor> resid,
                     at::Tensor& out) {
   const int T = out.size(0), H = out.size(1);
   const int ld = router_logits.has_value() ? router_logits->stride(0) : 0;
-  check_rc(afb::moe_combine(y.data_ptr(), ptr<int>(entry_row), k, optr<void>(shared), optr<float>(router_logits), ld,
+  check_rc(afb::moe_combine(y.data_ptr(), optr<int>(entry_row), k, optr<void>(shared), optr<float>(router_logits), ld,
                             sg_col, optr<void>(resid), out.data_ptr(), T, H, stream()),
            "moe_combine");
 }
@@ -1154,19 +1235,23 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("rot"), py::arg("qw"), py::arg("kw"), py::arg("positions"), py::arg("slots"), py::arg("cos_t"),
         py::arg("sin_t"), py::arg("eps"), py::arg("q_out"), py::arg("kcache"), py::arg("vcache"),
         py::arg("kscale") = py::none(), py::arg("vscale") = py::none());
-  m.def("router_topk", &router_topk_op);
+  m.def("router_topk", &router_topk_op, py::arg("logits"), py::arg("E"), py::arg("k"), py::arg("renorm"),
+        py::arg("ids"), py::arg("weights"), py::arg("cnt") = py::none(), py::arg("list") = py::none());
   m.def("expert_sort", &expert_sort_op);
   m.def("quant_rows_e4m3", &quant_rows_e4m3_op);
+  m.def("quant_rows_e4m3_row", &quant_rows_e4m3_row_op);
   m.def("moe_combine", &moe_combine_op);
-  m.def("moe_int3_gemm", &moe_int3_gemm_op, py::arg("codes"), py::arg("scales"), py::arg("offsets"), py::arg("x_q"),
-        py::arg("x_scales"), py::arg("pair"), py::arg("out_q"), py::arg("out_scales"), py::arg("out_bf16"),
-        py::arg("route_w"), py::arg("row_entry"), py::arg("dbg") = py::none(), py::arg("ep") = nullptr);
+  m.def("moe_int3_gemm", &moe_int3_gemm_op, py::arg("codes"), py::arg("scales"), py::arg("route_cnt"),
+        py::arg("route_list"), py::arg("x_div"), py::arg("x_q"), py::arg("x_scales"), py::arg("pair"), py::arg("out_q"),
+        py::arg("out_scales"), py::arg("out_bf16"), py::arg("route_w"), py::arg("dbg") = py::none(),
+        py::arg("ep") = nullptr, py::arg("ep_wait") = false);
   py::class_<EpCtx>(m, "EpCtx")
-      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, std::vector<int64_t>, std::vector<int64_t>, int64_t,
-                    const at::Tensor&, const at::Tensor&, const at::Tensor&>())
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, std::vector<int64_t>, std::vector<int64_t>,
+                    int64_t, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&>())
       .def("dispatch", &EpCtx::dispatch)
       .def("wait", &EpCtx::wait)
-      .def("gather", &EpCtx::gather);
+      .def("quant_routed", &EpCtx::quant_routed)
+      .def("combine", &EpCtx::combine);
   m.def("swiglu", &swiglu_op);
   m.def("int3_dequant", &int3_dequant_op);
   m.def("int3_scale_grad", &int3_scale_grad_op);

@@ -5,15 +5,21 @@ Per MoE layer (one launch each, all on the current stream, no host sync):
 1. router GEMM (tcgen05, fp32 out) over ``[W_router; w_shared_gate; 0-pad]`` -- the shared-expert gate logit rides
    along as column E;
 2. softmax + top-k + renormalise (one warp per token);
-3. stable counting sort of the (token, slot) entries by expert;
-4. gather + e4m3 quantisation of the routed rows, one scale per (row, 128 columns);
-5. INT3 w13 GEMM with SwiGLU and e4m3 requantisation fused in its epilogue;
-6. INT3 w2 GEMM with the routing weight fused in its epilogue;
-7. shared expert (two dense GEMMs + SwiGLU);
-8. combine: residual + sigmoid(gate) * shared + sum of the k routed rows, in a fixed order.
+   (the same kernel appends every (token, slot) entry to its expert's list: no sort);
+3. e4m3 quantisation of each token row, one scale per row (the reference's W3A8 activation rule:
+   s = max(amax, 1e-30) / 448, ``training/work/qwen38fn_lora/int3_moe.py:1-14,108-118``);
+5. INT3 w13 GEMM over each expert's listed entries (rows gathered inside the kernel) with SwiGLU fused in its
+   epilogue, h stored bf16 per entry;
+6. per-row e4m3 quantisation of h;
+7. INT3 w2 GEMM with the routing weight fused in its epilogue, y per entry;
+8. shared expert (two dense GEMMs + SwiGLU);
+9. combine: residual + sigmoid(gate) * shared + sum of the k routed rows of each token, in slot order.
 
-``moe_reference`` computes the same contract in fp32 PyTorch (activations quantised per 128-group to e4m3,
-weights (code - 4) * scale, group partial sums scaled in fp32).
+Block-FP8 experts (the QAD teacher) keep the block-FP8 contract instead: 1 x 128 activation scales for both GEMMs
+and the w13 epilogue's e4m3-per-128 SwiGLU output.
+
+``moe_reference`` computes the same contracts in fp32 PyTorch (weights (code - 4) * scale with group partial sums
+scaled in fp32; activations per row, h rounded to bf16 before its quantisation).
 """
 from __future__ import annotations
 
@@ -121,31 +127,29 @@ class Fp8ExpertBank:
         return dq(self.w13_codes, self.w13_scales), dq(self.w2_codes, self.w2_scales)
 
 
-SEG_PAD = 8  # expert segments start on multiples of 8 rows (16-byte bulk copies of per-row scales)
-
-
 class MoEWorkspace:
-    """Preallocated buffers for up to ``max_tokens`` tokens (stable addresses for CUDA graphs)."""
+    """Preallocated buffers for up to ``max_tokens`` tokens (stable addresses for CUDA graphs). Routed rows are
+    numbered by entry (token * k + slot)."""
 
     def __init__(self, max_tokens: int, E: int, k: int, H: int, I: int, Is: int, device):
-        R = max_tokens * k + (SEG_PAD - 1) * E  # routed rows + per-expert segment padding
-        self.k, self.E = k, E
+        n = max_tokens * k
+        self.k, self.E, self.rows = k, E, n
         dev = torch.device(device)
         i32 = dict(dtype=torch.int32, device=dev)
         self.logits = torch.empty(max_tokens, E + 8, dtype=torch.float32, device=dev)
         self.ids = torch.empty(max_tokens, k, **i32)
         self.weights = torch.empty(max_tokens, k, dtype=torch.float32, device=dev)
-        self.offsets = torch.empty(E + 1, **i32)
-        self.row_token = torch.empty(R, **i32)
-        self.row_entry = torch.empty(R, **i32)
-        self.entry_row = torch.empty(max_tokens * k, **i32)
-        self.rows = R
-        self.xq = torch.empty(R, H, dtype=torch.float8_e4m3fn, device=dev)
-        ld = (R + 32 + 3) // 4 * 4  # +32: chunk over-read slack; multiple of 4 for 16-byte bulk copies
-        self.xs = torch.zeros(H // 128, ld, dtype=torch.float32, device=dev)
-        self.hq = torch.empty(R, I, dtype=torch.float8_e4m3fn, device=dev)
-        self.hs = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
-        self.y = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+        self.cnt = torch.zeros(E, **i32)                 # entries per expert (the router fills both)
+        self.list = torch.zeros(E, max_tokens, **i32)    # each expert's entries
+        self.xq = torch.empty(max_tokens, H, dtype=torch.float8_e4m3fn, device=dev)
+        self.xs = torch.zeros(max_tokens, dtype=torch.float32, device=dev)   # INT3: one scale per token row
+        self.h = torch.empty(n, I, dtype=torch.bfloat16, device=dev)         # INT3: w13 output (SwiGLU, bf16)
+        self.hq = torch.empty(n, I, dtype=torch.float8_e4m3fn, device=dev)
+        self.hs = torch.zeros(n, dtype=torch.float32, device=dev)
+        # block-FP8 experts: 1 x 128 activation scales, group-major
+        self.xs_g = torch.zeros(H // 128, max_tokens, dtype=torch.float32, device=dev)
+        self.hs_g = torch.zeros(I // 128, n, dtype=torch.float32, device=dev)
+        self.y = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
         self.sh_gu = torch.empty(max_tokens, 2 * Is, dtype=torch.bfloat16, device=dev)
         self.sh_h = torch.empty(max_tokens, Is, dtype=torch.bfloat16, device=dev)
         self.sh_out = torch.empty(max_tokens, H, dtype=torch.bfloat16, device=dev)
@@ -171,21 +175,33 @@ def moe_forward(x: torch.Tensor, resid: torch.Tensor, router_ext: torch.Tensor, 
     logits = ws.logits[:T]
     c.gemm(x, router_ext, out=logits, out_fp32=True)
     ids, w = ws.ids[:T], ws.weights[:T]
-    c.router_topk(logits, E, k, renorm, ids, w)
-    R = n + (SEG_PAD - 1) * E
-    c.expert_sort(ids, E, None, ws.offsets, ws.row_token[:R], ws.row_entry[:R], ws.entry_row[:n], SEG_PAD)
-    # rows actually used = offsets[E] (device scalar): the launch covers the capacity, the kernel stops early
-    c.quant_rows_e4m3(x, ws.row_token[:R], ws.offsets[E:], R, ws.xq[:R], ws.xs, True)
-    c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.offsets, ws.xq[:R], ws.xs, True, ws.hq[:R], ws.hs, None,
-                    None, None)
-    c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.offsets, ws.hq[:R], ws.hs, False, None, None, ws.y[:R],
-                    w.view(-1), ws.row_entry[:R])
+    c.router_topk(logits, E, k, renorm, ids, w, ws.cnt, ws.list)
+    expert_gemms(c, bank, ws, x, T, w.view(-1))
     c.gemm(x, shared_w13, out=ws.sh_gu[:T])
     c.swiglu(ws.sh_gu[:T], ws.sh_h[:T])
     c.gemm(ws.sh_h[:T], shared_w2, out=ws.sh_out[:T])
     out = torch.empty_like(x) if out is None else out
-    c.moe_combine(ws.y[:R], ws.entry_row[:n], k, ws.sh_out[:T], logits, E, resid, out)
+    c.moe_combine(ws.y[:n], None, k, ws.sh_out[:T], logits, E, resid, out)
     return out
+
+
+def expert_gemms(c, bank, ws, x, T, route_w):
+    """The listed entries of ``T`` tokens -> w13 -> w2 on the native kernels; y rows per entry."""
+    k = ws.k
+    n = T * k
+    if isinstance(bank, Fp8ExpertBank):
+        c.quant_rows_e4m3(x, None, None, T, ws.xq[:T], ws.xs_g, True)
+        c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.cnt, ws.list, k, ws.xq[:T], ws.xs_g, True, ws.hq[:n],
+                        ws.hs_g, None, None)
+        c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.cnt, ws.list, 1, ws.hq[:n], ws.hs_g, False, None, None,
+                        ws.y[:n], route_w)
+        return
+    c.quant_rows_e4m3_row(x, None, None, T, ws.xq[:T], ws.xs)
+    c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.cnt, ws.list, k, ws.xq[:T], ws.xs, True, None, None,
+                    ws.h[:n], None)
+    c.quant_rows_e4m3_row(ws.h[:n], None, None, n, ws.hq[:n], ws.hs)
+    c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.cnt, ws.list, 1, ws.hq[:n], ws.hs, False, None, None,
+                    ws.y[:n], route_w)
 
 
 def moe_reference(x, resid, router_ext, bank: Int3ExpertBank, shared_w13, shared_w2, k, renorm=True):
@@ -199,15 +215,23 @@ def moe_reference(x, resid, router_ext, bank: Int3ExpertBank, shared_w13, shared
         w = w / w.sum(-1, keepdim=True)
     w13, w2 = bank.dequant(torch.float32)
     I = bank.inter
+    fp8_bank = isinstance(bank, Fp8ExpertBank)
+
+    def q(a):  # the activation quantisation of each contract, returned dequantised
+        if fp8_bank:
+            aq, s_ = fp8q.quantize_act_groups(a)
+            return fp8q.dequant_act_groups(aq, s_)
+        aq, s_ = fp8q.quantize_rows(a)
+        return aq.float() * s_[:, None]
+
     out = torch.zeros_like(xf)
     for e in torch.unique(ids).tolist():
         tok, slot = (ids == e).nonzero(as_tuple=True)
-        xq, xs = fp8q.quantize_act_groups(x[tok].float())
-        xd = fp8q.dequant_act_groups(xq, xs)
-        h = xd @ w13[e].t()
+        h = q(x[tok].float()) @ w13[e].t()
         hh = F.silu(h[:, :I]) * h[:, I:]
-        hq, hs = fp8q.quantize_act_groups(hh)
-        y = fp8q.dequant_act_groups(hq, hs) @ w2[e].t()
+        if not fp8_bank:
+            hh = hh.bfloat16().float()  # the server stores the SwiGLU output in bf16 before quantising it
+        y = q(hh) @ w2[e].t()
         out.index_add_(0, tok, y * w[tok, slot][:, None])
     sh = (F.silu(xf @ shared_w13.float()[: shared_w13.shape[0] // 2].t()) *
           (xf @ shared_w13.float()[shared_w13.shape[0] // 2:].t())) @ shared_w2.float().t()

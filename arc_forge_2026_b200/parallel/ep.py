@@ -2,10 +2,12 @@
 the routed experts are split in contiguous blocks of ``E / world`` per rank, and every MoE layer exchanges tokens
 through a symmetric device heap with the native kernels of ``csrc/ep.cu``:
 
-    router (local) -> ep_dispatch (e4m3 quantisation fused with the all-gather to every rank's receive region)
-    -> shared expert (local, overlaps the exchange) -> ep_wait -> expert_sort of all ranks' entries for the
-    local experts -> ep_gather -> w13 GEMM -> w2 GEMM whose epilogue stores each routed row into its token owner's
-    combine region and publishes the exchange -> ep_wait -> combine (k rows in slot order + shared + residual).
+    router (local; also lists each expert's entries) -> ep_dispatch (per-row e4m3 quantisation fused with the
+    all-gather to every rank's receive region; the lists go to each expert's owner) -> shared expert (local, overlaps
+    the exchange) -> w13 GEMM (waits in its prologue for every rank's dispatch, gathers the listed rows itself) ->
+    per-row requantisation of the listed h rows -> w2 GEMM whose epilogue stores each routed row into its token
+    owner's combine region and publishes the exchange -> combine (waits in its prologue; k rows in slot order +
+    shared + residual). No sort, gather or wait launches: 9 kernels per layer besides the router GEMM.
 
 The reference splits experts the same way (``--ep 4`` in its B200 server configs, ``training/run_records/A1/
 config/p30241.server.json:32``) and, on its L4 stack, dispatches by all-gather and combines by a reduce to the
@@ -21,7 +23,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops._ext import C
-from ..ops.moe import SEG_PAD, Int3ExpertBank
+from ..ops.moe import Int3ExpertBank
 
 EP_DISPATCH, EP_COMBINE = 0, 1
 MAX_RANKS = 8
@@ -68,12 +70,14 @@ class ExpertParallel:
         self.ld_s = (rows + 32 + 3) // 4 * 4
         off_x = 0
         off_s = _align(off_x + rows * H)
-        off_ids = _align(off_s + (H // 128) * self.ld_s * 4)
+        off_ids = _align(off_s + self.ld_s * 4)  # one activation scale per received row
         off_w = _align(off_ids + rows * k * 4)
         off_comb = _align(off_w + rows * k * 4)
         off_flags = _align(off_comb + T_cap * k * H * 2)
-        total = _align(off_flags + 2 * MAX_RANKS * 8)
-        self.offsets = [off_x, off_s, off_ids, off_w, off_comb, off_flags]
+        off_rcnt = _align(off_flags + 2 * MAX_RANKS * 8)     # [world sources][E_local] entries per local expert
+        off_rlist = _align(off_rcnt + world * self.E_local * 4)  # [world][E_local][T_cap] those entries
+        total = _align(off_rlist + world * self.E_local * T_cap * 4)
+        self.offsets = [off_x, off_s, off_ids, off_w, off_comb, off_flags, off_rcnt, off_rlist]
         ext = C()
         self.heap = ext.SymmHeap(total, rank, world, dev.index if dev.index is not None else 0)
         if world > 1:
@@ -82,17 +86,20 @@ class ExpertParallel:
             self.heap.open(handles)
             dist.barrier(group=group)  # every heap is zeroed and mapped before any rank stores a flag
         buf = self.heap.tensor()
+        self.recv_x = buf[off_x:off_x + rows * H].view(torch.float8_e4m3fn).view(rows, H)
+        self.recv_s = buf[off_s:off_s + rows * 4].view(torch.float32)
+        self.rcnt = buf[off_rcnt:off_rcnt + world * self.E_local * 4].view(torch.int32).view(world, self.E_local)
+        self.rlist = buf[off_rlist:off_rlist + world * self.E_local * T_cap * 4].view(torch.int32).view(
+            world, self.E_local, T_cap)
         self.recv_ids = buf[off_ids:off_ids + rows * k * 4].view(torch.int32).view(rows, k)
         self.recv_w = buf[off_w:off_w + rows * k * 4].view(torch.float32)
         self.comb = buf[off_comb:off_comb + T_cap * k * H * 2].view(torch.bfloat16).view(T_cap * k, H)
         self.done = torch.zeros(2, dtype=torch.int32, device=dev)
         self.sent = torch.zeros(2, dtype=torch.int64, device=dev)
         self.expected = torch.zeros(2, dtype=torch.int64, device=dev)
-        self.ctx = ext.EpCtx(world, rank, T_cap, H, k, list(self.heap.peers()), self.offsets, self.ld_s, self.done,
-                             self.sent, self.expected)
-        self.expert_map = torch.full((E,), -1, dtype=torch.int32, device=dev)
-        self.expert_map[self.e0:self.e1] = torch.arange(self.E_local, dtype=torch.int32, device=dev)
-        self.identity = torch.arange(T_cap * k, dtype=torch.int32, device=dev)  # combine rows are [t, slot]
+        self.wait_done = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.ctx = ext.EpCtx(world, rank, T_cap, H, k, self.E_local, list(self.heap.peers()), self.offsets, self.ld_s,
+                             self.done, self.sent, self.expected, self.wait_done)
 
     def close(self):
         if self.heap is not None:
@@ -101,28 +108,23 @@ class ExpertParallel:
 
 
 class EPMoEWorkspace:
-    """Per-layer buffers of the expert-parallel MoE (fixed addresses: CUDA-graph safe)."""
+    """Per-layer buffers of the expert-parallel MoE (fixed addresses: CUDA-graph safe). Entries are numbered over
+    all ranks (source * T_cap * k + t * k + slot)."""
 
     def __init__(self, ep: ExpertParallel, I: int, Is: int, device):
         dev = torch.device(device)
-        T, k, H, E_loc = ep.T_cap, ep.k, ep.H, ep.E_local
+        T, k, H, E = ep.T_cap, ep.k, ep.H, ep.E
         n = ep.world * T * k
-        R = n + (SEG_PAD - 1) * E_loc
         i32 = dict(dtype=torch.int32, device=dev)
-        self.n, self.rows = n, R
-        self.logits = torch.empty(T, ep.E + 8, dtype=torch.float32, device=dev)
+        self.n = n
+        self.logits = torch.empty(T, E + 8, dtype=torch.float32, device=dev)
         self.ids = torch.empty(T, k, **i32)
         self.weights = torch.empty(T, k, dtype=torch.float32, device=dev)
-        self.offsets = torch.empty(E_loc + 1, **i32)
-        self.row_token = torch.empty(R, **i32)
-        self.row_entry = torch.empty(R, **i32)
-        self.entry_row = torch.empty(n, **i32)
-        self.xq = torch.empty(R, H, dtype=torch.float8_e4m3fn, device=dev)
-        ld = (R + 32 + 3) // 4 * 4
-        self.xs = torch.zeros(H // 128, ld, dtype=torch.float32, device=dev)
-        self.hq = torch.empty(R, I, dtype=torch.float8_e4m3fn, device=dev)
-        self.hs = torch.zeros(I // 128, ld, dtype=torch.float32, device=dev)
-        self.y = torch.empty(8, H, dtype=torch.bfloat16, device=dev)  # unused: w2 rows go to the combine regions
+        self.lcnt = torch.zeros(E, **i32)       # this rank's entries per expert (router)
+        self.llist = torch.zeros(E, T, **i32)   # and the entries themselves
+        self.h = torch.empty(n, I, dtype=torch.bfloat16, device=dev)
+        self.hq = torch.empty(n, I, dtype=torch.float8_e4m3fn, device=dev)
+        self.hs = torch.zeros(n, dtype=torch.float32, device=dev)
         self.sh_gu = torch.empty(T, 2 * Is, dtype=torch.bfloat16, device=dev)
         self.sh_h = torch.empty(T, Is, dtype=torch.bfloat16, device=dev)
         self.sh_out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
@@ -141,22 +143,18 @@ def moe_forward_ep(x: torch.Tensor, resid: torch.Tensor, router_ext: torch.Tenso
     ids, w = ws.ids[:T], ws.weights[:T]
     if T > 0:
         c.gemm(x, router_ext, out=logits, out_fp32=True)
-        c.router_topk(logits, E, k, renorm, ids, w)
-    ep.ctx.dispatch(x, T, ws.ids, ws.weights)
+    c.router_topk(logits, E, k, renorm, ids, w, ws.lcnt, ws.llist)  # T == 0: the lists are only cleared
+    ep.ctx.dispatch(x, T, ws.ids, ws.weights, ws.lcnt, ws.llist)
     if T > 0:  # the shared expert runs while the peers' dispatch stores land
         c.gemm(x, shared_w13, out=ws.sh_gu[:T])
         c.swiglu(ws.sh_gu[:T], ws.sh_h[:T])
         c.gemm(ws.sh_h[:T], shared_w2, out=ws.sh_out[:T])
-    ep.ctx.wait(EP_DISPATCH)
-    R = ws.rows
-    c.expert_sort(ep.recv_ids, ep.E_local, ep.expert_map, ws.offsets, ws.row_token, ws.row_entry, ws.entry_row,
-                  SEG_PAD)
-    ep.ctx.gather(ws.row_token, ws.offsets[ep.E_local:], ws.xq, ws.xs)
-    c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.offsets, ws.xq[:R], ws.xs, True, ws.hq[:R], ws.hs, None,
-                    None, None)
-    c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.offsets, ws.hq[:R], ws.hs, False, None, None, ep.comb,
-                    ep.recv_w, ws.row_entry[:R], None, ep.ctx)
-    ep.ctx.wait(EP_COMBINE)
-    if T > 0:
-        c.moe_combine(ep.comb, ep.identity[:T * k], k, ws.sh_out[:T], logits, E, resid, out)
+    # w13 waits for every rank's dispatch in its prologue; rows and scales come from the receive region
+    c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ep.rcnt, ep.rlist, k, ep.recv_x, ep.recv_s, True, None, None,
+                    ws.h, None, None, ep.ctx, True)
+    ep.ctx.quant_routed(ws.h, ws.hq, ws.hs)
+    c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ep.rcnt, ep.rlist, 1, ws.hq, ws.hs, False, None, None, ep.comb,
+                    ep.recv_w, None, ep.ctx)
+    ep.ctx.combine(ep.comb, ws.sh_out[:T] if T > 0 else None, logits if T > 0 else None, E,
+                   resid if T > 0 else None, out, T)
     return out

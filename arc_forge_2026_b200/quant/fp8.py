@@ -60,10 +60,12 @@ def dequant_act_groups(q: torch.Tensor, scales: torch.Tensor, group: int = BLOCK
 
 
 def quantize_rows(x: torch.Tensor):
-    """Per-row e4m3 (the W3A8 expert input format): scale = max(amax, 1e-30)/448."""
+    """Per-row e4m3 (the W3A8 expert input format): scale = max(amax, 1e-30)/448, values multiplied by the fp32
+    reciprocal of the scale (as the kernels and the reference's quantiser do) and rounded to e4m3."""
     amax = x.float().abs().amax(-1).clamp_min(1e-30)
     scale = amax / FP8_MAX
-    return (x.float() / scale[:, None]).to(E4M3), scale
+    inv = 1.0 / scale
+    return (x.float() * inv[:, None]).clamp(-FP8_MAX, FP8_MAX).to(E4M3), scale
 
 
 def block_fp8_linear_ref(x: torch.Tensor, wq: torch.Tensor, w_scale_inv: torch.Tensor, group: int = BLOCK):

@@ -48,6 +48,9 @@ def time_cuda(fn, iters: int = 20, warmup: int = 3, flush_bytes: int = 256 << 20
 
 
 def bench_moe(T=640, E=320, H=2048, I=512, k=10):
+    """The routed-expert path of one MoE layer at the verify-step shape: per-row quantisation of the token rows, the
+    w13 GEMM over each expert's listed entries (SwiGLU epilogue, bf16 h), the per-row requantisation of h and the w2
+    GEMM. Bytes are the algorithmic ones: the INT3 weights and scales once, the activations read and written once."""
     from ..ops import C
     from ..ops.moe import Int3ExpertBank, MoEWorkspace
     peaks = load_peaks()
@@ -57,32 +60,38 @@ def bench_moe(T=640, E=320, H=2048, I=512, k=10):
     x = torch.randn(T, H, device=dev).bfloat16()
     logits = torch.randn(T, E + 8, device=dev)
     c = C()
-    c.router_topk(logits, E, k, True, ws.ids[:T], ws.weights[:T])
     n = T * k
-    R = ws.rows
-    c.expert_sort(ws.ids[:T], E, None, ws.offsets, ws.row_token, ws.row_entry, ws.entry_row[:n], 8)
-    c.quant_rows_e4m3(x, ws.row_token, ws.offsets[E:], R, ws.xq, ws.xs, True)
-    w13 = lambda: c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.offsets, ws.xq, ws.xs, True,  # noqa
-                                  ws.hq, ws.hs, None, None, None)
-    w2 = lambda: c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.offsets, ws.hq, ws.hs, False, None,  # noqa
-                                 None, ws.y, ws.weights[:T].view(-1), ws.row_entry)
-    dbg = torch.zeros(148 * 4 * 3, dtype=torch.int64, device=dev)
-    c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.offsets, ws.xq, ws.xs, True, ws.hq, ws.hs, None, None, None,
-                    dbg)
+    c.router_topk(logits, E, k, True, ws.ids[:T], ws.weights[:T], ws.cnt, ws.list)
+    c.quant_rows_e4m3_row(x, None, None, T, ws.xq[:T], ws.xs)
+    rw = ws.weights[:T].reshape(-1)
+    w13 = lambda dbg=None: c.moe_int3_gemm(bank.w13_codes, bank.w13_scales, ws.cnt, ws.list, k, ws.xq[:T],  # noqa
+                                           ws.xs, True, None, None, ws.h[:n], None, dbg)
+    hq = lambda: c.quant_rows_e4m3_row(ws.h[:n], None, None, n, ws.hq[:n], ws.hs)  # noqa
+    w2 = lambda dbg=None: c.moe_int3_gemm(bank.w2_codes, bank.w2_scales, ws.cnt, ws.list, 1, ws.hq[:n], ws.hs,  # noqa
+                                          False, None, None, ws.y[:n], rw, dbg)
+    w13()
+    hq()
     torch.cuda.synchronize()
-    d = dbg.view(148, 4, 3).float()
-    prof = {"kernel": "moe_w13_int3_roles", "wait_frac": [round(float(x), 3) for x in (d[:, :, 0] / d[:, :, 1]).mean(0)],
-            "cycles_per_kstep": round(float((d[:, 0, 1] / d[:, 0, 2].clamp_min(1)).mean()), 1)}
-    out = [prof]
-    for name, fn, wbytes, rows, kdim, ncols in (
-            ("moe_w13_int3", w13, bank.w13_codes.nbytes + bank.w13_scales.nbytes, n, H, 2 * I),
-            ("moe_w2_int3", w2, bank.w2_codes.nbytes + bank.w2_scales.nbytes, n, I, H)):
+    out = []
+    for name, fn in (("moe_w13_int3", w13), ("moe_w2_int3", w2)):
+        dbg = torch.zeros(148 * 4 * 3, dtype=torch.int64, device=dev)
+        fn(dbg)
+        torch.cuda.synchronize()
+        d = dbg.view(148, 4, 3).float()
+        live = d[:, 0, 2] > 0
+        out.append({"kernel": name + "_roles", "roles": ["loader", "dequant", "mma", "epilogue"],
+                    "wait_frac": [round(float(v), 3) for v in (d[live, :, 0] / d[live, :, 1]).mean(0)],
+                    "cycles_per_kstep": round(float((d[live, 0, 1] / d[live, 0, 2].clamp_min(1)).mean()), 1)})
+    wb13 = bank.w13_codes.nbytes + bank.w13_scales.nbytes
+    wb2 = bank.w2_codes.nbytes + bank.w2_scales.nbytes
+    for name, fn, byts, fl in (
+            ("moe_w13_int3", w13, wb13 + T * H + n * I * 2, 2 * n * H * 2 * I),
+            ("quant_rows_e4m3_row(h)", hq, n * I * 2 + n * I, 0),
+            ("moe_w2_int3", w2, wb2 + n * I + n * H * 2, 2 * n * I * H)):
         ms = time_cuda(fn)
-        act = rows * kdim + rows * ncols * (1 if name.endswith("w13_int3") else 2) // (2 if "w13" in name else 1)
-        byts = wbytes + act
         out.append({"kernel": name, "T": T, "E": E, "ms": round(ms, 4), "bytes": byts,
                     "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
-                    "tflops": round(2 * rows * kdim * ncols / ms / 1e9, 1)})
+                    "tflops": round(fl / ms / 1e9, 1)})
     return out
 
 

@@ -120,7 +120,7 @@ def count_launches(fn, census_out=None, time_out=None):
             "quant_rows", "moe_combine", "swiglu", "embedding", "paged_attn", "attn_merge", "gdn_", "select_tokens",
             "spec_accept", "build_window", "gather_rows", "expert_sort", "int3_dequant", "int3_scale_grad",
             "fp8_block_fakequant", "topk_tail_kl", "adamw_kernel", "train_kernel", "ep_dispatch", "ep_wait",
-            "ep_gather", "gdn_chunk_scan")
+            "ep_gather", "gdn_chunk_scan", "quant_routed")
     n_ours = n_all = 0
     census = collections.Counter()
     for e in prof.events():

@@ -150,9 +150,13 @@ def test_peer_wait_gives_up_with_status_and_the_context_survives():
     check_status()
     ep = ExpertParallel(1, 0, 8, 256, 2, 4, "cuda")
     x = torch.randn(8, 256, device="cuda").bfloat16()
-    ids = torch.zeros(8, 2, dtype=torch.int32, device="cuda")
+    ids = torch.tensor([[0, 1]] * 8, dtype=torch.int32, device="cuda")  # every token: experts 0 and 1
     w = torch.ones(8, 2, device="cuda")
-    ep.ctx.dispatch(x, 8, ids, w)
+    cnt = torch.tensor([8, 8, 0, 0], dtype=torch.int32, device="cuda")
+    lst = torch.zeros(4, 8, dtype=torch.int32, device="cuda")
+    lst[0] = torch.arange(0, 16, 2, dtype=torch.int32, device="cuda")
+    lst[1] = torch.arange(1, 16, 2, dtype=torch.int32, device="cuda")
+    ep.ctx.dispatch(x, 8, ids, w, cnt, lst)
     ep.ctx.wait(EP_DISPATCH)
     torch.cuda.synchronize()
     assert check_status() == 0
