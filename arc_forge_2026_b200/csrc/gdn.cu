@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
 // One CTA (512 threads, 4 per value column) per SM loops over (sequence, value head) items. While it runs the
 // recurrence of item i, bulk copies (no multicast) stage item i+1 into the other half of a shared-memory double
 // buffer: its 64 KB committed state, the k (and q) rows of the previous cycle's and this cycle's tokens, their v rows,
-// gates and the z rows of the output gate.
+// and gates (the z rows of the output gate are read from global memory by the norm pass).
 //
 // Per item:
 //   * keys and queries are converted once to fp32 into part-padded rows (conflict-free 16-byte loads);
@@ -210,8 +210,10 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
 //     step is two FMA passes (the dot k.S and the rank-1 update) instead of three -- the decay is applied to the
 //     scalar, S_true = Gamma * S. When log Gamma falls below -60 the registers are rescaled and Gamma restarts at 1;
 //   * after the accepted tokens of the previous cycle the committed state Gamma * S goes back into its shared-memory
-//     slot and one bulk copy stores the 64 KB (the state is not rewritten when no token was accepted);
-//   * this cycle's raw outputs go to shared memory; one pass then applies the gated RMSNorm per token.
+//     slot and each warp stores its 4 KB with one bulk copy (the state is not rewritten when no token was accepted);
+//   * this cycle's raw outputs go to shared memory with per-token sums of squares; the gated RMSNorm of an item is
+//     finished after the next item's barrier, one column per thread (fp32 keys, queries and outputs are
+//     double-buffered by item parity, the sums rotate over three slots), so each item costs one block-wide barrier.
 // State layout (DK = DV = 128, per (slot, head)): thread t = 4 * v + part owns rows part*32 .. part*32+31 of column v
 // and stores them contiguously, 16-byte chunk c at chunk position c ^ (t & 7) -- so every thread moves its slice
 // with 16-byte accesses and no two lanes of a quarter warp touch the same bank.
@@ -222,11 +224,11 @@ struct Smem {
   float state[2][DK * DV];
   __nv_bfloat16 kq[2][2 * MAXT][2][DK];  // token slots 0..7: previous cycle (k only), 8..15: this cycle (k, q)
   __nv_bfloat16 v[2][2 * MAXT][DV];
-  __nv_bfloat16 z[2][MAXT][DV];
   float gb[2][2][2 * MAXT];              // [buf][previous / this cycle][token * 2 + (g, beta)]
-  float kf[2 * MAXT][QT * KP];           // this item's keys, fp32, compact token order (accepted, then new)
-  float qf[MAXT][QT * KP];               // this item's queries, fp32
-  float o[MAXT][DV];                     // raw outputs of this cycle's tokens
+  float kf[2][2 * MAXT][QT * KP];        // per item parity: keys, fp32, compact token order (accepted, then new)
+  float qf[2][MAXT][QT * KP];            // per item parity: queries, fp32
+  float o[2][MAXT][DV];                  // per item parity: raw outputs of this cycle's tokens
+  float ssq[3][MAXT];                    // per item (mod 3): sum of squares of each token's raw outputs
   int slot[MAXS], ncommit[MAXS];
   uint64_t full[2];
 };
@@ -253,6 +255,7 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x, v = tid / QT, part = tid % QT;
+  const int wid = tid >> 5, lane = tid & 31;
   const int T = a.q_per_seq;
   const int nq = a.Hk * DK;
   const int cur = parity, prev = parity ^ 1;
@@ -275,15 +278,13 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
     const int seq = item / a.Hv, h = item % a.Hv;
     const int slot = sm.slot[seq], np = sm.ncommit[seq];
     const int kh = h / (a.Hv / a.Hk);
-    const int lane = tid & 31;
     if (lane == 0) {
-      bulk_store_wait_read();  // the committed-state store of two items ago has finished reading buffer b
-      const uint32_t bytes = DK * DV * 4 + np * (DK + DV) * 2 + T * (2 * DK + 2 * DV) * 2 + 2 * a.max_q * 8;
+      const uint32_t bytes = DK * DV * 4 + np * (DK + DV) * 2 + T * (2 * DK + DV) * 2 + 2 * a.max_q * 8;
       mbar_arrive_expect_tx(&sm.full[b], bytes);
     }
     __syncwarp();
-    // copy list: 0 state, 1 gb prev, 2 gb cur, then per accepted token (k, v), then per new token (k, q, v, z)
-    const int ncopies = 3 + 2 * np + 4 * T;
+    // copy list: 0 state, 1 gb prev, 2 gb cur, then per accepted token (k, v), then per new token (k, q, v)
+    const int ncopies = 3 + 2 * np + 3 * T;
     for (int c = lane; c < ncopies; c += 32) {
       if (c == 0) {
         bulk_copy(sm.state[b], a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV, DK * DV * 4, &sm.full[b]);
@@ -299,34 +300,42 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
         else
           bulk_copy(sm.v[b][t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
       } else {
-        const int t = (c - 3 - 2 * np) >> 2, w = (c - 3 - 2 * np) & 3;
+        const int t = (c - 3 - 2 * np) / 3, w = (c - 3 - 2 * np) % 3;
         const size_t base = ((size_t)cur * a.pend_slots + slot) * a.max_q + t;
         if (w == 0)
           bulk_copy(sm.kq[b][MAXT + t][0], a.pend_qk + base * (2 * nq) + nq + kh * DK, DK * 2, &sm.full[b]);
         else if (w == 1)
           bulk_copy(sm.kq[b][MAXT + t][1], a.pend_qk + base * (2 * nq) + kh * DK, DK * 2, &sm.full[b]);
-        else if (w == 2)
-          bulk_copy(sm.v[b][MAXT + t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
         else
-          bulk_copy(sm.z[b][t], a.mixed + ((size_t)seq * T + t) * a.mixed_ld + a.z_off + h * DV, DV * 2,
-                    &sm.full[b]);
+          bulk_copy(sm.v[b][MAXT + t], a.pend_v + base * (a.Hv * DV) + h * DV, DV * 2, &sm.full[b]);
       }
     }
   };
+  // gated RMSNorm of one finished item's raw outputs: the thread of part 0 of column v finishes column v of every
+  // token (the sums of squares were accumulated while the outputs were produced); z is read from global memory, so
+  // the item's staging buffer is already free for the next copies
+  auto norm_pass = [&](int item, int x, int q3) {
+    const int seq = item / a.Hv, h = item % a.Hv;
+    if (part == 0) {
+      const float w = __bfloat162float(a.norm_w[v]);
+      for (int t = 0; t < T; ++t) {
+        const size_t tok = (size_t)seq * T + t;
+        const float z = __bfloat162float(a.mixed[tok * a.mixed_ld + a.z_off + h * DV + v]);
+        const float rstd = rsqrtf(sm.ssq[q3][t] / DV + a.eps);
+        a.out[tok * (a.Hv * DV) + h * DV + v] = __float2bfloat16(sm.o[x][t][v] * rstd * w * silu(z));
+      }
+    }
+  };
+  for (int q = tid; q < 3 * MAXT; q += THREADS) (&sm.ssq[0][0])[q] = 0.f;
 
   int issued = 0, done = 0;
-  if (tid < 32 && blockIdx.x < items) {
+  if (wid == 0 && blockIdx.x < items) {
     issue(blockIdx.x, 0);
     issued = 1;
   }
-  int i = 0;
+  int i = 0, last = -1;
   for (int item = blockIdx.x; item < items; item += gridDim.x, ++i) {
-    const int b = i & 1;
-    const int next = item + gridDim.x;
-    if (tid < 32 && next < items) {  // buffer b ^ 1 was released by every thread at the end of the last item
-      issue(next, b ^ 1);
-      ++issued;
-    }
+    const int b = i & 1;  // staging buffer = item parity (kf / qf / o use the same parity)
     // every thread acquires the copies through the barrier; the vote makes a timeout (flagged in the status word)
     // end the loop on every thread together
     const bool ok = __syncthreads_and(mbar_wait(&sm.full[b], (i >> 1) & 1, status));
@@ -343,10 +352,10 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
       float* dst;
       if (row < L) {
         src = sm.kq[b][row < np ? row : MAXT + row - np][0] + c2;
-        dst = sm.kf[row];
+        dst = sm.kf[b][row];
       } else {
         src = sm.kq[b][MAXT + row - L][1] + c2;
-        dst = sm.qf[row - L];
+        dst = sm.qf[b][row - L];
       }
       const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
       const int pc = (c2 / HK) * KP + (c2 % HK);
@@ -363,7 +372,17 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
       S[4 * c + 2] = x.z;
       S[4 * c + 3] = x.w;
     }
-    __syncthreads();  // fp32 keys / queries ready
+    if (lane == 0) bulk_store_wait_read();  // this warp's state store of the last item has left buffer b ^ 1
+    // the one barrier per item: fp32 keys / queries ready; every thread is done with the previous item, so its
+    // staging buffer can be refilled and its outputs normalised
+    __syncthreads();
+    const int next = item + gridDim.x;
+    if (wid == 0 && next < items) {
+      issue(next, b ^ 1);
+      ++issued;
+    }
+    if (last >= 0) norm_pass(last, b ^ 1, (i + 2) % 3);
+    if (tid < MAXT) sm.ssq[(i + 1) % 3][tid] = 0.f;  // item i - 2's sums (read by the last norm pass) -> item i + 1
 
     float lg = 0.f;  // log Gamma
     // partial dot of this thread's slice with an fp32 row (four FMA chains), summed over the QT lanes of a column
@@ -406,47 +425,36 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
       }
     };
     for (int t = 0; t < np; ++t)
-      step(sm.gb[b][0][2 * t], sm.gb[b][0][2 * t + 1], __bfloat162float(sm.v[b][t][v]), sm.kf[t]);
-    if (np > 0) {  // the committed state Gamma * S back into its slot, stored by one bulk copy
+      step(sm.gb[b][0][2 * t], sm.gb[b][0][2 * t + 1], __bfloat162float(sm.v[b][t][v]), sm.kf[b][t]);
+    if (np > 0) {
+      // the committed state Gamma * S back into its slot; each warp stores its 32 threads' slices (4 KB,
+      // contiguous in the swizzled layout) with one bulk copy, so no block-wide barrier is needed
       const float gam = __expf(lg);
 #pragma unroll
       for (int c = 0; c < HK / 4; ++c)
         *reinterpret_cast<float4*>(&sm.state[b][tid * 32 + ((c ^ (tid & 7)) << 2)]) =
             make_float4(gam * S[4 * c], gam * S[4 * c + 1], gam * S[4 * c + 2], gam * S[4 * c + 3]);
       fence_proxy_async_smem();
-      __syncthreads();
-      if (tid == 0) bulk_store(a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV, sm.state[b], DK * DV * 4);
+      __syncwarp();
+      if (lane == 0)
+        bulk_store(a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV + wid * 32 * 32, &sm.state[b][wid * 32 * 32],
+                   32 * 32 * 4);
     }
     for (int t = 0; t < T; ++t) {
-      step(sm.gb[b][1][2 * t], sm.gb[b][1][2 * t + 1], __bfloat162float(sm.v[b][MAXT + t][v]), sm.kf[np + t]);
-      const float o = __expf(lg) * dot(sm.qf[t]);
-      if (part == 0) sm.o[t][v] = o;
+      step(sm.gb[b][1][2 * t], sm.gb[b][1][2 * t + 1], __bfloat162float(sm.v[b][MAXT + t][v]), sm.kf[b][np + t]);
+      const float o = __expf(lg) * dot(sm.qf[b][t]);
+      if (part == 0) sm.o[b][t][v] = o;
+      const float sq = warp_sum(part == 0 ? o * o : 0.f);  // this warp's 8 columns
+      if (lane == 0) atomicAdd(&sm.ssq[i % 3][t], sq);
     }
-    __syncthreads();  // raw outputs complete
-    // ---- gated RMSNorm per token: warp w takes token w, lane l columns 4l .. 4l+3
-    {
-      const int w = tid >> 5, l = tid & 31;
-      if (w < T) {
-        const float4 o4 = *reinterpret_cast<const float4*>(&sm.o[w][4 * l]);
-        const float rstd = rsqrtf(warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w) / DV + a.eps);
-        const uint2 zr = *reinterpret_cast<const uint2*>(&sm.z[b][w][4 * l]);
-        const __nv_bfloat162* z2 = reinterpret_cast<const __nv_bfloat162*>(&zr);
-        const float2 za = __bfloat1622float2(z2[0]), zb = __bfloat1622float2(z2[1]);
-        const float2 na = make_float2(__bfloat162float(a.norm_w[4 * l]), __bfloat162float(a.norm_w[4 * l + 1]));
-        const float2 nb = make_float2(__bfloat162float(a.norm_w[4 * l + 2]), __bfloat162float(a.norm_w[4 * l + 3]));
-        const size_t tok = (size_t)seq * T + w;
-        *reinterpret_cast<uint2*>(a.out + tok * (a.Hv * DV) + h * DV + 4 * l) =
-            make_uint2(pack_bf16x2(o4.x * rstd * na.x * silu(za.x), o4.y * rstd * na.y * silu(za.y)),
-                       pack_bf16x2(o4.z * rstd * nb.x * silu(zb.x), o4.w * rstd * nb.y * silu(zb.y)));
-      }
-    }
-    __syncthreads();  // o / kf / qf are rewritten by the next item; buffer b is refilled two items later
+    last = item;
   }
-  // drain copies still in flight (only after a failed wait), bounded; then the last committed-state stores
-  if (tid == 0) {
+  __syncthreads();
+  if (last >= 0) norm_pass(last, (i - 1) & 1, (i - 1) % 3);
+  // drain copies still in flight (only after a failed wait), bounded; then this warp's committed-state stores
+  if (tid == 0)
     for (int j = done; j < issued; ++j) mbar_wait(&sm.full[j & 1], (j >> 1) & 1, status);
-    bulk_store_wait_all();
-  }
+  if (lane == 0) bulk_store_wait_all();
 }
 
 int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cudaStream_t st) {

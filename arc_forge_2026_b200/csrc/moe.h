@@ -34,7 +34,8 @@ struct MoeGemmArgs {
   // [E, rows/128, K/128]; codes / scales above are then unused
   const uint8_t* fp8_w = nullptr;
   const float* fp8_scales = nullptr;
-  long long* dbg = nullptr;        // optional profiling counters [grid, 4 roles, 3]: wait cycles, total, k-steps
+  long long* dbg = nullptr;        // optional profiling counters [grid, 4 roles, 5]: wait cycles, total, k-steps,
+                                   // cycles of the role's main section and of a second one
   // !PAIR under expert parallelism: entry e belongs to rank e / ep_entries_per_rank and its routed row goes to that
   // rank's combine region at (e % ep_entries_per_rank); the last CTA then publishes the combine exchange on every
   // rank (flag protocol of ep.cu)

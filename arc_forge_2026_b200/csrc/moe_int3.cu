@@ -254,7 +254,9 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
   uint32_t ksteps = 0;
   bool bail = false;
   long long t_wait = 0;  // profiling counters (PROF only): cycles spent in waits by this role
+  long long t_sec = 0, t_sec2 = 0;  // PROF: cycles in the role's main work (see the role) and a second section
   const long long t_start = PROF ? clock64() : 0;
+  auto clk = [&]() -> long long { return PROF ? clock64() : 0; };
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if constexpr (PROF) {
       const long long t0 = clock64();
@@ -286,6 +288,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           if (bail) break;
           uint8_t* st = smem + rs.i * L::RAW;
           uint64_t* bar = &full[rs.i];
+          const long long c0 = clk();
           if (lane == 0) {
             mbar_arrive_expect_tx(bar, F8 ? T * moe::A_TILE : T * (moe::CODE_TILE + 256));
 #pragma unroll
@@ -307,6 +310,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
 #pragma unroll
           for (int c = 0; c < 8; ++c) cp_async16(xt + ((c ^ (lane & 7)) << 4), xrow + g * 128 + c * 16, xbytes);
           cp_async_arrive(bar);
+          t_sec += clk() - c0;
         }
       } else if (warp == moe::W_META) {
         // ---------------------------------------------------------------- chunk metadata
@@ -359,6 +363,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           } else {
             // the group's weight scales move to the epilogue's slot, so the raw stage can be refilled early
             if (dq < T * 64) reinterpret_cast<uint32_t*>(esc)[dq] = reinterpret_cast<const uint32_t*>(st + L::SW_OFF)[dq];
+            const long long c0 = clk();
             const uint4* rw = reinterpret_cast<const uint4*>(st + L::C_OFF + t * moe::CODE_TILE + r * 48);
             const uint4 w0 = rw[0], w1 = rw[1], w2 = rw[2];  // the row's 12 words (128 codes)
             uint32_t o[32];
@@ -367,8 +372,11 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
             decode32(w1.z, w1.w, w2.x, o + 16);
             decode32(w2.y, w2.z, w2.w, o + 24);
             // row r of the A tile: 32 columns of 4 e4m3 each, in K order
+            const long long c1 = clk();
             tmem_st32(tmem + ((uint32_t)(quad * 32) << 16) + L::A_COL + (ra.i * T + t) * 32, o);
             tmem_st_wait();
+            t_sec += c1 - c0;
+            t_sec2 += clk() - c1;
             tc_fence_before();
             __syncwarp();
           }
@@ -392,6 +400,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           if (lane == 0) {
             // the B tile came in through the generic proxy (async copies observed via the barriers): order it
             // before the tensor core's reads
+            const long long c0 = clk();
             fence_proxy_async_smem();
             const uint8_t* st = smem + rs.i * L::RAW;
             const uint64_t dx = sw128_desc(smem_u32(st + L::X_OFF));
@@ -409,9 +418,12 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
                 }
               }
             }
+            const long long c1 = clk();
             umma_commit(&dfull[rb.i]);
             umma_commit(&aempty[ra.i]);
             umma_commit(&empty[rs.i]);
+            t_sec += c1 - c0;
+            t_sec2 += clk() - c1;
           }
           __syncwarp();
         }
@@ -442,6 +454,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
             sw1 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(esc + 256)[r]);
           }
           // 16 columns at a time keeps the role at 32 accumulators per tile plus one 16-wide load in registers
+          const long long c0 = clk();
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int t = q >> 1, c0 = (q & 1) * 16;
@@ -453,6 +466,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) acc[c0 + i] = fmaf(F8 ? sw * sx[c0 + i] : sw, d[i], acc[c0 + i]);
           }
+          t_sec += clk() - c0;
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&dempty[rb.i]);  // TMEM buffer and scale slot rb.i are free again
@@ -524,9 +538,12 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
   if (PROF && args.dbg && lane == 0 &&
       (warp == moe::W_LD || warp == moe::W_DQ0 || warp == moe::W_MMA || warp == moe::W_EP0)) {
     const int role = warp == moe::W_LD ? 0 : warp == moe::W_DQ0 ? 1 : warp == moe::W_MMA ? 2 : 3;
-    args.dbg[(blockIdx.x * 4 + role) * 3 + 0] = t_wait;
-    args.dbg[(blockIdx.x * 4 + role) * 3 + 1] = clock64() - t_start;
-    args.dbg[(blockIdx.x * 4 + role) * 3 + 2] = ksteps;
+    long long* d = args.dbg + (blockIdx.x * 4 + role) * 5;
+    d[0] = t_wait;
+    d[1] = clock64() - t_start;
+    d[2] = ksteps;
+    d[3] = t_sec;
+    d[4] = t_sec2;
   }
   if (warp == moe::W_LD) {  // no async copy of this warp may still be writing shared memory at exit
     asm volatile("cp.async.wait_all;" ::: "memory");
