@@ -507,11 +507,19 @@ static int launch_attn(const AttnArgs& a, int splits, uint32_t* status, cudaStre
   return (int)cudaGetLastError();
 }
 
+int paged_attention_tc(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st);  // attention_tc.cu
+
 int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st) {
   if (a.q_per_seq * (a.Hq / a.Hkv) > 64) return 3;
   if (splits > 1 && (!a.part_o || !a.part_lse)) return 4;
   if (a.num_seqs == 0) return 0;
   const bool fp4 = a.kscale != nullptr;
+  if (const int rc = paged_attention_tc(a, splits, status, st); rc != -1) {
+    if (rc || splits == 1) return rc;
+    if (a.D == 256) attn_merge_kernel<256><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
+    else attn_merge_kernel<128><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
+    return (int)cudaGetLastError();
+  }
   if (a.D == 256) return fp4 ? launch_attn<256, true>(a, splits, status, st) : launch_attn<256, false>(a, splits, status, st);
   if (a.D == 128) return fp4 ? launch_attn<128, true>(a, splits, status, st) : launch_attn<128, false>(a, splits, status, st);
   return 3;

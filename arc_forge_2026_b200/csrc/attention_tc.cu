@@ -1,0 +1,398 @@
+// Paged decode / speculative-verify attention on the 5th-generation tensor cores (tcgen05, TMEM accumulators), bf16
+// KV cache, dense causal mode: the path the serving verify step runs for every full-attention layer.
+//
+// One CTA per (sequence, KV head, KV split), as in attention.cu: its query rows are the q_per_seq verify positions x
+// the Hq/Hkv query heads of the KV head (row r = t * group + h, at most 64 rows), so one KV page read from HBM
+// serves every head and position. Per 64-key page:
+//   S = Q K^T   tcgen05.mma kind::f16, M=128 (rows past the CTA's rows are never read), N=64, K=16 per op;
+//               Q and the K page are K-major 128-byte-swizzled shared-memory operands, S lands in TMEM
+//   softmax     two warps (TMEM lane quadrants 0 and 1 = rows 0..63) load S rows, mask (causality inside the verify
+//               window, the split's pages), keep a running max m and sum l in the log2 domain and write P = 2^(S - m)
+//               as bf16 into TMEM, where the next MMA reads it as its A operand
+//   O += P V    tcgen05.mma with A = P from TMEM and B = the V page as an MN-major operand (keys x D, D contiguous),
+//               N = D, accumulated in TMEM across pages
+// The running max is raised lazily: a row's O is rescaled (read from TMEM, scaled, written back) only when its max
+// grows by more than 8 (a factor of 256), which after the first pages almost never happens; P, l and O stay
+// consistent with whatever max the row currently uses.
+// Warp roles: 0 loader (TMA of Q and of the K and V pages, no multicast, 3-stage ring), 1 MMA issuer (+ TMEM),
+// 4-5 softmax / output (the rows), the others idle. S and P are double-buffered so the QK^T of page i+1 overlaps the
+// softmax of page i and the PV of page i-1. Splits write (O / l, m + log2 l) partials for attn_merge_kernel.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace afb {
+
+namespace attn_tc {
+constexpr int PAGE = 64;
+constexpr int THREADS = 256;
+constexpr int W_LD = 0, W_MMA = 1, W_SM0 = 4;  // softmax warps 4 and 5
+constexpr float RESCALE = 8.f;                 // log2 growth of a row max that forces an O rescale
+
+template <int D>
+struct Smem {
+  static constexpr uint32_t SUB = PAGE * 128;                 // one 64-row x 128-byte swizzled sub-tile
+  static constexpr uint32_t Q_BYTES = (D / 64) * SUB;         // 64 query rows; the MMA's rows 64..127 alias what
+                                                              // follows (their results are never read)
+  static constexpr uint32_t KV_BYTES = (D / 64) * SUB;        // one K (or V) page of one head
+  static constexpr int NS = D == 256 ? 3 : 6;                 // KV stages
+  static constexpr uint32_t STAGE = 2 * KV_BYTES;
+  static constexpr uint32_t KV_OFF = Q_BYTES;
+  static constexpr uint32_t BAR_OFF = KV_OFF + NS * STAGE;
+  // kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full[2], o_done[2], q_ready, mma_fin, tmem slot
+  static constexpr uint32_t TOTAL = BAR_OFF + (2 * NS + 10) * 8 + 16 + 1024;
+  // TMEM columns: O [D], S [2][64], P [2][32] (bf16 pairs)
+  static constexpr uint32_t O_COL = 0, S_COL = D, P_COL = D + 2 * PAGE;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(P_COL + 2 * PAGE / 2 <= TMEM_COLS, "TMEM columns");
+};
+}  // namespace attn_tc
+
+// K-major 128-byte-swizzle descriptor with an explicit leading (between 64-element MN blocks) and stride (between
+// 8-row groups) byte offset: the MN-major operand form (the V page read as keys x D, D contiguous)
+AFB_DEV uint64_t sw128_desc_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+// kind::f16 with the A operand in tensor memory
+AFB_DEV void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(attn_tc::THREADS, 1)
+    paged_attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                         const __grid_constant__ CUtensorMap tmQ, AttnArgs a, uint32_t* status) {
+  using namespace attn_tc;
+  using L = Smem<D>;
+  constexpr int NS = L::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* kv_empty = kv_full + NS;
+  uint64_t* s_full = kv_empty + NS;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* q_ready = o_done + 2;
+  uint64_t* mma_fin = q_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_fin + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seq = blockIdx.x / a.Hkv, kvh = blockIdx.x % a.Hkv;
+  const int split = blockIdx.y;
+  const int group = a.Hq / a.Hkv;
+  const int QR = a.q_per_seq * group;  // query rows of this CTA (<= 64)
+  const int seq_len = a.seq_lens[seq];
+  const int past = seq_len - a.q_per_seq;
+  const int npages = (seq_len + PAGE - 1) / PAGE;
+  const int p0 = split * a.pages_per_split;
+  const int p1 = min(npages, p0 + a.pages_per_split);
+  const int n = max(0, p1 - p0);
+  const int* bt = a.block_table + (size_t)seq * a.max_pages;
+
+  if (n == 0) {  // an empty split (or a sequence without keys): nothing to stream, no TMEM
+    const int r = threadIdx.x;
+    if (r < QR) {
+      const size_t tok = (size_t)seq * a.q_per_seq + r / group;
+      const int head = kvh * group + r % group;
+      if (gridDim.y > 1) {
+        a.part_lse[((size_t)split * a.num_tokens + tok) * a.Hq + head] = -INFINITY;
+      } else {
+        __nv_bfloat16* op = a.out + (tok * a.Hq + head) * D;
+        for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(op + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 2);  // the two softmax warps
+      mbar_init(&p_full[b], 2);
+      mbar_init(&o_done[b], 1);
+    }
+    mbar_init(q_ready, 1);
+    mbar_init(mma_fin, 1);
+    fence_mbar_init();
+  }
+  if (warp == W_MMA) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == W_LD) {
+    // ------------------------------------------------------------------ loader
+    // Q: one 3-D box {64 columns, group heads, q_per_seq tokens} per 64-column sub-tile lands rows t * group + h
+    if (lane == 0) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_ready, (uint32_t)QR * D * 2);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) tma_load_3d(smem + c * L::SUB, &tmQ, q_ready, c * 64, kvh * group, seq * a.q_per_seq);
+    }
+    // block-table entries 32 at a time (one per lane), then one K + V fill per page
+    int issued = 0;
+    for (int base = 0; base < n && ok; base += 32) {
+      const int mine = base + lane < n ? bt[p0 + base + lane] : 0;
+      const int cnt = min(32, n - base);
+      for (int j = 0; j < cnt; ++j) {
+        const int i = base + j, s = i % NS;
+        const int page = __shfl_sync(0xffffffffu, mine, j);
+        if (i >= NS && !__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((i / NS) & 1) ^ 1, status))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const int row = (page * a.Hkv + kvh) * PAGE;
+          uint8_t* st = smem + L::KV_OFF + s * L::STAGE;
+          mbar_arrive_expect_tx(&kv_full[s], L::STAGE);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_2d(st + c * L::SUB, &tmK, &kv_full[s], c * 64, row);
+            tma_load_2d(st + L::KV_BYTES + c * L::SUB, &tmV, &kv_full[s], c * 64, row);
+          }
+        }
+        ++issued;
+      }
+    }
+    // no copy may still be landing when the CTA exits (after a timeout elsewhere the MMA warp may not have
+    // consumed the last stages): wait, bounded, for Q and the last NS fills
+    if (lane == 0) {
+      mbar_wait(q_ready, 0, status);
+      for (int i = max(0, issued - NS); i < issued; ++i) mbar_wait(&kv_full[i % NS], (i / NS) & 1, status);
+    }
+  } else if (warp == W_MMA) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = idesc_f16(128, PAGE, 1);             // S = Q K^T
+    constexpr uint32_t idesc_o = idesc_f16(128, D, 1) | (1u << 16);   // O += P V, B (V) MN-major
+    ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0, status));
+    tc_fence_after();
+    const uint32_t q_base = smem_u32(smem);
+    auto issue_pv = [&](int j) {  // page j: wait for its P, then O += P V
+      const int sb = j & 1, s = j % NS;
+      if (!__all_sync(0xffffffffu, mbar_wait(&p_full[sb], (j >> 1) & 1, status))) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t v_base = smem_u32(smem + L::KV_OFF + s * L::STAGE + L::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < PAGE / 16; ++kk)  // 16 keys per op: 2 KB into the page (two 8-row swizzle atoms)
+          umma_f16_ta(tmem + L::O_COL, tmem + L::P_COL + sb * (PAGE / 2) + kk * 8,
+                      sw128_desc_mn(v_base + kk * 16 * 128, L::SUB, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&o_done[sb]);
+        umma_commit(&kv_empty[s]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int i = 0; i < n && ok; ++i) {
+      const int s = i % NS, sb = i & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[s], (i / NS) & 1, status)) ||
+          (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&s_empty[sb], ((i >> 1) & 1) ^ 1, status)))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t k_base = smem_u32(smem + L::KV_OFF + s * L::STAGE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::SUB + (kk & 3) * 32;
+          umma_f16(tmem + L::S_COL + sb * PAGE, sw128_desc(q_base + off), sw128_desc(k_base + off), idesc_s,
+                   kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+      }
+      __syncwarp();
+      if (i >= 1 && !issue_pv(i - 1)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok && n > 0) issue_pv(n - 1);
+    // every MMA this thread issued has completed before TMEM is released (also after a timeout)
+    if (lane == 0) umma_commit(mma_fin);
+    __syncwarp();
+    mbar_wait(mma_fin, 0, status);
+  } else if (warp == W_SM0 || warp == W_SM0 + 1) {
+    // ------------------------------------------------------------------ softmax + output (rows 0..63)
+    const int quad = warp - W_SM0;
+    const int r = quad * 32 + lane;  // query row = TMEM lane
+    const int t = r / group, hq = r % group;
+    const bool live = r < QR;
+    const int vis = past + t + 1;  // keys this row may see: positions < vis
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const int sb = i & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (i >> 1) & 1, status))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[PAGE];
+      tmem_ld32(lane_base + L::S_COL + sb * PAGE, sv);
+      tmem_ld32(lane_base + L::S_COL + sb * PAGE + 32, sv + 32);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[sb]);
+      const int kbase = (p0 + i) * PAGE;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < PAGE; ++j) {
+        const float x = (live && kbase + j < vis) ? sv[j] * a.scale_log2 : -INFINITY;
+        sv[j] = x;
+        mx = fmaxf(mx, x);
+      }
+      // lazy max: keep the current one unless this page raises it by more than RESCALE
+      float mnew = m;
+      if (mx > m + RESCALE || m == -INFINITY) mnew = mx;
+      const bool rescale = m != -INFINITY && mnew != m;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O must hold every earlier page before it is scaled: wait for the PV of page i - 1
+        if (i >= 1 && !__all_sync(0xffffffffu, mbar_wait(&o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, status))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = rescale ? exp2f(m - mnew) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          float ov[32];
+          tmem_ld32(lane_base + L::O_COL + c, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] *= f;
+          tmem_st32(lane_base + L::O_COL + c, reinterpret_cast<const uint32_t*>(ov));
+        }
+        tmem_st_wait();
+        l *= f;
+      }
+      m = mnew;
+      const float base = m == -INFINITY ? 0.f : m;
+      uint32_t pk[PAGE / 2];
+      float rs = 0.f;
+#pragma unroll
+      for (int j = 0; j < PAGE / 2; ++j) {
+        const float e0 = exp2f(sv[2 * j] - base), e1 = exp2f(sv[2 * j + 1] - base);
+        rs += e0 + e1;
+        pk[j] = pack_bf16x2(e0, e1);
+      }
+      l += rs;
+      // P of page i goes into P buffer sb; the PV of page i - 2 (which read that buffer) must be done
+      if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&o_done[sb], ((i - 2) >> 1) & 1, status))) {
+        ok = false;
+        break;
+      }
+      tmem_st32(lane_base + L::P_COL + sb * (PAGE / 2), pk);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+    }
+    // ---- output: O / l of the last PV (splits: partials with the log2-sum-exp)
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done[(n - 1) & 1], ((n - 1) >> 1) & 1, status))) {
+      tc_fence_after();
+      const size_t tok = (size_t)seq * a.q_per_seq + t;
+      const int head = kvh * group + hq;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool direct = gridDim.y == 1;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        float ov[32];
+        tmem_ld32(lane_base + L::O_COL + c, ov);
+        tmem_ld_wait();
+        if (!live) continue;
+        if (direct) {
+          __nv_bfloat16* op = a.out + (tok * a.Hq + head) * D + c;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float g[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              g[e] = 1.f;
+              if (a.gate) {
+                const float z = __bfloat162float(a.gate[tok * a.gate_ld + head * a.gate_head_stride + c + j + e]);
+                g[e] = 1.f / (1.f + __expf(-z));
+              }
+            }
+            *reinterpret_cast<uint4*>(op + j) =
+                make_uint4(pack_bf16x2(ov[j] * inv * g[0], ov[j + 1] * inv * g[1]),
+                           pack_bf16x2(ov[j + 2] * inv * g[2], ov[j + 3] * inv * g[3]),
+                           pack_bf16x2(ov[j + 4] * inv * g[4], ov[j + 5] * inv * g[5]),
+                           pack_bf16x2(ov[j + 6] * inv * g[6], ov[j + 7] * inv * g[7]));
+          }
+        } else {
+          float* pp = a.part_o + (((size_t)split * a.num_tokens + tok) * a.Hq + head) * D + c;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(pp + j) =
+                make_float4(ov[j] * inv, ov[j + 1] * inv, ov[j + 2] * inv, ov[j + 3] * inv);
+        }
+      }
+      if (live && !direct)
+        a.part_lse[((size_t)split * a.num_tokens + tok) * a.Hq + head] = l > 0.f ? m + log2f(l) : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == W_MMA) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+template <int D>
+static int launch_attn_tc(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st) {
+  using L = attn_tc::Smem<D>;
+  CUtensorMap tk{}, tv{};
+  const uint64_t rows = (uint64_t)a.num_pages * a.Hkv * attn_tc::PAGE;
+  int rc = make_tmap_2d(&tk, a.kcache, 2, D, rows, (uint64_t)D * 2, 64, attn_tc::PAGE, 1);
+  if (rc) return 1000 + rc;
+  rc = make_tmap_2d(&tv, a.vcache, 2, D, rows, (uint64_t)D * 2, 64, attn_tc::PAGE, 1);
+  if (rc) return 1000 + rc;
+  CUtensorMap tq{};
+  const int group = a.Hq / a.Hkv;
+  const uint64_t qdims[3] = {(uint64_t)D, (uint64_t)a.Hq, (uint64_t)a.num_tokens};
+  const uint64_t qstr[2] = {(uint64_t)D * 2, (uint64_t)a.Hq * D * 2};
+  const uint32_t qbox[3] = {64, (uint32_t)group, (uint32_t)a.q_per_seq};
+  rc = make_tmap_3d_bf16(&tq, a.q, qdims, qstr, qbox);
+  if (rc) return 1000 + rc;
+  static std::atomic<uint64_t> attr_devs{0};
+  if (const int e = smem_attr_once(attr_devs, (const void*)paged_attn_tc_kernel<D>, L::TOTAL)) return e;
+  dim3 grid(a.num_seqs * a.Hkv, splits);
+  paged_attn_tc_kernel<D><<<grid, attn_tc::THREADS, L::TOTAL, st>>>(tk, tv, tq, a, status);
+  return (int)cudaGetLastError();
+}
+
+// The tcgen05 path serves dense bf16 decode / verify (no window, no virtual prefill rows, no QSA union); returns -1
+// when the call is outside that set (the caller runs the mma.sync kernel), else the launch result.
+int paged_attention_tc(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st) {
+  if (a.impl == 1 || a.kscale || a.sp_count || a.window > 0 || a.bt_row || a.q_per_seq * (a.Hq / a.Hkv) > 64)
+    return -1;
+  if (a.D == 256) return launch_attn_tc<256>(a, splits, status, st);
+  if (a.D == 128) return launch_attn_tc<128>(a, splits, status, st);
+  return -1;
+}
+
+}  // namespace afb

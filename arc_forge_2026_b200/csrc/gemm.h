@@ -44,5 +44,8 @@ int gemm_bf16_grouped(const void* A, int lda, int rows_a, const void* B, int ldb
                       cudaStream_t stream);
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype_bytes, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle128);
+// bf16, 128-byte swizzle: dims / box innermost first, strides of dims 1 and 2 in bytes
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides_bytes[2],
+                      const uint32_t box[3]);
 
 }  // namespace afb

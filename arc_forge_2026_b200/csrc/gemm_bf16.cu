@@ -241,6 +241,20 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype_bytes, uint64_t i
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides_bytes[2],
+                      const uint32_t box[3]) {
+  auto encode = get_encode();
+  if (!encode) return -1;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t str[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, str, bx, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
 template <int BN, int STAGES>
 static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int splits,
                        const GemmEpilogue& epi, uint32_t* status, cudaStream_t stream) {

@@ -57,6 +57,9 @@ struct AttnArgs {
   const int* sp_count = nullptr;
   const int* sp_lpage = nullptr;
   const uint8_t* sp_mask = nullptr;
+  // 0: the tcgen05 kernel (attention_tc.cu) wherever it applies (bf16 cache, dense, no window, no virtual rows),
+  // else the mma.sync kernel; 1: always the mma.sync kernel
+  int impl = 0;
 };
 int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st);
 

@@ -313,7 +313,7 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
                         int64_t splits, int64_t pages_per_split, int64_t window, c10::optional<at::Tensor> bt_row,
                         c10::optional<at::Tensor> sp_count, c10::optional<at::Tensor> sp_lpage,
                         c10::optional<at::Tensor> sp_mask, c10::optional<at::Tensor> kscale,
-                        c10::optional<at::Tensor> vscale) {
+                        c10::optional<at::Tensor> vscale, int64_t impl) {
   AFB_CHECK_DT(q, at::kBFloat16);
   AFB_CHECK_CONTIG(q);
   AFB_CHECK_CONTIG(kcache);
@@ -346,6 +346,7 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
   a.pages_per_split = (int)pages_per_split;
   a.window = (int)window;
   a.bt_row = optr<int>(bt_row);
+  a.impl = (int)impl;
   if (sp_count.has_value()) {  // QSA sparse mode: block_table rows are page unions
     TORCH_CHECK(sp_lpage.has_value() && sp_mask.has_value(), "sparse attention needs sp_count, sp_lpage and sp_mask");
     AFB_CHECK_DT(sp_count.value(), at::kInt);
@@ -1288,7 +1289,7 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("gate"), py::arg("gate_ld"), py::arg("gate_head_stride"), py::arg("splits"),
         py::arg("pages_per_split"), py::arg("window"), py::arg("bt_row"), py::arg("sp_count") = py::none(),
         py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none(), py::arg("kscale") = py::none(),
-        py::arg("vscale") = py::none());
+        py::arg("vscale") = py::none(), py::arg("impl") = 0);
   m.def("qsa_prep", &qsa_prep_op);
   py::class_<GuardCtx>(m, "GuardCtx")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, const at::Tensor&,

@@ -22,8 +22,9 @@ def plan_splits(num_seqs: int, Hkv: int, max_pages: int, num_sms: int = 148) -> 
 
 
 def paged_attention(q, kcache, vcache, block_table, seq_lens, q_per_seq, out, gate=None, gate_ld=0,
-                    gate_head_stride=0, splits=None, max_pages=None, window=0, bt_row=None, kv_scales=None):
-    """``max_pages`` bounds the pages any sequence spans (it sizes the split plan; defaults to the table width).
+                    gate_head_stride=0, splits=None, max_pages=None, window=0, bt_row=None, kv_scales=None, impl=0):
+    """``impl`` 0 runs the tcgen05 kernel wherever it applies (bf16 cache, dense, no window, no virtual rows) and the
+    mma.sync kernel otherwise; 1 always runs the mma.sync kernel. ``max_pages`` bounds the pages any sequence spans (it sizes the split plan; defaults to the table width).
     ``window`` > 0 restricts each query to its last ``window`` keys. ``bt_row`` maps (virtual) sequences to
     block-table rows (prefill chunks of 8 queries share their sequence's row). ``kv_scales`` = (kscale, vscale):
     the cache is NVFP4 (see :func:`nvfp4_dequant`)."""
@@ -37,7 +38,7 @@ def paged_attention(q, kcache, vcache, block_table, seq_lens, q_per_seq, out, ga
         pps = math.ceil(mp / splits)
     ks, vs = kv_scales if kv_scales else (None, None)
     C().paged_attention(q, kcache, vcache, block_table, seq_lens, q_per_seq, 1.0 / math.sqrt(D), out, gate,
-                        gate_ld, gate_head_stride, splits, pps, window, bt_row, kscale=ks, vscale=vs)
+                        gate_ld, gate_head_stride, splits, pps, window, bt_row, kscale=ks, vscale=vs, impl=impl)
     return out
 
 

@@ -74,14 +74,19 @@ def bench_moe(T=640, E=320, H=2048, I=512, k=10):
     torch.cuda.synchronize()
     out = []
     for name, fn in (("moe_w13_int3", w13), ("moe_w2_int3", w2)):
-        dbg = torch.zeros(148 * 4 * 3, dtype=torch.int64, device=dev)
+        dbg = torch.zeros(148 * 4 * 5, dtype=torch.int64, device=dev)
         fn(dbg)
         torch.cuda.synchronize()
-        d = dbg.view(148, 4, 3).float()
+        d = dbg.view(148, 4, 5).float()
         live = d[:, 0, 2] > 0
+        ks = d[live, :, 2].clamp_min(1)
+        # per role and k-step: cycles waiting, in the main section (loader: copy issue; dequant: load + decode; MMA:
+        # MMA issue; epilogue: TMEM loads + FMAs) and in a second section (dequant: TMEM store; MMA: commits)
         out.append({"kernel": name + "_roles", "roles": ["loader", "dequant", "mma", "epilogue"],
                     "wait_frac": [round(float(v), 3) for v in (d[live, :, 0] / d[live, :, 1]).mean(0)],
-                    "cycles_per_kstep": round(float((d[live, 0, 1] / d[live, 0, 2].clamp_min(1)).mean()), 1)})
+                    "cycles_per_kstep": round(float((d[live, 0, 1] / d[live, 0, 2].clamp_min(1)).mean()), 1),
+                    "section_cycles_per_kstep": [round(float(v), 1) for v in (d[live, :, 3] / ks).mean(0)],
+                    "section2_cycles_per_kstep": [round(float(v), 1) for v in (d[live, :, 4] / ks).mean(0)]})
     wb13 = bank.w13_codes.nbytes + bank.w13_scales.nbytes
     wb2 = bank.w2_codes.nbytes + bank.w2_scales.nbytes
     for name, fn, byts, fl in (
@@ -164,8 +169,12 @@ def bench_attn(S=128, T=5, seed=0):
     out = torch.empty_like(q)
     ms = time_cuda(lambda: paged_attention(q, kc, vc, bt, seq_lens, T, out, max_pages=maxp), flush_bytes=1 << 20)
     byts = int(lens.sum()) * 2 * 2 * 256 * 2
-    res = [{"kernel": "paged_attn_verify", "S": S, "T": T, "ms": round(ms, 4), "kv_bytes": byts,
-            "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)}]
+    ms1 = time_cuda(lambda: paged_attention(q, kc, vc, bt, seq_lens, T, out, max_pages=maxp, impl=1),
+                    flush_bytes=1 << 20)
+    res = [{"kernel": "paged_attn_verify (tcgen05)", "S": S, "T": T, "ms": round(ms, 4), "kv_bytes": byts,
+            "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3)},
+           {"kernel": "paged_attn_verify (mma.sync)", "S": S, "T": T, "ms": round(ms1, 4),
+            "frac_hbm_of_measured": round(byts / ms1 / 1e6 / peaks["hbm_gbs"], 3)}]
     # the same contexts in an NVFP4 cache (random codes, unit scales): 0.5625 bytes per element
     del kc, vc
     k4 = torch.randint(0, 256, (P, 2, 64, 128), dtype=torch.uint8, device=dev)

@@ -13,13 +13,16 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
+@pytest.mark.parametrize("impl", [0, 1])  # tcgen05 kernel, mma.sync kernel
 @pytest.mark.parametrize("D,Hq,Hkv,qp,lens,splits", [
     (256, 16, 2, 5, [5, 64, 70, 1000], None),
     (256, 16, 2, 1, [1, 300, 4097], 4),
     (128, 16, 2, 5, [7, 129, 2000], 3),
     (256, 16, 2, 5, [24000, 4100], None),
+    (256, 16, 2, 8, [8, 520, 3000], 1),
+    (128, 8, 1, 8, [100, 1100], 2),
 ])
-def test_paged_attention(D, Hq, Hkv, qp, lens, splits):
+def test_paged_attention(D, Hq, Hkv, qp, lens, splits, impl):
     g = torch.Generator(device="cpu").manual_seed(D + qp + len(lens))
     S = len(lens)
     maxp = max((L + 63) // 64 for L in lens)
@@ -33,10 +36,31 @@ def test_paged_attention(D, Hq, Hkv, qp, lens, splits):
     gate_view = qkv_like[..., D:]
     out = torch.empty_like(q)
     paged_attention(q, kc, vc, perm, seq_lens, qp, out, gate=qkv_like[..., D:], gate_ld=Hq * 2 * D,
-                    gate_head_stride=2 * D, splits=splits)
+                    gate_head_stride=2 * D, splits=splits, impl=impl)
     torch.cuda.synchronize()
     check_status()
     ref = paged_attention_reference(q, kc, vc, perm, seq_lens, qp, gate=gate_view)
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [1, 3])
+def test_paged_attention_growing_scores(splits):
+    """Scores that grow page after page, so a row's running max jumps by more than 2^8 several times: the tcgen05
+    kernel's lazy rescale of O in tensor memory must keep O, l and m consistent."""
+    g = torch.Generator(device="cpu").manual_seed(7)
+    D, Hq, Hkv, qp, L = 256, 16, 2, 4, 1500
+    maxp = (L + 63) // 64
+    q = (torch.randn(qp, Hq, D, generator=g) * 3).bfloat16().to(dev)
+    grow = (1 + torch.arange(maxp).float() / 2).repeat_interleave(64)[:, None]        # per key position
+    kc = (torch.randn(maxp, Hkv, 64, D, generator=g) * grow.view(maxp, 1, 64, 1)).bfloat16().to(dev)
+    vc = torch.randn(maxp, Hkv, 64, D, generator=g).bfloat16().to(dev)
+    bt = torch.arange(maxp, dtype=torch.int32, device=dev)[None]
+    seq_lens = torch.tensor([L], dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    paged_attention(q, kc, vc, bt, seq_lens, qp, out, splits=splits)
+    torch.cuda.synchronize()
+    check_status()
+    ref = paged_attention_reference(q, kc, vc, bt, seq_lens, qp)
     assert _rel(out, ref) < 1e-2
 
 
