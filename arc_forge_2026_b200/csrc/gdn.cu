@@ -213,7 +213,9 @@ __global__ void __launch_bounds__(QT * DV, 1) gdn_recurrent_kernel(GdnArgs a, in
 //     slot and each warp stores its 4 KB with one bulk copy (the state is not rewritten when no token was accepted);
 //   * this cycle's raw outputs go to shared memory with per-token sums of squares; the gated RMSNorm of an item is
 //     finished after the next item's barrier, one column per thread (fp32 keys, queries and outputs are
-//     double-buffered by item parity, the sums rotate over three slots), so each item costs one block-wide barrier.
+//     double-buffered by item parity, the sums rotate over three slots), so each item costs one block-wide barrier;
+//     the output gate's z values of an item are loaded into registers when its recurrence starts, so the norm pass
+//     waits on no global load.
 // State layout (DK = DV = 128, per (slot, head)): thread t = 4 * v + part owns rows part*32 .. part*32+31 of column v
 // and stores them contiguously, 16-byte chunk c at chunk position c ^ (t & 7) -- so every thread moves its slice
 // with 16-byte accesses and no two lanes of a quarter warp touch the same bank.
@@ -314,15 +316,25 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
   // gated RMSNorm of one finished item's raw outputs: the thread of part 0 of column v finishes column v of every
   // token (the sums of squares were accumulated while the outputs were produced); z is read from global memory, so
   // the item's staging buffer is already free for the next copies
+  const float norm_w = part == 0 ? __bfloat162float(a.norm_w[v]) : 0.f;
+  float zr[MAXT];  // part 0: silu(z) of column v for the item being normalised next, loaded one item ahead
+  auto load_z = [&](int item) {
+    const int seq = item / a.Hv, h = item % a.Hv;
+#pragma unroll
+    for (int t = 0; t < MAXT; ++t)
+      zr[t] = (part == 0 && t < T)
+                  ? __bfloat162float(a.mixed[((size_t)seq * T + t) * a.mixed_ld + a.z_off + h * DV + v])
+                  : 0.f;
+  };
   auto norm_pass = [&](int item, int x, int q3) {
     const int seq = item / a.Hv, h = item % a.Hv;
     if (part == 0) {
-      const float w = __bfloat162float(a.norm_w[v]);
-      for (int t = 0; t < T; ++t) {
+#pragma unroll
+      for (int t = 0; t < MAXT; ++t) {
+        if (t >= T) break;
         const size_t tok = (size_t)seq * T + t;
-        const float z = __bfloat162float(a.mixed[tok * a.mixed_ld + a.z_off + h * DV + v]);
         const float rstd = rsqrtf(sm.ssq[q3][t] / DV + a.eps);
-        a.out[tok * (a.Hv * DV) + h * DV + v] = __float2bfloat16(sm.o[x][t][v] * rstd * w * silu(z));
+        a.out[tok * (a.Hv * DV) + h * DV + v] = __float2bfloat16(sm.o[x][t][v] * rstd * norm_w * silu(zr[t]));
       }
     }
   };
@@ -382,6 +394,7 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
       ++issued;
     }
     if (last >= 0) norm_pass(last, b ^ 1, (i + 2) % 3);
+    load_z(item);  // in flight while this item's recurrence runs; read by its norm pass after the next barrier
     if (tid < MAXT) sm.ssq[(i + 1) % 3][tid] = 0.f;  // item i - 2's sums (read by the last norm pass) -> item i + 1
 
     float lg = 0.f;  // log Gamma
