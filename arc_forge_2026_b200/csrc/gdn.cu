@@ -274,20 +274,20 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
   }
   __syncthreads();
 
-  // warp 0 stages an item: lane 0 arms the barrier, then every lane issues a share of the bulk copies (one lane per
-  // copy, so the warp is not held back by a serial issue loop)
+  // every warp stages a share of an item: copy c is issued by lane c / 16 of warp c % 16 (so no warp's recurrence
+  // is held back by a run of copy issues), and thread 0 arms the barrier with the item's bytes (the transaction
+  // count may go below zero until it does)
   auto issue = [&](int item, int b) {
     const int seq = item / a.Hv, h = item % a.Hv;
     const int slot = sm.slot[seq], np = sm.ncommit[seq];
     const int kh = h / (a.Hv / a.Hk);
-    if (lane == 0) {
+    if (tid == 0) {
       const uint32_t bytes = DK * DV * 4 + np * (DK + DV) * 2 + T * (2 * DK + DV) * 2 + 2 * a.max_q * 8;
       mbar_arrive_expect_tx(&sm.full[b], bytes);
     }
-    __syncwarp();
     // copy list: 0 state, 1 gb prev, 2 gb cur, then per accepted token (k, v), then per new token (k, q, v)
     const int ncopies = 3 + 2 * np + 3 * T;
-    for (int c = lane; c < ncopies; c += 32) {
+    for (int c = wid + (THREADS / 32) * lane; c < ncopies; c += THREADS) {
       if (c == 0) {
         bulk_copy(sm.state[b], a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV, DK * DV * 4, &sm.full[b]);
       } else if (c <= 2) {
@@ -341,17 +341,27 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
   for (int q = tid; q < 3 * MAXT; q += THREADS) (&sm.ssq[0][0])[q] = 0.f;
 
   int issued = 0, done = 0;
-  if (wid == 0 && blockIdx.x < items) {
+  if (blockIdx.x < items) {
     issue(blockIdx.x, 0);
     issued = 1;
   }
   int i = 0, last = -1;
+  long long sec[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // profiling (a.dbg): thread 0's cycles per section
+  long long tclk = a.dbg ? clock64() : 0;
+  auto mark = [&](int k) {
+    if (a.dbg && tid == 0) {
+      const long long now = clock64();
+      sec[k] += now - tclk;
+      tclk = now;
+    }
+  };
   for (int item = blockIdx.x; item < items; item += gridDim.x, ++i) {
     const int b = i & 1;  // staging buffer = item parity (kf / qf / o use the same parity)
     // every thread acquires the copies through the barrier; the vote makes a timeout (flagged in the status word)
     // end the loop on every thread together
     const bool ok = __syncthreads_and(mbar_wait(&sm.full[b], (i >> 1) & 1, status));
     if (!ok) break;
+    mark(0);
     ++done;
     const int seq = item / a.Hv, h = item % a.Hv;
     const int slot = sm.slot[seq], np = sm.ncommit[seq];
@@ -388,14 +398,18 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
     // the one barrier per item: fp32 keys / queries ready; every thread is done with the previous item, so its
     // staging buffer can be refilled and its outputs normalised
     __syncthreads();
+    mark(1);
     const int next = item + gridDim.x;
-    if (wid == 0 && next < items) {
+    if (next < items) {
       issue(next, b ^ 1);
       ++issued;
     }
+    mark(6);
     if (last >= 0) norm_pass(last, b ^ 1, (i + 2) % 3);
+    mark(7);
     load_z(item);  // in flight while this item's recurrence runs; read by its norm pass after the next barrier
     if (tid < MAXT) sm.ssq[(i + 1) % 3][tid] = 0.f;  // item i - 2's sums (read by the last norm pass) -> item i + 1
+    mark(2);
 
     float lg = 0.f;  // log Gamma
     // partial dot of this thread's slice with an fp32 row (four FMA chains), summed over the QT lanes of a column
@@ -418,7 +432,23 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
     // one token of the gated delta rule on S / Gamma: decay g (log), gate beta, value vv, key row kr
     auto step = [&](float g, float beta, float vv, const float* kr) {
       float lgn = lg + g;
-      const float mem = __expf(lgn) * dot(kr);
+      // the key slice stays in registers for both passes (the dot and the rank-1 update)
+      float4 kx[HK / 4];
+      const float4* r4 = reinterpret_cast<const float4*>(kr + part * KP);
+#pragma unroll
+      for (int q = 0; q < HK / 4; ++q) kx[q] = r4[q];
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+      for (int q = 0; q < HK / 4; ++q) {
+        d0 = fmaf(kx[q].x, S[4 * q], d0);
+        d1 = fmaf(kx[q].y, S[4 * q + 1], d1);
+        d2 = fmaf(kx[q].z, S[4 * q + 2], d2);
+        d3 = fmaf(kx[q].w, S[4 * q + 3], d3);
+      }
+      float d = (d0 + d1) + (d2 + d3);
+#pragma unroll
+      for (int o = 1; o < QT; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const float mem = __expf(lgn) * d;
       if (lgn < -60.f) {  // uniform over the CTA: the gates are per (token, head)
         const float f = __expf(lgn);
 #pragma unroll
@@ -427,10 +457,9 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
       }
       lg = lgn;
       const float c = beta * (vv - mem) * __expf(-lg);  // delta / Gamma
-      const float4* r4 = reinterpret_cast<const float4*>(kr + part * KP);
 #pragma unroll
       for (int q = 0; q < HK / 4; ++q) {
-        const float4 x = r4[q];
+        const float4 x = kx[q];
         S[4 * q] = fmaf(x.x, c, S[4 * q]);
         S[4 * q + 1] = fmaf(x.y, c, S[4 * q + 1]);
         S[4 * q + 2] = fmaf(x.z, c, S[4 * q + 2]);
@@ -439,6 +468,7 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
     };
     for (int t = 0; t < np; ++t)
       step(sm.gb[b][0][2 * t], sm.gb[b][0][2 * t + 1], __bfloat162float(sm.v[b][t][v]), sm.kf[b][t]);
+    mark(3);
     if (np > 0) {
       // the committed state Gamma * S back into its slot; each warp stores its 32 threads' slices (4 KB,
       // contiguous in the swizzled layout) with one bulk copy, so no block-wide barrier is needed
@@ -453,6 +483,7 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
         bulk_store(a.ssm_state + ((size_t)slot * a.Hv + h) * DK * DV + wid * 32 * 32, &sm.state[b][wid * 32 * 32],
                    32 * 32 * 4);
     }
+    mark(4);
     for (int t = 0; t < T; ++t) {
       step(sm.gb[b][1][2 * t], sm.gb[b][1][2 * t + 1], __bfloat162float(sm.v[b][MAXT + t][v]), sm.kf[b][np + t]);
       const float o = __expf(lg) * dot(sm.qf[b][t]);
@@ -460,7 +491,12 @@ __global__ void __launch_bounds__(gdnp::THREADS, 1) gdn_verify_persistent_kernel
       const float sq = warp_sum(part == 0 ? o * o : 0.f);  // this warp's 8 columns
       if (lane == 0) atomicAdd(&sm.ssq[i % 3][t], sq);
     }
+    mark(5);
     last = item;
+  }
+  if (a.dbg && tid == 0) {
+    for (int k = 0; k < 8; ++k) a.dbg[blockIdx.x * 10 + k] = sec[k];
+    a.dbg[blockIdx.x * 10 + 8] = done;
   }
   __syncthreads();
   if (last >= 0) norm_pass(last, (i - 1) & 1, (i - 1) % 3);

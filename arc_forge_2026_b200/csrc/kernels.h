@@ -155,6 +155,8 @@ struct GdnArgs {
   int conv_dim = 0, Hk = 0, Hv = 0, Dk = 0, Dv = 0;
   int commit_current = 0;
   float eps = 1e-6f;
+  long long* dbg = nullptr;  // optional profiling: per CTA of the verify kernel (10 slots), clock64 cycles of thread 0 in
+                             // [wait, stage, z loads, commit steps, state store, new steps, copy issue, norm pass, items, 0]
 };
 int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cudaStream_t st);
 

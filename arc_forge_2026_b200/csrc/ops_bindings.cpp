@@ -585,7 +585,7 @@ void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const
                    at::Tensor& pend_v, at::Tensor& pend_gb, const at::Tensor& n_commit, const at::Tensor& seq_slot,
                    const at::Tensor& A_log, const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor& out,
                    int64_t q_per_seq, int64_t Hk, int64_t Dk, int64_t Hv, int64_t Dv, bool commit_current,
-                   int64_t parity, double eps) {
+                   int64_t parity, double eps, c10::optional<at::Tensor> dbg) {
   AFB_CHECK_DT(mixed, at::kBFloat16);
   AFB_CHECK_DT(ssm_state, at::kFloat);
   AFB_CHECK_DT(conv_w, at::kFloat);
@@ -622,6 +622,7 @@ void gdn_decode_op(const at::Tensor& mixed, int64_t z_off, int64_t ba_off, const
   a.Dv = Dv;
   a.commit_current = commit_current;
   a.eps = (float)eps;
+  a.dbg = optr<long long>(dbg);
   TORCH_CHECK(mixed.size(0) == a.num_seqs * q_per_seq, "mixed rows must be num_seqs * q_per_seq");
   TORCH_CHECK(a.conv_dim == 2 * Hk * Dk + Hv * Dv, "conv_dim");
   TORCH_CHECK(pend_in.size(0) == 2 && pend_in.size(3) == a.conv_dim, "pend_in shape");
@@ -1263,7 +1264,11 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("spec_accept", &spec_accept_op);
   m.def("build_window", &build_window_op);
   m.def("gather_rows", &gather_rows_op);
-  m.def("gdn_decode", &gdn_decode_op);
+  m.def("gdn_decode", &gdn_decode_op, py::arg("mixed"), py::arg("z_off"), py::arg("ba_off"), py::arg("conv_w"),
+        py::arg("conv_state"), py::arg("ssm_state"), py::arg("pend_in"), py::arg("pend_qk"), py::arg("pend_v"),
+        py::arg("pend_gb"), py::arg("n_commit"), py::arg("seq_slot"), py::arg("A_log"), py::arg("dt_bias"),
+        py::arg("norm_w"), py::arg("out"), py::arg("q_per_seq"), py::arg("Hk"), py::arg("Dk"), py::arg("Hv"),
+        py::arg("Dv"), py::arg("commit_current"), py::arg("parity"), py::arg("eps"), py::arg("dbg") = py::none());
   m.def("gdn_train", &gdn_train_op);
   m.def("ple_lookup", &ple_lookup_op);
   m.def("lora_rows_times", &lora_rows_times_op);

@@ -73,12 +73,13 @@ class GdnScratch:
 
 def gdn_decode(mixed, shape: GdnShape, state: GdnState, conv_w, A_log, dt_bias, norm_w, n_commit, seq_slot, out,
                q_per_seq: int, parity: int = 0, commit_current: bool = False, scratch: GdnScratch | None = None,
-               eps: float = 1e-6):
-    """mixed [S*q, mixed_dim] bf16 -> out [S*q, Hv*Dv] bf16 (gated-RMSNorm'd GDN output)."""
+               eps: float = 1e-6, dbg=None):
+    """mixed [S*q, mixed_dim] bf16 -> out [S*q, Hv*Dv] bf16 (gated-RMSNorm'd GDN output). ``dbg``: optional int64
+    [CTAs * 10] section clocks of the persistent verify kernel (profiling)."""
     pend = scratch if commit_current else state
     C().gdn_decode(mixed, shape.z_off, shape.ba_off, conv_w, state.conv, state.ssm, pend.pend_in, pend.pend_qk,
                    pend.pend_v, pend.pend_gb, n_commit, seq_slot, A_log, dt_bias, norm_w, out, q_per_seq,
-                   shape.Hk, shape.Dk, shape.Hv, shape.Dv, commit_current, parity, eps)
+                   shape.Hk, shape.Dk, shape.Hv, shape.Dv, commit_current, parity, eps, dbg)
     return out
 
 
