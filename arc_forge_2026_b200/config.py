@@ -164,6 +164,10 @@ class DrafterConfig:
     hc_lowrank: int = 64
     ffn: str = "dense"  # dense | dense_shared (a dense SwiGLU plus a sigmoid-gated shared SwiGLU)
     shared_intermediate_size: int = 0
+    # candidate selector (0: none, proposals are the unary argmax): re-ranks the top-k draft candidates of each slot
+    # with a rank-r bilinear term in the predecessor token and the slot's hidden state (train/drafter_objective.py)
+    selector_top_k: int = 0
+    selector_rank: int = 64
 
     @property
     def k(self) -> int:

@@ -59,6 +59,37 @@ class Drafter:
         self.lm_head = randn(vd, H)
         cos, sin = rope_cos_sin(torch.arange(1 << 17, device=dev), D, cfg.rope_theta)
         self.rope_cos, self.rope_sin = cos.contiguous(), sin.contiguous()
+        self.selector = None
+
+    def set_selector(self, sel: dict | None):
+        """Candidate selector tensors (fp32): ``pred`` [Vd + 1, r], ``succ`` [Vd, r], ``proj`` [r, H] and ``top_k``;
+        None proposes the unary argmax."""
+        if sel is not None:
+            sel = dict(sel)
+            for k in ("pred", "succ", "proj"):
+                sel[k] = sel[k].detach().float().to(self.device).contiguous()
+            to_draft = torch.full((self.vocab_size,), -1, dtype=torch.long, device=self.device)
+            to_draft[self.draft_vocab.long()] = torch.arange(self.draft_vocab.shape[0], device=self.device)
+            sel["to_draft"] = to_draft
+        self.selector = sel
+
+    def _select(self, logits, y, anchor_ids, num_seqs: int, K: int):
+        """Greedy chain through the candidate selector: slot j's predecessor is the token chosen at j - 1 (the
+        anchor for slot 0); scores = unary + < P[pred] * (W y), S[c] > over the slot's top-k candidates."""
+        sel = self.selector
+        unary, cand = logits.float().view(num_seqs, K, -1).topk(sel["top_k"], -1)
+        proj = (y.float() @ sel["proj"].t()).view(num_seqs, K, -1)
+        succ = sel["succ"][cand]                                                   # [S, K, k, r]
+        pred = sel["to_draft"][anchor_ids.long()]
+        vd = sel["succ"].shape[0]
+        picks = []
+        for j in range(K):
+            row = torch.where(pred >= 0, pred, torch.full_like(pred, vd))
+            ctx = sel["pred"][row] * proj[:, j]
+            sc = unary[:, j] + torch.einsum("sr,skr->sk", ctx, succ[:, j])
+            pred = cand[:, j].gather(-1, sc.argmax(-1, keepdim=True)).squeeze(-1)
+            picks.append(pred)
+        return torch.stack(picks, 1)
 
     @classmethod
     def from_dir(cls, path, device, verify: bool = True) -> "Drafter":
@@ -147,6 +178,10 @@ class Drafter:
         cC.rmsnorm(x, None, self.final_norm, y, c.rms_norm_eps, True)
         logits = ws["logits"][:N]
         cC.gemm(y, self.lm_head, out=logits)
+        if self.selector is not None:
+            picks = self._select(logits, y, ids.view(num_seqs, K)[:, 0], num_seqs, K)
+            out_drafts.copy_(self.draft_vocab[picks])
+            return out_drafts
         tok = ws["tok"][:N]
         cC.select_tokens(logits, logits.shape[1], tok, 0.0, 0, None)
         out_drafts.copy_(self.draft_vocab[tok.long()].view(num_seqs, K))

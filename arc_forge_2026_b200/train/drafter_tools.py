@@ -212,6 +212,8 @@ def convert_plain(src: DrafterTrain, calib) -> tuple[DrafterTrain, dict]:
         md.post_norm.zero_()
     for n in ("embed", "fc", "lm_head"):
         getattr(model, n).copy_(getattr(src, n))
+    if src.selector is not None:  # the selector reads the final hidden state, which the fitted final norm keeps
+        model.selector.load_state_dict(src.selector.state_dict())
     model.final_norm.zero_()
     # the gains, one site at a time, each on the converted model's own upstream
     fits = {}

@@ -13,7 +13,9 @@ anchor positions a:
 
 Objectives (the reference's ``training/work/qwen38fn_dflash/objective.py``): ``ce`` (next-token cross-entropy on
 every slot) and, with teacher logits, ``kl`` (forward KL to the target's distribution restricted to the draft
-vocabulary), mixed by ``kl_weight``.
+vocabulary), mixed by ``kl_weight``; with a candidate selector (``selector_top_k`` > 0) also ``dpace``
+(D-PACE-weighted CE, selector CE, early KL), ``acceptance`` (coverage KL + WTV at the serving temperature) and the
+OPD terms over recorded verify cycles (``train/drafter_objective.py``).
 
 Two training-only variants (the reference's ``Config.residual`` / ``ffn_type``, ``qwen38fn_dflash/model.py:20-91``,
 ``:114 GatedResidual``): ``residual="hc"`` keeps G branches of the stream; each sub-layer reads the hyper-connection
@@ -31,6 +33,7 @@ from torch import nn
 
 from ..config import DrafterConfig
 from ..models.reference import HyperConnection, apply_rope, hc_inject, rms_norm, rope_cos_sin
+from .drafter_objective import CandidateSelector, Objective, acceptance_terms, combine, dpace_terms, opd_terms
 
 
 class DrafterTrain(nn.Module):
@@ -82,6 +85,8 @@ class DrafterTrain(nn.Module):
         to_draft = torch.full((vocab_size,), -1, dtype=torch.long)
         to_draft[draft_vocab.long().cpu()] = torch.arange(len(draft_vocab))
         self.register_buffer("to_draft", to_draft.to(device))
+        self.selector = (CandidateSelector(len(draft_vocab), H, cfg.selector_top_k, cfg.selector_rank, device, g, std)
+                         if cfg.selector_top_k > 0 else None)
 
     def _rope(self, x, pos):
         cos, sin = rope_cos_sin(pos, self.cfg.head_dim, self.cfg.rope_theta)
@@ -110,7 +115,8 @@ class DrafterTrain(nn.Module):
             out = out + torch.sigmoid(logit) * ((F.silu(sg[..., :Is]) * sg[..., Is:]) @ m.sw2.t())
         return out
 
-    def block_logits(self, tokens: torch.Tensor, hidden: torch.Tensor, anchors: torch.Tensor, probe=None) -> torch.Tensor:
+    def block_logits(self, tokens: torch.Tensor, hidden: torch.Tensor, anchors: torch.Tensor, probe=None,
+                     return_hidden: bool = False):
         """tokens [T], hidden [T, Ht], anchors [A] (1 <= a, a + K <= T - 1) -> draft-vocab logits [A, K, Vd].
         ``probe(site, stream, sub-layer input, gate)`` is called at every read (sites ``attn<i>``, ``mlp<i>``,
         ``final``; ``shared<i>`` with the shared-gate logits); it may raise to stop the forward early."""
@@ -160,7 +166,68 @@ class DrafterTrain(nn.Module):
             f = self._ffn(m, y, i, probe)
             x = hc_inject(x, f, gate_m) if self.hc else x + f
         y, _ = self._read("final", x, getattr(self, "final_norm", None), getattr(self, "hc_final", None), probe)
-        return y @ self.lm_head.t()
+        logits = y @ self.lm_head.t()
+        return (logits, y) if return_hidden else logits
+
+    def _block_targets(self, tokens, anchors, teacher_logits):
+        K = self.cfg.k
+        tgt_pos = anchors[:, None] + 1 + torch.arange(K, device=tokens.device)[None]
+        labels = self.to_draft[tokens[tgt_pos]]
+        pred = self.to_draft[tokens[tgt_pos - 1]]
+        teacher = None if teacher_logits is None else teacher_logits[tgt_pos - 1][..., self.draft_vocab]
+        return labels, pred, teacher
+
+    def objective_terms(self, tokens, hidden, anchors, obj: Objective, teacher_logits=None) -> dict:
+        """Additive terms of the ``dpace`` / ``acceptance`` objective for the blocks at ``anchors`` (teacher forcing:
+        slot j's predecessor is the data token x[a + j]); ``teacher_logits`` [T, V] are the target's logits."""
+        if self.selector is None:
+            raise ValueError("the dpace / acceptance objectives need a candidate selector (selector_top_k > 0)")
+        logits, y = self.block_logits(tokens, hidden, anchors, return_hidden=True)
+        labels, pred, teacher = self._block_targets(tokens, anchors, teacher_logits)
+        if obj.name == "dpace":
+            return dpace_terms(logits, labels, pred, y, self.selector, teacher, obj.dpace_alpha)
+        if teacher is None:
+            raise ValueError("the acceptance objective needs the teacher's logits")
+        return acceptance_terms(logits, labels, pred, y, self.selector, teacher, obj.temperature, obj.joint)
+
+    def opd_objective_terms(self, tokens, hidden, anchors, drafted, accepted, teacher_logits, obj: Objective,
+                            sampler_q=None, sampler_cand=None) -> dict:
+        """OPD terms of recorded verify cycles at ``anchors``: drafted [A, K] target ids the drafter proposed there,
+        accepted [A], teacher_logits [A, K, V] the target's verify rows on the proposal prefix."""
+        if self.selector is None:
+            raise ValueError("OPD needs a candidate selector")
+        logits, y = self.block_logits(tokens, hidden, anchors, return_hidden=True)
+        d = self.to_draft[drafted]
+        if (d < 0).any():
+            raise ValueError("a recorded draft lies outside the draft vocabulary")
+        return opd_terms(logits, d, self.to_draft[tokens[anchors]], y, self.selector,
+                         teacher_logits[..., self.draft_vocab], accepted, obj.temperature, obj.joint, sampler_q,
+                         None if sampler_cand is None else sampler_cand)
+
+    def objective_loss(self, tokens, hidden, anchors, obj: Objective, teacher_logits=None, opd=None):
+        """Loss of one chunk under ``obj``; ``opd``: the keyword arguments of :meth:`opd_objective_terms`."""
+        if obj.name == "ce":
+            return self.loss(tokens, hidden, anchors, teacher_logits, obj.kl_weight)
+        terms = self.objective_terms(tokens, hidden, anchors, obj, teacher_logits)
+        o = self.opd_objective_terms(obj=obj, **opd) if (opd is not None and obj.opd_weight) else None
+        return combine(obj, terms, o)
+
+    @torch.no_grad()
+    def propose_greedy(self, tokens, hidden, anchors) -> torch.Tensor:
+        """The serving drafter's greedy proposal chain at ``anchors`` [A] -> target ids [A, K]: the unary argmax
+        without a selector; with one, slot j takes the best-scored of its top-k candidates given the token chosen at
+        slot j - 1 (the anchor for slot 0)."""
+        logits, y = self.block_logits(tokens, hidden, anchors, return_hidden=True)
+        if self.selector is None:
+            return self.draft_vocab[logits.argmax(-1)]
+        unary, cand = logits.float().topk(self.selector.top_k, -1)
+        pred = self.to_draft[tokens[anchors]]
+        out = []
+        for j in range(logits.shape[1]):
+            sc = self.selector(cand[:, j], unary[:, j], y[:, j], pred)
+            pred = cand[:, j].gather(-1, sc.argmax(-1, keepdim=True)).squeeze(-1)
+            out.append(pred)
+        return self.draft_vocab[torch.stack(out, 1)]
 
     def loss(self, tokens, hidden, anchors, teacher_logits=None, kl_weight: float = 0.0):
         """Mean CE of every slot's next token (tokens outside the draft vocabulary are skipped), plus
@@ -193,3 +260,6 @@ class DrafterTrain(nn.Module):
         drafter.final_norm.copy_(self.final_norm.to(dt))
         drafter.lm_head.copy_(self.lm_head.to(dt))
         drafter.draft_vocab.copy_(self.draft_vocab.int())
+        drafter.set_selector(None if self.selector is None else dict(
+            top_k=self.selector.top_k, pred=self.selector.pred_codebook.float(),
+            succ=self.selector.succ_codebook.float(), proj=self.selector.proj.float()))

@@ -169,6 +169,44 @@ def test_trained_drafter_export_matches_serving_proposals():
     assert out[0].tolist() == want
 
 
+def test_drafter_with_candidate_selector_export_matches_serving_proposals(tmp_path):
+    """A drafter with a trained-looking candidate selector (non-zero successor codebook, so the selector reorders
+    the unary top-k): published through a drafter directory, the serving drafter's greedy chain equals the twin's."""
+    from arc_forge_2026_b200.train.drafter_tools import save_dir
+    from arc_forge_2026_b200.train.drafter_train import DrafterTrain
+    dcfg = drafter_preset("tiny", selector_top_k=8, selector_rank=16)
+    V, Ht, Lc = 4096, 256, 70
+    g = torch.Generator().manual_seed(11)
+    twin = DrafterTrain(dcfg, Ht, V, torch.randperm(V, generator=g)[:2048].sort().values, seed=5)
+    with torch.no_grad():
+        twin.lm_head.mul_(50.0)
+        twin.selector.succ_codebook.normal_(0, 2.0, generator=g)
+        twin.selector.pred_codebook.normal_(0, 2.0, generator=g)
+        twin.selector.proj.normal_(0, 0.5, generator=g)
+    serving = Drafter.from_dir(save_dir(twin, tmp_path / "d", kind="export"), dev)
+    tokens = torch.randint(0, V, (Lc + dcfg.k + 1,), generator=g)
+    hidden = torch.randn(Lc + dcfg.k + 1, Ht, generator=g) * 0.5
+    with torch.no_grad():
+        want = twin.propose_greedy(tokens, hidden.bfloat16().float(), torch.tensor([Lc]))[0].tolist()
+        plain = twin.draft_vocab[twin.block_logits(tokens, hidden.bfloat16().float(),
+                                                   torch.tensor([Lc])).argmax(-1)[0]].tolist()
+    kv = serving.new_kv_cache(4)
+    ws = serving.new_workspace(128)
+    i32 = dict(dtype=torch.int32, device=dev)
+    pos = torch.arange(Lc, **i32)
+    serving.inject(tokens[:Lc].int().to(dev), hidden[:Lc].bfloat16().to(dev), pos, pos.clone(), kv, ws)
+    blk = torch.full((dcfg.k,), serving.mask_id, **i32)
+    blk[0] = int(tokens[Lc])
+    bpos = torch.arange(Lc, Lc + dcfg.k, **i32)
+    out = torch.zeros(1, dcfg.k, **i32)
+    serving.propose(blk, hidden[Lc - 1:Lc].bfloat16().to(dev), bpos, bpos.clone(), torch.arange(4, **i32).view(1, 4),
+                    torch.tensor([Lc + dcfg.k], **i32), kv, ws, out, 1, max_pages=4)
+    torch.cuda.synchronize()
+    check_status()
+    assert out[0].tolist() == want
+    assert want != plain  # the selector changed the chain, so the test exercises it
+
+
 def test_model_from_package_equals_model_from_reference(tmp_path):
     from arc_forge_2026_b200.formats.int3_package import package_tensors, write_package
     from arc_forge_2026_b200.quant.int3_tiles import tiles_to_codes, tiles_to_scales
