@@ -1,5 +1,14 @@
-"""RL trainer service: HTTP-driven optimizer steps on the student with LoRA adapters (the reference's
-``training/work/qwen38fn_lora/train_rl_service.py:1-61``).
+"""RL trainer service: HTTP-driven optimizer steps on the student with LoRA adapters or, with
+``--trainable full``, on the projection weights themselves (the reference's
+``training/work/qwen38fn_lora/train_rl_service.py:1-61`` and ``dense_full_rl.py:1-37``).
+
+Full-weight mode: the LoRA's target projections of every layer past ``--freeze-first-layers`` plus the shared
+expert's gate / up / down projections are the trainable set, as fp32 masters (a bf16 master would drop most updates:
+an RL step's lr times the update is below the bf16 spacing of |w|) with fp32 AdamW state; the forward multiplies the
+bf16 cast (or the block-FP8 QAT weight) of the master, as deployed. Everything else stays frozen. ``/publish`` writes
+the merged version from the masters (trainer "full"); ``/save`` checkpoints masters and optimizer; a resumed trainer
+re-exports its restored masters at the checkpoint's weight version and refuses to continue unless that equals the
+published version byte for byte (the resume gate).
 
 Rank 0 serves HTTP; each request becomes one command that every rank executes (the command is broadcast over a
 gloo group with ``broadcast_object_list``, so the GPU process group carries only gradients). Routes:
@@ -37,19 +46,96 @@ import torch
 import torch.distributed as dist
 
 from ..parallel.shard_optim import average_gradients
-from .lora import attach_lora, export_merged, load_lora_state, lora_state
+from .lora import DEFAULT_TARGETS, PROJ_MODULE, attach_lora, export_merged, load_lora_state, lora_state
 from .losses import bpo_loss, mis_loss, selective_logprob
 from .optim import AdamWBF16, clip_grad_norm_
 from .routing_replay import RoutingReplay
 
 
+class FullWeights:
+    """The full-weight trainable set of a student: {package key: fp32 master} of the LoRA targets of layers
+    >= ``freeze_first_layers`` and of their shared expert (gate / up halves of the fused ``shared_w13`` and
+    ``shared_down``), the base weights hashed at install (what the merged manifest compares against), and the
+    trainable parameters in model order."""
+
+    def __init__(self, student, targets=DEFAULT_TARGETS, shared: bool = True, freeze_first_layers: int = 0):
+        n = len(student.layers)
+        if not 0 <= freeze_first_layers < n:
+            raise ValueError(f"--freeze-first-layers {freeze_first_layers} of {n} layers")
+        for p in student.parameters():
+            p.requires_grad_(False)
+        self.params, self.slots = [], []  # slots: (key, parameter, row slice or None)
+        for i, layer in enumerate(student.layers):
+            if i < freeze_first_layers:
+                continue
+            for name in targets:
+                w = getattr(layer, name, None)
+                if w is None:
+                    continue
+                self._train(w)
+                self.slots.append((f"model.layers.{i}.{PROJ_MODULE[name]}.{name}.weight", w, None))
+            moe = getattr(layer, "moe", None)
+            if shared and moe is not None and getattr(moe, "shared_w13", None) is not None:
+                Is = moe.shared_w13.shape[0] // 2
+                self._train(moe.shared_w13)
+                self._train(moe.shared_down)
+                p = f"model.layers.{i}.mlp.shared_expert"
+                self.slots += [(f"{p}.gate_proj.weight", moe.shared_w13, slice(0, Is)),
+                               (f"{p}.up_proj.weight", moe.shared_w13, slice(Is, 2 * Is)),
+                               (f"{p}.down_proj.weight", moe.shared_down, None)]
+        self.freeze_first_layers = freeze_first_layers
+        self.base = self.weights()
+
+    def _train(self, w):
+        if w.dtype != torch.float32:
+            raise RuntimeError("full-weight training needs fp32 master weights")
+        w.requires_grad_(True)
+        self.params.append(w)
+
+    def weights(self) -> dict[str, torch.Tensor]:
+        """{package key: fp32 CPU copy of the master}."""
+        return {k: (p.detach() if sl is None else p.detach()[sl]).float().cpu().clone() for k, p, sl in self.slots}
+
+    def load(self, state: dict[str, torch.Tensor]):
+        with torch.no_grad():
+            for k, p, sl in self.slots:
+                (p if sl is None else p[sl]).copy_(state[k].to(p.device))
+
+
+#: manifest fields a re-export must reproduce (the rest are timings and provenance)
+RESUME_EXPORT_FIELDS = ("format", "weight_version", "base_model", "tensors", "bytes", "trainer", "trained_keys")
+
+
+def export_differences(published: dict, again: dict) -> list[str]:
+    """What differs between a published merged manifest and a re-export of the same version: the
+    RESUME_EXPORT_FIELDS and every key's entry. [] = the same bytes."""
+    diff = [f"{f}: {published.get(f)!r} != {again.get(f)!r}" for f in RESUME_EXPORT_FIELDS
+            if published.get(f) != again.get(f)]
+    a, b = published.get("keys", {}), again.get("keys", {})
+    if set(a) != set(b):
+        diff.append(f"keys: {sorted(set(a) ^ set(b))[:3]} on one side only")
+    changed = sorted(k for k in set(a) & set(b) if a[k] != b[k])
+    if changed:
+        diff.append(f"{len(changed)} tensors differ, e.g. {changed[0]}")
+    return diff
+
+
 class RLTrainer:
     def __init__(self, student, out_dir, lr: float = 2e-5, r: int = 16, alpha: float = 32.0, max_norm: float = 1.0,
-                 group=None):
+                 group=None, trainable: str = "lora", freeze_first_layers: int = 0):
         self.student = student
         self.out = Path(out_dir)
-        self.params = attach_lora(student, r, alpha)
-        self.opt = AdamWBF16([{"params": self.params, "lr": lr}])
+        self.trainable = trainable
+        if trainable == "lora":
+            self.full = None
+            self.params = attach_lora(student, r, alpha)
+            self.opt = AdamWBF16([{"params": self.params, "lr": lr}])
+        elif trainable == "full":
+            self.full = FullWeights(student, freeze_first_layers=freeze_first_layers)
+            self.params = self.full.params
+            self.opt = torch.optim.AdamW(self.params, lr=lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0)
+        else:
+            raise ValueError(f"--trainable {trainable!r}: lora | full")
         self.max_norm = max_norm
         self.group = group
         self.step = 0
@@ -146,24 +232,62 @@ class RLTrainer:
         v = int(cmd["weight_version"])
         if v <= self.weight_version:
             raise ValueError(f"weight_version {v} must exceed the last published {self.weight_version}")
-        path = export_merged(self.student, self.out / "merged" / f"v{v:06d}", v, {"optimizer_step": self.step})
+        path = self._export(self.out / "merged" / f"v{v:06d}", v)
         self.weight_version = v
         return {"path": str(path), "weight_version": v}
+
+    def _export(self, path, v: int):
+        if self.full is None:
+            return export_merged(self.student, path, v, {"optimizer_step": self.step})
+        return export_merged(self.student, path, v, {"optimizer_step": self.step}, weights=self.full.weights(),
+                             base=self.full.base)
 
     def save(self, cmd: dict) -> dict:
         target = self.out / f"checkpoint-{self.step}"
         tmp = target.with_name(target.name + ".tmp")
         tmp.mkdir(parents=True, exist_ok=False)
-        torch.save({"lora": lora_state(self.student), "opt": self.opt.state_dict(), "step": self.step,
+        weights = {"lora": lora_state(self.student)} if self.full is None else {"full": self.full.weights(),
+                                                                                "base": self.full.base}
+        torch.save({**weights, "trainable": self.trainable, "opt": self.opt.state_dict(), "step": self.step,
                     "weight_version": self.weight_version}, tmp / "trainer_state.pt")
         os.replace(tmp, target)
         return {"path": str(target)}
 
     def load(self, path):
         st = torch.load(Path(path) / "trainer_state.pt", map_location="cpu", weights_only=False)
-        load_lora_state(self.student, st["lora"])
+        if st.get("trainable", "lora") != self.trainable:
+            raise ValueError(f"checkpoint trains {st.get('trainable', 'lora')!r}, this trainer {self.trainable!r}")
+        if self.full is None:
+            load_lora_state(self.student, st["lora"])
+        else:
+            self.full.load(st["full"])
+            self.full.base = st["base"]
         self.opt.load_state_dict(st["opt"])
         self.step, self.weight_version = st["step"], st["weight_version"]
+        if self.full is not None and self.weight_version > 0:
+            self.check_resumed_export()
+
+    def check_resumed_export(self):
+        """Resume gate (full mode): the restored masters exported again at the checkpoint's weight version must be the
+        published ``merged/v<version>`` byte for byte; raises otherwise."""
+        import shutil
+        import tempfile
+        v = self.weight_version
+        published = self.out / "merged" / f"v{v:06d}"
+        if not (published / "DONE").is_file():
+            raise RuntimeError(f"resume gate: {published} has no DONE, nothing to compare the restored weights with")
+        scratch = Path(tempfile.mkdtemp(prefix=f"resume-check-v{v:06d}-"))
+        try:
+            again = self._export(scratch / published.name, v)
+            a = json.loads((published / "merged_manifest.json").read_text())
+            b = json.loads((again / "merged_manifest.json").read_text())
+            a.pop("optimizer_step", None)
+            b.pop("optimizer_step", None)
+            diff = export_differences(a, b)
+        finally:
+            shutil.rmtree(scratch)
+        if diff:
+            raise RuntimeError(f"resume gate: restored weights differ from {published}: " + "; ".join(diff))
 
     def execute(self, cmd: dict) -> dict:
         """Run one command on this rank (every rank runs the same commands in the same order)."""
@@ -254,6 +378,10 @@ def main(argv=None):
     ap.add_argument("--port", type=int, default=8100)
     ap.add_argument("--resume", type=Path)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--trainable", choices=["lora", "full"], default="lora",
+                    help="lora: adapters on the projections; full: the projections (+ shared experts) themselves")
+    ap.add_argument("--freeze-first-layers", dest="freeze_first_layers", type=int, default=0,
+                    help="full: decoder layers 0..F-1 stay frozen")
     args = ap.parse_args(argv)
     from ..config import preset
     from .student import random_student
@@ -266,7 +394,8 @@ def main(argv=None):
                                 timeout=datetime.timedelta(seconds=600))
         control = dist.new_group(backend="gloo")
     student = random_student(preset(args.preset), dev, seed=args.seed)
-    trainer = RLTrainer(student, args.out, args.lr, args.lora_rank, args.lora_alpha)
+    trainer = RLTrainer(student, args.out, args.lr, args.lora_rank, args.lora_alpha, trainable=args.trainable,
+                        freeze_first_layers=args.freeze_first_layers)
     if args.resume:
         trainer.load(args.resume)
     if rank != 0:

@@ -1,6 +1,7 @@
 """RL / LoRA pieces on CPU: adapters (identity at init, gradients, exact merge), fn-lora-merged-v2 export, the
 delta-only weight patch, routing replay, and the HTTP trainer service taking optimizer steps."""
 import json
+from pathlib import Path
 
 import pytest
 import torch
@@ -190,3 +191,55 @@ def test_rl_step_accumulated_over_calls_equals_one_call(tmp_path):
     assert all(torch.allclose(s1[k].float(), s2[k].float(), atol=1e-6) for k in s1)
     with pytest.raises(RuntimeError):
         acc.step_opt()
+
+
+def test_full_weight_rl_trains_the_projections_publishes_and_resumes(tmp_path):
+    """--trainable full: fp32 masters of the LoRA targets and the shared experts of layers >= F train, nothing else
+    moves; /publish writes the merged version from the masters; a resumed trainer passes the resume gate and
+    continues exactly like an uninterrupted one, and a checkpoint whose masters do not re-export the published
+    version is refused."""
+    from safetensors.torch import load_file
+    from arc_forge_2026_b200.train.rl_service import RLTrainer
+    g = torch.Generator().manual_seed(5)
+    c = preset("tiny_cpu")
+    B, T = 2, 10
+    batch = {"ids": torch.randint(0, c.vocab_size, (B, T), generator=g),
+             "labels": torch.randint(0, c.vocab_size, (B, T), generator=g), "mask": torch.ones(B, T),
+             "advantages": torch.tensor([1.0, -0.5]), "behavior_logp": -torch.rand(B, T, generator=g) * 3}
+    st = _student(6)
+    before = {n: p.detach().clone() for n, p in st.named_parameters()}
+    tr = RLTrainer(st, tmp_path / "run", lr=1e-3, trainable="full", freeze_first_layers=1)
+    trainable = {id(p) for p in tr.params}
+    names = {n for n, p in st.named_parameters() if id(p) in trainable}
+    assert names and not any(n.startswith("layers.0.") for n in names)
+    assert all(p.dtype == torch.float32 for p in tr.params)
+    for _ in range(3):
+        rep = tr.train({"batch": batch})
+    assert rep["step"] == 3 and rep["grad_norm"] > 0
+    changed = {n for n, p in st.named_parameters() if not torch.equal(p.detach(), before[n])}
+    assert changed and changed <= names, sorted(changed - names)[:3]
+    path = Path(tr.publish({"weight_version": 1})["path"])
+    man = json.loads((path / "merged_manifest.json").read_text())
+    assert man["trainer"] == "full" and man["trained_keys"] == len(tr.full.slots)
+    tensors = load_file(str(path / "model.safetensors"))
+    w = tr.full.weights()
+    key = next(k for k in w if k.endswith("o_proj.weight"))
+    assert torch.equal(tensors[key], w[key].to(torch.bfloat16))
+    assert man["keys"][key]["changed_elements"] > 0
+    ck = Path(tr.save({})["path"])
+    tr.train({"batch": batch})
+    # resume from the checkpoint: the gate passes and the next step matches the uninterrupted trainer's
+    tr2 = RLTrainer(_student(6), tmp_path / "run", lr=1e-3, trainable="full", freeze_first_layers=1)
+    tr2.load(ck)
+    tr2.train({"batch": batch})
+    a, b = tr.full.weights(), tr2.full.weights()
+    assert all(torch.equal(a[k], b[k]) for k in a)
+    # a checkpoint whose masters were altered does not re-export the published version
+    state = torch.load(ck / "trainer_state.pt", weights_only=False)
+    state["full"][key] = state["full"][key] + 1e-2
+    bad = tmp_path / "bad"
+    bad.mkdir()
+    torch.save(state, bad / "trainer_state.pt")
+    tr3 = RLTrainer(_student(6), tmp_path / "run", lr=1e-3, trainable="full", freeze_first_layers=1)
+    with pytest.raises(RuntimeError, match="resume gate"):
+        tr3.load(bad)
