@@ -50,26 +50,6 @@ struct Smem {
 };
 }  // namespace attn_tc
 
-// K-major 128-byte-swizzle descriptor with an explicit leading (between 64-element MN blocks) and stride (between
-// 8-row groups) byte offset: the MN-major operand form (the V page read as keys x D, D contiguous)
-AFB_DEV uint64_t sw128_desc_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
-  return d;
-}
-// kind::f16 with the A operand in tensor memory
-AFB_DEV void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 template <int D>
 __global__ void __launch_bounds__(attn_tc::THREADS, 1)
     paged_attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,

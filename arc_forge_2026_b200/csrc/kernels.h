@@ -140,7 +140,7 @@ struct GdnArgs {
   int mixed_ld = 0, z_off = 0, ba_off = 0;
   const float* conv_w = nullptr;         // [C, 4]
   __nv_bfloat16* conv_state = nullptr;   // [slots, 3, C]
-  float* ssm_state = nullptr;            // [slots, Hv, Dk, Dv]
+  float* ssm_state = nullptr;            // [slots, Hv, Dv, Dk]: S transposed
   __nv_bfloat16* pend_in = nullptr;      // [2, pend_slots, max_q, C]
   __nv_bfloat16* pend_qk = nullptr;      // [2, pend_slots, max_q, 2*Hk*Dk]
   __nv_bfloat16* pend_v = nullptr;       // [2, pend_slots, max_q, Hv*Dv]
@@ -155,8 +155,7 @@ struct GdnArgs {
   int conv_dim = 0, Hk = 0, Hv = 0, Dk = 0, Dv = 0;
   int commit_current = 0;
   float eps = 1e-6f;
-  long long* dbg = nullptr;  // optional profiling: per CTA of the verify kernel (10 slots), clock64 cycles of thread 0 in
-                             // [wait, stage, z loads, commit steps, state store, new steps, copy issue, norm pass, items, 0]
+  long long* dbg = nullptr;  // optional profiling of the tensor-core verify kernel: per CTA 24 clock64 section sums
 };
 int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cudaStream_t st);
 

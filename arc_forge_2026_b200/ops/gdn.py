@@ -48,7 +48,7 @@ class GdnState:
         max_q += max_q % 2  # even: each head's (g, beta) block is then 16-byte aligned for bulk copies
         self.shape = s
         self.conv = torch.zeros(slots, 3, s.conv_dim, dtype=torch.bfloat16, device=dev)
-        self.ssm = torch.zeros(slots, s.Hv, s.Dk, s.Dv, dtype=state_dtype, device=dev)
+        self.ssm = torch.zeros(slots, s.Hv, s.Dv, s.Dk, dtype=state_dtype, device=dev)  # S transposed
         self.pend_in = torch.zeros(2, slots, max_q, s.conv_dim, dtype=torch.bfloat16, device=dev)
         self.pend_qk = torch.zeros(2, slots, max_q, 2 * s.Hk * s.Dk, dtype=torch.bfloat16, device=dev)
         self.pend_v = torch.zeros(2, slots, max_q, s.Hv * s.Dv, dtype=torch.bfloat16, device=dev)
@@ -75,7 +75,7 @@ def gdn_decode(mixed, shape: GdnShape, state: GdnState, conv_w, A_log, dt_bias, 
                q_per_seq: int, parity: int = 0, commit_current: bool = False, scratch: GdnScratch | None = None,
                eps: float = 1e-6, dbg=None):
     """mixed [S*q, mixed_dim] bf16 -> out [S*q, Hv*Dv] bf16 (gated-RMSNorm'd GDN output). ``dbg``: optional int64
-    [CTAs * 10] section clocks of the persistent verify kernel (profiling)."""
+    [CTAs * 24] section clocks of the tensor-core verify kernel (profiling)."""
     pend = scratch if commit_current else state
     C().gdn_decode(mixed, shape.z_off, shape.ba_off, conv_w, state.conv, state.ssm, pend.pend_in, pend.pend_qk,
                    pend.pend_v, pend.pend_gb, n_commit, seq_slot, A_log, dt_bias, norm_w, out, q_per_seq,

@@ -143,16 +143,22 @@ def bench_gdn(S=128, T=5):
         par[0] += 1
     ms = time_cuda(fn)
     byts = 2 * st.ssm.nbytes + mixed.nbytes + out.nbytes
-    dbg = torch.zeros(148 * 10, dtype=torch.int64, device=dev)
+    dbg = torch.zeros(148 * 24, dtype=torch.int64, device=dev)
     gdn_decode(mixed, sh, st, conv_w, A_log, dt, nw, n_commit, slots, out, T, par[0] & 1, dbg=dbg)
     torch.cuda.synchronize()
-    d = dbg.view(148, 10).double()
-    live = d[:, 8] > 0
-    per = (d[live, :8].sum(0) / d[live, 8].sum()).tolist()
+    d = dbg.view(148, 24).cpu()
+    items = int((d[:, 7] >> 40).sum())
+    d[:, 7] &= (1 << 40) - 1
+    names = ["wait", "stage", "barrier A", "phase 1", "mma1 wait", "solve", "barrier C", "commit"]
+    sections = {}
+    if items:
+        for who, off in (("thread0", 0), ("mma_thread", 8)):
+            sections[who] = {n: round(float(d[:, off + k].sum()) / items) for k, n in enumerate(names)}
+        sections["solve_parts"] = {n: round(float(d[:, 16 + k].sum()) / items) for k, n in
+                                   enumerate(["P load", "u chain", "outputs+sums", "U^T", "sums barrier", "norm"])}
     return [{"kernel": "gdn_decode(conv_prep+recurrent)", "S": S, "T": T, "ms": round(ms, 4), "bytes": byts,
              "gbs": round(byts / ms / 1e6, 1), "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
-             "cycles_per_item": dict(zip(["wait", "stage", "z+ssq", "commit", "store", "new", "issue", "norm"],
-                                         [round(v) for v in per]))}]
+             "cycles_per_item": sections}]
 
 
 def bench_attn(S=128, T=5, seed=0):
