@@ -18,7 +18,8 @@ Model presets:
   top-10 of 320 experts with intermediate 512 plus a 512-wide shared expert, vocab 151,936.
 * ``qwen3next_80b_teacher`` -- the same with 512 experts (QAD teacher, block FP8).
 * ``qwen38fn`` -- the reference's own shape (``training/run_records/A4/config/recorded-config-99c11efb.json``):
-  hidden 2560, 24Q/2KV x 256, GDN 16 QK / 48 V heads, 512 experts x 640, vocab 248,320, 4 hyper-connections.
+  hidden 2560, 24Q/2KV x 256, GDN 16 QK / 48 V heads, 512 experts x 640, vocab 248,320, 4 hyper-connections,
+  PLE at layer 2, QSA top-512 of 4-token blocks (indexer budget 2048, compress ratio 4, 4 heads x 128).
 """
 from __future__ import annotations
 
@@ -87,8 +88,10 @@ class ModelConfig:
             raise ValueError("GDN value heads must be a multiple of key heads")
         if not 1 <= self.num_experts_per_tok <= self.num_experts:
             raise ValueError("invalid top-k")
-        if self.qsa_topk and (self.qsa_block != 64 or self.qsa_indexer_dim != 128 or not 1 <= self.qsa_indexer_heads <= 4):
-            raise ValueError("QSA needs 64-token blocks (one KV page), 128-dim index heads and 1..4 of them")
+        if self.qsa_topk and (self.qsa_block not in (4, 8, 16, 32, 64) or self.qsa_indexer_dim != 128
+                              or not 1 <= self.qsa_indexer_heads <= 4):
+            raise ValueError("QSA needs blocks of 4..64 tokens dividing the 64-token page, 128-dim index heads and "
+                             "1..4 of them")
         rot = self.rotary_dim
         if rot <= 0 or rot % 2:
             raise ValueError("rotary dimension must be positive and even")
@@ -230,8 +233,8 @@ PRESETS: dict[str, dict[str, Any]] = {
         name="qwen38fn", vocab_size=248320, hidden_size=2560, num_layers=48, full_attention_interval=4,
         num_attention_heads=24, num_kv_heads=2, head_dim=256, linear_num_key_heads=16, linear_num_value_heads=48,
         linear_key_head_dim=128, linear_value_head_dim=128, num_experts=512, num_experts_per_tok=10,
-        moe_intermediate_size=640, shared_expert_intermediate_size=640, hc_count=4, qsa_block=4, qsa_topk=512,
-        expert_format="int3"),
+        moe_intermediate_size=640, shared_expert_intermediate_size=640, hc_count=4, ple_layer_ids=(2,), qsa_block=4,
+        qsa_topk=512, expert_format="int3"),
 }
 
 

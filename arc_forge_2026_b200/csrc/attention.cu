@@ -510,16 +510,18 @@ static int launch_attn(const AttnArgs& a, int splits, uint32_t* status, cudaStre
 int paged_attention_tc(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st);  // attention_tc.cu
 
 int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st) {
-  if (a.q_per_seq * (a.Hq / a.Hkv) > 64) return 3;
   if (splits > 1 && (!a.part_o || !a.part_lse)) return 4;
   if (a.num_seqs == 0) return 0;
   const bool fp4 = a.kscale != nullptr;
+  const bool gather = a.sp_count && a.sp_block != 64;  // sub-page QSA blocks: the tcgen05 kernel or nothing
+  if (gather && (a.sp_block < 1 || 64 % a.sp_block || a.sp_ld < 1)) return 3;
   if (const int rc = paged_attention_tc(a, splits, status, st); rc != -1) {
     if (rc || splits == 1) return rc;
     if (a.D == 256) attn_merge_kernel<256><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
     else attn_merge_kernel<128><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
     return (int)cudaGetLastError();
   }
+  if (gather || a.q_per_seq * (a.Hq / a.Hkv) > 64) return 3;  // the mma.sync kernel holds <= 64 rows per CTA
   if (a.D == 256) return fp4 ? launch_attn<256, true>(a, splits, status, st) : launch_attn<256, false>(a, splits, status, st);
   if (a.D == 128) return fp4 ? launch_attn<128, true>(a, splits, status, st) : launch_attn<128, false>(a, splits, status, st);
   return 3;

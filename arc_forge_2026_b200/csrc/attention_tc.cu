@@ -2,8 +2,9 @@
 // KV cache, dense causal mode: the path the serving verify step runs for every full-attention layer.
 //
 // One CTA per (sequence, KV head, KV split), as in attention.cu: its query rows are the q_per_seq verify positions x
-// the Hq/Hkv query heads of the KV head (row r = t * group + h, at most 64 rows), so one KV page read from HBM
-// serves every head and position. Per 64-key page:
+// the Hq/Hkv query heads of the KV head (row r = t * group + h, at most 64 rows; a wider set, e.g. 8 positions x 12
+// heads, is cut into runs of 64 / group positions over gridDim.z), so one KV page read serves every head and
+// position. Per 64-key page:
 //   S = Q K^T   tcgen05.mma kind::f16, M=128 (rows past the CTA's rows are never read), N=64, K=16 per op;
 //               Q and the K page are K-major 128-byte-swizzled shared-memory operands, S lands in TMEM
 //   softmax     two warps (TMEM lane quadrants 0 and 1 = rows 0..63) load S rows, mask (causality inside the verify
@@ -17,7 +18,16 @@
 // Warp roles: 0 loader (TMA of Q and of the K and V pages, no multicast, 3-stage ring), 1 MMA issuer (+ TMEM),
 // 4-5 softmax / output (the rows), the others idle. S and P are double-buffered so the QK^T of page i+1 overlaps the
 // softmax of page i and the PV of page i-1. Splits write (O / l, m + log2 l) partials for attn_merge_kernel.
+//
+// QSA sparse modes (sp_count set): the CTA walks its sequence's block union instead of its pages. With 64-token
+// blocks an entry is a page (the TMA loader reads the union's physical pages); with smaller blocks (4 for the
+// reference's QSA) warps 2, 3, 6 and 7 gather 64 / B entries into each 64-key tile with 16-byte cp.async copies
+// written at the 128-byte-swizzled offsets the TMA would use, a proxy fence per thread before its arrive. The
+// softmax warps turn each tile's (block, row mask) entries into a per-row 64-bit visibility mask (mask bit of the
+// row's verify position and causality), so the MMA side is the same in every mode.
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -30,6 +40,7 @@ constexpr int PAGE = 64;
 constexpr int THREADS = 256;
 constexpr int W_LD = 0, W_MMA = 1, W_SM0 = 4;  // softmax warps 4 and 5
 constexpr float RESCALE = 8.f;                 // log2 growth of a row max that forces an O rescale
+constexpr int GATHER_THREADS = 128;            // warps 2, 3, 6, 7 in the sub-page gather mode
 
 template <int D>
 struct Smem {
@@ -40,7 +51,9 @@ struct Smem {
   static constexpr int NS = D == 256 ? 3 : 6;                 // KV stages
   static constexpr uint32_t STAGE = 2 * KV_BYTES;
   static constexpr uint32_t KV_OFF = Q_BYTES;
-  static constexpr uint32_t BAR_OFF = KV_OFF + NS * STAGE;
+  static constexpr uint32_t VIS_OFF = KV_OFF + NS * STAGE;    // sparse modes: per stage, per key, the verify
+                                                              // positions (bits) that may see the key
+  static constexpr uint32_t BAR_OFF = VIS_OFF + NS * PAGE * 4;
   // kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full[2], o_done[2], q_ready, mma_fin, tmem slot
   static constexpr uint32_t TOTAL = BAR_OFF + (2 * NS + 10) * 8 + 16 + 1024;
   // TMEM columns: O [D], S [2][64], P [2][32] (bf16 pairs)
@@ -68,24 +81,40 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
   uint64_t* q_ready = o_done + 2;
   uint64_t* mma_fin = q_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_fin + 1);
+  uint32_t* vis_all = reinterpret_cast<uint32_t*>(smem + L::VIS_OFF);  // [NS][PAGE]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int seq = blockIdx.x / a.Hkv, kvh = blockIdx.x % a.Hkv;
-  const int split = blockIdx.y;
+  // blockIdx.x = (sequence, KV head, row run): the row runs of one (sequence, head) are neighbours in launch order,
+  // so they stream the same KV close together in time (the second read mostly hits L2)
   const int group = a.Hq / a.Hkv;
-  const int QR = a.q_per_seq * group;  // query rows of this CTA (<= 64)
+  const int tpc = min(a.q_per_seq, 64 / group);
+  const int nruns = (a.q_per_seq + tpc - 1) / tpc;
+  const int run = blockIdx.x % nruns;
+  const int seq = blockIdx.x / nruns / a.Hkv, kvh = blockIdx.x / nruns % a.Hkv;
+  const int split = blockIdx.y;
+  // query positions per CTA: all of them when q_per_seq x group <= 64, else a run of tpc positions
+  const int tbase = run * tpc;
+  const int QR = min(tpc, a.q_per_seq - tbase) * group;  // live query rows of this CTA (<= 64)
   const int seq_len = a.seq_lens[seq];
   const int past = seq_len - a.q_per_seq;
-  const int npages = (seq_len + PAGE - 1) / PAGE;
+  const bool sparse = a.sp_count != nullptr;
+  const bool gather = sparse && a.sp_block < PAGE;  // sub-page blocks gathered into 64-key tiles
+  const int spb = sparse ? a.sp_block : PAGE;       // tokens per union entry
+  const int ept = PAGE / spb;                       // entries per tile
+  const int cnt = sparse ? a.sp_count[seq] : 0;
+  const int npages = sparse ? (cnt + ept - 1) / ept : (seq_len + PAGE - 1) / PAGE;  // 64-key tiles
   const int p0 = split * a.pages_per_split;
   const int p1 = min(npages, p0 + a.pages_per_split);
   const int n = max(0, p1 - p0);
-  const int* bt = a.block_table + (size_t)seq * a.max_pages;
+  const int* bt = a.block_table + (size_t)(a.bt_row ? a.bt_row[seq] : seq) * a.max_pages;
+  const int sp_ld = a.sp_ld ? a.sp_ld : a.max_pages;
+  const int* spl = sparse ? a.sp_lpage + (size_t)seq * sp_ld : nullptr;
+  const uint8_t* spm = sparse ? a.sp_mask + (size_t)seq * sp_ld : nullptr;
 
   if (n == 0) {  // an empty split (or a sequence without keys): nothing to stream, no TMEM
     const int r = threadIdx.x;
     if (r < QR) {
-      const size_t tok = (size_t)seq * a.q_per_seq + r / group;
+      const size_t tok = (size_t)seq * a.q_per_seq + tbase + r / group;
       const int head = kvh * group + r % group;
       if (gridDim.y > 1) {
         a.part_lse[((size_t)split * a.num_tokens + tok) * a.Hq + head] = -INFINITY;
@@ -99,7 +128,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_full[s], gather ? GATHER_THREADS : 1);
       mbar_init(&kv_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -121,17 +150,20 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
 
   if (warp == W_LD) {
     // ------------------------------------------------------------------ loader
-    // Q: one 3-D box {64 columns, group heads, q_per_seq tokens} per 64-column sub-tile lands rows t * group + h
+    // Q: one 3-D box {64 columns, group heads, tpc tokens} per 64-column sub-tile lands rows t * group + h (rows
+    // past the live ones hold other positions or the out-of-range fill: never read)
     if (lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_ready, (uint32_t)QR * D * 2);
+      mbar_arrive_expect_tx(q_ready, (uint32_t)(tpc * group) * D * 2);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tma_load_3d(smem + c * L::SUB, &tmQ, q_ready, c * 64, kvh * group, seq * a.q_per_seq);
+      for (int c = 0; c < D / 64; ++c)
+        tma_load_3d(smem + c * L::SUB, &tmQ, q_ready, c * 64, kvh * group, seq * a.q_per_seq + tbase);
     }
-    // block-table entries 32 at a time (one per lane), then one K + V fill per page
+    // block-table entries 32 at a time (one per lane), then one K + V fill per page (the gather warps fill the
+    // tiles in the sub-page mode)
     int issued = 0;
-    for (int base = 0; base < n && ok; base += 32) {
+    for (int base = 0; base < n && ok && !gather; base += 32) {
       const int mine = base + lane < n ? bt[p0 + base + lane] : 0;
       const int cnt = min(32, n - base);
       for (int j = 0; j < cnt; ++j) {
@@ -140,6 +172,21 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
         if (i >= NS && !__all_sync(0xffffffffu, mbar_wait(&kv_empty[s], ((i / NS) & 1) ^ 1, status))) {
           ok = false;
           break;
+        }
+        if (sparse) {  // page union: every key of entry p0 + i, its logical position and row mask
+          const int e = p0 + i;
+          const int lp = spl[e];
+          const uint32_t mk = spm[e];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int pos = lp * PAGE + lane + 32 * h;
+            uint32_t vb = 0;
+#pragma unroll
+            for (int tt = 0; tt < 8; ++tt)
+              if (((mk >> tt) & 1u) && pos <= past + tt) vb |= 1u << tt;
+            vis_all[s * PAGE + lane + 32 * h] = vb;
+          }
+          __syncwarp();
         }
         if (lane == 0) {
           const int row = (page * a.Hkv + kvh) * PAGE;
@@ -160,6 +207,81 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       mbar_wait(q_ready, 0, status);
       for (int i = max(0, issued - NS); i < issued; ++i) mbar_wait(&kv_full[i % NS], (i / NS) & 1, status);
     }
+  } else if (gather && (warp == 2 || warp == 3 || warp == 6 || warp == 7)) {
+    // ------------------------------------------------------------------ sub-page gather (QSA blocks < 64 tokens)
+    // One 16-byte chunk per thread and copy: the 128 threads walk the tile's 64 rows x D/8 chunks chunk-fastest,
+    // so a warp's copy covers whole contiguous rows (512 or 256 bytes). Lane l resolves keys l and l + 32 (KV slot,
+    // position bits) for the NEXT tile while this tile's copies are issued; the slots go round by shuffles. Up to
+    // NS - 1 tiles of copies are in flight; tile i - (NS - 1) is published (this thread's wait for its group, a
+    // proxy fence, the arrive) BEFORE the wait for tile i's stage, since freeing that stage needs the QK^T of the
+    // tile after the one that used it.
+    constexpr int CH = D / 8;  // 16-byte chunks per row
+    constexpr int ITERS = PAGE * CH / GATHER_THREADS;
+    constexpr int LAG = NS - 1;
+    const int gw = (warp & 3) - 2 + (warp >> 2) * 2;  // warps 2, 3, 6, 7 -> 0..3
+    const int gt = gw * 32 + lane;
+    auto resolve = [&](int i, int (&slot)[2], uint32_t (&vb)[2]) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = lane + 32 * h, e = (p0 + i) * ept + k / spb;
+        slot[h] = -1;
+        vb[h] = 0;
+        if (i < n && e < cnt) {
+          const int sl = a.sp_slot[(size_t)seq * sp_ld + e] + k % spb;  // a block never crosses a page
+          const int pos = spl[e] * spb + k % spb;
+          const uint32_t mk = spm[e];
+#pragma unroll
+          for (int tt = 0; tt < 8; ++tt)
+            if (((mk >> tt) & 1u) && pos <= past + tt) vb[h] |= 1u << tt;
+          if (sl >= 0 && (sl >> 6) < a.num_pages) slot[h] = sl;
+          else flag_error(status, AFB_ERR_BOUNDS);
+        }
+      }
+    };
+    int cur[2], nxt[2];
+    uint32_t vcur[2], vnxt[2];
+    resolve(0, cur, vcur);
+    int issued = 0, published = 0;
+    for (int i = 0; i < n; ++i) {
+      const int s = i % NS;
+      if (i >= LAG) {
+        cp_async_wait<LAG - 1>();
+        fence_proxy_async_smem();
+        mbar_arrive(&kv_full[published % NS]);
+        ++published;
+      }
+      resolve(i + 1, nxt, vnxt);  // loads in flight under this tile's copies
+      if (i >= NS && !mbar_wait(&kv_empty[s], ((i / NS) & 1) ^ 1, status)) {
+        ok = false;
+        break;
+      }
+      if (gw == 0) {  // published by these threads' arrives for the tile
+        vis_all[s * PAGE + lane] = vcur[0];
+        vis_all[s * PAGE + 32 + lane] = vcur[1];
+      }
+      uint8_t* st = smem + L::KV_OFF + s * L::STAGE;
+      const char* kb = reinterpret_cast<const char*>(a.kcache);
+      const char* vbase = reinterpret_cast<const char*>(a.vcache);
+#pragma unroll
+      for (int it = 0; it < ITERS; ++it) {
+        const int idx = it * GATHER_THREADS + gt, key = idx / CH, c = idx % CH;
+        const int sl = __shfl_sync(0xffffffffu, key < 32 ? cur[0] : cur[1], key & 31);
+        const uint32_t bytes = sl >= 0 ? 16u : 0u;
+        const size_t off = sl >= 0 ? ((((size_t)(sl >> 6) * a.Hkv + kvh) * PAGE + (sl & 63)) * D * 2 + c * 16) : 0;
+        const uint32_t so = (c >> 3) * L::SUB + key * 128 + (((c & 7) ^ (key & 7)) << 4);
+        cp_async16(st + so, kb + off, bytes);
+        cp_async16(st + L::KV_BYTES + so, vbase + off, bytes);
+      }
+      cp_async_commit();
+      ++issued;
+      cur[0] = nxt[0];
+      cur[1] = nxt[1];
+      vcur[0] = vnxt[0];
+      vcur[1] = vnxt[1];
+    }
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    for (; published < issued; ++published) mbar_arrive(&kv_full[published % NS]);
   } else if (warp == W_MMA) {
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc_s = idesc_f16(128, PAGE, 1);             // S = Q K^T
@@ -216,7 +338,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
     // ------------------------------------------------------------------ softmax + output (rows 0..63)
     const int quad = warp - W_SM0;
     const int r = quad * 32 + lane;  // query row = TMEM lane
-    const int t = r / group, hq = r % group;
+    const int t = tbase + r / group, hq = r % group;  // verify position (0 .. q_per_seq - 1) and head
     const bool live = r < QR;
     const int vis = past + t + 1;  // keys this row may see: positions < vis
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
@@ -226,6 +348,27 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (i >> 1) & 1, status))) {
         ok = false;
         break;
+      }
+      // sparse: this row's visible keys of tile i, from the per-key position bits the loader wrote with the tile
+      // (its stage is not refilled before this tile's PV): two ballots per verify position
+      uint32_t vlo = 0, vhi = 0;
+      if (sparse) {
+        const int st = i % NS;
+        if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (i / NS) & 1, status))) {
+          ok = false;
+          break;
+        }
+        const uint32_t vb0 = vis_all[st * PAGE + lane], vb1 = vis_all[st * PAGE + 32 + lane];
+#pragma unroll
+        for (int tt = 0; tt < 8; ++tt) {
+          if (tt >= a.q_per_seq) break;
+          const uint32_t b0 = __ballot_sync(0xffffffffu, (vb0 >> tt) & 1u);
+          const uint32_t b1 = __ballot_sync(0xffffffffu, (vb1 >> tt) & 1u);
+          if (tt == t) {
+            vlo = b0;
+            vhi = b1;
+          }
+        }
       }
       tc_fence_after();
       float sv[PAGE];
@@ -239,7 +382,8 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < PAGE; ++j) {
-        const float x = (live && kbase + j < vis) ? sv[j] * a.scale_log2 : -INFINITY;
+        const bool see = sparse ? (((j < 32 ? vlo >> j : vhi >> (j - 32)) & 1u) != 0) : kbase + j < vis;
+        const float x = (live && see) ? sv[j] * a.scale_log2 : -INFINITY;
         sv[j] = x;
         mx = fmaxf(mx, x);
       }
@@ -355,21 +499,23 @@ static int launch_attn_tc(const AttnArgs& a, int splits, uint32_t* status, cudaS
   const int group = a.Hq / a.Hkv;
   const uint64_t qdims[3] = {(uint64_t)D, (uint64_t)a.Hq, (uint64_t)a.num_tokens};
   const uint64_t qstr[2] = {(uint64_t)D * 2, (uint64_t)a.Hq * D * 2};
-  const uint32_t qbox[3] = {64, (uint32_t)group, (uint32_t)a.q_per_seq};
+  const int tpc = std::min(a.q_per_seq, 64 / group);
+  const uint32_t qbox[3] = {64, (uint32_t)group, (uint32_t)tpc};
   rc = make_tmap_3d_bf16(&tq, a.q, qdims, qstr, qbox);
   if (rc) return 1000 + rc;
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)paged_attn_tc_kernel<D>, L::TOTAL)) return e;
-  dim3 grid(a.num_seqs * a.Hkv, splits);
+  dim3 grid(a.num_seqs * a.Hkv * ((a.q_per_seq + tpc - 1) / tpc), splits);
   paged_attn_tc_kernel<D><<<grid, attn_tc::THREADS, L::TOTAL, st>>>(tk, tv, tq, a, status);
   return (int)cudaGetLastError();
 }
 
-// The tcgen05 path serves dense bf16 decode / verify (no window, no virtual prefill rows, no QSA union); returns -1
-// when the call is outside that set (the caller runs the mma.sync kernel), else the launch result.
+// The tcgen05 path serves bf16 decode / verify and prefill rows, dense or over a QSA block union (no window);
+// returns -1 when the call is outside that set (the caller runs the mma.sync kernel), else the launch result.
 int paged_attention_tc(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st) {
-  if (a.impl == 1 || a.kscale || a.sp_count || a.window > 0 || a.bt_row || a.q_per_seq * (a.Hq / a.Hkv) > 64)
-    return -1;
+  if (a.impl == 1 || a.kscale || a.window > 0 || a.Hq / a.Hkv > 64) return -1;
+  if (a.bt_row && a.sp_count && a.sp_block == attn_tc::PAGE) return -1;  // page unions are per sequence
+  if (a.sp_count && (a.q_per_seq > 8 || a.sp_block < 1 || attn_tc::PAGE % a.sp_block)) return -1;
   if (a.D == 256) return launch_attn_tc<256>(a, splits, status, st);
   if (a.D == 128) return launch_attn_tc<128>(a, splits, status, st);
   return -1;

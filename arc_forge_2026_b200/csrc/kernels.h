@@ -51,19 +51,25 @@ struct AttnArgs {
   __nv_bfloat16* out = nullptr;         // [num_tokens, Hq, D]
   float* part_o = nullptr;              // [splits, num_tokens, Hq, D]
   float* part_lse = nullptr;            // [splits, num_tokens, Hq]
-  // QSA sparse mode (all null: dense). block_table rows then hold each sequence's page union (max_pages = union
-  // capacity); sp_count[seq] entries are live, sp_lpage gives each entry's page index in the sequence (key
-  // positions) and sp_mask the bitmask of verify rows that attend to it.
+  // QSA sparse mode (all null: dense). An entry is a block of sp_block tokens: sp_count[seq] entries are live,
+  // sp_lpage gives each entry's block index in the sequence (key positions) and sp_mask the bitmask of verify rows
+  // that attend to it (rows [seq, sp_ld]). sp_block 64: a block is a page and block_table rows hold the physical
+  // page of each entry (the union; sp_ld = max_pages). sp_block < 64 (a divisor of 64; tcgen05 kernel only): the
+  // block table is the sequences' own and the kernel gathers 64 / sp_block entries into each 64-key tile.
   const int* sp_count = nullptr;
   const int* sp_lpage = nullptr;
   const uint8_t* sp_mask = nullptr;
+  int sp_block = 64, sp_ld = 0;
+  const int* sp_slot = nullptr;      // sub-page mode: [seq, sp_ld] KV slot (page * 64 + offset) of each entry's first
+                                     // token (the union builder resolves the block table once per entry)
   // 0: the tcgen05 kernel (attention_tc.cu) wherever it applies (bf16 cache, dense, no window, no virtual rows),
   // else the mma.sync kernel; 1: always the mma.sync kernel
   int impl = 0;
 };
 int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st);
 
-// qsa.cu: QSA indexer, page selection and union for block-sparse verify attention (block = one 64-token page)
+// qsa.cu: QSA indexer, block selection and union for block-sparse verify attention (block = `block` tokens, a
+// divisor of the 64-token page: 64 makes a block one page)
 constexpr int QSA_MAX_LAYERS = 64;
 struct QsaArgs {
   int Hi = 4, Di = 128, rot = 64;           // index heads, head dim, RoPE dims
@@ -73,27 +79,39 @@ struct QsaArgs {
   const float* sin_t = nullptr;
   __nv_bfloat16* idx_q = nullptr;           // [tokens, Hi, Di]
   __nv_bfloat16* idx_raw = nullptr;         // [num_pages * 64, Di] per-token raw index keys (by KV slot)
-  const __nv_bfloat16* idx_key = nullptr;   // [S * max_pages, Di] pooled keys of finalised pages (session, page)
+  const __nv_bfloat16* idx_key = nullptr;   // [S * max_blocks, Di] pooled keys of finalised blocks (session, block)
 };
 struct QsaSelectArgs {
   const int* block_table = nullptr;  // [S, max_pages]
   int max_pages = 0, max_blocks = 0;
-  const int* fin = nullptr;          // [S] finalised pages per session
+  int block = 64;                    // tokens per block (divides 64)
+  const int* fin = nullptr;          // [sessions] finalised blocks per session
   const int* seq_lens = nullptr;     // [S] tokens including this cycle's W verify rows
+  const int* bt_row = nullptr;       // optional [S]: session of each row set (prefill); null: set s is session s
   int W = 1, K = 32;
-  int* u_page = nullptr;             // [S, ucap] physical pages of the union
-  int* u_lpage = nullptr;            // [S, ucap] page index in the sequence
-  uint8_t* u_mask = nullptr;         // [S, ucap] rows that attend to the page
+  // blocks completed inside the verify window have no pooled key yet: they are pooled on the fly from the raw keys
+  const __nv_bfloat16* k_norm = nullptr;
+  uint32_t* sel = nullptr;           // [S, max_blocks + 1] row bitmasks, all zero between calls (the union clears them)
+  int* u_page = nullptr;             // [S, ucap] physical page of each union entry (block 64), or the KV slot of
+                                     // its first token (smaller blocks)
+  int* u_lpage = nullptr;            // [S, ucap] block index in the sequence
+  uint8_t* u_mask = nullptr;         // [S, ucap] rows that attend to the block
   int* u_count = nullptr;            // [S]
   int ucap = 0;
+  // optional [S, W, scores_ld] fp32 scratch: the committed blocks' scores come from the tensor-core score kernel
+  // (W * Hi <= 32); null: the per-row kernel scores them on the CUDA cores
+  float* scores = nullptr;
+  int scores_ld = 0;
+  int key_rows = 0;                  // rows of idx_key (sessions * max_blocks), for its tensor map
+  int q_rows = 0;                    // rows of idx_q
 };
 struct QsaFinalizeArgs {
   const __nv_bfloat16* idx_raw[QSA_MAX_LAYERS] = {};
   __nv_bfloat16* idx_key[QSA_MAX_LAYERS] = {};
   const __nv_bfloat16* k_norm[QSA_MAX_LAYERS] = {};
   const int* block_table = nullptr;  // [S, max_pages]
-  int max_pages = 0;
-  int* fin = nullptr;                // [S] in: finalised so far; out: ctx / 64
+  int max_pages = 0, max_blocks = 0, block = 64;
+  int* fin = nullptr;                // [S] in: finalised blocks so far; out: ctx / block
   const int* ctx = nullptr;          // [S] committed tokens
   const float* cos_t = nullptr;
   const float* sin_t = nullptr;

@@ -114,12 +114,7 @@ AFB_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 
 AFB_DEV void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
-// 16-byte async copy global -> shared (zero-filled when src_bytes is 0) and the arrive of this thread's async
-// copies on an mbarrier (counted in the barrier's expected arrivals)
-AFB_DEV void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
+// the arrive of this thread's async copies (cp_async16) on an mbarrier (counted in the barrier's expected arrivals)
 AFB_DEV void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

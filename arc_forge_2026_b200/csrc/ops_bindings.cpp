@@ -313,7 +313,8 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
                         int64_t splits, int64_t pages_per_split, int64_t window, c10::optional<at::Tensor> bt_row,
                         c10::optional<at::Tensor> sp_count, c10::optional<at::Tensor> sp_lpage,
                         c10::optional<at::Tensor> sp_mask, c10::optional<at::Tensor> kscale,
-                        c10::optional<at::Tensor> vscale, int64_t impl) {
+                        c10::optional<at::Tensor> vscale, int64_t impl, int64_t sp_block,
+                        c10::optional<at::Tensor> sp_slot) {
   AFB_CHECK_DT(q, at::kBFloat16);
   AFB_CHECK_CONTIG(q);
   AFB_CHECK_CONTIG(kcache);
@@ -352,9 +353,26 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
     AFB_CHECK_DT(sp_count.value(), at::kInt);
     AFB_CHECK_DT(sp_lpage.value(), at::kInt);
     AFB_CHECK_DT(sp_mask.value(), at::kByte);
-    TORCH_CHECK(sp_lpage->sizes() == block_table.sizes() && sp_mask->sizes() == block_table.sizes(),
-                "sp_lpage / sp_mask must match the block table");
+    TORCH_CHECK(sp_block >= 1 && 64 % sp_block == 0, "sp_block must divide the 64-token page");
+    TORCH_CHECK(sp_lpage->dim() == 2 && sp_lpage->size(0) == a.num_seqs && sp_mask->sizes() == sp_lpage->sizes(),
+                "sp_lpage / sp_mask must be [num_seqs, union capacity]");
+    TORCH_CHECK(sp_block < 64 || sp_lpage->sizes() == block_table.sizes(),
+                "page-block sparse mode: the block table rows are the page unions (same shape as sp_lpage)");
+    TORCH_CHECK(sp_block == 64 || (impl == 0 && !kscale.has_value()),
+                "sub-page QSA blocks run on the tcgen05 kernel only (bf16 cache)");
+    TORCH_CHECK(sp_block < 64 || !bt_row.has_value(), "page-block sparse mode: the union rows are per sequence");
     TORCH_CHECK(q_per_seq <= 8 && window == 0, "sparse mode: at most 8 verify rows, no window");
+    AFB_CHECK_CONTIG(sp_lpage.value());
+    AFB_CHECK_CONTIG(sp_mask.value());
+    a.sp_block = (int)sp_block;
+    a.sp_ld = sp_lpage->size(1);
+    if (sp_block < 64) {
+      TORCH_CHECK(sp_slot.has_value() && sp_slot->sizes() == sp_lpage->sizes(),
+                  "sub-page mode needs sp_slot (the union's first-token KV slots), shaped as sp_lpage");
+      AFB_CHECK_DT(sp_slot.value(), at::kInt);
+      AFB_CHECK_CONTIG(sp_slot.value());
+      a.sp_slot = ptr<int>(sp_slot.value());
+    }
     a.sp_count = ptr<int>(sp_count.value());
     a.sp_lpage = ptr<int>(sp_lpage.value());
     a.sp_mask = ptr<uint8_t>(sp_mask.value());
@@ -399,40 +417,74 @@ void qsa_prep_op(const at::Tensor& proj, int64_t idx_off, const at::Tensor& posi
            "qsa_prep");
 }
 
-void qsa_select_op(const at::Tensor& idx_q, const at::Tensor& idx_key, const at::Tensor& block_table,
-                   const at::Tensor& fin, const at::Tensor& seq_lens, int64_t W, int64_t K, int64_t Hi,
-                   at::Tensor& u_page, at::Tensor& u_lpage, at::Tensor& u_mask, at::Tensor& u_count) {
+void qsa_select_op(const at::Tensor& idx_q, const at::Tensor& idx_key, const at::Tensor& idx_raw,
+                   const at::Tensor& k_norm, const at::Tensor& block_table, const at::Tensor& fin,
+                   const at::Tensor& seq_lens, int64_t W, int64_t K, int64_t Hi, int64_t block, at::Tensor& sel,
+                   const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t rot, double eps, at::Tensor& u_page,
+                   at::Tensor& u_lpage, at::Tensor& u_mask, at::Tensor& u_count, c10::optional<at::Tensor> bt_row,
+                   c10::optional<at::Tensor> scores) {
   AFB_CHECK_DT(idx_q, at::kBFloat16);
   AFB_CHECK_DT(idx_key, at::kBFloat16);
+  AFB_CHECK_DT(idx_raw, at::kBFloat16);
   AFB_CHECK_DT(block_table, at::kInt);
   AFB_CHECK_DT(u_mask, at::kByte);
+  AFB_CHECK_DT(sel, at::kInt);
+  AFB_CHECK_DT(cos_t, at::kFloat);
   const int S = seq_lens.size(0);
   TORCH_CHECK(idx_q.numel() >= (int64_t)S * W * Hi * 128, "idx_q rows");
   TORCH_CHECK(u_page.size(0) >= S && u_page.sizes() == u_lpage.sizes() && u_page.sizes() == u_mask.sizes(),
               "union buffers");
+  const int max_blocks = block_table.size(1) * (64 / (int)block);
+  TORCH_CHECK(sel.numel() >= (int64_t)S * (max_blocks + 1), "sel scratch [S, max_blocks + 1]");
+  TORCH_CHECK(idx_key.size(0) >= (int64_t)(bt_row.has_value() ? block_table.size(0) : S) * max_blocks,
+              "pooled key rows [sessions * max_blocks]");
+  if (bt_row.has_value()) {
+    AFB_CHECK_DT(bt_row.value(), at::kInt);
+    TORCH_CHECK(bt_row->numel() == S, "bt_row: one session per row set");
+  }
   afb::QsaArgs a;
   a.Hi = (int)Hi;
   a.idx_q = reinterpret_cast<__nv_bfloat16*>(idx_q.data_ptr());
   a.idx_key = reinterpret_cast<const __nv_bfloat16*>(idx_key.data_ptr());
+  a.idx_raw = reinterpret_cast<__nv_bfloat16*>(idx_raw.data_ptr());
+  a.cos_t = ptr<float>(cos_t);
+  a.sin_t = ptr<float>(sin_t);
+  a.rot = (int)rot;
+  a.eps = (float)eps;
   afb::QsaSelectArgs sa;
   sa.block_table = ptr<int>(block_table);
   sa.max_pages = block_table.size(1);
-  sa.max_blocks = block_table.size(1);
+  sa.block = (int)block;
+  sa.max_blocks = max_blocks;
   sa.fin = ptr<int>(fin);
   sa.seq_lens = ptr<int>(seq_lens);
   sa.W = (int)W;
   sa.K = (int)K;
+  sa.k_norm = reinterpret_cast<const __nv_bfloat16*>(k_norm.data_ptr());
+  sa.sel = reinterpret_cast<uint32_t*>(sel.data_ptr());
   sa.u_page = ptr<int>(u_page);
   sa.u_lpage = ptr<int>(u_lpage);
   sa.u_mask = ptr<uint8_t>(u_mask);
   sa.u_count = ptr<int>(u_count);
   sa.ucap = u_page.size(1);
+  sa.bt_row = optr<int>(bt_row);
+  if (scores.has_value()) {  // tensor-core scores of the committed blocks
+    AFB_CHECK_DT(scores.value(), at::kFloat);
+    TORCH_CHECK(scores->numel() >= (int64_t)S * W * max_blocks, "scores scratch [S * W * max_blocks]");
+    AFB_CHECK_CONTIG(idx_q);
+    AFB_CHECK_CONTIG(idx_key);
+    sa.scores = ptr<float>(scores.value());
+    sa.scores_ld = max_blocks;
+    sa.key_rows = idx_key.size(0);
+    sa.q_rows = idx_q.size(0) * Hi;
+  }
   check_rc(afb::qsa_select(a, sa, S, status_ptr(idx_q.get_device()), stream()), "qsa_select");
 }
 
 void qsa_finalize_op(const std::vector<at::Tensor>& idx_raw, const std::vector<at::Tensor>& idx_key,
                      const std::vector<at::Tensor>& k_norm, const at::Tensor& block_table, at::Tensor& fin,
-                     const at::Tensor& ctx, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t rot, double eps) {
+                     const at::Tensor& ctx, const at::Tensor& cos_t, const at::Tensor& sin_t, int64_t rot, double eps,
+                     int64_t block) {
   const int L = idx_raw.size();
   TORCH_CHECK(L >= 1 && L <= afb::QSA_MAX_LAYERS && (int)idx_key.size() == L && (int)k_norm.size() == L,
               "qsa_finalize: one raw cache, key cache and norm per layer");
@@ -444,6 +496,10 @@ void qsa_finalize_op(const std::vector<at::Tensor>& idx_raw, const std::vector<a
   }
   f.block_table = ptr<int>(block_table);
   f.max_pages = block_table.size(1);
+  f.block = (int)block;
+  f.max_blocks = f.max_pages * (64 / (int)block);
+  for (int l = 0; l < L; ++l)
+    TORCH_CHECK(idx_key[l].size(0) >= (int64_t)fin.size(0) * f.max_blocks, "pooled key rows [S * max_blocks]");
   f.fin = ptr<int>(fin);
   f.ctx = ptr<int>(ctx);
   f.cos_t = ptr<float>(cos_t);
@@ -1294,7 +1350,7 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("gate"), py::arg("gate_ld"), py::arg("gate_head_stride"), py::arg("splits"),
         py::arg("pages_per_split"), py::arg("window"), py::arg("bt_row"), py::arg("sp_count") = py::none(),
         py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none(), py::arg("kscale") = py::none(),
-        py::arg("vscale") = py::none(), py::arg("impl") = 0);
+        py::arg("vscale") = py::none(), py::arg("impl") = 0, py::arg("sp_block") = 64, py::arg("sp_slot") = py::none());
   m.def("qsa_prep", &qsa_prep_op);
   py::class_<GuardCtx>(m, "GuardCtx")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, const at::Tensor&,
@@ -1315,7 +1371,11 @@ void register_kernel_ops(pybind11::module& m) {
       .def("writeback", &HsCtx::writeback)
       .def("after_prefill", &HsCtx::after_prefill)
       .def("fetch", &HsCtx::fetch);
-  m.def("qsa_select", &qsa_select_op);
+  m.def("qsa_select", &qsa_select_op, py::arg("idx_q"), py::arg("idx_key"), py::arg("idx_raw"), py::arg("k_norm"),
+        py::arg("block_table"), py::arg("fin"), py::arg("seq_lens"), py::arg("W"), py::arg("K"), py::arg("Hi"),
+        py::arg("block"), py::arg("sel"), py::arg("cos_t"), py::arg("sin_t"), py::arg("rot"), py::arg("eps"),
+        py::arg("u_page"), py::arg("u_lpage"), py::arg("u_mask"), py::arg("u_count"), py::arg("bt_row") = py::none(), py::arg("scores") = py::none());
+
   m.def("qsa_finalize", &qsa_finalize_op);
   m.def("embedding", &embedding_op);
 }

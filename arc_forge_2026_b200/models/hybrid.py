@@ -93,8 +93,12 @@ def _random_ple(cfg: ModelConfig, std: float, gen, dev) -> PleServeWeights:
     h = NgramHash(cfg)
     G, H, E = cfg.hc_count, cfg.hidden_size, cfg.ple_embed_dim
     D = E // cfg.ngram_heads
-    # e4m3 rows drawn directly (a real table is ~51 GB: no fp32 staging), scale std per 128 x 128 block
-    rows = torch.randn(h.rows, D, generator=gen, device=dev).clamp_(-8, 8).to(torch.float8_e4m3fn)
+    # e4m3 rows drawn in chunks (a real table is ~51 GB: no full fp32 staging), scale std per 128 x 128 block
+    rows = torch.empty(h.rows, D, dtype=torch.float8_e4m3fn, device=dev)
+    step = max(1, (1 << 27) // D)
+    for r0 in range(0, h.rows, step):
+        n = min(step, h.rows - r0)
+        rows[r0:r0 + n] = torch.randn(n, D, generator=gen, device=dev).clamp_(-8, 8).to(torch.float8_e4m3fn)
     scale = torch.full(((h.rows + 127) // 128, (D + 127) // 128), std, dtype=torch.float32, device=dev)
 
     def rn(*s):
@@ -250,7 +254,11 @@ class HybridModel:
                               L.post_attention_layernorm.weight.detach().to(**bf))
             m = L.mixer
             if L.kind == FULL:
-                lw.w_qkv = torch.cat([m.q_proj.weight, m.k_proj.weight, m.v_proj.weight]).detach().to(**bf)
+                idx = [m.index_qk_proj.weight] if cfg.qsa_topk else []  # QSA index rows after q | k | v
+                lw.w_qkv = torch.cat([m.q_proj.weight, m.k_proj.weight, m.v_proj.weight, *idx]).detach().to(**bf)
+                if cfg.qsa_topk:
+                    lw.qsa_q_norm = m.index_q_norm.weight.detach().to(**bf)
+                    lw.qsa_k_norm = m.index_k_norm.weight.detach().to(**bf)
                 lw.q_norm = m.q_norm.weight.detach().to(**bf)
                 lw.k_norm = m.k_norm.weight.detach().to(**bf)
                 lw.w_o = m.o_proj.weight.detach().to(**bf).contiguous()
@@ -401,11 +409,12 @@ class HybridModel:
                  torch.zeros(shape, dtype=torch.bfloat16, device=self.device)) for _ in range(c.num_attention_layers)]
 
     def new_qsa_cache(self, num_pages: int, sessions: int, max_pages: int):
-        """Per full-attention layer: raw index keys by KV slot [pages*64, 128] and pooled page keys by (session
-        row, page index) [sessions * max_pages, 128]."""
+        """Per full-attention layer: raw index keys by KV slot [pages*64, 128] and pooled block keys by (session
+        row, block index) [sessions * max_pages * 64 / qsa_block, 128]."""
         z = dict(dtype=torch.bfloat16, device=self.device)
+        nb = max_pages * (PAGE // self.cfg.qsa_block)
         return [(torch.zeros(num_pages * PAGE, self.cfg.qsa_indexer_dim, **z),
-                 torch.zeros(sessions * max_pages, self.cfg.qsa_indexer_dim, **z))
+                 torch.zeros(sessions * nb, self.cfg.qsa_indexer_dim, **z))
                 for _ in range(self.cfg.num_attention_layers)]
 
     def new_ple_states(self, slots: int, max_q: int):
@@ -467,7 +476,17 @@ class HybridModel:
                 if qsa is not None and b.attn_bt_row is None:
                     qsa_attention(q.view(-1, Hq, D), kc, vc, b.block_table, b.seq_lens, qsa.fin, key, qsa.ws,
                                   attn.view(-1, Hq, D), gate=gate, gate_ld=row_len, gate_head_stride=2 * D,
-                                  splits=qsa.splits, hs=qsa.hs, layer=ai, replay=qsa.replay, kv_scales=kvs)
+                                  splits=qsa.splits, hs=qsa.hs, layer=ai, replay=qsa.replay, kv_scales=kvs,
+                                  raw=raw, k_norm=lw.qsa_k_norm, rope=(self.rope_cos, self.rope_sin),
+                                  rot=c.rotary_dim, eps=c.rms_norm_eps)
+                elif b.attn_bt_row is not None and qsa is not None and qsa.pf is not None:
+                    # prefill under QSA: row sets of attn_q_per_seq positions select their blocks like verify rows
+                    qp = b.attn_q_per_seq
+                    nv = b.attn_bt_row.shape[0]
+                    qsa.prefill_attention(ws.q[: nv * qp].view(-1, Hq, D), kc, vc, b.block_table, b.attn_seq_lens,
+                                          b.attn_bt_row, ai, raw, key, lw.qsa_k_norm,
+                                          ws.attn[: nv * qp].view(-1, Hq, D), ws.qkv[: nv * qp, D:], row_len, 2 * D,
+                                          kv_scales=kvs)
                 elif b.attn_bt_row is not None:
                     # prefill: virtual rows of attn_q_per_seq queries; rows past N are padding (scratch)
                     qp = b.attn_q_per_seq

@@ -137,6 +137,50 @@ class GatedAttention(nn.Module):
         self.o_proj = nn.Linear(cfg.num_attention_heads * D, H, bias=False)
         self.q_norm = RMSNorm(D, cfg.rms_norm_eps)
         self.k_norm = RMSNorm(D, cfg.rms_norm_eps)
+        if cfg.qsa_topk:  # QSA indexer: Hi query heads + one raw key per token, zero-centred norms
+            Di, Hi = cfg.qsa_indexer_dim, cfg.qsa_indexer_heads
+            self.index_qk_proj = nn.Linear(H, (Hi + 1) * Di, bias=False)
+            self.index_q_norm = RMSNorm(Di, cfg.rms_norm_eps)
+            self.index_k_norm = RMSNorm(Di, cfg.rms_norm_eps)
+
+    def qsa_allowed(self, x, positions, cache, S):
+        """QSA block selection (``training/work/qwen38fn_lora/sparse_qsa.py:83-153``) -> allowed [B, T, S] or None
+        (every query keeps all its complete blocks). A query at position p sees its complete blocks b < (p + 1) / B:
+        all when there are <= K, else the top-K by sum_h relu(q_h . k_b) / sqrt(Di) (ties to the lower index), plus
+        its own incomplete block. k_b = RoPE_{B b}(norm_k(mean of the block's raw keys, in the raw keys' dtype))."""
+        c = self.cfg
+        Bsz, T, _ = x.shape
+        Di, Hi, Bk, K = c.qsa_indexer_dim, c.qsa_indexer_heads, c.qsa_block, c.qsa_topk
+        proj = self.index_qk_proj(x)
+        iq, raw = proj[..., :Hi * Di].view(Bsz, T, Hi, Di), proj[..., Hi * Di:]
+        cos, sin = rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
+        iq = apply_rope(self.index_q_norm(iq), cos, sin)
+        if cache is not None:
+            if "idx_raw" in cache:
+                raw = torch.cat([cache["idx_raw"], raw], dim=1)
+            cache["idx_raw"] = raw
+        qpos = torch.arange(S - T, S, device=x.device)
+        complete = (qpos + 1) // Bk
+        nb = S // Bk
+        if int(complete.max()) <= K:
+            return None
+        pooled = raw[:, :nb * Bk].reshape(Bsz, nb, Bk, Di).float().mean(2).to(raw.dtype)
+        bc, bs = rope_cos_sin(torch.arange(nb, device=x.device) * Bk, c.rotary_dim, c.rope_theta)
+        keys = apply_rope(self.index_k_norm(pooled)[:, :, None], bc, bs)[:, :, 0]
+        sc = torch.einsum("bthd,bnd->bthn", iq.float(), keys.float()).relu().sum(2) / math.sqrt(Di)
+        allowed = torch.ones(Bsz, T, S, dtype=torch.bool, device=x.device)
+        blk = torch.arange(S, device=x.device) // Bk
+        for t in range(T):
+            n = int(complete[t])
+            if n <= K:
+                continue
+            for b in range(Bsz):
+                order = torch.sort(sc[b, t, :n], descending=True, stable=True).indices[:K]
+                keep = torch.zeros(nb + 1, dtype=torch.bool, device=x.device)
+                keep[order] = True
+                keep[n:] = True  # the own incomplete block (later keys are causally masked)
+                allowed[b, t] = keep[blk]
+        return allowed
 
     def qkv(self, x, positions):
         """x [B,T,H] -> q [B,T,Hq,D] (normed, roped), gate [B,T,Hq*D], k,v [B,T,Hkv,D] (k normed, roped)."""
@@ -161,6 +205,7 @@ class GatedAttention(nn.Module):
                 v = torch.cat([cache["v"], v], dim=1)
             cache["k"], cache["v"] = k, v
         S = k.shape[1]
+        allowed = self.qsa_allowed(x, positions, cache, S) if c.qsa_topk else None
         rep = c.num_attention_heads // c.num_kv_heads
         kk = k.repeat_interleave(rep, dim=2)
         vv = v.repeat_interleave(rep, dim=2)
@@ -168,6 +213,8 @@ class GatedAttention(nn.Module):
         qpos = torch.arange(S - T, S, device=x.device)
         mask = torch.arange(S, device=x.device)[None, :] > qpos[:, None]
         scores = scores.masked_fill(mask, float("-inf"))
+        if allowed is not None:
+            scores = scores.masked_fill(~allowed[:, None], float("-inf"))
         attn = torch.einsum("bhts,bshd->bthd", torch.softmax(scores, dim=-1), vv.float()).to(x.dtype)
         out = attn.reshape(B, T, -1) * torch.sigmoid(gate.float()).to(x.dtype)
         return self.o_proj(out)

@@ -70,6 +70,8 @@ class SpecEngine:
         W = self.W = K + 1
         self.max_context = max_context
         self.maxp = math.ceil((max_context + 2 * W + 8) / PAGE)
+        # prefill attention runs virtual sequences of this many consecutive queries (x the GQA group <= 64 rows)
+        self.prefill_rows = max(1, min(8, 64 // (model.cfg.num_attention_heads // model.cfg.num_kv_heads)))
         self.hs_slots = 0
         if scfg.hisparse:  # GPU pages: per-session caches and rings, prefill staging, scratch (the host holds history)
             if not model.cfg.qsa_topk:
@@ -82,6 +84,10 @@ class SpecEngine:
         # writes never land in another session's pages
         self.scratch_page = num_pages - 1
         self.alloc = C().PageAllocator(num_pages - 1, PAGE)
+        if scfg.hisparse and model.cfg.qsa_block != 64:
+            raise ValueError("HiSparse moves whole KV pages: it needs 64-token QSA blocks (qsa_block=64)")
+        if scfg.kv_dtype == "nvfp4" and model.cfg.qsa_topk and model.cfg.qsa_block != 64:
+            raise ValueError("QSA blocks smaller than a page run on the bf16 KV cache")
         if scfg.kv_dtype == "nvfp4" and scfg.hisparse:
             raise ValueError("the HiSparse host pool holds bf16 / e4m3 pages: use kv_dtype='bf16' with hisparse")
         self.kv = model.new_kv_cache(num_pages, scfg.kv_dtype)
@@ -138,7 +144,10 @@ class SpecEngine:
         self.qsa = None
         if model.cfg.qsa_topk:
             from ..ops.qsa import QsaState
-            self.qsa = QsaState(model, S, W, num_pages, self.maxp, max(S * W, PREFILL_CHUNK), splits=scfg.qsa_splits)
+            # index-query rows: a verify step's S * W, or a prefill chunk rounded up to whole row sets
+            self.qsa = QsaState(model, S, W, num_pages, self.maxp, max(S * W, PREFILL_CHUNK + 8), splits=scfg.qsa_splits,
+                                prefill_sets=math.ceil(PREFILL_CHUNK / self.prefill_rows),
+                                prefill_rows=self.prefill_rows)
         self.hs = None
         if scfg.hisparse:
             from ..ops.hisparse import HiSparseState
@@ -369,12 +378,15 @@ class SpecEngine:
             T = min(PREFILL_CHUNK, L - c0)
             pos = torch.arange(c0, c0 + T, device=dev, dtype=torch.int32)
             slots = (pages[pos.long() // PAGE] * PAGE + (pos.long() % PAGE)).int()
-            nv = (T + 7) // 8
-            vlen = torch.clamp(torch.arange(1, nv + 1, device=dev, dtype=torch.int32) * 8 + c0, max=c0 + nv * 8)
+            qp = self.prefill_rows
+            nv = (T + qp - 1) // qp
+            vlen = torch.arange(1, nv + 1, device=dev, dtype=torch.int32) * qp + c0
+            if self.qsa is not None:  # this chunk's QSA bookkeeping: the blocks its raw keys complete
+                self.qsa.prefill_chunk(sess.row, c0 if c0 > start else 0, c0 + T)
             b = StepBatch(ids_all[c0:c0 + T].contiguous(), pos, slots, self.block_table, None, slot_row,
                           self.n_commit, T, 0, commit_current=True, max_pages=self.maxp,
                           attn_bt_row=torch.full((nv,), sess.row, dtype=torch.int32, device=dev),
-                          attn_seq_lens=vlen, attn_q_per_seq=8)
+                          attn_seq_lens=vlen, attn_q_per_seq=qp)
             hidden = m.forward(b, self.kv, self.gdn, self.ws, self.gdn_scratch, qsa=self.qsa, ple=self.ple)
             if on_chunk is not None:
                 on_chunk(hidden[:T], c0)

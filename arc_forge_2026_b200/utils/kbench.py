@@ -4,6 +4,7 @@
     python -m arc_forge_2026_b200.utils.kbench gemm     # dense bf16 GEMMs of the decode step
     python -m arc_forge_2026_b200.utils.kbench gdn_scan # chunked-GDN inter-chunk scan at the QAD shape
     python -m arc_forge_2026_b200.utils.kbench gdn_train # chunked-GDN layer forward + backward at the QAD shape
+    python -m arc_forge_2026_b200.utils.kbench qsa      # QSA selection + sparse verify attention (block 4 and 64)
 
 Prints one JSON line per kernel: time, bytes, FLOPs and the fraction of MEASURED_PEAKS.json.
 """
@@ -204,6 +205,59 @@ def bench_attn(S=128, T=5, seed=0):
     return res
 
 
+def bench_qsa(S=110, ctx=32100, W=8, block=4, K=512, Hq=24, Hkv=2, D=256, seed=0):
+    """QSA verify step of one full-attention layer: selection (scores over every complete block of each verify row,
+    top-K, the per-session union) and the block-sparse attention over the union. Defaults: the reference model's
+    QSA (4-token blocks, top-512, 24Q/2KV x 256) at BASELINE config 5's 110 sessions x 64k context; ``block=64,
+    K=32, Hq=16`` is config 5's own shape. Bytes: pooled keys read by the selection; K + V of the union's tokens.
+    The reference publishes 149.4 us for its grouped indexer logits alone at B=110, ctx 32,100, 8 rows
+    (``runtime/patches/sglang-0.5.20/README.md:177-184``); ``qsa_select`` here is scores + top-K + union."""
+    from ..models.reference import rope_cos_sin
+    from ..ops.qsa import PAGE, QsaWorkspace, qsa_attention
+    peaks = load_peaks()
+    dev = "cuda"
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.full((S,), ctx + W, dtype=torch.int64)
+    maxp = (ctx + W + PAGE - 1) // PAGE
+    P = S * maxp
+    bt = torch.randperm(P, generator=g).view(S, maxp).int().to(dev)
+    kc = torch.randn(P, Hkv, PAGE, D, device=dev).bfloat16()
+    vc = torch.randn(P, Hkv, PAGE, D, device=dev).bfloat16()
+    raw = torch.randn(P * PAGE, 128, device=dev).bfloat16()
+    ws = QsaWorkspace(S, W, K, maxp, 4, dev, block=block)
+    keys = torch.randn(S * ws.max_blocks, 128, device=dev).bfloat16()
+    kn = torch.zeros(128, dtype=torch.bfloat16, device=dev)
+    cos, sin = (t.contiguous().to(dev) for t in rope_cos_sin(torch.arange(ctx + 2 * W + 64), 64, 1.0e7))
+    ws.idx_q.copy_(torch.randn(S * W, 4, 128, device=dev).bfloat16())
+    q = torch.randn(S * W, Hq, D, device=dev).bfloat16()
+    out = torch.empty_like(q)
+    seq_lens = lens.int().to(dev)
+    fin = (seq_lens - W) // block
+    c = __import__("arc_forge_2026_b200.ops._ext", fromlist=["C"]).C()
+
+    def select():
+        c.qsa_select(ws.idx_q, keys, raw, kn, bt, fin, seq_lens, W, K, 4, block, ws.sel, cos, sin, 64, 1e-6,
+                     ws.u_page, ws.u_lpage, ws.u_mask, ws.u_count, None, ws.scores)
+
+    def full():
+        qsa_attention(q, kc, vc, bt, seq_lens, fin, keys, ws, out, splits=4, raw=raw, k_norm=kn, rope=(cos, sin))
+
+    ms_sel = time_cuda(select, flush_bytes=256 << 20)
+    ms_all = time_cuda(full, flush_bytes=256 << 20)
+    torch.cuda.synchronize()
+    union_tokens = int(ws.u_count.sum()) * block
+    sel_bytes = S * (ctx // block) * 128 * 2
+    att_bytes = union_tokens * Hkv * D * 2 * 2
+    ms_att = max(ms_all - ms_sel, 1e-6)
+    tag = f"block {block} top-{K}"
+    return [{"kernel": f"qsa_select ({tag})", "S": S, "ctx": ctx, "W": W, "ms": round(ms_sel, 4),
+             "key_bytes": sel_bytes, "frac_hbm_of_measured": round(sel_bytes / ms_sel / 1e6 / peaks["hbm_gbs"], 3)},
+            {"kernel": f"qsa_sparse_attention ({tag}, {Hq}Q/{Hkv}KV x {D})", "S": S, "ctx": ctx, "W": W,
+             "ms": round(ms_att, 4), "union_tokens_per_session": round(union_tokens / S, 1), "kv_bytes": att_bytes,
+             "frac_hbm_of_measured": round(att_bytes / ms_att / 1e6 / peaks["hbm_gbs"], 3)},
+            {"kernel": f"qsa_layer_total ({tag})", "ms": round(ms_all, 4)}]
+
+
 def bench_grouped(E=320, T=16384, k=10, H=2048, I=512, seed=0):
     """Grouped expert GEMMs of one QAD layer (w13: K=H, N=2I; w2: K=I, N=H; routed rows T*k): the native grouped
     tcgen05 GEMM (forward, dX, dW) against torch._grouped_mm."""
@@ -318,7 +372,7 @@ def bench_gdn_train(B=1, T=16384, Hk=16, Hv=32):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "gdn_scan", "gdn_train", "grouped", "ple", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "qsa", "gdn_scan", "gdn_train", "grouped", "ple", "all"])
     ap.add_argument("--T", type=int, default=640)
     ap.add_argument("--S", type=int, default=128, help="sessions of the attn case")
     ap.add_argument("--seq", type=int, default=16384, help="sequence length of the gdn_scan / gdn_train cases")
@@ -332,6 +386,10 @@ def main():
         res += bench_gdn()
     if a.what in ("attn", "all"):
         res += bench_attn(S=a.S)
+    if a.what in ("qsa", "all"):
+        res += bench_qsa(ctx=32100, W=8)                      # the reference's published shape (B=110, S=8)
+        res += bench_qsa(ctx=65536, W=5)                      # config 5 sessions and context, the model's blocks
+        res += bench_qsa(ctx=65536, W=5, block=64, K=32, Hq=16)  # config 5 as specified
     if a.what in ("gdn_scan", "all"):
         res += bench_gdn_scan(n=(a.seq + 63) // 64)
     if a.what in ("ple", "all"):

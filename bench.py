@@ -155,6 +155,16 @@ def main():
     ap.add_argument("--global-batch", dest="global_batch", type=int, default=32, help="qad: sequences per step")
     ap.add_argument("--topk", type=int, default=64, help="qad: teacher top-k")
     ap.add_argument("--census", action="store_true", help="print the kernel-time shares of one step (stderr)")
+    ap.add_argument("--model", default="qwen3next_80b", choices=["qwen3next_80b", "qwen38fn"],
+                    help="serve / qsa: the served model. qwen38fn: the reference's own shape (HC4, PLE at layer 2, "
+                         "hidden 2560, 24Q/2KV x 256, QSA top-512 of 4-token blocks), the like-for-like anchor "
+                         "against its published ~41 ms per cycle")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="routed experts (default: 320 for both models, the gEAN-pruned count)")
+    ap.add_argument("--qsa-block", dest="qsa_block", type=int, default=64,
+                    help="qsa: tokens per block (64: BASELINE config 5; 4: the reference model's own QSA)")
+    ap.add_argument("--qsa-topk", dest="qsa_topk", type=int, default=None,
+                    help="qsa: blocks kept per query (default 2048 tokens / block: 32 at block 64, 512 at block 4)")
     ap.add_argument("--hisparse", action="store_true", help="qsa: KV history in pinned host memory (HiSparse)")
     ap.add_argument("--hisparse-fp8", dest="hisparse_fp8", action="store_true",
                     help="qsa: host pool in e4m3 with per-(page, head) scales")
@@ -165,12 +175,15 @@ def main():
     if args.mode == "qad":
         return qad_main(args)
     qsa = args.mode == "qsa"
-    for k, serve_v, qsa_v in (("sessions", 128, 110), ("min_ctx", 4096, 65536), ("max_ctx", 24576, 65536),
-                              ("out_tokens", 2048, 4096)):
+    anchor = args.model == "qwen38fn"
+    for k, serve_v, qsa_v in (("sessions", 64 if anchor else 128, 110), ("min_ctx", 4096, 65536),
+                              ("max_ctx", 24576, 65536), ("out_tokens", 2048, 4096)):
         if getattr(args, k) is None:
             setattr(args, k, qsa_v if qsa else serve_v)
     if args.warmup < 3:
         args.warmup = 3
+    if args.qsa_topk is None:
+        args.qsa_topk = 2048 // args.qsa_block
 
     import torch
     import torch.distributed as dist
@@ -190,7 +203,11 @@ def main():
     from arc_forge_2026_b200.serve.engine import SpecEngine
 
     dev = torch.device("cuda", local)
-    cfg = preset("qwen3next_80b", num_layers=args.layers, **(dict(qsa_block=64, qsa_topk=32) if qsa else {}))
+    if anchor:  # the model's own QSA (top-512 of 4-token blocks) in every mode
+        cfg = preset("qwen38fn", num_layers=args.layers, num_experts=args.experts or 320)
+    else:
+        cfg = preset("qwen3next_80b", num_layers=args.layers, num_experts=args.experts or 320,
+                     **(dict(qsa_block=args.qsa_block, qsa_topk=args.qsa_topk) if qsa else {}))
     S_total = args.sessions
     # contexts of all sessions drawn once, dealt to ranks in snake order of decreasing length (equal counts,
     # near-equal KV per rank: the placement a serving scheduler makes so no rank gates the per-layer exchanges)
@@ -253,7 +270,7 @@ def main():
             for raw, key in eng.qsa.cache:
                 raw.normal_(0, 1.0)
                 key.normal_(0, 1.0)
-            eng.qsa.fin.copy_((ctx // PAGE).int().to(dev))
+            eng.qsa.fin.copy_((ctx // cfg.qsa_block).int().to(dev))
     torch.cuda.synchronize()
     eng.capture()
     check_status()
@@ -275,7 +292,7 @@ def main():
         if i == 0 or g != (i - 1) * G // n:
             eng.ctx_len.copy_(ctx_dev + offsets[g])
             if eng.qsa is not None:
-                eng.qsa.fin.copy_((ctx_dev + offsets[g]) // PAGE)
+                eng.qsa.fin.copy_((ctx_dev + offsets[g]) // cfg.qsa_block)
 
     # ---------------- device-timed: K graph replays
     for _ in range(args.warmup):
@@ -355,19 +372,27 @@ def main():
         "vs_baseline": None, "baseline_note": SERVE_BASELINE_NOTE, "dtype": "bf16",
         "data": f"synthetic (random-init weights; random tokens; contexts U[{args.min_ctx},{args.max_ctx}] as random "
                 f"KV/GDN/indexer state)",
-        "config": {"model": "qwen3next_80b-shaped hybrid MoE, 48L, 320 experts top-10 INT3 g128 + shared; "
-                            "8-layer DFlash drafter", "global_batch": S_total, "seq_len": f"U[{args.min_ctx},"
+        "config": {"model": (f"qwen38fn (reference shape: HC4, PLE layer 2, hidden 2560, 24Q/2KV x 256, GDN 16/48 "
+                             f"heads), {args.layers}L, {cfg.num_experts} experts x 640 top-10 INT3 g128 + shared, "
+                             f"QSA top-{cfg.qsa_topk} of {cfg.qsa_block}-token blocks; 8-layer DFlash drafter")
+                            if anchor else
+                            (f"qwen3next_80b-shaped hybrid MoE, {args.layers}L, {cfg.num_experts} experts top-10 INT3 "
+                             f"g128 + shared; 8-layer DFlash drafter"),
+                   "global_batch": S_total, "seq_len": f"U[{args.min_ctx},"
                             f"{args.max_ctx}] context + decode",
                    "parallelism": f"dp{world}-attn+ep{world}" if world > 1 else "dp1",
                    "placement": "sessions dealt to ranks in snake order of context length" if world > 1 else None,
                    "spec_k": K, "acceptance": "seeded Bernoulli(0.7) per position", "layers": args.layers,
-                   "attention": "QSA top-32 of 64-token blocks (+ local pages)" if qsa else "dense",
+                   "attention": (f"QSA top-{cfg.qsa_topk} of {cfg.qsa_block}-token blocks (+ each row's own incomplete "
+                                  f"block)") if qsa else "dense",
                    "kv_offload": ("HiSparse host pool " + ("e4m3" if args.hisparse_fp8 else "bf16"))
                    if scfg.hisparse else "none (all KV on the GPU)",
                    "l2": "inputs larger than L2 (weights 24 GB, KV > 40 GB streamed every cycle)",
                    "decode_span": f"timed cycles in {G} groups at context + {offsets} of {args.out_tokens} output "
                                   f"tokens"},
         "p50_tpot_ms": round(p50, 3) if p50 else None,
+        "cycle_ms": round(ms / args.steps, 3),
+        "reference_cycle_ms": 41.0 if anchor else None,  # paper App. E.11 (p. 85): ~41 ms per cycle on one B200
         "accepted_per_cycle": round(emitted / (args.steps * S_total), 3),
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": n_ours * args.steps,

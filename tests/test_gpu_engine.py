@@ -1,8 +1,10 @@
 """End-to-end GPU tests of the hybrid model and the speculative engine (tiny shape)."""
+import dataclasses
+
 import pytest
 import torch
 
-from arc_forge_2026_b200.config import ServeConfig, drafter_preset, preset
+from arc_forge_2026_b200.config import FULL, ServeConfig, drafter_preset, preset
 from arc_forge_2026_b200.models.drafter import Drafter
 from arc_forge_2026_b200.models.hybrid import HybridModel
 from arc_forge_2026_b200.models.reference import build_reference
@@ -14,8 +16,8 @@ pytestmark = pytest.mark.gpu
 dev = "cuda"
 
 
-def _models(seed=0, **over):
-    cfg = preset("tiny_gpu", **over)
+def _models(seed=0, name="tiny_gpu", **over):
+    cfg = preset(name, **over)
     ref = build_reference(cfg, seed=seed)
     with torch.no_grad():
         ref.lm_head.weight.mul_(40.0)  # peaky logits: argmax far from ties
@@ -62,6 +64,74 @@ def test_spec_greedy_equals_plain_greedy():
     # reference greedy decode of the first prompt agrees with the engine on the leading tokens
     toks, _ = ref.greedy_decode(torch.tensor([prompts[0]]), 8)
     assert toks[0].tolist()[:4] == out_plain[0][:4]
+
+
+@pytest.mark.parametrize("spec_k", [0, 4])
+def test_qwen38fn_qsa_decode_matches_reference(spec_k):
+    """The reference model's own shape (24Q/2KV x 256 attention, 16/48-head GDN, 4 hyper-connection branches, PLE at
+    layer 2, QSA over 4-token blocks) at reduced width, depth and n-gram table, top-16 blocks so decoding runs past the dense range (64
+    tokens). Teacher-forced against the fp32 reference with its QSA selection: every token the engine emits (plain
+    decode, or speculative verify of 5 rows) is the reference's argmax up to a near-tie, and the engine's QSA prefill
+    of the whole sequence gives the reference's logits."""
+    cfg, ref, model = _models(4, "qwen38fn", num_layers=4, hidden_size=512, vocab_size=4096, num_experts=16,
+                              qsa_topk=16, ngram_vocab_size_base=4096, ple_embed_dim=512)
+    assert cfg.qsa_block == 4 and cfg.hc_count == 4
+    g = torch.Generator().manual_seed(4)
+    prompt = torch.randint(0, cfg.vocab_size, (50,), generator=g).tolist()
+    drafter = (Drafter(drafter_preset("tiny"), cfg.hidden_size, cfg.vocab_size, dev, draft_vocab=4096)
+               if spec_k else None)
+    eng = SpecEngine(model, drafter, ServeConfig(spec_k=spec_k, accept_mode="greedy"), 2, 1024)
+    assert eng.qsa is not None and eng.qsa.ws.block == 4
+    out = eng.generate([prompt], 60)[0]
+    torch.cuda.synchronize()
+    check_status()
+    seq = prompt + out
+    with torch.no_grad():
+        ref_logits = ref(torch.tensor([seq]))[0].float()
+        dense_cfg = dataclasses.replace(cfg, qsa_topk=1 << 20)  # same weights, every block kept
+        for lay in ref.layers:
+            if lay.kind == FULL:
+                lay.mixer.cfg = dense_cfg
+        dense_logits = ref(torch.tensor([seq]))[0].float()
+    L = len(prompt)
+    # decode: each emitted token is the reference's best up to a near-tie (a few flips of near-tied block scores
+    # between the bf16 engine and the fp32 reference are expected: a bf16 copy of the reference shows them too)
+    far = [i for i, t in enumerate(out)
+           if float(ref_logits[L - 1 + i].max() - ref_logits[L - 1 + i][t]) >
+           0.03 * float(ref_logits[L - 1 + i].max() - ref_logits[L - 1 + i].median())]
+    assert len(far) <= len(out) // 10, far
+    # prefill of the whole sequence through the engine (QSA row sets past 64 tokens) against both references:
+    # close to the QSA one (bf16-level error), far from the dense one past the dense range
+    rows = []
+    eng.score(seq, lambda h, s: rows.append(model.logits(h, fp32=True).float().cpu()))
+    torch.cuda.synchronize()
+    check_status()
+    got = torch.cat(rows)[:len(seq)]
+
+    def rel(x, y):
+        return (x - y).norm(dim=-1) / y.norm(dim=-1)
+    e_qsa, e_dense = rel(got, ref_logits), rel(got, dense_logits)
+    # (the engine's own bf16 / INT3 error is ~4 % already in the dense range; a flipped near-tie adds an outlier)
+    assert e_qsa.median() < 0.06 and e_qsa[70:].median() < 0.06, e_qsa
+    assert e_qsa[70:].median() < 0.4 * e_dense[70:].median(), (e_qsa[70:], e_dense[70:])
+    assert (got.argmax(-1) == ref_logits.argmax(-1)).float().mean() > 0.85
+
+
+def test_qwen38fn_full_width_constructs_and_decodes():
+    """preset('qwen38fn') at full width (hidden 2560, 512 experts x 640 INT3, vocab 248,320, the full n-gram table
+    of the PLE layer in e4m3, top-512 of 4-token blocks), 4 of its 48 layers: random init on the GPU, prefill (one
+    prompt past the 2,048-token dense range) and speculative decode through the engine."""
+    cfg = preset("qwen38fn", num_layers=4)
+    model = HybridModel.random(cfg, dev, seed=5)
+    drafter = Drafter(drafter_preset("tiny"), cfg.hidden_size, cfg.vocab_size, dev, draft_vocab=4096)
+    eng = SpecEngine(model, drafter, ServeConfig(spec_k=4, accept_mode="greedy"), 2, 4096)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (300, 2100)]
+    out = eng.generate(prompts, 16)
+    torch.cuda.synchronize()
+    check_status()
+    assert [len(o) for o in out] == [16, 16]
+    assert all(0 <= t < cfg.vocab_size for o in out for t in o)
 
 
 def test_bernoulli_acceptance_and_graph_replay():
