@@ -224,6 +224,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
+// The encoder validates the address against the calling thread's current context. A thread that has made no CUDA
+// runtime call yet (PyTorch's autograd device thread, when a backward starts with a native op) has none: a runtime
+// call makes the device's primary context current.
+static bool ensure_context() {
+  int dev = 0;
+  return cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess && cudaFree(nullptr) == cudaSuccess;
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype_bytes, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle128) {
   auto encode = get_encode();
@@ -235,9 +243,13 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype_bytes, uint64_t i
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  auto run = [&] {
+    return encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = run();
+  if (r == CUDA_ERROR_INVALID_CONTEXT && ensure_context()) r = run();
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
@@ -249,9 +261,13 @@ int make_tmap_3d_bf16(CUtensorMap* map, const void* base, const uint64_t dims[3]
   cuuint64_t str[2] = {strides_bytes[0], strides_bytes[1]};
   cuuint32_t bx[3] = {box[0], box[1], box[2]};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, str, bx, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  auto run = [&] {
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, str, bx, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = run();
+  if (r == CUDA_ERROR_INVALID_CONTEXT && ensure_context()) r = run();
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 

@@ -252,6 +252,27 @@ int hc_norm_bwd(const void* h, const float* w, const float* rstd, const float* d
   }
   return (int)cudaGetLastError();
 }
+// Serving read-side activations of the down / inject projection du [rows, ld] (bf16): s = silu(du[:, :R] / 4) and
+// gate = 2 sigmoid(du[:, R:R+G] / 4), both bf16 (one launch instead of the elementwise chain).
+__global__ void __launch_bounds__(256) hc_act_kernel(const bf16* __restrict__ du, int ld, int64_t rows, int R, int G,
+                                                     bf16* __restrict__ s, bf16* __restrict__ gate) {
+  const int per = R + (gate ? G : 0);
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * per) return;
+  const int64_t r = i / per;
+  const int c = (int)(i % per);
+  const float z = __bfloat162float(du[r * ld + c]) * 0.25f;
+  if (c < R) s[r * R + c] = __float2bfloat16(z / (1.f + __expf(-z)));
+  else gate[r * G + (c - R)] = __float2bfloat16(2.f / (1.f + __expf(-z)));
+}
+int hc_act_fwd(const void* du, int ld, int64_t rows, int R, int G, void* s, void* gate, cudaStream_t st) {
+  if (rows < 1) return 0;
+  if (R < 1 || G < 0 || ld < R + (gate ? G : 0)) return 3;
+  const int64_t n = rows * (R + (gate ? G : 0));
+  hc_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const bf16*)du, ld, rows, R, G, (bf16*)s, (bf16*)gate);
+  return (int)cudaGetLastError();
+}
+
 int hc_mix_fwd(const void* pre, const void* zb, void* x, int64_t rows, int G, int H, cudaStream_t st) {
   if (rows < 1) return 0;
   if (H % 8 || G < 1 || G > MAXG) return 3;

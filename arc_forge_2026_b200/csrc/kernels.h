@@ -68,6 +68,30 @@ struct AttnArgs {
 };
 int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st);
 
+// attention_train.cu: variable-length causal attention of packed training rows, forward and backward (tcgen05)
+struct AttnTrainArgs {
+  const __nv_bfloat16* q = nullptr;     // [T, Hq, D] (normed, rotated)
+  const __nv_bfloat16* k = nullptr;     // [T, Hkv, D]
+  const __nv_bfloat16* v = nullptr;     // [T, Hkv, D]
+  const int* cu = nullptr;              // [segments + 1] row offsets
+  const int2* tiles = nullptr;          // [ntiles] (segment, first position of a 64-position tile)
+  int ntiles = 0;
+  int T = 0, Hq = 0, Hkv = 0, D = 0;
+  float scale = 0.f, scale_log2 = 0.f;  // softmax scale, and times log2(e)
+  __nv_bfloat16* out = nullptr;         // forward: written; backward: read
+  float* lse = nullptr;                 // [Hq, T] row log-sum-exp of the scaled scores, log2 domain
+  const __nv_bfloat16* dout = nullptr;  // backward
+  const float* delta = nullptr;         // [Hq, T] backward scratch: rowsum(dO * O)
+  __nv_bfloat16* dq = nullptr;          // [T, Hq, D]
+  __nv_bfloat16* dk = nullptr;          // [T, Hkv, D]
+  __nv_bfloat16* dv = nullptr;
+  float* dk_part = nullptr;             // [T, Hq, D] backward scratch: each query head's fp32 contribution
+  float* dv_part = nullptr;
+};
+int attn_train_fwd(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st);
+// kv_tiles: the same tiles ordered for the dK / dV pass (most work first)
+int attn_train_bwd(const AttnTrainArgs& a, const int2* kv_tiles, uint32_t* status, cudaStream_t st);
+
 // qsa.cu: QSA indexer, block selection and union for block-sparse verify attention (block = `block` tokens, a
 // divisor of the 64-token page: 64 makes a block one page)
 constexpr int QSA_MAX_LAYERS = 64;
@@ -340,6 +364,7 @@ int hc_norm_fwd(const void* h, const float* w, void* zb, float* rstd, int64_t ro
 int hc_norm_bwd(const void* h, const float* w, const float* rstd, const float* dzb, void* dh, int64_t rows, int G,
                 int H, cudaStream_t st);
 int hc_mix_fwd(const void* pre, const void* zb, void* x, int64_t rows, int G, int H, cudaStream_t st);
+int hc_act_fwd(const void* du, int ld, int64_t rows, int R, int G, void* s, void* gate, cudaStream_t st);
 int hc_mix_bwd(const void* pre, const void* zb, const void* dx, void* dpre, float* dzb, int64_t rows, int G, int H,
                cudaStream_t st);
 int hc_inject_fwd(const void* h, const void* y, const void* gate, void* out, int64_t rows, int G, int H,

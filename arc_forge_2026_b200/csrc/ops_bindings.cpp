@@ -393,6 +393,78 @@ void paged_attention_op(const at::Tensor& q, const at::Tensor& kcache, const at:
   check_rc(afb::paged_attention(a, (int)splits, status_ptr(q.get_device()), stream()), "paged_attention");
 }
 
+// Training attention (attention_train.cu). tiles: int32 [n, 2] (segment, first position) on the device.
+static afb::AttnTrainArgs train_attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                          const at::Tensor& cu, const at::Tensor& tiles, double scale) {
+  for (const at::Tensor* t : {&q, &k, &v}) {
+    AFB_CHECK_DT((*t), at::kBFloat16);
+    AFB_CHECK_CONTIG((*t));
+    TORCH_CHECK(t->dim() == 3, "q / k / v are [T, heads, D]");
+  }
+  AFB_CHECK_DT(cu, at::kInt);
+  AFB_CHECK_DT(tiles, at::kInt);
+  AFB_CHECK_CONTIG(tiles);
+  TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 2, "tiles is [n, 2]");
+  TORCH_CHECK(k.sizes() == v.sizes() && k.size(0) == q.size(0) && k.size(2) == q.size(2), "k / v shapes");
+  afb::AttnTrainArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.cu = ptr<int>(cu);
+  a.tiles = reinterpret_cast<const int2*>(tiles.data_ptr());
+  a.ntiles = tiles.size(0);
+  a.T = q.size(0);
+  a.Hq = q.size(1);
+  a.Hkv = k.size(1);
+  a.D = q.size(2);
+  a.scale = (float)scale;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  return a;
+}
+
+void attn_train_fwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
+                       const at::Tensor& tiles, double scale, at::Tensor& out, at::Tensor& lse) {
+  afb::AttnTrainArgs a = train_attn_args(q, k, v, cu, tiles, scale);
+  AFB_CHECK_CONTIG(out);
+  TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16, "out is bf16 like q");
+  AFB_CHECK_DT(lse, at::kFloat);
+  TORCH_CHECK(lse.numel() == (int64_t)a.Hq * a.T, "lse is [Hq, T]");
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.lse = ptr<float>(lse);
+  check_rc(afb::attn_train_fwd(a, status_ptr(q.get_device()), stream()), "attn_train_fwd");
+}
+
+void attn_train_bwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
+                       const at::Tensor& tiles, const at::Tensor& kv_tiles, double scale, const at::Tensor& out,
+                       const at::Tensor& lse, const at::Tensor& dout, at::Tensor& delta, at::Tensor& dq,
+                       at::Tensor& dk, at::Tensor& dv, at::Tensor& dk_part, at::Tensor& dv_part) {
+  afb::AttnTrainArgs a = train_attn_args(q, k, v, cu, tiles, scale);
+  AFB_CHECK_CONTIG(dout);
+  AFB_CHECK_CONTIG(out);
+  TORCH_CHECK(dout.sizes() == q.sizes() && out.sizes() == q.sizes(), "out / dout shapes");
+  TORCH_CHECK(dq.sizes() == q.sizes() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(), "gradient shapes");
+  AFB_CHECK_CONTIG(dq);
+  AFB_CHECK_CONTIG(dk);
+  AFB_CHECK_CONTIG(dv);
+  TORCH_CHECK(kv_tiles.sizes() == tiles.sizes(), "kv_tiles is the tile list in another order");
+  TORCH_CHECK(delta.numel() == (int64_t)a.Hq * a.T && lse.numel() == delta.numel(), "lse / delta are [Hq, T]");
+  a.out = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(out.data_ptr()));
+  a.lse = const_cast<float*>(ptr<float>(lse));
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.delta = ptr<float>(delta);
+  a.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  AFB_CHECK_DT(dk_part, at::kFloat);
+  AFB_CHECK_DT(dv_part, at::kFloat);
+  TORCH_CHECK(dk_part.numel() == q.numel() && dv_part.numel() == q.numel(), "dk_part / dv_part are fp32 [T, Hq, D]");
+  a.dk_part = ptr<float>(dk_part);
+  a.dv_part = ptr<float>(dv_part);
+  check_rc(afb::attn_train_bwd(a, reinterpret_cast<const int2*>(kv_tiles.data_ptr()), status_ptr(q.get_device()),
+                               stream()),
+           "attn_train_bwd");
+}
+
 // QSA (see qsa.cu). proj: projection rows whose columns [idx_off, idx_off + (Hi + 1) * 128) hold the index
 // query heads then the raw index key.
 void qsa_prep_op(const at::Tensor& proj, int64_t idx_off, const at::Tensor& positions, const at::Tensor& slots,
@@ -1142,6 +1214,19 @@ void hc_mix_op(const at::Tensor& pre, const at::Tensor& zb, at::Tensor& x, c10::
     check_rc(afb::hc_mix_fwd(pre.data_ptr(), zb.data_ptr(), x.data_ptr(), rows, G, H, stream()), "hc_mix_fwd");
   }
 }
+void hc_act_op(const at::Tensor& du, int64_t R, int64_t G, at::Tensor& s, c10::optional<at::Tensor> gate) {
+  AFB_CHECK_DT(du, at::kBFloat16);
+  TORCH_CHECK(du.dim() == 2 && du.stride(1) == 1, "hc_act: du rows with unit column stride");
+  AFB_CHECK_CONTIG(s);
+  TORCH_CHECK(s.numel() == du.size(0) * R, "hc_act: s is [rows, R]");
+  if (gate.has_value()) {
+    AFB_CHECK_CONTIG(gate.value());
+    TORCH_CHECK(gate->numel() == du.size(0) * G, "hc_act: gate is [rows, G]");
+  }
+  check_rc(afb::hc_act_fwd(du.data_ptr(), du.stride(0), du.size(0), R, G, s.data_ptr(),
+                           gate.has_value() ? gate->data_ptr() : nullptr, stream()),
+           "hc_act");
+}
 void hc_inject_op(const at::Tensor& h, const at::Tensor& y, const at::Tensor& gate, at::Tensor& out,
                   c10::optional<at::Tensor> dout, c10::optional<at::Tensor> dy, c10::optional<at::Tensor> dgate) {
   int64_t rows;
@@ -1332,6 +1417,7 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("lora_tgrad", &lora_tgrad_op);
   m.def("hc_norm", &hc_norm_op);
   m.def("hc_mix", &hc_mix_op);
+  m.def("hc_act", &hc_act_op);
   m.def("hc_inject", &hc_inject_op);
   m.def("conv_silu", &conv_silu_op, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("dy"), py::arg("dx"),
         py::arg("pos") = py::none());
@@ -1352,6 +1438,8 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none(), py::arg("kscale") = py::none(),
         py::arg("vscale") = py::none(), py::arg("impl") = 0, py::arg("sp_block") = 64, py::arg("sp_slot") = py::none());
   m.def("qsa_prep", &qsa_prep_op);
+  m.def("attn_train_fwd", &attn_train_fwd_op);
+  m.def("attn_train_bwd", &attn_train_bwd_op);
   py::class_<GuardCtx>(m, "GuardCtx")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, const at::Tensor&,
                     const at::Tensor&>())

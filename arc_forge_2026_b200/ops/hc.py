@@ -22,7 +22,6 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
 
 from . import C
 
@@ -74,11 +73,12 @@ def hc_read(h: torch.Tensor, w: HCWeights, G: int) -> tuple[torch.Tensor, torch.
     rstd = torch.empty(N, G, dtype=torch.float32, device=h.device)
     c.hc_norm(h, w.norm_w, w.eps, zb, rstd, None, None)
     du = c.gemm(zb.view(N, G * H), w.wcat)
-    s = F.silu(du[:, :w.rank].float() * 0.25).to(_BF)
+    s = torch.empty(N, w.rank, dtype=_BF, device=h.device)
+    gate = torch.empty(N, G, dtype=_BF, device=h.device) if w.inject else None
+    c.hc_act(du, w.rank, G, s, gate)  # s = silu(du_down / 4), gate = 2 sigmoid(du_inject / 4)
     pre = c.gemm(s, w.w_up)
     x = torch.empty(N, H, dtype=_BF, device=h.device)
     c.hc_mix(pre, zb, x, None, None, None)
-    gate = (2.0 * torch.sigmoid(du[:, w.rank:w.rank + G].float() * 0.25)).to(_BF) if w.inject else None
     return x, gate
 
 

@@ -21,7 +21,7 @@ import threading
 
 NAMES = ("gdn_chunk", "conv_silu", "rms_norm", "gated_rms_norm", "swiglu", "moe_combine", "moe_dispatch",
          "int3_weight", "fp8_weight", "topk_tail_kl", "hc", "ple", "lora_grad",
-         "grouped_gemm")
+         "grouped_gemm", "attention")
 
 # opt-in kernels: correct and tested, but slower than the path they replace at the QAD shapes (measured), so "all"
 # leaves them off; name them explicitly to run them

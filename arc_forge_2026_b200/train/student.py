@@ -74,8 +74,16 @@ class _Dispatch(torch.autograd.Function):
 
 def packed_attention(q, k, v, cu_seqlens, max_seqlen: int):
     """Causal attention inside each segment of a packed row: q [T, Hq, D], k / v [T, Hkv, D] -> [T, Hq, D].
-    CUDA: the variable-length flash-attention kernel (library) with its deterministic backward (the gradients stay
-    bitwise reproducible); otherwise one SDPA call per segment."""
+    CUDA: the native tcgen05 varlen kernels (``train/attention.py``: forward, dQ, dK / dV, deterministic), or with
+    that fast kernel disabled the library flash-attention varlen kernel with its deterministic backward; otherwise
+    one SDPA call per segment."""
+    from . import kernels
+    if q.is_cuda and q.dtype == torch.bfloat16 and q.shape[-1] in (128, 256):
+        native = kernels.use("attention")
+        kernels.hit("attention", native)
+        if native:
+            from .attention import varlen_attention
+            return varlen_attention(q, k, v, cu_seqlens)
     if q.is_cuda:
         try:
             from flash_attn import flash_attn_varlen_func

@@ -258,6 +258,43 @@ def bench_qsa(S=110, ctx=32100, W=8, block=4, K=512, Hq=24, Hkv=2, D=256, seed=0
             {"kernel": f"qsa_layer_total ({tag})", "ms": round(ms_all, 4)}]
 
 
+def bench_train_attn(T=16384, segs=(16384,), Hq=16, Hkv=2, D=256, seed=0):
+    """Training attention of one packed row (QAD shape: 16Q/2KV x 256, 16k tokens): the native tcgen05 forward and
+    backward (``train/attention.py``) beside the library flash-attention varlen kernels on the same inputs.
+    FLOPs: causal 2 x 2 x sum(L^2 / 2) x Hq x D forward, 2.5x that backward."""
+    from ..train.attention import varlen_attention
+    peaks = load_peaks()
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    cu = torch.tensor([0] + list(torch.tensor(segs).cumsum(0)), dtype=torch.int32)
+    q = torch.randn(T, Hq, D, device="cuda", generator=g).bfloat16().requires_grad_()
+    k = torch.randn(T, Hkv, D, device="cuda", generator=g).bfloat16().requires_grad_()
+    v = torch.randn(T, Hkv, D, device="cuda", generator=g).bfloat16().requires_grad_()
+    do = torch.randn(T, Hq, D, device="cuda", generator=g).bfloat16()
+    flops_f = sum(2 * 2 * L * L / 2 * Hq * D for L in segs)
+    res = []
+    arms = [("native tcgen05", lambda: varlen_attention(q, k, v, cu))]
+    try:
+        from flash_attn import flash_attn_varlen_func
+        cud = cu.cuda()
+        arms.append(("flash_attn varlen (library)", lambda: flash_attn_varlen_func(
+            q, k, v, cud, cud, max(segs), max(segs), causal=True, deterministic=True)))
+    except ImportError:
+        pass
+    for name, fn in arms:
+        ms_f = time_cuda(lambda: fn(), flush_bytes=1 << 20)
+        out = fn()
+        ms_fb = time_cuda(lambda: torch.autograd.grad(fn(), (q, k, v), do), flush_bytes=1 << 20)
+        ms_b = ms_fb - ms_f
+        res.append({"kernel": f"train attention fwd ({name})", "T": T, "segments": len(segs), "ms": round(ms_f, 3),
+                    "tflops": round(flops_f / ms_f / 1e9, 1),
+                    "frac_bf16_of_measured": round(flops_f / ms_f / 1e9 / peaks["bf16_tflops"], 3)})
+        res.append({"kernel": f"train attention bwd ({name})", "T": T, "ms": round(ms_b, 3),
+                    "tflops": round(2.5 * flops_f / ms_b / 1e9, 1),
+                    "frac_bf16_of_measured": round(2.5 * flops_f / ms_b / 1e9 / peaks["bf16_tflops"], 3)})
+        del out
+    return res
+
+
 def bench_grouped(E=320, T=16384, k=10, H=2048, I=512, seed=0):
     """Grouped expert GEMMs of one QAD layer (w13: K=H, N=2I; w2: K=I, N=H; routed rows T*k): the native grouped
     tcgen05 GEMM (forward, dX, dW) against torch._grouped_mm."""
@@ -372,7 +409,7 @@ def bench_gdn_train(B=1, T=16384, Hk=16, Hv=32):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "qsa", "gdn_scan", "gdn_train", "grouped", "ple", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "qsa", "train_attn", "gdn_scan", "gdn_train", "grouped", "ple", "all"])
     ap.add_argument("--T", type=int, default=640)
     ap.add_argument("--S", type=int, default=128, help="sessions of the attn case")
     ap.add_argument("--seq", type=int, default=16384, help="sequence length of the gdn_scan / gdn_train cases")
@@ -390,6 +427,9 @@ def main():
         res += bench_qsa(ctx=32100, W=8)                      # the reference's published shape (B=110, S=8)
         res += bench_qsa(ctx=65536, W=5)                      # config 5 sessions and context, the model's blocks
         res += bench_qsa(ctx=65536, W=5, block=64, K=32, Hq=16)  # config 5 as specified
+    if a.what in ("train_attn", "all"):
+        res += bench_train_attn()
+        res += bench_train_attn(T=16384, segs=(4096,) * 4, Hq=24, Hkv=2)
     if a.what in ("gdn_scan", "all"):
         res += bench_gdn_scan(n=(a.seq + 63) // 64)
     if a.what in ("ple", "all"):

@@ -129,7 +129,7 @@ def count_launches(fn, census_out=None, time_out=None):
             census[e.name[:90]] += 1
             if time_out is not None:
                 time_out[e.name[:90]] += e.device_time_total
-            if any(k in e.name for k in ours):
+            if "afb::" in e.name or any(k in e.name for k in ours):  # every kernel of csrc/ lives in namespace afb
                 n_ours += 1
     if census_out is not None:
         census_out.update(census)
@@ -384,7 +384,7 @@ def main():
                    "placement": "sessions dealt to ranks in snake order of context length" if world > 1 else None,
                    "spec_k": K, "acceptance": "seeded Bernoulli(0.7) per position", "layers": args.layers,
                    "attention": (f"QSA top-{cfg.qsa_topk} of {cfg.qsa_block}-token blocks (+ each row's own incomplete "
-                                  f"block)") if qsa else "dense",
+                                  f"block)") if cfg.qsa_topk else "dense",
                    "kv_offload": ("HiSparse host pool " + ("e4m3" if args.hisparse_fp8 else "bf16"))
                    if scfg.hisparse else "none (all KV on the GPU)",
                    "l2": "inputs larger than L2 (weights 24 GB, KV > 40 GB streamed every cycle)",
