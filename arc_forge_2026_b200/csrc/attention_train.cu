@@ -73,8 +73,8 @@ struct Dkv {
   static constexpr int NS = 2;
   static constexpr uint32_t STAGE = 2 * T_BYTES;  // Q + dO of one unit
   static constexpr uint32_t ST_OFF = 2 * T_BYTES;
-  static constexpr uint32_t ROWS_OFF = ST_OFF + NS * STAGE;       // lse[NS][64], delta[NS][64]
-  static constexpr uint32_t BAR_OFF = ROWS_OFF + NS * 2 * TILE * 4;
+  static constexpr uint32_t ROWS_OFF = ST_OFF + NS * STAGE;       // lse[NS][64], delta[NS][64], qsa field[NS][64]
+  static constexpr uint32_t BAR_OFF = ROWS_OFF + NS * 3 * TILE * 4;
   static constexpr uint32_t TOTAL = BAR_OFF + (2 * NS + 10) * 8 + 16 + 1024;
   static constexpr bool DV = MODE & 1, DK = MODE & 2;
   static constexpr uint32_t DV_COL = 0;
@@ -87,6 +87,19 @@ struct Dkv {
   static_assert(END <= 512, "TMEM columns");
 };
 }  // namespace attn_tr
+
+// QSA: the 64 keys of key tile kt that row `row` may see by its block selection (bit j = key kt * 64 + j); all
+// ones without a map. Blocks of B tokens: the tile's 64 / B blocks are one aligned bit field of one map word.
+AFB_DEV uint64_t qsa_key_mask(const AttnTrainArgs& a, size_t row, int kt) {
+  if (!a.blkmap) return ~0ull;
+  const int B = a.qsa_block, bpt = attn_tr::TILE / B, b0 = kt * bpt;
+  const uint32_t w = a.blkmap[row * a.blk_words + (b0 >> 5)];
+  const uint32_t f = (w >> (b0 & 31)) & (bpt == 32 ? 0xffffffffu : ((1u << bpt) - 1u));
+  uint64_t m = 0;
+  for (int b = 0; b < bpt; ++b)
+    if ((f >> b) & 1u) m |= (B == 64 ? ~0ull : ((1ull << B) - 1ull)) << (b * B);
+  return m;
+}
 
 // ---------------------------------------------------------------------------------------------------- forward
 template <int D>
@@ -233,10 +246,11 @@ __global__ void __launch_bounds__(attn_tr::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
       const int kbase = i * TILE;
+      const uint64_t km = live ? qsa_key_mask(a, (size_t)(s0 + qpos), i) : 0ull;
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < TILE; ++j) {
-        const float x = (live && kbase + j <= qpos) ? sv[j] * a.scale_log2 : -INFINITY;
+        const float x = (live && kbase + j <= qpos && ((km >> j) & 1ull)) ? sv[j] * a.scale_log2 : -INFINITY;
         sv[j] = x;
         mx = fmaxf(mx, x);
       }
@@ -465,6 +479,7 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(sd_empty);
       const int kbase = i * TILE + half * 32;
+      const uint32_t km = live ? (uint32_t)(qsa_key_mask(a, row, i) >> (half * 32)) : 0u;
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -472,7 +487,7 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int jj = 2 * j + e;
-          const float p = (live && kbase + jj <= qpos) ? exp2f(sv[jj] * a.scale_log2 - lse) : 0.f;
+          const float p = (live && kbase + jj <= qpos && ((km >> jj) & 1u)) ? exp2f(sv[jj] * a.scale_log2 - lse) : 0.f;
           d2[e] = p * (dp[jj] - dlt);
         }
         pk[j] = pack_bf16x2(d2[0], d2[1]);
@@ -534,6 +549,7 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_fin + 1);
   float* rows_lse = reinterpret_cast<float*>(smem + L::ROWS_OFF);       // [NS][64]
   float* rows_dlt = rows_lse + NS * TILE;                                // [NS][64]
+  uint32_t* rows_map = reinterpret_cast<uint32_t*>(rows_dlt + NS * TILE);  // [NS][64]: the key tile's block bits
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qh = blockIdx.x, kvh = qh / (a.Hq / a.Hkv);
@@ -591,6 +607,12 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
         const size_t idx = (size_t)h * a.T + s0 + q0 + r;
         rows_lse[s * TILE + r] = in ? a.lse[idx] : 0.f;
         rows_dlt[s * TILE + r] = in ? a.delta[idx] : 0.f;
+        uint32_t f = 0xffffffffu;
+        if (a.blkmap && in) {  // this key tile's 64 / B block bits of the row
+          const int bpt = TILE / a.qsa_block, b0 = (k0 / TILE) * bpt;
+          f = a.blkmap[(size_t)(s0 + q0 + r) * a.blk_words + (b0 >> 5)] >> (b0 & 31);
+        }
+        rows_map[s * TILE + r] = f;
       }
       __syncwarp();
       if (lane == 0) {
@@ -697,6 +719,8 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
       if (lane == 0) mbar_arrive(sx_empty);
       const float* lse = rows_lse + s * TILE + half * 32;
       const float* dlt = rows_dlt + s * TILE + half * 32;
+      const uint32_t* fmap = rows_map + s * TILE + half * 32;
+      const int kblk = kr / a.qsa_block;  // this key's block within the tile
       uint32_t ppk[L::DV ? 16 : 1], dpk[L::DK ? 16 : 1];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -704,7 +728,9 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int c = 2 * j + e, qpos = q0 + c;
-          const float p = (klive && kpos <= qpos && qpos < Lseg) ? exp2f(sv[c] * a.scale_log2 - lse[c]) : 0.f;
+          const bool sel = ((fmap[c] >> kblk) & 1u) != 0u;
+          const float p =
+              (klive && kpos <= qpos && qpos < Lseg && sel) ? exp2f(sv[c] * a.scale_log2 - lse[c]) : 0.f;
           pv[e] = p;
           if (L::DK) dv2[e] = p * (dp[c] - dlt[c]);
         }
@@ -823,7 +849,35 @@ static int qkv_maps(const AttnTrainArgs& a, CUtensorMap* tq, CUtensorMap* tk, CU
 
 static int check_args(const AttnTrainArgs& a) {
   if ((a.D != 128 && a.D != 256) || a.Hkv < 1 || a.Hq % a.Hkv || a.T < 1 || !a.cu || !a.tiles) return 3;
+  if (a.blkmap && (a.qsa_block < 2 || attn_tr::TILE % a.qsa_block || a.blk_words < 1)) return 3;
   return 0;
+}
+
+// QSA row map from the per-set unions: one thread per (set, union entry), OR-ing the entry's block into the bitmap
+// row of every real row its mask names (distinct bits: the result does not depend on the order)
+__global__ void qsa_rowmap_kernel(const int* __restrict__ u_lpage, const uint8_t* __restrict__ u_mask,
+                                  const int* __restrict__ u_count, const int* __restrict__ set_row0,
+                                  const int* __restrict__ set_rows, int S, int W, int ucap, uint32_t* blkmap,
+                                  int words) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)S * ucap) return;
+  const int s = (int)(i / ucap), e = (int)(i % ucap);
+  if (e >= u_count[s]) return;
+  const int b = u_lpage[i];
+  const uint32_t m = u_mask[i];
+  if (b < 0 || (b >> 5) >= words) return;
+  for (int r = 0; r < min(W, set_rows[s]); ++r)
+    if ((m >> r) & 1u) atomicOr(&blkmap[(size_t)(set_row0[s] + r) * words + (b >> 5)], 1u << (b & 31));
+}
+
+int qsa_rowmap(const int* u_lpage, const uint8_t* u_mask, const int* u_count, const int* set_row0,
+               const int* set_rows, int S, int W, int ucap, uint32_t* blkmap, int words, cudaStream_t st) {
+  if (S <= 0) return 0;
+  if (W < 1 || W > 8 || ucap < 1 || words < 1) return 3;
+  const int64_t n = (int64_t)S * ucap;
+  qsa_rowmap_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(u_lpage, u_mask, u_count, set_row0, set_rows, S, W,
+                                                                 ucap, blkmap, words);
+  return (int)cudaGetLastError();
 }
 
 template <int D>

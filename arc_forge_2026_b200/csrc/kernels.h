@@ -87,10 +87,18 @@ struct AttnTrainArgs {
   __nv_bfloat16* dv = nullptr;
   float* dk_part = nullptr;             // [T, Hq, D] backward scratch: each query head's fp32 contribution
   float* dv_part = nullptr;
+  // QSA (optional): per row, bit b of blkmap[row * blk_words + b / 32] = the row attends to block b of its segment
+  // (blocks of qsa_block tokens); keys of unmarked blocks are masked like future keys
+  const uint32_t* blkmap = nullptr;
+  int blk_words = 0, qsa_block = 64;
 };
 int attn_train_fwd(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st);
 // kv_tiles: the same tiles ordered for the dK / dV pass (most work first)
 int attn_train_bwd(const AttnTrainArgs& a, const int2* kv_tiles, uint32_t* status, cudaStream_t st);
+// QSA training selection -> per-row block bitmap: row set s (W rows starting at packed row set_row0[s], the first
+// set_rows[s] of them real) marks block u_lpage[s][e] for each row whose bit is set in u_mask[s][e]
+int qsa_rowmap(const int* u_lpage, const uint8_t* u_mask, const int* u_count, const int* set_row0,
+               const int* set_rows, int S, int W, int ucap, uint32_t* blkmap, int words, cudaStream_t st);
 
 // qsa.cu: QSA indexer, block selection and union for block-sparse verify attention (block = `block` tokens, a
 // divisor of the 64-token page: 64 makes a block one page)

@@ -422,9 +422,22 @@ static afb::AttnTrainArgs train_attn_args(const at::Tensor& q, const at::Tensor&
   return a;
 }
 
+static void train_attn_qsa(afb::AttnTrainArgs& a, const c10::optional<at::Tensor>& blkmap, int64_t qsa_block) {
+  if (!blkmap.has_value()) return;
+  AFB_CHECK_DT(blkmap.value(), at::kInt);
+  AFB_CHECK_CONTIG(blkmap.value());
+  TORCH_CHECK(blkmap->dim() == 2 && blkmap->size(0) == a.T, "blkmap is int32 [T, words]");
+  TORCH_CHECK(qsa_block >= 2 && 64 % qsa_block == 0, "qsa_block must divide 64");
+  a.blkmap = reinterpret_cast<const uint32_t*>(blkmap->data_ptr());
+  a.blk_words = blkmap->size(1);
+  a.qsa_block = (int)qsa_block;
+}
+
 void attn_train_fwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
-                       const at::Tensor& tiles, double scale, at::Tensor& out, at::Tensor& lse) {
+                       const at::Tensor& tiles, double scale, at::Tensor& out, at::Tensor& lse,
+                       c10::optional<at::Tensor> blkmap, int64_t qsa_block) {
   afb::AttnTrainArgs a = train_attn_args(q, k, v, cu, tiles, scale);
+  train_attn_qsa(a, blkmap, qsa_block);
   AFB_CHECK_CONTIG(out);
   TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16, "out is bf16 like q");
   AFB_CHECK_DT(lse, at::kFloat);
@@ -437,8 +450,10 @@ void attn_train_fwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tenso
 void attn_train_bwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
                        const at::Tensor& tiles, const at::Tensor& kv_tiles, double scale, const at::Tensor& out,
                        const at::Tensor& lse, const at::Tensor& dout, at::Tensor& delta, at::Tensor& dq,
-                       at::Tensor& dk, at::Tensor& dv, at::Tensor& dk_part, at::Tensor& dv_part) {
+                       at::Tensor& dk, at::Tensor& dv, at::Tensor& dk_part, at::Tensor& dv_part,
+                       c10::optional<at::Tensor> blkmap, int64_t qsa_block) {
   afb::AttnTrainArgs a = train_attn_args(q, k, v, cu, tiles, scale);
+  train_attn_qsa(a, blkmap, qsa_block);
   AFB_CHECK_CONTIG(dout);
   AFB_CHECK_CONTIG(out);
   TORCH_CHECK(dout.sizes() == q.sizes() && out.sizes() == q.sizes(), "out / dout shapes");
@@ -1438,8 +1453,29 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("sp_lpage") = py::none(), py::arg("sp_mask") = py::none(), py::arg("kscale") = py::none(),
         py::arg("vscale") = py::none(), py::arg("impl") = 0, py::arg("sp_block") = 64, py::arg("sp_slot") = py::none());
   m.def("qsa_prep", &qsa_prep_op);
-  m.def("attn_train_fwd", &attn_train_fwd_op);
-  m.def("attn_train_bwd", &attn_train_bwd_op);
+  m.def("attn_train_fwd", &attn_train_fwd_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu"),
+        py::arg("tiles"), py::arg("scale"), py::arg("out"), py::arg("lse"), py::arg("blkmap") = py::none(),
+        py::arg("qsa_block") = 64);
+  m.def("attn_train_bwd", &attn_train_bwd_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu"),
+        py::arg("tiles"), py::arg("kv_tiles"), py::arg("scale"), py::arg("out"), py::arg("lse"), py::arg("dout"),
+        py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dk_part"), py::arg("dv_part"),
+        py::arg("blkmap") = py::none(), py::arg("qsa_block") = 64);
+  m.def("qsa_rowmap", [](const at::Tensor& u_lpage, const at::Tensor& u_mask, const at::Tensor& u_count,
+                         const at::Tensor& set_row0, const at::Tensor& set_rows, int64_t W, at::Tensor& blkmap) {
+    AFB_CHECK_DT(u_lpage, at::kInt);
+    AFB_CHECK_DT(u_mask, at::kByte);
+    AFB_CHECK_DT(blkmap, at::kInt);
+    AFB_CHECK_CONTIG(blkmap);
+    const int S = u_count.size(0);
+    TORCH_CHECK(u_lpage.size(0) >= S && u_lpage.sizes() == u_mask.sizes() && set_row0.numel() >= S &&
+                    set_rows.numel() >= S, "qsa_rowmap shapes");
+    afb_bind::check_rc(afb::qsa_rowmap(afb_bind::ptr<int>(u_lpage), afb_bind::ptr<uint8_t>(u_mask),
+                                       afb_bind::ptr<int>(u_count), afb_bind::ptr<int>(set_row0),
+                                       afb_bind::ptr<int>(set_rows), S, (int)W, u_lpage.size(1),
+                                       reinterpret_cast<uint32_t*>(blkmap.data_ptr()), blkmap.size(1),
+                                       afb_bind::stream()),
+                       "qsa_rowmap");
+  });
   py::class_<GuardCtx>(m, "GuardCtx")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, int64_t, int64_t, const at::Tensor&,
                     const at::Tensor&>())

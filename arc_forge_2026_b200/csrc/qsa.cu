@@ -381,9 +381,21 @@ __global__ void __launch_bounds__(qsa::THREADS) qsa_score_kernel(QsaArgs a, QsaS
   __syncthreads();
   const float rs = rsqrtf((float)qsa::DI);
   // committed blocks: the tensor-core scores, or one thread per block with keys from the pooled cache
-  if (sa.scores) {
+  if (sa.scores) {  // 8 independent loads in flight per thread (a load-then-store loop would wait on each)
     const float* src = sa.scores + ((size_t)s * W + r) * sa.scores_ld;
-    for (int b = tid; b < F; b += blockDim.x) score[b] = src[b];
+    for (int base = 0; base < F; base += 8 * qsa::THREADS) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int b = base + u * qsa::THREADS + tid;
+        v[u] = b < F ? __ldg(src + b) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int b = base + u * qsa::THREADS + tid;
+        if (b < F) score[b] = v[u];
+      }
+    }
   }
   for (int b = sa.scores ? F : tid; b < F; b += blockDim.x) {
     const uint4* kr = reinterpret_cast<const uint4*>(a.idx_key + ((size_t)sr * sa.max_blocks + b) * qsa::DI);
@@ -451,14 +463,19 @@ __global__ void __launch_bounds__(qsa::THREADS) qsa_score_kernel(QsaArgs a, QsaS
     pmask |= (uint32_t)(nb - 1) << shift;
     kk -= red[1];
   }
-  int above = 0;
+  int above = 0, equal = 0;
   for (int b = tid; b < C; b += blockDim.x) {
-    const bool gt = order_key(score[b]) > prefix;
-    above += gt;
-    if (gt) atomicOr(&sel[b], bit);
+    const uint32_t key = order_key(score[b]);
+    above += key > prefix;
+    equal += key == prefix;
+    if (key > prefix) atomicOr(&sel[b], bit);
   }
   const int need = K - block_count(above, red);
-  if (warp == 0) {  // ties at the threshold: the lowest block indices first
+  const int n_equal = block_count(equal, red);
+  if (n_equal <= need) {  // every key at the threshold is taken: no ordering needed
+    for (int b = tid; b < C; b += blockDim.x)
+      if (order_key(score[b]) == prefix) atomicOr(&sel[b], bit);
+  } else if (warp == 0) {  // more ties than places: the lowest block indices first
     int need_eq = need;
     for (int base = 0; base < C && need_eq > 0; base += 32) {
       const int b = base + lane;
@@ -483,12 +500,22 @@ __global__ void __launch_bounds__(qsa::THREADS) qsa_union_kernel(QsaSelectArgs s
   const int n_scan = min(seq_len / sa.block + 1, sa.max_blocks + 1);
   uint32_t* sel = sa.sel + (size_t)s * (sa.max_blocks + 1);
   const int* bt = sa.block_table + (size_t)(sa.bt_row ? sa.bt_row[s] : s) * sa.max_pages;
-  for (int e = tid; e < n_scan; e += blockDim.x) {
-    const uint32_t m = sel[e];
-    marks[e] = m;
-    if (m) sel[e] = 0u;
+  for (int base = 0; base < n_scan; base += 8 * qsa::THREADS) {  // 8 independent loads in flight per thread
+    uint32_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = base + u * qsa::THREADS + tid;
+      v[u] = e < n_scan ? sel[e] : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = base + u * qsa::THREADS + tid;
+      if (e < n_scan) marks[e] = v[u];
+    }
   }
   __syncthreads();
+  for (int e = tid; e < n_scan; e += blockDim.x)
+    if (marks[e]) sel[e] = 0u;
   const int chunk = (n_scan + qsa::THREADS - 1) / qsa::THREADS;
   const int lo = min(n_scan, tid * chunk), hi = min(n_scan, lo + chunk);
   int c = 0;

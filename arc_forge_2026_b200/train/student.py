@@ -153,6 +153,9 @@ def layer_tensors_from_reference(L: R.DecoderLayer, codes_scales) -> dict:
     if L.kind == FULL:
         t.update(q_proj=m.q_proj.weight, k_proj=m.k_proj.weight, v_proj=m.v_proj.weight, o_proj=m.o_proj.weight,
                  q_norm=m.q_norm.weight, k_norm=m.k_norm.weight)
+        if getattr(m, "index_qk_proj", None) is not None:  # QSA indexer (frozen)
+            t.update(index_qk_proj=m.index_qk_proj.weight, index_q_norm=m.index_q_norm.weight,
+                     index_k_norm=m.index_k_norm.weight)
     else:
         t.update(in_proj_qkvz=m.in_proj_qkvz.weight, in_proj_ba=m.in_proj_ba.weight, out_proj=m.out_proj.weight,
                  conv1d=m.conv1d, A_log=m.A_log, dt_bias=m.dt_bias, g_norm=m.norm)
@@ -198,6 +201,10 @@ def random_layer_tensors(cfg: ModelConfig, kind: str, device, gen: torch.Generat
         D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_kv_heads
         t.update(q_proj=rn(Hq * 2 * D, H), k_proj=rn(Hkv * D, H), v_proj=rn(Hkv * D, H), o_proj=rn(H, Hq * D),
                  q_norm=torch.zeros(D, device=device), k_norm=torch.zeros(D, device=device))
+        if cfg.qsa_topk:
+            Di = cfg.qsa_indexer_dim
+            t.update(index_qk_proj=rn((cfg.qsa_indexer_heads + 1) * Di, H), index_q_norm=torch.zeros(Di, device=device),
+                     index_k_norm=torch.zeros(Di, device=device))
     else:
         Hv, Dv = cfg.linear_num_value_heads, cfg.linear_value_head_dim
         dt = torch.exp(torch.empty(Hv, device=device).uniform_(math.log(1e-3), math.log(1e-1), generator=gen))
@@ -241,6 +248,10 @@ class StudentLayer(nn.Module):
                 setattr(self, n, _master(t[n]))
             buf("q_norm")
             buf("k_norm")
+            if "index_qk_proj" in t:  # QSA indexer: frozen (selection only, no gradient through it)
+                self.register_buffer("index_qk_proj", t["index_qk_proj"].to(torch.bfloat16).clone())
+                buf("index_q_norm")
+                buf("index_k_norm")
         else:
             for n in ("in_proj_qkvz", "in_proj_ba", "out_proj"):
                 setattr(self, n, _master(t[n]))
@@ -318,13 +329,40 @@ class StudentLayer(nn.Module):
         positions = torch.arange(T, device=x.device) if pack is None else pack["pos"][0]
         cos, sin = R.rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
         q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
+        blkmap = self._qsa_blocks(x, positions, pack) if pack is not None else None
         if pack is None:
             o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                                is_causal=True, enable_gqa=True).transpose(1, 2).reshape(B, T, -1)
+        elif blkmap is not None:
+            from .attention import varlen_attention
+            o = varlen_attention(q[0], k[0], v[0], pack["cu_seqlens"], blkmap, c.qsa_block).reshape(B, T, -1)
         else:
             o = packed_attention(q[0], k[0], v[0], pack["cu_seqlens"], pack["max_seqlen"]).reshape(B, T, -1)
         o = o * torch.sigmoid(gate.float()).to(o.dtype)
         return self._lin("o_proj", o, False)
+
+    @torch.no_grad()
+    def _qsa_blocks(self, x, positions, pack):
+        """QSA selection of a packed row (``train/attention.py`` ``qsa_select_packed``), or None while every
+        segment fits the budget (topk x block tokens: each query then keeps all its blocks, the dense path). The
+        indexer is frozen: index queries and raw keys come from its projection without a gradient."""
+        c = self.cfg
+        if not c.qsa_topk or getattr(self, "index_qk_proj", None) is None or not x.is_cuda:
+            return None
+        if int(pack["max_seqlen"]) <= c.qsa_topk * c.qsa_block:
+            return None
+        from .attention import qsa_select_packed
+        Hi, Di = c.qsa_indexer_heads, c.qsa_indexer_dim
+        proj = F.linear(x[0].to(torch.bfloat16), self.index_qk_proj)
+        iq = R.rms_norm(proj[:, :Hi * Di].view(-1, Hi, Di), self.index_q_norm, c.rms_norm_eps)
+        cos, sin = R.rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
+        iq = R.apply_rope(iq[None], cos[None], sin[None])[0].to(torch.bfloat16).contiguous()
+        raw = proj[:, Hi * Di:].contiguous()
+        tab_cos, tab_sin = R.rope_cos_sin(torch.arange(int(pack["max_seqlen"]) + 64, device=x.device), c.rotary_dim,
+                                          c.rope_theta)
+        return qsa_select_packed(iq, raw, self.index_k_norm.to(torch.bfloat16), tab_cos.contiguous(),
+                                 tab_sin.contiguous(), c.rotary_dim, c.rms_norm_eps, pack["cu_seqlens"], c.qsa_block,
+                                 c.qsa_topk)
 
     def _gdn(self, x, B, T, pack=None):
         c = self.cfg
