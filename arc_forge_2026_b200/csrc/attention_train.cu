@@ -10,15 +10,16 @@
 //            bf16 back into TMEM, O += P V with P as the A operand from TMEM; writes O and the row log-sum-exp (log2).
 //   dQ       CTA (query head, 64-query tile): per key tile S = Q K^T and dP = dO V^T into TMEM, the softmax warps
 //            form dS = P (dP - delta) as bf16 in TMEM, dQ += dS K with K as an MN-major operand; dQ stays in TMEM.
-//   dK / dV  CTA (query head, 64-key tile): walks every query tile at or after it; per unit S^T = K Q^T and
+//   dK / dV  CTA (query head, 128-key tile): walks every query row group at or after it; per unit S^T = K Q^T and
 //            dP^T = V dO^T into TMEM, the epilogue warps (TMEM lanes = keys) form P^T and dS^T, dV += P^T dO and
 //            dK += dS^T Q with dO / Q as MN-major operands, both resident in TMEM; each CTA writes its query head's
 //            fp32 contribution, and a reduce kernel sums the heads of each KV group in a fixed order. With D = 256
 //            the two accumulators do not fit TMEM together: dV and dK run as two launches.
 // Every output element is produced by exactly one thread in a fixed order: no atomics, bitwise deterministic.
 // Warp roles: 0 TMA loader (no multicast), 1 MMA issuer (+ TMEM); forward: 4-7 softmax (32 full rows each: the
-// running max); dQ and dK / dV: 4, 5, 8, 9 epilogue (warps 4 and 8 share TMEM lanes 0..31, 5 and 9 lanes 32..63,
-// each warp of a pair takes half of the 64 columns: no row-wide reduction is needed there).
+// running max); dQ: 4, 5, 8, 9 epilogue (warps 4 and 8 share TMEM lanes 0..31, 5 and 9 lanes 32..63, each warp of a
+// pair takes half of the 64 columns: no row-wide reduction is needed there); dK / dV: 4..11 epilogue (warp w the
+// lanes of quadrant w & 3 = 32 keys, warps 4-7 and 8-11 the two halves of a unit's query columns).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -32,7 +33,8 @@ namespace afb {
 namespace attn_tr {
 constexpr int TILE = 64;
 constexpr int THREADS = 256;
-constexpr int THREADS_BWD = 320;  // warps 0..9: epilogue warps 4, 5, 8, 9
+constexpr int THREADS_BWD = 320;  // dQ: warps 0..9, epilogue warps 4, 5, 8, 9
+constexpr int THREADS_KV = 384;   // dK / dV: warps 0..11, epilogue warps 4..11
 constexpr int W_LD = 0, W_MMA = 1, W_SM0 = 4;
 AFB_DEV bool bwd_epi_warp(int w) { return w == 4 || w == 5 || w == 8 || w == 9; }
 constexpr float RESCALE = 8.f;
@@ -68,23 +70,30 @@ struct Dq {
 
 template <int D, int MODE>  // MODE bit 0: dV, bit 1: dK
 struct Dkv {
-  static constexpr uint32_t T_BYTES = (D / 64) * SUB;
+  static constexpr bool DV = MODE & 1, DK = MODE & 2;
+  static constexpr int KT = 128;                              // keys per CTA: the MMA's full M
+  static constexpr int QU = (D == 256 && DK) ? 32 : 64;       // query rows per unit (the N of S^T)
+  static constexpr bool HAS_V = DK;                           // V is read only for dP^T
+  static constexpr uint32_t KSUB = KT * 128;                  // one 128-key x 64-column sub-tile
+  static constexpr uint32_t QSUB = QU * 128;
+  static constexpr uint32_t T_BYTES = (D / 64) * KSUB;
   static constexpr uint32_t K_OFF = 0, V_OFF = T_BYTES;
   static constexpr int NS = 2;
-  static constexpr uint32_t STAGE = 2 * T_BYTES;  // Q + dO of one unit
-  static constexpr uint32_t ST_OFF = 2 * T_BYTES;
-  static constexpr uint32_t ROWS_OFF = ST_OFF + NS * STAGE;       // lse[NS][64], delta[NS][64], qsa field[NS][64]
-  static constexpr uint32_t BAR_OFF = ROWS_OFF + NS * 3 * TILE * 4;
+  static constexpr uint32_t U_BYTES = (D / 64) * QSUB;        // Q (or dO) rows of one unit
+  static constexpr uint32_t STAGE = 2 * U_BYTES;              // Q + dO
+  static constexpr uint32_t ST_OFF = (HAS_V ? 2 : 1) * T_BYTES;
+  static constexpr uint32_t ROWS_OFF = ST_OFF + NS * STAGE;   // lse[NS][QU], delta[NS][QU], qsa field[NS][QU]
+  static constexpr uint32_t BAR_OFF = ROWS_OFF + NS * 3 * QU * 4;
   static constexpr uint32_t TOTAL = BAR_OFF + (2 * NS + 10) * 8 + 16 + 1024;
-  static constexpr bool DV = MODE & 1, DK = MODE & 2;
   static constexpr uint32_t DV_COL = 0;
   static constexpr uint32_t DK_COL = DV ? D : 0;
   static constexpr uint32_t S_COL = (DV ? D : 0) + (DK ? D : 0);
-  static constexpr uint32_t DP_COL = S_COL + TILE;                 // dK only
-  static constexpr uint32_t PT_COL = S_COL + (DK ? 2 : 1) * TILE;  // P^T [2][32] (dV)
-  static constexpr uint32_t DS_COL = PT_COL + (DV ? TILE : 0);     // dS^T [2][32] (dK)
-  static constexpr uint32_t END = DS_COL + (DK ? TILE : 0);
+  static constexpr uint32_t DP_COL = S_COL + QU;                   // dK only
+  static constexpr uint32_t PT_COL = S_COL + (DK ? 2 : 1) * QU;    // P^T bf16 pairs [2][QU / 2] (dV)
+  static constexpr uint32_t DS_COL = PT_COL + (DV ? QU : 0);       // dS^T [2][QU / 2] (dK)
+  static constexpr uint32_t END = DS_COL + (DK ? QU : 0);
   static_assert(END <= 512, "TMEM columns");
+  static_assert(TOTAL <= 232448, "shared memory");
 };
 }  // namespace attn_tr
 
@@ -529,13 +538,13 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
 
 // ---------------------------------------------------------------------------------------------------- dK / dV
 template <int D, int MODE>
-__global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
+__global__ void __launch_bounds__(attn_tr::THREADS_KV, 1)
     attn_train_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                            const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            AttnTrainArgs a, uint32_t* status) {
   using namespace attn_tr;
   using L = Dkv<D, MODE>;
-  constexpr int NS = L::NS;
+  constexpr int NS = L::NS, KT = L::KT, QU = L::QU;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* st_full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);  // [NS] Q + dO (+ rows) of a unit landed
@@ -547,17 +556,17 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
   uint64_t* kv_ready = pt_done + 2;
   uint64_t* mma_fin = kv_ready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_fin + 1);
-  float* rows_lse = reinterpret_cast<float*>(smem + L::ROWS_OFF);       // [NS][64]
-  float* rows_dlt = rows_lse + NS * TILE;                                // [NS][64]
-  uint32_t* rows_map = reinterpret_cast<uint32_t*>(rows_dlt + NS * TILE);  // [NS][64]: the key tile's block bits
+  float* rows_lse = reinterpret_cast<float*>(smem + L::ROWS_OFF);            // [NS][QU]
+  float* rows_dlt = rows_lse + NS * QU;                                        // [NS][QU]
+  uint32_t* rows_map = reinterpret_cast<uint32_t*>(rows_dlt + NS * QU);       // [NS][QU]: the key tile's block bits
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qh = blockIdx.x, kvh = qh / (a.Hq / a.Hkv);
   const int2 tl = a.tiles[blockIdx.y];
   const int s0 = a.cu[tl.x], Lseg = a.cu[tl.x + 1] - s0, k0 = tl.y;
-  const int KR = min(TILE, Lseg - k0);
-  const int nq = (Lseg + TILE - 1) / TILE, qt0 = k0 / TILE;
-  const int U = nq - qt0;  // units: the query tiles at or after this key tile
+  const int KR = min(KT, Lseg - k0);
+  const int nq = (Lseg + QU - 1) / QU, qt0 = k0 / QU;
+  const int U = nq - qt0;  // units: the query row groups at or after this key tile
   if (KR <= 0 || U <= 0) return;
 
   if (threadIdx.x == 0) {
@@ -566,9 +575,9 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
       mbar_init(&st_empty[s], 1);
     }
     mbar_init(sx_full, 1);
-    mbar_init(sx_empty, 4);
+    mbar_init(sx_empty, 8);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&pt_full[b], 4);
+      mbar_init(&pt_full[b], 8);
       mbar_init(&pt_done[b], 1);
     }
     mbar_init(kv_ready, 1);
@@ -584,35 +593,34 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
 
   if (warp == W_LD) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(kv_ready, 2 * L::T_BYTES);
+      mbar_arrive_expect_tx(kv_ready, (L::HAS_V ? 2 : 1) * L::T_BYTES);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        tma_load_3d(smem + L::K_OFF + c * SUB, &tmK, kv_ready, c * 64, kvh, s0 + k0);
-        tma_load_3d(smem + L::V_OFF + c * SUB, &tmV, kv_ready, c * 64, kvh, s0 + k0);
+        tma_load_3d(smem + L::K_OFF + c * L::KSUB, &tmK, kv_ready, c * 64, kvh, s0 + k0);
+        if (L::HAS_V) tma_load_3d(smem + L::V_OFF + c * L::KSUB, &tmV, kv_ready, c * 64, kvh, s0 + k0);
       }
     }
     int issued = 0;
+    const int bpt = a.blkmap ? KT / a.qsa_block : 0, b0 = a.blkmap ? (k0 / a.qsa_block) : 0;
     for (int u = 0; u < U && ok; ++u) {
       const int s = u % NS;
-      const int q0 = (qt0 + u) * TILE, h = qh;
+      const int q0 = (qt0 + u) * QU;
       if (u >= NS && !__all_sync(0xffffffffu, mbar_wait(&st_empty[s], ((u / NS) & 1) ^ 1, status))) {
         ok = false;
         break;
       }
-      // the unit's row statistics (plain loads; published by lane 0's arrive below)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int r = lane + 32 * hh;
+      // the unit's row statistics and QSA fields (plain loads; published by lane 0's arrive below)
+      for (int r = lane; r < QU; r += 32) {
         const bool in = q0 + r < Lseg;
-        const size_t idx = (size_t)h * a.T + s0 + q0 + r;
-        rows_lse[s * TILE + r] = in ? a.lse[idx] : 0.f;
-        rows_dlt[s * TILE + r] = in ? a.delta[idx] : 0.f;
+        const size_t idx = (size_t)qh * a.T + s0 + q0 + r;
+        rows_lse[s * QU + r] = in ? a.lse[idx] : 0.f;
+        rows_dlt[s * QU + r] = in ? a.delta[idx] : 0.f;
         uint32_t f = 0xffffffffu;
-        if (a.blkmap && in) {  // this key tile's 64 / B block bits of the row
-          const int bpt = TILE / a.qsa_block, b0 = (k0 / TILE) * bpt;
-          f = a.blkmap[(size_t)(s0 + q0 + r) * a.blk_words + (b0 >> 5)] >> (b0 & 31);
+        if (a.blkmap && in) {  // this key tile's KT / B block bits of the row (one aligned field of one word)
+          const uint32_t w = a.blkmap[(size_t)(s0 + q0 + r) * a.blk_words + (b0 >> 5)];
+          f = bpt >= 32 ? w : (w >> (b0 & 31));
         }
-        rows_map[s * TILE + r] = f;
+        rows_map[s * QU + r] = f;
       }
       __syncwarp();
       if (lane == 0) {
@@ -620,8 +628,8 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
         mbar_arrive_expect_tx(&st_full[s], L::STAGE);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(st + c * SUB, &tmQ, &st_full[s], c * 64, h, s0 + q0);
-          tma_load_3d(st + L::T_BYTES + c * SUB, &tmDO, &st_full[s], c * 64, h, s0 + q0);
+          tma_load_3d(st + c * L::QSUB, &tmQ, &st_full[s], c * 64, qh, s0 + q0);
+          tma_load_3d(st + L::U_BYTES + c * L::QSUB, &tmDO, &st_full[s], c * 64, qh, s0 + q0);
         }
       }
       __syncwarp();
@@ -632,7 +640,7 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
       for (int u = max(0, issued - NS); u < issued; ++u) mbar_wait(&st_full[u % NS], (u / NS) & 1, status);
     }
   } else if (warp == W_MMA) {
-    constexpr uint32_t idesc_s = idesc_f16(128, TILE, 1);             // S^T = K Q^T, dP^T = V dO^T
+    constexpr uint32_t idesc_s = idesc_f16(128, QU, 1);             // S^T = K Q^T, dP^T = V dO^T
     constexpr uint32_t idesc_acc = idesc_f16(128, D, 1) | (1u << 16); // dV += P^T dO, dK += dS^T Q (B MN-major)
     ok = __all_sync(0xffffffffu, mbar_wait(kv_ready, 0, status));
     tc_fence_after();
@@ -643,15 +651,17 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t q_base = smem_u32(smem + L::ST_OFF + s * L::STAGE);
-        const uint32_t do_base = q_base + L::T_BYTES;
+        const uint32_t do_base = q_base + L::U_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; ++kk) {
+        for (int kk = 0; kk < QU / 16; ++kk) {
           if (L::DV)
-            umma_f16_ta(tmem + L::DV_COL, tmem + L::PT_COL + b * (TILE / 2) + kk * 8,
-                        sw128_desc_mn(do_base + kk * 16 * 128, SUB, 1024), idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ta(tmem + L::DV_COL, tmem + L::PT_COL + b * (QU / 2) + kk * 8,
+                        sw128_desc_mn(do_base + kk * 16 * 128, L::QSUB, 1024), idesc_acc,
+                        (j > 0 || kk > 0) ? 1u : 0u);
           if (L::DK)
-            umma_f16_ta(tmem + L::DK_COL, tmem + L::DS_COL + b * (TILE / 2) + kk * 8,
-                        sw128_desc_mn(q_base + kk * 16 * 128, SUB, 1024), idesc_acc, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ta(tmem + L::DK_COL, tmem + L::DS_COL + b * (QU / 2) + kk * 8,
+                        sw128_desc_mn(q_base + kk * 16 * 128, L::QSUB, 1024), idesc_acc,
+                        (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&pt_done[b]);
         umma_commit(&st_empty[s]);
@@ -669,19 +679,16 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t q_base = smem_u32(smem + L::ST_OFF + s * L::STAGE);
-        const uint32_t do_base = q_base + L::T_BYTES;
+        const uint32_t do_base = q_base + L::U_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
-          umma_f16(tmem + L::S_COL, sw128_desc(k_base + off), sw128_desc(q_base + off), idesc_s, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16(tmem + L::S_COL, sw128_desc(k_base + (kk >> 2) * L::KSUB + (kk & 3) * 32),
+                   sw128_desc(q_base + (kk >> 2) * L::QSUB + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
         if (L::DK) {
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
-            umma_f16(tmem + L::DP_COL, sw128_desc(v_base + off), sw128_desc(do_base + off), idesc_s,
-                     kk > 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_f16(tmem + L::DP_COL, sw128_desc(v_base + (kk >> 2) * L::KSUB + (kk & 3) * 32),
+                     sw128_desc(do_base + (kk >> 2) * L::QSUB + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(sx_full);
       }
@@ -695,35 +702,42 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
     if (lane == 0) umma_commit(mma_fin);
     __syncwarp();
     mbar_wait(mma_fin, 0, status);
-  } else if (bwd_epi_warp(warp)) {
-    const int quad = warp & 1, half = warp >= 8;  // TMEM lane quadrant, column half
-    const int kr = quad * 32 + lane;               // key row = TMEM lane
+  } else if (warp >= 4 && warp < 12) {
+    // epilogue: warp w owns TMEM lanes (w & 3) * 32 .. + 31 (keys) and half of the unit's QU columns
+    constexpr int HC = QU / 2;  // columns per warp
+    const int quad = warp & 3, half = warp >= 8;
+    const int kr = quad * 32 + lane;
     const bool klive = kr < KR;
     const int kpos = k0 + kr;
+    const int kblk = a.blkmap ? kr / a.qsa_block : 0;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     for (int u = 0; u < U; ++u) {
       const int b = u & 1, s = u % NS;
-      const int q0 = (qt0 + u) * TILE + half * 32;  // this warp's 32 query columns
+      const int q0 = (qt0 + u) * QU + half * HC;  // this warp's HC query columns
       if (!__all_sync(0xffffffffu, mbar_wait(sx_full, u & 1, status)) ||
           !__all_sync(0xffffffffu, mbar_wait(&st_full[s], (u / NS) & 1, status))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[32], dp[L::DK ? 32 : 1];
-      tmem_ld32(lane_base + L::S_COL + half * 32, sv);
-      if (L::DK) tmem_ld32(lane_base + L::DP_COL + half * 32, dp);
+      float sv[HC], dp[L::DK ? HC : 1];
+      if constexpr (HC == 32) {
+        tmem_ld32(lane_base + L::S_COL + half * HC, sv);
+        if (L::DK) tmem_ld32(lane_base + L::DP_COL + half * HC, dp);
+      } else {
+        tmem_ld16(lane_base + L::S_COL + half * HC, sv);
+        if (L::DK) tmem_ld16(lane_base + L::DP_COL + half * HC, dp);
+      }
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sx_empty);
-      const float* lse = rows_lse + s * TILE + half * 32;
-      const float* dlt = rows_dlt + s * TILE + half * 32;
-      const uint32_t* fmap = rows_map + s * TILE + half * 32;
-      const int kblk = kr / a.qsa_block;  // this key's block within the tile
-      uint32_t ppk[L::DV ? 16 : 1], dpk[L::DK ? 16 : 1];
+      const float* lse = rows_lse + s * QU + half * HC;
+      const float* dlt = rows_dlt + s * QU + half * HC;
+      const uint32_t* fmap = rows_map + s * QU + half * HC;
+      uint32_t ppk[L::DV ? HC / 2 : 1], dpk[L::DK ? HC / 2 : 1];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < HC / 2; ++j) {
         float pv[2], dv2[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
@@ -741,8 +755,13 @@ __global__ void __launch_bounds__(attn_tr::THREADS_BWD, 1)
         ok = false;
         break;
       }
-      if (L::DV) tmem_st16(lane_base + L::PT_COL + b * (TILE / 2) + half * 16, ppk);
-      if (L::DK) tmem_st16(lane_base + L::DS_COL + b * (TILE / 2) + half * 16, dpk);
+      if constexpr (HC == 32) {
+        if (L::DV) tmem_st16(lane_base + L::PT_COL + b * (QU / 2) + half * (HC / 2), ppk);
+        if (L::DK) tmem_st16(lane_base + L::DS_COL + b * (QU / 2) + half * (HC / 2), dpk);
+      } else {
+        if (L::DV) tmem_st8(lane_base + L::PT_COL + b * (QU / 2) + half * (HC / 2), ppk);
+        if (L::DK) tmem_st8(lane_base + L::DS_COL + b * (QU / 2) + half * (HC / 2), dpk);
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -849,7 +868,7 @@ static int qkv_maps(const AttnTrainArgs& a, CUtensorMap* tq, CUtensorMap* tk, CU
 
 static int check_args(const AttnTrainArgs& a) {
   if ((a.D != 128 && a.D != 256) || a.Hkv < 1 || a.Hq % a.Hkv || a.T < 1 || !a.cu || !a.tiles) return 3;
-  if (a.blkmap && (a.qsa_block < 2 || attn_tr::TILE % a.qsa_block || a.blk_words < 1)) return 3;
+  if (a.blkmap && (a.qsa_block < 4 || attn_tr::TILE % a.qsa_block || a.blk_words < 1)) return 3;
   return 0;
 }
 
@@ -898,19 +917,30 @@ int attn_train_fwd(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st) {
   return a.D == 256 ? launch_fwd<256>(a, status, st) : launch_fwd<128>(a, status, st);
 }
 
+// dK / dV: 128-key tiles (kv_tiles lists them) and QU-row query units
 template <int D, int MODE>
-static int launch_dkdv(const AttnTrainArgs& a, const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tk,
-                       const CUtensorMap& tv, uint32_t* status, cudaStream_t st) {
+static int launch_dkdv(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st) {
   using L = attn_tr::Dkv<D, MODE>;
+  CUtensorMap tq{}, tk{}, tv{}, tdo{};
+  const uint64_t qd[3] = {(uint64_t)a.D, (uint64_t)a.Hq, (uint64_t)a.T};
+  const uint64_t qs[2] = {(uint64_t)a.D * 2, (uint64_t)a.Hq * a.D * 2};
+  const uint64_t kd[3] = {(uint64_t)a.D, (uint64_t)a.Hkv, (uint64_t)a.T};
+  const uint64_t ks[2] = {(uint64_t)a.D * 2, (uint64_t)a.Hkv * a.D * 2};
+  const uint32_t kbox[3] = {64, 1, (uint32_t)L::KT}, qbox[3] = {64, 1, (uint32_t)L::QU};
+  int rc = make_tmap_3d_bf16(&tq, a.q, qd, qs, qbox);
+  if (!rc) rc = make_tmap_3d_bf16(&tdo, a.dout, qd, qs, qbox);
+  if (!rc) rc = make_tmap_3d_bf16(&tk, a.k, kd, ks, kbox);
+  if (!rc) rc = make_tmap_3d_bf16(&tv, a.v, kd, ks, kbox);
+  if (rc) return 1000 + rc;
   static std::atomic<uint64_t> devs{0};
   if (const int e = smem_attr_once(devs, (const void*)attn_train_dkdv_kernel<D, MODE>, L::TOTAL)) return e;
-  attn_train_dkdv_kernel<D, MODE><<<dim3(a.Hq, a.ntiles), attn_tr::THREADS_BWD, L::TOTAL, st>>>(tq, tdo, tk, tv, a,
-                                                                                               status);
+  attn_train_dkdv_kernel<D, MODE><<<dim3(a.Hq, a.ntiles), attn_tr::THREADS_KV, L::TOTAL, st>>>(tq, tdo, tk, tv, a,
+                                                                                             status);
   return (int)cudaGetLastError();
 }
 
 template <int D>
-static int launch_bwd(const AttnTrainArgs& a, const int2* kv_tiles, uint32_t* status, cudaStream_t st) {
+static int launch_bwd(const AttnTrainArgs& a, const int2* kv_tiles, int nkv, uint32_t* status, cudaStream_t st) {
   using Lq = attn_tr::Dq<D>;
   CUtensorMap tq{}, tk{}, tv{}, tdo{};
   if (const int rc = qkv_maps(a, &tq, &tk, &tv, &tdo)) return rc;
@@ -922,12 +952,13 @@ static int launch_bwd(const AttnTrainArgs& a, const int2* kv_tiles, uint32_t* st
   attn_train_dq_kernel<D><<<dim3(a.Hq, a.ntiles), attn_tr::THREADS_BWD, Lq::TOTAL, st>>>(tq, tdo, tk, tv, a, status);
   AttnTrainArgs b = a;
   b.tiles = kv_tiles;
+  b.ntiles = nkv;
   int rc;
   if constexpr (D == 128) {
-    rc = launch_dkdv<D, 3>(b, tq, tdo, tk, tv, status, st);
+    rc = launch_dkdv<D, 3>(b, status, st);
   } else {  // dV and dK accumulators (2 x 256 TMEM columns) do not fit together: two passes
-    rc = launch_dkdv<D, 1>(b, tq, tdo, tk, tv, status, st);
-    if (!rc) rc = launch_dkdv<D, 2>(b, tq, tdo, tk, tv, status, st);
+    rc = launch_dkdv<D, 1>(b, status, st);
+    if (!rc) rc = launch_dkdv<D, 2>(b, status, st);
   }
   if (rc) return rc;
   const int64_t n4 = (int64_t)a.T * a.Hkv * D / 4;
@@ -936,11 +967,11 @@ static int launch_bwd(const AttnTrainArgs& a, const int2* kv_tiles, uint32_t* st
   return (int)cudaGetLastError();
 }
 
-int attn_train_bwd(const AttnTrainArgs& a, const int2* kv_tiles, uint32_t* status, cudaStream_t st) {
+int attn_train_bwd(const AttnTrainArgs& a, const int2* kv_tiles, int nkv, uint32_t* status, cudaStream_t st) {
   if (const int e = check_args(a)) return e;
   if (!a.dout || !a.out || !a.delta || !a.dq || !a.dk || !a.dv || !a.dk_part || !a.dv_part || !kv_tiles) return 3;
   if (a.ntiles == 0) return 0;
-  return a.D == 256 ? launch_bwd<256>(a, kv_tiles, status, st) : launch_bwd<128>(a, kv_tiles, status, st);
+  return a.D == 256 ? launch_bwd<256>(a, kv_tiles, nkv, status, st) : launch_bwd<128>(a, kv_tiles, nkv, status, st);
 }
 
 }  // namespace afb

@@ -93,8 +93,8 @@ struct AttnTrainArgs {
   int blk_words = 0, qsa_block = 64;
 };
 int attn_train_fwd(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st);
-// kv_tiles: the same tiles ordered for the dK / dV pass (most work first)
-int attn_train_bwd(const AttnTrainArgs& a, const int2* kv_tiles, uint32_t* status, cudaStream_t st);
+// kv_tiles [nkv]: the 128-key tiles of the dK / dV kernels (most work first); a.tiles: 64-row query tiles of dQ
+int attn_train_bwd(const AttnTrainArgs& a, const int2* kv_tiles, int nkv, uint32_t* status, cudaStream_t st);
 // QSA training selection -> per-row block bitmap: row set s (W rows starting at packed row set_row0[s], the first
 // set_rows[s] of them real) marks block u_lpage[s][e] for each row whose bit is set in u_mask[s][e]
 int qsa_rowmap(const int* u_lpage, const uint8_t* u_mask, const int* u_count, const int* set_row0,

@@ -461,7 +461,9 @@ void attn_train_bwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   AFB_CHECK_CONTIG(dq);
   AFB_CHECK_CONTIG(dk);
   AFB_CHECK_CONTIG(dv);
-  TORCH_CHECK(kv_tiles.sizes() == tiles.sizes(), "kv_tiles is the tile list in another order");
+  AFB_CHECK_DT(kv_tiles, at::kInt);
+  AFB_CHECK_CONTIG(kv_tiles);
+  TORCH_CHECK(kv_tiles.dim() == 2 && kv_tiles.size(1) == 2, "kv_tiles is [n, 2]");
   TORCH_CHECK(delta.numel() == (int64_t)a.Hq * a.T && lse.numel() == delta.numel(), "lse / delta are [Hq, T]");
   a.out = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(out.data_ptr()));
   a.lse = const_cast<float*>(ptr<float>(lse));
@@ -475,8 +477,8 @@ void attn_train_bwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   TORCH_CHECK(dk_part.numel() == q.numel() && dv_part.numel() == q.numel(), "dk_part / dv_part are fp32 [T, Hq, D]");
   a.dk_part = ptr<float>(dk_part);
   a.dv_part = ptr<float>(dv_part);
-  check_rc(afb::attn_train_bwd(a, reinterpret_cast<const int2*>(kv_tiles.data_ptr()), status_ptr(q.get_device()),
-                               stream()),
+  check_rc(afb::attn_train_bwd(a, reinterpret_cast<const int2*>(kv_tiles.data_ptr()), (int)kv_tiles.size(0),
+                               status_ptr(q.get_device()), stream()),
            "attn_train_bwd");
 }
 

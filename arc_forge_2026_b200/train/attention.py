@@ -18,15 +18,14 @@ TILE = 64
 
 
 def tile_lists(cu: list[int], device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """(segment, first position) of every query tile of the forward (128 positions), and of every 64-position tile
-    of the backward: ordered for the forward / dQ kernels (longest causal prefix first) and for the dK / dV kernels
-    (most query tiles after the key tile first)."""
+    """(segment, first position) of the tiles of each kernel: the forward's 128-query tiles and dQ's 64-query tiles
+    (longest causal prefix first), the dK / dV kernels' 128-key tiles (most query rows after the key tile first)."""
     def tiles(step):
         return [(s, p, cu[s + 1] - cu[s]) for s in range(len(cu) - 1) for p in range(0, cu[s + 1] - cu[s], step)]
     mk = lambda ts: torch.tensor([[s, p] for s, p, _ in ts], dtype=torch.int32).reshape(-1, 2).to(device)  # noqa: E731
-    t64 = tiles(TILE)
-    return (mk(sorted(tiles(2 * TILE), key=lambda t: -t[1])), mk(sorted(t64, key=lambda t: -t[1])),
-            mk(sorted(t64, key=lambda t: -(t[2] - t[1]))))
+    t128 = tiles(2 * TILE)
+    return (mk(sorted(t128, key=lambda t: -t[1])), mk(sorted(tiles(TILE), key=lambda t: -t[1])),
+            mk(sorted(t128, key=lambda t: -(t[2] - t[1]))))
 
 
 class VarlenCausalAttention(torch.autograd.Function):

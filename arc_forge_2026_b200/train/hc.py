@@ -10,7 +10,6 @@ fall back to ``models.reference`` (the oracle of the GPU tests).
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from ..models import reference as R
 
@@ -35,13 +34,19 @@ class _HCRead(torch.autograd.Function):
         rstd = torch.empty(rows, G, dtype=torch.float32, device=h.device)
         c = _ext()
         c.hc_norm(h2, norm_w, eps, zb, rstd, None, None)
-        wcat = w_down if w_inject is None else torch.cat([w_down, w_inject])
-        du = zb.view(rows, G * H) @ wcat.t()                         # [rows, R (+ G)]
-        s = F.silu(du[:, :R_].float() * 0.25).to(_BF)
+        # [W_down; W_inject] padded to a multiple of 16 rows: one GEMM gives the low-rank input and the gate logits
+        n_out = R_ + (0 if w_inject is None else G)
+        wcat = torch.zeros((n_out + 15) // 16 * 16, G * H, dtype=_BF, device=h.device)
+        wcat[:R_] = w_down
+        if w_inject is not None:
+            wcat[R_:n_out] = w_inject
+        du = zb.view(rows, G * H) @ wcat.t()                         # [rows, R (+ G) + pad]
+        s = torch.empty(rows, R_, dtype=_BF, device=h.device)
+        gate = None if w_inject is None else torch.empty(rows, G, dtype=_BF, device=h.device)
+        c.hc_act(du, R_, G, s, gate)                                  # silu(du / 4), 2 sigmoid(di / 4)
         pre = s @ w_up.t()                                            # [rows, G*H]
         x = torch.empty(rows, H, dtype=_BF, device=h.device)
         c.hc_mix(pre.contiguous(), zb, x, None, None, None)
-        gate = None if w_inject is None else (2.0 * torch.sigmoid(du[:, R_:].float() * 0.25)).to(_BF)
         ctx.save_for_backward(h2, norm_w, wcat, w_up, rstd, zb, du, pre)
         ctx.shape, ctx.R, ctx.has_gate = (lead, G, H), R_, w_inject is not None
         return x.view(*lead, H), (gate.view(*lead, G) if gate is not None else None)
@@ -65,8 +70,8 @@ class _HCRead(torch.autograd.Function):
         ddu = torch.zeros_like(du, dtype=torch.float32)
         ddu[:, :R_] = ds.float() * sv * (1.0 + v * (1.0 - sv)) * 0.25
         if ctx.has_gate and dgate is not None:
-            sg = torch.sigmoid(du[:, R_:].float() * 0.25)
-            ddu[:, R_:] = dgate.reshape(rows, G).float() * 2.0 * sg * (1.0 - sg) * 0.25
+            sg = torch.sigmoid(du[:, R_:R_ + G].float() * 0.25)
+            ddu[:, R_:R_ + G] = dgate.reshape(rows, G).float() * 2.0 * sg * (1.0 - sg) * 0.25
         dzb += (ddu.to(_BF) @ wcat).float().view(rows, G, H)
         dh = torch.empty_like(h2)
         c.hc_norm(h2, norm_w, 0.0, dh, rstd, dzb, dh)

@@ -330,7 +330,12 @@ class StudentLayer(nn.Module):
         cos, sin = R.rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
         q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
         blkmap = self._qsa_blocks(x, positions, pack) if pack is not None else None
-        if pack is None:
+        if pack is None and q.is_cuda and q.dtype == torch.bfloat16 and D in (128, 256):
+            # unpacked rows are B segments of T tokens: the native varlen kernels
+            cu = torch.arange(B + 1, dtype=torch.int32) * T
+            o = packed_attention(q.reshape(B * T, *q.shape[2:]), k.reshape(B * T, *k.shape[2:]),
+                                 v.reshape(B * T, *v.shape[2:]), cu, T).reshape(B, T, -1)
+        elif pack is None:
             o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                                is_causal=True, enable_gqa=True).transpose(1, 2).reshape(B, T, -1)
         elif blkmap is not None:
