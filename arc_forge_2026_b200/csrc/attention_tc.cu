@@ -26,10 +26,11 @@
 // softmax warps turn each tile's (block, row mask) entries into a per-row 64-bit visibility mask (mask bit of the
 // row's verify position and causality), so the MMA side is the same in every mode.
 //
-// NVFP4 KV (kscale set; dense or 64-token QSA blocks): warps 2, 3, 6 and 7 read each page-head's e2m1 codes and e4m3
-// scales (0.5625 bytes per element) with plain 16-byte loads one tile ahead, dequantise them exactly to bf16 (a
-// 256-entry byte -> bf16-pair table, one bf16x2 multiply by the scale: e2m1 x e4m3 needs at most 5 significant
-// bits) and store the swizzled bf16 tiles the MMAs read, so NVFP4 moves 3.6x fewer bytes through the same pipeline.
+// NVFP4 KV (kscale set; dense or 64-token QSA blocks): warps 2, 3 and 6..11 read each page-head's e2m1 codes and e4m3
+// scales (0.5625 bytes per element) with plain 16-byte loads one tile ahead, dequantise them exactly to f16 (the
+// hardware e2m1x2 / e4m3x2 -> f16x2 conversions and one f16x2 multiply by the scale: e2m1 x e4m3 needs at most 5
+// significant bits) and store the swizzled f16 tiles the MMAs read; Q is converted to f16 in place and P is written
+// as f16, so the MMAs of this mode are f16 x f16 and NVFP4 moves 3.6x fewer bytes through the same pipeline.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -42,10 +43,14 @@ namespace afb {
 
 namespace attn_tc {
 constexpr int PAGE = 64;
-constexpr int THREADS = 256;
+constexpr int THREADS = 384;                   // warps 0..11 (8..11 work only in the NVFP4 mode)
 constexpr int W_LD = 0, W_MMA = 1, W_SM0 = 4;  // softmax warps 4 and 5
 constexpr float RESCALE = 8.f;                 // log2 growth of a row max that forces an O rescale
-constexpr int GATHER_THREADS = 128;            // warps 2, 3, 6, 7 in the sub-page gather and NVFP4 modes
+constexpr int GATHER_THREADS = 128;            // warps 2, 3, 6, 7 in the sub-page gather mode
+constexpr int CONV_THREADS = 256;              // warps 2, 3, 6, 7, 8..11 in the NVFP4 mode (every SM sub-partition)
+AFB_DEV int conv_index(int warp) {             // NVFP4 converter warp -> 0..7, or -1
+  return warp == 2 || warp == 3 ? warp - 2 : warp == 6 || warp == 7 ? warp - 4 : warp >= 8 && warp < 12 ? warp - 4 : -1;
+}
 
 template <int D>
 struct Smem {
@@ -58,10 +63,9 @@ struct Smem {
   static constexpr uint32_t KV_OFF = Q_BYTES;
   static constexpr uint32_t VIS_OFF = KV_OFF + NS * STAGE;    // sparse modes: per stage, per key, the verify
                                                               // positions (bits) that may see the key
-  static constexpr uint32_t LUT_OFF = VIS_OFF + NS * PAGE * 4;  // NVFP4: byte (two e2m1 codes) -> bf16 pair
-  static constexpr uint32_t BAR_OFF = LUT_OFF + 256 * 4;
-  // kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full[2], o_done[2], q_ready, mma_fin, tmem slot
-  static constexpr uint32_t TOTAL = BAR_OFF + (2 * NS + 10) * 8 + 16 + 1024;
+  static constexpr uint32_t BAR_OFF = VIS_OFF + NS * PAGE * 4;
+  // kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full[2], o_done[2], q_ready, mma_fin, q_conv, tmem slot
+  static constexpr uint32_t TOTAL = BAR_OFF + (2 * NS + 11) * 8 + 16 + 1024;
   // TMEM columns: O [D], S [2][64], P [2][32] (bf16 pairs)
   static constexpr uint32_t O_COL = 0, S_COL = D, P_COL = D + 2 * PAGE;
   static constexpr uint32_t TMEM_COLS = 512;
@@ -86,7 +90,8 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
   uint64_t* o_done = p_full + 2;
   uint64_t* q_ready = o_done + 2;
   uint64_t* mma_fin = q_ready + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_fin + 1);
+  uint64_t* q_conv = mma_fin + 1;  // NVFP4 mode: Q converted to f16 in place
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_conv + 1);
   uint32_t* vis_all = reinterpret_cast<uint32_t*>(smem + L::VIS_OFF);  // [NS][PAGE]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,7 +140,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&kv_full[s], (gather || fp4) ? GATHER_THREADS : 1);
+      mbar_init(&kv_full[s], fp4 ? CONV_THREADS : gather ? GATHER_THREADS : 1);
       mbar_init(&kv_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -145,6 +150,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       mbar_init(&o_done[b], 1);
     }
     mbar_init(q_ready, 1);
+    mbar_init(q_conv, CONV_THREADS);
     mbar_init(mma_fin, 1);
     fence_mbar_init();
   }
@@ -216,35 +222,44 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       mbar_wait(q_ready, 0, status);
       for (int i = max(0, issued - NS); i < issued; ++i) mbar_wait(&kv_full[i % NS], (i / NS) & 1, status);
     }
-  } else if (fp4 && (warp == 2 || warp == 3 || warp == 6 || warp == 7)) {
+  } else if (fp4 && conv_index(warp) >= 0) {
     // ------------------------------------------------------------------ NVFP4 dequantisation into the tiles
     // thread gt converts units of 32 elements (16 bytes of codes + 2 scales) of the K and V page-head: unit u of a
     // tile is row u / (D / 32), column group u % (D / 32). The next tile's codes and scales are loaded (plain
     // loads) before this tile's stage wait; a tile is published (this thread's proxy fence, then its arrive) as
     // soon as its stores are done.
     constexpr int UPR = D / 32;                 // 32-element units per row
-    constexpr int UPT = PAGE * UPR / GATHER_THREADS;  // units per thread per K (or V) tile
-    const int gw = (warp & 3) - 2 + (warp >> 2) * 2;
-    const int gt = gw * 32 + lane;
-    uint32_t* lut = reinterpret_cast<uint32_t*>(smem + L::LUT_OFF);
-    // bf16 of e2m1 code c: 0, 0.5, 1, 1.5, 2, 3, 4, 6 and their negatives
-    auto e2m1_bf16 = [](uint32_t c) -> uint32_t {
-      const uint32_t mag = c & 7u, e = mag >> 1, m = mag & 1u;
-      const uint32_t v = e ? (((e + 126u) << 7) | (m << 6)) : (m ? (126u << 7) : 0u);
-      return v | ((c & 8u) << 12);
-    };
-    for (int b = gt; b < 256; b += GATHER_THREADS) lut[b] = e2m1_bf16(b & 15u) | (e2m1_bf16(b >> 4) << 16);
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four converter warps: the table is complete
+    constexpr int UPT = PAGE * UPR / CONV_THREADS;  // units per thread per K (or V) tile
+    const int gt = conv_index(warp) * 32 + lane;
+    // Q to f16 in place (the MMAs of this mode take f16 operands: K / V dequantise exactly to f16 with the
+    // hardware e2m1 / e4m3 conversions; Q's bf16 values are exact in f16 at normalised magnitudes)
+    if (!mbar_wait(q_ready, 0, status)) ok = false;
+    for (int i = gt; i < (int)(L::Q_BYTES / 16); i += CONV_THREADS) {
+      uint4* p = reinterpret_cast<uint4*>(smem) + i;
+      uint4 v = *p;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+        w[j] = pack_f16x2(f.x, f.y);
+      }
+      *p = v;
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(q_conv);
     const uint8_t* kc = reinterpret_cast<const uint8_t*>(a.kcache);
     const uint8_t* vc = reinterpret_cast<const uint8_t*>(a.vcache);
     uint4 ck[UPT], cv[UPT];
     uint32_t sk[UPT], sv2[UPT];
+    // the page of tile i + 1 is read one iteration ahead, so a tile's code loads wait on no block-table load
+    int page_next = n > 0 ? bt[p0] : 0;
     auto fetch = [&](int i) {
       if (i >= n) return;
-      const size_t ph = (size_t)bt[p0 + i] * a.Hkv + kvh;  // page-head: 64 rows (union pages in QSA mode)
+      const size_t ph = (size_t)page_next * a.Hkv + kvh;  // page-head: 64 rows (union pages in QSA mode)
+      page_next = i + 1 < n ? bt[p0 + i + 1] : 0;
 #pragma unroll
       for (int u = 0; u < UPT; ++u) {
-        const int unit = u * GATHER_THREADS + gt, r = unit / UPR, cg = unit % UPR;
+        const int unit = u * CONV_THREADS + gt, r = unit / UPR, cg = unit % UPR;
         const size_t crow = (ph * PAGE + r) * (D / 2) + cg * 16, srow = (ph * PAGE + r) * (D / 16) + cg * 2;
         ck[u] = __ldg(reinterpret_cast<const uint4*>(kc + crow));
         cv[u] = __ldg(reinterpret_cast<const uint4*>(vc + crow));
@@ -252,25 +267,37 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
         sv2[u] = *reinterpret_cast<const uint16_t*>(a.vscale + srow);
       }
     };
-    auto scale_bf2 = [](uint32_t e4m3) -> __nv_bfloat162 {  // e4m3 byte -> (s, s) in bf16 (exact)
-      const __nv_fp8_e4m3 f = *reinterpret_cast<const __nv_fp8_e4m3*>(&e4m3);
-      const __nv_bfloat16 b = __float2bfloat16(float(f));
-      return __nv_bfloat162(b, b);
+    auto scale_h2 = [](uint32_t e4m3) -> uint32_t {  // e4m3 byte -> (s, s) in f16 (exact)
+      uint32_t d;
+      const uint16_t two = (uint16_t)(e4m3 | (e4m3 << 8));
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(two));
+      return d;
+    };
+    auto e2m1x2_h2 = [](uint32_t byte) -> uint32_t {  // two e2m1 codes (first in the low nibble) -> f16 pair
+      uint32_t d;
+      const uint16_t b = (uint16_t)byte;
+      asm("{\n\t.reg .b8 t;\n\tcvt.u8.u16 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(d) : "h"(b));
+      return d;
     };
     auto store_unit = [&](uint8_t* tile, int unit, const uint4& codes, uint32_t scales) {
       const int r = unit / UPR, cg = unit % UPR;
       const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {  // word q: 8 elements, chunk cg * 4 + q
-        const __nv_bfloat162 s2 = scale_bf2((scales >> (8 * (q >> 1))) & 0xffu);
+      for (int q = 0; q < 4; ++q) {
+        // step q stores word qq = (q + cg / 2) % 4 (8 elements, chunk cg * 4 + qq): the 8 lanes of a row then hit
+        // 8 different 16-byte positions of their 128-byte row, whichever sub-tile each lands in (no bank conflict
+        // beyond the four wavefronts a 16-byte store of 32 lanes needs)
+        const int qq = (q + (cg >> 1)) & 3;
+        const uint32_t wq = qq == 0 ? w[0] : qq == 1 ? w[1] : qq == 2 ? w[2] : w[3];
+        const uint32_t s2 = scale_h2((scales >> (8 * (qq >> 1))) & 0xffu);
         uint32_t o[4];
 #pragma unroll
         for (int bb = 0; bb < 4; ++bb) {
-          const uint32_t pr = lut[(w[q] >> (8 * bb)) & 0xffu];
-          const __nv_bfloat162 x = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&pr), s2);
+          const uint32_t pr = e2m1x2_h2((wq >> (8 * bb)) & 0xffu);
+          const __half2 x = __hmul2(*reinterpret_cast<const __half2*>(&pr), *reinterpret_cast<const __half2*>(&s2));
           o[bb] = *reinterpret_cast<const uint32_t*>(&x);
         }
-        const int c = cg * 4 + q;
+        const int c = cg * 4 + qq;
         const uint32_t so = (c >> 3) * L::SUB + r * 128 + (((c & 7) ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(tile + so) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -292,7 +319,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
         ok = false;
         break;
       }
-      if (sparse && gw == 0) {  // page union: the entry's positions and row mask (published by the arrive)
+      if (sparse && gt < 32) {  // page union: the entry's positions and row mask (published by the arrive)
         const int e = p0 + i, lp = spl[e];
         const uint32_t mk = spm[e];
 #pragma unroll
@@ -308,8 +335,8 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       uint8_t* st = smem + L::KV_OFF + s * L::STAGE;
 #pragma unroll
       for (int u = 0; u < UPT; ++u) {
-        store_unit(st, u * GATHER_THREADS + gt, ck0[u], sk0[u]);
-        store_unit(st + L::KV_BYTES, u * GATHER_THREADS + gt, cv0[u], sv0[u]);
+        store_unit(st, u * CONV_THREADS + gt, ck0[u], sk0[u]);
+        store_unit(st + L::KV_BYTES, u * CONV_THREADS + gt, cv0[u], sv0[u]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&kv_full[s]);
@@ -391,9 +418,10 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
     for (; published < issued; ++published) mbar_arrive(&kv_full[published % NS]);
   } else if (warp == W_MMA) {
     // ------------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc_s = idesc_f16(128, PAGE, 1);             // S = Q K^T
-    constexpr uint32_t idesc_o = idesc_f16(128, D, 1) | (1u << 16);   // O += P V, B (V) MN-major
-    ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0, status));
+    // bf16 operands; f16 in the NVFP4 mode (Q converted in place, K / V dequantised to f16, P written as f16)
+    const uint32_t idesc_s = idesc_f16(128, PAGE, fp4 ? 0 : 1);             // S = Q K^T
+    const uint32_t idesc_o = idesc_f16(128, D, fp4 ? 0 : 1) | (1u << 16);   // O += P V, B (V) MN-major
+    ok = __all_sync(0xffffffffu, mbar_wait(fp4 ? q_conv : q_ready, 0, status));
     tc_fence_after();
     const uint32_t q_base = smem_u32(smem);
     auto issue_pv = [&](int j) {  // page j: wait for its P, then O += P V
@@ -526,7 +554,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       for (int j = 0; j < PAGE / 2; ++j) {
         const float e0 = exp2f(sv[2 * j] - base), e1 = exp2f(sv[2 * j + 1] - base);
         rs += e0 + e1;
-        pk[j] = pack_bf16x2(e0, e1);
+        pk[j] = fp4 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
       }
       l += rs;
       // P of page i goes into P buffer sb; the PV of page i - 2 (which read that buffer) must be done
