@@ -507,6 +507,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
   if (waiting) {
     if (threadIdx.x == 0) {
       const uint64_t want = ew.expected[1] + 1;
+      const uint64_t tw0 = globaltimer_ns();
       for (int p = 0; p < ew.world; ++p) {
         const uint64_t* f = reinterpret_cast<const uint64_t*>(ew.peer[ew.rank] + ew.off_flags) + EP_MAX_RANKS + p;
         const uint64_t t0 = globaltimer_ns();
@@ -519,6 +520,8 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
           __nanosleep(64);
         }
       }
+      if (ew.wait_ns && blockIdx.x == 0 && blockIdx.y == 0)
+        atomicAdd(ew.wait_ns + 1, (unsigned long long)(globaltimer_ns() - tw0));
     }
     __syncthreads();
   }

@@ -322,6 +322,9 @@ struct EpArgs {
   // dispatch: this rank's per-expert entry lists from the router (cnt [E], list [E, T_cap], local entry indices)
   const int* lcnt = nullptr;
   const int* llist = nullptr;
+  // optional wait accounting: block 0 of the w13 GEMM adds its dispatch wait (ns) to wait_ns[0], block 0 of the
+  // combine its combine wait to wait_ns[1] (a per-layer slot of the caller's log)
+  unsigned long long* wait_ns = nullptr;
 };
 int ep_dispatch(const EpArgs& a, const void* x, int ldx, const int* ids, const float* weights, cudaStream_t st);
 int ep_wait(const EpArgs& a, int type, uint32_t* status, cudaStream_t st);

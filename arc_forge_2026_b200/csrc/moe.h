@@ -47,6 +47,7 @@ struct MoeGemmArgs {
   // PAIR under expert parallelism: wait (bounded) in the prologue until every source rank has published this
   // exchange's dispatch (flags [sources] in the local heap), then count it consumed (last CTA)
   const uint64_t* ep_wait_flags = nullptr;
+  unsigned long long* ep_wait_ns = nullptr;  // optional: block 0 adds its dispatch wait (ns) here
   unsigned long long* ep_expected = nullptr;
   unsigned* ep_wait_done = nullptr;
 };

@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
     fence_mbar_init();
     if (args.ep_wait_flags) {  // the routed rows of every source rank have landed in this rank's heap
       const uint64_t want = *args.ep_expected + 1;
+      const uint64_t tw0 = globaltimer_ns();
       for (int p = 0; p < args.route_srcs; ++p) {
         const uint64_t t0 = globaltimer_ns();
         uint32_t polls = 0;
@@ -233,6 +234,7 @@ __global__ void __launch_bounds__(moe::THREADS, 1)
           __nanosleep(64);
         }
       }
+      if (args.ep_wait_ns && blockIdx.x == 0) atomicAdd(args.ep_wait_ns, (unsigned long long)(globaltimer_ns() - tw0));
     }
   }
   if (warp == moe::W_MMA) tmem_alloc(tmem_slot, L::TMEM_COLS);

@@ -155,6 +155,10 @@ struct EpCtx {
     TORCH_CHECK(lcnt.numel() >= (int64_t)a.E_local * a.world && llist.dim() == 2 && llist.size(1) == a.T_cap &&
                     llist.is_contiguous(),
                 "ep dispatch lists: cnt [E], list [E, T_cap]");
+    if (slots > 0) {  // this layer's wait slot, used by the w13 GEMM and the combine that follow
+      slot = (slot + 1) % slots;
+      a.wait_ns = reinterpret_cast<unsigned long long*>(wait_log.data_ptr()) + 2 * slot;
+    }
     afb::EpArgs b = a;
     b.T = (int)T;
     b.lcnt = ptr<int>(lcnt);
@@ -162,6 +166,20 @@ struct EpCtx {
     check_rc(afb::ep_dispatch(b, x.data_ptr(), x.stride(0), ptr<int>(ids), ptr<float>(w), stream()), "ep_dispatch");
   }
   void wait(int64_t type) { check_rc(afb::ep_wait(a, (int)type, status_ptr(current_device()), stream()), "ep_wait"); }
+  // per-layer wait accounting: log int64 [slots, 2] (dispatch, combine ns, accumulated); begin_step() restarts the
+  // slot counter, each dispatch() moves to the next slot (under CUDA-graph capture every layer keeps its own slot)
+  at::Tensor wait_log;
+  int64_t slots = 0, slot = -1;
+  void set_wait_log(const at::Tensor& log) {
+    AFB_CHECK_DT(log, at::kLong);
+    AFB_CHECK_CONTIG(log);
+    TORCH_CHECK(log.dim() == 2 && log.size(1) == 2, "wait log is int64 [slots, 2]");
+    wait_log = log;
+    slots = log.size(0);
+    slot = -1;
+    a.wait_ns = nullptr;
+  }
+  void begin_step() { slot = -1; }
   // per-row e4m3 of the entry rows h [world * T_cap * k, I] that this rank's lists name
   void quant_routed(const at::Tensor& h, at::Tensor& q, at::Tensor& scales) {
     AFB_CHECK_DT(h, at::kBFloat16);
@@ -269,6 +287,7 @@ void moe_int3_gemm_op(const at::Tensor& codes, const at::Tensor& scales, const a
     if (ep_wait) {
       TORCH_CHECK(ep, "ep_wait needs the exchange context");
       a.ep_wait_flags = reinterpret_cast<const uint64_t*>(ep->a.peer[ep->a.rank] + ep->a.off_flags);  // dispatch
+      a.ep_wait_ns = ep->a.wait_ns;
       a.ep_expected = ep->a.expected;
       a.ep_wait_done = ep->a.wait_done;
       TORCH_CHECK(srcs == ep->a.world, "expert-parallel lists have one row per rank");
@@ -1411,7 +1430,9 @@ void register_kernel_ops(pybind11::module& m) {
       .def("dispatch", &EpCtx::dispatch)
       .def("wait", &EpCtx::wait)
       .def("quant_routed", &EpCtx::quant_routed)
-      .def("combine", &EpCtx::combine);
+      .def("combine", &EpCtx::combine)
+      .def("set_wait_log", &EpCtx::set_wait_log)
+      .def("begin_step", &EpCtx::begin_step);
   m.def("swiglu", &swiglu_op);
   m.def("int3_dequant", &int3_dequant_op);
   m.def("int3_scale_grad", &int3_scale_grad_op);

@@ -156,6 +156,7 @@ class HybridModel:
                 raise ValueError(f"layer holds {lw.bank.num_experts} experts, expected {c.num_experts} or {e1 - e0}")
         self.ep = ExpertParallel(world, rank, T_cap, c.hidden_size, c.num_experts_per_tok, c.num_experts,
                                  self.device, group)
+        self.ep.track_waits(c.num_layers)
         return self.ep
 
     # ------------------------------------------------------------------ construction
@@ -436,6 +437,8 @@ class HybridModel:
         the model has PLE layers."""
         c, cC = self.cfg, C()
         N, H = b.num_tokens, c.hidden_size
+        if self.ep is not None:
+            self.ep.ctx.begin_step()  # per-layer wait slots restart with the stack
         h = ws.h[:N]
         cC.embedding(b.ids, self.embed, h)
         y = ws.y[:N]

@@ -100,6 +100,15 @@ class ExpertParallel:
         self.wait_done = torch.zeros(2, dtype=torch.int32, device=dev)
         self.ctx = ext.EpCtx(world, rank, T_cap, H, k, self.E_local, list(self.heap.peers()), self.offsets, self.ld_s,
                              self.done, self.sent, self.expected, self.wait_done)
+        self.wait_log = None
+
+    def track_waits(self, layers: int):
+        """Accumulate, per MoE layer, the nanoseconds this rank's w13 GEMM waited for the dispatch exchange and its
+        combine waited for the combine exchange (block 0 of each kernel; ``wait_log`` int64 [layers, 2]). The
+        model's forward restarts the layer count (``ctx.begin_step``); zero the log to start a measurement."""
+        self.wait_log = torch.zeros(layers, 2, dtype=torch.int64, device=self.done.device)
+        self.ctx.set_wait_log(self.wait_log)
+        return self.wait_log
 
     def close(self):
         if self.heap is not None:

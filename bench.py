@@ -107,6 +107,35 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
+def ep_wait_summary(wait_log, steps: int, world: int, rank: int):
+    """Per-rank expert-parallel wait accounting of the timed cycles (every rank takes part in the gather; rank 0
+    gets the summary): how long each rank's w13 GEMM waited for the dispatch exchange and its combine for the combine
+    exchange, per cycle, and the distribution of the per-(rank, layer) waits."""
+    import torch
+    import torch.distributed as dist
+    allw = [torch.zeros_like(wait_log) for _ in range(world)]
+    dist.all_gather(allw, wait_log)
+    if rank != 0:
+        return None
+    w = torch.stack(allw).double().cpu() / max(steps, 1) / 1e3  # [world, layers, 2] microseconds per cycle
+    edges = [0, 10, 25, 50, 100, 200, 500, float("inf")]
+
+    def hist(x):
+        x = x.flatten()
+        return {f"{lo:g}-{hi:g}us" if hi != float("inf") else f">{lo:g}us": int(((x >= lo) & (x < hi)).sum())
+                for lo, hi in zip(edges[:-1], edges[1:])}
+
+    def q(x, p):
+        return round(float(torch.quantile(x.flatten(), p)), 1)
+    return {"per_rank_ms_per_cycle": {"dispatch": [round(float(v), 3) for v in w[:, :, 0].sum(1) / 1e3],
+                                      "combine": [round(float(v), 3) for v in w[:, :, 1].sum(1) / 1e3]},
+            "per_layer_us": {"dispatch": {"p50": q(w[:, :, 0], 0.5), "p90": q(w[:, :, 0], 0.9),
+                                          "max": q(w[:, :, 0], 1.0), "hist": hist(w[:, :, 0])},
+                             "combine": {"p50": q(w[:, :, 1], 0.5), "p90": q(w[:, :, 1], 0.9),
+                                         "max": q(w[:, :, 1], 1.0), "hist": hist(w[:, :, 1])}},
+            "note": "block 0 of each w13 GEMM / combine kernel, wall time from entering its wait to the last flag"}
+
+
 def count_launches(fn, census_out=None, time_out=None):
     """Kernels of this repository launched by one call of ``fn`` (kernel list from the profiler's trace; used
     only for counting, never for timing)."""
@@ -303,6 +332,10 @@ def main():
     barrier()
     torch.cuda.synchronize()
     total0 = int(eng.total.item())
+    wait_log = model.ep.wait_log if (world > 1 and model.ep is not None) else None
+    if wait_log is not None:
+        wait_log.zero_()
+        torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         ev[0].record()
         for i in range(args.steps):
@@ -314,6 +347,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     ms = ev[0].elapsed_time(ev[-1])
+    ep_waits = ep_wait_summary(wait_log, args.steps, world, rank) if wait_log is not None else None
     cyc_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
     emitted = int(eng.total.item()) - total0
     check_status()
@@ -391,6 +425,7 @@ def main():
                    "decode_span": f"timed cycles in {G} groups at context + {offsets} of {args.out_tokens} output "
                                   f"tokens"},
         "p50_tpot_ms": round(p50, 3) if p50 else None,
+        "ep_waits": ep_waits,
         "cycle_ms": round(ms / args.steps, 3),
         "reference_cycle_ms": 41.0 if anchor else None,  # paper App. E.11 (p. 85): ~41 ms per cycle on one B200
         "accepted_per_cycle": round(emitted / (args.steps * S_total), 3),
