@@ -21,7 +21,7 @@
 //
 // QSA sparse modes (sp_count set): the CTA walks its sequence's block union instead of its pages. With 64-token
 // blocks an entry is a page (the TMA loader reads the union's physical pages); with smaller blocks (4 for the
-// reference's QSA) warps 2, 3, 6 and 7 gather 64 / B entries into each 64-key tile with 16-byte cp.async copies
+// reference's QSA) warps 2, 3 and 6..11 gather 64 / B entries into each 64-key tile with 16-byte cp.async copies
 // written at the 128-byte-swizzled offsets the TMA would use, a proxy fence per thread before its arrive. The
 // softmax warps turn each tile's (block, row mask) entries into a per-row 64-bit visibility mask (mask bit of the
 // row's verify position and causality), so the MMA side is the same in every mode.
@@ -46,9 +46,9 @@ constexpr int PAGE = 64;
 constexpr int THREADS = 384;                   // warps 0..11 (8..11 work only in the NVFP4 mode)
 constexpr int W_LD = 0, W_MMA = 1, W_SM0 = 4;  // softmax warps 4 and 5
 constexpr float RESCALE = 8.f;                 // log2 growth of a row max that forces an O rescale
-constexpr int GATHER_THREADS = 128;            // warps 2, 3, 6, 7 in the sub-page gather mode
+constexpr int GATHER_THREADS = 256;            // warps 2, 3, 6..11 in the sub-page gather mode
 constexpr int CONV_THREADS = 256;              // warps 2, 3, 6, 7, 8..11 in the NVFP4 mode (every SM sub-partition)
-AFB_DEV int conv_index(int warp) {             // NVFP4 converter warp -> 0..7, or -1
+AFB_DEV int conv_index(int warp) {             // gather / NVFP4 converter warp -> 0..7, or -1
   return warp == 2 || warp == 3 ? warp - 2 : warp == 6 || warp == 7 ? warp - 4 : warp >= 8 && warp < 12 ? warp - 4 : -1;
 }
 
@@ -115,7 +115,9 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
   const int ept = PAGE / spb;                       // entries per tile
   const int cnt = sparse ? a.sp_count[seq] : 0;
   const int npages = sparse ? (cnt + ept - 1) / ept : (seq_len + PAGE - 1) / PAGE;  // 64-key tiles
-  const int p0 = split * a.pages_per_split;
+  // sliding window (dense mode): the first page any row of the CTA can see
+  const int pbeg = (!sparse && a.window > 0) ? max(0, past + 1 - a.window) / PAGE : 0;
+  const int p0 = pbeg + split * a.pages_per_split;
   const int p1 = min(npages, p0 + a.pages_per_split);
   const int n = max(0, p1 - p0);
   const int* bt = a.block_table + (size_t)(a.bt_row ? a.bt_row[seq] : seq) * a.max_pages;
@@ -341,7 +343,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(&kv_full[s]);
     }
-  } else if (gather && (warp == 2 || warp == 3 || warp == 6 || warp == 7)) {
+  } else if (gather && conv_index(warp) >= 0) {
     // ------------------------------------------------------------------ sub-page gather (QSA blocks < 64 tokens)
     // One 16-byte chunk per thread and copy: the 128 threads walk the tile's 64 rows x D/8 chunks chunk-fastest,
     // so a warp's copy covers whole contiguous rows (512 or 256 bytes). Lane l resolves keys l and l + 32 (KV slot,
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
     constexpr int CH = D / 8;  // 16-byte chunks per row
     constexpr int ITERS = PAGE * CH / GATHER_THREADS;
     constexpr int LAG = NS - 1;
-    const int gw = (warp & 3) - 2 + (warp >> 2) * 2;  // warps 2, 3, 6, 7 -> 0..3
+    const int gw = conv_index(warp);  // warps 2, 3, 6..11 -> 0..7
     const int gt = gw * 32 + lane;
     auto resolve = [&](int i, int (&slot)[2], uint32_t (&vb)[2]) {
 #pragma unroll
@@ -517,7 +519,8 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < PAGE; ++j) {
-        const bool see = sparse ? (((j < 32 ? vlo >> j : vhi >> (j - 32)) & 1u) != 0) : kbase + j < vis;
+        const bool see = sparse ? (((j < 32 ? vlo >> j : vhi >> (j - 32)) & 1u) != 0)
+                                : kbase + j < vis && (a.window <= 0 || kbase + j >= vis - a.window);
         const float x = (live && see) ? sv[j] * a.scale_log2 : -INFINITY;
         sv[j] = x;
         mx = fmaxf(mx, x);
@@ -648,10 +651,12 @@ static int launch_attn_tc(const AttnArgs& a, int splits, uint32_t* status, cudaS
   return (int)cudaGetLastError();
 }
 
-// The tcgen05 path serves bf16 decode / verify and prefill rows, dense or over a QSA block union (no window);
+// The tcgen05 path serves bf16 decode / verify and prefill rows, dense (optionally a sliding window) or over a QSA
+// block union, and NVFP4 KV dense or over a page union;
 // returns -1 when the call is outside that set (the caller runs the mma.sync kernel), else the launch result.
 int paged_attention_tc(const AttnArgs& a, int splits, uint32_t* status, cudaStream_t st) {
-  if (a.impl == 1 || a.window > 0 || a.Hq / a.Hkv > 64) return -1;
+  if (a.impl == 1 || a.Hq / a.Hkv > 64) return -1;
+  if (a.window > 0 && (a.sp_count || a.kscale)) return -1;  // windows: dense bf16 only
   if (a.kscale && (!a.vscale || (a.sp_count && a.sp_block != attn_tc::PAGE))) return -1;
   if (a.bt_row && a.sp_count && a.sp_block == attn_tc::PAGE) return -1;  // page unions are per sequence
   if (a.sp_count && (a.q_per_seq > 8 || a.sp_block < 1 || attn_tc::PAGE % a.sp_block)) return -1;
