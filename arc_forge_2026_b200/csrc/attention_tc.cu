@@ -34,6 +34,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <climits>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -478,6 +479,7 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
     const int t = tbase + r / group, hq = r % group;  // verify position (0 .. q_per_seq - 1) and head
     const bool live = r < QR;
     const int vis = past + t + 1;  // keys this row may see: positions < vis
+    const int win_lo = a.window > 0 ? vis - a.window : INT_MIN / 2;  // and >= win_lo (sliding window)
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     float m = -INFINITY, l = 0.f;
     for (int i = 0; i < n; ++i) {
@@ -515,12 +517,13 @@ __global__ void __launch_bounds__(attn_tc::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
+      // the page's visible key range, relative to its first key (hoisted: one compare pair per key)
       const int kbase = (p0 + i) * PAGE;
+      const int j_hi = vis - kbase, j_lo = win_lo - kbase;
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < PAGE; ++j) {
-        const bool see = sparse ? (((j < 32 ? vlo >> j : vhi >> (j - 32)) & 1u) != 0)
-                                : kbase + j < vis && (a.window <= 0 || kbase + j >= vis - a.window);
+        const bool see = sparse ? (((j < 32 ? vlo >> j : vhi >> (j - 32)) & 1u) != 0) : (j < j_hi && j >= j_lo);
         const float x = (live && see) ? sv[j] * a.scale_log2 : -INFINITY;
         sv[j] = x;
         mx = fmaxf(mx, x);
