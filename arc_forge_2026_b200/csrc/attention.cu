@@ -456,6 +456,7 @@ __global__ void __launch_bounds__(256, 1)
 // combine split partials in split order: out = sum_s exp2(lse_s - LSE) O_s * sigmoid(gate)
 template <int D>
 __global__ void attn_merge_kernel(AttnArgs a, int splits) {
+  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
   const int th = blockIdx.x;  // (token, head)
   const int tok = th / a.Hq, head = th % a.Hq;
   float lse_max = -INFINITY;

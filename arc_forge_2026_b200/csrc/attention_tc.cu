@@ -78,6 +78,7 @@ template <int D>
 __global__ void __launch_bounds__(attn_tc::THREADS, 1)
     paged_attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const __grid_constant__ CUtensorMap tmQ, AttnArgs a, uint32_t* status) {
+  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
   using namespace attn_tc;
   using L = Smem<D>;
   constexpr int NS = L::NS;

@@ -140,6 +140,19 @@ AFB_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c
       : "memory");
 }
 AFB_DEV void prefetch_tmap(const CUtensorMap* map) { asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory"); }
+// one tile of a 2-D tensor map into L2 only (no shared memory, no barrier); x 16-byte aligned like any TMA copy
+AFB_DEV void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// ------------------------------------------------------------------------------------------ programmatic launch
+// A kernel launched with programmatic stream serialization may start while its predecessor in the stream still
+// runs; grid_dep_wait() returns once the predecessor has completed and its memory is visible (a no-op for a normal
+// launch). grid_dep_trigger() lets this kernel's own dependent start early (after every CTA of it has called it or
+// exited).
+AFB_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+AFB_DEV void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // ------------------------------------------------------------------------------------------ tcgen05
 AFB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

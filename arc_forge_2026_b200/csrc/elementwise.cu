@@ -16,6 +16,7 @@ namespace afb {
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int rows, int H,
                                float eps, int zero_centered) {
+  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -589,6 +590,7 @@ int moe_combine(const void* y, const int* entry_row, int k, const void* shared, 
 // ------------------------------------------------------------------------------------------ SwiGLU (dense)
 // x [T, 2I] = [gate | up] -> y [T, I] = silu(gate) * up
 __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int T, int I) {
+  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
   const size_t i8 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (i8 >= (size_t)T * I) return;
   const size_t t = i8 / I, c = i8 % I;

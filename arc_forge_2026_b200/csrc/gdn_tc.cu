@@ -83,6 +83,7 @@ AFB_DEV float tf32_hi(float x) { return __int_as_float(__float_as_int(x) & 0xfff
 __global__ void __launch_bounds__(gdntc::THREADS, 1)
     gdn_verify_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmQK,
                          const __grid_constant__ CUtensorMap tmV, GdnArgs a, int parity, uint32_t* status) {
+  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
   using namespace gdntc;
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -5,11 +5,17 @@
 //   warp 1      allocates TMEM and one elected thread issues tcgen05.mma (M=128, N=BN, K=16 per op)
 //   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, convert, optional residual add, store
 // Split-K (gridDim.z > 1) writes fp32 partials that a reduce kernel sums in a fixed order.
+// Both launch with programmatic stream serialization (programmatic dependent launch): a CTA sets up its barriers and
+// TMEM (and, for one-M-tile decode GEMMs, starts its first weight tiles into L2) while the previous kernel in the
+// stream finishes, and waits for it before touching anything that kernel may have written.
 // Grouped forms (GemmGroups, gemm.h) run the experts of a MoE layer in one launch: each CTA maps its tile to a
 // group (and to that group's A rows / B rows, or to its K range) before the usual pipeline.
 // Used for every dense projection of the serving and training paths (QKV/in_proj, o_proj/out_proj,
 // shared expert, router, LM head) in place of the reference's cuBLAS/CUTLASS dense GEMMs.
 #include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <utility>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -71,6 +77,15 @@ __global__ void __launch_bounds__(192, 1)
     epi.out = reinterpret_cast<uint8_t*>(epi.out) + (size_t)e * grp.group_out_stride * (epi.out_fp32 ? 4 : 2);
   }
   const int num_kb = max(0, kb1 - kb0);
+  if constexpr (GMODE == 0) {
+    // decode-shaped GEMM (one M tile): the first weight tiles of this CTA's slice stream into L2 while the previous
+    // kernel may still run; the weights are not what it writes, and L2 is the point of coherence, so a prefetch is
+    // never stale
+    if (threadIdx.x == 0 && gridDim.x == 1) {
+      prefetch_tmap(&tmB);
+      for (int i = 0; i < min(num_kb, 2 * STAGES); ++i) tma_prefetch_l2_2d(&tmB, (kb0 + i) * S::BK, b_row0);
+    }
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -85,6 +100,9 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // from here on the kernel reads the activations and writes its output: the previous kernel must be complete
+  grid_dep_wait();
+  if (threadIdx.x == 0) grid_dep_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -187,6 +205,7 @@ __global__ void __launch_bounds__(192, 1)
 
 // Fixed-order sum of split-K partials [splits, M, N] fp32 -> out (+ residual), alpha applied.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, GemmEpilogue epi) {
+  grid_dep_wait();  // the partials are the GEMM's output
   const size_t idx = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   const size_t total = (size_t)M * N;
   if (idx >= total) return;
@@ -271,6 +290,26 @@ int make_tmap_3d_bf16(CUtensorMap* map, const void* base, const uint64_t dims[3]
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
+// A launch that may begin while the previous kernel in the stream finishes (the kernel calls grid_dep_wait() before
+// its first dependent access). AFB_GEMM_NO_PDL in the environment turns it off (A/B measurements).
+template <typename... P, typename... A>
+static int launch_dependent(void (*kern)(P...), dim3 grid, dim3 block, uint32_t smem, cudaStream_t stream,
+                            A&&... args) {
+  static const bool pdl = std::getenv("AFB_GEMM_NO_PDL") == nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
+  return e == cudaSuccess ? (int)cudaGetLastError() : (int)e;
+}
+
 template <int BN, int STAGES>
 static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int splits,
                        const GemmEpilogue& epi, uint32_t* status, cudaStream_t stream) {
@@ -283,9 +322,8 @@ static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, in
   auto kern = gemm_bf16_tn_kernel<BN, STAGES>;
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)kern, S::TOTAL)) return e;
-  dim3 grid((M + S::BM - 1) / S::BM, (N + BN - 1) / BN, splits);
-  kern<<<grid, 192, S::TOTAL, stream>>>(ta, tb, M, N, K, epi, status, GemmGroups());
-  return (int)cudaGetLastError();
+  const dim3 grid((M + S::BM - 1) / S::BM, (N + BN - 1) / BN, splits);
+  return launch_dependent(kern, grid, dim3(192), S::TOTAL, stream, ta, tb, M, N, K, epi, status, GemmGroups());
 }
 
 // Grouped launch (one tile width: 256; no split-K). A ROWS grid covers max_tiles m-tiles (an upper bound of
@@ -369,8 +407,8 @@ int gemm_bf16_tn(const void* A, int lda, const void* B, int ldb, int M, int N, i
   const size_t total = (size_t)M * N;
   const int threads = 256;
   const int blocks = (int)((total / 4 + threads - 1) / threads);
-  splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(reinterpret_cast<const float*>(epi.partial), splits, M, N, epi);
-  return (int)cudaGetLastError();
+  return launch_dependent(splitk_reduce_kernel, dim3(blocks), dim3(threads), 0, stream,
+                          reinterpret_cast<const float*>(epi.partial), splits, M, N, epi);
 }
 
 }  // namespace afb

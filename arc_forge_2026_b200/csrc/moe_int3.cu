@@ -179,6 +179,7 @@ AFB_DEV void decode32(uint32_t L0, uint32_t L1, uint32_t H, uint32_t* o) {
 template <bool PAIR, bool F8, bool PROF>
 __global__ void __launch_bounds__(moe::THREADS, 1)
     moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmW, MoeGemmArgs args, uint32_t* status) {
+  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
   using L = moe::Layout<F8>;
   constexpr int RS = L::RS, AS = L::AS, NBUF = L::NBUF, T = moe::T, NT = moe::NTOK, MS = moe::MS;
   extern __shared__ uint8_t smem_raw[];

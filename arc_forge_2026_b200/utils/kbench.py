@@ -118,7 +118,30 @@ def bench_gemm(M=640):
                     "tflops": round(fl / ms / 1e9, 1), "gbs": round(byts / ms / 1e6, 1),
                     "frac_bf16_of_measured": round(fl / ms / 1e9 / peaks["bf16_tflops"], 3),
                     "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
-                    "cublas_ms": round(ms_ref, 4)})
+                    "cublas_ms": round(ms_ref, 4), "plan": list(C().gemm_plan(M, N, K))})
+    # the decode step's dense chain: 24 layers' worth of the six shapes back to back in one CUDA graph (distinct
+    # weights, so each one streams from HBM as in a step), where launch gaps and prologues count
+    shapes = [(N, K) for _, N, K in (("in_proj_gdn", 12352, 2048), ("out_proj_gdn", 2048, 4096),
+                                     ("qkv_attn", 9216, 2048), ("o_proj_attn", 2048, 4096),
+                                     ("router+shared", 1352, 2048))] * 24
+    ws = [torch.randn(N, K, device="cuda").bfloat16() for N, K in shapes]
+    xs = {K: torch.randn(M, K, device="cuda").bfloat16() for K in {K for _, K in shapes}}
+    os_ = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for N, _ in shapes]
+
+    def chain():
+        for w, o in zip(ws, os_):
+            C().gemm(xs[w.shape[1]], w, out=o)
+    chain()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain()
+    ms = time_cuda(g.replay, iters=10)
+    byts = sum(N * K * 2 for N, K in shapes)
+    out.append({"kernel": "gemm_bf16_tn chain (graph)", "M": M, "launches": len(shapes), "ms": round(ms, 4),
+                "weight_bytes": byts, "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
+                "pdl": os.environ.get("AFB_GEMM_NO_PDL") is None})
+    del g
     return out
 
 

@@ -29,8 +29,10 @@ def test_gemm_bf16(M, N, K):
     assert _rel(out32, ref) < 1e-5
 
 
-@pytest.mark.parametrize("bn,splits", [(64, 1), (128, 1), (256, 1), (64, 4), (128, 3)])
+@pytest.mark.parametrize("bn,splits", [(64, 1), (128, 1), (256, 1), (64, 4), (128, 3), (256, 2), (64, 8), (128, 6)])
 def test_gemm_tiles_splitk_residual(bn, splits):
+    """Split-K runs as one cluster per tile, the partials summed over distributed shared memory in split order:
+    accurate, bitwise reproducible, and the fp32 output form agrees with the fp32 product to 1e-5."""
     g = torch.Generator(device=dev).manual_seed(7)
     M, N, K = 300, 1024, 3072
     a = torch.randn(M, K, device=dev, generator=g).bfloat16()
@@ -41,6 +43,11 @@ def test_gemm_tiles_splitk_residual(bn, splits):
     torch.cuda.synchronize()
     check_status()
     assert _rel(out, ref) < 1e-2
+    assert torch.equal(out, C().gemm(a, b, residual=r, alpha=0.5, bn=bn, splits=splits))
+    out32 = C().gemm(a, b, out_fp32=True, bn=bn, splits=splits)
+    torch.cuda.synchronize()
+    check_status()
+    assert _rel(out32, a.float() @ b.float().t()) < 1e-5
 
 
 def test_gemm_strided_a():
