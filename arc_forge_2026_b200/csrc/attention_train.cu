@@ -135,7 +135,9 @@ __global__ void __launch_bounds__(attn_tr::THREADS, 1)
   const int2 tl = a.tiles[blockIdx.y];
   const int s0 = a.cu[tl.x], Lseg = a.cu[tl.x + 1] - s0, q0 = tl.y;
   const int QR = min(L::QT, Lseg - q0);
-  const int n = (q0 + QR + TILE - 1) / TILE;  // causal: key tiles 0 .. n-1
+  // key tiles 0 .. n-1: up to the last query row (causal) or the whole segment (bidirectional)
+  const int n = ((a.causal ? q0 + QR : Lseg) + TILE - 1) / TILE;
+  const int klim_off = a.causal ? 0 : Lseg;  // bidirectional: keys below the segment end, whatever the row
   if (QR <= 0) return;
 
   if (threadIdx.x == 0) {
@@ -238,6 +240,7 @@ __global__ void __launch_bounds__(attn_tr::THREADS, 1)
     const int r = quad * 32 + lane;
     const bool live = r < QR;
     const int qpos = q0 + r;
+    const int kmax = klim_off ? klim_off - 1 : qpos;  // last visible key position
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     float m = -INFINITY, l = 0.f;
     for (int i = 0; i < n; ++i) {
@@ -259,7 +262,7 @@ __global__ void __launch_bounds__(attn_tr::THREADS, 1)
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < TILE; ++j) {
-        const float x = (live && kbase + j <= qpos && ((km >> j) & 1ull)) ? sv[j] * a.scale_log2 : -INFINITY;
+        const float x = (live && kbase + j <= kmax && ((km >> j) & 1ull)) ? sv[j] * a.scale_log2 : -INFINITY;
         sv[j] = x;
         mx = fmaxf(mx, x);
       }
@@ -913,6 +916,7 @@ static int launch_fwd(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st)
 // a.tiles: 128-position query tiles (the backward's are 64-position tiles)
 int attn_train_fwd(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st) {
   if (const int e = check_args(a)) return e;
+  if (!a.causal && a.blkmap) return 3;  // QSA maps are causal selections
   if (a.ntiles == 0) return 0;
   return a.D == 256 ? launch_fwd<256>(a, status, st) : launch_fwd<128>(a, status, st);
 }

@@ -454,9 +454,10 @@ static void train_attn_qsa(afb::AttnTrainArgs& a, const c10::optional<at::Tensor
 
 void attn_train_fwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
                        const at::Tensor& tiles, double scale, at::Tensor& out, at::Tensor& lse,
-                       c10::optional<at::Tensor> blkmap, int64_t qsa_block) {
+                       c10::optional<at::Tensor> blkmap, int64_t qsa_block, bool causal) {
   afb::AttnTrainArgs a = train_attn_args(q, k, v, cu, tiles, scale);
   train_attn_qsa(a, blkmap, qsa_block);
+  a.causal = causal ? 1 : 0;
   AFB_CHECK_CONTIG(out);
   TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16, "out is bf16 like q");
   AFB_CHECK_DT(lse, at::kFloat);
@@ -464,6 +465,82 @@ void attn_train_fwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.lse = ptr<float>(lse);
   check_rc(afb::attn_train_fwd(a, status_ptr(q.get_device()), stream()), "attn_train_fwd");
+}
+
+// ------------------------------------------------------------------------------------------ vision tower
+static const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+void vit_patch_pos_op(const at::Tensor& acc, const at::Tensor& bias, const at::Tensor& table, const at::Tensor& idx,
+                      const at::Tensor& wts, at::Tensor& h) {
+  AFB_CHECK_DT(acc, at::kFloat);
+  AFB_CHECK_CONTIG(acc);
+  AFB_CHECK_DT(idx, at::kInt);
+  AFB_CHECK_CONTIG(idx);
+  AFB_CHECK_DT(wts, at::kBFloat16);
+  AFB_CHECK_DT(table, at::kBFloat16);
+  AFB_CHECK_DT(h, at::kBFloat16);
+  AFB_CHECK_CONTIG(h);
+  const int P = acc.size(0), C = acc.size(1);
+  TORCH_CHECK(h.size(0) == P && h.size(1) == C && idx.numel() == 4 * P && wts.numel() == 4 * P &&
+                  table.size(1) == C && bias.numel() == C,
+              "vit_patch_pos shapes");
+  check_rc(afb::vit_patch_pos(ptr<float>(acc), bias.data_ptr(), table.data_ptr(), ptr<int>(idx), wts.data_ptr(),
+                              h.data_ptr(), P, C, stream()),
+           "vit_patch_pos");
+}
+
+void vit_qkv_rope_op(const at::Tensor& acc, const at::Tensor& bias, const at::Tensor& cosv, const at::Tensor& sinv,
+                     int64_t H, int64_t Dh, at::Tensor& q, at::Tensor& k, at::Tensor& v) {
+  AFB_CHECK_DT(acc, at::kFloat);
+  AFB_CHECK_CONTIG(acc);
+  AFB_CHECK_DT(cosv, at::kFloat);
+  AFB_CHECK_DT(sinv, at::kFloat);
+  AFB_CHECK_CONTIG(cosv);
+  AFB_CHECK_CONTIG(sinv);
+  for (const at::Tensor* t : {&q, &k, &v}) {
+    AFB_CHECK_DT((*t), at::kBFloat16);
+    AFB_CHECK_CONTIG((*t));
+  }
+  const int P = acc.size(0), Dp = q.size(2);
+  TORCH_CHECK(acc.size(1) == 3 * H * Dh && bias.numel() == 3 * H * Dh && q.size(0) == P && q.size(1) == H &&
+                  k.sizes() == q.sizes() && v.sizes() == q.sizes() && cosv.numel() == (int64_t)P * (Dh / 2) &&
+                  sinv.numel() == cosv.numel(),
+              "vit_qkv_rope shapes");
+  check_rc(afb::vit_qkv_rope(ptr<float>(acc), bias.data_ptr(), ptr<float>(cosv), ptr<float>(sinv), P, (int)H, (int)Dh,
+                             Dp, q.data_ptr(), k.data_ptr(), v.data_ptr(), stream()),
+           "vit_qkv_rope");
+}
+
+void vit_residual_ln_op(c10::optional<at::Tensor> acc, c10::optional<at::Tensor> bias, at::Tensor& h,
+                        c10::optional<at::Tensor> w, c10::optional<at::Tensor> b, double eps,
+                        c10::optional<at::Tensor> y) {
+  AFB_CHECK_DT(h, at::kBFloat16);
+  AFB_CHECK_CONTIG(h);
+  const int rows = h.size(0), C = h.size(1);
+  if (acc.has_value()) {
+    AFB_CHECK_DT((*acc), at::kFloat);
+    AFB_CHECK_CONTIG((*acc));
+    TORCH_CHECK(acc->sizes() == h.sizes(), "vit_residual_ln: acc shape");
+  }
+  if (y.has_value()) {
+    AFB_CHECK_CONTIG((*y));
+    TORCH_CHECK(y->sizes() == h.sizes() && w.has_value() && b.has_value() && w->numel() == C && b->numel() == C,
+                "vit_residual_ln: y / norm shapes");
+  }
+  check_rc(afb::vit_residual_ln(acc.has_value() ? ptr<float>(*acc) : nullptr, opt_ptr(bias), h.data_ptr(), opt_ptr(w),
+                                opt_ptr(b), (float)eps, y.has_value() ? y->data_ptr() : nullptr, rows, C, stream()),
+           "vit_residual_ln");
+}
+
+void vit_bias_act_op(const at::Tensor& acc, const at::Tensor& bias, at::Tensor& y, int64_t act) {
+  AFB_CHECK_DT(acc, at::kFloat);
+  AFB_CHECK_CONTIG(acc);
+  AFB_CHECK_DT(y, at::kBFloat16);
+  AFB_CHECK_CONTIG(y);
+  TORCH_CHECK(y.sizes() == acc.sizes() && bias.numel() == acc.size(1), "vit_bias_act shapes");
+  check_rc(afb::vit_bias_act(ptr<float>(acc), bias.data_ptr(), y.data_ptr(), acc.size(0), acc.size(1), (int)act,
+                             stream()),
+           "vit_bias_act");
 }
 
 void attn_train_bwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
@@ -1478,7 +1555,12 @@ void register_kernel_ops(pybind11::module& m) {
   m.def("qsa_prep", &qsa_prep_op);
   m.def("attn_train_fwd", &attn_train_fwd_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu"),
         py::arg("tiles"), py::arg("scale"), py::arg("out"), py::arg("lse"), py::arg("blkmap") = py::none(),
-        py::arg("qsa_block") = 64);
+        py::arg("qsa_block") = 64, py::arg("causal") = true);
+  m.def("vit_patch_pos", &vit_patch_pos_op);
+  m.def("vit_qkv_rope", &vit_qkv_rope_op);
+  m.def("vit_residual_ln", &vit_residual_ln_op, py::arg("acc"), py::arg("bias"), py::arg("h"), py::arg("w"),
+        py::arg("b"), py::arg("eps"), py::arg("y"));
+  m.def("vit_bias_act", &vit_bias_act_op);
   m.def("attn_train_bwd", &attn_train_bwd_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu"),
         py::arg("tiles"), py::arg("kv_tiles"), py::arg("scale"), py::arg("out"), py::arg("lse"), py::arg("dout"),
         py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dk_part"), py::arg("dv_part"),

@@ -5,6 +5,7 @@
     python -m arc_forge_2026_b200.utils.kbench gdn_scan # chunked-GDN inter-chunk scan at the QAD shape
     python -m arc_forge_2026_b200.utils.kbench gdn_train # chunked-GDN layer forward + backward at the QAD shape
     python -m arc_forge_2026_b200.utils.kbench qsa      # QSA selection + sparse verify attention (block 4 and 64)
+    python -m arc_forge_2026_b200.utils.kbench vision   # the 27-block vision tower beside the HF bf16 model
 
 Prints one JSON line per kernel: time, bytes, FLOPs and the fraction of MEASURED_PEAKS.json.
 """
@@ -142,6 +143,39 @@ def bench_gemm(M=640):
                 "weight_bytes": byts, "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
                 "pdl": os.environ.get("AFB_GEMM_NO_PDL") is None})
     del g
+    return out
+
+
+def bench_vision(grids=((1, 64, 64), (1, 32, 48)), depth=27, seed=0):
+    """The vision tower (full width, 27 blocks, random weights) on one batch of images: the native path (tcgen05 GEMMs,
+    bidirectional tcgen05 attention, csrc/vision.cu) beside Hugging Face's bf16 Qwen3-VL vision model (SDPA) with the
+    same weights on the same inputs."""
+    from ..models.vision import VisionConfig, VisionTower
+    cfg = VisionConfig(depth=depth)
+    P = sum(t * h * w for t, h, w in grids)
+    pixels = torch.randn(P, cfg.patch_dim, generator=torch.Generator().manual_seed(seed)).cuda()
+    grid = torch.tensor(grids)
+    tower = VisionTower.random(cfg, seed=seed)
+    out = []
+    try:
+        from transformers.models.qwen3_vl_moe import configuration_qwen3_vl_moe as hfc
+        from transformers.models.qwen3_vl_moe import modeling_qwen3_vl_moe as hfm
+        c = hfc.Qwen3VLMoeVisionConfig(depth=depth, out_hidden_size=cfg.out_hidden_size)
+        c._attn_implementation = "sdpa"
+        model = hfm.Qwen3VLMoeVisionModel(c)
+        model.load_state_dict(tower.state_dict(), strict=True)
+        model = model.cuda().bfloat16().eval()
+        with torch.no_grad():
+            ms_hf = time_cuda(lambda: model(pixels.bfloat16(), grid_thw=grid.cuda()), iters=5)
+        del model
+    except ImportError:
+        ms_hf = None
+    tower = tower.cuda()
+    ms = time_cuda(lambda: tower(pixels, grid), iters=5)
+    flops = 2 * P * cfg.depth * (4 * cfg.hidden_size ** 2 + 2 * cfg.hidden_size * cfg.intermediate_size)
+    out.append({"kernel": "vision tower (27 blocks, native)", "patches": P, "ms": round(ms, 3),
+                "patches_per_s": round(P / ms * 1e3), "linear_tflops": round(flops / ms / 1e9, 1),
+                "hf_bf16_sdpa_ms": None if ms_hf is None else round(ms_hf, 3)})
     return out
 
 
@@ -546,7 +580,7 @@ def bench_gdn_train(B=1, T=16384, Hk=16, Hv=32):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "qsa", "train_attn", "ref_triton", "gdn_scan", "gdn_train", "grouped", "ple", "all"])
+    ap.add_argument("what", choices=["moe", "gemm", "gdn", "attn", "qsa", "train_attn", "ref_triton", "gdn_scan", "gdn_train", "grouped", "ple", "vision", "all"])
     ap.add_argument("--T", type=int, default=640)
     ap.add_argument("--S", type=int, default=128, help="sessions of the attn case")
     ap.add_argument("--seq", type=int, default=16384, help="sequence length of the gdn_scan / gdn_train cases")
@@ -577,6 +611,8 @@ def main():
         res += bench_grouped()
     if a.what in ("gdn_train", "all"):
         res += bench_gdn_train(T=a.seq)
+    if a.what in ("vision", "all"):
+        res += bench_vision()
     for r in res:
         print(json.dumps(r))
 

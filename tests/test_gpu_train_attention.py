@@ -51,6 +51,34 @@ def test_forward_and_gradients_match_oracle(Hq, Hkv, D, lens):
         assert torch.equal(a, t.grad)
 
 
+@pytest.mark.parametrize("D,lens", [(128, [300, 129, 64, 1000]), (256, [77, 513])])
+def test_bidirectional_forward_matches_oracle(D, lens):
+    """The forward's bidirectional mode (every key of the segment, e.g. a vision tower's attention within a frame)
+    against fp32 softmax attention per segment."""
+    from arc_forge_2026_b200.ops import C
+    from arc_forge_2026_b200.train.attention import tile_lists
+    g = torch.Generator().manual_seed(D)
+    T, Hq, Hkv = sum(lens), 8, 2
+    cu_host = [0] + torch.tensor(lens).cumsum(0).tolist()
+    q = torch.randn(T, Hq, D, generator=g).bfloat16().to(dev)
+    k = torch.randn(T, Hkv, D, generator=g).bfloat16().to(dev)
+    v = torch.randn(T, Hkv, D, generator=g).bfloat16().to(dev)
+    out = torch.empty_like(q)
+    lse = torch.empty(Hq, T, dtype=torch.float32, device=dev)
+    cu = torch.tensor(cu_host, dtype=torch.int32, device=dev)
+    C().attn_train_fwd(q, k, v, cu, tile_lists(cu_host, dev)[0], D ** -0.5, out, lse, None, 64, False)
+    torch.cuda.synchronize()
+    check_status()
+    ref = torch.empty(T, Hq, D, device=dev)
+    rep = Hq // Hkv
+    for s0, s1 in zip(cu_host[:-1], cu_host[1:]):
+        qq = q[s0:s1].float().transpose(0, 1)
+        kk = k[s0:s1].float().repeat_interleave(rep, 1).transpose(0, 1)
+        vv = v[s0:s1].float().repeat_interleave(rep, 1).transpose(0, 1)
+        ref[s0:s1] = ((qq @ kk.transpose(1, 2)) * D ** -0.5).softmax(-1).matmul(vv).transpose(0, 1)
+    assert _rel(out, ref) < 1e-2
+
+
 @pytest.mark.parametrize("block,topk,D", [(4, 32, 128), (4, 24, 256), (64, 3, 128)])
 def test_qsa_training_selection_and_attention_match_oracle(block, topk, D):
     """QSA in training: the packed-row selection (serving select kernels over row sets) equals the per-query
