@@ -456,7 +456,8 @@ __global__ void __launch_bounds__(256, 1)
 // combine split partials in split order: out = sum_s exp2(lse_s - LSE) O_s * sigmoid(gate)
 template <int D>
 __global__ void attn_merge_kernel(AttnArgs a, int splits) {
-  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int th = blockIdx.x;  // (token, head)
   const int tok = th / a.Hq, head = th % a.Hq;
   float lse_max = -INFINITY;
@@ -504,7 +505,10 @@ static int launch_attn(const AttnArgs& a, int splits, uint32_t* status, cudaStre
   paged_attn_kernel<D, FP4><<<grid, 256, S::TOTAL, st>>>(tk, tv, a, status);
   rc = (int)cudaGetLastError();
   if (rc || splits == 1) return rc;
-  attn_merge_kernel<D><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
+  {
+    const int pdl_rc = launch_pdl(attn_merge_kernel<D>, dim3(a.num_tokens * a.Hq), dim3(128), 0, st, a, splits);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 
@@ -518,9 +522,9 @@ int paged_attention(const AttnArgs& a, int splits, uint32_t* status, cudaStream_
   if (gather && (a.sp_block < 1 || 64 % a.sp_block || a.sp_ld < 1)) return 3;
   if (const int rc = paged_attention_tc(a, splits, status, st); rc != -1) {
     if (rc || splits == 1) return rc;
-    if (a.D == 256) attn_merge_kernel<256><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
-    else attn_merge_kernel<128><<<a.num_tokens * a.Hq, 128, 0, st>>>(a, splits);
-    return (int)cudaGetLastError();
+    const dim3 grid(a.num_tokens * a.Hq);
+    return a.D == 256 ? launch_pdl(attn_merge_kernel<256>, grid, dim3(128), 0, st, a, splits)
+                      : launch_pdl(attn_merge_kernel<128>, grid, dim3(128), 0, st, a, splits);
   }
   if (gather || a.q_per_seq * (a.Hq / a.Hkv) > 64) return 3;  // the mma.sync kernel holds <= 64 rows per CTA
   if (a.D == 256) return fp4 ? launch_attn<256, true>(a, splits, status, st) : launch_attn<256, false>(a, splits, status, st);

@@ -78,7 +78,8 @@ template <int D>
 __global__ void __launch_bounds__(attn_tc::THREADS, 1)
     paged_attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const __grid_constant__ CUtensorMap tmQ, AttnArgs a, uint32_t* status) {
-  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   using namespace attn_tc;
   using L = Smem<D>;
   constexpr int NS = L::NS;
@@ -651,7 +652,10 @@ static int launch_attn_tc(const AttnArgs& a, int splits, uint32_t* status, cudaS
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)paged_attn_tc_kernel<D>, L::TOTAL)) return e;
   dim3 grid(a.num_seqs * a.Hkv * ((a.q_per_seq + tpc - 1) / tpc), splits);
-  paged_attn_tc_kernel<D><<<grid, attn_tc::THREADS, L::TOTAL, st>>>(tk, tv, tq, a, status);
+  {
+    const int pdl_rc = launch_pdl(paged_attn_tc_kernel<D>, dim3(grid), dim3(attn_tc::THREADS), L::TOTAL, st, tk, tv, tq, a, status);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 

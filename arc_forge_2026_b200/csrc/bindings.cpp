@@ -50,7 +50,8 @@ at::Tensor status_tensor(int64_t dev) {
 
 // ------------------------------------------------------------------------------------------ GEMM
 at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tensor> out,
-                c10::optional<at::Tensor> residual, double alpha, bool out_fp32, int64_t bn, int64_t splits) {
+                c10::optional<at::Tensor> residual, double alpha, bool out_fp32, int64_t bn, int64_t splits,
+                c10::optional<at::Tensor> bias, int64_t act) {
   CHECK_CUDA(a);
   CHECK_CUDA(b);
   CHECK_DT(a, at::kBFloat16);
@@ -77,6 +78,13 @@ at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tens
     epi.residual = residual->data_ptr();
     epi.ldr = residual->stride(0);
   }
+  if (bias.has_value()) {
+    CHECK_DT((*bias), at::kBFloat16);
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == N, "gemm: bias is bf16 [N]");
+    epi.bias = bias->data_ptr();
+  }
+  TORCH_CHECK(act >= 0 && act <= 2, "gemm: act is 0 (none), 1 (tanh-GELU) or 2 (erf-GELU)");
+  epi.act = (int)act;
   afb::GemmPlan p = afb::plan_gemm(M, N, K, num_sms());
   if (bn > 0) p.bn = (int)bn;
   if (splits > 0) p.splits = (int)splits;
@@ -156,9 +164,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_tensor", &status_tensor, "per-device kernel status words (int32[16])");
   m.def("gemm_grouped", &gemm_grouped, py::arg("a"), py::arg("b"), py::arg("seg"), py::arg("tiles"), py::arg("mode"),
         py::arg("group_rows"), py::arg("max_tiles"), py::arg("out"));
-  m.def("gemm", &gemm, "bf16 tcgen05 GEMM: out = alpha * a @ b.T (+ residual)", py::arg("a"), py::arg("b"),
+  m.def("gemm", &gemm, "bf16 tcgen05 GEMM: out = act(alpha * a @ b.T + bias) (+ residual)", py::arg("a"), py::arg("b"),
         py::arg("out") = py::none(), py::arg("residual") = py::none(), py::arg("alpha") = 1.0,
-        py::arg("out_fp32") = false, py::arg("bn") = 0, py::arg("splits") = 0);
+        py::arg("out_fp32") = false, py::arg("bn") = 0, py::arg("splits") = 0, py::arg("bias") = py::none(),
+        py::arg("act") = 0);
   m.def("gemm_plan", &gemm_plan);
   register_kernel_ops(m);
   register_runtime(m);

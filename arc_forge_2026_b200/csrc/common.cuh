@@ -13,6 +13,8 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <utility>
 
 #define AFB_DEV __device__ __forceinline__
 
@@ -28,6 +30,30 @@
 #endif
 
 namespace afb {
+
+// Programmatic dependent launch: a kernel launched this way may start while the previous kernel in the stream is
+// still running (once every CTA of that kernel has called grid_dep_trigger() or exited); it must call
+// grid_dep_wait() before its first access to memory that earlier work wrote or reads. Every kernel launched through
+// launch_pdl() does so as its first statement. AFB_NO_PDL in the environment turns the attribute off (A/B runs).
+inline bool pdl_enabled() {
+  static const bool on = std::getenv("AFB_NO_PDL") == nullptr;
+  return on;
+}
+template <typename... P, typename... A>
+inline int launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
+  return e == cudaSuccess ? (int)cudaGetLastError() : (int)e;
+}
 
 // Raise a kernel's dynamic shared-memory limit once per device. The attribute belongs to the current device's
 // context, so every GPU a process launches on needs its own call; `done` (one per call site) keeps a bit per

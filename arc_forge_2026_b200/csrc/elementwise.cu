@@ -16,7 +16,8 @@ namespace afb {
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int rows, int H,
                                float eps, int zero_centered) {
-  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -68,9 +69,12 @@ int rmsnorm(const void* x, void* residual, const void* w, void* y, int rows, int
   if (H % 8) return 3;
   if (!rows) return 0;
   const int warps = 4;
-  rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, st>>>(
+  {
+    const int pdl_rc = launch_pdl(rmsnorm_kernel, dim3((rows + warps - 1) / warps), dim3(warps * 32), 0, st,
       (const __nv_bfloat16*)x, (__nv_bfloat16*)residual, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, rows, H, eps,
       zero_centered);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 
@@ -108,6 +112,8 @@ __global__ void qk_norm_rope_store_kernel(const __nv_bfloat16* __restrict__ qkv,
                                           const float* __restrict__ sin_t, float eps, __nv_bfloat16* __restrict__ q_out,
                                           __nv_bfloat16* __restrict__ kcache, __nv_bfloat16* __restrict__ vcache,
                                           int page_size, uint8_t* __restrict__ kscale, uint8_t* __restrict__ vscale) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   __shared__ float buf[8][256];
   __shared__ float obuf[8][256];
   const int wi = threadIdx.x >> 5;
@@ -188,10 +194,13 @@ int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, i
   if (!T) return 0;
   const int warps = 8;
   const int total = T * (Hq + 2 * Hkv);
-  qk_norm_rope_store_kernel<<<(total + warps - 1) / warps, warps * 32, 0, st>>>(
+  {
+    const int pdl_rc = launch_pdl(qk_norm_rope_store_kernel, dim3((total + warps - 1) / warps), dim3(warps * 32), 0, st,
       (const __nv_bfloat16*)qkv, ld, T, Hq, Hkv, D, rot, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, positions,
       slots, cos_t, sin_t, eps, (__nv_bfloat16*)q_out, (__nv_bfloat16*)kcache, (__nv_bfloat16*)vcache, page_size,
       kscale, vscale);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 
@@ -204,6 +213,8 @@ int qk_norm_rope_store(const void* qkv, int ld, int T, int Hq, int Hkv, int D, i
 __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int k, int renorm,
                                    int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ cnt,
                                    int* __restrict__ list, int cap) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -275,8 +286,11 @@ int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, in
     if (e != cudaSuccess) return (int)e;
   }
   if (T <= 0) return 0;
-  router_topk_kernel<<<(T + warps - 1) / warps, warps * 32, 0, st>>>(logits, ld, T, E, k, renorm, ids, weights, cnt,
+  {
+    const int pdl_rc = launch_pdl(router_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, st, logits, ld, T, E, k, renorm, ids, weights, cnt,
                                                                       list, cap);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 
@@ -444,6 +458,8 @@ int quant_rows_e4m3(const void* x, int ldx, const int* row_token, const int* nro
 __global__ void quant_rows_e4m3_row_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                            const int* __restrict__ row_token, const int* __restrict__ nrows_dev,
                                            int nrows, int K, uint8_t* __restrict__ q, float* __restrict__ scales) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int n = nrows_dev ? min(*nrows_dev, nrows) : nrows;
@@ -486,8 +502,11 @@ int quant_rows_e4m3_row(const void* x, int ldx, const int* row_token, const int*
   if (K % 8 || ldx % 8) return 3;
   if (nrows <= 0) return 0;
   const int warps = 8;
-  quant_rows_e4m3_row_kernel<<<(nrows + warps - 1) / warps, warps * 32, 0, st>>>(
+  {
+    const int pdl_rc = launch_pdl(quant_rows_e4m3_row_kernel, dim3((nrows + warps - 1) / warps), dim3(warps * 32), 0, st,
       (const __nv_bfloat16*)x, ldx, row_token, nrows_dev, nrows, K, (uint8_t*)q, scales);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 
@@ -501,6 +520,8 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
                                    const __nv_bfloat16* __restrict__ shared, const float* __restrict__ router_logits,
                                    int ld_logits, int sg_col, const __nv_bfloat16* __restrict__ resid,
                                    __nv_bfloat16* __restrict__ out, int T, int H, EpArgs ew, uint32_t* status) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   // one CTA per token, one thread per 8 columns; all k row loads of a thread are issued before the sums
   const int t = blockIdx.x;
   const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
@@ -581,16 +602,20 @@ int moe_combine(const void* y, const int* entry_row, int k, const void* shared, 
   if (rows <= 0) return 0;
   const int threads = 256;
   dim3 grid(rows, (H / 8 + threads - 1) / threads);
-  moe_combine_kernel<<<grid, threads, 0, st>>>((const __nv_bfloat16*)y, entry_row, k, (const __nv_bfloat16*)shared,
+  {
+    const int pdl_rc = launch_pdl(moe_combine_kernel, dim3(grid), dim3(threads), 0, st, (const __nv_bfloat16*)y, entry_row, k, (const __nv_bfloat16*)shared,
                                                router_logits, ld_logits, sg_col, (const __nv_bfloat16*)resid,
                                                (__nv_bfloat16*)out, T, H, ew, status);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------------ SwiGLU (dense)
 // x [T, 2I] = [gate | up] -> y [T, I] = silu(gate) * up
 __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int T, int I) {
-  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const size_t i8 = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (i8 >= (size_t)T * I) return;
   const size_t t = i8 / I, c = i8 % I;
@@ -609,7 +634,10 @@ int swiglu(const void* x, void* y, int T, int I, cudaStream_t st) {
   if (I % 8) return 3;
   const size_t n = (size_t)T * I / 8;
   if (!n) return 0;
-  swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)y, T, I);
+  {
+    const int pdl_rc = launch_pdl(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const __nv_bfloat16*)x, (__nv_bfloat16*)y, T, I);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 

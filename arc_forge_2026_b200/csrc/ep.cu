@@ -50,6 +50,8 @@ AFB_DEV void ep_signal_last_cta(const EpArgs& a, int type) {
 __global__ void __launch_bounds__(128) ep_dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x, int ldx,
                                                           const int* __restrict__ ids,
                                                           const float* __restrict__ weights) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   constexpr int MAXV = 3;  // 16-byte vectors per thread: H <= 128 * 8 * 3
   __shared__ float red[4];
   if (blockIdx.x >= a.T_cap) {  // list CTAs: warp w copies expert e's entries of this rank to e's owner
@@ -126,7 +128,10 @@ int ep_dispatch(const EpArgs& a, const void* x, int ldx, const int* ids, const f
       a.T_cap < 1 || !a.lcnt || !a.llist || a.E_local < 1)
     return 3;
   const int E = a.E_local * a.world;
-  ep_dispatch_kernel<<<a.T_cap + (E + 3) / 4, 128, 0, st>>>(a, (const __nv_bfloat16*)x, ldx, ids, weights);
+  {
+    const int pdl_rc = launch_pdl(ep_dispatch_kernel, dim3(a.T_cap + (E + 3) / 4), dim3(128), 0, st, a, (const __nv_bfloat16*)x, ldx, ids, weights);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 
@@ -161,6 +166,8 @@ int ep_wait(const EpArgs& a, int type, uint32_t* status, cudaStream_t st) {
 __global__ void quant_routed_rows_kernel(const __nv_bfloat16* __restrict__ x, int K, const int* __restrict__ cnt,
                                          const int* __restrict__ list, int E, int cap, uint8_t* __restrict__ q,
                                          float* __restrict__ scales, int slots) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (w >= slots) return;
   const int pe = w / cap, i = w - pe * cap;  // (source * E + expert), position
@@ -203,8 +210,11 @@ int quant_routed_rows(const void* x, int K, const int* cnt, const int* list, int
   if (K % 8 || srcs < 1 || E < 1 || cap < 1) return 3;
   const int slots = srcs * E * cap;
   const int warps = 8;
-  quant_routed_rows_kernel<<<(slots + warps - 1) / warps, warps * 32, 0, st>>>(
+  {
+    const int pdl_rc = launch_pdl(quant_routed_rows_kernel, dim3((slots + warps - 1) / warps), dim3(warps * 32), 0, st,
       (const __nv_bfloat16*)x, K, cnt, list, E, cap, (uint8_t*)q, scales, slots);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 

@@ -83,7 +83,8 @@ AFB_DEV float tf32_hi(float x) { return __int_as_float(__float_as_int(x) & 0xfff
 __global__ void __launch_bounds__(gdntc::THREADS, 1)
     gdn_verify_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmQK,
                          const __grid_constant__ CUtensorMap tmV, GdnArgs a, int parity, uint32_t* status) {
-  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   using namespace gdntc;
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -515,8 +516,8 @@ int gdn_verify_tc(const GdnArgs& a, int parity, int num_sms, uint32_t* status, c
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)gdn_verify_tc_kernel, (int)smem)) return e;
   const int items = a.num_seqs * a.Hv;
-  gdn_verify_tc_kernel<<<items < num_sms ? items : num_sms, THREADS, smem, st>>>(ts, tq, tv, a, parity, status);
-  return (int)cudaGetLastError();
+  return launch_pdl(gdn_verify_tc_kernel, dim3(items < num_sms ? items : num_sms), dim3(THREADS), smem, st, ts, tq, tv, a,
+                    parity, status);
 }
 
 }  // namespace afb

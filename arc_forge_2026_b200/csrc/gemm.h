@@ -13,6 +13,8 @@ struct GemmEpilogue {
   const void* residual = nullptr;  // optional bf16 [M, ldr] added after alpha
   int ldr = 0;
   float alpha = 1.f;
+  const void* bias = nullptr;      // optional bf16 [N], added after alpha (before the activation and the residual)
+  int act = 0;                     // 0 none, 1 tanh-GELU, 2 erf-GELU (applied to alpha * acc + bias)
   void* partial = nullptr;         // split-K scratch: fp32 [splits, M, N]
 };
 

@@ -1,4 +1,5 @@
-// Dense bf16 GEMM on the 5th-gen tensor cores: C[M,N] = alpha * A[M,K] * B[N,K]^T (+ residual).
+// Dense bf16 GEMM on the 5th-gen tensor cores: C[M,N] = act(alpha * A[M,K] * B[N,K]^T + bias) (+ residual),
+// act none / tanh-GELU / erf-GELU, bias bf16 [N] (both optional).
 //
 // Both operands are K-major (nn.Linear layout). One CTA computes a 128 x BN tile:
 //   warp 0      one elected thread issues TMA loads (128-byte swizzle) into a STAGES-deep ring
@@ -14,8 +15,6 @@
 // shared expert, router, LM head) in place of the reference's cuBLAS/CUTLASS dense GEMMs.
 #include <cudaTypedefs.h>
 
-#include <cstdlib>
-#include <utility>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -31,6 +30,25 @@ struct GemmSmem {
   static constexpr uint32_t TOTAL = BAR_OFF + (2 * STAGES + 1) * 8 + 16 + 1024;  // +1024 for manual alignment
   static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
 };
+
+// epilogue math on 4 consecutive columns: v = act(alpha * acc + bias) (+ the residual, by the caller)
+AFB_DEV float gemm_act(float x, int act) {
+  if (act == 1) return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+  if (act == 2) return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
+  return x;
+}
+AFB_DEV void gemm_bias_act4(float* v, const GemmEpilogue& epi, int col) {
+  if (epi.bias) {
+    const uint2 q = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(epi.bias) + col);
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) v[t] += __bfloat162float(h[t]);
+  }
+  if (epi.act) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) v[t] = gemm_act(v[t], epi.act);
+  }
+}
 
 template <int BN, int STAGES, int GMODE = 0>
 __global__ void __launch_bounds__(192, 1)
@@ -166,6 +184,11 @@ __global__ void __launch_bounds__(192, 1)
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= epi.alpha;
+      if (epi.bias || epi.act) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          if (col0 + j < N) gemm_bias_act4(v + j, epi, col0 + j);
+      }
       if (epi.residual) {
         const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(epi.residual) + (size_t)row * epi.ldr + col0;
 #pragma unroll
@@ -216,6 +239,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
     acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
   }
   float v[4] = {acc.x * epi.alpha, acc.y * epi.alpha, acc.z * epi.alpha, acc.w * epi.alpha};
+  gemm_bias_act4(v, epi, col);
   if (epi.residual) {
     const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(epi.residual) + (size_t)row * epi.ldr + col;
     for (int t = 0; t < 4; ++t) v[t] += __bfloat162float(r[t]);
@@ -290,26 +314,6 @@ int make_tmap_3d_bf16(CUtensorMap* map, const void* base, const uint64_t dims[3]
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
-// A launch that may begin while the previous kernel in the stream finishes (the kernel calls grid_dep_wait() before
-// its first dependent access). AFB_GEMM_NO_PDL in the environment turns it off (A/B measurements).
-template <typename... P, typename... A>
-static int launch_dependent(void (*kern)(P...), dim3 grid, dim3 block, uint32_t smem, cudaStream_t stream,
-                            A&&... args) {
-  static const bool pdl = std::getenv("AFB_GEMM_NO_PDL") == nullptr;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute at;
-  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at.val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = &at;
-  cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
-  return e == cudaSuccess ? (int)cudaGetLastError() : (int)e;
-}
-
 template <int BN, int STAGES>
 static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int splits,
                        const GemmEpilogue& epi, uint32_t* status, cudaStream_t stream) {
@@ -323,7 +327,7 @@ static int launch_gemm(const void* A, int lda, const void* B, int ldb, int M, in
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)kern, S::TOTAL)) return e;
   const dim3 grid((M + S::BM - 1) / S::BM, (N + BN - 1) / BN, splits);
-  return launch_dependent(kern, grid, dim3(192), S::TOTAL, stream, ta, tb, M, N, K, epi, status, GemmGroups());
+  return launch_pdl(kern, grid, dim3(192), S::TOTAL, stream, ta, tb, M, N, K, epi, status, GemmGroups());
 }
 
 // Grouped launch (one tile width: 256; no split-K). A ROWS grid covers max_tiles m-tiles (an upper bound of
@@ -335,7 +339,7 @@ int gemm_bf16_grouped(const void* A, int lda, int rows_a, const void* B, int ldb
                                        // pipeline fill is paid once per tile; REDUCE tiles have few K blocks)
   using S = GemmSmem<BN, STAGES>;
   if (g.mode != 1 && g.mode != 2) return 3;
-  if ((K % 8) || (lda % 8) || (ldb % 8) || (N % 8) || epi.partial) return 3;
+  if ((K % 8) || (lda % 8) || (ldb % 8) || (N % 8) || epi.partial || epi.bias || epi.act) return 3;
   if (rows_a <= 0 || rows_b <= 0 || N <= 0 || g.E <= 0) return 0;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, 2, K, rows_a, (uint64_t)lda * 2, S::BK, S::BM, 1);
@@ -394,7 +398,7 @@ GemmPlan plan_gemm(int M, int N, int K, int num_sms) {
 int gemm_bf16_tn(const void* A, int lda, const void* B, int ldb, int M, int N, int K, const GemmEpilogue& epi,
                  int bn, int splits, uint32_t* status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  if ((K % 8) || (N % 8) || (lda % 8) || (ldb % 8)) return 3;
+  if ((K % 8) || (N % 8) || (lda % 8) || (ldb % 8) || epi.act < 0 || epi.act > 2) return 3;
   if (splits > 1 && !epi.partial) return 4;
   int rc;
   if (bn == 128)
@@ -407,7 +411,7 @@ int gemm_bf16_tn(const void* A, int lda, const void* B, int ldb, int M, int N, i
   const size_t total = (size_t)M * N;
   const int threads = 256;
   const int blocks = (int)((total / 4 + threads - 1) / threads);
-  return launch_dependent(splitk_reduce_kernel, dim3(blocks), dim3(threads), 0, stream,
+  return launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(threads), 0, stream,
                           reinterpret_cast<const float*>(epi.partial), splits, M, N, epi);
 }
 

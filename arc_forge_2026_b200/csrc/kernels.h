@@ -96,15 +96,12 @@ struct AttnTrainArgs {
 };
 int attn_train_fwd(const AttnTrainArgs& a, uint32_t* status, cudaStream_t st);
 
-// vision tower (csrc/vision.cu): acc = fp32 GEMM outputs, bf16 elsewhere
+// vision tower (csrc/vision.cu): acc = the fp32 patch-embedding GEMM output, bf16 elsewhere
 int vit_patch_pos(const float* acc, const void* bias, const void* table, const int* idx, const void* wts, void* h,
                   int P, int C, cudaStream_t st);
-int vit_qkv_rope(const float* acc, const void* bias, const float* cosv, const float* sinv, int P, int H, int Dh,
-                 int Dp, void* q, void* k, void* v, cudaStream_t st);
-// acc == nullptr: y = LayerNorm(h) only; y == nullptr: the residual add only
-int vit_residual_ln(const float* acc, const void* bias, void* h, const void* w, const void* b, float eps, void* y,
-                    int rows, int C, cudaStream_t st);
-int vit_bias_act(const float* acc, const void* bias, void* y, int rows, int C, int act, cudaStream_t st);
+int vit_qkv_rope(const void* qkv, const float* cosv, const float* sinv, int P, int H, int Dh, int Dp, void* q,
+                 void* k, void* v, cudaStream_t st);
+int vit_layernorm(const void* x, const void* w, const void* b, float eps, void* y, int rows, int C, cudaStream_t st);
 // kv_tiles [nkv]: the 128-key tiles of the dK / dV kernels (most work first); a.tiles: 64-row query tiles of dQ
 int attn_train_bwd(const AttnTrainArgs& a, const int2* kv_tiles, int nkv, uint32_t* status, cudaStream_t st);
 // QSA training selection -> per-row block bitmap: row set s (W rows starting at packed row set_row0[s], the first

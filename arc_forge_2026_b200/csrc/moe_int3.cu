@@ -179,7 +179,8 @@ AFB_DEV void decode32(uint32_t L0, uint32_t L1, uint32_t H, uint32_t* o) {
 template <bool PAIR, bool F8, bool PROF>
 __global__ void __launch_bounds__(moe::THREADS, 1)
     moe_int3_gemm_kernel(const __grid_constant__ CUtensorMap tmW, MoeGemmArgs args, uint32_t* status) {
-  grid_dep_trigger();  // a dependent GEMM launched with programmatic serialization may set up meanwhile
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   using L = moe::Layout<F8>;
   constexpr int RS = L::RS, AS = L::AS, NBUF = L::NBUF, T = moe::T, NT = moe::NTOK, MS = moe::MS;
   extern __shared__ uint8_t smem_raw[];
@@ -578,7 +579,10 @@ static int launch_moe_t(const CUtensorMap& tw, const MoeGemmArgs& a, int grid, u
   using L = moe::Layout<F8>;
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)moe_int3_gemm_kernel<PAIR, F8, PROF>, L::TOTAL)) return e;
-  moe_int3_gemm_kernel<PAIR, F8, PROF><<<grid, moe::THREADS, L::TOTAL, st>>>(tw, a, status);
+  {
+    const int pdl_rc = launch_pdl(moe_int3_gemm_kernel<PAIR, F8, PROF>, dim3(grid), dim3(moe::THREADS), L::TOTAL, st, tw, a, status);
+    if (pdl_rc) return pdl_rc;
+  }
   return (int)cudaGetLastError();
 }
 

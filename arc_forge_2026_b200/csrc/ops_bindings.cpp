@@ -468,8 +468,6 @@ void attn_train_fwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tenso
 }
 
 // ------------------------------------------------------------------------------------------ vision tower
-static const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
-
 void vit_patch_pos_op(const at::Tensor& acc, const at::Tensor& bias, const at::Tensor& table, const at::Tensor& idx,
                       const at::Tensor& wts, at::Tensor& h) {
   AFB_CHECK_DT(acc, at::kFloat);
@@ -489,10 +487,10 @@ void vit_patch_pos_op(const at::Tensor& acc, const at::Tensor& bias, const at::T
            "vit_patch_pos");
 }
 
-void vit_qkv_rope_op(const at::Tensor& acc, const at::Tensor& bias, const at::Tensor& cosv, const at::Tensor& sinv,
-                     int64_t H, int64_t Dh, at::Tensor& q, at::Tensor& k, at::Tensor& v) {
-  AFB_CHECK_DT(acc, at::kFloat);
-  AFB_CHECK_CONTIG(acc);
+void vit_qkv_rope_op(const at::Tensor& qkv, const at::Tensor& cosv, const at::Tensor& sinv, int64_t H, int64_t Dh,
+                     at::Tensor& q, at::Tensor& k, at::Tensor& v) {
+  AFB_CHECK_DT(qkv, at::kBFloat16);
+  AFB_CHECK_CONTIG(qkv);
   AFB_CHECK_DT(cosv, at::kFloat);
   AFB_CHECK_DT(sinv, at::kFloat);
   AFB_CHECK_CONTIG(cosv);
@@ -501,46 +499,27 @@ void vit_qkv_rope_op(const at::Tensor& acc, const at::Tensor& bias, const at::Te
     AFB_CHECK_DT((*t), at::kBFloat16);
     AFB_CHECK_CONTIG((*t));
   }
-  const int P = acc.size(0), Dp = q.size(2);
-  TORCH_CHECK(acc.size(1) == 3 * H * Dh && bias.numel() == 3 * H * Dh && q.size(0) == P && q.size(1) == H &&
-                  k.sizes() == q.sizes() && v.sizes() == q.sizes() && cosv.numel() == (int64_t)P * (Dh / 2) &&
-                  sinv.numel() == cosv.numel(),
+  const int P = qkv.size(0), Dp = q.size(2);
+  TORCH_CHECK(qkv.size(1) == 3 * H * Dh && q.size(0) == P && q.size(1) == H && k.sizes() == q.sizes() &&
+                  v.sizes() == q.sizes() && cosv.numel() == (int64_t)P * (Dh / 2) && sinv.numel() == cosv.numel(),
               "vit_qkv_rope shapes");
-  check_rc(afb::vit_qkv_rope(ptr<float>(acc), bias.data_ptr(), ptr<float>(cosv), ptr<float>(sinv), P, (int)H, (int)Dh,
-                             Dp, q.data_ptr(), k.data_ptr(), v.data_ptr(), stream()),
+  check_rc(afb::vit_qkv_rope(qkv.data_ptr(), ptr<float>(cosv), ptr<float>(sinv), P, (int)H, (int)Dh, Dp,
+                             q.data_ptr(), k.data_ptr(), v.data_ptr(), stream()),
            "vit_qkv_rope");
 }
 
-void vit_residual_ln_op(c10::optional<at::Tensor> acc, c10::optional<at::Tensor> bias, at::Tensor& h,
-                        c10::optional<at::Tensor> w, c10::optional<at::Tensor> b, double eps,
-                        c10::optional<at::Tensor> y) {
-  AFB_CHECK_DT(h, at::kBFloat16);
-  AFB_CHECK_CONTIG(h);
-  const int rows = h.size(0), C = h.size(1);
-  if (acc.has_value()) {
-    AFB_CHECK_DT((*acc), at::kFloat);
-    AFB_CHECK_CONTIG((*acc));
-    TORCH_CHECK(acc->sizes() == h.sizes(), "vit_residual_ln: acc shape");
-  }
-  if (y.has_value()) {
-    AFB_CHECK_CONTIG((*y));
-    TORCH_CHECK(y->sizes() == h.sizes() && w.has_value() && b.has_value() && w->numel() == C && b->numel() == C,
-                "vit_residual_ln: y / norm shapes");
-  }
-  check_rc(afb::vit_residual_ln(acc.has_value() ? ptr<float>(*acc) : nullptr, opt_ptr(bias), h.data_ptr(), opt_ptr(w),
-                                opt_ptr(b), (float)eps, y.has_value() ? y->data_ptr() : nullptr, rows, C, stream()),
-           "vit_residual_ln");
-}
-
-void vit_bias_act_op(const at::Tensor& acc, const at::Tensor& bias, at::Tensor& y, int64_t act) {
-  AFB_CHECK_DT(acc, at::kFloat);
-  AFB_CHECK_CONTIG(acc);
+void vit_layernorm_op(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, double eps, at::Tensor& y) {
+  AFB_CHECK_DT(x, at::kBFloat16);
+  AFB_CHECK_CONTIG(x);
   AFB_CHECK_DT(y, at::kBFloat16);
   AFB_CHECK_CONTIG(y);
-  TORCH_CHECK(y.sizes() == acc.sizes() && bias.numel() == acc.size(1), "vit_bias_act shapes");
-  check_rc(afb::vit_bias_act(ptr<float>(acc), bias.data_ptr(), y.data_ptr(), acc.size(0), acc.size(1), (int)act,
-                             stream()),
-           "vit_bias_act");
+  AFB_CHECK_DT(w, at::kBFloat16);
+  AFB_CHECK_DT(b, at::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && y.sizes() == x.sizes() && w.numel() == x.size(1) && b.numel() == x.size(1),
+              "vit_layernorm shapes");
+  check_rc(afb::vit_layernorm(x.data_ptr(), w.data_ptr(), b.data_ptr(), (float)eps, y.data_ptr(), x.size(0), x.size(1),
+                              stream()),
+           "vit_layernorm");
 }
 
 void attn_train_bwd_op(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
@@ -1558,9 +1537,7 @@ void register_kernel_ops(pybind11::module& m) {
         py::arg("qsa_block") = 64, py::arg("causal") = true);
   m.def("vit_patch_pos", &vit_patch_pos_op);
   m.def("vit_qkv_rope", &vit_qkv_rope_op);
-  m.def("vit_residual_ln", &vit_residual_ln_op, py::arg("acc"), py::arg("bias"), py::arg("h"), py::arg("w"),
-        py::arg("b"), py::arg("eps"), py::arg("y"));
-  m.def("vit_bias_act", &vit_bias_act_op);
+  m.def("vit_layernorm", &vit_layernorm_op);
   m.def("attn_train_bwd", &attn_train_bwd_op, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu"),
         py::arg("tiles"), py::arg("kv_tiles"), py::arg("scale"), py::arg("out"), py::arg("lse"), py::arg("dout"),
         py::arg("delta"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dk_part"), py::arg("dv_part"),

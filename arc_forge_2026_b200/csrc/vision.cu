@@ -1,15 +1,14 @@
 // Elementwise kernels of the vision tower (a Qwen3-VL-style ViT: patch embedding, learned position table resampled to
-// the image grid, 2-D rotary attention blocks, 2x2 patch mergers). The tower's GEMMs run on the tcgen05 GEMM with
-// fp32 outputs and its attention on the tcgen05 training-attention forward (bidirectional mode, heads padded to 128);
-// these kernels do everything between them, each in one pass over the rows:
-//   vit_patch_pos      h = bf16(bf16(acc + b) + pos), pos = the four-tap bilinear resample of the position table with
-//                      bf16 products and bf16 running sums (the deployed interpolation's rounding)
-//   vit_qkv_rope       q / k / v = bf16(acc + b) split per head, 2-D rotary on q and k in fp32, written head-padded
-//   vit_residual_ln    h = bf16(h + bf16(acc + b)) in place, then y = LayerNorm(h) (fp32 statistics)
-//   vit_layernorm      y = LayerNorm(x) over rows of any width (the post-shuffle norm of the deepstack mergers)
-//   vit_bias_act       y = act(bf16(acc + b)), act = identity / tanh-GELU / erf-GELU
-// The rounding points follow the bf16 module graph (a Linear's output is rounded once with its bias, the residual add
-// rounds again), so the tower tracks a bf16 PyTorch forward of the same weights closely.
+// the image grid, 2-D rotary attention blocks, 2x2 patch mergers). The tower's projections run on the tcgen05 GEMM
+// with bias, GELU and the residual add in its epilogue, and its attention on the tcgen05 training-attention forward
+// (bidirectional mode, heads padded to 128); these kernels do the rest, each in one pass over the rows:
+//   vit_patch_pos   h = bf16(bf16(acc + b) + pos), acc the fp32 patch-embedding GEMM, pos the four-tap bilinear
+//                   resample of the position table with bf16 products and bf16 running sums (the deployed
+//                   interpolation's rounding)
+//   vit_qkv_rope    q / k / v split per head from the bf16 QKV projection, 2-D rotary on q and k in fp32, written
+//                   head-padded (zeros past the head dim)
+//   vit_layernorm   y = LayerNorm(x) with fp32 statistics, rows of any width up to 5,120 (the post-shuffle norm of
+//                   the deepstack mergers normalises four patches' rows as one)
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -29,25 +28,6 @@ AFB_DEV float block_sum(float v, float* red) {
   float t = 0.f;
   for (int i = 0; i < nw; ++i) t += red[i];
   return t;
-}
-
-// LayerNorm of one row held as fp32 values v[0..per) per thread (stride blockDim.x), written as bf16
-AFB_DEV void ln_row(const float* v, int per, int width, const __nv_bfloat16* w, const __nv_bfloat16* b, float eps,
-                    __nv_bfloat16* y, float* red) {
-  float s = 0.f;
-  for (int i = 0; i < per; ++i) s += v[i];
-  const float mean = block_sum(s, red) / (float)width;
-  float q = 0.f;
-  for (int i = 0; i < per; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    if (c < width) q += (v[i] - mean) * (v[i] - mean);
-  }
-  const float rstd = rsqrtf(block_sum(q, red) / (float)width + eps);
-  for (int i = 0; i < per; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    if (c < width)
-      y[c] = __float2bfloat16((v[i] - mean) * rstd * __bfloat162float(w[c]) + __bfloat162float(b[c]));
-  }
 }
 
 constexpr int LN_THREADS = 256, LN_PER = 20;  // rows up to 5,120 wide
@@ -73,22 +53,22 @@ __global__ void vit_patch_pos_kernel(const float* __restrict__ acc, const __nv_b
   }
 }
 
-// one block per patch; thread j of a head handles rotary pair (j, j + Dh / 2)
-__global__ void vit_qkv_rope_kernel(const float* __restrict__ acc, const __nv_bfloat16* __restrict__ bias,
-                                    const float* __restrict__ cosv, const float* __restrict__ sinv, int P, int H,
-                                    int Dh, int Dp, __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
+// one block per patch; rotary pair (j, j + Dh / 2) of each head
+__global__ void vit_qkv_rope_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ cosv,
+                                    const float* __restrict__ sinv, int P, int H, int Dh, int Dp,
+                                    __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
                                     __nv_bfloat16* __restrict__ v) {
   const int p = blockIdx.x;
   if (p >= P) return;
   const int half = Dh / 2, W = H * Dh;
-  const float* a = acc + (size_t)p * 3 * W;
+  const __nv_bfloat16* a = qkv + (size_t)p * 3 * W;
   for (int e = threadIdx.x; e < H * Dp; e += blockDim.x) {  // v, and the zero padding of all three
     const int hd = e / Dp, d = e - hd * Dp;
     const size_t o = (size_t)p * H * Dp + e;
     if (d >= Dh) {
       q[o] = k[o] = v[o] = __float2bfloat16(0.f);
     } else {
-      v[o] = __float2bfloat16(a[2 * W + hd * Dh + d] + __bfloat162float(bias[2 * W + hd * Dh + d]));
+      v[o] = a[2 * W + hd * Dh + d];
     }
   }
   for (int e = threadIdx.x; e < H * half; e += blockDim.x) {
@@ -98,8 +78,7 @@ __global__ void vit_qkv_rope_kernel(const float* __restrict__ acc, const __nv_bf
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
       const int base = which * W + hd * Dh;
-      const float x0 = bf(a[base + j] + __bfloat162float(bias[base + j]));
-      const float x1 = bf(a[base + j + half] + __bfloat162float(bias[base + j + half]));
+      const float x0 = __bfloat162float(a[base + j]), x1 = __bfloat162float(a[base + j + half]);
       __nv_bfloat16* dst = which ? k : q;
       dst[o + j] = __float2bfloat16(x0 * c - x1 * s);
       dst[o + j + half] = __float2bfloat16(x1 * c + x0 * s);
@@ -107,44 +86,32 @@ __global__ void vit_qkv_rope_kernel(const float* __restrict__ acc, const __nv_bf
   }
 }
 
-__global__ void __launch_bounds__(LN_THREADS) vit_residual_ln_kernel(const float* __restrict__ acc,
-                                                                     const __nv_bfloat16* __restrict__ bias,
-                                                                     __nv_bfloat16* __restrict__ h,
-                                                                     const __nv_bfloat16* __restrict__ w,
-                                                                     const __nv_bfloat16* __restrict__ b, float eps,
-                                                                     __nv_bfloat16* __restrict__ y, int C) {
+__global__ void __launch_bounds__(LN_THREADS) vit_layernorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   const __nv_bfloat16* __restrict__ b, float eps,
+                                                                   __nv_bfloat16* __restrict__ y, int C) {
   __shared__ float red[LN_THREADS / 32];
   const size_t r = blockIdx.x;
   float v[LN_PER];
   const int per = (C + LN_THREADS - 1) / LN_THREADS;
+  float s = 0.f;
   for (int i = 0; i < per; ++i) {
     const int c = threadIdx.x + i * LN_THREADS;
-    float x = 0.f;
-    if (c < C) {
-      x = __bfloat162float(h[r * C + c]);
-      if (acc) {
-        x = bf(x + bf(acc[r * C + c] + (bias ? __bfloat162float(bias[c]) : 0.f)));
-        h[r * C + c] = __float2bfloat16(x);
-      }
-    }
-    v[i] = x;
+    v[i] = c < C ? __bfloat162float(x[r * C + c]) : 0.f;
+    s += v[i];
   }
-  if (y) ln_row(v, per, C, w, b, eps, y + r * C, red);
-}
-
-__global__ void vit_bias_act_kernel(const float* __restrict__ acc, const __nv_bfloat16* __restrict__ bias,
-                                    __nv_bfloat16* __restrict__ y, size_t n, int C, int act) {
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const float t = bf(acc[i] + __bfloat162float(bias[i % C]));
-  float o = t;
-  if (act == 1) {  // tanh approximation of GELU
-    const float u = 0.7978845608028654f * (t + 0.044715f * t * t * t);
-    o = 0.5f * t * (1.f + tanhf(u));
-  } else if (act == 2) {  // exact GELU
-    o = 0.5f * t * (1.f + erff(t * 0.7071067811865476f));
+  const float mean = block_sum(s, red) / (float)C;
+  float q = 0.f;
+  for (int i = 0; i < per; ++i) {
+    const int c = threadIdx.x + i * LN_THREADS;
+    if (c < C) q += (v[i] - mean) * (v[i] - mean);
   }
-  y[i] = __float2bfloat16(o);
+  const float rstd = rsqrtf(block_sum(q, red) / (float)C + eps);
+  for (int i = 0; i < per; ++i) {
+    const int c = threadIdx.x + i * LN_THREADS;
+    if (c < C)
+      y[r * C + c] = __float2bfloat16((v[i] - mean) * rstd * __bfloat162float(w[c]) + __bfloat162float(b[c]));
+  }
 }
 
 int vit_patch_pos(const float* acc, const void* bias, const void* table, const int* idx, const void* wts, void* h,
@@ -155,31 +122,20 @@ int vit_patch_pos(const float* acc, const void* bias, const void* table, const i
   return (int)cudaGetLastError();
 }
 
-int vit_qkv_rope(const float* acc, const void* bias, const float* cosv, const float* sinv, int P, int H, int Dh,
-                 int Dp, void* q, void* k, void* v, cudaStream_t st) {
+int vit_qkv_rope(const void* qkv, const float* cosv, const float* sinv, int P, int H, int Dh, int Dp, void* q,
+                 void* k, void* v, cudaStream_t st) {
   if (Dh % 2 || Dh > Dp) return 3;
   if (P <= 0) return 0;
-  vit_qkv_rope_kernel<<<P, 256, 0, st>>>(acc, (const __nv_bfloat16*)bias, cosv, sinv, P, H, Dh, Dp,
-                                         (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v);
+  vit_qkv_rope_kernel<<<P, 256, 0, st>>>((const __nv_bfloat16*)qkv, cosv, sinv, P, H, Dh, Dp, (__nv_bfloat16*)q,
+                                         (__nv_bfloat16*)k, (__nv_bfloat16*)v);
   return (int)cudaGetLastError();
 }
 
-int vit_residual_ln(const float* acc, const void* bias, void* h, const void* w, const void* b, float eps, void* y,
-                    int rows, int C, cudaStream_t st) {
-  if (C > LN_THREADS * LN_PER || (y && (!w || !b))) return 3;
+int vit_layernorm(const void* x, const void* w, const void* b, float eps, void* y, int rows, int C, cudaStream_t st) {
+  if (C > LN_THREADS * LN_PER || C < 1) return 3;
   if (rows <= 0) return 0;
-  vit_residual_ln_kernel<<<rows, LN_THREADS, 0, st>>>(acc, (const __nv_bfloat16*)bias, (__nv_bfloat16*)h,
-                                                      (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, eps,
-                                                      (__nv_bfloat16*)y, C);
-  return (int)cudaGetLastError();
-}
-
-int vit_bias_act(const float* acc, const void* bias, void* y, int rows, int C, int act, cudaStream_t st) {
-  if (act < 0 || act > 2) return 3;
-  const size_t n = (size_t)rows * C;
-  if (n == 0) return 0;
-  vit_bias_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(acc, (const __nv_bfloat16*)bias,
-                                                                   (__nv_bfloat16*)y, n, C, act);
+  vit_layernorm_kernel<<<rows, LN_THREADS, 0, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w,
+                                                    (const __nv_bfloat16*)b, eps, (__nv_bfloat16*)y, C);
   return (int)cudaGetLastError();
 }
 

@@ -11,13 +11,14 @@ Here:
   ``blocks.{i}.{norm1,attn.qkv,attn.proj,norm2,mlp.linear_fc1,mlp.linear_fc2}``, ``merger``,
   ``deepstack_merger_list.{j}``), so a checkpoint's ``model.visual.*`` tensors load with ``load_state_dict``;
 * :meth:`VisionTower.forward_reference` is an fp32 PyTorch statement of the tower (the oracle of the tests);
-* :meth:`VisionTower.forward` is the B200 path: every projection on the tcgen05 GEMM (fp32 outputs, biases added in
-  the following kernel, so each Linear rounds once as a bf16 module does), attention on the tcgen05 training-attention
+* :meth:`VisionTower.forward` is the B200 path: every projection on the tcgen05 GEMM with its bias, GELU and residual
+  add in the epilogue (one bf16 rounding per projection), attention on the tcgen05 training-attention
   forward in its bidirectional mode with the 72-wide heads zero-padded to 128 (the output projection's weight is
   padded to match once), and the elementwise work in ``csrc/vision.cu``;
 * :func:`vit_interp` is the deployed position-table resampling (align-corners bilinear taps, weights rounded to the
   table's dtype, bf16 products and running sums), :func:`vision_rope_angles` the 2-D rotary angles and
-  :func:`mrope_positions` the text model's three-row positions around image runs;
+  :func:`mrope_positions` the text model's three-row positions around image runs and
+  :func:`mrope_angles` the interleaved multimodal rotary angles they give;
 * :func:`merge_image_features` writes the merged image features over the image-token rows of a text embedding.
 
 The tower is frozen everywhere in the reference, so only the forward is provided (no vision LoRA).
@@ -150,6 +151,23 @@ def mrope_positions(token_types: torch.Tensor, image_grid_thw, merge: int) -> to
         cur += max(h, w) // merge
         i += n
     return pos
+
+
+def mrope_angles(pos3: torch.Tensor, rot: int, theta: float, sections: tuple[int, int, int]) -> torch.Tensor:
+    """Rotary angles [T, rot / 2] (fp32) of the text attention from three-row positions [3, T], interleaved:
+    frequency f takes its position from the height row when f = 1 (mod 3) and f < 3 sections[1], from the width row
+    when f = 2 (mod 3) and f < 3 sections[2], else from the temporal row. For text tokens the three rows are equal,
+    so this is ordinary RoPE at that position (decode after an image continues at token index + a per-sequence
+    delta)."""
+    nf = rot // 2
+    if sum(sections) != nf:
+        raise ValueError(f"sections {sections} do not cover {nf} frequencies")
+    inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.float32, device=pos3.device) / rot))
+    f = torch.arange(nf, device=pos3.device)
+    row = torch.zeros(nf, dtype=torch.long, device=pos3.device)
+    row[(f % 3 == 1) & (f < 3 * sections[1])] = 1
+    row[(f % 3 == 2) & (f < 3 * sections[2])] = 2
+    return pos3.float()[row].t() * inv[None, :]
 
 
 def merge_image_features(embeds: torch.Tensor, ids: torch.Tensor, image_token_id: int,
@@ -325,65 +343,47 @@ class VisionTower(nn.Module):
         P, Hd, H, Dh, Dp = pixels.shape[0], c.hidden_size, c.num_heads, c.head_dim, 128
         if sum(t * h * w for t, h, w in grids) != P:
             raise ValueError("pixels rows do not match grid_thw")
-        f32 = dict(dtype=torch.float32, device=dev)
         b16 = dict(dtype=torch.bfloat16, device=dev)
         # patch embedding (+ bias) + resampled position table
         acc = cc.gemm(pixels.to(torch.bfloat16).contiguous(), nat["wpe"], out_fp32=True)
         idx, wts = vit_interp(grids, c.grid_side, c.spatial_merge_size, torch.bfloat16, dev)
         h = torch.empty(P, Hd, **b16)
         cc.vit_patch_pos(acc, nat["bpe"], nat["table"], idx.to(torch.int32).contiguous(), wts.contiguous(), h)
+        del acc
         ang = vision_rope_angles(grids, Dh, c.spatial_merge_size, c.rope_theta, dev)
         cosv, sinv = ang.cos().contiguous(), ang.sin().contiguous()
-        seg = [h_ * w_ for t_, h_, w_ in grids for _ in range(t_)]
+        seg = [h_ * w_ for t_, h_, w_ in grids for _ in range(t_)]  # attention within each frame
         cu_host = [0]
         for n in seg:
             cu_host.append(cu_host[-1] + n)
         cu = torch.tensor(cu_host, dtype=torch.int32, device=dev)
         fwd_tiles = tile_lists(cu_host, dev)[0]
         q, k, v, o = (torch.empty(P, H, Dp, **b16) for _ in range(4))
-        lse = torch.empty(H, P, **f32)
+        lse = torch.empty(H, P, dtype=torch.float32, device=dev)
         y = torch.empty(P, Hd, **b16)
+        qkv = torch.empty(P, 3 * Hd, **b16)
         m = torch.empty(P, c.intermediate_size, **b16)
         scale = 1.0 / math.sqrt(Dh)
         ds = []
-        blocks = nat["blocks"]
-        cc.vit_residual_ln(None, None, h, blocks[0]["n1w"], blocks[0]["n1b"], c.eps, y)
-        for li, b in enumerate(blocks):
-            acc = cc.gemm(y, b["wqkv"], out_fp32=True)
-            cc.vit_qkv_rope(acc, b["bqkv"], cosv, sinv, H, Dh, q, k, v)
+        for li, b in enumerate(nat["blocks"]):
+            cc.vit_layernorm(h, b["n1w"], b["n1b"], c.eps, y)
+            cc.gemm(y, b["wqkv"], out=qkv, bias=b["bqkv"])
+            cc.vit_qkv_rope(qkv, cosv, sinv, H, Dh, q, k, v)
             cc.attn_train_fwd(q, k, v, cu, fwd_tiles, scale, o, lse, None, 64, False)
-            acc = cc.gemm(o.view(P, H * Dp), b["wproj"], out_fp32=True)
-            cc.vit_residual_ln(acc, b["bproj"], h, b["n2w"], b["n2b"], c.eps, y)
-            acc = cc.gemm(y, b["w1"], out_fp32=True)
-            cc.vit_bias_act(acc, b["b1"], m, 1)
-            acc = cc.gemm(m, b["w2"], out_fp32=True)
-            last = li + 1 == len(blocks)
-            if li in c.deepstack_visual_indexes or last:
-                cc.vit_residual_ln(acc, b["b2"], h, None, None, c.eps, None)
-                if li in c.deepstack_visual_indexes:
-                    ds.append(self._merge_native(h, nat["ds"][c.deepstack_visual_indexes.index(li)]))
-                if not last:
-                    nb = blocks[li + 1]
-                    cc.vit_residual_ln(None, None, h, nb["n1w"], nb["n1b"], c.eps, y)
-            else:
-                nb = blocks[li + 1]
-                cc.vit_residual_ln(acc, b["b2"], h, nb["n1w"], nb["n1b"], c.eps, y)
+            cc.gemm(o.view(P, H * Dp), b["wproj"], out=h, residual=h, bias=b["bproj"])
+            cc.vit_layernorm(h, b["n2w"], b["n2b"], c.eps, y)
+            cc.gemm(y, b["w1"], out=m, bias=b["b1"], act=1)
+            cc.gemm(m, b["w2"], out=h, residual=h, bias=b["b2"])
+            if li in c.deepstack_visual_indexes:
+                ds.append(self._merge_native(h, nat["ds"][c.deepstack_visual_indexes.index(li)]))
         return self._merge_native(h, nat["merger"]), ds
 
     def _merge_native(self, h: torch.Tensor, m: dict) -> torch.Tensor:
         from ..ops import C
         c, cc = self.cfg, C()
         rows = h.shape[0] // c.spatial_merge_size ** 2
-        if m["post"]:
-            x = h.view(rows, c.merged_dim)
-            y = torch.empty_like(x)
-            cc.vit_residual_ln(None, None, x, m["nw"], m["nb"], c.eps, y)
-        else:
-            y = torch.empty_like(h)
-            cc.vit_residual_ln(None, None, h, m["nw"], m["nb"], c.eps, y)
-            y = y.view(rows, c.merged_dim)
-        t = torch.empty(rows, c.merged_dim, dtype=torch.bfloat16, device=h.device)
-        cc.vit_bias_act(cc.gemm(y, m["w1"], out_fp32=True), m["b1"], t, 2)
-        out = torch.empty(rows, c.out_hidden_size, dtype=torch.bfloat16, device=h.device)
-        cc.vit_bias_act(cc.gemm(t, m["w2"], out_fp32=True), m["b2"], out, 0)
-        return out
+        x = h.view(rows, c.merged_dim) if m["post"] else h
+        y = torch.empty_like(x)
+        cc.vit_layernorm(x, m["nw"], m["nb"], c.eps, y)
+        t = cc.gemm(y.view(rows, c.merged_dim), m["w1"], bias=m["b1"], act=2)
+        return cc.gemm(t, m["w2"], bias=m["b2"])

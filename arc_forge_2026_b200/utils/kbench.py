@@ -141,7 +141,7 @@ def bench_gemm(M=640):
     byts = sum(N * K * 2 for N, K in shapes)
     out.append({"kernel": "gemm_bf16_tn chain (graph)", "M": M, "launches": len(shapes), "ms": round(ms, 4),
                 "weight_bytes": byts, "frac_hbm_of_measured": round(byts / ms / 1e6 / peaks["hbm_gbs"], 3),
-                "pdl": os.environ.get("AFB_GEMM_NO_PDL") is None})
+                "pdl": os.environ.get("AFB_NO_PDL") is None})
     del g
     return out
 

@@ -50,6 +50,26 @@ def test_gemm_tiles_splitk_residual(bn, splits):
     assert _rel(out32, a.float() @ b.float().t()) < 1e-5
 
 
+@pytest.mark.parametrize("act,splits", [(0, 1), (1, 1), (2, 1), (1, 3), (2, 4)])
+def test_gemm_bias_gelu_residual_epilogue(act, splits):
+    """out = act(alpha * a @ b.T + bias) + residual, in the GEMM's epilogue and in the split-K reduce."""
+    import torch.nn.functional as F
+    g = torch.Generator(device=dev).manual_seed(11 + act)
+    M, N, K = 200, 1024, 2048
+    a = torch.randn(M, K, device=dev, generator=g).bfloat16()
+    b = (torch.randn(N, K, device=dev, generator=g) * 0.03).bfloat16()
+    bias = torch.randn(N, device=dev, generator=g).bfloat16()
+    r = torch.randn(M, N, device=dev, generator=g).bfloat16()
+    x = 0.5 * (a.float() @ b.float().t()) + bias.float()
+    x = {0: x, 1: F.gelu(x, approximate="tanh"), 2: F.gelu(x)}[act]
+    out = C().gemm(a, b, residual=r, alpha=0.5, bias=bias, act=act, splits=splits)
+    torch.cuda.synchronize()
+    check_status()
+    assert _rel(out, x + r.float()) < 1e-2
+    out32 = C().gemm(a, b, alpha=0.5, bias=bias, act=act, splits=splits, out_fp32=True)
+    assert _rel(out32, x) < 1e-4
+
+
 def test_gemm_strided_a():
     g = torch.Generator(device=dev).manual_seed(8)
     big = torch.randn(64, 4096, device=dev, generator=g).bfloat16()

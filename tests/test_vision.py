@@ -83,3 +83,17 @@ def test_multimodal_positions_match_hf_rope_index():
     feats = torch.randn(n0 + n1, 8)
     out = merge_image_features(emb, ids, 99, feats)
     assert torch.equal(out[ids == 99], feats) and torch.equal(out[ids != 99], emb[ids != 99])
+
+
+def test_interleaved_mrope_angles_match_hf_text_rotary():
+    from arc_forge_2026_b200.models.vision import mrope_angles
+    cfg = hfc.Qwen3VLMoeTextConfig(head_dim=128, rope_parameters={"rope_type": "default", "rope_theta": 5e5,
+                                                                   "mrope_section": [24, 20, 20],
+                                                                   "mrope_interleaved": True})
+    rope = hf.Qwen3VLMoeTextRotaryEmbedding(cfg)
+    types_ = torch.tensor([0] * 3 + [1] * 12 + [0] * 2)
+    pos3 = mrope_positions(types_, torch.tensor([[1, 6, 8]]), 2)
+    cos, sin = rope(torch.zeros(1, dtype=torch.float32), pos3[:, None, :])
+    ang = mrope_angles(pos3, 128, 5e5, (24, 20, 20))
+    torch.testing.assert_close(torch.cat([ang, ang], -1).cos(), cos[0], rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(torch.cat([ang, ang], -1).sin(), sin[0], rtol=1e-6, atol=1e-6)
