@@ -644,6 +644,8 @@ int swiglu(const void* x, void* y, int T, int I, cudaStream_t st) {
 // ------------------------------------------------------------------------------------------ embedding
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  __nv_bfloat16* __restrict__ out, int T, int H, int V, uint32_t* status) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int t = blockIdx.x;
   int id = ids[t];
   if (id < 0 || id >= V) {
@@ -658,7 +660,7 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
 int embedding(const int* ids, const void* table, void* out, int T, int H, int V, uint32_t* status, cudaStream_t st) {
   if (H % 8) return 3;
   if (!T) return 0;
-  embedding_kernel<<<T, 128, 0, st>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, H, V, status);
+  if (const int pdl_rc = launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, st, ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, H, V, status)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 

@@ -110,6 +110,8 @@ __global__ void __launch_bounds__(256) hc_norm_bwd_kernel(const bf16* __restrict
 // thread per (row, 8 columns)
 __global__ void __launch_bounds__(256) hc_mix_fwd_kernel(const bf16* __restrict__ pre, const bf16* __restrict__ zb,
                                                          bf16* __restrict__ x, int64_t rows, int G, int H) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int c8 = H / 8;
   const float inv = 1.f / G;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < rows * c8; q += (int64_t)gridDim.x * blockDim.x) {
@@ -161,6 +163,8 @@ __global__ void __launch_bounds__(256) hc_mix_bwd_kernel(const bf16* __restrict_
 __global__ void __launch_bounds__(256) hc_inject_fwd_kernel(const bf16* __restrict__ h, const bf16* __restrict__ y,
                                                             const bf16* __restrict__ gate, bf16* __restrict__ out,
                                                             int64_t rows, int G, int H) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int c8 = H / 8;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < rows * c8; q += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = q / c8;
@@ -256,6 +260,8 @@ int hc_norm_bwd(const void* h, const float* w, const float* rstd, const float* d
 // gate = 2 sigmoid(du[:, R:R+G] / 4), both bf16 (one launch instead of the elementwise chain).
 __global__ void __launch_bounds__(256) hc_act_kernel(const bf16* __restrict__ du, int ld, int64_t rows, int R, int G,
                                                      bf16* __restrict__ s, bf16* __restrict__ gate) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int per = R + (gate ? G : 0);
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * per) return;
@@ -269,14 +275,14 @@ int hc_act_fwd(const void* du, int ld, int64_t rows, int R, int G, void* s, void
   if (rows < 1) return 0;
   if (R < 1 || G < 0 || ld < R + (gate ? G : 0)) return 3;
   const int64_t n = rows * (R + (gate ? G : 0));
-  hc_act_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const bf16*)du, ld, rows, R, G, (bf16*)s, (bf16*)gate);
+  if (const int pdl_rc = launch_pdl(hc_act_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const bf16*)du, ld, rows, R, G, (bf16*)s, (bf16*)gate)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
 int hc_mix_fwd(const void* pre, const void* zb, void* x, int64_t rows, int G, int H, cudaStream_t st) {
   if (rows < 1) return 0;
   if (H % 8 || G < 1 || G > MAXG) return 3;
-  hc_mix_fwd_kernel<<<grid8(rows * (H / 8)), 256, 0, st>>>((const bf16*)pre, (const bf16*)zb, (bf16*)x, rows, G, H);
+  if (const int pdl_rc = launch_pdl(hc_mix_fwd_kernel, dim3(grid8(rows * (H / 8))), dim3(256), 0, st, (const bf16*)pre, (const bf16*)zb, (bf16*)x, rows, G, H)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 int hc_mix_bwd(const void* pre, const void* zb, const void* dx, void* dpre, float* dzb, int64_t rows, int G, int H,
@@ -291,8 +297,8 @@ int hc_inject_fwd(const void* h, const void* y, const void* gate, void* out, int
                   cudaStream_t st) {
   if (rows < 1) return 0;
   if (H % 8 || G < 1 || G > MAXG) return 3;
-  hc_inject_fwd_kernel<<<grid8(rows * (H / 8)), 256, 0, st>>>((const bf16*)h, (const bf16*)y, (const bf16*)gate,
-                                                              (bf16*)out, rows, G, H);
+  if (const int pdl_rc = launch_pdl(hc_inject_fwd_kernel, dim3(grid8(rows * (H / 8))), dim3(256), 0, st, (const bf16*)h, (const bf16*)y, (const bf16*)gate,
+                                                              (bf16*)out, rows, G, H)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 int hc_inject_bwd(const void* y, const void* gate, const void* dout, void* dy, float* dgate, int64_t rows, int G,

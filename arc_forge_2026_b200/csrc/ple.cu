@@ -30,6 +30,8 @@ AFB_DEV int64_t wrap_mul(int64_t a, int64_t b) {
 
 template <bool FP8>
 __global__ void __launch_bounds__(256) ple_lookup_kernel(PleLookupArgs a) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // one warp per token
   const int lane = threadIdx.x & 31;
   const int heads = (a.n - 1) * a.hpn;  // <= 32 (checked at launch): lane h hashes head h
@@ -119,10 +121,8 @@ int ple_lookup(const PleLookupArgs& a, bool fp8, cudaStream_t st) {
   const int64_t warps = a.rows;
   if (warps == 0) return 0;
   const int64_t blocks = (warps * 32 + 255) / 256;
-  if (fp8)
-    pled::ple_lookup_kernel<true><<<(unsigned)blocks, 256, 0, st>>>(a);
-  else
-    pled::ple_lookup_kernel<false><<<(unsigned)blocks, 256, 0, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : 1;
+  const int rc = fp8 ? launch_pdl(pled::ple_lookup_kernel<true>, dim3((unsigned)blocks), dim3(256), 0, st, a)
+                    : launch_pdl(pled::ple_lookup_kernel<false>, dim3((unsigned)blocks), dim3(256), 0, st, a);
+  return rc == 0 ? 0 : 1;
 }
 }  // namespace afb

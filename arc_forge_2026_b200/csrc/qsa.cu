@@ -44,6 +44,8 @@ constexpr int THREADS = 256;
 // one warp per (token, j): j < Hi -> index query head j, j == Hi -> raw index key
 __global__ void qsa_prep_kernel(QsaArgs a, const __nv_bfloat16* __restrict__ proj, int ld, int T,
                                 const int* __restrict__ positions, const int* __restrict__ slots) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   __shared__ float buf[8][qsa::DI];
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -93,8 +95,8 @@ int qsa_prep(const QsaArgs& a, const void* proj, int ld, int T, const int* posit
   if (a.Di != qsa::DI || a.Hi < 1 || a.Hi > qsa::MAXH || a.rot > qsa::DI || a.rot % 2 || ld % 4) return 3;
   if (T <= 0) return 0;
   const int warps = 8, total = T * (a.Hi + 1);
-  qsa_prep_kernel<<<(total + warps - 1) / warps, warps * 32, 0, st>>>(a, (const __nv_bfloat16*)proj, ld, T,
-                                                                      positions, slots);
+  if (const int pdl_rc = launch_pdl(qsa_prep_kernel, dim3((total + warps - 1) / warps), dim3(warps * 32), 0, st, a, (const __nv_bfloat16*)proj, ld, T,
+                                                                      positions, slots)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
@@ -146,6 +148,8 @@ AFB_DEV void qsa_pooled_key(const __nv_bfloat16* raw, const int* bt, int B, int 
 // ------------------------------------------------------------------------------------------------ finalize
 // grid (sessions, layers), 8 warps: blocks [fin[s], ctx[s] / B) of session s get pooled keys, one warp per block.
 __global__ void qsa_finalize_kernel(QsaFinalizeArgs f) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int s = blockIdx.x, l = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lo = f.fin[s], hi = min(f.ctx[s] / f.block, f.max_blocks);
   const int* bt = f.block_table + (size_t)s * f.max_pages;
@@ -159,6 +163,8 @@ __global__ void qsa_finalize_kernel(QsaFinalizeArgs f) {
 }
 
 __global__ void qsa_fin_update_kernel(int* fin, const int* ctx, int S, int block, int max_blocks) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s < S) fin[s] = min(ctx[s] / block, max_blocks);
 }
@@ -168,8 +174,8 @@ int qsa_finalize(const QsaFinalizeArgs& f, int S, int layers, cudaStream_t st) {
       f.max_blocks != f.max_pages * (64 / f.block))
     return 3;
   if (S <= 0) return 0;
-  qsa_finalize_kernel<<<dim3(S, layers), 256, 0, st>>>(f);
-  qsa_fin_update_kernel<<<(S + 127) / 128, 128, 0, st>>>(f.fin, f.ctx, S, f.block, f.max_blocks);
+  if (const int pdl_rc = launch_pdl(qsa_finalize_kernel, dim3(dim3(S, layers)), dim3(256), 0, st, f)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(qsa_fin_update_kernel, dim3((S + 127) / 128), dim3(128), 0, st, f.fin, f.ctx, S, f.block, f.max_blocks)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
@@ -221,6 +227,8 @@ AFB_DEV void row_scores(const float* v, int W, float rs, float* dst, int ld) {
 __global__ void __launch_bounds__(qsa_tc::THREADS, 1)
     qsa_scores_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                          QsaArgs a, QsaSelectArgs sa, uint32_t* status) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   using namespace qsa_tc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -358,6 +366,8 @@ AFB_DEV int block_excl_scan(int c, int* wtot, int* total) {
 
 // grid (sessions, W rows), 256 threads; dynamic shared memory: the row's scores [max_blocks] + its index query
 __global__ void __launch_bounds__(qsa::THREADS) qsa_score_kernel(QsaArgs a, QsaSelectArgs sa, uint32_t* status) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ int red[qsa::THREADS / 32];
   const int s = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -492,6 +502,8 @@ __global__ void __launch_bounds__(qsa::THREADS) qsa_score_kernel(QsaArgs a, QsaS
 // staged in shared memory by independent coalesced loads, then each thread compacts a contiguous run of them at the
 // offset a block scan of the per-thread counts gives (no per-chunk barrier round trips through global memory).
 __global__ void __launch_bounds__(qsa::THREADS) qsa_union_kernel(QsaSelectArgs sa, uint32_t* status) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   extern __shared__ uint32_t marks[];
   __shared__ int wtot[qsa::THREADS / 32];
   __shared__ int total;
@@ -560,16 +572,16 @@ int qsa_select(const QsaArgs& a, const QsaSelectArgs& sa, int S, uint32_t* statu
     static std::atomic<uint64_t> tc_devs{0};
     if (const int e = smem_attr_once(tc_devs, (const void*)qsa_scores_tc_kernel, qsa_tc::TOTAL)) return e;
     const int tiles = (sa.max_blocks + qsa_tc::TM - 1) / qsa_tc::TM;
-    qsa_scores_tc_kernel<<<dim3(S, (tiles + qsa_tc::TPC - 1) / qsa_tc::TPC), qsa_tc::THREADS, qsa_tc::TOTAL, st>>>(
-        tk, tq, a, sa, status);
+    if (const int pdl_rc = launch_pdl(qsa_scores_tc_kernel, dim3(dim3(S, (tiles + qsa_tc::TPC - 1) / qsa_tc::TPC)), dim3(qsa_tc::THREADS), qsa_tc::TOTAL, st,
+        tk, tq, a, sa, status)) return pdl_rc;
   } else {
     sb.scores = nullptr;  // the per-row kernel scores every block itself
   }
-  qsa_score_kernel<<<dim3(S, sa.W), qsa::THREADS, smem, st>>>(a, sb, status);
+  if (const int pdl_rc = launch_pdl(qsa_score_kernel, dim3(dim3(S, sa.W)), dim3(qsa::THREADS), smem, st, a, sb, status)) return pdl_rc;
   static std::atomic<uint64_t> union_devs{0};
   const size_t usmem = (size_t)(sa.max_blocks + 1) * 4;
   if (const int e = smem_attr_once(union_devs, (const void*)qsa_union_kernel, 220 * 1024)) return e;
-  qsa_union_kernel<<<S, qsa::THREADS, usmem, st>>>(sa, status);
+  if (const int pdl_rc = launch_pdl(qsa_union_kernel, dim3(S), dim3(qsa::THREADS), usmem, st, sa, status)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 

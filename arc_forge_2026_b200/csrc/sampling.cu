@@ -33,6 +33,8 @@ AFB_DEV float uniform01(uint64_t seed, uint64_t a, uint64_t b, uint64_t c) {
 __global__ void __launch_bounds__(256) select_tokens_kernel(const __nv_bfloat16* __restrict__ logits, int ld, int V,
                                                             int* __restrict__ out, float inv_temp, uint64_t seed,
                                                             const int* __restrict__ step, uint32_t* status) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int row = blockIdx.x;
   const __nv_bfloat16* z = logits + (size_t)row * ld;
   const uint64_t st = step ? (uint64_t)*step : 0;
@@ -96,12 +98,14 @@ int select_tokens(const void* logits, int ld, int rows, int V, int* out, float t
                   const int* step, uint32_t* status, cudaStream_t st) {
   if (!rows) return 0;
   if (ld % 8) return 3;
-  select_tokens_kernel<<<rows, 256, 0, st>>>((const __nv_bfloat16*)logits, ld, V, out,
-                                             temperature > 0.f ? 1.f / temperature : 0.f, seed, step, status);
+  if (const int pdl_rc = launch_pdl(select_tokens_kernel, dim3(rows), dim3(256), 0, st, (const __nv_bfloat16*)logits, ld, V, out,
+                                             temperature > 0.f ? 1.f / temperature : 0.f, seed, step, status)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
 __global__ void spec_accept_kernel(SpecArgs a) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= a.num_seqs) return;
   const int K = a.k;
@@ -136,6 +140,8 @@ __global__ void spec_accept_kernel(SpecArgs a) {
 // The next verify window: ids = [anchor, drafts], positions ctx..ctx+K, KV slots from the page table,
 // attention length ctx + K + 1. One thread per window row. Also bumps the step counter (thread 0).
 __global__ void build_window_kernel(WindowArgs a) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int W = a.width;
   if (i == 0 && a.step) *a.step += 1;
@@ -152,20 +158,22 @@ __global__ void build_window_kernel(WindowArgs a) {
 
 int spec_accept(const SpecArgs& a, cudaStream_t st) {
   if (!a.num_seqs) return 0;
-  spec_accept_kernel<<<(a.num_seqs + 127) / 128, 128, 0, st>>>(a);
+  if (const int pdl_rc = launch_pdl(spec_accept_kernel, dim3((a.num_seqs + 127) / 128), dim3(128), 0, st, a)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
 int build_window(const WindowArgs& a, cudaStream_t st) {
   const int n = a.num_seqs * a.width;
   if (!n) return 0;
-  build_window_kernel<<<(n + 255) / 256, 256, 0, st>>>(a);
+  if (const int pdl_rc = launch_pdl(build_window_kernel, dim3((n + 255) / 256), dim3(256), 0, st, a)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
 // gather rows: out[i] = src[idx[i]] (bf16 rows of width H)
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const int* __restrict__ idx,
                                    __nv_bfloat16* __restrict__ out, int H) {
+  grid_dep_wait();     // launched with programmatic serialization: the previous kernel must be complete
+  grid_dep_trigger();
   const int i = blockIdx.x;
   const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)idx[i] * H);
   uint4* d = reinterpret_cast<uint4*>(out + (size_t)i * H);
@@ -175,7 +183,7 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const 
 int gather_rows(const void* src, const int* idx, void* out, int rows, int H, cudaStream_t st) {
   if (!rows) return 0;
   if (H % 8) return 3;
-  gather_rows_kernel<<<rows, 128, 0, st>>>((const __nv_bfloat16*)src, idx, (__nv_bfloat16*)out, H);
+  if (const int pdl_rc = launch_pdl(gather_rows_kernel, dim3(rows), dim3(128), 0, st, (const __nv_bfloat16*)src, idx, (__nv_bfloat16*)out, H)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 

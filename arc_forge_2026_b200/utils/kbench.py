@@ -172,10 +172,38 @@ def bench_vision(grids=((1, 64, 64), (1, 32, 48)), depth=27, seed=0):
         ms_hf = None
     tower = tower.cuda()
     ms = time_cuda(lambda: tower(pixels, grid), iters=5)
+    # where one block's time goes (each piece timed alone, times the depth)
+    from ..ops import C
+    from ..train.attention import tile_lists
+    H, Dp = cfg.num_heads, 128
+    cu_host = [0]
+    for t, h, w in grids:
+        for _ in range(t):
+            cu_host.append(cu_host[-1] + h * w)
+    cu = torch.tensor(cu_host, dtype=torch.int32, device="cuda")
+    tiles = tile_lists(cu_host, "cuda")[0]
+    q, k, v, o = (torch.randn(P, H, Dp, device="cuda").bfloat16() for _ in range(4))
+    lse = torch.empty(H, P, device="cuda")
+    ms_attn = time_cuda(lambda: C().attn_train_fwd(q, k, v, cu, tiles, cfg.head_dim ** -0.5, o, lse, None, 64, False),
+                        iters=5)
+    b = tower._native["blocks"][0]
+    y = torch.randn(P, cfg.hidden_size, device="cuda").bfloat16()
+    m = torch.randn(P, cfg.intermediate_size, device="cuda").bfloat16()
+
+    def gemms():
+        C().gemm(y, b["wqkv"], bias=b["bqkv"])
+        C().gemm(o.view(P, H * Dp), b["wproj"], bias=b["bproj"])
+        C().gemm(y, b["w1"], bias=b["b1"], act=1)
+        C().gemm(m, b["w2"], bias=b["b2"])
+    ms_gemm = time_cuda(gemms, iters=5)
+    att_flops = sum(4 * (h * w) ** 2 * 128 * H * t for t, h, w in grids)
     flops = 2 * P * cfg.depth * (4 * cfg.hidden_size ** 2 + 2 * cfg.hidden_size * cfg.intermediate_size)
     out.append({"kernel": "vision tower (27 blocks, native)", "patches": P, "ms": round(ms, 3),
                 "patches_per_s": round(P / ms * 1e3), "linear_tflops": round(flops / ms / 1e9, 1),
-                "hf_bf16_sdpa_ms": None if ms_hf is None else round(ms_hf, 3)})
+                "hf_bf16_sdpa_ms": None if ms_hf is None else round(ms_hf, 3),
+                "attention_ms_x_depth": round(ms_attn * cfg.depth, 3),
+                "attention_tflops_padded": round(att_flops / ms_attn / 1e9, 1),
+                "block_gemms_ms_x_depth": round(ms_gemm * cfg.depth, 3)})
     return out
 
 
