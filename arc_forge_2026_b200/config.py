@@ -80,6 +80,10 @@ class ModelConfig:
     qsa_indexer_dim: int = 128
     # storage format of the routed experts: "int3" (uint3 g128), "fp8" (128x128 block), "bf16"
     expert_format: str = "bf16"
+    # multimodal RoPE: frequencies of the rotary dims split (temporal, height, width), interleaved; None = text-only
+    # 1-D RoPE. With three-row positions (``models/vision.py`` ``mrope_positions``) image tokens rotate by their grid
+    # position; text tokens have equal rows and get plain RoPE.
+    mrope_section: tuple | None = None
 
     def __post_init__(self):
         if self.num_attention_heads % self.num_kv_heads:
@@ -95,6 +99,11 @@ class ModelConfig:
         rot = self.rotary_dim
         if rot <= 0 or rot % 2:
             raise ValueError("rotary dimension must be positive and even")
+        if self.mrope_section is not None:
+            self.mrope_section = tuple(int(x) for x in self.mrope_section)
+            if len(self.mrope_section) != 3 or sum(self.mrope_section) != rot // 2:
+                raise ValueError(f"mrope_section {self.mrope_section} must split the {rot // 2} rotary frequencies "
+                                 "into (temporal, height, width)")
         if self.expert_format not in ("int3", "fp8", "bf16"):
             raise ValueError(f"expert_format {self.expert_format!r}")
         self.ple_layer_ids = tuple(int(i) for i in self.ple_layer_ids)

@@ -49,10 +49,26 @@ def gated_rms_norm(x: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float
     return (xf * w.float() * F.silu(z.float())).to(x.dtype)
 
 
-def rope_cos_sin(positions: torch.Tensor, rot: int, theta: float) -> tuple[torch.Tensor, torch.Tensor]:
+def rope_cos_sin(positions: torch.Tensor, rot: int, theta: float,
+                 sections: tuple | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos / sin [..., rot / 2] of positions [...]. With ``sections`` (multimodal RoPE) ``positions`` may be three-row
+    [3, ...] (temporal, height, width): frequency f takes the height row when f = 1 (mod 3) and f < 3 sections[1],
+    the width row when f = 2 (mod 3) and f < 3 sections[2], else the temporal row (the interleaved layout)."""
     inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.float64, device=positions.device) / rot))
-    ang = positions.double()[..., None] * inv
+    if sections is not None and positions.dim() >= 2 and positions.shape[0] == 3:
+        f = torch.arange(rot // 2, device=positions.device)
+        row = torch.zeros_like(f)
+        row[(f % 3 == 1) & (f < 3 * sections[1])] = 1
+        row[(f % 3 == 2) & (f < 3 * sections[2])] = 2
+        pos = positions.double().movedim(0, -1)[..., row]  # [..., rot / 2]
+        ang = pos * inv
+    else:
+        ang = positions.double()[..., None] * inv
     return ang.cos().float(), ang.sin().float()
+
+
+def is_three_row(positions) -> bool:
+    return positions is not None and positions.dim() >= 2 and positions.shape[0] == 3
 
 
 def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
@@ -151,6 +167,8 @@ class GatedAttention(nn.Module):
         c = self.cfg
         Bsz, T, _ = x.shape
         Di, Hi, Bk, K = c.qsa_indexer_dim, c.qsa_indexer_heads, c.qsa_block, c.qsa_topk
+        if is_three_row(positions):
+            raise ValueError("QSA selection with multimodal (three-row) positions is not supported")
         proj = self.index_qk_proj(x)
         iq, raw = proj[..., :Hi * Di].view(Bsz, T, Hi, Di), proj[..., Hi * Di:]
         cos, sin = rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
@@ -191,7 +209,7 @@ class GatedAttention(nn.Module):
         k = self.k_proj(x).view(B, T, c.num_kv_heads, c.head_dim)
         v = self.v_proj(x).view(B, T, c.num_kv_heads, c.head_dim)
         q, k = self.q_norm(q), self.k_norm(k)
-        cos, sin = rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
+        cos, sin = rope_cos_sin(positions, c.rotary_dim, c.rope_theta, c.mrope_section)
         q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
         return q, gate.reshape(B, T, -1), k, v
 
@@ -469,14 +487,35 @@ class HybridMoE(nn.Module):
     def new_cache(self):
         return [dict() for _ in self.layers]
 
-    def hidden(self, ids, cache=None, start_pos: int = 0):
+    def hidden(self, ids, cache=None, start_pos: int = 0, positions=None, image_features=None, deepstack=None,
+               image_token_id: int | None = None):
+        """Final hidden states. Multimodal (one sequence, B = 1): ``positions`` three-row [3, T]
+        (``models/vision.py`` ``mrope_positions``, with ``cfg.mrope_section``), ``image_features`` [n, H] replace
+        the embeddings of the ``image_token_id`` tokens in order, and the i-th ``deepstack`` feature [n, H] is added
+        to those tokens' hidden state after decoder layer i (Qwen3-VL's deepstack; in every branch of a
+        hyper-connection stream). Decoding after an image continues with 1-D positions offset by the sequence's
+        delta (last three-row position + 1 - length)."""
         B, T = ids.shape
-        positions = torch.arange(start_pos, start_pos + T, device=ids.device)
+        if positions is None:
+            positions = torch.arange(start_pos, start_pos + T, device=ids.device)
+        elif is_three_row(positions) and self.cfg.mrope_section is None:
+            raise ValueError("three-row positions need cfg.mrope_section")
         x = self.embed_tokens(ids)
+        mask = None
+        if image_features is not None:
+            mask = ids == image_token_id
+            if int(mask.sum()) != image_features.shape[0]:
+                raise ValueError(f"{int(mask.sum())} image tokens for {image_features.shape[0]} image features")
+            x = x.clone()
+            x[mask] = image_features.to(x.dtype)
         if self.hc_final is not None:  # every branch starts as the embedding
             x = x[..., None, :].expand(*x.shape[:-1], self.cfg.hc_count, x.shape[-1]).contiguous()
         for i, layer in enumerate(self.layers):
             x = layer(x, positions, None if cache is None else cache[i], ids)
+            if deepstack is not None and i < len(deepstack):
+                add = deepstack[i].to(x.dtype)
+                x = x.clone()
+                x[mask] = x[mask] + (add[:, None, :] if self.hc_final is not None else add)
         if self.hc_final is not None:
             x = self.hc_final(x)[0]
         return self.norm(x)

@@ -327,7 +327,10 @@ class StudentLayer(nn.Module):
         v = self._lin("v_proj", x, True).view(B, T, c.num_kv_heads, D)
         q, k = fused.rms_norm(q, self.q_norm, c.rms_norm_eps), fused.rms_norm(k, self.k_norm, c.rms_norm_eps)
         positions = torch.arange(T, device=x.device) if pack is None else pack["pos"][0]
-        cos, sin = R.rope_cos_sin(positions, c.rotary_dim, c.rope_theta)
+        rope_pos = pack["pos3"] if pack is not None and pack.get("pos3") is not None else positions
+        if R.is_three_row(rope_pos) and (c.mrope_section is None or c.qsa_topk):
+            raise ValueError("three-row (multimodal) positions need cfg.mrope_section and no QSA")
+        cos, sin = R.rope_cos_sin(rope_pos, c.rotary_dim, c.rope_theta, c.mrope_section)
         q, k = R.apply_rope(q, cos, sin), R.apply_rope(k, cos, sin)
         blkmap = self._qsa_blocks(x, positions, pack) if pack is not None else None
         if pack is None and q.is_cuda and q.dtype == torch.bfloat16 and D in (128, 256):
@@ -441,18 +444,32 @@ class QADStudent(nn.Module):
                 g[k] += v
         return g
 
-    def hidden(self, ids, pack: dict | None = None):
+    def hidden(self, ids, pack: dict | None = None, image_features=None, deepstack=None,
+               image_token_id: int | None = None):
         """Final hidden states of ``ids`` [B, T]; ``pack`` (``train/packing.py`` ``PackedBin.forward_args``) makes
-        the row a packed bin of several sequences (B = 1)."""
+        the row a packed bin of several sequences (B = 1). Multimodal rows (the same contract as
+        ``models.reference.HybridMoE.hidden``): ``pack["pos3"]`` three-row positions [3, T], ``image_features``
+        [n, H] over the ``image_token_id`` tokens, ``deepstack[i]`` added to them after layer i."""
         x = F.embedding(ids, self.embed)
+        mask = None
+        if image_features is not None:
+            mask = ids == image_token_id
+            if int(mask.sum()) != image_features.shape[0]:
+                raise ValueError(f"{int(mask.sum())} image tokens for {image_features.shape[0]} image features")
+            x = x.clone()
+            x[mask] = image_features.to(x.dtype)
         hc = getattr(self, "hc_final", None)
         if hc is not None:  # every branch starts as the embedding
             x = x[..., None, :].expand(*x.shape[:-1], self.cfg.hc_count, x.shape[-1]).contiguous()
-        for L in self.layers:
+        for i, L in enumerate(self.layers):
             if self.ckpt and torch.is_grad_enabled():
                 x = checkpoint(L, x, pack, ids, use_reentrant=False)
             else:
                 x = L(x, pack, ids)
+            if deepstack is not None and i < len(deepstack):
+                add = deepstack[i].to(x.dtype)
+                x = x.clone()
+                x[mask] = x[mask] + (add[:, None, :] if hc is not None else add)
         if hc is not None:
             x = hc_read(x, hc)[0]
         return fused.rms_norm(x, self.final_norm, self.cfg.rms_norm_eps)

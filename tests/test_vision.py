@@ -97,3 +97,58 @@ def test_interleaved_mrope_angles_match_hf_text_rotary():
     ang = mrope_angles(pos3, 128, 5e5, (24, 20, 20))
     torch.testing.assert_close(torch.cat([ang, ang], -1).cos(), cos[0], rtol=1e-6, atol=1e-6)
     torch.testing.assert_close(torch.cat([ang, ang], -1).sin(), sin[0], rtol=1e-6, atol=1e-6)
+
+
+def _mm_ref(seed=0):
+    from arc_forge_2026_b200.config import preset
+    from arc_forge_2026_b200.models.reference import build_reference
+    cfg = preset("tiny_cpu", mrope_section=(4, 2, 2))
+    return cfg, build_reference(cfg, seed=seed)
+
+
+def test_multimodal_rope_reduces_to_text_rope_on_text_tokens():
+    cfg, ref = _mm_ref()
+    ids = torch.randint(0, cfg.vocab_size, (1, 40), generator=torch.Generator().manual_seed(1))
+    pos3 = torch.arange(40).expand(3, 40)
+    with torch.no_grad():
+        torch.testing.assert_close(ref.hidden(ids, positions=pos3), ref.hidden(ids), rtol=0, atol=0)
+
+
+def test_decode_after_an_image_continues_with_the_position_delta():
+    """Prefill text + image + text with three-row positions and image features, then decode one token at
+    1-D position index + delta: the same hidden state as the whole sequence in one pass."""
+    cfg, ref = _mm_ref(seed=2)
+    img_id = 7
+    g = torch.Generator().manual_seed(3)
+    grid = torch.tensor([[1, 4, 6]])
+    ids = torch.randint(10, cfg.vocab_size, (1, 16), generator=g)
+    ids[0, 5:11] = img_id  # 4 x 6 patches -> 6 merged tokens
+    feats = torch.randn(6, cfg.hidden_size, generator=g) * 0.02
+    ds = [torch.randn(6, cfg.hidden_size, generator=g) * 0.02]
+    pos3 = mrope_positions((ids[0] == img_id).long(), grid, 2)
+    with torch.no_grad():
+        full = ref.hidden(ids, positions=pos3, image_features=feats, deepstack=ds, image_token_id=img_id)
+        cache = ref.new_cache()
+        ref.hidden(ids[:, :15], cache, positions=pos3[:, :15], image_features=feats, deepstack=ds,
+                   image_token_id=img_id)
+        delta = int(pos3[:, :15].max()) + 1 - 15
+        step = ref.hidden(ids[:, 15:], cache, start_pos=15 + delta)
+    torch.testing.assert_close(step[0, -1], full[0, -1], rtol=1e-4, atol=1e-5)
+    assert delta < 0  # the image took fewer positions than tokens
+
+
+def test_sft_reads_image_examples(tmp_path):
+    import json
+
+    import numpy as np
+
+    from arc_forge_2026_b200.train import sft
+    np.save(tmp_path / "a.npy", np.zeros((64, 1536), dtype=np.float32))
+    rows = [{"ids": [1, 2, 3, 4]}, {"ids": [5] + [9] * 16 + [6], "images": [{"pixels": "a.npy", "grid_thw": [1, 8, 8]}]}]
+    (tmp_path / "d.jsonl").write_text("\n".join(json.dumps(r) for r in rows))
+    media = []
+    seqs, masks = sft.load_examples(tmp_path / "d.jsonl", media)
+    assert len(seqs) == 2 and media[0] is None and media[1][0]["grid_thw"] == [1, 8, 8]
+    assert media[1][0]["pixels"] == tmp_path / "a.npy"
+    with pytest.raises(ValueError):
+        sft.load_examples(tmp_path / "d.jsonl")
