@@ -152,3 +152,17 @@ def test_sft_reads_image_examples(tmp_path):
     assert media[1][0]["pixels"] == tmp_path / "a.npy"
     with pytest.raises(ValueError):
         sft.load_examples(tmp_path / "d.jsonl")
+
+
+def test_reference_rope_tables_agree_with_the_vision_module_angles():
+    """The text model's three-row RoPE tables (models/reference.py) and models/vision.py's angles are one rule."""
+    from arc_forge_2026_b200.models.reference import rope_cos_sin
+    from arc_forge_2026_b200.models.vision import mrope_angles
+    types_ = torch.tensor([0] * 4 + [1] * 30 + [0] * 6)
+    pos3 = mrope_positions(types_, torch.tensor([[1, 10, 12]]), 2)
+    cos, sin = rope_cos_sin(pos3, 32, 1.0e7, (6, 5, 5))
+    ang = mrope_angles(pos3, 32, 1.0e7, (6, 5, 5))
+    torch.testing.assert_close(cos, ang.double().cos().float(), rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(sin, ang.double().sin().float(), rtol=1e-6, atol=1e-6)
+    text = rope_cos_sin(torch.arange(40), 32, 1.0e7, (6, 5, 5))  # 1-D positions: plain RoPE
+    torch.testing.assert_close(text[0], rope_cos_sin(torch.arange(40), 32, 1.0e7)[0], rtol=0, atol=0)
