@@ -653,7 +653,8 @@ static int launch_attn_tc(const AttnArgs& a, int splits, uint32_t* status, cudaS
   if (const int e = smem_attr_once(attr_devs, (const void*)paged_attn_tc_kernel<D>, L::TOTAL)) return e;
   dim3 grid(a.num_seqs * a.Hkv * ((a.q_per_seq + tpc - 1) / tpc), splits);
   {
-    const int pdl_rc = launch_pdl(paged_attn_tc_kernel<D>, dim3(grid), dim3(attn_tc::THREADS), L::TOTAL, st, tk, tv, tq, a, status);
+    const int pdl_rc = launch_pdl(paged_attn_tc_kernel<D>, dim3(grid), dim3(attn_tc::THREADS), L::TOTAL, st, tk, tv,
+        tq, a, status);
     if (pdl_rc) return pdl_rc;
   }
   return (int)cudaGetLastError();

@@ -287,7 +287,8 @@ int router_topk(const float* logits, int ld, int T, int E, int k, int renorm, in
   }
   if (T <= 0) return 0;
   {
-    const int pdl_rc = launch_pdl(router_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, st, logits, ld, T, E, k, renorm, ids, weights, cnt,
+    const int pdl_rc = launch_pdl(router_topk_kernel, dim3((T + warps - 1) / warps), dim3(warps * 32), 0, st, logits,
+        ld, T, E, k, renorm, ids, weights, cnt,
                                                                       list, cap);
     if (pdl_rc) return pdl_rc;
   }
@@ -503,7 +504,8 @@ int quant_rows_e4m3_row(const void* x, int ldx, const int* row_token, const int*
   if (nrows <= 0) return 0;
   const int warps = 8;
   {
-    const int pdl_rc = launch_pdl(quant_rows_e4m3_row_kernel, dim3((nrows + warps - 1) / warps), dim3(warps * 32), 0, st,
+    const int pdl_rc = launch_pdl(quant_rows_e4m3_row_kernel, dim3((nrows + warps - 1) / warps), dim3(warps * 32), 0,
+        st,
       (const __nv_bfloat16*)x, ldx, row_token, nrows_dev, nrows, K, (uint8_t*)q, scales);
     if (pdl_rc) return pdl_rc;
   }
@@ -603,7 +605,8 @@ int moe_combine(const void* y, const int* entry_row, int k, const void* shared, 
   const int threads = 256;
   dim3 grid(rows, (H / 8 + threads - 1) / threads);
   {
-    const int pdl_rc = launch_pdl(moe_combine_kernel, dim3(grid), dim3(threads), 0, st, (const __nv_bfloat16*)y, entry_row, k, (const __nv_bfloat16*)shared,
+    const int pdl_rc = launch_pdl(moe_combine_kernel, dim3(grid), dim3(threads), 0, st, (const __nv_bfloat16*)y,
+        entry_row, k, (const __nv_bfloat16*)shared,
                                                router_logits, ld_logits, sg_col, (const __nv_bfloat16*)resid,
                                                (__nv_bfloat16*)out, T, H, ew, status);
     if (pdl_rc) return pdl_rc;
@@ -635,7 +638,8 @@ int swiglu(const void* x, void* y, int T, int I, cudaStream_t st) {
   const size_t n = (size_t)T * I / 8;
   if (!n) return 0;
   {
-    const int pdl_rc = launch_pdl(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const __nv_bfloat16*)x, (__nv_bfloat16*)y, T, I);
+    const int pdl_rc = launch_pdl(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st,
+        (const __nv_bfloat16*)x, (__nv_bfloat16*)y, T, I);
     if (pdl_rc) return pdl_rc;
   }
   return (int)cudaGetLastError();
@@ -660,7 +664,8 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
 int embedding(const int* ids, const void* table, void* out, int T, int H, int V, uint32_t* status, cudaStream_t st) {
   if (H % 8) return 3;
   if (!T) return 0;
-  if (const int pdl_rc = launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, st, ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, H, V, status)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, st, ids, (const __nv_bfloat16*)table,
+      (__nv_bfloat16*)out, T, H, V, status)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 

@@ -129,7 +129,8 @@ int ep_dispatch(const EpArgs& a, const void* x, int ldx, const int* ids, const f
     return 3;
   const int E = a.E_local * a.world;
   {
-    const int pdl_rc = launch_pdl(ep_dispatch_kernel, dim3(a.T_cap + (E + 3) / 4), dim3(128), 0, st, a, (const __nv_bfloat16*)x, ldx, ids, weights);
+    const int pdl_rc = launch_pdl(ep_dispatch_kernel, dim3(a.T_cap + (E + 3) / 4), dim3(128), 0, st, a,
+        (const __nv_bfloat16*)x, ldx, ids, weights);
     if (pdl_rc) return pdl_rc;
   }
   return (int)cudaGetLastError();

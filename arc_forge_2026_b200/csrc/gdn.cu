@@ -203,12 +203,14 @@ int gdn_decode(const GdnArgs& a, int parity, int num_sms, uint32_t* status, cuda
   const int C = a.conv_dim;
   if (a.Dk == 128 && a.Dv == 128) {
     if (C % 128) return 3;
-    if (const int rc = launch_pdl(gdn_conv_prep_kernel<128>, dim3(a.num_seqs, C / 128), dim3(128), 0, st, a, parity)) return rc;
+    if (const int rc = launch_pdl(gdn_conv_prep_kernel<128>, dim3(a.num_seqs, C / 128), dim3(128), 0, st, a,
+        parity)) return rc;
     if (const int rc = gdn_verify_tc(a, parity, num_sms, status, st); rc != -1) return rc;
     gdn_recurrent_kernel<128, 128, 4><<<dim3(a.num_seqs, a.Hv), 512, 0, st>>>(a, parity);
   } else if (a.Dk == 64 && a.Dv == 64) {
     if (C % 64) return 3;
-    if (const int rc = launch_pdl(gdn_conv_prep_kernel<64>, dim3(a.num_seqs, C / 64), dim3(64), 0, st, a, parity)) return rc;
+    if (const int rc = launch_pdl(gdn_conv_prep_kernel<64>, dim3(a.num_seqs, C / 64), dim3(64), 0, st, a,
+        parity)) return rc;
     gdn_recurrent_kernel<64, 64, 2><<<dim3(a.num_seqs, a.Hv), 128, 0, st>>>(a, parity);
   } else {
     return 3;

@@ -516,7 +516,8 @@ int gdn_verify_tc(const GdnArgs& a, int parity, int num_sms, uint32_t* status, c
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)gdn_verify_tc_kernel, (int)smem)) return e;
   const int items = a.num_seqs * a.Hv;
-  return launch_pdl(gdn_verify_tc_kernel, dim3(items < num_sms ? items : num_sms), dim3(THREADS), smem, st, ts, tq, tv, a,
+  return launch_pdl(gdn_verify_tc_kernel, dim3(items < num_sms ? items : num_sms), dim3(THREADS), smem, st, ts, tq,
+      tv, a,
                     parity, status);
 }
 

@@ -275,14 +275,16 @@ int hc_act_fwd(const void* du, int ld, int64_t rows, int R, int G, void* s, void
   if (rows < 1) return 0;
   if (R < 1 || G < 0 || ld < R + (gate ? G : 0)) return 3;
   const int64_t n = rows * (R + (gate ? G : 0));
-  if (const int pdl_rc = launch_pdl(hc_act_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const bf16*)du, ld, rows, R, G, (bf16*)s, (bf16*)gate)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(hc_act_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st,
+      (const bf16*)du, ld, rows, R, G, (bf16*)s, (bf16*)gate)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
 int hc_mix_fwd(const void* pre, const void* zb, void* x, int64_t rows, int G, int H, cudaStream_t st) {
   if (rows < 1) return 0;
   if (H % 8 || G < 1 || G > MAXG) return 3;
-  if (const int pdl_rc = launch_pdl(hc_mix_fwd_kernel, dim3(grid8(rows * (H / 8))), dim3(256), 0, st, (const bf16*)pre, (const bf16*)zb, (bf16*)x, rows, G, H)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(hc_mix_fwd_kernel, dim3(grid8(rows * (H / 8))), dim3(256), 0, st,
+      (const bf16*)pre, (const bf16*)zb, (bf16*)x, rows, G, H)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 int hc_mix_bwd(const void* pre, const void* zb, const void* dx, void* dpre, float* dzb, int64_t rows, int G, int H,
@@ -297,7 +299,8 @@ int hc_inject_fwd(const void* h, const void* y, const void* gate, void* out, int
                   cudaStream_t st) {
   if (rows < 1) return 0;
   if (H % 8 || G < 1 || G > MAXG) return 3;
-  if (const int pdl_rc = launch_pdl(hc_inject_fwd_kernel, dim3(grid8(rows * (H / 8))), dim3(256), 0, st, (const bf16*)h, (const bf16*)y, (const bf16*)gate,
+  if (const int pdl_rc = launch_pdl(hc_inject_fwd_kernel, dim3(grid8(rows * (H / 8))), dim3(256), 0, st,
+      (const bf16*)h, (const bf16*)y, (const bf16*)gate,
                                                               (bf16*)out, rows, G, H)) return pdl_rc;
   return (int)cudaGetLastError();
 }

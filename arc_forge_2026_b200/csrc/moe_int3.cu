@@ -580,7 +580,8 @@ static int launch_moe_t(const CUtensorMap& tw, const MoeGemmArgs& a, int grid, u
   static std::atomic<uint64_t> attr_devs{0};
   if (const int e = smem_attr_once(attr_devs, (const void*)moe_int3_gemm_kernel<PAIR, F8, PROF>, L::TOTAL)) return e;
   {
-    const int pdl_rc = launch_pdl(moe_int3_gemm_kernel<PAIR, F8, PROF>, dim3(grid), dim3(moe::THREADS), L::TOTAL, st, tw, a, status);
+    const int pdl_rc = launch_pdl(moe_int3_gemm_kernel<PAIR, F8, PROF>, dim3(grid), dim3(moe::THREADS), L::TOTAL, st,
+        tw, a, status);
     if (pdl_rc) return pdl_rc;
   }
   return (int)cudaGetLastError();

@@ -95,7 +95,8 @@ int qsa_prep(const QsaArgs& a, const void* proj, int ld, int T, const int* posit
   if (a.Di != qsa::DI || a.Hi < 1 || a.Hi > qsa::MAXH || a.rot > qsa::DI || a.rot % 2 || ld % 4) return 3;
   if (T <= 0) return 0;
   const int warps = 8, total = T * (a.Hi + 1);
-  if (const int pdl_rc = launch_pdl(qsa_prep_kernel, dim3((total + warps - 1) / warps), dim3(warps * 32), 0, st, a, (const __nv_bfloat16*)proj, ld, T,
+  if (const int pdl_rc = launch_pdl(qsa_prep_kernel, dim3((total + warps - 1) / warps), dim3(warps * 32), 0, st, a,
+      (const __nv_bfloat16*)proj, ld, T,
                                                                       positions, slots)) return pdl_rc;
   return (int)cudaGetLastError();
 }
@@ -175,7 +176,8 @@ int qsa_finalize(const QsaFinalizeArgs& f, int S, int layers, cudaStream_t st) {
     return 3;
   if (S <= 0) return 0;
   if (const int pdl_rc = launch_pdl(qsa_finalize_kernel, dim3(dim3(S, layers)), dim3(256), 0, st, f)) return pdl_rc;
-  if (const int pdl_rc = launch_pdl(qsa_fin_update_kernel, dim3((S + 127) / 128), dim3(128), 0, st, f.fin, f.ctx, S, f.block, f.max_blocks)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(qsa_fin_update_kernel, dim3((S + 127) / 128), dim3(128), 0, st, f.fin, f.ctx, S,
+      f.block, f.max_blocks)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
@@ -572,16 +574,19 @@ int qsa_select(const QsaArgs& a, const QsaSelectArgs& sa, int S, uint32_t* statu
     static std::atomic<uint64_t> tc_devs{0};
     if (const int e = smem_attr_once(tc_devs, (const void*)qsa_scores_tc_kernel, qsa_tc::TOTAL)) return e;
     const int tiles = (sa.max_blocks + qsa_tc::TM - 1) / qsa_tc::TM;
-    if (const int pdl_rc = launch_pdl(qsa_scores_tc_kernel, dim3(dim3(S, (tiles + qsa_tc::TPC - 1) / qsa_tc::TPC)), dim3(qsa_tc::THREADS), qsa_tc::TOTAL, st,
+    if (const int pdl_rc = launch_pdl(qsa_scores_tc_kernel, dim3(dim3(S, (tiles + qsa_tc::TPC - 1) / qsa_tc::TPC)),
+        dim3(qsa_tc::THREADS), qsa_tc::TOTAL, st,
         tk, tq, a, sa, status)) return pdl_rc;
   } else {
     sb.scores = nullptr;  // the per-row kernel scores every block itself
   }
-  if (const int pdl_rc = launch_pdl(qsa_score_kernel, dim3(dim3(S, sa.W)), dim3(qsa::THREADS), smem, st, a, sb, status)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(qsa_score_kernel, dim3(dim3(S, sa.W)), dim3(qsa::THREADS), smem, st, a, sb,
+      status)) return pdl_rc;
   static std::atomic<uint64_t> union_devs{0};
   const size_t usmem = (size_t)(sa.max_blocks + 1) * 4;
   if (const int e = smem_attr_once(union_devs, (const void*)qsa_union_kernel, 220 * 1024)) return e;
-  if (const int pdl_rc = launch_pdl(qsa_union_kernel, dim3(S), dim3(qsa::THREADS), usmem, st, sa, status)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(qsa_union_kernel, dim3(S), dim3(qsa::THREADS), usmem, st, sa,
+      status)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 

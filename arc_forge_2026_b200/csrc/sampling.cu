@@ -98,7 +98,8 @@ int select_tokens(const void* logits, int ld, int rows, int V, int* out, float t
                   const int* step, uint32_t* status, cudaStream_t st) {
   if (!rows) return 0;
   if (ld % 8) return 3;
-  if (const int pdl_rc = launch_pdl(select_tokens_kernel, dim3(rows), dim3(256), 0, st, (const __nv_bfloat16*)logits, ld, V, out,
+  if (const int pdl_rc = launch_pdl(select_tokens_kernel, dim3(rows), dim3(256), 0, st, (const __nv_bfloat16*)logits,
+      ld, V, out,
                                              temperature > 0.f ? 1.f / temperature : 0.f, seed, step, status)) return pdl_rc;
   return (int)cudaGetLastError();
 }
@@ -158,7 +159,8 @@ __global__ void build_window_kernel(WindowArgs a) {
 
 int spec_accept(const SpecArgs& a, cudaStream_t st) {
   if (!a.num_seqs) return 0;
-  if (const int pdl_rc = launch_pdl(spec_accept_kernel, dim3((a.num_seqs + 127) / 128), dim3(128), 0, st, a)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(spec_accept_kernel, dim3((a.num_seqs + 127) / 128), dim3(128), 0, st,
+      a)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
@@ -183,7 +185,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, const 
 int gather_rows(const void* src, const int* idx, void* out, int rows, int H, cudaStream_t st) {
   if (!rows) return 0;
   if (H % 8) return 3;
-  if (const int pdl_rc = launch_pdl(gather_rows_kernel, dim3(rows), dim3(128), 0, st, (const __nv_bfloat16*)src, idx, (__nv_bfloat16*)out, H)) return pdl_rc;
+  if (const int pdl_rc = launch_pdl(gather_rows_kernel, dim3(rows), dim3(128), 0, st, (const __nv_bfloat16*)src, idx,
+      (__nv_bfloat16*)out, H)) return pdl_rc;
   return (int)cudaGetLastError();
 }
 
