@@ -166,3 +166,30 @@ def test_reference_rope_tables_agree_with_the_vision_module_angles():
     torch.testing.assert_close(sin, ang.double().sin().float(), rtol=1e-6, atol=1e-6)
     text = rope_cos_sin(torch.arange(40), 32, 1.0e7, (6, 5, 5))  # 1-D positions: plain RoPE
     torch.testing.assert_close(text[0], rope_cos_sin(torch.arange(40), 32, 1.0e7)[0], rtol=0, atol=0)
+
+
+def test_cpu_engine_serves_an_image_prompt():
+    """The CPU serving engine with a vision tower: greedy tokens after an image prompt equal a full recompute of the
+    whole sequence (three-row positions over prompt + generated text) at every step."""
+    from arc_forge_2026_b200.serve.cpu_engine import CPUEngine
+    cfg, ref = _mm_ref(seed=4)
+    vcfg = VisionConfig(depth=2, hidden_size=64, num_heads=4, intermediate_size=96, out_hidden_size=cfg.hidden_size,
+                        num_position_embeddings=64, deepstack_visual_indexes=(0,))
+    tower = VisionTower.random(vcfg, seed=5)
+    img = 7
+    g = torch.Generator().manual_seed(6)
+    pixels = torch.randn(4 * 6, vcfg.patch_dim, generator=g)
+    prompt = [11, 12, 13] + [img] * 6 + [14, 15]
+    eng = CPUEngine(ref, vision=tower, image_token_id=img)
+    s = eng.add_session(0, prompt, 5, images=[(pixels, (1, 4, 6))])
+    while not s.done:
+        eng.step()
+    merged, ds = tower.forward_reference(pixels, torch.tensor([[1, 4, 6]]))
+    seq = list(prompt)
+    for tok in s.generated:
+        ids = torch.tensor([seq])
+        pos3 = mrope_positions((ids[0] == img).long(), torch.tensor([[1, 4, 6]]), 2)
+        with torch.no_grad():
+            h = ref.hidden(ids, positions=pos3, image_features=merged, deepstack=ds, image_token_id=img)
+        assert int(ref.lm_head(h)[0, -1].argmax()) == tok
+        seq.append(tok)
