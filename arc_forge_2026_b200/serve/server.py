@@ -5,7 +5,9 @@ server-side sessions and ``/close_session``, usage accounting):
 
     GET  /health                 liveness
     GET  /v1/models              the served model
-    POST /v1/completions         {"prompt": str | [int], "max_tokens", "stream"}
+    POST /v1/completions         {"prompt": str | [int], "max_tokens", "stream", "images"?}; "images" (an extension):
+                                 [{"pixels": processor patches [P][patch_dim], "grid_thw": [t, h, w]}] for the
+                                 prompt's image-token runs, served by an engine with a vision tower
     POST /v1/chat/completions    {"messages": [...], "max_tokens", "stream"}
     POST /v1/responses           {"input": str | [messages], "session_id"?, "max_output_tokens", "stream"}
                                  a session keeps its transcript (and, on engines that can extend a session, its
@@ -56,6 +58,7 @@ class Request:
     rid: str = ""
     aborted: bool = False
     out: list = field(default_factory=list)
+    images: list | None = None         # [(pixels [P, patch_dim], (t, h, w))] for the prompt's image tokens
 
 
 class EngineLoop:
@@ -149,7 +152,12 @@ class EngineLoop:
                     sess = eng.add_session(sid, self.transcripts[key] + (req.extend or []), req.max_new)
             else:
                 sid = next(self._sids)
-                sess = eng.add_session(sid, req.prompt, req.max_new)
+                if req.images:
+                    if getattr(eng, "vision", None) is None:
+                        raise ValueError("this engine has no vision tower: image prompts are not served")
+                    sess = eng.add_session(sid, req.prompt, req.max_new, images=req.images)
+                else:
+                    sess = eng.add_session(sid, req.prompt, req.max_new)
                 if key is not None:
                     self.keyed[key] = sid
         except Exception as e:  # noqa: BLE001 - reported to the client
@@ -303,9 +311,9 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200", ledge
     app = FastAPI(title="arc_forge_2026_b200", lifespan=lifespan)
     app.state.engine_loop = loop_
 
-    async def _generate(prompt, max_new, key=None, extend=None, rid=None, state=None):
+    async def _generate(prompt, max_new, key=None, extend=None, rid=None, state=None, images=None):
         loop = asyncio.get_running_loop()
-        req = Request(prompt, max_new, loop, asyncio.Queue(), key, extend, rid=rid or "")
+        req = Request(prompt, max_new, loop, asyncio.Queue(), key, extend, rid=rid or "", images=images)
         loop_.submit(req)
         while True:
             kind, val = await req.queue.get()
@@ -354,13 +362,16 @@ def create_app(engine, tokenizer=None, model_name: str = "arc-forge-b200", ledge
         max_new = int(body.get("max_tokens", 16))
         rid = body.get("rid") or "cmpl-" + uuid.uuid4().hex[:24]
         st = {}
+        # images (an extension of this server): the processor's flattened patches and grid of each image, in the
+        # order of the prompt's image-token runs
+        images = [(im["pixels"], tuple(int(x) for x in im["grid_thw"])) for im in body.get("images") or []] or None
         if body.get("stream"):
             async def chunks():
-                async for t in _generate(ids, max_new, rid=rid, state=st):
+                async for t in _generate(ids, max_new, rid=rid, state=st, images=images):
                     yield {"id": rid, "object": "text_completion", "model": model_name,
                            "choices": [{"index": 0, "text": tok.decode([t]), "token_ids": [t], "finish_reason": None}]}
             return _sse(chunks())
-        out = await _collect(_generate(ids, max_new, rid=rid, state=st))
+        out = await _collect(_generate(ids, max_new, rid=rid, state=st, images=images))
         return {"id": rid, "object": "text_completion", "created": int(time.time()), "model": model_name,
                 "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out,
                              "finish_reason": _reason(st, len(out), max_new)}],

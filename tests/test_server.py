@@ -115,3 +115,30 @@ def test_update_weights_from_disk_swaps_the_served_model(tmp_path):
         for _ in range(4):
             ids.append(int(ref(torch.tensor([ids]))[0, -1].argmax()))
     assert out["token_ids"] == ids[len(prompt):]
+
+
+def test_completion_with_an_image_matches_the_engine(setup):
+    """Image prompts through the server (the ``images`` extension of /v1/completions) give the CPU engine's tokens;
+    an engine without a vision tower refuses them with a 400."""
+    from arc_forge_2026_b200.models.vision import VisionConfig, VisionTower
+    client, _ = setup
+    img = 7
+    prompt = [11, 12] + [img] * 6 + [13]
+    pixels = torch.randn(24, 96, generator=torch.Generator().manual_seed(9))
+    body = {"prompt": prompt, "max_tokens": 4, "images": [{"pixels": pixels.tolist(), "grid_thw": [1, 4, 6]}]}
+    assert client.post("/v1/completions", json=body).status_code == 400
+    cfg = preset("tiny_cpu", mrope_section=(4, 2, 2))
+    ref = build_reference(cfg, seed=1)
+    tower = VisionTower.random(VisionConfig(depth=1, hidden_size=64, num_heads=4, intermediate_size=96, patch_size=4,
+                                            out_hidden_size=cfg.hidden_size, num_position_embeddings=64,
+                                            deepstack_visual_indexes=()), seed=2)
+    app = create_app(CPUEngine(ref, max_sessions=2, vision=tower, image_token_id=img), _NoEos(), "tiny")
+    with TestClient(app) as c2:
+        r = c2.post("/v1/completions", json=body)
+        assert r.status_code == 200, r.text
+        got = r.json()["choices"][0]["token_ids"]
+    eng = CPUEngine(ref, vision=tower, image_token_id=img)
+    s = eng.add_session(0, prompt, 4, images=[(pixels, (1, 4, 6))])
+    while not s.done:
+        eng.step()
+    assert got == s.generated
